@@ -1,0 +1,211 @@
+/*
+ * ptsim_b200.h -- the C ABI of the B200 functional executor for PyTorchSim-Triton-Backend tile programs.
+ *
+ * The reference executes a compiled kernel object by running Spike + the Coprocessor model over the
+ * kernel's ELF, one process per program range:
+ *   - argv assembly and process spawn:  pytorchsim_triton_compiler/runtime/spike.py:44-56, :100-120
+ *   - the program loop inside the ELF:  pytorchsim_triton_compiler/codegen/wrapper.py:238-266
+ *     (pid_x = f % gx, pid_y = (f / gx) % gy, pid_z = f / (gx * gy) for f in [lo, hi))
+ *   - trap codes on failure:            pytorchsim_triton_compiler/runtime/spike.py:12 (200, 201)
+ * This library replaces both: a launch descriptor (the "binary" the B200 lowering emits in place of the
+ * ELF) plus caller-owned device pointers go in, and one sm_100a kernel (or a short fixed sequence of
+ * them) runs the programs [lo, hi) of the launch on the caller's stream.
+ *
+ * Rules of the ABI:
+ *   - plain C types only; every pointer is caller-owned; ptsim_launch allocates nothing;
+ *   - every call returns 0 on success or a PTSIM_E_* code; ptsim_last_error() gives the message of the
+ *     calling thread's last failure;
+ *   - device-side failures (a bounds check, a bounded wait that gave up) are recorded in a per-device
+ *     status word and returned by ptsim_sync(); a kernel that records one returns early, it never traps.
+ */
+#ifndef PTSIM_B200_H
+#define PTSIM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PTSIM_ABI_VERSION 1
+#define PTSIM_DESC_MAGIC 0x42535450u /* "PTSB" little endian */
+
+/* Status codes.  200/201 keep the numbers of the reference's named Spike traps
+ * (runtime/spike.py:12 TRAP_HINT = {200: INVALID_SPAD_ACCESS, 201: STACK_OVERFLOW}). */
+#define PTSIM_OK 0
+#define PTSIM_E_DESC 1          /* malformed or unsupported descriptor */
+#define PTSIM_E_ARGS 2          /* pointer count, alignment, range or size mismatch */
+#define PTSIM_E_CUDA 3          /* a CUDA runtime/driver call failed */
+#define PTSIM_E_UNSUPPORTED 4   /* a shape this executor does not run (refused, never approximated) */
+#define PTSIM_E_OOB 200         /* a device-side bounds check caught an access outside a tensor */
+#define PTSIM_E_RESOURCE 201    /* shared memory / TMEM / workspace too small for the launch */
+#define PTSIM_E_TIMEOUT 202     /* a bounded device-side wait gave up (pipeline stall) */
+
+/* Descriptor kinds: one per tile-program class the lowering recognises. */
+#define PTSIM_KIND_ELEMENTWISE 1   /* DMA loads at affine index maps + vector-unit ops + one DMA store */
+#define PTSIM_KIND_ROW_SOFTMAX 2   /* row max (NaN-propagating), sum of exp, divide */
+#define PTSIM_KIND_ROW_RMSNORM 3   /* row mean of squares, rsqrt(mean + eps), times weight */
+#define PTSIM_KIND_QKNORM_ROPE 4   /* per-head RMSNorm over head_dim + rotary embedding + head-major store */
+#define PTSIM_KIND_GEMM 5          /* C = A.B (+ residual), bf16 inputs, fp32 accumulate, cast on store */
+#define PTSIM_KIND_ATTN_PREFILL 6  /* causal GQA flash attention forward, fp32 online softmax */
+#define PTSIM_KIND_REDUCE_ALL 7    /* a whole-tensor sum or max to one fp32 value */
+
+/* Element types of tensor arguments (kernel.json dtype names, contract/kernel_object.py:43-56). */
+#define PTSIM_DT_F32 0
+#define PTSIM_DT_BF16 1
+#define PTSIM_DT_F16 2
+#define PTSIM_DT_I32 3
+#define PTSIM_DT_I64 4
+#define PTSIM_DT_I16 5
+#define PTSIM_DT_I8 6
+#define PTSIM_DT_U8 7
+#define PTSIM_DT_F64 8
+
+/* Vector-unit opcodes of an ELEMENTWISE program (fp32 registers, IEEE round-to-nearest). */
+#define PTSIM_OP_LOAD 1    /* r[dst] = widen(arg[map a][index])                        (DMA MVIN) */
+#define PTSIM_OP_CONST 2   /* r[dst] = imm */
+#define PTSIM_OP_ADD 3
+#define PTSIM_OP_SUB 4
+#define PTSIM_OP_MUL 5
+#define PTSIM_OP_DIV 6
+#define PTSIM_OP_NEG 7
+#define PTSIM_OP_EXP 8     /* 2^(x * log2 e), as the EUP computes exp (lower_vector_functions.py:310) */
+#define PTSIM_OP_RSQRT 9
+#define PTSIM_OP_SQRT 10
+#define PTSIM_OP_MAX 11    /* NaN-propagating maximum (PyTorchSimTpuOps.td:70-74) */
+#define PTSIM_OP_MIN 12    /* NaN-propagating minimum */
+#define PTSIM_OP_RBF16 13  /* round to bf16 (RNE) and widen back: an explicit .to(bfloat16) */
+#define PTSIM_OP_ABS 14
+#define PTSIM_OP_STORE 15  /* arg[store map][index] = narrow(r[a])                        (DMA MVOUT) */
+
+/* REDUCE_ALL operations. */
+#define PTSIM_RED_SUM 0
+#define PTSIM_RED_MAX 1
+
+#define PTSIM_MAX_ARGS 16
+#define PTSIM_MAX_MAPS 8
+#define PTSIM_MAX_DIGITS 4
+#define PTSIM_MAX_CODE 32
+#define PTSIM_MAX_REGS 8
+
+/* One DMA transfer's index map (the 4-D strided box of pytorchsim.transfer, PyTorchSimOps.td:20-72):
+ * element offset in tensor `arg` of flat launch index i = offset + sum_d ((i / div[d]) % mod[d]) * stride[d]. */
+typedef struct ptsim_map {
+  int32_t arg;
+  int32_t ndigit;
+  int64_t offset;
+  int64_t div[PTSIM_MAX_DIGITS];
+  int64_t mod[PTSIM_MAX_DIGITS];
+  int64_t stride[PTSIM_MAX_DIGITS];
+} ptsim_map;
+
+typedef struct ptsim_insn {
+  uint8_t op, dst, a, b;
+  float imm;
+} ptsim_insn;
+
+typedef struct ptsim_ew_params {
+  int64_t numel;          /* flat index space of the store */
+  int32_t nmap, ncode;
+  int32_t store_map;      /* index into map[] of the store */
+  int32_t pure_copy;      /* 1: one load stored unchanged to the same dtype -> byte copy (bit exact) */
+  ptsim_map map[PTSIM_MAX_MAPS];
+  ptsim_insn code[PTSIM_MAX_CODE];
+} ptsim_ew_params;
+
+typedef struct ptsim_row_params {
+  int64_t rows, cols;
+  int64_t in_row_stride, out_row_stride;
+  int32_t in_arg, out_arg, weight_arg, pad0; /* weight_arg -1 when absent */
+  float eps;              /* RMSNorm epsilon */
+  float inv_cols;         /* unused by the kernels (they divide by cols in fp32, as the program does) */
+} ptsim_row_params;
+
+typedef struct ptsim_qkrope_params {
+  int64_t tokens, heads, dim;           /* input rows are (token, head) pairs of `dim` values */
+  int64_t out_tok_stride, out_head_stride; /* output element offset = t*tok_stride + h*head_stride + d */
+  int32_t in_arg, weight_arg, cos_arg, sin_arg, out_arg, pad0;
+  float eps, pad1;
+} ptsim_qkrope_params;
+
+typedef struct ptsim_gemm_params {
+  int64_t M, N, K;
+  int64_t lda, ldb, ldc, ldr;  /* row strides in elements: A [M,K] row-major; B [K,N] or [N,K]; C, R [M,N] */
+  int32_t a_arg, b_arg, c_arg, r_arg;  /* r_arg: residual added before the store, -1 when absent */
+  int32_t b_kmajor;            /* 0: B is [K,N] with N contiguous (the Inductor mm layout); 1: B is [N,K] */
+  int32_t pad0;
+} ptsim_gemm_params;
+
+typedef struct ptsim_attn_params {
+  int64_t batch, hq, hkv, seq, dim;
+  int32_t q_arg, k_arg, v_arg, o_arg;
+  int32_t causal, pad0;
+  float scale, pad1;
+  int64_t ref_bq, ref_bkv;     /* the reference program's query/key block sizes (its m_i/l_i restarts) */
+} ptsim_attn_params;
+
+typedef struct ptsim_reduce_params {
+  int64_t numel;
+  int32_t in_arg, out_arg, op, pad0;
+} ptsim_reduce_params;
+
+typedef struct ptsim_desc {
+  uint32_t magic;        /* PTSIM_DESC_MAGIC */
+  uint32_t version;      /* PTSIM_ABI_VERSION */
+  uint32_t kind;         /* PTSIM_KIND_* */
+  uint32_t flags;
+  int32_t nargs, pad0;
+  int32_t arg_dtype[PTSIM_MAX_ARGS];
+  int64_t arg_numel[PTSIM_MAX_ARGS];
+  int64_t grid[3];       /* the reference launch grid the lowering was made for */
+  int64_t units;         /* partition units of a launch: [lo, hi) of ptsim_launch index these */
+  int64_t unit_size;     /* elements (ELEMENTWISE), rows (row kinds), M rows (GEMM), (b, h) (attention) per unit */
+  int64_t workspace_bytes; /* scratch the launch needs from the caller (REDUCE_ALL partials), else 0 */
+  union {
+    ptsim_ew_params ew;
+    ptsim_row_params row;
+    ptsim_qkrope_params qk;
+    ptsim_gemm_params gemm;
+    ptsim_attn_params attn;
+    ptsim_reduce_params red;
+  } p;
+} ptsim_desc;
+
+/* ABI version the library was built with (PTSIM_ABI_VERSION). */
+int ptsim_version(void);
+
+/* sizeof(ptsim_desc) as compiled, so a binding can check its own mirror of the struct. */
+size_t ptsim_desc_size(void);
+
+/* Select `device`, create its status word and check it is an sm_100 part.  Idempotent per device.
+ * Replaces the reference's discovery of Spike/pk/model (toolchain.py:19-75, kernel_object.py:289-320). */
+int ptsim_init(int device);
+
+/* Validate a descriptor without running it (magic, version, kind, sizes, map ranges).  Host only. */
+int ptsim_check(const void *desc, size_t desc_bytes);
+
+/* Number of partition units of the descriptor's launch (the [lo, hi) range ptsim_launch takes). */
+int64_t ptsim_units(const void *desc, size_t desc_bytes);
+
+/* Run units [lo, hi) of the launch `desc` over the tensors `dev_ptrs[0..nptr)` (argument order of
+ * kernel.json, contract/kernel_object.py:131-133 argv_order) on `stream` (a cudaStream_t; NULL = legacy
+ * default).  `workspace` holds desc->workspace_bytes of device scratch, or is NULL when that is 0.
+ * Asynchronous: returns once the kernels are enqueued.  Replaces runtime/spike.py:100-120 (launch) and
+ * the ELF's program loop codegen/wrapper.py:254-266. */
+int ptsim_launch(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int nptr,
+                 int64_t lo, int64_t hi, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Synchronise `stream` and return (and clear) the device status word of the current device:
+ * *device_status receives PTSIM_OK or PTSIM_E_OOB / PTSIM_E_TIMEOUT as a kernel recorded it.
+ * Replaces the exit-code check of runtime/spike.py:23-33 (run_process). */
+int ptsim_sync(void *stream, int32_t *device_status);
+
+/* Copy the calling thread's last error message into buf (NUL-terminated, truncated to n). */
+int ptsim_last_error(char *buf, int n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PTSIM_B200_H */

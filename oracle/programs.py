@@ -1,0 +1,200 @@
+"""CPU oracle of the validation-class tile programs -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference arm may import this module,
+and only as the checker or the timed CPU baseline; the B200 product path never calls it.
+
+Each function restates one program of the reference (the Triton source the reference compiles, cited per
+function) in torch CPU arithmetic: fp32 compute, bf16 storage rounded to nearest-even, casts exactly where
+the source casts, and the NPU's own op rules where the source leaves a choice to the target:
+  - exp is 2^(x * log2 e), as the EUP computes it (targets/tpu/lower_vector_functions.py:310-329);
+  - max/min propagate NaN (PyTorchSimTpuOps.td:64-74; tl.PropagateNan.ALL);
+  - bf16 results are packed round-to-nearest-even (PyTorchSimTpuOps.td:46-50, lower_matmul.py:585-591).
+torch CPU runs every op on all host threads (torch.set_num_threads), which is how the CPU baseline uses the
+box's cores.  Tensors are flat, as kernel.json states them; bf16 arguments are torch.bfloat16."""
+import math
+
+import torch
+
+LOG2E = 1.4426950408889634
+
+
+def f32(t):
+    return t.to(torch.float32)
+
+
+def bf16(t):
+    """Round an fp32 tensor to bf16 (RNE), as a store to a bf16 pointer does."""
+    return t.to(torch.bfloat16)
+
+
+def npu_exp(x):
+    return torch.exp2(x * torch.tensor(LOG2E, dtype=torch.float32))
+
+
+def nan_max(a, dim=None):
+    """max that returns NaN whenever a NaN takes part (torch.max / amax already propagate NaN)."""
+    return torch.amax(a, dim=dim, keepdim=True) if dim is not None else torch.amax(a)
+
+
+# ---------------------------------------------------------------------------------------------------
+# Pointwise programs
+# ---------------------------------------------------------------------------------------------------
+
+def vector_add(x, y):
+    """tests/cases/smoke/add.py:20-25: o = x + y (fp32, bit exact)."""
+    return x + y
+
+
+def add_one(x):
+    """validation/pytorchsim/vector_add1_*/00_*_triton.py: out = bf16(float(x) + 1.0)."""
+    return bf16(f32(x) + 1.0)
+
+
+def slice_add_one(x):
+    """validation/pytorchsim/vector_slice_*/00_*_triton.py: out[0] = float(x[0]) + 1.0 (fp32 output)."""
+    return (f32(x[:1]) + 1.0).to(torch.float32)
+
+
+def heads_to_token_major(x, tokens, heads, dim):
+    """qwen3_8b_layer_prefill_*/07_*: out[t, h, d] = in[h, t, d] (bit exact)."""
+    return x.view(heads, tokens, dim).transpose(0, 1).contiguous().view(-1)
+
+
+def token_to_head_major(x, tokens, heads, dim):
+    """qwen3_8b_layer_prefill_*/05_*: out[h, t, d] = in[t, h, d] (bit exact)."""
+    return x.view(tokens, heads, dim).transpose(0, 1).contiguous().view(-1)
+
+
+def silu_mul(x, tokens, inter):
+    """qwen3_8b_layer_prefill_*/10_*: x = [gate | up] per token; out = bf16(gate / (1 + exp(-gate)) * up)."""
+    v = f32(x).view(tokens, 2 * inter)
+    g, u = v[:, :inter], v[:, inter:]
+    return bf16(g / (npu_exp(-g) + 1.0) * u).reshape(-1)
+
+
+# ---------------------------------------------------------------------------------------------------
+# Row programs
+# ---------------------------------------------------------------------------------------------------
+
+def softmax_rows(x, rows, cols):
+    """validation/pytorchsim/vector_softmax_*/00_*_triton.py:17-68: per row m = max (NaN-propagating),
+    s = sum exp(x - m), out = bf16(exp(x - m) / s)."""
+    v = f32(x).view(rows, cols)
+    m = nan_max(v, 1)
+    e = npu_exp(v - m)
+    return bf16(e / e.sum(dim=1, keepdim=True)).reshape(-1)
+
+
+def rmsnorm_rows(x, w, rows, cols, eps):
+    """qwen3_8b_layer_prefill_*/00_*_triton.py: r = rsqrt(sum(x^2) / cols + eps); out = bf16((x * r) * w)."""
+    v = f32(x).view(rows, cols)
+    ss = (v * v).sum(dim=1, keepdim=True)
+    r = torch.rsqrt(ss / float(cols) + torch.tensor(eps, dtype=torch.float32))
+    return bf16((v * r) * f32(w).view(1, cols)).reshape(-1)
+
+
+def qknorm_rope(x, w, cos, sin, tokens, heads, eps, dim=128):
+    """qwen3_8b_layer_prefill_*/02_*, 04_*: each (token, head) row of `dim`: r = rsqrt(mean(x^2) + eps),
+    n = (x * r) * w, rot = cat(-n[half:], n[:half]), out[h, t] = bf16(n * cos[t] + rot * sin[t]), stored
+    head-major (out index d + dim * t + tokens * dim * h)."""
+    v = f32(x).view(tokens, heads, dim)
+    r = torch.rsqrt((v * v).sum(dim=2, keepdim=True) / float(dim) + torch.tensor(eps, dtype=torch.float32))
+    n = (v * r) * f32(w).view(1, 1, dim)
+    half = dim // 2
+    rot = torch.cat([-n[..., half:], n[..., :half]], dim=2)
+    c = f32(cos).view(tokens, 1, dim)
+    s = f32(sin).view(tokens, 1, dim)
+    out = n * c + rot * s
+    return bf16(out).transpose(0, 1).contiguous().reshape(-1)
+
+
+def reduce_all(x, op):
+    """vector_sum_* / vector_max_*: one fp32 value over the whole tensor."""
+    v = f32(x).reshape(-1)
+    return (v.sum() if op == "sum" else torch.amax(v)).reshape(1)
+
+
+# ---------------------------------------------------------------------------------------------------
+# Matrix-unit programs
+# ---------------------------------------------------------------------------------------------------
+
+def gemm(a, b, M, N, K, residual=None, b_kn=True, out_dtype=torch.bfloat16):
+    """gemm_*/00_*_triton.py and Qwen3 01/03/08/09/11: acc = A . B in fp32 from bf16 inputs (the MXU's f32
+    pop, lower_matmul.py:421-506); + float(residual) when the epilogue adds one; stored as bf16."""
+    A = f32(a).view(M, K)
+    B = f32(b).view(K, N) if b_kn else f32(b).view(N, K).t()
+    acc = A @ B
+    if residual is not None:
+        acc = acc + f32(residual).view(M, N)
+    return acc.to(out_dtype).reshape(-1)
+
+
+def attention_prefill(q, k, v, batch, hq, g, seq, dim, bq, bkv, causal, scale):
+    """validation/pytorchsim/attention_prefill_*/00__prefill_kernel/_prefill_kernel_triton.py:3-44, block for
+    block: per query block of bq rows m = -1e30, l = 0, acc = 0; per key block of bkv below the diagonal and
+    then the diagonal block (masked to -1e30 where key > query): qk = (q . k^T) * SCALE in fp32,
+    m' = max(m, rowmax), alpha = exp(m - m'), p = exp(qk - m'), l = l*alpha + rowsum p,
+    acc = acc*alpha + bf16(p) . v; out = bf16(acc / l)."""
+    hkv = hq // g
+    Q = f32(q).view(batch, hq, seq, dim)
+    Kt = f32(k).view(batch, hkv, seq, dim)
+    V = f32(v).view(batch, hkv, seq, dim)
+    out = torch.empty(batch, hq, seq, dim, dtype=torch.bfloat16)
+    sc = torch.tensor(scale, dtype=torch.float32)
+    for qb in range(seq // bq):
+        rm = torch.arange(qb * bq, (qb + 1) * bq)
+        qt = Q[:, :, qb * bq:(qb + 1) * bq, :]                      # [B, HQ, bq, D]
+        m = torch.full((batch, hq, bq, 1), -1.0e30)
+        l = torch.zeros((batch, hq, bq, 1))
+        acc = torch.zeros((batch, hq, bq, dim))
+        starts = list(range(0, qb * bq if causal else seq, bkv))
+        blocks = [(s, False) for s in starts] + ([(qb * bq, True)] if causal else [])
+        for start, diag in blocks:
+            kb = Kt[:, :, start:start + bkv, :].repeat_interleave(g, dim=1)
+            vb = V[:, :, start:start + bkv, :].repeat_interleave(g, dim=1)
+            qk = (qt @ kb.transpose(2, 3)) * sc
+            if diag:
+                n = torch.arange(start, start + bkv)
+                qk = torch.where(rm[:, None] >= n[None, :], qk, torch.tensor(-1.0e30))
+            m_new = torch.maximum(m, torch.amax(qk, dim=3, keepdim=True))
+            alpha = npu_exp(m - m_new)
+            p = npu_exp(qk - m_new)
+            l = l * alpha + p.sum(dim=3, keepdim=True)
+            acc = acc * alpha + f32(p.to(torch.bfloat16)) @ vb
+            m = m_new
+        out[:, :, qb * bq:(qb + 1) * bq, :] = (acc / l).to(torch.bfloat16)
+    return out.reshape(-1)
+
+
+def rope_tables(tokens, dim=128, theta=1.0e6):
+    """cos/sin tables [tokens, dim] in fp32 for RoPE with base `theta` (the Qwen3 layer feeds them as the
+    fp32 inputs in_ptr2/in_ptr3 of 02/04)."""
+    inv = 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=torch.float64) / dim))
+    t = torch.arange(tokens, dtype=torch.float64)
+    f = torch.outer(t, inv)
+    emb = torch.cat([f, f], dim=1)
+    return emb.cos().to(torch.float32).reshape(-1), emb.sin().to(torch.float32).reshape(-1)
+
+
+def decoder_layer(x, p, T, hidden=4096, hq=32, hkv=8, dim=128, inter=12288, eps=1e-6, cos=None, sin=None,
+                  bq=1024, bkv=1024):
+    """The Qwen3-8B-shaped prefill layer as the 14 launches of validation/pytorchsim/
+    qwen3_8b_layer_prefill_2048x2048_bf16/manifest.json run it: RMSNorm, q/k/v projections, QK-RMSNorm +
+    RoPE into head-major q/k, v relayout, causal GQA attention, head -> token relayout, o projection +
+    residual, RMSNorm, gate_up projection, SiLU * mul, down projection + residual.  `p` holds the weights
+    (bf16, [in, out] row-major as the bundle feeds them)."""
+    h = rmsnorm_rows(x, p["ln1"], T, hidden, eps)
+    q = gemm(h, p["wq"], T, hq * dim, hidden)
+    k = gemm(h, p["wk"], T, hkv * dim, hidden)
+    v = gemm(h, p["wv"], T, hkv * dim, hidden)
+    qh = qknorm_rope(q, p["qn"], cos, sin, T, hq, eps, dim)
+    kh = qknorm_rope(k, p["kn"], cos, sin, T, hkv, eps, dim)
+    vh = token_to_head_major(v, T, hkv, dim)
+    bq_, bkv_ = min(bq, T), min(bkv, T)
+    o = attention_prefill(qh, kh, vh, 1, hq, hq // hkv, T, dim, bq_, bkv_, True, 1.0 / math.sqrt(dim))
+    ot = heads_to_token_major(o, T, hq, dim)
+    x1 = gemm(ot, p["wo"], T, hidden, hq * dim, residual=x)
+    h2 = rmsnorm_rows(x1, p["ln2"], T, hidden, eps)
+    gu = gemm(h2, p["wgu"], T, 2 * inter, hidden)
+    a = silu_mul(gu, T, inter)
+    return gemm(a, p["wd"], T, hidden, inter, residual=x1)

@@ -1,0 +1,301 @@
+// Causal GQA flash-attention forward on the tensor core: the attention_prefill_* / Qwen3 06 program of
+// the validation bundle (validation/pytorchsim/attention_prefill_32x8x4096_bf16/00__prefill_kernel/
+// _prefill_kernel_triton.py:3-44).  Per query row: m = -1e30, l = 0, acc = 0; per key block
+// qk = (q . k^T) * SCALE in fp32 (masked to -1e30 above the diagonal), m' = max(m, rowmax qk),
+// alpha = exp(m - m'), p = exp(qk - m'), l = l * alpha + rowsum p, acc = acc * alpha + bf16(p) . v;
+// out = bf16(acc / l).  exp is 2^(x * log2 e) as the NPU's EUP computes it.
+//
+// One CTA per (batch, query head, 128-row query tile), heaviest (most key tiles) first.  Roles:
+//   warp 0      TMA: the Q tile once, then K and V tiles of 128 keys into a two-deep ring;
+//   warp 1      TMEM owner + MMA issuer: S_j = Q . K_j^T (M=128 N=128 K=128) into one of two TMEM S
+//               buffers, then O += P_j . V_j (M=128 N=128 K=128) into the TMEM O accumulator; S_{j+1}
+//               is issued before PV_j so the softmax of tile j+1 overlaps PV_j;
+//   warps 2..5  softmax/correction: one query row per thread -- tcgen05.ld of S, row max / exp / row sum
+//               in fp32 registers, P rounded to bf16 into 128B-swizzled shared memory, O rescaled in
+//               TMEM by alpha (skipped when a whole warp has alpha == 1), finally O / l stored as bf16.
+#pragma once
+#include "sm100.cuh"
+#include "gemm.cuh"
+#include <initializer_list>
+
+namespace ptsim {
+
+constexpr int kAttnBM = 128;   // query rows per CTA
+constexpr int kAttnBN = 128;   // keys per tile
+constexpr int kAttnD = 128;    // head dim
+constexpr int kAttnThreads = 192;
+constexpr int kAttnTile = kAttnBM * kAttnD * 2;  // 32 KB: a [128 x 128] bf16 tile as two 16 KB swizzled halves
+constexpr int kAttnSmem = 6 * kAttnTile + 1024 + 256;  // Q, K x2, V x2, P
+
+struct AttnArgs {
+  CUtensorMap tq, tk, tv;  // [rows, 128] bf16, box {64, 128}
+  uint16_t *o;
+  int64_t hq, hkv, seq;
+  int32_t q_tiles, causal;
+  int64_t unit_begin, unit_end;  // (batch, head) units of this launch
+  float scale;
+};
+
+// Store 128 bf16 values of row r of a [128 x 128] K-major operand tile (two 64-column halves, each
+// 128 rows x 128 B with the 128-byte swizzle: 16-byte unit u of row r lands at unit u ^ (r % 8)).
+__device__ __forceinline__ void store_sw128_row(uint8_t *tile, int r, const uint32_t (&packed)[64]) {
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    uint8_t *base = tile + c * 16384 + r * 128;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int w = c * 32 + u * 4;
+      *reinterpret_cast<uint4 *>(base + ((u ^ (r & 7)) << 4)) = make_uint4(packed[w], packed[w + 1], packed[w + 2], packed[w + 3]);
+    }
+  }
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_constant__ AttnArgs g) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sQ = smem;
+  uint8_t *sK = smem + kAttnTile;       // 2 stages
+  uint8_t *sV = smem + 3 * kAttnTile;   // 2 stages
+  uint8_t *sP = smem + 5 * kAttnTile;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 6 * kAttnTile);
+  uint64_t *q_full = bars + 0;
+  uint64_t *k_full = bars + 1;    // 2
+  uint64_t *v_full = bars + 3;    // 2
+  uint64_t *kv_empty = bars + 5;  // 2
+  uint64_t *s_full = bars + 7;    // 2
+  uint64_t *p_full = bars + 9;
+  uint64_t *pv_done = bars + 10;
+  uint64_t *drain = bars + 11;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Work item: heaviest query tiles first.
+  const int64_t units = g.unit_end - g.unit_begin;
+  const int64_t item = blockIdx.x;
+  const int qt = g.q_tiles - 1 - int(item / units);
+  const int64_t unit = g.unit_begin + item % units;  // b * hq + h
+  const int64_t b = unit / g.hq, h = unit % g.hq;
+  const int64_t kvh = b * g.hkv + h / (g.hq / g.hkv);
+  const int q_row0 = int(unit * g.seq + int64_t(qt) * kAttnBM);
+  const int kv_row0 = int(kvh * g.seq);
+  const int nkv = g.causal ? qt + 1 : int(g.seq / kAttnBN);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 12; ++i) sm100::mbar_init(&bars[i], i == 9 ? 4u : 1u);  // p_full: one per softmax warp
+    *abort_flag = 0;
+    sm100::fence_barrier_init();
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(tmem_slot, 512);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS0 = tmem, tO = tmem + 256;  // S buffers at columns [0,128) and [128,256); O at [256,384)
+
+  if (warp == 0) {
+    if (lane == 0) {
+      sm100::mbar_arrive_expect_tx(q_full, kAttnTile);
+      sm100::tma_load_2d(sQ, &g.tq, q_full, 0, q_row0);
+      sm100::tma_load_2d(sQ + 16384, &g.tq, q_full, 64, q_row0);
+      for (int j = 0; j < nkv; ++j) {
+        const int st = j & 1;
+        if (!sm100::mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1)) { *abort_flag = 1; break; }
+        const int kr = kv_row0 + j * kAttnBN;
+        sm100::mbar_arrive_expect_tx(&k_full[st], kAttnTile);
+        sm100::tma_load_2d(sK + st * kAttnTile, &g.tk, &k_full[st], 0, kr);
+        sm100::tma_load_2d(sK + st * kAttnTile + 16384, &g.tk, &k_full[st], 64, kr);
+        sm100::mbar_arrive_expect_tx(&v_full[st], kAttnTile);
+        sm100::tma_load_2d(sV + st * kAttnTile, &g.tv, &v_full[st], 0, kr);
+        sm100::tma_load_2d(sV + st * kAttnTile + 16384, &g.tv, &v_full[st], 64, kr);
+      }
+      // Copies in flight land before exit: wait on the last fill of each stage.
+      for (int j = nkv - 2 < 0 ? 0 : nkv - 2; j < nkv && *abort_flag; ++j) {
+        sm100::mbar_wait(&k_full[j & 1], (j >> 1) & 1);
+        sm100::mbar_wait(&v_full[j & 1], (j >> 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = sm100::idesc_bf16_f32(kAttnBM, kAttnBN, false, false);
+      constexpr uint32_t idesc_o = sm100::idesc_bf16_f32(kAttnBM, kAttnD, false, true);
+      const uint32_t q_addr = sm100::smem_u32(sQ), p_addr = sm100::smem_u32(sP);
+      bool ok = sm100::mbar_wait(q_full, 0);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!sm100::mbar_wait(&k_full[st], (j >> 1) & 1)) return false;
+        sm100::tc_fence_after();
+        const uint32_t k_addr = sm100::smem_u32(sK + st * kAttnTile);
+#pragma unroll
+        for (int k = 0; k < kAttnD / 16; ++k) {
+          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
+          sm100::mma_bf16_ss(tS0 + st * 128, sm100::sw128_desc(q_addr + off, 16, 1024),
+                             sm100::sw128_desc(k_addr + off, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
+        }
+        sm100::mma_commit(&s_full[st]);
+        return true;
+      };
+      auto issue_pv = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!sm100::mbar_wait(p_full, j & 1)) return false;
+        if (!sm100::mbar_wait(&v_full[st], (j >> 1) & 1)) return false;
+        sm100::tc_fence_after();
+        const uint32_t v_addr = sm100::smem_u32(sV + st * kAttnTile);
+#pragma unroll
+        for (int k = 0; k < kAttnBN / 16; ++k) {
+          const uint32_t aoff = (k >> 2) * 16384 + (k & 3) * 32;
+          sm100::mma_bf16_ss(tO, sm100::sw128_desc(p_addr + aoff, 16, 1024),
+                             sm100::sw128_desc(v_addr + k * 16 * 128, 16384, 1024), idesc_o,
+                             (j > 0 || k > 0) ? 1u : 0u);
+        }
+        sm100::mma_commit(pv_done);
+        sm100::mma_commit(&kv_empty[st]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 1; ok && j < nkv; ++j) {
+        ok = issue_s(j);
+        if (ok) ok = issue_pv(j - 1);
+      }
+      if (ok) ok = issue_pv(nkv - 1);
+      if (!ok) *abort_flag = 1;
+      sm100::mma_commit(drain);
+      sm100::mbar_wait(drain, 0);
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // query row within the tile = TMEM lane
+    const uint32_t lane_off = uint32_t(quarter * 32) << 16;
+    const float sl2 = g.scale;
+    const float kLog2e = 1.4426950408889634f;
+    float m = -1.0e30f, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      const int st = j & 1;
+      if (*abort_flag || !sm100::mbar_wait(&s_full[st], (j >> 1) & 1)) { ok = false; break; }
+      sm100::tc_fence_after();
+      float s[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        sm100::tmem_ld32(tS0 + st * 128 + lane_off + c * 32, v);
+        sm100::tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < 32; ++q) s[c * 32 + q] = __fmul_rn(__uint_as_float(v[q]), sl2);
+      }
+      const bool diag = g.causal && j == qt;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int q = 0; q < 128; ++q) {
+        if (diag && q > r) s[q] = -1.0e30f;
+        mx = fmaxf(mx, s[q]);
+      }
+      const float m_new = fmaxf(m, mx);
+      const float alpha = exp2f(__fmul_rn(__fsub_rn(m, m_new), kLog2e));
+      float rs = 0.f;
+      uint32_t pk[64];
+#pragma unroll
+      for (int q = 0; q < 64; ++q) {
+        const float p0 = exp2f(__fmul_rn(__fsub_rn(s[2 * q], m_new), kLog2e));
+        const float p1 = exp2f(__fmul_rn(__fsub_rn(s[2 * q + 1], m_new), kLog2e));
+        rs = __fadd_rn(__fadd_rn(rs, p0), p1);
+        pk[q] = pack_bf16x2(p0, p1);
+      }
+      l = __fadd_rn(__fmul_rn(l, alpha), rs);
+      m = m_new;
+      if (j > 0) {
+        // PV_{j-1} has finished: the P buffer is free and O holds every earlier tile.
+        if (!sm100::mbar_wait(pv_done, (j - 1) & 1)) { ok = false; break; }
+        sm100::tc_fence_after();
+      }
+      store_sw128_row(sP, r, pk);
+      fence_proxy_async_smem();
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          sm100::tmem_ld32(tO + lane_off + c * 32, v);
+          sm100::tmem_wait_ld();
+#pragma unroll
+          for (int q = 0; q < 32; ++q) v[q] = __float_as_uint(__fmul_rn(__uint_as_float(v[q]), alpha));
+          uint32_t lo16[16], hi16[16];
+#pragma unroll
+          for (int q = 0; q < 16; ++q) { lo16[q] = v[q]; hi16[q] = v[16 + q]; }
+          sm100::tmem_st16(tO + lane_off + c * 32, lo16);
+          sm100::tmem_st16(tO + lane_off + c * 32 + 16, hi16);
+        }
+        sm100::tmem_wait_st();
+      }
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(p_full);
+    }
+    if (ok && !*abort_flag && sm100::mbar_wait(pv_done, (nkv - 1) & 1)) {
+      sm100::tc_fence_after();
+      const float inv_l = l;  // divide, as the program does (acc / l)
+      uint16_t *orow = g.o + (int64_t(q_row0) + r) * kAttnD;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        sm100::tmem_ld32(tO + lane_off + c * 32, v);
+        sm100::tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 w;
+          w.x = pack_bf16x2(__fdiv_rn(__uint_as_float(v[q * 8 + 0]), inv_l), __fdiv_rn(__uint_as_float(v[q * 8 + 1]), inv_l));
+          w.y = pack_bf16x2(__fdiv_rn(__uint_as_float(v[q * 8 + 2]), inv_l), __fdiv_rn(__uint_as_float(v[q * 8 + 3]), inv_l));
+          w.z = pack_bf16x2(__fdiv_rn(__uint_as_float(v[q * 8 + 4]), inv_l), __fdiv_rn(__uint_as_float(v[q * 8 + 5]), inv_l));
+          w.w = pack_bf16x2(__fdiv_rn(__uint_as_float(v[q * 8 + 6]), inv_l), __fdiv_rn(__uint_as_float(v[q * 8 + 7]), inv_l));
+          reinterpret_cast<uint4 *>(orow + c * 32)[q] = w;
+        }
+      }
+    } else {
+      *abort_flag = 1;
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, 512);
+  }
+}
+
+int launch_attention(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c) {
+  const ptsim_attn_params &a = d.p.attn;
+  if (a.dim != kAttnD) return fail(PTSIM_E_UNSUPPORTED, "attention runs head_dim 128, not %lld", (long long)a.dim);
+  if (a.seq % kAttnBM != 0) return fail(PTSIM_E_UNSUPPORTED, "attention sequence %lld is not a multiple of 128", (long long)a.seq);
+  for (int t : {a.q_arg, a.k_arg, a.v_arg, a.o_arg})
+    if (d.arg_dtype[t] != PTSIM_DT_BF16) return fail(PTSIM_E_UNSUPPORTED, "attention tensors must be bf16");
+  // Units are (batch, query head) pairs.
+  const int64_t u0 = lo * d.unit_size, u1 = hi * d.unit_size < a.batch * a.hq ? hi * d.unit_size : a.batch * a.hq;
+  if (u1 <= u0) return PTSIM_OK;
+  AttnArgs g;
+  memset(&g, 0, sizeof(g));
+  int rc;
+  if ((rc = make_tmap_2d(&g.tq, ptrs[a.q_arg], 128, uint64_t(a.batch * a.hq * a.seq), 128, 64, 128))) return rc;
+  if ((rc = make_tmap_2d(&g.tk, ptrs[a.k_arg], 128, uint64_t(a.batch * a.hkv * a.seq), 128, 64, 128))) return rc;
+  if ((rc = make_tmap_2d(&g.tv, ptrs[a.v_arg], 128, uint64_t(a.batch * a.hkv * a.seq), 128, 64, 128))) return rc;
+  g.o = reinterpret_cast<uint16_t *>(ptrs[a.o_arg]);
+  g.hq = a.hq;
+  g.hkv = a.hkv;
+  g.seq = a.seq;
+  g.q_tiles = int(a.seq / kAttnBM);
+  g.causal = a.causal;
+  g.unit_begin = u0;
+  g.unit_end = u1;
+  g.scale = a.scale;
+  if (int64_t(a.batch * a.hkv * a.seq) >= (int64_t(1) << 31)) return fail(PTSIM_E_UNSUPPORTED, "attention rows exceed int32");
+  PTSIM_CUDA(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
+  const int64_t grid = (u1 - u0) * g.q_tiles;
+  attn_fwd_kernel<<<unsigned(grid), kAttnThreads, kAttnSmem, c.stream>>>(g);
+  PTSIM_CUDA(cudaGetLastError());
+  return PTSIM_OK;
+}
+
+}  // namespace ptsim

@@ -1,0 +1,99 @@
+// Shared device/host helpers of the B200 executor: element conversions with the NPU's rounding rules,
+// the per-device status word kernels report failures through, and bounded waits.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/ptsim_b200.h"
+
+namespace ptsim {
+
+// ---------------------------------------------------------------------------------------------------
+// Status word.  A kernel that detects an out-of-bounds index or a wait that never completes records a
+// PTSIM_E_* code here (first one wins) and returns; the host reads and clears it in ptsim_sync.  This is
+// the GPU analogue of the reference's Spike trap exit codes (runtime/spike.py:12).
+// ---------------------------------------------------------------------------------------------------
+__device__ int g_status = 0;  // one translation unit: defined here
+
+__device__ __forceinline__ void record_status(int code) { atomicCAS(&g_status, 0, code); }
+
+// Iteration cap of every spin-wait on an mbarrier or flag: far above any legitimate wait of these
+// kernels (a few microseconds), far below a watchdog.  A wait that reaches it records PTSIM_E_TIMEOUT.
+constexpr uint32_t kSpinLimit = 1u << 26;
+
+// ---------------------------------------------------------------------------------------------------
+// bf16 <-> fp32.  Widening is exact (bits << 16).  Narrowing rounds to nearest, ties to even, and keeps
+// NaN a quiet NaN: the NPU's misc.pack (PyTorchSimTpuOps.td:46-50) and torch's .to(bfloat16).
+// ---------------------------------------------------------------------------------------------------
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) { return __uint_as_float(uint32_t(b) << 16); }
+
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+// Two packed bf16 (lo in bits 0-15) from two floats, RNE.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&v);
+}
+
+__device__ __forceinline__ float lo_bf16(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float hi_bf16(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// exp as the EUP computes it: 2^(x * log2(e)) (targets/tpu/lower_vector_functions.py:310-329).
+__device__ __forceinline__ float npu_exp(float x) { return exp2f(x * 1.4426950408889634f); }
+
+// NaN-propagating max/min (the vmax/vmin rule of PyTorchSimTpuOps.td:64-74; tl.PropagateNan.ALL).
+__device__ __forceinline__ float nan_max(float a, float b) {
+  return (a != a || b != b) ? __int_as_float(0x7fc00000) : fmaxf(a, b);
+}
+__device__ __forceinline__ float nan_min(float a, float b) {
+  return (a != a || b != b) ? __int_as_float(0x7fc00000) : fminf(a, b);
+}
+
+__host__ __device__ __forceinline__ int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Element size in bytes of a PTSIM_DT_* type.
+__host__ __device__ __forceinline__ int dtype_size(int dt) {
+  switch (dt) {
+    case PTSIM_DT_F32: case PTSIM_DT_I32: return 4;
+    case PTSIM_DT_BF16: case PTSIM_DT_F16: case PTSIM_DT_I16: return 2;
+    case PTSIM_DT_I64: case PTSIM_DT_F64: return 8;
+    case PTSIM_DT_I8: case PTSIM_DT_U8: return 1;
+  }
+  return 0;
+}
+
+// ---------------------------------------------------------------------------------------------------
+// Host-side launch helpers.
+// ---------------------------------------------------------------------------------------------------
+struct LaunchCtx {
+  cudaStream_t stream;
+  int device;
+  int sm_count;
+};
+
+// Sets the thread's last error message (printf-style) and returns `code`.
+int fail(int code, const char *fmt, ...);
+
+// Checks a CUDA call's result; on failure records the message and returns PTSIM_E_CUDA.
+#define PTSIM_CUDA(call)                                                                   \
+  do {                                                                                     \
+    cudaError_t _e = (call);                                                               \
+    if (_e != cudaSuccess)                                                                 \
+      return ::ptsim::fail(PTSIM_E_CUDA, "%s failed: %s (%s:%d)", #call,                   \
+                           cudaGetErrorString(_e), __FILE__, __LINE__);                    \
+  } while (0)
+
+// Per-kind launchers (each validates what only it knows and enqueues its kernels).
+int launch_elementwise(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c);
+int launch_rowops(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c);
+int launch_qkrope(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c);
+int launch_reduce(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, void *ws, size_t ws_bytes,
+                  const LaunchCtx &c);
+int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c);
+int launch_attention(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c);
+
+}  // namespace ptsim

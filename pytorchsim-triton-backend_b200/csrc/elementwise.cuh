@@ -1,0 +1,296 @@
+// ELEMENTWISE tile programs: DMA loads at affine index maps, a short vector-unit program in fp32
+// registers, one DMA store.  This is what the NPU runs for every Inductor pointwise kernel of the
+// validation bundle (vector_add1_*, the Qwen3 layer's relayout copies 05/07 and SiLU-mul 10, tests/cases
+// smoke/add.py): per program, MVIN of each operand box (targets/tpu/lower_dma.py:466-492), RVV/EUP ops
+// (passes/utils/math_ops.py:10-16, lower_vector_functions.py), MVOUT of the result (lower_dma.py:17).
+//
+// B200 mapping: the flat index space [begin, end) of the store is cut into groups of 8 consecutive
+// indices, one group per thread per grid-stride step.  An operand whose innermost index digit is
+// contiguous is fetched with one 16-byte (bf16) or two 16-byte (fp32) vector loads per group; any
+// other map gathers element by element.  The program is decoded once per group (uniform across the
+// warp), so the per-element cost is the arithmetic itself.  A pure copy moves raw bits (bit exact).
+#pragma once
+#include "common.cuh"
+
+namespace ptsim {
+
+struct EwLaunch {
+  ptsim_ew_params p;
+  const void *ptr[PTSIM_MAX_ARGS];
+  int64_t numel[PTSIM_MAX_ARGS];
+  int32_t dtype[PTSIM_MAX_ARGS];
+  int32_t vec[PTSIM_MAX_MAPS];  // 1: the map is contiguous over every aligned group of 8 indices
+  int64_t begin, end;
+};
+
+__device__ __forceinline__ int64_t map_index(const ptsim_map &m, int64_t i) {
+  int64_t idx = m.offset;
+#pragma unroll
+  for (int d = 0; d < PTSIM_MAX_DIGITS; ++d)
+    if (d < m.ndigit) idx += ((i / m.div[d]) % m.mod[d]) * m.stride[d];
+  return idx;
+}
+
+__device__ __forceinline__ float load_elem(const void *p, int dt, int64_t idx) {
+  switch (dt) {
+    case PTSIM_DT_F32: return __ldg(reinterpret_cast<const float *>(p) + idx);
+    case PTSIM_DT_BF16: return bf16_bits_to_f32(__ldg(reinterpret_cast<const unsigned short *>(p) + idx));
+    case PTSIM_DT_F16: return __half2float(__ldg(reinterpret_cast<const __half *>(p) + idx));
+    case PTSIM_DT_I32: return float(__ldg(reinterpret_cast<const int *>(p) + idx));
+    case PTSIM_DT_I64: return float(__ldg(reinterpret_cast<const long long *>(p) + idx));
+    case PTSIM_DT_I16: return float(__ldg(reinterpret_cast<const short *>(p) + idx));
+    case PTSIM_DT_I8: return float(reinterpret_cast<const signed char *>(p)[idx]);
+    case PTSIM_DT_U8: return float(reinterpret_cast<const unsigned char *>(p)[idx]);
+    case PTSIM_DT_F64: return float(__ldg(reinterpret_cast<const double *>(p) + idx));
+  }
+  return 0.f;
+}
+
+__device__ __forceinline__ void store_elem(void *p, int dt, int64_t idx, float v) {
+  switch (dt) {
+    case PTSIM_DT_F32: reinterpret_cast<float *>(p)[idx] = v; break;
+    case PTSIM_DT_BF16: reinterpret_cast<unsigned short *>(p)[idx] = f32_to_bf16_bits(v); break;
+    case PTSIM_DT_F16: reinterpret_cast<__half *>(p)[idx] = __float2half_rn(v); break;
+    case PTSIM_DT_I32: reinterpret_cast<int *>(p)[idx] = int(v); break;
+    case PTSIM_DT_I64: reinterpret_cast<long long *>(p)[idx] = (long long)(v); break;
+    case PTSIM_DT_I16: reinterpret_cast<short *>(p)[idx] = short(v); break;
+    case PTSIM_DT_I8: reinterpret_cast<signed char *>(p)[idx] = (signed char)(v); break;
+    case PTSIM_DT_U8: reinterpret_cast<unsigned char *>(p)[idx] = (unsigned char)(v); break;
+    case PTSIM_DT_F64: reinterpret_cast<double *>(p)[idx] = double(v); break;
+  }
+}
+
+// 8 operand values of group i0 (n valid) through map m.
+__device__ __forceinline__ void load8(const EwLaunch &L, int mi, int64_t i0, int n, float v[8]) {
+  const ptsim_map &m = L.p.map[mi];
+  const void *p = L.ptr[m.arg];
+  const int dt = L.dtype[m.arg];
+  if (n == 8 && L.vec[mi]) {
+    const int64_t base = map_index(m, i0);
+    if (base < 0 || base + 8 > L.numel[m.arg]) { record_status(PTSIM_E_OOB); for (int k = 0; k < 8; ++k) v[k] = 0.f; return; }
+    if (dt == PTSIM_DT_BF16) {
+      uint4 w = __ldg(reinterpret_cast<const uint4 *>(reinterpret_cast<const unsigned short *>(p) + base));
+      v[0] = lo_bf16(w.x); v[1] = hi_bf16(w.x); v[2] = lo_bf16(w.y); v[3] = hi_bf16(w.y);
+      v[4] = lo_bf16(w.z); v[5] = hi_bf16(w.z); v[6] = lo_bf16(w.w); v[7] = hi_bf16(w.w);
+      return;
+    }
+    if (dt == PTSIM_DT_F32) {
+      const float4 *q = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(p) + base);
+      float4 a = __ldg(q), b = __ldg(q + 1);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      return;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    v[k] = 0.f;
+    if (k < n) {
+      const int64_t idx = map_index(m, i0 + k);
+      if (idx < 0 || idx >= L.numel[m.arg]) { record_status(PTSIM_E_OOB); continue; }
+      v[k] = load_elem(p, dt, idx);
+    }
+  }
+}
+
+__device__ __forceinline__ void store8(const EwLaunch &L, int64_t i0, int n, const float v[8]) {
+  const ptsim_map &m = L.p.map[L.p.store_map];
+  void *p = const_cast<void *>(L.ptr[m.arg]);
+  const int dt = L.dtype[m.arg];
+  if (n == 8 && L.vec[L.p.store_map]) {
+    const int64_t base = map_index(m, i0);
+    if (base < 0 || base + 8 > L.numel[m.arg]) { record_status(PTSIM_E_OOB); return; }
+    if (dt == PTSIM_DT_BF16) {
+      uint4 w;
+      w.x = pack_bf16x2(v[0], v[1]); w.y = pack_bf16x2(v[2], v[3]);
+      w.z = pack_bf16x2(v[4], v[5]); w.w = pack_bf16x2(v[6], v[7]);
+      *reinterpret_cast<uint4 *>(reinterpret_cast<unsigned short *>(p) + base) = w;
+      return;
+    }
+    if (dt == PTSIM_DT_F32) {
+      float4 *q = reinterpret_cast<float4 *>(reinterpret_cast<float *>(p) + base);
+      q[0] = make_float4(v[0], v[1], v[2], v[3]);
+      q[1] = make_float4(v[4], v[5], v[6], v[7]);
+      return;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    if (k < n) {
+      const int64_t idx = map_index(m, i0 + k);
+      if (idx < 0 || idx >= L.numel[m.arg]) { record_status(PTSIM_E_OOB); continue; }
+      store_elem(p, dt, idx, v[k]);
+    }
+  }
+}
+
+// Register file access with static indices only, so the 8 x 8 register file stays in registers.
+#define PTSIM_REG_CASES(X) X(0) X(1) X(2) X(3) X(4) X(5) X(6) X(7)
+
+__device__ __forceinline__ void reg_read(const float (&r)[PTSIM_MAX_REGS][8], int i, float v[8]) {
+  switch (i) {
+#define PTSIM_RD(c) case c: _Pragma("unroll") for (int k = 0; k < 8; ++k) v[k] = r[c][k]; break;
+    PTSIM_REG_CASES(PTSIM_RD)
+#undef PTSIM_RD
+  }
+}
+
+__device__ __forceinline__ void reg_write(float (&r)[PTSIM_MAX_REGS][8], int i, const float v[8]) {
+  switch (i) {
+#define PTSIM_WR(c) case c: _Pragma("unroll") for (int k = 0; k < 8; ++k) r[c][k] = v[k]; break;
+    PTSIM_REG_CASES(PTSIM_WR)
+#undef PTSIM_WR
+  }
+}
+
+__global__ void __launch_bounds__(256) ew_program_kernel(const __grid_constant__ EwLaunch L) {
+  const int64_t groups = ceil_div(L.end - L.begin, 8);
+  float r[PTSIM_MAX_REGS][8];
+#pragma unroll
+  for (int a = 0; a < PTSIM_MAX_REGS; ++a)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) r[a][k] = 0.f;
+  for (int64_t g = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; g < groups; g += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t i0 = L.begin + g * 8;
+    const int n = int((L.end - i0) < 8 ? (L.end - i0) : 8);
+    for (int pc = 0; pc < L.p.ncode; ++pc) {
+      const ptsim_insn in = L.p.code[pc];
+      float x[8], y[8];
+      switch (in.op) {
+        case PTSIM_OP_LOAD: load8(L, in.a, i0, n, x); reg_write(r, in.dst, x); break;
+        case PTSIM_OP_CONST:
+#pragma unroll
+          for (int k = 0; k < 8; ++k) x[k] = in.imm;
+          reg_write(r, in.dst, x);
+          break;
+        case PTSIM_OP_STORE: reg_read(r, in.a, x); store8(L, i0, n, x); break;
+        default: {
+          reg_read(r, in.a, x);
+          reg_read(r, in.b, y);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            float a = x[k], b = y[k], o = 0.f;
+            switch (in.op) {
+              case PTSIM_OP_ADD: o = __fadd_rn(a, b); break;
+              case PTSIM_OP_SUB: o = __fsub_rn(a, b); break;
+              case PTSIM_OP_MUL: o = __fmul_rn(a, b); break;
+              case PTSIM_OP_DIV: o = __fdiv_rn(a, b); break;
+              case PTSIM_OP_NEG: o = -a; break;
+              case PTSIM_OP_EXP: o = npu_exp(a); break;
+              case PTSIM_OP_RSQRT: o = rsqrtf(a); break;
+              case PTSIM_OP_SQRT: o = __fsqrt_rn(a); break;
+              case PTSIM_OP_MAX: o = nan_max(a, b); break;
+              case PTSIM_OP_MIN: o = nan_min(a, b); break;
+              case PTSIM_OP_RBF16: o = bf16_bits_to_f32(f32_to_bf16_bits(a)); break;
+              case PTSIM_OP_ABS: o = fabsf(a); break;
+            }
+            x[k] = o;
+          }
+          reg_write(r, in.dst, x);
+        }
+      }
+    }
+  }
+}
+
+// Pure copy: the loaded element's bytes go to the store unchanged (bit exact for every dtype).
+template <int ESIZE>
+__global__ void __launch_bounds__(256) ew_copy_kernel(const __grid_constant__ EwLaunch L) {
+  using T = typename std::conditional<ESIZE == 1, uint8_t,
+            typename std::conditional<ESIZE == 2, uint16_t,
+            typename std::conditional<ESIZE == 4, uint32_t, uint64_t>::type>::type>::type;
+  const ptsim_map &src = L.p.map[0];
+  const ptsim_map &dst = L.p.map[L.p.store_map];
+  const T *sp = reinterpret_cast<const T *>(L.ptr[src.arg]);
+  T *dp = reinterpret_cast<T *>(const_cast<void *>(L.ptr[dst.arg]));
+  const int64_t groups = ceil_div(L.end - L.begin, 8);
+  const bool vs = L.vec[0] && ESIZE == 2, vd = L.vec[L.p.store_map] && ESIZE == 2;
+  for (int64_t g = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; g < groups; g += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t i0 = L.begin + g * 8;
+    const int n = int((L.end - i0) < 8 ? (L.end - i0) : 8);
+    T v[8];
+    if (n == 8 && vs) {
+      const int64_t b = map_index(src, i0);
+      if (b < 0 || b + 8 > L.numel[src.arg]) { record_status(PTSIM_E_OOB); continue; }
+      *reinterpret_cast<uint4 *>(v) = __ldg(reinterpret_cast<const uint4 *>(sp + b));
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        v[k] = 0;
+        if (k < n) {
+          const int64_t idx = map_index(src, i0 + k);
+          if (idx < 0 || idx >= L.numel[src.arg]) { record_status(PTSIM_E_OOB); continue; }
+          v[k] = sp[idx];
+        }
+      }
+    }
+    if (n == 8 && vd) {
+      const int64_t b = map_index(dst, i0);
+      if (b < 0 || b + 8 > L.numel[dst.arg]) { record_status(PTSIM_E_OOB); continue; }
+      *reinterpret_cast<uint4 *>(dp + b) = *reinterpret_cast<uint4 *>(v);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (k < n) {
+          const int64_t idx = map_index(dst, i0 + k);
+          if (idx < 0 || idx >= L.numel[dst.arg]) { record_status(PTSIM_E_OOB); continue; }
+          dp[idx] = v[k];
+        }
+      }
+    }
+  }
+}
+
+// Whether map m addresses 8 consecutive elements from a 16-byte aligned start for every group of 8
+// flat indices that starts at a multiple of 8.
+static bool map_vectorizable(const ptsim_map &m, int dt, const void *ptr) {
+  if (m.ndigit < 1) return false;
+  if (m.div[0] != 1 || m.stride[0] != 1 || m.mod[0] % 8 != 0) return false;
+  for (int d = 1; d < m.ndigit; ++d) {
+    if (m.div[d] % 8 != 0) return false;                       // higher digits constant over a group
+    if ((m.stride[d] * dtype_size(dt)) % 16 != 0) return false; // each group starts 16-byte aligned
+  }
+  if ((m.offset * dtype_size(dt)) % 16 != 0) return false;
+  if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) return false;
+  return dt == PTSIM_DT_BF16 || dt == PTSIM_DT_F32 || (dt == PTSIM_DT_F16);
+}
+
+int launch_elementwise(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c) {
+  EwLaunch L;
+  memset(&L, 0, sizeof(L));
+  L.p = d.p.ew;
+  for (int a = 0; a < d.nargs; ++a) {
+    L.ptr[a] = ptrs[a];
+    L.numel[a] = d.arg_numel[a];
+    L.dtype[a] = d.arg_dtype[a];
+  }
+  L.begin = lo * d.unit_size;
+  L.end = hi * d.unit_size < d.p.ew.numel ? hi * d.unit_size : d.p.ew.numel;
+  if (L.end <= L.begin) return PTSIM_OK;
+  const bool aligned = (L.begin % 8) == 0;
+  for (int m = 0; m < L.p.nmap; ++m) {
+    const int dt = d.arg_dtype[L.p.map[m].arg];
+    L.vec[m] = aligned && map_vectorizable(L.p.map[m], dt, ptrs[L.p.map[m].arg]) ? 1 : 0;
+    if (dt == PTSIM_DT_F16 && L.vec[m] && !L.p.pure_copy) L.vec[m] = 0;  // fp16 vector path: copy only
+  }
+  const int64_t groups = ceil_div(L.end - L.begin, 8);
+  const int threads = 256;
+  int64_t blocks = ceil_div(groups, threads);
+  const int64_t cap = int64_t(c.sm_count) * 8;
+  if (blocks > cap) blocks = cap;
+  if (L.p.pure_copy) {
+    const int es = dtype_size(d.arg_dtype[L.p.map[0].arg]);
+    switch (es) {
+      case 1: ew_copy_kernel<1><<<unsigned(blocks), threads, 0, c.stream>>>(L); break;
+      case 2: ew_copy_kernel<2><<<unsigned(blocks), threads, 0, c.stream>>>(L); break;
+      case 4: ew_copy_kernel<4><<<unsigned(blocks), threads, 0, c.stream>>>(L); break;
+      case 8: ew_copy_kernel<8><<<unsigned(blocks), threads, 0, c.stream>>>(L); break;
+      default: return fail(PTSIM_E_DESC, "elementwise copy of a %d-byte element", es);
+    }
+  } else {
+    ew_program_kernel<<<unsigned(blocks), threads, 0, c.stream>>>(L);
+  }
+  PTSIM_CUDA(cudaGetLastError());
+  return PTSIM_OK;
+}
+
+}  // namespace ptsim

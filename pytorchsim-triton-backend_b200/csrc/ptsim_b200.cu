@@ -1,0 +1,253 @@
+// The C ABI of libptsim_b200.so (declared in include/ptsim_b200.h): descriptor validation, per-device
+// setup, dispatch of a launch's unit range to the kernel of its tile-program class, and the status word.
+// Everything is one translation unit so the device status word needs no relocatable device code.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "elementwise.cuh"
+#include "rowops.cuh"
+#include "gemm.cuh"
+#include "attention.cuh"
+
+namespace ptsim {
+
+
+
+static thread_local char t_err[1024] = {0};
+
+int fail(int code, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_err, sizeof(t_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+struct DeviceInfo {
+  bool ready = false;
+  int sm_count = 0;
+  int major = 0, minor = 0;
+};
+static std::mutex g_dev_mu;
+static DeviceInfo g_dev[64];
+
+static int device_info(int dev, DeviceInfo *out) {
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (dev < 0 || dev >= 64) return fail(PTSIM_E_ARGS, "device %d out of range", dev);
+  if (!g_dev[dev].ready) {
+    cudaDeviceProp prop;
+    PTSIM_CUDA(cudaGetDeviceProperties(&prop, dev));
+    g_dev[dev].sm_count = prop.multiProcessorCount;
+    g_dev[dev].major = prop.major;
+    g_dev[dev].minor = prop.minor;
+    g_dev[dev].ready = true;
+  }
+  *out = g_dev[dev];
+  return PTSIM_OK;
+}
+
+static bool valid_dtype(int dt) { return dt >= PTSIM_DT_F32 && dt <= PTSIM_DT_F64; }
+
+static int check_arg(const ptsim_desc &d, int a, const char *what) {
+  if (a < 0 || a >= d.nargs) return fail(PTSIM_E_DESC, "%s refers to argument %d of %d", what, a, d.nargs);
+  return PTSIM_OK;
+}
+
+// Largest element offset map m reaches over flat indices [0, numel), for non-negative strides.
+static int64_t map_max_index(const ptsim_map &m, int64_t numel) {
+  int64_t hi = m.offset;
+  for (int d = 0; d < m.ndigit; ++d) {
+    int64_t top = (numel - 1) / m.div[d];
+    if (top > m.mod[d] - 1) top = m.mod[d] - 1;
+    hi += top * m.stride[d];
+  }
+  return hi;
+}
+
+static int check_desc(const void *p, size_t bytes) {
+  if (p == nullptr || bytes < sizeof(ptsim_desc))
+    return fail(PTSIM_E_DESC, "descriptor of %zu bytes; this library reads %zu", bytes, sizeof(ptsim_desc));
+  const ptsim_desc &d = *reinterpret_cast<const ptsim_desc *>(p);
+  if (d.magic != PTSIM_DESC_MAGIC) return fail(PTSIM_E_DESC, "descriptor magic 0x%08x is not PTSB", d.magic);
+  if (d.version != PTSIM_ABI_VERSION)
+    return fail(PTSIM_E_DESC, "descriptor ABI version %u, this library runs %d", d.version, PTSIM_ABI_VERSION);
+  if (d.nargs < 1 || d.nargs > PTSIM_MAX_ARGS) return fail(PTSIM_E_DESC, "descriptor names %d arguments", d.nargs);
+  for (int a = 0; a < d.nargs; ++a) {
+    if (!valid_dtype(d.arg_dtype[a])) return fail(PTSIM_E_DESC, "argument %d has dtype code %d", a, d.arg_dtype[a]);
+    if (d.arg_numel[a] < 0) return fail(PTSIM_E_DESC, "argument %d has %lld elements", a, (long long)d.arg_numel[a]);
+  }
+  if (d.units < 0 || d.unit_size < 1) return fail(PTSIM_E_DESC, "descriptor has %lld units of %lld", (long long)d.units, (long long)d.unit_size);
+  int rc = PTSIM_OK;
+  switch (d.kind) {
+    case PTSIM_KIND_ELEMENTWISE: {
+      const ptsim_ew_params &e = d.p.ew;
+      if (e.nmap < 1 || e.nmap > PTSIM_MAX_MAPS || e.ncode < 1 || e.ncode > PTSIM_MAX_CODE)
+        return fail(PTSIM_E_DESC, "elementwise program with %d maps and %d instructions", e.nmap, e.ncode);
+      if (e.store_map < 0 || e.store_map >= e.nmap) return fail(PTSIM_E_DESC, "store map %d of %d", e.store_map, e.nmap);
+      for (int m = 0; m < e.nmap; ++m) {
+        const ptsim_map &mp = e.map[m];
+        if ((rc = check_arg(d, mp.arg, "index map"))) return rc;
+        if (mp.ndigit < 0 || mp.ndigit > PTSIM_MAX_DIGITS) return fail(PTSIM_E_DESC, "map %d has %d digits", m, mp.ndigit);
+        for (int k = 0; k < mp.ndigit; ++k) {
+          if (mp.div[k] < 1 || mp.mod[k] < 1) return fail(PTSIM_E_DESC, "map %d digit %d divides by %lld mod %lld", m, k, (long long)mp.div[k], (long long)mp.mod[k]);
+          if (mp.stride[k] < 0) return fail(PTSIM_E_UNSUPPORTED, "map %d digit %d has a negative stride", m, k);
+        }
+        if (mp.offset < 0 || (e.numel > 0 && map_max_index(mp, e.numel) >= d.arg_numel[mp.arg]))
+          return fail(PTSIM_E_OOB, "index map %d reaches element %lld of argument %d, which holds %lld", m,
+                      (long long)map_max_index(mp, e.numel), mp.arg, (long long)d.arg_numel[mp.arg]);
+      }
+      for (int i = 0; i < e.ncode; ++i) {
+        const ptsim_insn &in = e.code[i];
+        if (in.op < PTSIM_OP_LOAD || in.op > PTSIM_OP_STORE) return fail(PTSIM_E_DESC, "instruction %d has opcode %d", i, in.op);
+        if (in.dst >= PTSIM_MAX_REGS || in.a >= PTSIM_MAX_REGS || in.b >= PTSIM_MAX_REGS)
+          return fail(PTSIM_E_DESC, "instruction %d names a register past %d", i, PTSIM_MAX_REGS);
+        if (in.op == PTSIM_OP_LOAD && in.a >= e.nmap) return fail(PTSIM_E_DESC, "instruction %d loads map %d", i, in.a);
+      }
+      break;
+    }
+    case PTSIM_KIND_ROW_SOFTMAX:
+    case PTSIM_KIND_ROW_RMSNORM: {
+      const ptsim_row_params &r = d.p.row;
+      if ((rc = check_arg(d, r.in_arg, "row input")) || (rc = check_arg(d, r.out_arg, "row output"))) return rc;
+      if (d.kind == PTSIM_KIND_ROW_RMSNORM && (rc = check_arg(d, r.weight_arg, "RMSNorm weight"))) return rc;
+      if (r.rows < 0 || r.cols < 1) return fail(PTSIM_E_DESC, "row program over %lld x %lld", (long long)r.rows, (long long)r.cols);
+      if (r.rows > 0) {
+        if ((r.rows - 1) * r.in_row_stride + r.cols > d.arg_numel[r.in_arg] ||
+            (r.rows - 1) * r.out_row_stride + r.cols > d.arg_numel[r.out_arg])
+          return fail(PTSIM_E_OOB, "row program reads or writes past its tensors");
+        if (d.kind == PTSIM_KIND_ROW_RMSNORM && r.cols > d.arg_numel[r.weight_arg])
+          return fail(PTSIM_E_OOB, "RMSNorm weight holds fewer than %lld values", (long long)r.cols);
+      }
+      break;
+    }
+    case PTSIM_KIND_QKNORM_ROPE: {
+      const ptsim_qkrope_params &q = d.p.qk;
+      if ((rc = check_arg(d, q.in_arg, "qk input")) || (rc = check_arg(d, q.weight_arg, "qk weight")) ||
+          (rc = check_arg(d, q.cos_arg, "cos")) || (rc = check_arg(d, q.sin_arg, "sin")) || (rc = check_arg(d, q.out_arg, "qk output")))
+        return rc;
+      if (q.tokens * q.heads * q.dim > d.arg_numel[q.in_arg] || q.tokens * q.dim > d.arg_numel[q.cos_arg] ||
+          q.tokens * q.dim > d.arg_numel[q.sin_arg] ||
+          (q.tokens > 0 && (q.tokens - 1) * q.out_tok_stride + (q.heads - 1) * q.out_head_stride + q.dim > d.arg_numel[q.out_arg]))
+        return fail(PTSIM_E_OOB, "QK-norm+RoPE reads or writes past its tensors");
+      if (d.arg_dtype[q.cos_arg] != PTSIM_DT_F32 || d.arg_dtype[q.sin_arg] != PTSIM_DT_F32 ||
+          d.arg_dtype[q.in_arg] != PTSIM_DT_BF16 || d.arg_dtype[q.out_arg] != PTSIM_DT_BF16 || d.arg_dtype[q.weight_arg] != PTSIM_DT_BF16)
+        return fail(PTSIM_E_UNSUPPORTED, "QK-norm+RoPE runs bf16 rows with fp32 cos/sin tables");
+      break;
+    }
+    case PTSIM_KIND_GEMM: {
+      const ptsim_gemm_params &g = d.p.gemm;
+      if ((rc = check_arg(d, g.a_arg, "A")) || (rc = check_arg(d, g.b_arg, "B")) || (rc = check_arg(d, g.c_arg, "C"))) return rc;
+      if (g.r_arg >= 0 && (rc = check_arg(d, g.r_arg, "residual"))) return rc;
+      if (g.M < 0 || g.N < 1 || g.K < 1) return fail(PTSIM_E_DESC, "GEMM %lldx%lldx%lld", (long long)g.M, (long long)g.N, (long long)g.K);
+      if (g.M > 0) {
+        const int64_t b_need = g.b_kmajor ? (g.N - 1) * g.ldb + g.K : (g.K - 1) * g.ldb + g.N;
+        if ((g.M - 1) * g.lda + g.K > d.arg_numel[g.a_arg] || b_need > d.arg_numel[g.b_arg] ||
+            (g.M - 1) * g.ldc + g.N > d.arg_numel[g.c_arg] || (g.r_arg >= 0 && (g.M - 1) * g.ldr + g.N > d.arg_numel[g.r_arg]))
+          return fail(PTSIM_E_OOB, "GEMM operands extend past their tensors");
+      }
+      break;
+    }
+    case PTSIM_KIND_ATTN_PREFILL: {
+      const ptsim_attn_params &a = d.p.attn;
+      if ((rc = check_arg(d, a.q_arg, "q")) || (rc = check_arg(d, a.k_arg, "k")) || (rc = check_arg(d, a.v_arg, "v")) ||
+          (rc = check_arg(d, a.o_arg, "o")))
+        return rc;
+      if (a.hkv < 1 || a.hq % a.hkv != 0) return fail(PTSIM_E_DESC, "attention with %lld query heads over %lld KV heads", (long long)a.hq, (long long)a.hkv);
+      if (a.batch * a.hq * a.seq * a.dim > d.arg_numel[a.q_arg] || a.batch * a.hq * a.seq * a.dim > d.arg_numel[a.o_arg] ||
+          a.batch * a.hkv * a.seq * a.dim > d.arg_numel[a.k_arg] || a.batch * a.hkv * a.seq * a.dim > d.arg_numel[a.v_arg])
+        return fail(PTSIM_E_OOB, "attention tensors are smaller than batch x heads x seq x dim");
+      break;
+    }
+    case PTSIM_KIND_REDUCE_ALL: {
+      const ptsim_reduce_params &r = d.p.red;
+      if ((rc = check_arg(d, r.in_arg, "reduce input")) || (rc = check_arg(d, r.out_arg, "reduce output"))) return rc;
+      if (r.numel > d.arg_numel[r.in_arg] || d.arg_numel[r.out_arg] < 1) return fail(PTSIM_E_OOB, "reduction past its tensors");
+      break;
+    }
+    default:
+      return fail(PTSIM_E_DESC, "descriptor kind %u is not one this library runs", d.kind);
+  }
+  return PTSIM_OK;
+}
+
+}  // namespace ptsim
+
+using namespace ptsim;
+
+extern "C" {
+
+int ptsim_version(void) { return PTSIM_ABI_VERSION; }
+
+size_t ptsim_desc_size(void) { return sizeof(ptsim_desc); }
+
+int ptsim_init(int device) {
+  int n = 0;
+  PTSIM_CUDA(cudaGetDeviceCount(&n));
+  if (device < 0 || device >= n) return fail(PTSIM_E_ARGS, "device %d of %d", device, n);
+  PTSIM_CUDA(cudaSetDevice(device));
+  DeviceInfo info;
+  int rc = device_info(device, &info);
+  if (rc) return rc;
+  if (info.major != 10)
+    return fail(PTSIM_E_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a (B200)", device, info.major, info.minor);
+  int zero = 0;
+  PTSIM_CUDA(cudaMemcpyToSymbol(g_status, &zero, sizeof(int)));
+  return PTSIM_OK;
+}
+
+int ptsim_check(const void *desc, size_t desc_bytes) { return check_desc(desc, desc_bytes); }
+
+int64_t ptsim_units(const void *desc, size_t desc_bytes) {
+  if (check_desc(desc, desc_bytes)) return -1;
+  return reinterpret_cast<const ptsim_desc *>(desc)->units;
+}
+
+int ptsim_launch(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int nptr, int64_t lo, int64_t hi,
+                 void *workspace, size_t workspace_bytes, void *stream) {
+  int rc = check_desc(desc, desc_bytes);
+  if (rc) return rc;
+  const ptsim_desc &d = *reinterpret_cast<const ptsim_desc *>(desc);
+  if (nptr != d.nargs) return fail(PTSIM_E_ARGS, "%d pointers for a launch of %d arguments", nptr, d.nargs);
+  for (int a = 0; a < nptr; ++a)
+    if (dev_ptrs[a] == nullptr && d.arg_numel[a] > 0) return fail(PTSIM_E_ARGS, "argument %d is a null pointer", a);
+  if (lo < 0 || hi > d.units || lo > hi)
+    return fail(PTSIM_E_ARGS, "unit range [%lld, %lld) outside [0, %lld)", (long long)lo, (long long)hi, (long long)d.units);
+  if (lo == hi) return PTSIM_OK;
+  LaunchCtx c;
+  c.stream = reinterpret_cast<cudaStream_t>(stream);
+  PTSIM_CUDA(cudaGetDevice(&c.device));
+  DeviceInfo info;
+  if ((rc = device_info(c.device, &info))) return rc;
+  c.sm_count = info.sm_count;
+  switch (d.kind) {
+    case PTSIM_KIND_ELEMENTWISE: return launch_elementwise(d, dev_ptrs, lo, hi, c);
+    case PTSIM_KIND_ROW_SOFTMAX:
+    case PTSIM_KIND_ROW_RMSNORM: return launch_rowops(d, dev_ptrs, lo, hi, c);
+    case PTSIM_KIND_QKNORM_ROPE: return launch_qkrope(d, dev_ptrs, lo, hi, c);
+    case PTSIM_KIND_GEMM: return launch_gemm(d, dev_ptrs, lo, hi, c);
+    case PTSIM_KIND_ATTN_PREFILL: return launch_attention(d, dev_ptrs, lo, hi, c);
+    case PTSIM_KIND_REDUCE_ALL: return launch_reduce(d, dev_ptrs, lo, hi, workspace, workspace_bytes, c);
+  }
+  return fail(PTSIM_E_DESC, "descriptor kind %u", d.kind);
+}
+
+int ptsim_sync(void *stream, int32_t *device_status) {
+  PTSIM_CUDA(cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)));
+  int st = 0, zero = 0;
+  PTSIM_CUDA(cudaMemcpyFromSymbol(&st, g_status, sizeof(int)));
+  if (st != 0) PTSIM_CUDA(cudaMemcpyToSymbol(g_status, &zero, sizeof(int)));
+  if (device_status) *device_status = st;
+  return PTSIM_OK;
+}
+
+int ptsim_last_error(char *buf, int n) {
+  if (buf == nullptr || n <= 0) return PTSIM_E_ARGS;
+  strncpy(buf, t_err, size_t(n) - 1);
+  buf[n - 1] = 0;
+  return PTSIM_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,426 @@
+// Row programs of the vector unit: softmax and RMSNorm over rows (the validation bundle's
+// vector_softmax_* kernels, e.g. validation/pytorchsim/vector_softmax_4096x4096_bf16/00_*/..._triton.py:17-68,
+// and the Qwen3 layer's RMSNorm qwen3_8b_layer_prefill_2048x2048_bf16/00_*/..._triton.py), the per-head
+// QK-RMSNorm + rotary embedding (02_*/04_*), and whole-tensor sum/max (vector_sum_*, vector_max_*).
+//
+// On the NPU a program loads XBLOCK rows into the scratchpad, reduces each row across lanes on the XLU
+// (PyTorchSimOps.td:124-136, PyTorchSimTpuOps.td:135-144) and applies the vector ops.  On the B200 a row
+// is owned by TPR threads (a half warp, a warp or two warps); each thread keeps CH 16-byte chunks of the
+// row in registers, so the row is read from HBM exactly once and written once; the cross-lane
+// reductions are warp shuffles (plus one shared-memory exchange when a row spans two warps).
+// Accumulation is fp32, as the programs' .to(tl.float32) casts state; the store rounds to the output
+// dtype (RNE).
+#pragma once
+#include "common.cuh"
+
+namespace ptsim {
+
+enum RowKind { kSoftmax = 0, kRmsNorm = 1 };
+
+struct RowLaunch {
+  const void *in;
+  void *out;
+  const void *weight;
+  int64_t rows_begin, rows_end, cols, in_stride, out_stride;
+  int32_t in_dt, out_dt, w_dt, pad;
+  float eps;
+};
+
+template <int TPR>
+__device__ __forceinline__ float row_allreduce(float v, bool is_max, float *smem_slot) {
+  // Butterfly within the row's lanes (TPR <= 32), then across the row's warps through shared memory.
+#pragma unroll
+  for (int o = (TPR < 32 ? TPR : 32) / 2; o > 0; o >>= 1) {
+    float w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? nan_max(v, w) : __fadd_rn(v, w);
+  }
+  if constexpr (TPR > 32) {
+    constexpr int W = TPR / 32;
+    const int lane = threadIdx.x & 31;
+    const int warp_in_row = (threadIdx.x % TPR) / 32;
+    if (lane == 0) smem_slot[warp_in_row] = v;
+    __syncwarp();
+    __syncthreads();
+    float t = smem_slot[0];
+#pragma unroll
+    for (int w2 = 1; w2 < W; ++w2) t = is_max ? nan_max(t, smem_slot[w2]) : __fadd_rn(t, smem_slot[w2]);
+    __syncthreads();
+    v = t;
+  }
+  return v;
+}
+
+// Fast path: bf16 rows whose length is TPR * 8 * CH.
+template <int KIND, int TPR, int CH>
+__global__ void __launch_bounds__(256) row_fast_kernel(const __grid_constant__ RowLaunch L) {
+  __shared__ float red[256 / 32 * 2];
+  constexpr int RPC = 256 / TPR;  // rows per CTA per step
+  const int lane_in_row = threadIdx.x % TPR;
+  const int row_in_cta = threadIdx.x / TPR;
+  float *slot = red + (row_in_cta * (TPR / 32 > 0 ? TPR / 32 : 1)) % (256 / 32 * 2);
+  const int64_t nrows = L.rows_end - L.rows_begin;
+  // Every thread runs the same number of loop steps (row-exchange barriers for TPR > 32).
+  const int64_t steps = ceil_div(nrows, int64_t(gridDim.x) * RPC);
+  for (int64_t s = 0; s < steps; ++s) {
+    const int64_t r = L.rows_begin + (s * gridDim.x + blockIdx.x) * RPC + row_in_cta;
+    const bool live = r < L.rows_end;
+    uint4 v[CH];
+    const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(L.in) + (live ? r : L.rows_begin) * L.in_stride);
+#pragma unroll
+    for (int c = 0; c < CH; ++c) v[c] = live ? __ldcs(src + c * TPR + lane_in_row) : make_uint4(0, 0, 0, 0);
+    uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(L.out) + (live ? r : L.rows_begin) * L.out_stride);
+    if constexpr (KIND == kSoftmax) {
+      float m = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        const uint32_t w[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) m = nan_max(nan_max(m, lo_bf16(w[j])), hi_bf16(w[j]));
+      }
+      m = row_allreduce<TPR>(m, true, slot);
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        const uint32_t w[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          sum = __fadd_rn(sum, npu_exp(__fsub_rn(lo_bf16(w[j]), m)));
+          sum = __fadd_rn(sum, npu_exp(__fsub_rn(hi_bf16(w[j]), m)));
+        }
+      }
+      sum = row_allreduce<TPR>(sum, false, slot);
+      if (live) {
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+          uint32_t w[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            w[j] = pack_bf16x2(__fdiv_rn(npu_exp(__fsub_rn(lo_bf16(w[j]), m)), sum),
+                               __fdiv_rn(npu_exp(__fsub_rn(hi_bf16(w[j]), m)), sum));
+          __stcs(dst + c * TPR + lane_in_row, make_uint4(w[0], w[1], w[2], w[3]));
+        }
+      }
+    } else {
+      float ss = 0.f;
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        const uint32_t w[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float a = lo_bf16(w[j]), b = hi_bf16(w[j]);
+          ss = __fadd_rn(ss, __fmul_rn(a, a));
+          ss = __fadd_rn(ss, __fmul_rn(b, b));
+        }
+      }
+      ss = row_allreduce<TPR>(ss, false, slot);
+      const float rs = rsqrtf(__fadd_rn(__fdiv_rn(ss, float(L.cols)), L.eps));
+      if (live) {
+        const uint4 *wsrc = reinterpret_cast<const uint4 *>(L.weight);
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+          const uint4 wv = __ldg(wsrc + c * TPR + lane_in_row);
+          uint32_t x[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+          const uint32_t g[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            x[j] = pack_bf16x2(__fmul_rn(__fmul_rn(lo_bf16(x[j]), rs), lo_bf16(g[j])),
+                               __fmul_rn(__fmul_rn(hi_bf16(x[j]), rs), hi_bf16(g[j])));
+          __stcs(dst + c * TPR + lane_in_row, make_uint4(x[0], x[1], x[2], x[3]));
+        }
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ float ld_any(const void *p, int dt, int64_t i) {
+  switch (dt) {
+    case PTSIM_DT_F32: return reinterpret_cast<const float *>(p)[i];
+    case PTSIM_DT_BF16: return bf16_bits_to_f32(reinterpret_cast<const uint16_t *>(p)[i]);
+    case PTSIM_DT_F16: return __half2float(reinterpret_cast<const __half *>(p)[i]);
+  }
+  return 0.f;
+}
+__device__ __forceinline__ void st_any(void *p, int dt, int64_t i, float v) {
+  switch (dt) {
+    case PTSIM_DT_F32: reinterpret_cast<float *>(p)[i] = v; break;
+    case PTSIM_DT_BF16: reinterpret_cast<uint16_t *>(p)[i] = f32_to_bf16_bits(v); break;
+    case PTSIM_DT_F16: reinterpret_cast<__half *>(p)[i] = __float2half_rn(v); break;
+  }
+}
+
+// General path: any row length and float dtype; one warp per row, three passes over the row (the later
+// passes hit L1/L2).
+template <int KIND>
+__global__ void __launch_bounds__(256) row_generic_kernel(const __grid_constant__ RowLaunch L) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t r = L.rows_begin + warp; r < L.rows_end; r += nwarps) {
+    const int64_t ib = r * L.in_stride, ob = r * L.out_stride;
+    if constexpr (KIND == kSoftmax) {
+      float m = -INFINITY;
+      for (int64_t c = lane; c < L.cols; c += 32) m = nan_max(m, ld_any(L.in, L.in_dt, ib + c));
+      m = row_allreduce<32>(m, true, nullptr);
+      float s = 0.f;
+      for (int64_t c = lane; c < L.cols; c += 32) s = __fadd_rn(s, npu_exp(__fsub_rn(ld_any(L.in, L.in_dt, ib + c), m)));
+      s = row_allreduce<32>(s, false, nullptr);
+      for (int64_t c = lane; c < L.cols; c += 32)
+        st_any(L.out, L.out_dt, ob + c, __fdiv_rn(npu_exp(__fsub_rn(ld_any(L.in, L.in_dt, ib + c), m)), s));
+    } else {
+      float ss = 0.f;
+      for (int64_t c = lane; c < L.cols; c += 32) { const float x = ld_any(L.in, L.in_dt, ib + c); ss = __fadd_rn(ss, __fmul_rn(x, x)); }
+      ss = row_allreduce<32>(ss, false, nullptr);
+      const float rs = rsqrtf(__fadd_rn(__fdiv_rn(ss, float(L.cols)), L.eps));
+      for (int64_t c = lane; c < L.cols; c += 32)
+        st_any(L.out, L.out_dt, ob + c,
+               __fmul_rn(__fmul_rn(ld_any(L.in, L.in_dt, ib + c), rs), ld_any(L.weight, L.w_dt, c)));
+    }
+  }
+}
+
+template <int KIND, int TPR, int CH>
+static void launch_row_fast(const RowLaunch &L, const LaunchCtx &c) {
+  constexpr int RPC = 256 / TPR;
+  const int64_t rows = L.rows_end - L.rows_begin;
+  int64_t blocks = ceil_div(rows, RPC);
+  // Registers per thread ~ 4*CH + 40: keep the grid at the resident-CTA count of one wave.
+  const int64_t per_sm = CH >= 12 ? 2 : (CH >= 6 ? 3 : 4);
+  const int64_t cap = int64_t(c.sm_count) * per_sm;
+  if (blocks > cap) blocks = cap;
+  row_fast_kernel<KIND, TPR, CH><<<unsigned(blocks), 256, 0, c.stream>>>(L);
+}
+
+template <int KIND, int TPR>
+static bool dispatch_ch(const RowLaunch &L, const LaunchCtx &c, int ch) {
+  switch (ch) {
+    case 1: launch_row_fast<KIND, TPR, 1>(L, c); return true;
+    case 2: launch_row_fast<KIND, TPR, 2>(L, c); return true;
+    case 3: launch_row_fast<KIND, TPR, 3>(L, c); return true;
+    case 4: launch_row_fast<KIND, TPR, 4>(L, c); return true;
+    case 6: launch_row_fast<KIND, TPR, 6>(L, c); return true;
+    case 8: launch_row_fast<KIND, TPR, 8>(L, c); return true;
+    case 12: launch_row_fast<KIND, TPR, 12>(L, c); return true;
+    case 16: launch_row_fast<KIND, TPR, 16>(L, c); return true;
+  }
+  return false;
+}
+
+template <int KIND>
+static int launch_row_kind(const RowLaunch &L, const LaunchCtx &c) {
+  const bool bf16_io = L.in_dt == PTSIM_DT_BF16 && L.out_dt == PTSIM_DT_BF16 &&
+                       (KIND == kSoftmax || L.w_dt == PTSIM_DT_BF16);
+  const bool aligned = (reinterpret_cast<uintptr_t>(L.in) % 16 == 0) && (reinterpret_cast<uintptr_t>(L.out) % 16 == 0) &&
+                       (KIND == kSoftmax || reinterpret_cast<uintptr_t>(L.weight) % 16 == 0) &&
+                       (L.in_stride % 8 == 0) && (L.out_stride % 8 == 0);
+  if (bf16_io && aligned && L.cols % 8 == 0) {
+    const int64_t chunks = L.cols / 8;
+    const int tprs[3] = {32, 64, 16};
+    for (int t : tprs) {
+      if (chunks % t) continue;
+      const int64_t ch = chunks / t;
+      bool ok = false;
+      if (t == 16) ok = dispatch_ch<KIND, 16>(L, c, int(ch));
+      else if (t == 32) ok = dispatch_ch<KIND, 32>(L, c, int(ch));
+      else ok = dispatch_ch<KIND, 64>(L, c, int(ch));
+      if (ok) { PTSIM_CUDA(cudaGetLastError()); return PTSIM_OK; }
+    }
+  }
+  int64_t blocks = ceil_div(L.rows_end - L.rows_begin, 8);
+  if (blocks > int64_t(c.sm_count) * 8) blocks = int64_t(c.sm_count) * 8;
+  row_generic_kernel<KIND><<<unsigned(blocks), 256, 0, c.stream>>>(L);
+  PTSIM_CUDA(cudaGetLastError());
+  return PTSIM_OK;
+}
+
+int launch_rowops(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c) {
+  const ptsim_row_params &p = d.p.row;
+  RowLaunch L;
+  memset(&L, 0, sizeof(L));
+  L.in = ptrs[p.in_arg];
+  L.out = ptrs[p.out_arg];
+  L.weight = p.weight_arg >= 0 ? ptrs[p.weight_arg] : nullptr;
+  L.rows_begin = lo * d.unit_size;
+  L.rows_end = hi * d.unit_size < p.rows ? hi * d.unit_size : p.rows;
+  L.cols = p.cols;
+  L.in_stride = p.in_row_stride;
+  L.out_stride = p.out_row_stride;
+  L.in_dt = d.arg_dtype[p.in_arg];
+  L.out_dt = d.arg_dtype[p.out_arg];
+  L.w_dt = p.weight_arg >= 0 ? d.arg_dtype[p.weight_arg] : PTSIM_DT_BF16;
+  L.eps = p.eps;
+  if (L.rows_end <= L.rows_begin) return PTSIM_OK;
+  if (d.kind == PTSIM_KIND_ROW_SOFTMAX) return launch_row_kind<kSoftmax>(L, c);
+  return launch_row_kind<kRmsNorm>(L, c);
+}
+
+// ---------------------------------------------------------------------------------------------------
+// QK-RMSNorm + RoPE (validation/pytorchsim/qwen3_8b_layer_prefill_2048x2048_bf16/02_*/..._triton.py):
+// row (t, h) of `dim` = 128 values: r = rsqrt(mean(x^2) + eps); n = (x * r) * w; the rotated half is
+// cat(-n[64:], n[:64]); out[t, h] stored head-major = n * cos[t] + rot * sin[t].  One warp per row, four
+// values per lane; lane l's rotation partner holds d +- 64, i.e. lane l ^ 16.
+// ---------------------------------------------------------------------------------------------------
+struct QkLaunch {
+  const uint16_t *in;
+  const uint16_t *w;
+  const float *cosb, *sinb;
+  uint16_t *out;
+  int64_t row_begin, row_end, heads, tok_stride, head_stride;
+  float eps;
+};
+
+__global__ void __launch_bounds__(256) qk_rope_kernel(const __grid_constant__ QkLaunch L) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+  const uint2 wv = __ldg(reinterpret_cast<const uint2 *>(L.w) + lane);
+  const float w[4] = {lo_bf16(wv.x), hi_bf16(wv.x), lo_bf16(wv.y), hi_bf16(wv.y)};
+  for (int64_t row = L.row_begin + warp; row < L.row_end; row += nwarps) {
+    const int64_t t = row / L.heads, h = row % L.heads;
+    const uint2 xv = __ldcs(reinterpret_cast<const uint2 *>(L.in + row * 128) + lane);
+    const float x[4] = {lo_bf16(xv.x), hi_bf16(xv.x), lo_bf16(xv.y), hi_bf16(xv.y)};
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ss = __fadd_rn(ss, __fmul_rn(x[j], x[j]));
+    ss = row_allreduce<32>(ss, false, nullptr);
+    const float rs = rsqrtf(__fadd_rn(__fdiv_rn(ss, 128.f), L.eps));
+    float n[4], o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) n[j] = __fmul_rn(__fmul_rn(x[j], rs), w[j]);
+    const float4 cs = __ldg(reinterpret_cast<const float4 *>(L.cosb + t * 128) + lane);
+    const float4 sn = __ldg(reinterpret_cast<const float4 *>(L.sinb + t * 128) + lane);
+    const float cv[4] = {cs.x, cs.y, cs.z, cs.w}, sv[4] = {sn.x, sn.y, sn.z, sn.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float partner = __shfl_xor_sync(0xffffffffu, n[j], 16);
+      const float rot = lane < 16 ? -partner : partner;
+      o[j] = __fadd_rn(__fmul_rn(n[j], cv[j]), __fmul_rn(rot, sv[j]));
+    }
+    uint2 ov;
+    ov.x = pack_bf16x2(o[0], o[1]);
+    ov.y = pack_bf16x2(o[2], o[3]);
+    *reinterpret_cast<uint2 *>(L.out + t * L.tok_stride + h * L.head_stride + lane * 4) = ov;
+  }
+}
+
+int launch_qkrope(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c) {
+  const ptsim_qkrope_params &p = d.p.qk;
+  if (p.dim != 128) return fail(PTSIM_E_UNSUPPORTED, "QK-norm+RoPE runs head_dim 128, not %lld", (long long)p.dim);
+  if (p.out_tok_stride % 4 || p.out_head_stride % 4)
+    return fail(PTSIM_E_UNSUPPORTED, "QK-norm+RoPE output strides must keep 8-byte alignment");
+  QkLaunch L;
+  L.in = reinterpret_cast<const uint16_t *>(ptrs[p.in_arg]);
+  L.w = reinterpret_cast<const uint16_t *>(ptrs[p.weight_arg]);
+  L.cosb = reinterpret_cast<const float *>(ptrs[p.cos_arg]);
+  L.sinb = reinterpret_cast<const float *>(ptrs[p.sin_arg]);
+  L.out = reinterpret_cast<uint16_t *>(ptrs[p.out_arg]);
+  const int64_t rows = p.tokens * p.heads;
+  L.row_begin = lo * d.unit_size;
+  L.row_end = hi * d.unit_size < rows ? hi * d.unit_size : rows;
+  L.heads = p.heads;
+  L.tok_stride = p.out_tok_stride;
+  L.head_stride = p.out_head_stride;
+  L.eps = p.eps;
+  if (L.row_end <= L.row_begin) return PTSIM_OK;
+  int64_t blocks = ceil_div(L.row_end - L.row_begin, 8);
+  if (blocks > int64_t(c.sm_count) * 8) blocks = int64_t(c.sm_count) * 8;
+  qk_rope_kernel<<<unsigned(blocks), 256, 0, c.stream>>>(L);
+  PTSIM_CUDA(cudaGetLastError());
+  return PTSIM_OK;
+}
+
+// ---------------------------------------------------------------------------------------------------
+// Whole-tensor sum / max to one fp32 value (validation/pytorchsim/vector_sum_4096x4096_bf16/00_*:
+// lanes accumulate strided slices of the tensor, then one cross-lane reduction).  Pass 1: every thread
+// accumulates a grid-strided slice in fp32, each CTA reduces its threads and writes one partial to the
+// caller's workspace; pass 2: one CTA reduces the partials in a fixed order.  Deterministic.
+// ---------------------------------------------------------------------------------------------------
+constexpr int kReduceThreads = 256;
+
+template <bool IS_MAX>
+__device__ __forceinline__ float block_reduce(float v, float *sh) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = IS_MAX ? nan_max(v, w) : __fadd_rn(v, w);
+  }
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    v = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : (IS_MAX ? -INFINITY : 0.f);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float w = __shfl_xor_sync(0xffffffffu, v, o);
+      v = IS_MAX ? nan_max(v, w) : __fadd_rn(v, w);
+    }
+  }
+  return v;
+}
+
+template <bool IS_MAX>
+__global__ void __launch_bounds__(kReduceThreads) reduce_pass1(const void *in, int dt, int64_t begin, int64_t end,
+                                                               float *partials) {
+  __shared__ float sh[32];
+  float acc = IS_MAX ? -INFINITY : 0.f;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  if (dt == PTSIM_DT_BF16 && begin % 8 == 0 && (reinterpret_cast<uintptr_t>(in) % 16) == 0) {
+    const uint16_t *p = reinterpret_cast<const uint16_t *>(in);
+    const int64_t nvec = (end - begin) / 8;
+    for (int64_t g = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; g < nvec; g += stride) {
+      const uint4 w = __ldcs(reinterpret_cast<const uint4 *>(p + begin) + g);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc = IS_MAX ? nan_max(acc, lo_bf16(ws[j])) : __fadd_rn(acc, lo_bf16(ws[j]));
+        acc = IS_MAX ? nan_max(acc, hi_bf16(ws[j])) : __fadd_rn(acc, hi_bf16(ws[j]));
+      }
+    }
+    for (int64_t i = begin + nvec * 8 + int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < end; i += stride) {
+      const float x = bf16_bits_to_f32(p[i]);
+      acc = IS_MAX ? nan_max(acc, x) : __fadd_rn(acc, x);
+    }
+  } else {
+    for (int64_t i = begin + int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < end; i += stride) {
+      const float x = ld_any(in, dt, i);
+      acc = IS_MAX ? nan_max(acc, x) : __fadd_rn(acc, x);
+    }
+  }
+  acc = block_reduce<IS_MAX>(acc, sh);
+  if (threadIdx.x == 0) partials[blockIdx.x] = acc;
+}
+
+template <bool IS_MAX>
+__global__ void __launch_bounds__(kReduceThreads) reduce_pass2(const float *partials, int n, float *out) {
+  __shared__ float sh[32];
+  float acc = IS_MAX ? -INFINITY : 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) acc = IS_MAX ? nan_max(acc, partials[i]) : __fadd_rn(acc, partials[i]);
+  acc = block_reduce<IS_MAX>(acc, sh);
+  if (threadIdx.x == 0) *out = acc;
+}
+
+// Partials one launch writes: one per CTA of pass 1 (4 CTAs per SM, at most 1024).
+static int reduce_blocks(int sm_count) { return sm_count * 4 < 1024 ? sm_count * 4 : 1024; }
+
+int launch_reduce(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, void *ws, size_t ws_bytes,
+                  const LaunchCtx &c) {
+  const ptsim_reduce_params &p = d.p.red;
+  if (lo != 0 || hi != d.units)
+    return fail(PTSIM_E_ARGS, "a whole-tensor reduction runs as one unit (lo=0, hi=%lld)", (long long)d.units);
+  const int blocks = reduce_blocks(c.sm_count);
+  if (ws == nullptr || ws_bytes < size_t(blocks) * sizeof(float))
+    return fail(PTSIM_E_RESOURCE, "reduction needs %zu workspace bytes, got %zu", size_t(blocks) * sizeof(float), ws_bytes);
+  float *partials = reinterpret_cast<float *>(ws);
+  float *out = reinterpret_cast<float *>(ptrs[p.out_arg]);
+  if (d.arg_dtype[p.out_arg] != PTSIM_DT_F32) return fail(PTSIM_E_UNSUPPORTED, "reduction output must be float32");
+  const int dt = d.arg_dtype[p.in_arg];
+  if (p.op == PTSIM_RED_MAX) {
+    reduce_pass1<true><<<blocks, kReduceThreads, 0, c.stream>>>(ptrs[p.in_arg], dt, 0, p.numel, partials);
+    reduce_pass2<true><<<1, kReduceThreads, 0, c.stream>>>(partials, blocks, out);
+  } else {
+    reduce_pass1<false><<<blocks, kReduceThreads, 0, c.stream>>>(ptrs[p.in_arg], dt, 0, p.numel, partials);
+    reduce_pass2<false><<<1, kReduceThreads, 0, c.stream>>>(partials, blocks, out);
+  }
+  PTSIM_CUDA(cudaGetLastError());
+  return PTSIM_OK;
+}
+
+}  // namespace ptsim

@@ -1,0 +1,138 @@
+"""Descriptor builders: launch descriptors of each executor class from plain shapes, for programs that
+arrive without Triton source (a launch stated directly by a caller, as the reference's tests state
+kernel.json manifests by hand in tests/runtime/spike_launch_cases.py:23-25).  The lowering
+(targets/b200/lower.py) fills the same structures from a traced kernel."""
+from . import descriptors as D
+
+
+def _args(specs):
+    return [{"name": n, "dtype": dt, "shape": [int(numel)]} for n, dt, numel in specs]
+
+
+def elementwise_add(n, dtype="float32", block=1024):
+    """o = x + y over n elements (tests/cases/smoke/add.py, scaled)."""
+    d = D.new(D.ELEMENTWISE, _args([("x", dtype, n), ("y", dtype, n), ("o", dtype, n)]), [-(-n // block)],
+              units=-(-n // block), unit_size=block)
+    e = d.p.ew
+    e.numel, e.nmap, e.store_map = n, 3, 2
+    for i in range(3):
+        m = e.map[i]
+        m.arg, m.ndigit, m.offset = i, 1, 0
+        m.div[0], m.mod[0], m.stride[0] = 1, max(1, n), 1
+    prog = [("load", 0, 0, 0), ("load", 1, 1, 0), ("add", 2, 0, 1), ("store", 0, 2, 0)]
+    e.ncode = len(prog)
+    for i, (op, dst, a, b) in enumerate(prog):
+        e.code[i].op, e.code[i].dst, e.code[i].a, e.code[i].b = D.OP[op], dst, a, b
+    return d
+
+
+def row_softmax(rows, cols, dtype="bfloat16", xblock=128):
+    d = D.new(D.ROW_SOFTMAX, _args([("in_ptr0", dtype, rows * cols), ("out_ptr2", dtype, rows * cols)]),
+              [-(-rows // xblock)], units=-(-rows // xblock), unit_size=xblock)
+    r = d.p.row
+    r.rows, r.cols, r.in_row_stride, r.out_row_stride = rows, cols, cols, cols
+    r.in_arg, r.out_arg, r.weight_arg = 0, 1, -1
+    return d
+
+
+def row_rmsnorm(rows, cols, eps=1e-6, dtype="bfloat16", xblock=256):
+    d = D.new(D.ROW_RMSNORM, _args([("in_ptr0", dtype, rows * cols), ("in_ptr1", dtype, cols),
+                                    ("out_ptr1", dtype, rows * cols)]),
+              [-(-rows // xblock)], units=-(-rows // xblock), unit_size=xblock)
+    r = d.p.row
+    r.rows, r.cols, r.in_row_stride, r.out_row_stride = rows, cols, cols, cols
+    r.in_arg, r.weight_arg, r.out_arg, r.eps = 0, 1, 2, eps
+    return d
+
+
+def qknorm_rope(tokens, heads, dim=128, eps=1e-6, xblock=8192):
+    rows = tokens * heads
+    d = D.new(D.QKNORM_ROPE, _args([("in_ptr0", "bfloat16", rows * dim), ("in_ptr1", "bfloat16", dim),
+                                    ("in_ptr2", "float32", tokens * dim), ("in_ptr3", "float32", tokens * dim),
+                                    ("out_ptr2", "bfloat16", rows * dim)]),
+              [-(-rows // xblock)], units=-(-rows // xblock), unit_size=xblock)
+    q = d.p.qk
+    q.tokens, q.heads, q.dim, q.eps = tokens, heads, dim, eps
+    q.out_tok_stride, q.out_head_stride = dim, tokens * dim
+    q.in_arg, q.weight_arg, q.cos_arg, q.sin_arg, q.out_arg = 0, 1, 2, 3, 4
+    return d
+
+
+def gemm(M, N, K, residual=False, b_kmajor=False, out_dtype="bfloat16"):
+    """C[M,N] = A[M,K] . B (+ R[M,N]); B is [K,N] (the Inductor mm layout) or [N,K] when b_kmajor."""
+    specs = ([("in_ptr0", "bfloat16", M * N)] if residual else []) + [
+        ("arg_A", "bfloat16", M * K), ("arg_B", "bfloat16", K * N), ("out_ptr0", out_dtype, M * N)]
+    d = D.new(D.GEMM, _args(specs), [1], units=M, unit_size=1)
+    g = d.p.gemm
+    off = 1 if residual else 0
+    g.M, g.N, g.K = M, N, K
+    g.lda, g.ldb, g.ldc, g.ldr = K, (K if b_kmajor else N), N, N
+    g.a_arg, g.b_arg, g.c_arg, g.r_arg = off, off + 1, off + 2, (0 if residual else -1)
+    g.b_kmajor = 1 if b_kmajor else 0
+    return d
+
+
+def attention(batch, hq, hkv, seq, dim=128, causal=True, scale=None, bq=1024, bkv=1024):
+    import math
+    scale = 1.0 / math.sqrt(dim) if scale is None else scale
+    nq, nk = batch * hq * seq * dim, batch * hkv * seq * dim
+    d = D.new(D.ATTN_PREFILL, _args([("q_ptr", "bfloat16", nq), ("k_ptr", "bfloat16", nk), ("v_ptr", "bfloat16", nk),
+                                     ("o_ptr", "bfloat16", nq)]), [batch * hq], units=batch * hq, unit_size=1)
+    a = d.p.attn
+    a.batch, a.hq, a.hkv, a.seq, a.dim = batch, hq, hkv, seq, dim
+    a.q_arg, a.k_arg, a.v_arg, a.o_arg = 0, 1, 2, 3
+    a.causal, a.scale, a.ref_bq, a.ref_bkv = 1 if causal else 0, scale, min(bq, seq), min(bkv, seq)
+    return d
+
+
+def reduce_all(numel, op="sum", dtype="bfloat16"):
+    d = D.new(D.REDUCE_ALL, _args([("in_ptr0", dtype, numel), ("out_ptr0", "float32", 1)]), [1], units=1, unit_size=1,
+              workspace_bytes=D.REDUCE_WORKSPACE_BYTES)
+    r = d.p.red
+    r.numel, r.in_arg, r.out_arg, r.op = numel, 0, 1, (D.RED_MAX if op == "max" else D.RED_SUM)
+    return d
+
+
+def copy_map(in_numel, out_numel, digits, dtype="bfloat16", block=None):
+    """out[i] = in[sum ((i // div) % mod) * stride] (a relayout DMA), digits = [(div, mod, stride), ...]."""
+    block = block or out_numel
+    d = D.new(D.ELEMENTWISE, _args([("in_ptr0", dtype, in_numel), ("out_ptr0", dtype, out_numel)]),
+              [-(-out_numel // block)], units=-(-out_numel // block), unit_size=block)
+    e = d.p.ew
+    e.numel, e.nmap, e.store_map, e.pure_copy = out_numel, 2, 1, 1
+    m = e.map[0]
+    m.arg, m.ndigit, m.offset = 0, len(digits), 0
+    for k, (dv, md, st) in enumerate(sorted(digits)):
+        m.div[k], m.mod[k], m.stride[k] = dv, md, st
+    s = e.map[1]
+    s.arg, s.ndigit, s.offset = 1, 1, 0
+    s.div[0], s.mod[0], s.stride[0] = 1, out_numel, 1
+    prog = [("load", 0, 0, 0), ("store", 0, 0, 0)]
+    e.ncode = 2
+    for i, (op, dst, a, b) in enumerate(prog):
+        e.code[i].op, e.code[i].dst, e.code[i].a, e.code[i].b = D.OP[op], dst, a, b
+    return d
+
+
+def silu_mul(tokens, inter, block=2097152):
+    n = tokens * inter
+    d = D.new(D.ELEMENTWISE, _args([("in_ptr0", "bfloat16", 2 * n), ("out_ptr0", "bfloat16", n)]),
+              [-(-n // block)], units=-(-n // block), unit_size=block)
+    e = d.p.ew
+    e.numel, e.nmap, e.store_map = n, 3, 2
+    # gate = in[x % inter + 2*inter * (x // inter)], up = the same + inter
+    for i, off in enumerate((0, inter)):
+        m = e.map[i]
+        m.arg, m.ndigit, m.offset = 0, 2, off
+        m.div[0], m.mod[0], m.stride[0] = 1, inter, 1
+        m.div[1], m.mod[1], m.stride[1] = inter, tokens, 2 * inter
+    s = e.map[2]
+    s.arg, s.ndigit, s.offset = 1, 1, 0
+    s.div[0], s.mod[0], s.stride[0] = 1, n, 1
+    prog = [("load", 0, 0, 0, 0.0), ("neg", 1, 0, 0, 0.0), ("exp", 1, 1, 1, 0.0), ("const", 2, 0, 0, 1.0),
+            ("add", 2, 1, 2, 0.0), ("div", 2, 0, 2, 0.0), ("load", 0, 1, 0, 0.0), ("mul", 0, 2, 0, 0.0),
+            ("store", 0, 0, 0, 0.0)]
+    e.ncode = len(prog)
+    for i, (op, dst, a, b, imm) in enumerate(prog):
+        e.code[i].op, e.code[i].dst, e.code[i].a, e.code[i].b, e.code[i].imm = D.OP[op], dst, a, b, imm
+    return d

@@ -1,0 +1,159 @@
+"""Launch descriptors: the "binary" the B200 lowering emits where the reference's codegen emits a RISC-V ELF
+(pytorchsim_triton_compiler/codegen/build.py:467-502 in the reference).  A descriptor is the packed
+`ptsim_desc` struct of include/ptsim_b200.h; this module mirrors it with ctypes, builds one per tile-program
+class, and reads one back.  The struct layout is checked against the library's own sizeof at load time
+(runtime/native.py), so a mismatch between the two sides fails loudly instead of misreading fields."""
+import ctypes as C
+
+ABI_VERSION = 1
+MAGIC = 0x42535450  # "PTSB"
+
+MAX_ARGS, MAX_MAPS, MAX_DIGITS, MAX_CODE, MAX_REGS = 16, 8, 4, 32, 8
+
+# Kinds (PTSIM_KIND_*).
+ELEMENTWISE, ROW_SOFTMAX, ROW_RMSNORM, QKNORM_ROPE, GEMM, ATTN_PREFILL, REDUCE_ALL = 1, 2, 3, 4, 5, 6, 7
+KIND_NAME = {ELEMENTWISE: "elementwise", ROW_SOFTMAX: "row_softmax", ROW_RMSNORM: "row_rmsnorm",
+             QKNORM_ROPE: "qknorm_rope", GEMM: "gemm", ATTN_PREFILL: "attn_prefill", REDUCE_ALL: "reduce_all"}
+
+# Element types (PTSIM_DT_*), keyed by kernel.json dtype names (contract/kernel_object.py NP_DTYPE keys).
+DTYPE_CODE = {"float32": 0, "bfloat16": 1, "float16": 2, "int32": 3, "int64": 4, "int16": 5, "int8": 6,
+              "uint8": 7, "float64": 8, "bool": 6}
+
+# Vector-unit opcodes (PTSIM_OP_*).
+OP = {"load": 1, "const": 2, "add": 3, "sub": 4, "mul": 5, "div": 6, "neg": 7, "exp": 8, "rsqrt": 9,
+      "sqrt": 10, "max": 11, "min": 12, "rbf16": 13, "abs": 14, "store": 15}
+OP_NAME = {v: k for k, v in OP.items()}
+
+RED_SUM, RED_MAX = 0, 1
+
+# Status codes (PTSIM_E_*).
+OK, E_DESC, E_ARGS, E_CUDA, E_UNSUPPORTED, E_OOB, E_RESOURCE, E_TIMEOUT = 0, 1, 2, 3, 4, 200, 201, 202
+STATUS_NAME = {OK: "OK", E_DESC: "BAD_DESCRIPTOR", E_ARGS: "BAD_ARGUMENTS", E_CUDA: "CUDA_ERROR",
+               E_UNSUPPORTED: "UNSUPPORTED", E_OOB: "INVALID_SPAD_ACCESS", E_RESOURCE: "STACK_OVERFLOW",
+               E_TIMEOUT: "WAIT_TIMEOUT"}
+
+
+class Map(C.Structure):
+    _fields_ = [("arg", C.c_int32), ("ndigit", C.c_int32), ("offset", C.c_int64),
+                ("div", C.c_int64 * MAX_DIGITS), ("mod", C.c_int64 * MAX_DIGITS), ("stride", C.c_int64 * MAX_DIGITS)]
+
+
+class Insn(C.Structure):
+    _fields_ = [("op", C.c_uint8), ("dst", C.c_uint8), ("a", C.c_uint8), ("b", C.c_uint8), ("imm", C.c_float)]
+
+
+class EwParams(C.Structure):
+    _fields_ = [("numel", C.c_int64), ("nmap", C.c_int32), ("ncode", C.c_int32), ("store_map", C.c_int32),
+                ("pure_copy", C.c_int32), ("map", Map * MAX_MAPS), ("code", Insn * MAX_CODE)]
+
+
+class RowParams(C.Structure):
+    _fields_ = [("rows", C.c_int64), ("cols", C.c_int64), ("in_row_stride", C.c_int64), ("out_row_stride", C.c_int64),
+                ("in_arg", C.c_int32), ("out_arg", C.c_int32), ("weight_arg", C.c_int32), ("pad0", C.c_int32),
+                ("eps", C.c_float), ("inv_cols", C.c_float)]
+
+
+class QkParams(C.Structure):
+    _fields_ = [("tokens", C.c_int64), ("heads", C.c_int64), ("dim", C.c_int64), ("out_tok_stride", C.c_int64),
+                ("out_head_stride", C.c_int64), ("in_arg", C.c_int32), ("weight_arg", C.c_int32),
+                ("cos_arg", C.c_int32), ("sin_arg", C.c_int32), ("out_arg", C.c_int32), ("pad0", C.c_int32),
+                ("eps", C.c_float), ("pad1", C.c_float)]
+
+
+class GemmParams(C.Structure):
+    _fields_ = [("M", C.c_int64), ("N", C.c_int64), ("K", C.c_int64), ("lda", C.c_int64), ("ldb", C.c_int64),
+                ("ldc", C.c_int64), ("ldr", C.c_int64), ("a_arg", C.c_int32), ("b_arg", C.c_int32),
+                ("c_arg", C.c_int32), ("r_arg", C.c_int32), ("b_kmajor", C.c_int32), ("pad0", C.c_int32)]
+
+
+class AttnParams(C.Structure):
+    _fields_ = [("batch", C.c_int64), ("hq", C.c_int64), ("hkv", C.c_int64), ("seq", C.c_int64), ("dim", C.c_int64),
+                ("q_arg", C.c_int32), ("k_arg", C.c_int32), ("v_arg", C.c_int32), ("o_arg", C.c_int32),
+                ("causal", C.c_int32), ("pad0", C.c_int32), ("scale", C.c_float), ("pad1", C.c_float),
+                ("ref_bq", C.c_int64), ("ref_bkv", C.c_int64)]
+
+
+class ReduceParams(C.Structure):
+    _fields_ = [("numel", C.c_int64), ("in_arg", C.c_int32), ("out_arg", C.c_int32), ("op", C.c_int32),
+                ("pad0", C.c_int32)]
+
+
+class Params(C.Union):
+    _fields_ = [("ew", EwParams), ("row", RowParams), ("qk", QkParams), ("gemm", GemmParams),
+                ("attn", AttnParams), ("red", ReduceParams)]
+
+
+class Desc(C.Structure):
+    _fields_ = [("magic", C.c_uint32), ("version", C.c_uint32), ("kind", C.c_uint32), ("flags", C.c_uint32),
+                ("nargs", C.c_int32), ("pad0", C.c_int32), ("arg_dtype", C.c_int32 * MAX_ARGS),
+                ("arg_numel", C.c_int64 * MAX_ARGS), ("grid", C.c_int64 * 3), ("units", C.c_int64),
+                ("unit_size", C.c_int64), ("workspace_bytes", C.c_int64), ("p", Params)]
+
+
+SIZE = C.sizeof(Desc)
+
+# Workspace of a REDUCE_ALL launch: one fp32 partial per pass-1 CTA, at most 1024 of them.
+REDUCE_WORKSPACE_BYTES = 1024 * 4
+
+
+def new(kind, args, grid, units, unit_size, workspace_bytes=0):
+    """A zeroed descriptor of `kind` over the manifest arguments `args` ([{name, dtype, shape}])."""
+    import math
+    if len(args) > MAX_ARGS:
+        raise ValueError(f"{len(args)} tensor arguments; the executor takes at most {MAX_ARGS}")
+    d = Desc()
+    d.magic, d.version, d.kind = MAGIC, ABI_VERSION, kind
+    d.nargs = len(args)
+    for i, a in enumerate(args):
+        if a["dtype"] not in DTYPE_CODE:
+            raise ValueError(f"argument {a['name']} has dtype {a['dtype']}, which the executor does not carry")
+        d.arg_dtype[i] = DTYPE_CODE[a["dtype"]]
+        d.arg_numel[i] = math.prod(a["shape"])
+    g = (list(grid) + [1, 1, 1])[:3]
+    for i in range(3):
+        d.grid[i] = int(g[i])
+    d.units, d.unit_size, d.workspace_bytes = int(units), int(unit_size), int(workspace_bytes)
+    return d
+
+
+def to_bytes(d):
+    return bytes(C.string_at(C.addressof(d), SIZE))
+
+
+def from_bytes(blob):
+    if len(blob) != SIZE:
+        raise ValueError(f"descriptor of {len(blob)} bytes; this build writes {SIZE}")
+    d = Desc.from_buffer_copy(blob)
+    if d.magic != MAGIC or d.version != ABI_VERSION:
+        raise ValueError(f"not a version-{ABI_VERSION} PTSB descriptor (magic 0x{d.magic:08x}, version {d.version})")
+    return d
+
+
+def describe(d):
+    """A JSON-able summary of descriptor `d` (what kernel.json records next to the blob)."""
+    out = {"kind": KIND_NAME.get(d.kind, d.kind), "units": d.units, "unit_size": d.unit_size,
+           "grid": list(d.grid), "workspace_bytes": d.workspace_bytes}
+    if d.kind == ELEMENTWISE:
+        e = d.p.ew
+        out["numel"] = e.numel
+        out["pure_copy"] = bool(e.pure_copy)
+        out["maps"] = [{"arg": m.arg, "offset": m.offset,
+                        "digits": [(m.div[k], m.mod[k], m.stride[k]) for k in range(m.ndigit)]}
+                       for m in list(e.map)[:e.nmap]]
+        out["code"] = [(OP_NAME.get(i.op, i.op), i.dst, i.a, i.b, i.imm) for i in list(e.code)[:e.ncode]]
+    elif d.kind in (ROW_SOFTMAX, ROW_RMSNORM):
+        r = d.p.row
+        out.update(rows=r.rows, cols=r.cols, eps=r.eps)
+    elif d.kind == QKNORM_ROPE:
+        q = d.p.qk
+        out.update(tokens=q.tokens, heads=q.heads, dim=q.dim, eps=q.eps,
+                   out_strides=[q.out_tok_stride, q.out_head_stride])
+    elif d.kind == GEMM:
+        g = d.p.gemm
+        out.update(M=g.M, N=g.N, K=g.K, residual=g.r_arg >= 0, b_kmajor=bool(g.b_kmajor))
+    elif d.kind == ATTN_PREFILL:
+        a = d.p.attn
+        out.update(batch=a.batch, hq=a.hq, hkv=a.hkv, seq=a.seq, dim=a.dim, causal=bool(a.causal), scale=a.scale)
+    elif d.kind == REDUCE_ALL:
+        out.update(numel=d.p.red.numel, op="max" if d.p.red.op == RED_MAX else "sum")
+    return out

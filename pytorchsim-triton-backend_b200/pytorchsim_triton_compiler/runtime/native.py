@@ -1,0 +1,123 @@
+"""ctypes binding of libptsim_b200.so, the sm_100a executor (include/ptsim_b200.h).
+
+There is no CPU path behind this module: when the library is missing or cannot load, every call raises
+NativeUnavailable, so a launch fails loudly instead of computing anything elsewhere."""
+import ctypes as C
+import os
+import threading
+
+from ..codegen import descriptors as D
+
+LIB_NAME = "libptsim_b200.so"
+LIB_PATH = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "_lib", LIB_NAME)
+
+#: Every symbol include/ptsim_b200.h declares, with its ctypes signature.
+SYMBOLS = {
+    "ptsim_version": (C.c_int, []),
+    "ptsim_desc_size": (C.c_size_t, []),
+    "ptsim_init": (C.c_int, [C.c_int]),
+    "ptsim_check": (C.c_int, [C.c_void_p, C.c_size_t]),
+    "ptsim_units": (C.c_int64, [C.c_void_p, C.c_size_t]),
+    "ptsim_launch": (C.c_int, [C.c_void_p, C.c_size_t, C.POINTER(C.c_void_p), C.c_int, C.c_int64, C.c_int64,
+                               C.c_void_p, C.c_size_t, C.c_void_p]),
+    "ptsim_sync": (C.c_int, [C.c_void_p, C.POINTER(C.c_int32)]),
+    "ptsim_last_error": (C.c_int, [C.c_char_p, C.c_int]),
+}
+
+
+class NativeUnavailable(RuntimeError):
+    """The executor library is not built or does not load: nothing can run."""
+
+
+class ExecutorError(RuntimeError):
+    """A launch the executor refused or a kernel reported; `code` is the PTSIM_E_* status."""
+
+    def __init__(self, code, message):
+        super().__init__(f"{D.STATUS_NAME.get(code, code)} ({code}): {message}")
+        self.code = code
+
+
+_lib = None
+_lock = threading.Lock()
+_inited = set()
+
+
+def library_path():
+    return os.environ.get("PTSIM_B200_LIB", LIB_PATH)
+
+
+def load():
+    """The loaded library (built on first use when nvcc is present and the .so is missing)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = library_path()
+        if not os.path.exists(path):
+            raise NativeUnavailable(f"{path} is not built: run __graft_entry__.build() (nvcc, sm_100a)")
+        try:
+            lib = C.CDLL(path)
+        except OSError as e:
+            raise NativeUnavailable(f"{path} does not load: {e}") from None
+        for name, (res, argt) in SYMBOLS.items():
+            fn = getattr(lib, name)
+            fn.restype, fn.argtypes = res, argt
+        if lib.ptsim_version() != D.ABI_VERSION:
+            raise NativeUnavailable(f"{path} implements ABI {lib.ptsim_version()}, this package {D.ABI_VERSION}")
+        if lib.ptsim_desc_size() != D.SIZE:
+            raise NativeUnavailable(f"{path} reads {lib.ptsim_desc_size()}-byte descriptors, the Python mirror "
+                                    f"writes {D.SIZE}: rebuild the library")
+        _lib = lib
+        return lib
+
+
+def last_error():
+    buf = C.create_string_buffer(1024)
+    load().ptsim_last_error(buf, 1024)
+    return buf.value.decode(errors="replace")
+
+
+def _check(rc):
+    if rc != 0:
+        raise ExecutorError(rc, last_error())
+
+
+def init(device):
+    """Select `device` for this thread and prepare it (idempotent)."""
+    lib = load()
+    _check(lib.ptsim_init(int(device)))
+    _inited.add(int(device))
+
+
+def check(blob):
+    """Validate a descriptor blob on the host (no GPU needed)."""
+    buf = C.create_string_buffer(bytes(blob), len(blob))
+    _check(load().ptsim_check(buf, len(blob)))
+
+
+def units(blob):
+    buf = C.create_string_buffer(bytes(blob), len(blob))
+    n = load().ptsim_units(buf, len(blob))
+    if n < 0:
+        raise ExecutorError(D.E_DESC, last_error())
+    return n
+
+
+def launch(blob, ptrs, lo, hi, workspace=0, workspace_bytes=0, stream=0):
+    """Enqueue units [lo, hi) of descriptor `blob` over device pointers `ptrs` on `stream` (a raw
+    cudaStream_t as int).  Asynchronous; sync() reports device-side failures."""
+    lib = load()
+    buf = C.create_string_buffer(bytes(blob), len(blob))
+    arr = (C.c_void_p * max(1, len(ptrs)))(*[C.c_void_p(int(p)) for p in ptrs])
+    _check(lib.ptsim_launch(buf, len(blob), arr, len(ptrs), int(lo), int(hi), C.c_void_p(int(workspace) or None),
+                            int(workspace_bytes), C.c_void_p(int(stream) or None)))
+
+
+def sync(stream=0):
+    """Wait for `stream`; raise ExecutorError when a kernel recorded a device-side failure."""
+    st = C.c_int32(0)
+    _check(load().ptsim_sync(C.c_void_p(int(stream) or None), C.byref(st)))
+    if st.value:
+        raise ExecutorError(st.value, "reported by a kernel on the device (status word)")

@@ -1,0 +1,504 @@
+"""Lowering of a traced tile program into a B200 launch descriptor (the bridge from the reference's L3
+compiler to a CUDA L1): the program's class decides which executor kernel runs it, and the program's index
+maps, constants and argument roles fill that kernel's descriptor.
+
+Classes (each with the reference program it was written against):
+  ELEMENTWISE   Inductor pointwise kernels and tests/cases smoke/add.py: loads at affine index maps of the
+                flat launch index, fp32 vector ops, one store.  Compiled to the executor's vector program.
+  ROW_SOFTMAX   vector_softmax_* (validation/pytorchsim/vector_softmax_4096x4096_bf16/00_*).
+  ROW_RMSNORM   qwen3_8b_layer_prefill_*/00_* (mean of squares, rsqrt(mean + eps), times weight).
+  QKNORM_ROPE   qwen3_8b_layer_prefill_*/02_*, 04_* (per-head RMSNorm, rotary embedding, head-major store).
+  REDUCE_ALL    vector_sum_*, vector_max_* (a whole tensor to one fp32 value).
+  GEMM          every kernel with one tl.dot: gemm_*, Qwen3 01/03/08/09/11 (with a residual epilogue).
+  ATTN_PREFILL  _prefill_kernel (causal GQA flash attention).
+A program none of these match is refused with a Reason; nothing runs anywhere else."""
+import ast
+import math
+import re
+
+from ...codegen import descriptors as D
+from ...contract.stop import Reason, Refused
+from . import frontend as F
+
+
+class Lowered:
+    """A lowered kernel: the descriptor, its class name and a JSON-able summary."""
+
+    def __init__(self, desc, summary):
+        self.desc = desc
+        self.blob = D.to_bytes(desc)
+        self.summary = summary
+
+    @property
+    def kind(self):
+        return self.summary["kind"]
+
+
+def _manifest_args(spec):
+    return [{"name": a.name, "dtype": a.dtype, "shape": list(a.shape)} for a in spec.args]
+
+
+def _lookup(spec, prog, *names, default=None):
+    """A size the program states: a constant assigned in its body, a constexpr, or a scalar value."""
+    for n in names:
+        if prog is not None and n in prog.assigned:
+            return prog.assigned[n]
+        if n in spec.constexprs and isinstance(spec.constexprs[n], (int, float)):
+            return spec.constexprs[n]
+        sv = spec.extra.get("scalar_values", {})
+        if n in sv and sv[n] is not None:
+            return sv[n]
+    return default
+
+
+def _grid_programs(spec):
+    g = (list(spec.grid) + [1, 1, 1])[:3]
+    return g
+
+
+# ---------------------------------------------------------------------------------------------------
+# Structural helpers over the value DAG
+# ---------------------------------------------------------------------------------------------------
+
+def key(n):
+    """A canonical, hashable form of value node `n` (structural equality)."""
+    if isinstance(n, F.Const):
+        return ("c", n.v)
+    if isinstance(n, F.Load):
+        return ("l", n.arg, tuple(sorted(n.index.terms.items())), n.index.const, n.mask is not None)
+    if isinstance(n, F.Op):
+        return ("o", n.name) + tuple(key(a) if isinstance(a, F.Node) else ("m",) for a in n.args)
+    if isinstance(n, F.Reduce):
+        return ("r", n.op, key(n.value))
+    if isinstance(n, F.Dot):
+        return ("d", key(n.a), key(n.b))
+    return ("?", id(n))
+
+
+def walk(n, seen=None):
+    """Every node reachable from `n` (pre-order, once each)."""
+    seen = set() if seen is None else seen
+    if id(n) in seen:
+        return
+    seen.add(id(n))
+    yield n
+    if isinstance(n, F.Op):
+        for a in n.args:
+            if isinstance(a, F.Node):
+                yield from walk(a, seen)
+    elif isinstance(n, F.Reduce):
+        yield from walk(n.value, seen)
+    elif isinstance(n, F.Dot):
+        yield from walk(n.a, seen)
+        yield from walk(n.b, seen)
+
+
+def strip_casts(n):
+    """`n` without round-trips through fp32 (Inductor's repeated .to(tl.float32))."""
+    return n
+
+
+def _row_index(idx, what):
+    """(row stride) of an index r + stride * x, else Refused."""
+    r = idx.coeff_of("r")
+    x = idx.coeff_of("x")
+    if idx.const != 0 or r != {F.Digit("r"): 1} or len(x) != 1 or F.Digit("x") not in x or len(idx.terms) != 2:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{what} index {idx} is not r + stride * x")
+    return x[F.Digit("x")]
+
+
+# ---------------------------------------------------------------------------------------------------
+# Classes
+# ---------------------------------------------------------------------------------------------------
+
+def lower(spec, fn=None):
+    """The Lowered kernel of `spec` (a contract.kernel_spec.KernelSpec), or Refused."""
+    if fn is None:
+        fn = F.load_kernel(spec)
+    src, name = F.kernel_source(fn)
+    tree = ast.parse(src)
+    dots = [n for n in ast.walk(tree) if isinstance(n, ast.Call) and isinstance(n.func, ast.Attribute) and n.func.attr == "dot"]
+    if dots:
+        if len(dots) >= 2 and {"HQ", "G", "S", "D", "SCALE"} <= set(spec.constexprs):
+            return _lower_attention(spec, tree)
+        return _lower_gemm(spec, tree, src)
+    prog = F.Evaluator(spec, F.Program()).run(src, name)
+    if len(prog.stores) != 1:
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: {len(prog.stores)} stores; the executor's "
+                                                    f"vector programs have one")
+    st = prog.stores[0]
+    reduces = [n for n in walk(st.value) if isinstance(n, F.Reduce)]
+    if not reduces:
+        return _lower_elementwise(spec, prog, st)
+    ops = {n.name for n in walk(st.value) if isinstance(n, F.Op)}
+    loads = [n for n in walk(st.value) if isinstance(n, F.Load)]
+    args = {l.arg for l in loads}
+    if not st.index.terms:
+        return _lower_reduce_all(spec, prog, st, reduces)
+    if "where" in ops and "rsqrt" in ops:
+        return _lower_qknorm_rope(spec, prog, st, loads)
+    if "rsqrt" in ops and len(args) == 2:
+        return _lower_rmsnorm(spec, prog, st, loads)
+    if "exp" in ops and {r.op for r in reduces} == {"max", "add"} and len(args) == 1:
+        return _lower_softmax(spec, prog, st, reduces)
+    raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a reduction program of ops {sorted(ops)}")
+
+
+def _lower_elementwise(spec, prog, st):
+    xnumel = _lookup(spec, prog, "xnumel", "n", "N", "numel")
+    gx, gy, gz = _grid_programs(spec)
+    if gy != 1 or gz != 1:
+        raise Refused(Reason.SHAPE_NOT_RUN, f"{spec.name}: a pointwise program over a {gx}x{gy}x{gz} grid")
+    block = prog.block.get("x")
+    if block is None:
+        # No pid * BLOCK + arange index: one program covers the whole (possibly broadcast) store.
+        block = max(1, spec.args[st.arg].numel if not st.index.terms else spec.args[st.arg].numel)
+    numel = gx * block
+    if xnumel is not None:
+        numel = min(numel, int(xnumel))
+    if st.mask is not None:
+        raise Refused(Reason.MASKED_STORE_NOT_A_BOX, f"{spec.name}: a masked pointwise store")
+    maps, code = [], []
+
+    def map_of(arg, idx):
+        if idx.vars() - {"x"}:
+            raise Refused(Reason.INDEX_NOT_AFFINE, f"{spec.name}: index {idx} uses {sorted(idx.vars())}")
+        m = D.Map()
+        m.arg = arg
+        m.offset = idx.const
+        digits = list(idx.terms.items())
+        if len(digits) > D.MAX_DIGITS:
+            raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: an index of {len(digits)} digits")
+        digits.sort(key=lambda dc: dc[0].div)
+        m.ndigit = len(digits)
+        for k, (dg, c) in enumerate(digits):
+            if c < 0:
+                raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: a negative stride in {idx}")
+            m.div[k] = dg.div
+            m.mod[k] = dg.mod if dg.mod is not None else max(1, -(-numel // dg.div))
+            m.stride[k] = c
+        if len(maps) >= D.MAX_MAPS:
+            raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: more than {D.MAX_MAPS} transfers")
+        maps.append(m)
+        return len(maps) - 1
+
+    # Register allocation over the DAG: each node's value is computed once; a register is freed after the
+    # last use of the node it holds.
+    uses = {}
+    for n in walk(st.value):
+        for a in (n.args if isinstance(n, F.Op) else ()):
+            if isinstance(a, F.Node):
+                uses[id(a)] = uses.get(id(a), 0) + 1
+    reg_of, free = {}, list(range(D.MAX_REGS))[::-1]
+
+    def emit(op, dst=0, a=0, b=0, imm=0.0):
+        if len(code) >= D.MAX_CODE:
+            raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: a vector program over {D.MAX_CODE} ops")
+        ins = D.Insn()
+        ins.op, ins.dst, ins.a, ins.b, ins.imm = D.OP[op], dst, a, b, imm
+        code.append(ins)
+
+    def release(n):
+        uses[id(n)] -= 1
+        if uses[id(n)] == 0:
+            free.append(reg_of.pop(id(n)))
+
+    def take():
+        if not free:
+            raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: more than {D.MAX_REGS} live values")
+        return free.pop()
+
+    def gen(n):
+        if id(n) in reg_of:
+            return reg_of[id(n)]
+        if isinstance(n, F.Load):
+            if n.mask is not None:
+                raise Refused(Reason.MASKED_BOX_BEFORE_TENSOR, f"{spec.name}: a masked pointwise load")
+            r = take()
+            emit("load", r, map_of(n.arg, n.index))
+        elif isinstance(n, F.Const):
+            r = take()
+            emit("const", r, imm=n.v)
+        elif isinstance(n, F.Op):
+            if n.name == "sigmoid":
+                x = n.args[0]
+                one = F.Const(1.0)
+                return gen(_retarget(n, F.Op("div", one, F.Op("add", one, F.Op("exp", F.Op("neg", x)))), uses))
+            if n.name not in D.OP or n.name in ("load", "const", "store"):
+                raise Refused(Reason.MATH_UNLOWERED, f"{spec.name}: vector op {n.name}")
+            srcs = [gen(a) for a in n.args]
+            for a in n.args:
+                release(a)
+            r = take()
+            emit(n.name, r, srcs[0], srcs[1] if len(srcs) > 1 else srcs[0])
+        else:
+            raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a {type(n).__name__} in a pointwise program")
+        reg_of[id(n)] = r
+        uses.setdefault(id(n), 0)
+        return r
+
+    uses[id(st.value)] = uses.get(id(st.value), 0) + 1
+    out_reg = gen(st.value)
+    store_map = map_of(st.arg, st.index)
+    emit("store", 0, out_reg)
+    d = D.new(D.ELEMENTWISE, _manifest_args(spec), spec.grid, units=gx, unit_size=block)
+    e = d.p.ew
+    e.numel = numel
+    e.nmap, e.ncode, e.store_map = len(maps), len(code), store_map
+    for i, m in enumerate(maps):
+        e.map[i] = m
+    for i, c in enumerate(code):
+        e.code[i] = c
+    # A pure copy: the stored value is one load, of the store's dtype.
+    v = st.value
+    if isinstance(v, F.Op) and v.name == "rbf16" and spec.args[st.arg].dtype == "bfloat16":
+        v = v.args[0]
+    if isinstance(v, F.Load) and spec.args[v.arg].dtype == spec.args[st.arg].dtype and len(maps) == 2:
+        e.pure_copy = 1
+        # Map 0 must be the load for the copy kernel.
+        if maps[0].arg != v.arg:
+            e.map[0], e.map[1] = maps[1], maps[0]
+            e.store_map = 0 if store_map == 1 else 1
+    summary = D.describe(d)
+    return Lowered(d, summary)
+
+
+def _retarget(old, new, uses):
+    uses[id(new)] = uses.get(id(old), 1)
+    for n in walk(new):
+        for a in (n.args if isinstance(n, F.Op) else ()):
+            if isinstance(a, F.Node):
+                uses[id(a)] = uses.get(id(a), 0) + 1
+    return new
+
+
+def _row_sizes(spec, prog, what):
+    rows = _lookup(spec, prog, "xnumel")
+    cols = _lookup(spec, prog, "r0_numel", "rnumel")
+    xblock = _lookup(spec, prog, "XBLOCK")
+    if rows is None or cols is None or xblock is None:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: {what} without xnumel/r0_numel/XBLOCK")
+    return int(rows), int(cols), int(xblock)
+
+
+def _lower_softmax(spec, prog, st, reduces):
+    rows, cols, xblock = _row_sizes(spec, prog, "softmax")
+    v = st.value
+    if not (isinstance(v, F.Op) and v.name == "div" and isinstance(v.args[1], F.Reduce) and v.args[1].op == "add"):
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: not exp(x - max) / sum")
+    num = v.args[0]
+    if not (isinstance(num, F.Op) and num.name == "exp" and key(num) == key(v.args[1].value)):
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: the softmax numerator is not the summed exp")
+    sub = num.args[0]
+    if not (isinstance(sub, F.Op) and sub.name == "sub" and isinstance(sub.args[1], F.Reduce) and sub.args[1].op == "max"
+            and isinstance(sub.args[0], F.Load) and key(sub.args[1].value) == key(sub.args[0])):
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: not exp(x - rowmax(x))")
+    ld = sub.args[0]
+    d = D.new(D.ROW_SOFTMAX, _manifest_args(spec), spec.grid, units=_grid_programs(spec)[0], unit_size=xblock)
+    r = d.p.row
+    r.rows, r.cols = rows, cols
+    r.in_row_stride = _row_index(ld.index, "softmax load")
+    r.out_row_stride = _row_index(st.index, "softmax store")
+    r.in_arg, r.out_arg, r.weight_arg = ld.arg, st.arg, -1
+    return Lowered(d, D.describe(d))
+
+
+def _lower_rmsnorm(spec, prog, st, loads):
+    rows, cols, xblock = _row_sizes(spec, prog, "RMSNorm")
+    row_loads = [l for l in loads if "x" in l.index.vars()]
+    w_loads = [l for l in loads if l.index.vars() == {"r"}]
+    if not row_loads or not w_loads or len({l.arg for l in row_loads}) != 1 or len({l.arg for l in w_loads}) != 1:
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: RMSNorm wants one row input and one weight")
+    rs = [n for n in walk(st.value) if isinstance(n, F.Op) and n.name == "rsqrt"]
+    inner = rs[0].args[0]
+    if not (isinstance(inner, F.Op) and inner.name == "add" and isinstance(inner.args[1], F.Const)):
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: rsqrt of something other than mean + eps")
+    eps = inner.args[1].v
+    mean = inner.args[0]
+    if not (isinstance(mean, F.Op) and mean.name == "div" and isinstance(mean.args[0], F.Reduce)
+            and isinstance(mean.args[1], F.Const) and mean.args[1].v == float(cols)):
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: the mean is not sum / {cols}")
+    sq = mean.args[0].value
+    if not (isinstance(sq, F.Op) and sq.name == "mul" and key(sq.args[0]) == key(sq.args[1])):
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: the reduced value is not x * x")
+    d = D.new(D.ROW_RMSNORM, _manifest_args(spec), spec.grid, units=_grid_programs(spec)[0], unit_size=xblock)
+    r = d.p.row
+    r.rows, r.cols, r.eps = rows, cols, eps
+    r.in_row_stride = _row_index(row_loads[0].index, "RMSNorm load")
+    r.out_row_stride = _row_index(st.index, "RMSNorm store")
+    r.in_arg, r.out_arg, r.weight_arg = row_loads[0].arg, st.arg, w_loads[0].arg
+    return Lowered(d, D.describe(d))
+
+
+def _lower_qknorm_rope(spec, prog, st, loads):
+    rows, cols, xblock = _row_sizes(spec, prog, "QK-norm+RoPE")
+    if cols != 128:
+        raise Refused(Reason.SHAPE_NOT_RUN, f"{spec.name}: head_dim {cols}; the executor runs 128")
+    dt = {a: spec.args[a].dtype for a in {l.arg for l in loads}}
+    f32 = sorted(a for a, t in dt.items() if t == "float32")
+    bf = sorted(a for a, t in dt.items() if t == "bfloat16")
+    if len(f32) != 2 or len(bf) != 2:
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: QK-norm+RoPE wants bf16 x, w and fp32 cos, sin")
+    x_arg = next(l.arg for l in loads if l.arg in bf and "x" in l.index.vars())
+    w_arg = next(a for a in bf if a != x_arg)
+    # cos multiplies the normalised row, sin the rotated one (the branch holding the where).
+    v = st.value
+    if not (isinstance(v, F.Op) and v.name == "add" and all(isinstance(a, F.Op) and a.name == "mul" for a in v.args)):
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: not n * cos + rot * sin")
+    cos_arg = sin_arg = None
+    for m in v.args:
+        tab = [a for a in m.args if isinstance(a, F.Load) and a.arg in f32]
+        if len(tab) != 1:
+            raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a rotary product without its table")
+        other = [a for a in m.args if a is not tab[0]][0]
+        if any(isinstance(n, F.Op) and n.name == "where" for n in walk(other)):
+            sin_arg, sin_load = tab[0].arg, tab[0]
+        else:
+            cos_arg = tab[0].arg
+    if cos_arg is None or sin_arg is None:
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: cannot tell the cos table from the sin table")
+    tdig = [dg for dg in sin_load.index.terms if dg.var == "x"]
+    if len(tdig) != 1 or tdig[0].mod is not None:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: the table index is not x // heads")
+    heads = tdig[0].div
+    tok = st.index.terms.get(F.Digit("x", heads, None))
+    head = st.index.terms.get(F.Digit("x", 1, heads))
+    if tok is None or head is None or st.index.terms.get(F.Digit("r")) != 1:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: the store index {st.index} is not r + t*T + h*H")
+    rs = [n for n in walk(v) if isinstance(n, F.Op) and n.name == "rsqrt"]
+    inner = rs[0].args[0]
+    if not (isinstance(inner, F.Op) and inner.name == "add" and isinstance(inner.args[1], F.Const)):
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: rsqrt of something other than mean + eps")
+    d = D.new(D.QKNORM_ROPE, _manifest_args(spec), spec.grid, units=_grid_programs(spec)[0], unit_size=xblock)
+    q = d.p.qk
+    q.tokens, q.heads, q.dim = rows // heads, heads, cols
+    q.out_tok_stride, q.out_head_stride = tok, head
+    q.in_arg, q.weight_arg, q.cos_arg, q.sin_arg, q.out_arg = x_arg, w_arg, cos_arg, sin_arg, st.arg
+    q.eps = inner.args[1].v
+    return Lowered(d, D.describe(d))
+
+
+def _lower_reduce_all(spec, prog, st, reduces):
+    xnumel = _lookup(spec, prog, "xnumel", default=1)
+    cols = _lookup(spec, prog, "r0_numel", "rnumel")
+    if int(xnumel) != 1 or cols is None or len(reduces) != 1:
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a whole-tensor reduction wants xnumel 1")
+    red = reduces[0]
+    v = red.value
+    if not isinstance(v, F.Load) or v.index.vars() != {"r"} or v.index.const != 0:
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: reduces something other than one contiguous load")
+    if red.op not in ("add", "max"):
+        raise Refused(Reason.MATH_UNLOWERED, f"{spec.name}: reduction {red.op}")
+    d = D.new(D.REDUCE_ALL, _manifest_args(spec), spec.grid, units=1, unit_size=1,
+              workspace_bytes=D.REDUCE_WORKSPACE_BYTES)
+    r = d.p.red
+    r.numel, r.in_arg, r.out_arg = int(cols), v.arg, st.arg
+    r.op = D.RED_MAX if red.op == "max" else D.RED_SUM
+    return Lowered(d, D.describe(d))
+
+
+# ---------------------------------------------------------------------------------------------------
+# Matrix-unit programs
+# ---------------------------------------------------------------------------------------------------
+
+def _int_assigns(tree):
+    out = {}
+    for n in ast.walk(tree):
+        if isinstance(n, (ast.Assign, ast.AnnAssign)):
+            tgt = n.targets[0] if isinstance(n, ast.Assign) else n.target
+            val = n.value
+            if isinstance(tgt, ast.Name) and isinstance(val, ast.Constant) and isinstance(val.value, int) \
+                    and not isinstance(val.value, bool):
+                out[tgt.id] = val.value
+    return out
+
+
+def _pointer_params(spec):
+    return [n for n, s in spec.signature.items() if isinstance(s, str) and s.startswith("*")]
+
+
+def _lower_gemm(spec, tree, src):
+    c = _int_assigns(tree)
+    for n in ("M", "N", "K"):
+        if n not in c:
+            raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a tl.dot program without constant {n}")
+    M, N, K = c["M"], c["N"], c["K"]
+    ptrs = _pointer_params(spec)
+    alias = {}
+    for n in ast.walk(tree):
+        if isinstance(n, ast.Assign) and isinstance(n.targets[0], ast.Name) and isinstance(n.value, ast.Name) \
+                and n.value.id in ptrs:
+            alias[n.targets[0].id] = n.value.id
+
+    def resolve(name):
+        return alias.get(name, name)
+
+    loaded, stored = [], []
+    for n in ast.walk(tree):
+        if isinstance(n, ast.Call) and isinstance(n.func, ast.Attribute) and n.func.attr in ("load", "store") and n.args:
+            base = n.args[0]
+            while isinstance(base, ast.BinOp):
+                base = base.left
+            if isinstance(base, ast.Name) and resolve(base.id) in ptrs:
+                (loaded if n.func.attr == "load" else stored).append(resolve(base.id))
+    a_name = resolve("A") if "A" in alias else ("arg_A" if "arg_A" in ptrs else None)
+    b_name = resolve("B") if "B" in alias else ("arg_B" if "arg_B" in ptrs else None)
+    if a_name is None or b_name is None or len(set(stored)) != 1:
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: cannot name the matmul operands")
+    c_name = stored[0]
+    resid = [p for p in set(loaded) if p not in (a_name, b_name)]
+    if len(resid) > 1:
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: an epilogue reading {resid}")
+    idx = {n: i for i, n in enumerate(ptrs)}
+    a, b, cc = idx[a_name], idx[b_name], idx[c_name]
+    for t, nm in ((a, "A"), (b, "B")):
+        if spec.args[t].dtype != "bfloat16":
+            raise Refused(Reason.DTYPE_NOT_RUN, f"{spec.name}: matmul operand {nm} is {spec.args[t].dtype}; the "
+                                                f"executor's tensor-core path takes bf16")
+    if M == 1:
+        raise Refused(Reason.MATRIX_UNIT_ONE_ROW, f"{spec.name}: M=1 (the reference refuses it on the MXU too)")
+    sam, sak = c.get("stride_am", K), c.get("stride_ak", 1)
+    sbk, sbn = c.get("stride_bk", N), c.get("stride_bn", 1)
+    if sak != 1:
+        raise Refused(Reason.SHAPE_NOT_RUN, f"{spec.name}: A with K stride {sak}")
+    if sbn == 1:
+        b_kmajor, ldb = 0, sbk
+    elif sbk == 1:
+        b_kmajor, ldb = 1, sbn
+    else:
+        raise Refused(Reason.SHAPE_NOT_RUN, f"{spec.name}: B with strides ({sbk}, {sbn})")
+    m = re.search(r"(?:idx_n|out_n)\s*\+\s*(\d+)\s*\*\s*(?:idx_m|out_m)", src)
+    ldc = int(m.group(1)) if m else N
+    d = D.new(D.GEMM, _manifest_args(spec), spec.grid, units=M, unit_size=1)
+    g = d.p.gemm
+    g.M, g.N, g.K = M, N, K
+    g.lda, g.ldb, g.ldc, g.ldr = sam, ldb, ldc, ldc
+    g.a_arg, g.b_arg, g.c_arg = a, b, cc
+    g.r_arg = idx[resid[0]] if resid else -1
+    g.b_kmajor = b_kmajor
+    return Lowered(d, D.describe(d))
+
+
+def _lower_attention(spec, tree):
+    ce = spec.constexprs
+    HQ, G, S, Dh = int(ce["HQ"]), int(ce["G"]), int(ce["S"]), int(ce["D"])
+    ptrs = _pointer_params(spec)
+    idx = {n: i for i, n in enumerate(ptrs)}
+    need = ("q_ptr", "k_ptr", "v_ptr", "o_ptr")
+    if not all(n in idx for n in need):
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: attention wants q_ptr, k_ptr, v_ptr, o_ptr")
+    q = spec.args[idx["q_ptr"]]
+    batch = q.numel // (HQ * S * Dh)
+    if batch * HQ * S * Dh != q.numel or HQ % G:
+        raise Refused(Reason.SHAPE_NOT_RUN, f"{spec.name}: q of {q.numel} elements is not B x {HQ} x {S} x {Dh}")
+    gx = _grid_programs(spec)[0]
+    if gx != batch * HQ:
+        raise Refused(Reason.SHAPE_NOT_RUN, f"{spec.name}: grid {gx} is not batch x heads = {batch * HQ}")
+    d = D.new(D.ATTN_PREFILL, _manifest_args(spec), spec.grid, units=gx, unit_size=1)
+    a = d.p.attn
+    a.batch, a.hq, a.hkv, a.seq, a.dim = batch, HQ, HQ // G, S, Dh
+    a.q_arg, a.k_arg, a.v_arg, a.o_arg = idx["q_ptr"], idx["k_ptr"], idx["v_ptr"], idx["o_ptr"]
+    a.causal = 1 if ce.get("CAUSAL", True) else 0
+    a.scale = float(ce["SCALE"])
+    a.ref_bq, a.ref_bkv = int(ce.get("BQ", 0)), int(ce.get("BKV", 0))
+    return Lowered(d, D.describe(d))

@@ -1,0 +1,273 @@
+"""Generate the committed parity fixtures from the reference (run in the build container, where the read-only
+reference tree exists; the GPU box only reads what this writes):
+
+  tests/golden/objects/<case>/kernel.json + desc.bin
+      the B200 lowering of the reference's own kernel (its KernelSpec and Triton source, loaded from the
+      reference tree), i.e. the kernel object the CUDA device runs; plus case.json: the input convention
+      (the reference spec's make_inputs: one generator seeded 0, randn per read argument in order) and the
+      oracle program with its parameters, read off the kernel source by hand (cited below);
+  tests/golden/vectors/<case>.npz
+      for the small cases, the outputs of the reference's kernel executed by the Triton interpreter
+      (TRITON_INTERPRET=1, numpy) on make_inputs(torch, seed=0): the functional result of the reference's
+      program.  Outputs over 8192 elements are stored as an evenly strided sample plus the SHA-256 of the
+      whole output.
+
+Two shims make the interpreter run these kernels, neither changing what a kernel computes:
+  - Triton 3.6's interpreter multiplies bf16 tl.dot operands as their raw uint16 bits; the shim widens
+    them to fp32 first (the value tl.dot(bf16, bf16, out_dtype=fp32) is defined to use);
+  - Inductor's `libdevice.exp / rsqrt` resolve to the CUDA libdevice module, which the interpreter does not
+    patch; the shim routes them to tl.exp / tl.rsqrt.
+The interpreter's and Triton's block limit (2**20 elements) is lifted so the bundle's large blocks run.
+
+    python tests/golden/make_golden.py [--only <case>]"""
+import argparse
+import contextlib
+import copy
+import dataclasses
+import hashlib
+import json
+import math
+import os
+import shutil
+import sys
+
+os.environ["TRITON_INTERPRET"] = "1"
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+REF = os.environ.get("PTSIM_REFERENCE", "/root/reference")
+sys.path.insert(0, os.path.join(ROOT, "pytorchsim-triton-backend_b200"))
+sys.path.insert(0, ROOT)
+
+V = os.path.join(REF, "validation", "pytorchsim")
+Q2048 = "qwen3_8b_layer_prefill_2048x2048_bf16"
+Q128 = "qwen3_8b_layer_prefill_128x128_bf16"
+Q4096 = "qwen3_8b_layer_prefill_4096x4096_bf16"
+EPS = 1e-6
+
+
+def kdir(workload, idx):
+    """The kernel directory `idx` (two digits) of a bundle workload."""
+    base = os.path.join(V, workload)
+    d = next(n for n in sorted(os.listdir(base)) if n.startswith(f"{idx:02d}_"))
+    return os.path.join(base, d)
+
+
+def spec_file(workload, idx):
+    d = kdir(workload, idx)
+    return os.path.join(d, next(f for f in os.listdir(d) if f.endswith("_spec.py")))
+
+
+def qwen_cases(wl, T, tag, golden):
+    """The 12 kernels of a Qwen3-8B prefill layer workload (manifest.json launches), with the oracle program
+    each restates (parameters from the kernel sources: hidden 4096, 32 q / 8 kv heads of 128, SiLU
+    intermediate 12288, eps 1e-6 -- e.g. qwen3_8b_layer_prefill_2048x2048_bf16/00_*_triton.py xnumel/r0_numel,
+    09_*: N = 24576)."""
+    H, HQ, HKV, D, I = 4096, 32, 8, 128, 12288
+    return [
+        (f"{tag}_00_rmsnorm", spec_file(wl, 0), {"family": "rmsnorm_rows", "rows": T, "cols": H, "eps": EPS}, golden),
+        (f"{tag}_01_q_mm", spec_file(wl, 1), {"family": "gemm", "M": T, "N": HQ * D, "K": H, "residual": False}, golden),
+        (f"{tag}_02_qnorm_rope", spec_file(wl, 2), {"family": "qknorm_rope", "tokens": T, "heads": HQ, "eps": EPS}, golden),
+        (f"{tag}_03_kv_mm", spec_file(wl, 3), {"family": "gemm", "M": T, "N": HKV * D, "K": H, "residual": False}, golden),
+        (f"{tag}_04_knorm_rope", spec_file(wl, 4), {"family": "qknorm_rope", "tokens": T, "heads": HKV, "eps": EPS}, golden),
+        (f"{tag}_05_v_relayout", spec_file(wl, 5), {"family": "token_to_head_major", "tokens": T, "heads": HKV, "dim": D}, golden),
+        (f"{tag}_06_attention", spec_file(wl, 6), {"family": "attention_prefill", "batch": 1, "hq": HQ, "g": HQ // HKV,
+                                                   "seq": T, "dim": D, "causal": True, "scale": 1 / math.sqrt(D)}, golden),
+        (f"{tag}_07_o_relayout", spec_file(wl, 7), {"family": "heads_to_token_major", "tokens": T, "heads": HQ, "dim": D}, golden),
+        (f"{tag}_08_o_mm_residual", spec_file(wl, 8), {"family": "gemm", "M": T, "N": H, "K": HQ * D, "residual": True}, golden),
+        (f"{tag}_09_gate_up_mm", spec_file(wl, 9), {"family": "gemm", "M": T, "N": 2 * I, "K": H, "residual": False}, golden),
+        (f"{tag}_10_silu_mul", spec_file(wl, 10), {"family": "silu_mul", "tokens": T, "inter": I}, golden),
+        (f"{tag}_11_down_mm_residual", spec_file(wl, 11), {"family": "gemm", "M": T, "N": H, "K": I, "residual": True}, golden),
+    ]
+
+
+def add_config(spec):
+    """tests/cases/smoke/add.py at BASELINE.json configs[0]: x, y fp32 of 1,048,576, BLOCK_SIZE 1024."""
+    from pytorchsim_triton_compiler.contract.kernel_spec import Arg
+    n, blk = 1_048_576, 1024
+    s = copy.copy(spec)
+    s.constexprs = {"n": n, "BLOCK": blk}
+    s.args = [Arg(a.name, a.role, a.dtype, (n,)) for a in spec.args]
+    s.grid = (n // blk,)
+    return s
+
+
+def attention_batch4(spec):
+    """The bundle's attention_prefill_32x8x4096_bf16 kernel at BASELINE.json's batch 4 (its program index
+    decodes b = pid // HQ, _prefill_kernel_triton.py:7-11): q/o of 4x the elements, grid 4 x 32."""
+    from pytorchsim_triton_compiler.contract.kernel_spec import Arg
+    s = copy.copy(spec)
+    s.args = [Arg(a.name, a.role, a.dtype, (a.numel * 4,)) for a in spec.args]
+    s.grid = (4 * spec.grid[0], 1, 1)
+    return s
+
+
+def cases():
+    out = [
+        ("smoke_add_1024", os.path.join(REF, "tests", "cases", "smoke", "add.py"), {"family": "vector_add"}, True),
+        ("vector_add_1m", os.path.join(REF, "tests", "cases", "smoke", "add.py"), {"family": "vector_add", "modify": "add_config"}, False),
+        ("vector_add1_8x128", spec_file("vector_add1_8x128_bf16", 0), {"family": "add_one"}, True),
+        ("vector_add1_4096x4096", spec_file("vector_add1_4096x4096_bf16", 0), {"family": "add_one"}, False),
+        ("vector_slice_8x128", spec_file("vector_slice_8x128_bf16", 0), {"family": "slice_add_one"}, True),
+        ("vector_sum_8x128", spec_file("vector_sum_8x128_bf16", 0), {"family": "reduce_all", "op": "sum"}, True),
+        ("vector_max_8x128", spec_file("vector_max_8x128_bf16", 0), {"family": "reduce_all", "op": "max"}, True),
+        ("vector_sum_4096x4096", spec_file("vector_sum_4096x4096_bf16", 0), {"family": "reduce_all", "op": "sum"}, False),
+        ("vector_max_4096x4096", spec_file("vector_max_4096x4096_bf16", 0), {"family": "reduce_all", "op": "max"}, False),
+        ("softmax_32x128", spec_file("vector_softmax_32x128_bf16", 0), {"family": "softmax_rows", "rows": 32, "cols": 128}, True),
+        ("softmax_128x1536", spec_file("vector_softmax_128x1536_bf16", 0), {"family": "softmax_rows", "rows": 128, "cols": 1536}, True),
+        ("softmax_4096x4096", spec_file("vector_softmax_4096x4096_bf16", 0), {"family": "softmax_rows", "rows": 4096, "cols": 4096}, False),
+        ("rmsnorm_4096x4096", spec_file(Q4096, 0), {"family": "rmsnorm_rows", "rows": 4096, "cols": 4096, "eps": EPS}, False),
+        ("gemm_32x768x768", spec_file("gemm_32x768x768_bf16", 0), {"family": "gemm", "M": 32, "N": 768, "K": 768, "residual": False}, True),
+        ("gemm_128x768x768", spec_file("gemm_128x768x768_bf16", 0), {"family": "gemm", "M": 128, "N": 768, "K": 768, "residual": False}, True),
+        ("attention_16x8x128", spec_file("attention_prefill_16x8x128_bf16", 0),
+         {"family": "attention_prefill", "batch": 1, "hq": 16, "g": 2, "seq": 128, "dim": 128, "causal": True,
+          "scale": 1 / math.sqrt(128)}, True),
+        ("attention_32x8x4096_b4", spec_file("attention_prefill_32x8x4096_bf16", 0),
+         {"family": "attention_prefill", "batch": 4, "hq": 32, "g": 4, "seq": 4096, "dim": 128, "causal": True,
+          "scale": 1 / math.sqrt(128), "modify": "attention_batch4"}, False),
+    ]
+    for m in (128, 512, 2048, 4096, 8192):
+        out.append((f"gemm_{m}x4096x4096", spec_file(f"gemm_{m}x4096x4096_bf16", 0),
+                    {"family": "gemm", "M": m, "N": 4096, "K": 4096, "residual": False}, False))
+    out += qwen_cases(Q128, 128, "qwen3_t128", True)
+    out += qwen_cases(Q2048, 2048, "qwen3_t2048", False)
+    return out
+
+
+MODIFY = {"add_config": add_config, "attention_batch4": attention_batch4}
+
+# ---------------------------------------------------------------------------------------------------
+# Triton interpreter shims
+# ---------------------------------------------------------------------------------------------------
+
+
+def install_interpreter_shims():
+    import numpy as np
+    import triton._utils as tu
+    import triton.language.core as tc
+    from triton.runtime import interpreter as I
+    tu.TRITON_MAX_TENSOR_NUMEL = 1 << 40
+    tc.TRITON_MAX_TENSOR_NUMEL = 1 << 40
+    orig = I.InterpreterBuilder.create_dot
+
+    def create_dot(self, a, b, d, input_precision, max_num_imprecise_acc):
+        def widen(h):
+            if str(h.dtype.scalar) == "bf16":
+                return I.TensorHandle((h.data.astype(np.uint32) << 16).view(np.float32), I.tl.float32)
+            return h
+        return orig(self, widen(a), widen(b), d, input_precision, max_num_imprecise_acc)
+
+    I.InterpreterBuilder.create_dot = create_dot
+
+
+class _Libdevice:
+    """libdevice.<fn> of Inductor kernels routed to the interpreter's tl.<fn>."""
+
+    def __getattr__(self, name):
+        import triton.language as tl
+        return getattr(tl, name)
+
+
+def interpret(spec, inputs):
+    """Run `spec`'s kernel under the Triton interpreter over copies of `inputs`; return every written arg."""
+    import torch
+    import triton
+    from pytorchsim_triton_compiler.targets.b200.frontend import load_kernel
+    fn = load_kernel(spec)
+    while hasattr(fn, "fn") and not isinstance(fn, triton.runtime.interpreter.InterpretedFunction):
+        fn = fn.fn
+    inner = getattr(fn, "fn", fn)
+    if "libdevice" in getattr(inner, "__globals__", {}):
+        inner.__globals__["libdevice"] = _Libdevice()
+    tens = []
+    for a in spec.args:
+        if a.name in inputs:
+            tens.append(inputs[a.name].clone())
+        else:
+            tens.append(torch.zeros(a.shape, dtype=getattr(torch, a.dtype)))
+    scal = spec.extra.get("scalar_values", {})
+    kw = {}
+    ti = 0
+    for n, s in spec.signature.items():
+        if n in spec.constexprs:
+            kw[n] = spec.constexprs[n]
+        elif s == "constexpr":
+            continue
+        elif s.startswith("*"):
+            kw[n] = tens[ti]
+            ti += 1
+        else:
+            kw[n] = scal.get(n, 0)
+    fn[tuple(spec.grid)](**kw)
+    return {a.name: t for a, t in zip(spec.args, tens) if a.role in ("out", "inout")}
+
+
+def bits(t):
+    import torch
+    t = t.contiguous()
+    return t.view(torch.int16).numpy() if t.dtype == torch.bfloat16 else t.numpy()
+
+
+def main():
+    import numpy as np
+    import torch
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", default=None)
+    ap.add_argument("--no-golden", action="store_true")
+    opts = ap.parse_args()
+    from pytorchsim_triton_compiler.contract import kernel_object as ko
+    from pytorchsim_triton_compiler.contract.kernel_spec import load_spec
+    from pytorchsim_triton_compiler.targets.b200 import lower as L
+    install_interpreter_shims()
+    objdir, vecdir = os.path.join(HERE, "objects"), os.path.join(HERE, "vectors")
+    os.makedirs(objdir, exist_ok=True)
+    os.makedirs(vecdir, exist_ok=True)
+    index = []
+    for name, path, oracle, golden in cases():
+        if opts.only and opts.only != name:
+            continue
+        spec = load_spec(path)
+        if oracle.get("modify"):
+            spec = MODIFY[oracle.pop("modify")](spec)
+        lowered = L.lower(spec)
+        d = os.path.join(objdir, name)
+        shutil.rmtree(d, ignore_errors=True)
+        ko.write(d, spec, lowered.summary, lowered.blob)
+        gen = [{"name": a.name, "role": a.role, "dtype": a.dtype, "numel": a.numel} for a in spec.args]
+        reads = [a.name for a in spec.args if a.role in ("in", "inout")]
+        case = {"name": name, "source": os.path.relpath(path, REF), "kind": lowered.kind, "args": gen,
+                "inputs": reads, "oracle": oracle, "golden": None}
+        if golden and not opts.no_golden:
+            g = torch.Generator().manual_seed(0)
+            if spec.make_inputs is None:
+                raise SystemExit(f"{name}: no make_inputs")
+            inputs = spec.make_inputs(torch, seed=0)
+            if list(inputs) != reads:
+                raise SystemExit(f"{name}: make_inputs builds {list(inputs)}, the read arguments are {reads}")
+            outs = interpret(spec, inputs)
+            payload = {}
+            for k, t in outs.items():
+                flat = t.reshape(-1)
+                full = bits(flat)
+                payload[f"{k}__sha256"] = np.frombuffer(hashlib.sha256(full.tobytes()).digest(), dtype=np.uint8)
+                if flat.numel() > 8192:
+                    stride = -(-flat.numel() // 8192)
+                    payload[f"{k}__stride"] = np.array([stride], dtype=np.int64)
+                    payload[k] = full[::stride].copy()
+                else:
+                    payload[f"{k}__stride"] = np.array([1], dtype=np.int64)
+                    payload[k] = full
+            np.savez_compressed(os.path.join(vecdir, f"{name}.npz"), **payload)
+            case["golden"] = f"vectors/{name}.npz"
+        with open(os.path.join(d, "case.json"), "w") as fh:
+            json.dump(case, fh, indent=1)
+            fh.write("\n")
+        index.append(name)
+        print(f"{name:32s} {lowered.kind:12s} golden={'yes' if case['golden'] else 'no'}", flush=True)
+    if not opts.only:
+        with open(os.path.join(HERE, "index.json"), "w") as fh:
+            json.dump(index, fh, indent=1)
+            fh.write("\n")
+
+
+if __name__ == "__main__":
+    main()
