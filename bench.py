@@ -1,0 +1,390 @@
+"""Benchmark of the B200 functional executor on BASELINE.json's headline configuration.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--no-suite]
+
+Workload (the metric's "GB/s vs B200 roofline"): one step = the reference's
+vector-unit row programs over bf16 [4096, 4096] -- the bundle's softmax kernel
+(vector_softmax_4096x4096_bf16/00_*) and the Qwen3 RMSNorm kernel (qwen3_8b_layer_prefill_4096x4096_bf16/00_*,
+weight N(1, 0.02), eps 1e-6) -- each executed from its lowered kernel object (tests/golden/objects/) through
+the C ABI.  Inputs N(0, 1) from seed 0, resident in HBM; L2 (126 MB) is flushed by a 512 MiB write before
+every timed step; each step is timed with CUDA events on the launching stream, max over ranks.
+Multi-GPU: every rank runs its own copy of the workload (independent programs, no collective): weak
+scaling, value = all ranks' bytes / the slowest rank's time.
+
+Algorithmic bytes per step: softmax 2 * 2 * 4096^2 = 67,108,864; RMSNorm 67,108,864 + 8,192 (weight).
+`e2e` repeats the step through the same API with the inputs copied from pinned host memory and both
+outputs read back inside the timed region.  `cpu_baseline` times the CPU oracle (torch, all host threads)
+on the same programs.  --impl reference runs only that CPU restatement of the reference's programs (the
+reference's own functional simulator, Spike + the Coprocessor model, is not installable here)."""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "pytorchsim-triton-backend_b200"))
+sys.path.insert(0, ROOT)
+
+OBJECTS = os.path.join(ROOT, "tests", "golden", "objects")
+METRIC = "lowered-kernel GB/s (softmax + RMSNorm bf16 4096x4096) vs B200 HBM roofline"
+SOFTMAX_BYTES = 2 * 2 * 4096 * 4096
+RMSNORM_BYTES = 2 * 2 * 4096 * 4096 + 2 * 4096
+STEP_BYTES = SOFTMAX_BYTES + RMSNORM_BYTES
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            p = json.load(fh)
+        return float(p["hbm_gbs"]), float(p.get("bf16_tflops", 1590.0)), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, 1590.0, "fallback"
+
+
+def load_object(name):
+    from pytorchsim_triton_compiler.contract import kernel_object as ko
+    d = os.path.join(OBJECTS, name)
+    m = ko.read(d)
+    return m, ko.read_desc(d, m)
+
+
+def profile_traffic(kernel):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary (profiles/traffic.json), or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as fh:
+            t = json.load(fh)
+        return t.get(kernel, {}).get("dram_bytes_per_launch")
+    except (OSError, ValueError):
+        return None
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clock and throttle reasons during the timed region."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.proc, self.path = index, None, None
+
+    def start(self):
+        import tempfile
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.index), "-lms", "200"], stdout=open(self.path, "w"),
+                                         stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as fh:
+            for line in fh:
+                f = [x.strip() for x in line.split(",")]
+                if len(f) >= 9:
+                    rows.append(f)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        loaded = [s for s in sm if s > 0.5 * (max(mx) if mx else 1)] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def dist_setup(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and args.impl == "b200":
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    return world, rank, local
+
+
+def reduce_max(v, world, device=None):
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(v)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ---------------------------------------------------------------------------------------------------
+# CPU oracle timing (cpu_baseline and the reference arm)
+# ---------------------------------------------------------------------------------------------------
+
+def cpu_step_inputs(rows):
+    import torch
+    g = torch.Generator().manual_seed(0)
+    xs = torch.randn(rows * 4096, generator=g).to(torch.bfloat16)
+    xr = torch.randn(rows * 4096, generator=g).to(torch.bfloat16)
+    w = (torch.randn(4096, generator=g) * 0.02 + 1.0).to(torch.bfloat16)
+    return xs, xr, w
+
+
+def cpu_rate(seconds=10.0, rows=4096):
+    """GB/s of the CPU oracle on the workload, timed for about `seconds` of repeated full steps."""
+    import torch
+    from oracle import programs as O
+    torch.set_num_threads(max(1, len(os.sched_getaffinity(0))))
+    xs, xr, w = cpu_step_inputs(rows)
+    O.softmax_rows(xs, rows, 4096)
+    O.rmsnorm_rows(xr, w, rows, 4096, 1e-6)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        O.softmax_rows(xs, rows, 4096)
+        O.rmsnorm_rows(xr, w, rows, 4096, 1e-6)
+        n += 1
+        dt = time.perf_counter() - t0
+        if dt >= seconds or n >= 200:
+            break
+    bytes_per = (STEP_BYTES * rows) / 4096
+    return {"value": round(n * bytes_per / dt / 1e9, 3), "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"{n} full steps ({rows}x4096 softmax + RMSNorm) in {dt:.1f} s, torch CPU "
+                                      f"restatement of the reference programs (oracle/programs.py)"}, dt / n
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    base, sec_per_step = cpu_rate(seconds=min(30.0, 4.0 * max(1, args.steps)))
+    line = {"metric": METRIC, "value": base["value"], "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(sec_per_step * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "softmax+rmsnorm bf16 [4096,4096] (BASELINE.json configs[1])", "rows": 4096,
+                       "cols": 4096, "l2": "n/a (CPU)"},
+            "impl": "reference", "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the reference's functional simulator (Spike + Coprocessor model) is not installable here; "
+                    "this arm times the CPU restatement of the same programs on all host threads"}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------------------
+# B200 arm
+# ---------------------------------------------------------------------------------------------------
+
+def run_b200(args, world, rank, local):
+    import torch
+    from pytorchsim_triton_compiler.codegen import descriptors as D
+    from pytorchsim_triton_compiler.runtime import cuda as RC
+    from pytorchsim_triton_compiler.runtime import native
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    native.init(local)
+    m_s, d_s = load_object("softmax_4096x4096")
+    m_r, d_r = load_object("rmsnorm_4096x4096")
+    xs_h, xr_h, w_h = cpu_step_inputs(4096)
+    xs, xr, w = xs_h.to(dev), xr_h.to(dev), w_h.to(dev)
+    ys = torch.empty_like(xs)
+    yr = torch.empty_like(xr)
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+
+    def step(ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        native.launch(d_s, [xs.data_ptr(), ys.data_ptr()], 0, D.from_bytes(d_s).units, stream=sp)
+        if ev is not None:
+            ev[1].record(stream)
+        native.launch(d_r, [xr.data_ptr(), w.data_ptr(), yr.data_ptr()], 0, D.from_bytes(d_r).units, stream=sp)
+        if ev is not None:
+            ev[2].record(stream)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    native.sync(sp)
+    # Correctness of what is timed: compare one row block against the oracle.
+    from oracle import programs as O
+    chk = slice(0, 64 * 4096)
+    want_s = O.softmax_rows(xs_h[chk], 64, 4096)
+    want_r = O.rmsnorm_rows(xr_h[chk], w_h, 64, 4096, 1e-6)
+    ok = torch.allclose(ys[chk].float().cpu(), want_s.float(), rtol=1e-2, atol=1e-4) and \
+        torch.allclose(yr[chk].float().cpu(), want_r.float(), rtol=1e-2, atol=1e-2)
+    if not ok:
+        raise SystemExit("bench: the timed kernels disagree with the oracle")
+
+    clocks = Clocks(local)
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks.start()
+    for k in range(args.steps):
+        flush.zero_()               # L2 flush, outside the timed events
+        step(events[k])
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    native.sync(sp)
+    t_soft = [e[0].elapsed_time(e[1]) for e in events]
+    t_rms = [e[1].elapsed_time(e[2]) for e in events]
+    total_ms = sum(t_soft) + sum(t_rms)
+    total_ms = reduce_max(total_ms, world, dev)
+    ms_per_step = total_ms / args.steps
+    value = world * STEP_BYTES * args.steps / (total_ms / 1e3) / 1e9
+
+    # e2e: the same step through the C ABI with host buffers (pinned), copies inside the timed region.
+    xs_p, xr_p, w_p = xs_h.pin_memory(), xr_h.pin_memory(), w_h.pin_memory()
+    ys_p, yr_p = torch.empty_like(xs_p).pin_memory(), torch.empty_like(xr_p).pin_memory()
+    e2e_steps = max(3, args.steps)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h2d = xs_p.numel() * 2 + xr_p.numel() * 2 + w_p.numel() * 2
+    d2h = ys_p.numel() * 2 + yr_p.numel() * 2
+    e2e_ms = 0.0
+    for k in range(e2e_steps + 1):
+        flush.zero_()
+        e0.record(stream)
+        xs.copy_(xs_p, non_blocking=True)
+        xr.copy_(xr_p, non_blocking=True)
+        w.copy_(w_p, non_blocking=True)
+        step()
+        ys_p.copy_(ys, non_blocking=True)
+        yr_p.copy_(yr, non_blocking=True)
+        e1.record(stream)
+        e1.synchronize()
+        if k > 0:
+            e2e_ms += e0.elapsed_time(e1)
+    native.sync(sp)
+    e2e_ms = reduce_max(e2e_ms, world, dev)
+    e2e_val = world * STEP_BYTES * e2e_steps / (e2e_ms / 1e3) / 1e9
+
+    hbm, _, peak_src = peaks()
+    soft_ms, rms_ms = sum(t_soft) / len(t_soft), sum(t_rms) / len(t_rms)
+    dom, dom_ms, dom_bytes = ("row_softmax", soft_ms, SOFTMAX_BYTES) if sum(t_soft) >= sum(t_rms) else \
+        ("row_rmsnorm", rms_ms, RMSNORM_BYTES)
+    achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+    line = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "softmax+rmsnorm bf16 [4096,4096] (BASELINE.json configs[1])",
+                       "rows": 4096, "cols": 4096, "programs": ["vector_softmax_4096x4096_bf16/00",
+                                                                 "qwen3_8b_layer_prefill_4096x4096_bf16/00"],
+                       "l2": "flushed (512 MiB write) before every timed step", "parallelism": f"replicas x{world}"},
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(achieved / hbm, 4), "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)",
+                         "traffic": profile_traffic(dom),
+                         "per_kernel": {"row_softmax": {"ms": round(soft_ms, 4), "GB/s": round(SOFTMAX_BYTES / soft_ms / 1e6, 1)},
+                                        "row_rmsnorm": {"ms": round(rms_ms, 4), "GB/s": round(RMSNORM_BYTES / rms_ms / 1e6, 1)}}},
+            "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "api": "runtime.native.launch (C ABI ptsim_launch) with pinned host buffers"},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk}
+    if rank == 0 and world == 1:
+        base, _ = cpu_rate(seconds=10.0)
+        line["cpu_baseline"] = base
+        if args.suite:
+            line["suite"] = suite(dev, stream)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def suite(dev, stream, iters=5):
+    """Device-timed throughput of the other BASELINE.json configurations' lowered kernels (not the
+    headline): median of `iters` launches with an L2 flush before each."""
+    import torch
+    from pytorchsim_triton_compiler.codegen import descriptors as D
+    from pytorchsim_triton_compiler.runtime import native
+    hbm, tflops, _ = peaks()
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    out = {}
+
+    def timed(name, bound, work):
+        m, blob = load_object(name)
+        d = D.from_bytes(blob)
+        g = torch.Generator(device=dev).manual_seed(0)
+        ts = []
+        for a in m["args"]:
+            dt = getattr(torch, a["dtype"])
+            n = math.prod(a["shape"])
+            if a["role"] in ("in", "inout") and dt.is_floating_point:
+                std = 1.0
+                if d.kind == D.GEMM and a["name"] in ("arg_A", "arg_B"):
+                    std = 1.0 / math.sqrt(d.p.gemm.K)   # N(0, 1/sqrt(K))
+                ts.append((torch.randn(n, generator=g, device=dev) * std).to(dt))
+            else:
+                ts.append(torch.zeros(n, dtype=dt, device=dev))
+        ws = torch.empty(max(1, d.workspace_bytes), dtype=torch.uint8, device=dev)
+        ptrs = [t.data_ptr() for t in ts]
+        times = []
+        for k in range(iters + 1):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            native.launch(blob, ptrs, 0, d.units, ws.data_ptr(), d.workspace_bytes, stream.cuda_stream)
+            b.record(stream)
+            b.synchronize()
+            if k:
+                times.append(a.elapsed_time(b))
+        native.sync(stream.cuda_stream)
+        ms = statistics.median(times)
+        if bound == "hbm":
+            gbs = work / ms / 1e6
+            out[name] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm, 3)}
+        else:
+            tf = work / ms / 1e9
+            out[name] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1), "frac_bf16": round(tf / tflops, 3)}
+
+    timed("vector_add_1m", "hbm", 3 * 4 * 1_048_576)
+    for m in (128, 512, 2048, 4096, 8192):
+        timed(f"gemm_{m}x4096x4096", "tensor", 2 * m * 4096 * 4096)
+    timed("attention_32x8x4096_b4", "tensor", 549_755_813_888)
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--no-suite", dest="suite", action="store_false")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_b200(args, world, rank, local)
+    finally:
+        if world > 1 and args.impl == "b200":
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,79 @@
+"""The Triton backend's launch side, kept call-compatible with the reference
+(pytorchsim_triton_compiler/triton_extension/python/pytorchsim_triton_backend/driver.py:14-149):
+
+  set_launcher(fn)   registers the function that runs a compiled kernel,
+                     fn(binary, kernel_object, grid, args, artifacts=); None unregisters;
+  _Launcher          Triton's per-kernel launcher: drops constexpr arguments, passes constexpr values in
+                     the kernel object's "constexprs", and hands (binary, kernel_object, grid, args) to the
+                     registered function; a launch with none registered raises RuntimeError;
+  PYTORCHSIM_COLLECT_FAILURES makes a launch a no-op, as in the reference.
+
+B200 edition: `binary` is the kernel object's launch descriptor (desc.bin) instead of the ELF, and
+`cuda_launcher` is the launcher this package offers the device owner: it runs the descriptor on the CUDA
+device holding the tensor arguments (runtime/cuda.py launch_tensors), in place, on torch's current stream."""
+import json
+import os
+
+_LAUNCHER = None
+
+
+def set_launcher(fn):
+    """Register the function that runs a compiled kernel (None unregisters)."""
+    global _LAUNCHER
+    _LAUNCHER = fn
+
+
+def _launcher():
+    if _LAUNCHER is None:
+        raise RuntimeError("no launcher is registered with the pytorchsim triton backend: the owner of the device "
+                           "registers one with pytorchsim_triton_backend.driver.set_launcher")
+    return _LAUNCHER
+
+
+class _Launcher:
+    """Triton's launcher for one compiled kernel.  `signature` is the kernel's {name: type} (constexpr
+    parameters typed "constexpr"), `constants` the constexpr values by parameter position."""
+
+    def __init__(self, src, metadata):
+        self.metadata = metadata
+        sig = getattr(src, "signature", {}) or {}
+        self.width = len(sig)
+        consts = getattr(src, "constants", {}) or {}
+        self.constexpr = {i for i, ty in enumerate(sig.values()) if ty == "constexpr"} | \
+                         {k[0] for k in consts if isinstance(k, tuple)}
+        names = list(sig)
+        self.constexprs = {names[k[0]]: v for k, v in consts.items()
+                           if isinstance(k, tuple) and len(k) == 1 and k[0] < len(names)
+                           and isinstance(v, (int, float, bool))}
+        _launcher()
+
+    def __call__(self, grid_x, grid_y, grid_z, stream, function, packed_metadata, launch_metadata,
+                 enter_hook, exit_hook, *args):
+        if os.environ.get("PYTORCHSIM_COLLECT_FAILURES"):
+            return
+        kobj = getattr(self.metadata, "kernel_object", "")
+        if not kobj:
+            raise RuntimeError("this kernel was compiled without pytorchsim_spec, which stops at the Triton IR: it "
+                               "has no binary to launch")
+        if len(args) == self.width:
+            args = tuple(a for i, a in enumerate(args) if i not in self.constexpr)
+        if self.constexprs:
+            kobj = json.dumps({**json.loads(kobj), "constexprs": self.constexprs})
+        _launcher()(function, kobj, (grid_x, grid_y, grid_z), args,
+                    artifacts=getattr(self.metadata, "artifacts", None))
+
+
+def cuda_launcher(binary, kernel_object, grid, args, artifacts=None):
+    """A launcher for set_launcher: run descriptor `binary` over the tensor arguments `args` (scalars, which
+    the lowering already folded into the descriptor, are skipped) on their CUDA device."""
+    from pytorchsim_triton_compiler.contract import kernel_object as ko
+    from pytorchsim_triton_compiler.runtime import cuda as RC
+    manifest = json.loads(kernel_object) if isinstance(kernel_object, (str, bytes)) else kernel_object
+    ko.refuse_grid_past_bound(manifest, grid)
+    if tuple(ko.grid3(grid)) != tuple(ko.grid3(manifest["grid"])):
+        raise RuntimeError(f"{manifest.get('name')}: lowered for grid {tuple(ko.grid3(manifest['grid']))}, launched "
+                           f"with {tuple(ko.grid3(grid))}; relower for the new grid")
+    tensors = [a for a in args if hasattr(a, "data_ptr")]
+    if len(tensors) != len(manifest["args"]):
+        raise RuntimeError(f"{manifest.get('name')}: {len(tensors)} tensors for {len(manifest['args'])} arguments")
+    return RC.launch_tensors(bytes(binary), [t.contiguous() if not t.is_contiguous() else t for t in tensors])

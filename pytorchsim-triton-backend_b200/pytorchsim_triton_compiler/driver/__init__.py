@@ -1,1 +1,1 @@
-"""B200 driver package."""
+"""The stage machine (driver/compiler.py): lower a kernel file into a kernel object, run it, verify it."""

@@ -579,6 +579,8 @@ class Evaluator:
             return Reduce(op, v)
         if name in ("fma",):
             return Op("add", Op("mul", self.value(args[0]), self.value(args[1])), self.value(args[2]))
+        if name.startswith("atomic"):
+            raise Refused(Reason.ATOMICS, f"{f.name}: atomics have no tile program on this executor")
         raise Refused(Reason.MATH_UNLOWERED, f"call of {f.name}")
 
     def method(self, obj, attr, args, kw):

@@ -467,8 +467,11 @@ def _lower_gemm(spec, tree, src):
         b_kmajor, ldb = 1, sbn
     else:
         raise Refused(Reason.SHAPE_NOT_RUN, f"{spec.name}: B with strides ({sbk}, {sbn})")
-    m = re.search(r"(?:idx_n|out_n)\s*\+\s*(\d+)\s*\*\s*(?:idx_m|out_m)", src)
-    ldc = int(m.group(1)) if m else N
+    # The output index is the last `n + ldc * m` the template forms (the earlier ones index the operands).
+    found = re.findall(r"(?:idx_n|out_n)\s*\+\s*(\d+)\s*\*\s*(?:idx_m|out_m)", src)
+    ldc = int(found[-1]) if found else N
+    if ldc < N:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: output row stride {ldc} below N = {N}")
     d = D.new(D.GEMM, _manifest_args(spec), spec.grid, units=M, unit_size=1)
     g = d.p.gemm
     g.M, g.N, g.K = M, N, K

@@ -12,11 +12,14 @@ reference tree exists; the GPU box only reads what this writes):
       program.  Outputs over 8192 elements are stored as an evenly strided sample plus the SHA-256 of the
       whole output.
 
-Two shims make the interpreter run these kernels, neither changing what a kernel computes:
+Three shims make the interpreter run these kernels as the NPU defines them:
   - Triton 3.6's interpreter multiplies bf16 tl.dot operands as their raw uint16 bits; the shim widens
     them to fp32 first (the value tl.dot(bf16, bf16, out_dtype=fp32) is defined to use);
   - Inductor's `libdevice.exp / rsqrt` resolve to the CUDA libdevice module, which the interpreter does not
-    patch; the shim routes them to tl.exp / tl.rsqrt.
+    patch; the shim routes them to tl.exp / tl.rsqrt;
+  - the interpreter narrows fp32 to bf16 by truncation; the NPU packs bf16 rounding to nearest, ties to
+    even (misc.pack, targets/tpu/include/Dialect/PyTorchSimTpu/IR/PyTorchSimTpuOps.td:46-50), and so does
+    Triton's own default cast; the shim rounds to nearest even.
 The interpreter's and Triton's block limit (2**20 elements) is lifted so the bundle's large blocks run.
 
     python tests/golden/make_golden.py [--only <case>]"""
@@ -157,6 +160,31 @@ def install_interpreter_shims():
         return orig(self, widen(a), widen(b), d, input_precision, max_num_imprecise_acc)
 
     I.InterpreterBuilder.create_dot = create_dot
+
+    def to_bf16_rne(data):
+        b = np.ascontiguousarray(data, dtype=np.float32).view(np.uint32).astype(np.uint64)
+        r = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+        nan = np.isnan(np.ascontiguousarray(data, dtype=np.float32))
+        return np.where(nan, ((b >> 16) | 0x40).astype(np.uint16), r)
+
+    orig_cast = I.InterpreterBuilder.cast_impl
+
+    def cast_impl(self, src, dst_type):
+        if src.dtype.scalar == I.tl.float32 and dst_type.scalar == I.tl.bfloat16:
+            return I.TensorHandle(to_bf16_rne(src.data), dst_type.scalar)
+        return orig_cast(self, src, dst_type)
+
+    I.InterpreterBuilder.cast_impl = cast_impl
+    for name in ("create_fp_ext", "create_fp_trunc"):
+        setattr(I.InterpreterBuilder, name, lambda self, src, dst_type: self.cast_impl(src, dst_type))
+    orig_fp_to_fp = I.InterpreterBuilder.create_fp_to_fp
+
+    def create_fp_to_fp(self, src, dst_type, rounding_mode):
+        if src.dtype.scalar == I.tl.float32 and dst_type.scalar == I.tl.bfloat16:
+            return I.TensorHandle(to_bf16_rne(src.data), dst_type.scalar)
+        return orig_fp_to_fp(self, src, dst_type, rounding_mode)
+
+    I.InterpreterBuilder.create_fp_to_fp = create_fp_to_fp
 
 
 class _Libdevice:

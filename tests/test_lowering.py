@@ -1,0 +1,71 @@
+"""The B200 lowering (targets/b200): the reference's own kernels lower to the committed descriptors (when
+the reference tree is present), kernels written for this suite lower to the expected classes and index
+maps, and programs outside the executor's classes are refused with a Reason, never approximated."""
+import json
+import os
+
+import pytest
+
+from pytorchsim_triton_compiler.codegen import descriptors as D
+from pytorchsim_triton_compiler.contract import kernel_object as ko
+from pytorchsim_triton_compiler.contract.kernel_spec import load_spec
+from pytorchsim_triton_compiler.contract.stop import Reason, Refused
+from pytorchsim_triton_compiler.targets.b200 import frontend as F
+from pytorchsim_triton_compiler.targets.b200 import lower as L
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF = os.environ.get("PTSIM_REFERENCE", "/root/reference")
+OBJ = os.path.join(HERE, "golden", "objects")
+
+
+def test_index_algebra():
+    x = F.Index.var("x")
+    e = x.mod(128) + x.floordiv(262144).scale(128) + x.floordiv(128).mod(2048).scale(1024)
+    assert e.terms == {F.Digit("x", 1, 128): 1, F.Digit("x", 262144, None): 128, F.Digit("x", 128, 2048): 1024}
+    with pytest.raises(Refused):
+        (x + 1).floordiv(4)
+    with pytest.raises(Refused):
+        x.floordiv(128).mod(2048).floordiv(3)
+
+
+def test_own_pointwise_kernel_lowers_to_its_dma_boxes():
+    spec = load_spec(os.path.join(HERE, "kernels", "relayout_scale.py"))
+    lo = L.lower(spec)
+    d = lo.desc
+    assert d.kind == D.ELEMENTWISE and d.units == 4 and d.unit_size == 2048
+    maps = {m.arg: sorted((m.div[k], m.mod[k], m.stride[k]) for k in range(m.ndigit)) for m in list(d.p.ew.map)[:d.p.ew.nmap]}
+    assert maps[0] == [(1, 32, 1), (32, 4, 2048), (128, 64, 32)]
+    assert maps[1] == [(1, 8192, 1)] and maps[2] == [(1, 8192, 1)]
+    ops = [D.OP_NAME[i.op] for i in list(d.p.ew.code)[:d.p.ew.ncode]]
+    assert ops.count("load") == 2 and "mul" in ops and "add" in ops and ops[-1] == "store"
+
+
+def test_own_softmax_kernel_is_a_row_program():
+    spec = load_spec(os.path.join(HERE, "kernels", "row_softmax.py"))
+    lo = L.lower(spec)
+    r = lo.desc.p.row
+    assert lo.desc.kind == D.ROW_SOFTMAX and (r.rows, r.cols, r.in_row_stride, r.out_row_stride) == (256, 512, 512, 512)
+    assert lo.desc.units == 16 and lo.desc.unit_size == 16
+
+
+def test_atomics_are_refused():
+    spec = load_spec(os.path.join(HERE, "kernels", "atomic_accumulate.py"))
+    with pytest.raises(Refused) as e:
+        L.lower(spec)
+    assert e.value.reason == spec.expect_stop.reason
+
+
+def fixture_names():
+    with open(os.path.join(HERE, "golden", "index.json")) as fh:
+        return json.load(fh)
+
+
+@pytest.mark.skipif(not os.path.isdir(REF), reason="the reference tree is only in the build container")
+@pytest.mark.parametrize("name", [n for n in fixture_names() if "t2048" not in n and "4096x4096" not in n
+                                  and "8192" not in n and "b4" not in n and "1m" not in n])
+def test_reference_kernels_lower_to_the_committed_descriptors(name):
+    d = os.path.join(OBJ, name)
+    case = json.load(open(os.path.join(d, "case.json")))
+    spec = load_spec(os.path.join(REF, case["source"]))
+    lo = L.lower(spec)
+    assert lo.blob == ko.read_desc(d), name

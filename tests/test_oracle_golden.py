@@ -1,0 +1,122 @@
+"""The oracle is pinned: each restatement in oracle/programs.py reproduces the outputs of the reference's own
+kernel (its Triton source run by the Triton interpreter, tests/golden/make_golden.py) on the reference's
+seeded inputs (make_inputs(torch, seed=0)).  Bit exact where the program is exact (copies, fp32 adds, bf16
++ 1, max); within the bf16 tolerance of the reference's bf16-store case (rtol = atol = 1e-2,
+tests/cases/mechanism/ops/ops_bf16_store_gemm.py) otherwise; fp32 sums within 1e-5 of the sum of
+magnitudes.  CPU only."""
+import json
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import programs as O
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+OBJ = os.path.join(HERE, "golden", "objects")
+
+
+def golden_cases():
+    with open(os.path.join(HERE, "golden", "index.json")) as fh:
+        names = json.load(fh)
+    out = []
+    for n in names:
+        with open(os.path.join(OBJ, n, "case.json")) as fh:
+            c = json.load(fh)
+        if c["golden"]:
+            out.append(c)
+    return out
+
+
+def make_inputs(case):
+    """The reference's input convention (validation/pytorchsim/*/..._spec.py make_inputs): one generator
+    seeded 0, randn(numel) per read argument in argument order, cast to the argument's dtype."""
+    g = torch.Generator().manual_seed(0)
+    out = {}
+    for a in case["args"]:
+        dt = getattr(torch, a["dtype"])
+        if a["role"] in ("in", "inout"):
+            out[a["name"]] = torch.randn(a["numel"], generator=g).to(dt)
+        else:
+            out[a["name"]] = torch.zeros(a["numel"], dtype=dt)
+    return out
+
+
+def run_oracle(case, ins):
+    """(output argument name, oracle output) of the case's program family."""
+    o = dict(case["oracle"])
+    fam = o.pop("family")
+    args = case["args"]
+    reads = [a["name"] for a in args if a["role"] in ("in", "inout")]
+    outs = [a["name"] for a in args if a["role"] in ("out", "inout")]
+    x = [ins[n] for n in reads]
+    if fam == "vector_add":
+        return outs[0], O.vector_add(x[0], x[1])
+    if fam == "add_one":
+        return outs[0], O.add_one(x[0])
+    if fam == "slice_add_one":
+        return outs[0], O.slice_add_one(x[0])
+    if fam == "reduce_all":
+        return outs[0], O.reduce_all(x[0], o["op"])
+    if fam == "softmax_rows":
+        return outs[0], O.softmax_rows(x[0], o["rows"], o["cols"])
+    if fam == "rmsnorm_rows":
+        return outs[0], O.rmsnorm_rows(x[0], x[1], o["rows"], o["cols"], o["eps"])
+    if fam == "qknorm_rope":
+        return outs[0], O.qknorm_rope(x[0], x[1], x[2], x[3], o["tokens"], o["heads"], o["eps"])
+    if fam == "token_to_head_major":
+        return outs[0], O.token_to_head_major(x[0], o["tokens"], o["heads"], o["dim"])
+    if fam == "heads_to_token_major":
+        return outs[0], O.heads_to_token_major(x[0], o["tokens"], o["heads"], o["dim"])
+    if fam == "silu_mul":
+        return outs[0], O.silu_mul(x[0], o["tokens"], o["inter"])
+    if fam == "gemm":
+        if o["residual"]:
+            return outs[0], O.gemm(x[1], x[2], o["M"], o["N"], o["K"], residual=x[0])
+        return outs[0], O.gemm(x[0], x[1], o["M"], o["N"], o["K"])
+    if fam == "attention_prefill":
+        bq = case.get("ref_bq") or min(1024, o["seq"])
+        return outs[0], O.attention_prefill(x[0], x[1], x[2], o["batch"], o["hq"], o["g"], o["seq"], o["dim"],
+                                            bq, bq, o["causal"], o["scale"])
+    raise AssertionError(f"no oracle family {fam}")
+
+
+EXACT = {"vector_add", "add_one", "slice_add_one", "token_to_head_major", "heads_to_token_major"}
+
+
+def as_bits(t):
+    t = t.contiguous()
+    return t.view(torch.int16).numpy() if t.dtype == torch.bfloat16 else t.numpy()
+
+
+def as_float(bits, dtype):
+    if dtype == "bfloat16":
+        return torch.from_numpy(bits.astype(np.int16)).view(torch.bfloat16).float()
+    return torch.from_numpy(bits).float()
+
+
+@pytest.mark.parametrize("case", golden_cases(), ids=lambda c: c["name"])
+def test_oracle_matches_reference_kernel(case):
+    ins = make_inputs(case)
+    name, got = run_oracle(case, ins)
+    gold = np.load(os.path.join(HERE, "golden", case["golden"]))
+    stride = int(gold[f"{name}__stride"][0])
+    want_bits = gold[name]
+    dt = next(a["dtype"] for a in case["args"] if a["name"] == name)
+    got_bits = as_bits(got.reshape(-1))
+    fam = case["oracle"]["family"]
+    if fam in EXACT or (fam == "reduce_all" and case["oracle"]["op"] == "max"):
+        # Exact programs: the whole output's hash matches, not only the sample.
+        import hashlib
+        assert hashlib.sha256(got_bits.tobytes()).digest() == bytes(gold[f"{name}__sha256"]), case["name"]
+        return
+    g = as_float(got_bits[::stride], dt)
+    w = as_float(want_bits, dt)
+    if fam == "reduce_all":
+        scale = float(ins[case["inputs"][0]].float().abs().sum())
+        assert abs(float(g[0]) - float(w[0])) <= 1e-5 * scale
+        return
+    ok = torch.allclose(g, w, rtol=1e-2, atol=1e-2, equal_nan=True)
+    assert ok, f"{case['name']}: max abs err {float((g - w).abs().max()):.4g}"
