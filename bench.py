@@ -302,7 +302,7 @@ def run_b200(args, world, rank, local):
                     "api": "runtime.native.launch (C ABI ptsim_launch) with pinned host buffers"},
             "gpu_launches": 2 * args.steps,
             "clocks": clk}
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and args.cpu:
         base, _ = cpu_rate(seconds=10.0)
         line["cpu_baseline"] = base
         if args.suite:
@@ -371,6 +371,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--no-suite", dest="suite", action="store_false")
+    ap.add_argument("--no-cpu", dest="cpu", action="store_false", help="skip the CPU baseline (profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
