@@ -77,37 +77,54 @@ class Clocks:
         import tempfile
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
+        self.err = self.path + ".err"
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv",
                                           "-i", str(self.index), "-lms", "200"], stdout=open(self.path, "w"),
-                                         stderr=subprocess.DEVNULL)
+                                         stderr=open(self.err, "w"))
         except OSError:
             self.proc = None
 
     def stop(self):
         if self.proc is None:
-            return None
+            return {"error": "nvidia-smi not runnable"}
+        time.sleep(0.3)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        rows = []
-        with open(self.path) as fh:
-            for line in fh:
-                f = [x.strip() for x in line.split(",")]
-                if len(f) >= 9:
-                    rows.append(f)
+        lines = [ln.strip() for ln in open(self.path) if ln.strip()]
+        err = open(self.err).read().strip()
         os.unlink(self.path)
-        if not rows:
-            return None
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
-        loaded = [s for s in sm if s > 0.5 * (max(mx) if mx else 1)] or sm
-        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+        os.unlink(self.err)
+        if len(lines) < 2:
+            return {"error": (err or "no samples")[:200]}
+        head = [h.strip() for h in lines[0].split(",")]
+
+        def col(name):
+            return next((i for i, h in enumerate(head) if h.startswith(name)), None)
+
+        def num(x):
+            try:
+                return float(x.strip().split()[0])
+            except (ValueError, IndexError):
+                return None
+
+        ism, imax = col("clocks.current.sm"), col("clocks.max.sm")
+        rows = [[f.strip() for f in ln.split(",")] for ln in lines[1:] if not ln.startswith("index")]
+        sm = [num(r[ism]) for r in rows if ism is not None and len(r) == len(head)]
+        mx = [num(r[imax]) for r in rows if imax is not None and len(r) == len(head)]
+        sm, mx = [x for x in sm if x is not None], [x for x in mx if x is not None]
+        reasons = set()
+        for name in ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"):
+            i = next((k for k, h in enumerate(head) if h.endswith("." + name)), None)
+            if i is not None and any(len(r) == len(head) and r[i].lower() == "active" for r in rows):
+                reasons.add(name)
+        top = max(mx) if mx else None
+        loaded = [x for x in sm if top and x > 0.5 * top] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": top,
+                "reasons": sorted(reasons), "samples": len(rows)}
 
 
 def dist_setup(args):
@@ -311,7 +328,7 @@ def run_b200(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
-def suite(dev, stream, iters=5):
+def suite(dev, stream, iters=5, only=None, warm=1):
     """Device-timed throughput of the other BASELINE.json configurations' lowered kernels (not the
     headline): median of `iters` launches with an L2 flush before each."""
     import torch
@@ -322,6 +339,8 @@ def suite(dev, stream, iters=5):
     out = {}
 
     def timed(name, bound, work):
+        if only is not None and name != only:
+            return
         m, blob = load_object(name)
         d = D.from_bytes(blob)
         g = torch.Generator(device=dev).manual_seed(0)
@@ -339,14 +358,14 @@ def suite(dev, stream, iters=5):
         ws = torch.empty(max(1, d.workspace_bytes), dtype=torch.uint8, device=dev)
         ptrs = [t.data_ptr() for t in ts]
         times = []
-        for k in range(iters + 1):
+        for k in range(iters + warm):
             flush.zero_()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
             native.launch(blob, ptrs, 0, d.units, ws.data_ptr(), d.workspace_bytes, stream.cuda_stream)
             b.record(stream)
             b.synchronize()
-            if k:
+            if k >= warm:
                 times.append(a.elapsed_time(b))
         native.sync(stream.cuda_stream)
         ms = statistics.median(times)
@@ -372,9 +391,16 @@ def main():
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--no-suite", dest="suite", action="store_false")
     ap.add_argument("--no-cpu", dest="cpu", action="store_false", help="skip the CPU baseline (profiling runs)")
+    ap.add_argument("--kernel", default=None, help="time one suite kernel object only (for ncu captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.kernel:
+        import torch
+        dev = torch.device("cuda", 0)
+        print(json.dumps(suite(dev, torch.cuda.current_stream(dev), iters=max(1, args.steps), only=args.kernel,
+                               warm=args.warmup)))
+        return
     world, rank, local = dist_setup(args)
     try:
         if args.impl == "reference":

@@ -28,7 +28,8 @@ struct RowLaunch {
 
 template <int TPR>
 __device__ __forceinline__ float row_allreduce(float v, bool is_max, float *smem_slot) {
-  // Butterfly within the row's lanes (TPR <= 32), then across the row's warps through shared memory.
+  // Butterfly within the row's lanes (TPR <= 32), then across the row's warps through shared memory
+  // (smem_slot: TPR / 32 floats owned by this row).  Every thread of the CTA must call it.
 #pragma unroll
   for (int o = (TPR < 32 ? TPR : 32) / 2; o > 0; o >>= 1) {
     float w = __shfl_xor_sync(0xffffffffu, v, o);
@@ -39,94 +40,99 @@ __device__ __forceinline__ float row_allreduce(float v, bool is_max, float *smem
     const int lane = threadIdx.x & 31;
     const int warp_in_row = (threadIdx.x % TPR) / 32;
     if (lane == 0) smem_slot[warp_in_row] = v;
-    __syncwarp();
     __syncthreads();
     float t = smem_slot[0];
 #pragma unroll
     for (int w2 = 1; w2 < W; ++w2) t = is_max ? nan_max(t, smem_slot[w2]) : __fadd_rn(t, smem_slot[w2]);
-    __syncthreads();
     v = t;
   }
   return v;
 }
 
-// Fast path: bf16 rows whose length is TPR * 8 * CH.
+// 2^x on the special-function unit (one MUFU op; denormal results flush to zero, which the downstream
+// bf16 rounding of a softmax probability would also produce).
+__device__ __forceinline__ float ex2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// a / b with the reciprocal r = 1/b computed once per row: q = a*r, then one residual correction
+// q' = q + (a - q*b) * r (Markstein's refinement of a reciprocal-based quotient), which returns the
+// correctly rounded quotient for all but rare boundary cases at a fraction of the cost of a full division.
+__device__ __forceinline__ float div_by(float a, float b, float r) {
+  const float q = __fmul_rn(a, r);
+  const float e = __fmaf_rn(-q, b, a);
+  return __fmaf_rn(e, r, q);
+}
+
+// Fast path: bf16 rows whose length is TPR * 8 * CH.  A CTA of 256 threads owns 256 / TPR rows; each
+// thread keeps CH 16-byte chunks of its row (8 * CH values) in registers: one HBM read, one write.
 template <int KIND, int TPR, int CH>
 __global__ void __launch_bounds__(256) row_fast_kernel(const __grid_constant__ RowLaunch L) {
-  __shared__ float red[256 / 32 * 2];
-  constexpr int RPC = 256 / TPR;  // rows per CTA per step
+  constexpr int RPC = 256 / TPR;                 // rows per CTA
+  constexpr int W = TPR >= 32 ? TPR / 32 : 1;    // warps per row
+  __shared__ float red_a[RPC * W], red_b[RPC * W];
   const int lane_in_row = threadIdx.x % TPR;
   const int row_in_cta = threadIdx.x / TPR;
-  float *slot = red + (row_in_cta * (TPR / 32 > 0 ? TPR / 32 : 1)) % (256 / 32 * 2);
-  const int64_t nrows = L.rows_end - L.rows_begin;
-  // Every thread runs the same number of loop steps (row-exchange barriers for TPR > 32).
-  const int64_t steps = ceil_div(nrows, int64_t(gridDim.x) * RPC);
-  for (int64_t s = 0; s < steps; ++s) {
-    const int64_t r = L.rows_begin + (s * gridDim.x + blockIdx.x) * RPC + row_in_cta;
-    const bool live = r < L.rows_end;
-    uint4 v[CH];
+  const int64_t r = L.rows_begin + int64_t(blockIdx.x) * RPC + row_in_cta;
+  const bool live = r < L.rows_end;
+  float v[CH * 8];
+  {
     const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(L.in) + (live ? r : L.rows_begin) * L.in_stride);
+    uint4 raw[CH];
 #pragma unroll
-    for (int c = 0; c < CH; ++c) v[c] = live ? __ldcs(src + c * TPR + lane_in_row) : make_uint4(0, 0, 0, 0);
-    uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(L.out) + (live ? r : L.rows_begin) * L.out_stride);
-    if constexpr (KIND == kSoftmax) {
-      float m = -INFINITY;
+    for (int c = 0; c < CH; ++c) raw[c] = live ? __ldcs(src + c * TPR + lane_in_row) : make_uint4(0, 0, 0, 0);
 #pragma unroll
-      for (int c = 0; c < CH; ++c) {
-        const uint32_t w[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+    for (int c = 0; c < CH; ++c) {
+      const uint32_t w[4] = {raw[c].x, raw[c].y, raw[c].z, raw[c].w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) m = nan_max(nan_max(m, lo_bf16(w[j])), hi_bf16(w[j]));
-      }
-      m = row_allreduce<TPR>(m, true, slot);
-      float sum = 0.f;
+      for (int j = 0; j < 4; ++j) { v[c * 8 + 2 * j] = lo_bf16(w[j]); v[c * 8 + 2 * j + 1] = hi_bf16(w[j]); }
+    }
+  }
+  uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(L.out) + (live ? r : L.rows_begin) * L.out_stride);
+  if constexpr (KIND == kSoftmax) {
+    float m = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < CH; ++c) {
-        const uint32_t w[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+    for (int i = 0; i < CH * 8; ++i) m = nan_max(m, v[i]);
+    m = row_allreduce<TPR>(m, true, red_a + row_in_cta * W);
+    const float kLog2e = 1.4426950408889634f;
+    float sum = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          sum = __fadd_rn(sum, npu_exp(__fsub_rn(lo_bf16(w[j]), m)));
-          sum = __fadd_rn(sum, npu_exp(__fsub_rn(hi_bf16(w[j]), m)));
-        }
-      }
-      sum = row_allreduce<TPR>(sum, false, slot);
-      if (live) {
-#pragma unroll
-        for (int c = 0; c < CH; ++c) {
-          uint32_t w[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            w[j] = pack_bf16x2(__fdiv_rn(npu_exp(__fsub_rn(lo_bf16(w[j]), m)), sum),
-                               __fdiv_rn(npu_exp(__fsub_rn(hi_bf16(w[j]), m)), sum));
-          __stcs(dst + c * TPR + lane_in_row, make_uint4(w[0], w[1], w[2], w[3]));
-        }
-      }
-    } else {
-      float ss = 0.f;
+    for (int i = 0; i < CH * 8; ++i) {
+      v[i] = ex2_fast(__fmul_rn(__fsub_rn(v[i], m), kLog2e));   // exp(x - m), once per element
+      sum = __fadd_rn(sum, v[i]);
+    }
+    sum = row_allreduce<TPR>(sum, false, red_b + row_in_cta * W);
+    const float rcp = __frcp_rn(sum);
+    if (live) {
 #pragma unroll
       for (int c = 0; c < CH; ++c) {
-        const uint32_t w[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+        uint32_t w[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float a = lo_bf16(w[j]), b = hi_bf16(w[j]);
-          ss = __fadd_rn(ss, __fmul_rn(a, a));
-          ss = __fadd_rn(ss, __fmul_rn(b, b));
-        }
+        for (int j = 0; j < 4; ++j)
+          w[j] = pack_bf16x2(div_by(v[c * 8 + 2 * j], sum, rcp), div_by(v[c * 8 + 2 * j + 1], sum, rcp));
+        __stcs(dst + c * TPR + lane_in_row, make_uint4(w[0], w[1], w[2], w[3]));
       }
-      ss = row_allreduce<TPR>(ss, false, slot);
-      const float rs = rsqrtf(__fadd_rn(__fdiv_rn(ss, float(L.cols)), L.eps));
-      if (live) {
-        const uint4 *wsrc = reinterpret_cast<const uint4 *>(L.weight);
+    }
+  } else {
+    float ss = 0.f;
 #pragma unroll
-        for (int c = 0; c < CH; ++c) {
-          const uint4 wv = __ldg(wsrc + c * TPR + lane_in_row);
-          uint32_t x[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
-          const uint32_t g[4] = {wv.x, wv.y, wv.z, wv.w};
+    for (int i = 0; i < CH * 8; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+    ss = row_allreduce<TPR>(ss, false, red_a + row_in_cta * W);
+    const float rs = rsqrtf(__fadd_rn(__fdiv_rn(ss, float(L.cols)), L.eps));
+    if (live) {
+      const uint4 *wsrc = reinterpret_cast<const uint4 *>(L.weight);
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            x[j] = pack_bf16x2(__fmul_rn(__fmul_rn(lo_bf16(x[j]), rs), lo_bf16(g[j])),
-                               __fmul_rn(__fmul_rn(hi_bf16(x[j]), rs), hi_bf16(g[j])));
-          __stcs(dst + c * TPR + lane_in_row, make_uint4(x[0], x[1], x[2], x[3]));
-        }
+      for (int c = 0; c < CH; ++c) {
+        const uint4 wv = __ldg(wsrc + c * TPR + lane_in_row);
+        const uint32_t g[4] = {wv.x, wv.y, wv.z, wv.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          o[j] = pack_bf16x2(__fmul_rn(__fmul_rn(v[c * 8 + 2 * j], rs), lo_bf16(g[j])),
+                             __fmul_rn(__fmul_rn(v[c * 8 + 2 * j + 1], rs), hi_bf16(g[j])));
+        __stcs(dst + c * TPR + lane_in_row, make_uint4(o[0], o[1], o[2], o[3]));
       }
     }
   }
@@ -182,12 +188,7 @@ template <int KIND, int TPR, int CH>
 static void launch_row_fast(const RowLaunch &L, const LaunchCtx &c) {
   constexpr int RPC = 256 / TPR;
   const int64_t rows = L.rows_end - L.rows_begin;
-  int64_t blocks = ceil_div(rows, RPC);
-  // Registers per thread ~ 4*CH + 40: keep the grid at the resident-CTA count of one wave.
-  const int64_t per_sm = CH >= 12 ? 2 : (CH >= 6 ? 3 : 4);
-  const int64_t cap = int64_t(c.sm_count) * per_sm;
-  if (blocks > cap) blocks = cap;
-  row_fast_kernel<KIND, TPR, CH><<<unsigned(blocks), 256, 0, c.stream>>>(L);
+  row_fast_kernel<KIND, TPR, CH><<<unsigned(ceil_div(rows, RPC)), 256, 0, c.stream>>>(L);
 }
 
 template <int KIND, int TPR>
@@ -197,10 +198,6 @@ static bool dispatch_ch(const RowLaunch &L, const LaunchCtx &c, int ch) {
     case 2: launch_row_fast<KIND, TPR, 2>(L, c); return true;
     case 3: launch_row_fast<KIND, TPR, 3>(L, c); return true;
     case 4: launch_row_fast<KIND, TPR, 4>(L, c); return true;
-    case 6: launch_row_fast<KIND, TPR, 6>(L, c); return true;
-    case 8: launch_row_fast<KIND, TPR, 8>(L, c); return true;
-    case 12: launch_row_fast<KIND, TPR, 12>(L, c); return true;
-    case 16: launch_row_fast<KIND, TPR, 16>(L, c); return true;
   }
   return false;
 }
@@ -213,15 +210,20 @@ static int launch_row_kind(const RowLaunch &L, const LaunchCtx &c) {
                        (KIND == kSoftmax || reinterpret_cast<uintptr_t>(L.weight) % 16 == 0) &&
                        (L.in_stride % 8 == 0) && (L.out_stride % 8 == 0);
   if (bf16_io && aligned && L.cols % 8 == 0) {
+    // Spread a row over as many threads as keep at most 4 chunks (32 values) each in registers.
     const int64_t chunks = L.cols / 8;
-    const int tprs[3] = {32, 64, 16};
+    const int tprs[5] = {16, 32, 64, 128, 256};
     for (int t : tprs) {
-      if (chunks % t) continue;
-      const int64_t ch = chunks / t;
+      if (chunks % t || chunks / t > 4) continue;
+      const int ch = int(chunks / t);
       bool ok = false;
-      if (t == 16) ok = dispatch_ch<KIND, 16>(L, c, int(ch));
-      else if (t == 32) ok = dispatch_ch<KIND, 32>(L, c, int(ch));
-      else ok = dispatch_ch<KIND, 64>(L, c, int(ch));
+      switch (t) {
+        case 16: ok = dispatch_ch<KIND, 16>(L, c, ch); break;
+        case 32: ok = dispatch_ch<KIND, 32>(L, c, ch); break;
+        case 64: ok = dispatch_ch<KIND, 64>(L, c, ch); break;
+        case 128: ok = dispatch_ch<KIND, 128>(L, c, ch); break;
+        case 256: ok = dispatch_ch<KIND, 256>(L, c, ch); break;
+      }
       if (ok) { PTSIM_CUDA(cudaGetLastError()); return PTSIM_OK; }
     }
   }
