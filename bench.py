@@ -259,6 +259,9 @@ def run_b200(args, world, rank, local):
     barrier(world)
     torch.cuda.synchronize()
     clocks.start()
+    # The GPU spins while the host enqueues every timed step, so the events measure kernels, not the
+    # host's launch latency.
+    torch.cuda._sleep(int(1e7))
     for k in range(args.steps):
         flush.zero_()               # L2 flush, outside the timed events
         step(events[k])
@@ -357,17 +360,16 @@ def suite(dev, stream, iters=5, only=None, warm=1):
                 ts.append(torch.zeros(n, dtype=dt, device=dev))
         ws = torch.empty(max(1, d.workspace_bytes), dtype=torch.uint8, device=dev)
         ptrs = [t.data_ptr() for t in ts]
-        times = []
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters + warm)]
+        torch.cuda.synchronize()
+        torch.cuda._sleep(int(1e7))       # the host enqueues every launch before the GPU reaches them
         for k in range(iters + warm):
             flush.zero_()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
+            ev[k][0].record(stream)
             native.launch(blob, ptrs, 0, d.units, ws.data_ptr(), d.workspace_bytes, stream.cuda_stream)
-            b.record(stream)
-            b.synchronize()
-            if k >= warm:
-                times.append(a.elapsed_time(b))
+            ev[k][1].record(stream)
         native.sync(stream.cuda_stream)
+        times = [a.elapsed_time(b) for a, b in ev[warm:]]
         ms = statistics.median(times)
         if bound == "hbm":
             gbs = work / ms / 1e6
@@ -377,10 +379,44 @@ def suite(dev, stream, iters=5, only=None, warm=1):
             out[name] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1), "frac_bf16": round(tf / tflops, 3)}
 
     timed("vector_add_1m", "hbm", 3 * 4 * 1_048_576)
+    timed("vector_add1_4096x4096", "hbm", 2 * 2 * 4096 * 4096)
     for m in (128, 512, 2048, 4096, 8192):
         timed(f"gemm_{m}x4096x4096", "tensor", 2 * m * 4096 * 4096)
     timed("attention_32x8x4096_b4", "tensor", 549_755_813_888)
+    if only is None or only == "qwen3_layer":
+        out["qwen3_layer_t2048"] = layer_timing(dev, stream, iters, warm, flush, tflops)
     return out
+
+
+def layer_timing(dev, stream, iters, warm, flush, tflops):
+    """BASELINE.json config 4 on one GPU: the Qwen3-8B-shaped prefill layer (T = 2048) as the 14 launches
+    of the reference's lowered kernel objects, replayed from a CUDA graph; TFLOP/s of GEMM + attention."""
+    import torch
+    from oracle import programs as O
+    from pytorchsim_triton_compiler.contract import kernel_object as ko
+    from pytorchsim_triton_compiler.runtime import qwen3 as Q
+    T = 2048
+    objs = {n.split("_")[2]: ko.read_desc(os.path.join(OBJECTS, n)) for n in os.listdir(OBJECTS)
+            if n.startswith("qwen3_t2048_")}
+    p = Q.random_params(0)
+    x = torch.randn(T * Q.HIDDEN, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
+    cos, sin = O.rope_tables(T)
+    g, _ = Q.build_layer(dev, T, p, cos, sin, x, objects=objs)
+    g.capture()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters + warm)]
+    torch.cuda.synchronize()
+    torch.cuda._sleep(int(1e7))
+    for k in range(iters + warm):
+        flush.zero_()
+        ev[k][0].record(stream)
+        g.run()
+        ev[k][1].record(stream)
+    torch.cuda.synchronize()
+    times = [a.elapsed_time(b) for a, b in ev[warm:]]
+    ms = statistics.median(times)
+    tf = Q.layer_flops(T) / ms / 1e9
+    return {"ms": round(ms, 4), "TFLOP/s": round(tf, 1), "frac_bf16": round(tf / tflops, 3), "launches": g.launch_count(),
+            "flops": Q.layer_flops(T)}
 
 
 def main():

@@ -176,6 +176,31 @@ def rope_tables(tokens, dim=128, theta=1.0e6):
     return emb.cos().to(torch.float32).reshape(-1), emb.sin().to(torch.float32).reshape(-1)
 
 
+def layer_attention_half(x, p, T, hq, hkv, residual, hidden=4096, dim=128, eps=1e-6, cos=None, sin=None,
+                         bq=1024, bkv=1024):
+    """Launches 00-08 of the layer for `hq` query / `hkv` KV heads (a tensor-parallel rank's share when
+    they are fewer than 32 / 8): bf16 o-projection output, plus `x` when `residual`."""
+    h = rmsnorm_rows(x, p["ln1"], T, hidden, eps)
+    q = gemm(h, p["wq"], T, hq * dim, hidden)
+    k = gemm(h, p["wk"], T, hkv * dim, hidden)
+    v = gemm(h, p["wv"], T, hkv * dim, hidden)
+    qh = qknorm_rope(q, p["qn"], cos, sin, T, hq, eps, dim)
+    kh = qknorm_rope(k, p["kn"], cos, sin, T, hkv, eps, dim)
+    vh = token_to_head_major(v, T, hkv, dim)
+    o = attention_prefill(qh, kh, vh, 1, hq, hq // hkv, T, dim, min(bq, T), min(bkv, T), True, 1.0 / math.sqrt(dim))
+    ot = heads_to_token_major(o, T, hq, dim)
+    return gemm(ot, p["wo"], T, hidden, hq * dim, residual=x if residual else None)
+
+
+def layer_mlp_half(x1, p, T, inter, residual, hidden=4096, eps=1e-6):
+    """Launches 00, 09-11 of the layer for `inter` intermediate columns: bf16 down-projection output,
+    plus `x1` when `residual`."""
+    h2 = rmsnorm_rows(x1, p["ln2"], T, hidden, eps)
+    gu = gemm(h2, p["wgu"], T, 2 * inter, hidden)
+    a = silu_mul(gu, T, inter)
+    return gemm(a, p["wd"], T, hidden, inter, residual=x1 if residual else None)
+
+
 def decoder_layer(x, p, T, hidden=4096, hq=32, hkv=8, dim=128, inter=12288, eps=1e-6, cos=None, sin=None,
                   bq=1024, bkv=1024):
     """The Qwen3-8B-shaped prefill layer as the 14 launches of validation/pytorchsim/

@@ -46,11 +46,16 @@ __device__ __forceinline__ float hi_bf16(uint32_t w) { return __uint_as_float(w 
 __device__ __forceinline__ float npu_exp(float x) { return exp2f(x * 1.4426950408889634f); }
 
 // NaN-propagating max/min (the vmax/vmin rule of PyTorchSimTpuOps.td:64-74; tl.PropagateNan.ALL).
+// max.NaN / min.NaN return the canonical NaN when either operand is NaN (one instruction on sm_80+).
 __device__ __forceinline__ float nan_max(float a, float b) {
-  return (a != a || b != b) ? __int_as_float(0x7fc00000) : fmaxf(a, b);
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
 }
 __device__ __forceinline__ float nan_min(float a, float b) {
-  return (a != a || b != b) ? __int_as_float(0x7fc00000) : fminf(a, b);
+  float r;
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
 }
 
 __host__ __device__ __forceinline__ int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }

@@ -123,30 +123,34 @@ __device__ __forceinline__ void store8(const EwLaunch &L, int64_t i0, int n, con
   }
 }
 
-// Register file access with static indices only, so the 8 x 8 register file stays in registers.
-#define PTSIM_REG_CASES(X) X(0) X(1) X(2) X(3) X(4) X(5) X(6) X(7)
-
-__device__ __forceinline__ void reg_read(const float (&r)[PTSIM_MAX_REGS][8], int i, float v[8]) {
-  switch (i) {
-#define PTSIM_RD(c) case c: _Pragma("unroll") for (int k = 0; k < 8; ++k) v[k] = r[c][k]; break;
-    PTSIM_REG_CASES(PTSIM_RD)
-#undef PTSIM_RD
-  }
+// Register file access with static indices only, so the NREG x 8 register file stays in registers
+// (a register index past NREG cannot occur: the host picks NREG above the program's highest register).
+template <int NREG>
+__device__ __forceinline__ void reg_read(const float (&r)[NREG][8], int i, float v[8]) {
+#pragma unroll
+  for (int c = 0; c < NREG; ++c)
+    if (i == c) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = r[c][k];
+    }
 }
 
-__device__ __forceinline__ void reg_write(float (&r)[PTSIM_MAX_REGS][8], int i, const float v[8]) {
-  switch (i) {
-#define PTSIM_WR(c) case c: _Pragma("unroll") for (int k = 0; k < 8; ++k) r[c][k] = v[k]; break;
-    PTSIM_REG_CASES(PTSIM_WR)
-#undef PTSIM_WR
-  }
+template <int NREG>
+__device__ __forceinline__ void reg_write(float (&r)[NREG][8], int i, const float v[8]) {
+#pragma unroll
+  for (int c = 0; c < NREG; ++c)
+    if (i == c) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) r[c][k] = v[k];
+    }
 }
 
+template <int NREG>
 __global__ void __launch_bounds__(256) ew_program_kernel(const __grid_constant__ EwLaunch L) {
   const int64_t groups = ceil_div(L.end - L.begin, 8);
-  float r[PTSIM_MAX_REGS][8];
+  float r[NREG][8];
 #pragma unroll
-  for (int a = 0; a < PTSIM_MAX_REGS; ++a)
+  for (int a = 0; a < NREG; ++a)
 #pragma unroll
     for (int k = 0; k < 8; ++k) r[a][k] = 0.f;
   for (int64_t g = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; g < groups; g += int64_t(gridDim.x) * blockDim.x) {
@@ -156,16 +160,16 @@ __global__ void __launch_bounds__(256) ew_program_kernel(const __grid_constant__
       const ptsim_insn in = L.p.code[pc];
       float x[8], y[8];
       switch (in.op) {
-        case PTSIM_OP_LOAD: load8(L, in.a, i0, n, x); reg_write(r, in.dst, x); break;
+        case PTSIM_OP_LOAD: load8(L, in.a, i0, n, x); reg_write<NREG>(r, in.dst, x); break;
         case PTSIM_OP_CONST:
 #pragma unroll
           for (int k = 0; k < 8; ++k) x[k] = in.imm;
-          reg_write(r, in.dst, x);
+          reg_write<NREG>(r, in.dst, x);
           break;
-        case PTSIM_OP_STORE: reg_read(r, in.a, x); store8(L, i0, n, x); break;
+        case PTSIM_OP_STORE: reg_read<NREG>(r, in.a, x); store8(L, i0, n, x); break;
         default: {
-          reg_read(r, in.a, x);
-          reg_read(r, in.b, y);
+          reg_read<NREG>(r, in.a, x);
+          reg_read<NREG>(r, in.b, y);
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
             float a = x[k], b = y[k], o = 0.f;
@@ -185,7 +189,7 @@ __global__ void __launch_bounds__(256) ew_program_kernel(const __grid_constant__
             }
             x[k] = o;
           }
-          reg_write(r, in.dst, x);
+          reg_write<NREG>(r, in.dst, x);
         }
       }
     }
@@ -287,7 +291,18 @@ int launch_elementwise(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64
       default: return fail(PTSIM_E_DESC, "elementwise copy of a %d-byte element", es);
     }
   } else {
-    ew_program_kernel<<<unsigned(blocks), threads, 0, c.stream>>>(L);
+    int top = 0;
+    for (int i = 0; i < L.p.ncode; ++i) {
+      const ptsim_insn &in = L.p.code[i];
+      top = in.dst > top ? in.dst : top;
+      if (in.op != PTSIM_OP_LOAD && in.op != PTSIM_OP_CONST) {
+        top = in.a > top ? in.a : top;
+        top = in.b > top ? in.b : top;
+      }
+    }
+    if (top < 2) ew_program_kernel<2><<<unsigned(blocks), threads, 0, c.stream>>>(L);
+    else if (top < 4) ew_program_kernel<4><<<unsigned(blocks), threads, 0, c.stream>>>(L);
+    else ew_program_kernel<8><<<unsigned(blocks), threads, 0, c.stream>>>(L);
   }
   PTSIM_CUDA(cudaGetLastError());
   return PTSIM_OK;

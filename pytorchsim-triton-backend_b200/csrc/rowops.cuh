@@ -12,6 +12,7 @@
 // dtype (RNE).
 #pragma once
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace ptsim {
 
@@ -138,6 +139,140 @@ __global__ void __launch_bounds__(256) row_fast_kernel(const __grid_constant__ R
   }
 }
 
+// ---------------------------------------------------------------------------------------------------
+// Streaming path for long rows (cols = 1024 * CH, CH <= 8): a persistent CTA of 128 threads owns rows
+// blockIdx.x, blockIdx.x + gridDim.x, ...; thread 0 keeps SLOTS whole rows in flight with bulk async
+// copies (cp.async.bulk, completion on an mbarrier per slot) into a shared-memory ring, so HBM sees
+// SLOTS x row bytes outstanding per CTA at all times; the 128 threads take a row out of its slot into
+// registers (CH 16-byte chunks each), release the slot for the row SLOTS ahead, reduce across the 4
+// warps, and write the row back with streaming 16-byte stores.
+// ---------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void bulk_load(void *dst_smem, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   sm100::smem_u32(dst_smem)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(sm100::smem_u32(bar))
+               : "memory");
+}
+
+template <int KIND, int CH>
+__global__ void __launch_bounds__(128) row_stream_kernel(const __grid_constant__ RowLaunch L, int slots) {
+  extern __shared__ __align__(128) uint8_t ring[];
+  __shared__ uint64_t full[16];
+  __shared__ float red_a[4], red_b[4];
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t row_bytes = uint32_t(L.cols) * 2u;
+  const int64_t nrows = L.rows_end - L.rows_begin;
+  const int64_t mine = nrows > blockIdx.x ? (nrows - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  auto row_of = [&](int64_t k) { return L.rows_begin + int64_t(blockIdx.x) + k * int64_t(gridDim.x); };
+  if (tid == 0) {
+    for (int s = 0; s < slots; ++s) sm100::mbar_init(&full[s], 1);
+    abort_flag = 0;
+    sm100::fence_barrier_init();
+    for (int64_t k = 0; k < mine && k < slots; ++k) {
+      sm100::mbar_arrive_expect_tx(&full[k], row_bytes);
+      bulk_load(ring + size_t(k) * row_bytes, reinterpret_cast<const uint16_t *>(L.in) + row_of(k) * L.in_stride,
+                row_bytes, &full[k]);
+    }
+  }
+  __syncthreads();
+  uint4 wv[KIND == kRmsNorm ? CH : 1];
+  if constexpr (KIND == kRmsNorm) {
+#pragma unroll
+    for (int c = 0; c < CH; ++c) wv[c] = __ldg(reinterpret_cast<const uint4 *>(L.weight) + c * 128 + tid);
+  }
+  int64_t k = 0;
+  for (; k < mine; ++k) {
+    const int s = int(k % slots);
+    const uint32_t phase = uint32_t(k / slots) & 1u;
+    if (!sm100::mbar_wait(&full[s], phase)) abort_flag = 1;
+    float v[CH * 8];
+    const uint4 *src = reinterpret_cast<const uint4 *>(ring + size_t(s) * row_bytes);
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const uint4 raw = src[c * 128 + tid];
+      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) { v[c * 8 + 2 * j] = lo_bf16(w[j]); v[c * 8 + 2 * j + 1] = hi_bf16(w[j]); }
+    }
+    __syncthreads();  // every thread has its chunks out of slot s (and has seen any abort)
+    if (abort_flag) break;
+    if (tid == 0 && k + slots < mine) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      sm100::mbar_arrive_expect_tx(&full[s], row_bytes);
+      bulk_load(ring + size_t(s) * row_bytes,
+                reinterpret_cast<const uint16_t *>(L.in) + row_of(k + slots) * L.in_stride, row_bytes, &full[s]);
+    }
+    uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(L.out) + row_of(k) * L.out_stride);
+    if constexpr (KIND == kSoftmax) {
+      float m = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < CH * 8; ++i) m = nan_max(m, v[i]);
+      m = row_allreduce<128>(m, true, red_a);
+      const float kLog2e = 1.4426950408889634f;
+      float sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < CH * 8; ++i) {
+        v[i] = ex2_fast(__fmul_rn(__fsub_rn(v[i], m), kLog2e));
+        sum = __fadd_rn(sum, v[i]);
+      }
+      sum = row_allreduce<128>(sum, false, red_b);
+      const float rcp = __frcp_rn(sum);
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          w[j] = pack_bf16x2(div_by(v[c * 8 + 2 * j], sum, rcp), div_by(v[c * 8 + 2 * j + 1], sum, rcp));
+        __stcs(dst + c * 128 + tid, make_uint4(w[0], w[1], w[2], w[3]));
+      }
+    } else {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < CH * 8; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+      ss = row_allreduce<128>(ss, false, red_a);
+      const float rs = rsqrtf(__fadd_rn(__fdiv_rn(ss, float(L.cols)), L.eps));
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        const uint32_t g[4] = {wv[c].x, wv[c].y, wv[c].z, wv[c].w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          o[j] = pack_bf16x2(__fmul_rn(__fmul_rn(v[c * 8 + 2 * j], rs), lo_bf16(g[j])),
+                             __fmul_rn(__fmul_rn(v[c * 8 + 2 * j + 1], rs), hi_bf16(g[j])));
+        __stcs(dst + c * 128 + tid, make_uint4(o[0], o[1], o[2], o[3]));
+      }
+    }
+    // red_a / red_b are safe to reuse without another barrier: the next row writes them only after the
+    // slot-read barrier, which every thread reaches after its reads of this row's partials.
+  }
+  if (abort_flag && tid == 0) {
+    // Copies still in flight land before the CTA's shared memory is released.
+    for (int64_t j = k; j < mine && j < k + slots; ++j)
+      sm100::mbar_wait(&full[int(j % slots)], uint32_t(j / slots) & 1u);
+  }
+}
+
+template <int KIND, int CH>
+static int launch_row_stream(const RowLaunch &L, const LaunchCtx &c) {
+  const int64_t row_bytes = L.cols * 2;
+  int slots = int((48 * 1024) / row_bytes);
+  if (slots > 16) slots = 16;
+  if (slots < 2) slots = 2;
+  const int smem = int(slots * row_bytes);
+  auto kern = row_stream_kernel<KIND, CH>;
+  PTSIM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int64_t rows = L.rows_end - L.rows_begin;
+  int per_sm = int((200 * 1024) / (smem + 1024));
+  if (per_sm > 8) per_sm = 8;
+  if (per_sm < 1) per_sm = 1;
+  int64_t grid = int64_t(c.sm_count) * per_sm;
+  if (grid > rows) grid = rows;
+  kern<<<unsigned(grid), 128, smem, c.stream>>>(L, slots);
+  PTSIM_CUDA(cudaGetLastError());
+  return PTSIM_OK;
+}
+
 __device__ __forceinline__ float ld_any(const void *p, int dt, int64_t i) {
   switch (dt) {
     case PTSIM_DT_F32: return reinterpret_cast<const float *>(p)[i];
@@ -209,6 +344,17 @@ static int launch_row_kind(const RowLaunch &L, const LaunchCtx &c) {
   const bool aligned = (reinterpret_cast<uintptr_t>(L.in) % 16 == 0) && (reinterpret_cast<uintptr_t>(L.out) % 16 == 0) &&
                        (KIND == kSoftmax || reinterpret_cast<uintptr_t>(L.weight) % 16 == 0) &&
                        (L.in_stride % 8 == 0) && (L.out_stride % 8 == 0);
+  if (bf16_io && aligned && L.cols % 1024 == 0 && L.cols <= 8192 && L.in_stride % 8 == 0) {
+    switch (L.cols / 1024) {
+      case 1: return launch_row_stream<KIND, 1>(L, c);
+      case 2: return launch_row_stream<KIND, 2>(L, c);
+      case 3: return launch_row_stream<KIND, 3>(L, c);
+      case 4: return launch_row_stream<KIND, 4>(L, c);
+      case 6: return launch_row_stream<KIND, 6>(L, c);
+      case 8: return launch_row_stream<KIND, 8>(L, c);
+      default: break;
+    }
+  }
   if (bf16_io && aligned && L.cols % 8 == 0) {
     // Spread a row over as many threads as keep at most 4 chunks (32 values) each in registers.
     const int64_t chunks = L.cols / 8;

@@ -1,0 +1,103 @@
+"""A launch graph: the kernel objects of one workload run back to back on one stream over named device
+buffers -- what PyTorchSim does when it runs a model's kernels one after another (the bundle's
+manifest.json lists a workload's launches in order, e.g. validation/pytorchsim/
+qwen3_8b_layer_prefill_2048x2048_bf16/manifest.json).  Buffers are allocated once and stay resident;
+a graph can be captured into a CUDA graph so a many-launch workload costs one launch from the host."""
+import math
+
+from ..codegen import descriptors as D
+from . import native
+
+
+class Graph:
+    def __init__(self, device):
+        import torch
+        self.torch = torch
+        self.device = torch.device(device)
+        self.buffers = {}
+        self.steps = []          # (name, blob, [buffer names], workspace)
+        self.cuda_graph = None
+
+    def buffer(self, name, numel, dtype, init=None):
+        """A device buffer `name` of `numel` elements (`dtype`: a kernel.json dtype name), optionally
+        filled from `init` (a CPU tensor of that many elements)."""
+        torch = self.torch
+        dt = getattr(torch, dtype)
+        if name in self.buffers:
+            t = self.buffers[name]
+            if t.numel() != numel or t.dtype != dt:
+                raise ValueError(f"buffer {name} exists as {t.numel()} x {t.dtype}, asked {numel} x {dt}")
+        else:
+            t = torch.empty(int(numel), dtype=dt, device=self.device)
+            self.buffers[name] = t
+        if init is not None:
+            t.copy_(init.reshape(-1).to(dt))
+        return t
+
+    def add(self, name, blob, bufs):
+        """Append a launch of descriptor `blob` whose tensor arguments are the buffers `bufs`, in the
+        descriptor's argument order; every buffer must exist with the descriptor's element count."""
+        d = D.from_bytes(blob)
+        if len(bufs) != d.nargs:
+            raise ValueError(f"{name}: {len(bufs)} buffers for {d.nargs} arguments")
+        for i, b in enumerate(bufs):
+            t = self.buffers[b]
+            if t.numel() != d.arg_numel[i]:
+                raise ValueError(f"{name}: buffer {b} holds {t.numel()} elements, argument {i} wants {d.arg_numel[i]}")
+        ws = None
+        if d.workspace_bytes:
+            ws = self.torch.empty(int(d.workspace_bytes), dtype=self.torch.uint8, device=self.device)
+        native.check(blob)
+        self.steps.append((name, bytes(blob), list(bufs), ws, d.units))
+
+    def launch_count(self):
+        return len(self.steps)
+
+    def run(self, stream=None, sync=False):
+        """Enqueue every launch in order on `stream` (torch's current stream by default)."""
+        torch = self.torch
+        s = stream or torch.cuda.current_stream(self.device)
+        if self.cuda_graph is not None and stream is None:
+            self.cuda_graph.replay()
+        else:
+            for name, blob, bufs, ws, units in self.steps:
+                native.launch(blob, [self.buffers[b].data_ptr() for b in bufs], 0, units,
+                              ws.data_ptr() if ws is not None else 0, ws.numel() if ws is not None else 0,
+                              s.cuda_stream)
+        if sync:
+            native.sync(s.cuda_stream)
+
+    def capture(self):
+        """Capture the launch sequence into a CUDA graph (replayed by run())."""
+        torch = self.torch
+        native.init(self.device.index or 0)
+        self.run(sync=True)   # first use of every kernel outside the capture
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for name, blob, bufs, ws, units in self.steps:
+                    native.launch(blob, [self.buffers[b].data_ptr() for b in bufs], 0, units,
+                                  ws.data_ptr() if ws is not None else 0, ws.numel() if ws is not None else 0,
+                                  s.cuda_stream)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        self.cuda_graph = g
+        return g
+
+
+def flops_of(blob):
+    """Algorithmic flops of one launch (GEMM 2MNK, causal attention 2*B*HQ*S^2*D), else 0."""
+    d = D.from_bytes(blob)
+    if d.kind == D.GEMM:
+        g = d.p.gemm
+        return 2 * g.M * g.N * g.K
+    if d.kind == D.ATTN_PREFILL:
+        a = d.p.attn
+        full = 4 * a.batch * a.hq * a.seq * a.seq * a.dim
+        return full // 2 if a.causal else full
+    return 0
+
+
+def numel(shape):
+    return math.prod(shape)

@@ -105,11 +105,25 @@ def units(blob):
     return n
 
 
+_desc_buffers = {}
+
+
+def _desc_buffer(blob):
+    """The ctypes copy of a descriptor, made once per distinct descriptor (launch overhead)."""
+    blob = bytes(blob)
+    buf = _desc_buffers.get(blob)
+    if buf is None:
+        if len(_desc_buffers) > 4096:
+            _desc_buffers.clear()
+        buf = _desc_buffers[blob] = C.create_string_buffer(blob, len(blob))
+    return buf
+
+
 def launch(blob, ptrs, lo, hi, workspace=0, workspace_bytes=0, stream=0):
     """Enqueue units [lo, hi) of descriptor `blob` over device pointers `ptrs` on `stream` (a raw
     cudaStream_t as int).  Asynchronous; sync() reports device-side failures."""
     lib = load()
-    buf = C.create_string_buffer(bytes(blob), len(blob))
+    buf = _desc_buffer(blob)
     arr = (C.c_void_p * max(1, len(ptrs)))(*[C.c_void_p(int(p)) for p in ptrs])
     _check(lib.ptsim_launch(buf, len(blob), arr, len(ptrs), int(lo), int(hi), C.c_void_p(int(workspace) or None),
                             int(workspace_bytes), C.c_void_p(int(stream) or None)))

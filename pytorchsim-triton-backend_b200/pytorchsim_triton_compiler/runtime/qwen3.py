@@ -1,0 +1,140 @@
+"""The Qwen3-8B-shaped decoder layer (prefill) as the launch sequence of the validation bundle's workload
+(validation/pytorchsim/qwen3_8b_layer_prefill_2048x2048_bf16/manifest.json, 14 launches):
+
+    00 RMSNorm -> 01 q proj -> 02 q-norm + RoPE -> 03 k proj -> 04 k-norm + RoPE -> 03 v proj -> 05 v relayout
+    -> 06 causal GQA attention -> 07 head->token relayout -> 08 o proj + residual -> 00 RMSNorm
+    -> 09 gate_up proj -> 10 SiLU * mul -> 11 down proj + residual
+
+wired over resident buffers (runtime/graph.py).  On one GPU the launches are the reference kernels' own
+lowered objects (`objects`: launch name -> (kernel.json, desc blob)) or descriptors built for the shape.
+
+Tensor parallel over `tp` GPUs (no counterpart in the reference, which runs one device): q/k/v and
+gate_up are split by output columns (heads / intermediate), o and down by input rows; each rank's o and
+down projections produce a partial sum and one NCCL all-reduce per row-parallel projection adds them
+(two per layer), the residual added by rank 0's epilogue only.  RMSNorms and the RoPE tables are
+replicated.  Shards: 32/tp query heads and 8/tp KV heads per rank (tp <= 8), 12288/tp intermediate."""
+from ..codegen import build as B
+from ..codegen import descriptors as D
+from .graph import Graph
+
+HIDDEN, HQ, HKV, DIM, INTER = 4096, 32, 8, 128, 12288
+
+
+def weight_shapes(T):
+    """Element counts of the layer's tensors (bf16 unless named fp32)."""
+    return {"x": T * HIDDEN, "ln1": HIDDEN, "wq": HIDDEN * HQ * DIM, "wk": HIDDEN * HKV * DIM,
+            "wv": HIDDEN * HKV * DIM, "qn": DIM, "kn": DIM, "wo": HQ * DIM * HIDDEN, "ln2": HIDDEN,
+            "wgu": HIDDEN * 2 * INTER, "wd": INTER * HIDDEN}
+
+
+def shard(p, rank, tp):
+    """Rank `rank`'s shards of the full weights `p` (CPU tensors, [in, out] row-major as the bundle feeds
+    them): column shards of wq/wk/wv/wgu (gate and up halves sharded alike), row shards of wo/wd."""
+    import torch
+    hq, hkv, it = HQ // tp, HKV // tp, INTER // tp
+
+    def cols(w, rows, ncols, lo, hi):
+        return w.view(rows, ncols)[:, lo:hi].contiguous().reshape(-1)
+
+    def rows_(w, nrows, ncols, lo, hi):
+        return w.view(nrows, ncols)[lo:hi].contiguous().reshape(-1)
+
+    q0, k0, i0 = rank * hq * DIM, rank * hkv * DIM, rank * it
+    gu = p["wgu"].view(HIDDEN, 2 * INTER)
+    return {
+        "ln1": p["ln1"], "ln2": p["ln2"], "qn": p["qn"], "kn": p["kn"],
+        "wq": cols(p["wq"], HIDDEN, HQ * DIM, q0, q0 + hq * DIM),
+        "wk": cols(p["wk"], HIDDEN, HKV * DIM, k0, k0 + hkv * DIM),
+        "wv": cols(p["wv"], HIDDEN, HKV * DIM, k0, k0 + hkv * DIM),
+        "wo": rows_(p["wo"], HQ * DIM, HIDDEN, q0, q0 + hq * DIM),
+        "wgu": torch.cat([gu[:, i0:i0 + it], gu[:, INTER + i0:INTER + i0 + it]], dim=1).contiguous().reshape(-1),
+        "wd": rows_(p["wd"], INTER, HIDDEN, i0, i0 + it),
+    }
+
+
+def build_layer(device, T, params, cos, sin, x, tp=1, rank=0, objects=None):
+    """A Graph of one layer on `device` for `T` tokens (rank `rank` of `tp`).  `params` are this rank's
+    (sharded when tp > 1) weights, `x` the input hidden states.  With tp > 1 the graph stops before each
+    all-reduce: it returns the two segments and the caller all-reduces `x1` between them and `y` after."""
+    hq, hkv, it = HQ // tp, HKV // tp, INTER // tp
+    g = Graph(device)
+    bf = "bfloat16"
+    g.buffer("x", T * HIDDEN, bf, x)
+    for n in ("ln1", "ln2", "qn", "kn", "wq", "wk", "wv", "wo", "wgu", "wd"):
+        g.buffer(n, params[n].numel(), bf, params[n])
+    g.buffer("cos", T * DIM, "float32", cos)
+    g.buffer("sin", T * DIM, "float32", sin)
+    for n, cnt in (("h", T * HIDDEN), ("q", T * hq * DIM), ("k", T * hkv * DIM), ("v", T * hkv * DIM),
+                   ("qh", hq * T * DIM), ("kh", hkv * T * DIM), ("vh", hkv * T * DIM), ("o", hq * T * DIM),
+                   ("ot", T * hq * DIM), ("x1", T * HIDDEN), ("h2", T * HIDDEN), ("gu", T * 2 * it),
+                   ("a", T * it), ("y", T * HIDDEN)):
+        g.buffer(n, cnt, bf)
+
+    def obj(key, fallback):
+        if objects and key in objects and tp == 1:
+            return objects[key]
+        return D.to_bytes(fallback())
+
+    resid_o = rank == 0
+    seg1 = [
+        ("00_rmsnorm", obj("00", lambda: B.row_rmsnorm(T, HIDDEN, 1e-6)), ["x", "ln1", "h"]),
+        ("01_q_mm", obj("01", lambda: B.gemm(T, hq * DIM, HIDDEN)), ["h", "wq", "q"]),
+        ("02_qnorm_rope", obj("02", lambda: B.qknorm_rope(T, hq)), ["q", "qn", "cos", "sin", "qh"]),
+        ("03_k_mm", obj("03", lambda: B.gemm(T, hkv * DIM, HIDDEN)), ["h", "wk", "k"]),
+        ("04_knorm_rope", obj("04", lambda: B.qknorm_rope(T, hkv)), ["k", "kn", "cos", "sin", "kh"]),
+        ("03_v_mm", obj("03", lambda: B.gemm(T, hkv * DIM, HIDDEN)), ["h", "wv", "v"]),
+        ("05_v_relayout", obj("05", lambda: B.copy_map(T * hkv * DIM, T * hkv * DIM,
+                                                       [(1, DIM, 1), (DIM, T, hkv * DIM), (T * DIM, hkv, DIM)])),
+         ["v", "vh"]),
+        ("06_attention", obj("06", lambda: B.attention(1, hq, hkv, T)), ["qh", "kh", "vh", "o"]),
+        ("07_o_relayout", obj("07", lambda: B.copy_map(T * hq * DIM, T * hq * DIM,
+                                                       [(1, DIM, 1), (DIM, hq, T * DIM), (hq * DIM, T, DIM)])),
+         ["o", "ot"]),
+    ]
+    if resid_o:
+        seg1.append(("08_o_mm_residual", obj("08", lambda: B.gemm(T, HIDDEN, hq * DIM, residual=True)),
+                     ["x", "ot", "wo", "x1"]))
+    else:
+        seg1.append(("08_o_mm", D.to_bytes(B.gemm(T, HIDDEN, hq * DIM)), ["ot", "wo", "x1"]))
+    seg2 = [
+        ("00_rmsnorm_2", obj("00", lambda: B.row_rmsnorm(T, HIDDEN, 1e-6)), ["x1", "ln2", "h2"]),
+        ("09_gate_up_mm", obj("09", lambda: B.gemm(T, 2 * it, HIDDEN)), ["h2", "wgu", "gu"]),
+        ("10_silu_mul", obj("10", lambda: B.silu_mul(T, it)), ["gu", "a"]),
+    ]
+    if resid_o:
+        seg2.append(("11_down_mm_residual", obj("11", lambda: B.gemm(T, HIDDEN, it, residual=True)),
+                     ["x1", "a", "wd", "y"]))
+    else:
+        seg2.append(("11_down_mm", D.to_bytes(B.gemm(T, HIDDEN, it)), ["a", "wd", "y"]))
+    if tp == 1:
+        for name, blob, bufs in seg1 + seg2:
+            g.add(name, blob, bufs)
+        return g, None
+    g1, g2 = g, Graph(device)
+    g2.buffers = g.buffers
+    for name, blob, bufs in seg1:
+        g1.add(name, blob, bufs)
+    for name, blob, bufs in seg2:
+        g2.add(name, blob, bufs)
+    return g1, g2
+
+
+def layer_flops(T):
+    """GEMM + causal attention flops of one layer (824,633,720,832 at T = 2048)."""
+    gemm = 2 * T * HIDDEN * (HQ * DIM + 2 * HKV * DIM) + 2 * T * HQ * DIM * HIDDEN + 2 * T * HIDDEN * 2 * INTER \
+        + 2 * T * INTER * HIDDEN
+    attn = 4 * HQ * T * T * DIM // 2
+    return gemm + attn
+
+
+def random_params(seed=0):
+    """Weights of the layer: linear weights N(0, 0.02), norm weights N(1, 0.02), bf16."""
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    out = {}
+    for n, cnt in weight_shapes(1).items():
+        if n == "x":
+            continue
+        std, mean = 0.02, (1.0 if n in ("ln1", "ln2", "qn", "kn") else 0.0)
+        out[n] = (torch.randn(cnt, generator=g) * std + mean).to(torch.bfloat16)
+    return out
