@@ -253,6 +253,166 @@ __global__ void __launch_bounds__(128) row_stream_kernel(const __grid_constant__
   }
 }
 
+// ---------------------------------------------------------------------------------------------------
+// Warp-per-row streaming path (cols a multiple of 256, up to 16384): one CTA per SM with a producer warp
+// and 16 consumer warps.  The producer keeps a ring of up to 31 whole rows in shared memory filled by
+// bulk async copies (full/empty mbarrier per slot); each consumer warp takes rows k = w, w + 16, ... and
+// works on its slot alone -- warp shuffles only, no block barriers -- in three passes over shared memory
+// (softmax: max on packed bf16 pairs, sum of exp, exp / sum; RMSNorm: sum of squares, scale) with paired
+// fp32 arithmetic (FADD2/FMUL2/FFMA2), then releases the slot.  Per SM ~24 rows are in flight, which
+// covers HBM latency; each element is read from HBM once and written once.
+// ---------------------------------------------------------------------------------------------------
+constexpr int kRowConsumers = 16;
+constexpr int kRowWarpThreads = 32 * (kRowConsumers + 1);
+
+__device__ __forceinline__ float2 unpack_bf16x2(uint32_t w) { return make_float2(lo_bf16(w), hi_bf16(w)); }
+
+template <int KIND>
+__global__ void __launch_bounds__(kRowWarpThreads, 1) row_warp_kernel(const __grid_constant__ RowLaunch L, int slots) {
+  extern __shared__ __align__(128) uint8_t dyn[];
+  __shared__ uint64_t full[32], empty[32], wbar;
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t row_bytes = uint32_t(L.cols) * 2u;
+  const int chunks = int(L.cols / 8);
+  uint8_t *wrow = dyn;                                        // RMSNorm weight row
+  uint8_t *ring = dyn + (KIND == kRmsNorm ? row_bytes : 0);
+  const int64_t nrows = L.rows_end - L.rows_begin;
+  const int64_t mine = nrows > blockIdx.x ? (nrows - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  auto row_of = [&](int64_t k) { return L.rows_begin + int64_t(blockIdx.x) + k * int64_t(gridDim.x); };
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < slots; ++i) {
+      sm100::mbar_init(&full[i], 1);
+      sm100::mbar_init(&empty[i], 1);
+    }
+    sm100::mbar_init(&wbar, 1);
+    abort_flag = 0;
+    sm100::fence_barrier_init();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    if (lane == 0) {
+      if constexpr (KIND == kRmsNorm) {
+        sm100::mbar_arrive_expect_tx(&wbar, row_bytes);
+        bulk_load(wrow, L.weight, row_bytes, &wbar);
+      }
+      int64_t k = 0;
+      for (; k < mine && !abort_flag; ++k) {
+        const int s = int(k % slots);
+        if (k >= slots && !sm100::mbar_wait(&empty[s], uint32_t(k / slots - 1) & 1u)) { abort_flag = 1; break; }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        sm100::mbar_arrive_expect_tx(&full[s], row_bytes);
+        bulk_load(ring + size_t(s) * row_bytes, reinterpret_cast<const uint16_t *>(L.in) + row_of(k) * L.in_stride,
+                  row_bytes, &full[s]);
+      }
+      // Bulk copies still in flight land before the CTA exits (only an aborted run can leave some).
+      if (abort_flag)
+        for (int64_t j = (k > slots ? k - slots : 0); j < k; ++j)
+          sm100::mbar_wait(&full[int(j % slots)], uint32_t(j / slots) & 1u);
+      if constexpr (KIND == kRmsNorm) sm100::mbar_wait(&wbar, 0);
+    }
+    return;
+  }
+  const int c = warp - 1;
+  if constexpr (KIND == kRmsNorm) {
+    if (!sm100::mbar_wait(&wbar, 0)) abort_flag = 1;
+  }
+  for (int64_t k = c; k < mine && !abort_flag; k += kRowConsumers) {
+    const int s = int(k % slots);
+    if (!sm100::mbar_wait(&full[s], uint32_t(k / slots) & 1u)) { abort_flag = 1; break; }
+    const uint4 *src = reinterpret_cast<const uint4 *>(ring + size_t(s) * row_bytes);
+    uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(L.out) + row_of(k) * L.out_stride);
+    if constexpr (KIND == kSoftmax) {
+      __nv_bfloat162 mx2 = __floats2bfloat162_rn(-INFINITY, -INFINITY);
+      for (int q = lane; q < chunks; q += 32) {
+        const uint4 w = src[q];
+        mx2 = __hmax2_nan(mx2, *reinterpret_cast<const __nv_bfloat162 *>(&w.x));
+        mx2 = __hmax2_nan(mx2, *reinterpret_cast<const __nv_bfloat162 *>(&w.y));
+        mx2 = __hmax2_nan(mx2, *reinterpret_cast<const __nv_bfloat162 *>(&w.z));
+        mx2 = __hmax2_nan(mx2, *reinterpret_cast<const __nv_bfloat162 *>(&w.w));
+      }
+      float m = nan_max(__low2float(mx2), __high2float(mx2));
+      m = row_allreduce<32>(m, true, nullptr);
+      const float2 negm = make_float2(-m, -m), l2e = make_float2(1.4426950408889634f, 1.4426950408889634f);
+      float2 acc = make_float2(0.f, 0.f);
+      for (int q = lane; q < chunks; q += 32) {
+        const uint4 w = src[q];
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 t = __fmul2_rn(__fadd2_rn(unpack_bf16x2(ws[j]), negm), l2e);
+          acc = __fadd2_rn(acc, make_float2(ex2_fast(t.x), ex2_fast(t.y)));
+        }
+      }
+      float sum = row_allreduce<32>(__fadd_rn(acc.x, acc.y), false, nullptr);
+      const float r = __frcp_rn(sum);
+      const float2 r2 = make_float2(r, r), nsum2 = make_float2(-sum, -sum);
+      for (int q = lane; q < chunks; q += 32) {
+        const uint4 w = src[q];
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 t = __fmul2_rn(__fadd2_rn(unpack_bf16x2(ws[j]), negm), l2e);
+          const float2 e = make_float2(ex2_fast(t.x), ex2_fast(t.y));
+          // e / sum: reciprocal product plus one residual correction (see div_by).
+          const float2 q0 = __fmul2_rn(e, r2);
+          const float2 res = __ffma2_rn(q0, nsum2, e);
+          const float2 q1 = __ffma2_rn(res, r2, q0);
+          o[j] = pack_bf16x2(q1.x, q1.y);
+        }
+        __stcs(dst + q, make_uint4(o[0], o[1], o[2], o[3]));
+      }
+    } else {
+      float2 acc = make_float2(0.f, 0.f);
+      for (int q = lane; q < chunks; q += 32) {
+        const uint4 w = src[q];
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 x = unpack_bf16x2(ws[j]);
+          acc = __fadd2_rn(acc, __fmul2_rn(x, x));
+        }
+      }
+      const float ss = row_allreduce<32>(__fadd_rn(acc.x, acc.y), false, nullptr);
+      const float rs = rsqrtf(__fadd_rn(__fdiv_rn(ss, float(L.cols)), L.eps));
+      const float2 rs2 = make_float2(rs, rs);
+      const uint4 *wsrc = reinterpret_cast<const uint4 *>(wrow);
+      for (int q = lane; q < chunks; q += 32) {
+        const uint4 w = src[q], g = wsrc[q];
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w}, gs[4] = {g.x, g.y, g.z, g.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 y = __fmul2_rn(__fmul2_rn(unpack_bf16x2(ws[j]), rs2), unpack_bf16x2(gs[j]));
+          o[j] = pack_bf16x2(y.x, y.y);
+        }
+        __stcs(dst + q, make_uint4(o[0], o[1], o[2], o[3]));
+      }
+    }
+    __syncwarp();
+    if (lane == 0) sm100::mbar_arrive(&empty[s]);
+  }
+}
+
+template <int KIND>
+static int launch_row_warp(const RowLaunch &L, const LaunchCtx &c) {
+  const int64_t row_bytes = L.cols * 2;
+  const int64_t budget = 200 * 1024 - (KIND == kRmsNorm ? row_bytes : 0);
+  int slots = int(budget / row_bytes);
+  if (slots > 31) slots = 31;
+  if (slots < 2) return fail(PTSIM_E_RESOURCE, "row of %lld bf16 does not fit the shared-memory ring", (long long)L.cols);
+  const int smem = int(slots * row_bytes + (KIND == kRmsNorm ? row_bytes : 0));
+  auto kern = row_warp_kernel<KIND>;
+  PTSIM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int64_t rows = L.rows_end - L.rows_begin;
+  int64_t grid = c.sm_count;
+  if (grid > rows) grid = rows;
+  kern<<<unsigned(grid), kRowWarpThreads, smem, c.stream>>>(L, slots);
+  PTSIM_CUDA(cudaGetLastError());
+  return PTSIM_OK;
+}
+
 template <int KIND, int CH>
 static int launch_row_stream(const RowLaunch &L, const LaunchCtx &c) {
   const int64_t row_bytes = L.cols * 2;
@@ -344,6 +504,9 @@ static int launch_row_kind(const RowLaunch &L, const LaunchCtx &c) {
   const bool aligned = (reinterpret_cast<uintptr_t>(L.in) % 16 == 0) && (reinterpret_cast<uintptr_t>(L.out) % 16 == 0) &&
                        (KIND == kSoftmax || reinterpret_cast<uintptr_t>(L.weight) % 16 == 0) &&
                        (L.in_stride % 8 == 0) && (L.out_stride % 8 == 0);
+  if (bf16_io && aligned && L.cols % 256 == 0 && L.cols <= 16384 && (L.rows_end - L.rows_begin) >= 4 * c.sm_count &&
+      !(KIND == kRmsNorm && (reinterpret_cast<uintptr_t>(L.weight) % 16 != 0)))
+    return launch_row_warp<KIND>(L, c);
   if (bf16_io && aligned && L.cols % 1024 == 0 && L.cols <= 8192 && L.in_stride % 8 == 0) {
     switch (L.cols / 1024) {
       case 1: return launch_row_stream<KIND, 1>(L, c);
