@@ -266,6 +266,251 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
   }
 }
 
+// ---------------------------------------------------------------------------------------------------
+// Version 2 (sequence a multiple of 256): two 128-row query tiles A and B per CTA share each K/V tile.
+//   warp 0      TMA: Q_A, Q_B once; K_j, V_j into a two-deep ring;
+//   warp 1      MMA: S_A(j) = Q_A.K_j^T, S_B(j) = Q_B.K_j^T into TMEM; then O_A += P_A(j).V_j and
+//               O_B += P_B(j).V_j with P read from TMEM (the A operand of a TMEM-sourced MMA);
+//   warps 2..5  softmax of tile A, warps 6..9 softmax of tile B (one query row per thread): S is read
+//               from TMEM in 32-column chunks twice (row max, then exp / sum / bf16 pack), P is written
+//               back as packed bf16 pairs over the consumed S columns, O is rescaled in TMEM when the row
+//               max moved, and at the end O / l is stored.
+// The two softmax warpgroups alternate with the tensor core (while one computes exp, the MMA runs the
+// other tile's products).  In-order MMA execution makes S_X(j)'s commit imply PV_X(j-1) has finished,
+// so a softmax may rescale O_X and overwrite P_X as soon as S_X(j) is ready.
+// TMEM: S_A [0,128)  S_B [128,256)  O_A [256,384)  O_B [384,512).
+// ---------------------------------------------------------------------------------------------------
+constexpr int kAttn2Threads = 320;
+constexpr int kAttn2Smem = 6 * kAttnTile + 1024 + 256;  // Q_A, Q_B, K x2, V x2
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  uint32_t lo[16], hi[16];
+#pragma unroll
+  for (int q = 0; q < 16; ++q) { lo[q] = r[q]; hi[q] = r[16 + q]; }
+  sm100::tmem_st16(taddr, lo);
+  sm100::tmem_st16(taddr + 16, hi);
+}
+
+__global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __grid_constant__ AttnArgs g) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sQ = smem;                   // Q_A, Q_B
+  uint8_t *sK = smem + 2 * kAttnTile;   // 2 stages
+  uint8_t *sV = smem + 4 * kAttnTile;   // 2 stages
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 6 * kAttnTile);
+  uint64_t *q_full = bars + 0;
+  uint64_t *k_full = bars + 1;    // 2
+  uint64_t *v_full = bars + 3;    // 2
+  uint64_t *kv_empty = bars + 5;  // 2
+  uint64_t *s_full = bars + 7;    // [A, B]
+  uint64_t *p_full = bars + 9;    // [A, B], 4 arrivals each
+  uint64_t *o_done = bars + 11;   // [A, B]
+  uint64_t *drain = bars + 13;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 14);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t units = g.unit_end - g.unit_begin;
+  const int pairs = g.q_tiles / 2;
+  const int qp = pairs - 1 - int(int64_t(blockIdx.x) / units);   // heaviest query-tile pairs first
+  const int64_t unit = g.unit_begin + int64_t(blockIdx.x) % units;
+  const int64_t b = unit / g.hq, h = unit % g.hq;
+  const int64_t kvh = b * g.hkv + h / (g.hq / g.hkv);
+  const int q_row0 = int(unit * g.seq + int64_t(qp) * 2 * kAttnBM);
+  const int kv_row0 = int(kvh * g.seq);
+  const int nA = g.causal ? 2 * qp + 1 : int(g.seq / kAttnBN);   // key tiles of query tile A
+  const int nB = g.causal ? 2 * qp + 2 : nA;                      // and of tile B
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 14; ++i) sm100::mbar_init(&bars[i], (i == 9 || i == 10) ? 4u : 1u);
+    *abort_flag = 0;
+    sm100::fence_barrier_init();
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(tmem_slot, 512);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      sm100::mbar_arrive_expect_tx(q_full, 2 * kAttnTile);
+      sm100::tma_load_2d(sQ, &g.tq, q_full, 0, q_row0);
+      sm100::tma_load_2d(sQ + 16384, &g.tq, q_full, 64, q_row0);
+      sm100::tma_load_2d(sQ + kAttnTile, &g.tq, q_full, 0, q_row0 + kAttnBM);
+      sm100::tma_load_2d(sQ + kAttnTile + 16384, &g.tq, q_full, 64, q_row0 + kAttnBM);
+      int j = 0;
+      for (; j < nB; ++j) {
+        const int st = j & 1;
+        if (!sm100::mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1)) { *abort_flag = 1; break; }
+        const int kr = kv_row0 + j * kAttnBN;
+        sm100::mbar_arrive_expect_tx(&k_full[st], kAttnTile);
+        sm100::tma_load_2d(sK + st * kAttnTile, &g.tk, &k_full[st], 0, kr);
+        sm100::tma_load_2d(sK + st * kAttnTile + 16384, &g.tk, &k_full[st], 64, kr);
+        sm100::mbar_arrive_expect_tx(&v_full[st], kAttnTile);
+        sm100::tma_load_2d(sV + st * kAttnTile, &g.tv, &v_full[st], 0, kr);
+        sm100::tma_load_2d(sV + st * kAttnTile + 16384, &g.tv, &v_full[st], 64, kr);
+      }
+      if (*abort_flag) {
+        sm100::mbar_wait(q_full, 0);
+        for (int i = (j - 2 < 0 ? 0 : j - 2); i < j; ++i) {
+          sm100::mbar_wait(&k_full[i & 1], (i >> 1) & 1);
+          sm100::mbar_wait(&v_full[i & 1], (i >> 1) & 1);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = sm100::idesc_bf16_f32(kAttnBM, kAttnBN, false, false);
+      constexpr uint32_t idesc_o = sm100::idesc_bf16_f32(kAttnBM, kAttnD, false, true);
+      bool ok = sm100::mbar_wait(q_full, 0);
+      for (int j = 0; ok && j < nB; ++j) {
+        const int st = j & 1;
+        if (!sm100::mbar_wait(&k_full[st], (j >> 1) & 1)) { ok = false; break; }
+        sm100::tc_fence_after();
+        const uint32_t k_addr = sm100::smem_u32(sK + st * kAttnTile);
+        for (int t = 0; t < 2; ++t) {
+          if (t == 0 && j >= nA) continue;
+          const uint32_t q_addr = sm100::smem_u32(sQ + t * kAttnTile);
+#pragma unroll
+          for (int k = 0; k < kAttnD / 16; ++k) {
+            const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
+            sm100::mma_bf16_ss(tmem + t * 128, sm100::sw128_desc(q_addr + off, 16, 1024),
+                               sm100::sw128_desc(k_addr + off, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
+          }
+          sm100::mma_commit(&s_full[t]);
+        }
+        if (!sm100::mbar_wait(&v_full[st], (j >> 1) & 1)) { ok = false; break; }
+        const uint32_t v_addr = sm100::smem_u32(sV + st * kAttnTile);
+        for (int t = 0; t < 2; ++t) {
+          if (t == 0 && j >= nA) continue;
+          if (!sm100::mbar_wait(&p_full[t], j & 1)) { ok = false; break; }
+          sm100::tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < kAttnBN / 16; ++k)
+            sm100::mma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + k * 8,
+                               sm100::sw128_desc(v_addr + k * 16 * 128, 16384, 1024), idesc_o,
+                               (j > 0 || k > 0) ? 1u : 0u);
+          if (j == (t == 0 ? nA : nB) - 1) sm100::mma_commit(&o_done[t]);
+        }
+        if (!ok) break;
+        sm100::mma_commit(&kv_empty[st]);
+      }
+      if (!ok) *abort_flag = 1;
+      sm100::mma_commit(drain);
+      sm100::mbar_wait(drain, 0);
+    }
+  } else {
+    const int t = (warp - 2) >> 2;          // 0: tile A, 1: tile B
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;       // query row within the tile = TMEM lane
+    const uint32_t lane_off = uint32_t(quarter * 32) << 16;
+    const uint32_t tS = tmem + t * 128 + lane_off, tO = tmem + 256 + t * 128 + lane_off;
+    const int ntiles = t == 0 ? nA : nB;
+    const int diag = t == 0 ? 2 * qp : 2 * qp + 1;   // the key tile holding this query tile's diagonal
+    const float kLog2e = 1.4426950408889634f;
+    const float sc = g.scale, sl = g.scale * kLog2e;
+    float m = -1.0e30f, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      if (*abort_flag || !sm100::mbar_wait(&s_full[t], j & 1)) { ok = false; break; }
+      sm100::tc_fence_after();
+      const bool masked = g.causal && j == diag;
+      // Pass 1: row max of the raw products (scale > 0 keeps the arg max; masked keys excluded).
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        sm100::tmem_ld32(tS + c * 32, v);
+        sm100::tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+          const float x = __uint_as_float(v[q]);
+          if (!masked || c * 32 + q <= r) mx = fmaxf(mx, x);
+        }
+      }
+      const float m_new = fmaxf(m, __fmul_rn(mx, sc));
+      const float alpha = ex2_fast(__fmul_rn(__fsub_rn(m, m_new), kLog2e));
+      const float2 a2 = make_float2(sl, sl), b2 = make_float2(-m_new * kLog2e, -m_new * kLog2e);
+      float2 acc = make_float2(0.f, 0.f);
+      // Pass 2: p = exp(qk - m'), row sum, bf16 P packed over the consumed S columns.
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        sm100::tmem_ld32(tS + c * 32, v);
+        sm100::tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const float2 x = make_float2(__uint_as_float(v[2 * q]), __uint_as_float(v[2 * q + 1]));
+          const float2 u = __ffma2_rn(x, a2, b2);
+          float p0 = ex2_fast(u.x), p1 = ex2_fast(u.y);
+          if (masked) {
+            if (c * 32 + 2 * q > r) p0 = 0.f;
+            if (c * 32 + 2 * q + 1 > r) p1 = 0.f;
+          }
+          acc = __fadd2_rn(acc, make_float2(p0, p1));
+          pk[q] = pack_bf16x2(p0, p1);
+        }
+        sm100::tmem_st16(tS + c * 16, pk);
+      }
+      l = __fadd_rn(__fmul_rn(l, alpha), __fadd_rn(acc.x, acc.y));
+      m = m_new;
+      // O rescale (O already holds PV_X(j-1): S_X(j) was issued after it).
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+        const float2 al2 = make_float2(alpha, alpha);
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          sm100::tmem_ld32(tO + c * 32, v);
+          sm100::tmem_wait_ld();
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const float2 o = __fmul2_rn(make_float2(__uint_as_float(v[2 * q]), __uint_as_float(v[2 * q + 1])), al2);
+            v[2 * q] = __float_as_uint(o.x);
+            v[2 * q + 1] = __float_as_uint(o.y);
+          }
+          tmem_st32(tO + c * 32, v);
+        }
+      }
+      sm100::tmem_wait_st();
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&p_full[t]);
+    }
+    if (ok && !*abort_flag && sm100::mbar_wait(&o_done[t], 0)) {
+      sm100::tc_fence_after();
+      uint16_t *orow = g.o + (int64_t(q_row0) + t * kAttnBM + r) * kAttnD;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        sm100::tmem_ld32(tO + c * 32, v);
+        sm100::tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 w;
+          w.x = pack_bf16x2(__fdiv_rn(__uint_as_float(v[q * 8 + 0]), l), __fdiv_rn(__uint_as_float(v[q * 8 + 1]), l));
+          w.y = pack_bf16x2(__fdiv_rn(__uint_as_float(v[q * 8 + 2]), l), __fdiv_rn(__uint_as_float(v[q * 8 + 3]), l));
+          w.z = pack_bf16x2(__fdiv_rn(__uint_as_float(v[q * 8 + 4]), l), __fdiv_rn(__uint_as_float(v[q * 8 + 5]), l));
+          w.w = pack_bf16x2(__fdiv_rn(__uint_as_float(v[q * 8 + 6]), l), __fdiv_rn(__uint_as_float(v[q * 8 + 7]), l));
+          reinterpret_cast<uint4 *>(orow + c * 32)[q] = w;
+        }
+      }
+    } else {
+      *abort_flag = 1;
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, 512);
+  }
+}
+
 int launch_attention(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c) {
   const ptsim_attn_params &a = d.p.attn;
   if (a.dim != kAttnD) return fail(PTSIM_E_UNSUPPORTED, "attention runs head_dim 128, not %lld", (long long)a.dim);
@@ -291,6 +536,13 @@ int launch_attention(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t
   g.unit_end = u1;
   g.scale = a.scale;
   if (int64_t(a.batch * a.hkv * a.seq) >= (int64_t(1) << 31)) return fail(PTSIM_E_UNSUPPORTED, "attention rows exceed int32");
+  if (a.seq % (2 * kAttnBM) == 0 && getenv("PTSIM_ATTN_V1") == nullptr) {
+    PTSIM_CUDA(cudaFuncSetAttribute(attn2_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttn2Smem));
+    const int64_t grid = (u1 - u0) * (g.q_tiles / 2);
+    attn2_fwd_kernel<<<unsigned(grid), kAttn2Threads, kAttn2Smem, c.stream>>>(g);
+    PTSIM_CUDA(cudaGetLastError());
+    return PTSIM_OK;
+  }
   PTSIM_CUDA(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
   const int64_t grid = (u1 - u0) * g.q_tiles;
   attn_fwd_kernel<<<unsigned(grid), kAttnThreads, kAttnSmem, c.stream>>>(g);

@@ -45,6 +45,14 @@ __device__ __forceinline__ float hi_bf16(uint32_t w) { return __uint_as_float(w 
 // exp as the EUP computes it: 2^(x * log2(e)) (targets/tpu/lower_vector_functions.py:310-329).
 __device__ __forceinline__ float npu_exp(float x) { return exp2f(x * 1.4426950408889634f); }
 
+// 2^x on the special-function unit (one MUFU op; denormal results flush to zero, which the downstream
+// bf16 rounding of a softmax probability would also produce).
+__device__ __forceinline__ float ex2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // NaN-propagating max/min (the vmax/vmin rule of PyTorchSimTpuOps.td:64-74; tl.PropagateNan.ALL).
 // max.NaN / min.NaN return the canonical NaN when either operand is NaN (one instruction on sm_80+).
 __device__ __forceinline__ float nan_max(float a, float b) {

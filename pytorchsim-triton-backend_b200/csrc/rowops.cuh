@@ -23,6 +23,7 @@ struct RowLaunch {
   void *out;
   const void *weight;
   int64_t rows_begin, rows_end, cols, in_stride, out_stride;
+  int64_t rows_total;  // rows of the whole launch: the kernel choice depends on it, never on [lo, hi)
   int32_t in_dt, out_dt, w_dt, pad;
   float eps;
 };
@@ -48,14 +49,6 @@ __device__ __forceinline__ float row_allreduce(float v, bool is_max, float *smem
     v = t;
   }
   return v;
-}
-
-// 2^x on the special-function unit (one MUFU op; denormal results flush to zero, which the downstream
-// bf16 rounding of a softmax probability would also produce).
-__device__ __forceinline__ float ex2_fast(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
 }
 
 // a / b with the reciprocal r = 1/b computed once per row: q = a*r, then one residual correction
@@ -255,14 +248,14 @@ __global__ void __launch_bounds__(128) row_stream_kernel(const __grid_constant__
 
 // ---------------------------------------------------------------------------------------------------
 // Warp-per-row streaming path (cols a multiple of 256, up to 16384): one CTA per SM with a producer warp
-// and 16 consumer warps.  The producer keeps a ring of up to 31 whole rows in shared memory filled by
+// and 31 consumer warps.  The producer keeps a ring of up to 31 whole rows in shared memory filled by
 // bulk async copies (full/empty mbarrier per slot); each consumer warp takes rows k = w, w + 16, ... and
 // works on its slot alone -- warp shuffles only, no block barriers -- in three passes over shared memory
 // (softmax: max on packed bf16 pairs, sum of exp, exp / sum; RMSNorm: sum of squares, scale) with paired
 // fp32 arithmetic (FADD2/FMUL2/FFMA2), then releases the slot.  Per SM ~24 rows are in flight, which
 // covers HBM latency; each element is read from HBM once and written once.
 // ---------------------------------------------------------------------------------------------------
-constexpr int kRowConsumers = 16;
+constexpr int kRowConsumers = 31;
 constexpr int kRowWarpThreads = 32 * (kRowConsumers + 1);
 
 __device__ __forceinline__ float2 unpack_bf16x2(uint32_t w) { return make_float2(lo_bf16(w), hi_bf16(w)); }
@@ -504,7 +497,7 @@ static int launch_row_kind(const RowLaunch &L, const LaunchCtx &c) {
   const bool aligned = (reinterpret_cast<uintptr_t>(L.in) % 16 == 0) && (reinterpret_cast<uintptr_t>(L.out) % 16 == 0) &&
                        (KIND == kSoftmax || reinterpret_cast<uintptr_t>(L.weight) % 16 == 0) &&
                        (L.in_stride % 8 == 0) && (L.out_stride % 8 == 0);
-  if (bf16_io && aligned && L.cols % 256 == 0 && L.cols <= 16384 && (L.rows_end - L.rows_begin) >= 4 * c.sm_count &&
+  if (bf16_io && aligned && L.cols % 256 == 0 && L.cols <= 16384 && L.rows_total >= 4 * c.sm_count &&
       !(KIND == kRmsNorm && (reinterpret_cast<uintptr_t>(L.weight) % 16 != 0)))
     return launch_row_warp<KIND>(L, c);
   if (bf16_io && aligned && L.cols % 1024 == 0 && L.cols <= 8192 && L.in_stride % 8 == 0) {
@@ -552,6 +545,7 @@ int launch_rowops(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi
   L.weight = p.weight_arg >= 0 ? ptrs[p.weight_arg] : nullptr;
   L.rows_begin = lo * d.unit_size;
   L.rows_end = hi * d.unit_size < p.rows ? hi * d.unit_size : p.rows;
+  L.rows_total = p.rows;
   L.cols = p.cols;
   L.in_stride = p.in_row_stride;
   L.out_stride = p.out_row_stride;

@@ -141,7 +141,9 @@ def test_gemm_b_kmajor(M, N, K):
 
 
 @pytest.mark.parametrize("batch,hq,hkv,seq,causal", [(1, 4, 1, 256, True), (2, 8, 2, 512, True),
-                                                     (1, 2, 2, 256, False), (1, 32, 8, 1024, True)])
+                                                     (1, 2, 2, 256, False), (1, 32, 8, 1024, True),
+                                                     (1, 4, 2, 384, True), (2, 2, 1, 128, True),
+                                                     (1, 2, 1, 768, False)])
 def test_attention(batch, hq, hkv, seq, causal):
     dim = 128
     g = torch.Generator().manual_seed(9)
