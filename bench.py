@@ -358,7 +358,8 @@ def suite(dev, stream, iters=5, only=None, warm=1):
                 ts.append((torch.randn(n, generator=g, device=dev) * std).to(dt))
             else:
                 ts.append(torch.zeros(n, dtype=dt, device=dev))
-        ws = torch.empty(max(1, d.workspace_bytes), dtype=torch.uint8, device=dev)
+        wsn = native.workspace_size(blob, dev.index or 0)
+        ws = torch.empty(max(1, wsn), dtype=torch.uint8, device=dev)
         ptrs = [t.data_ptr() for t in ts]
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters + warm)]
         torch.cuda.synchronize()
@@ -366,7 +367,7 @@ def suite(dev, stream, iters=5, only=None, warm=1):
         for k in range(iters + warm):
             flush.zero_()
             ev[k][0].record(stream)
-            native.launch(blob, ptrs, 0, d.units, ws.data_ptr(), d.workspace_bytes, stream.cuda_stream)
+            native.launch(blob, ptrs, 0, d.units, ws.data_ptr(), wsn, stream.cuda_stream)
             ev[k][1].record(stream)
         native.sync(stream.cuda_stream)
         times = [a.elapsed_time(b) for a, b in ev[warm:]]

@@ -161,7 +161,8 @@ typedef struct ptsim_desc {
   int64_t grid[3];       /* the reference launch grid the lowering was made for */
   int64_t units;         /* partition units of a launch: [lo, hi) of ptsim_launch index these */
   int64_t unit_size;     /* elements (ELEMENTWISE), rows (row kinds), M rows (GEMM), (b, h) (attention) per unit */
-  int64_t workspace_bytes; /* scratch the launch needs from the caller (REDUCE_ALL partials), else 0 */
+  int64_t workspace_bytes; /* scratch the lowering knows a launch needs (REDUCE_ALL partials); the library's
+                              ptsim_workspace_size() gives the full amount for a device (split-K GEMM) */
   union {
     ptsim_ew_params ew;
     ptsim_row_params row;
@@ -195,6 +196,12 @@ int64_t ptsim_units(const void *desc, size_t desc_bytes);
  * the ELF's program loop codegen/wrapper.py:254-266. */
 int ptsim_launch(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int nptr,
                  int64_t lo, int64_t hi, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Bytes of device scratch a launch of `desc` wants on `device` (-1 on a bad descriptor): the REDUCE_ALL
+ * partials, or the split-K partial tiles of a GEMM whose output has fewer tiles than the device has SMs.
+ * A GEMM launched with less (or none) runs without split-K: same result, fewer SMs busy.  No reference
+ * counterpart (Spike needed no device scratch). */
+int64_t ptsim_workspace_size(const void *desc, size_t desc_bytes, int device);
 
 /* Synchronise `stream` and return (and clear) the device status word of the current device:
  * *device_status receives PTSIM_OK or PTSIM_E_OOB / PTSIM_E_TIMEOUT as a kernel recorded it.

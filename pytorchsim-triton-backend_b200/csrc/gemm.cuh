@@ -43,7 +43,55 @@ struct GemmArgs {
   float *c_f32;         // fp32 output instead of bf16 when non-null
   int64_t m_begin, m_end, N, K, ldc, ldr;
   int32_t tiles_m, tiles_n;
+  int32_t splits, kb_per_split;  // split-K: each output tile's K range cut into `splits` work items
+  int *counters;                 // per tile: how many splits have written their partial (zeroed per launch)
+  float *partials;               // [tile][split][BM][BN] fp32 partial accumulators
 };
+
+// The epilogue of 32 output columns of one row: + residual (bf16), then the store rounded to the output
+// dtype (bf16 RNE, or fp32).
+__device__ __forceinline__ void gemm_store_row32(const GemmArgs &g, int64_t row, int64_t col0, float (&acc)[32]) {
+  const bool full = col0 + 32 <= g.N;
+  if (g.r != nullptr) {
+    const uint16_t *rp = g.r + row * g.ldr + col0;
+    if (full && (g.ldr % 8 == 0)) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 w = __ldg(reinterpret_cast<const uint4 *>(rp) + q);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          acc[q * 8 + 2 * e] = __fadd_rn(acc[q * 8 + 2 * e], lo_bf16(ws[e]));
+          acc[q * 8 + 2 * e + 1] = __fadd_rn(acc[q * 8 + 2 * e + 1], hi_bf16(ws[e]));
+        }
+      }
+    } else {
+      for (int q = 0; q < 32; ++q)
+        if (col0 + q < g.N) acc[q] = __fadd_rn(acc[q], bf16_bits_to_f32(rp[q]));
+    }
+  }
+  if (g.c_f32 != nullptr) {
+    float *cp = g.c_f32 + row * g.ldc + col0;
+    for (int q = 0; q < 32; ++q)
+      if (col0 + q < g.N) cp[q] = acc[q];
+  } else {
+    uint16_t *cp = g.c + row * g.ldc + col0;
+    if (full && (g.ldc % 8 == 0)) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w;
+        w.x = pack_bf16x2(acc[q * 8 + 0], acc[q * 8 + 1]);
+        w.y = pack_bf16x2(acc[q * 8 + 2], acc[q * 8 + 3]);
+        w.z = pack_bf16x2(acc[q * 8 + 4], acc[q * 8 + 5]);
+        w.w = pack_bf16x2(acc[q * 8 + 6], acc[q * 8 + 7]);
+        reinterpret_cast<uint4 *>(cp)[q] = w;
+      }
+    } else {
+      for (int q = 0; q < 32; ++q)
+        if (col0 + q < g.N) cp[q] = f32_to_bf16_bits(acc[q]);
+    }
+  }
+}
 
 template <int BN, bool B_KMAJOR>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __grid_constant__ GemmArgs g) {
@@ -65,6 +113,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
   const int lane = threadIdx.x & 31;
   const int num_kb = int(ceil_div(g.K, kGemmBK));
   const int num_tiles = g.tiles_m * g.tiles_n;
+  const int num_items = num_tiles * g.splits;   // work item u: tile u / splits, K split u % splits
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -90,10 +139,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
   sm100::tc_fence_after();
   const uint32_t tmem_base = *tmem_base_slot;
 
-  // Tile order: M-major within groups of 8 N-tiles... (n outer, m inner keeps a B panel hot in L2).
+  // Tile order: m inner, n outer (neighbouring CTAs share a B panel in L2).
   auto tile_coords = [&](int t, int &tm, int &tn) {
     tm = t % g.tiles_m;
     tn = t / g.tiles_m;
+  };
+  auto kb_range = [&](int u, int &kb0, int &kb1) {
+    const int sp = u % g.splits;
+    kb0 = sp * g.kb_per_split;
+    kb1 = kb0 + g.kb_per_split < num_kb ? kb0 + g.kb_per_split : num_kb;
   };
 
   if (warp == 0) {
@@ -101,12 +155,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
       int stage = 0;
       uint32_t phase = 0;
       uint32_t pending = 0;  // bit s: stage s holds a load issued with parity bit (s + 16)
-      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
-        int tm, tn;
-        tile_coords(t, tm, tn);
+      for (int u = blockIdx.x; u < num_items && !*abort_flag; u += gridDim.x) {
+        int tm, tn, kb0, kb1;
+        tile_coords(u / g.splits, tm, tn);
+        kb_range(u, kb0, kb1);
         const int m0 = int(g.m_begin) + tm * kGemmBM;
         const int n0 = tn * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!sm100::mbar_wait(&empty_bar[stage], phase ^ 1)) { *abort_flag = 1; break; }
           sm100::mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
           pending = (pending | (1u << stage)) & ~(1u << (stage + 16));
@@ -135,14 +190,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
-      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++it) {
+      for (int u = blockIdx.x; u < num_items && !*abort_flag; u += gridDim.x, ++it) {
         const int buf = it & 1;
         const uint32_t use = uint32_t(it >> 1) & 1u;
         if (!sm100::mbar_wait(&tempty_bar[buf], use ^ 1)) { *abort_flag = 1; break; }
         sm100::tc_fence_after();
         const uint32_t d_tmem = tmem_base + uint32_t(buf * BN);
         bool ok = true;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        int kb0, kb1;
+        kb_range(u, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!sm100::mbar_wait(&full_bar[stage], phase)) { ok = false; break; }
           sm100::tc_fence_after();
           const uint32_t a_addr = sm100::smem_u32(sA + stage * Cfg::A_BYTES);
@@ -153,7 +210,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
             uint64_t bdesc;
             if constexpr (B_KMAJOR) bdesc = sm100::sw128_desc(b_addr + k * 32, 16, 1024);
             else bdesc = sm100::sw128_desc(b_addr + k * 16 * 128, kGemmBK * 128, 1024);
-            sm100::mma_bf16_ss(d_tmem, adesc, bdesc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            sm100::mma_bf16_ss(d_tmem, adesc, bdesc, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           sm100::mma_commit(&empty_bar[stage]);  // frees the smem stage once these MMAs have read it
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -169,17 +226,67 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
     // Epilogue warps 2..5: TMEM lane quarter = warp % 4.
     const int quarter = warp & 3;
     const int row_in_tile = quarter * 32 + lane;
+    __shared__ int last_split;
     int it = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+    for (int u = blockIdx.x; u < num_items; u += gridDim.x, ++it) {
       const int buf = it & 1;
       const uint32_t use = uint32_t(it >> 1) & 1u;
       if (*abort_flag || !sm100::mbar_wait(&tfull_bar[buf], use)) { *abort_flag = 1; break; }
       sm100::tc_fence_after();
+      const int t = u / g.splits;
       int tm, tn;
       tile_coords(t, tm, tn);
       const int64_t row = g.m_begin + int64_t(tm) * kGemmBM + row_in_tile;
       const int64_t n0 = int64_t(tn) * BN;
       const bool row_ok = row < g.m_end;
+      if (g.splits > 1) {
+        // Split-K: park this split's fp32 accumulator in the workspace; the split that arrives last sums
+        // every split's partial in split order (deterministic) and runs the real epilogue.
+        float *mine = g.partials + (size_t(t) * g.splits + (u % g.splits)) * (kGemmBM * BN) + size_t(row_in_tile) * BN;
+#pragma unroll 1
+        for (int j = 0; j < BN / 32; ++j) {
+          uint32_t v[32];
+          sm100::tmem_ld32(tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(buf * BN + j * 32), v);
+          sm100::tmem_wait_ld();
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            __stcg(reinterpret_cast<float4 *>(mine + j * 32) + q,
+                   make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]), __uint_as_float(v[4 * q + 2]),
+                               __uint_as_float(v[4 * q + 3])));
+        }
+        sm100::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(&tempty_bar[buf]);   // the accumulator is free for the next item
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (threadIdx.x == 64) last_split = atomicAdd(&g.counters[t], 1) == g.splits - 1;
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (!last_split) continue;
+        __threadfence();
+        if (!row_ok) continue;
+        const float *base = g.partials + size_t(t) * g.splits * (kGemmBM * BN) + size_t(row_in_tile) * BN;
+#pragma unroll 1
+        for (int j = 0; j < BN / 32; ++j) {
+          const int64_t col0 = n0 + j * 32;
+          if (col0 >= g.N) continue;
+          float acc[32];
+#pragma unroll
+          for (int q = 0; q < 32; ++q) acc[q] = 0.f;
+          for (int sp = 0; sp < g.splits; ++sp) {
+            const float4 *src = reinterpret_cast<const float4 *>(base + size_t(sp) * (kGemmBM * BN) + j * 32);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float4 w = __ldcg(src + q);
+              acc[4 * q] = __fadd_rn(acc[4 * q], w.x);
+              acc[4 * q + 1] = __fadd_rn(acc[4 * q + 1], w.y);
+              acc[4 * q + 2] = __fadd_rn(acc[4 * q + 2], w.z);
+              acc[4 * q + 3] = __fadd_rn(acc[4 * q + 3], w.w);
+            }
+          }
+          gemm_store_row32(g, row, col0, acc);
+        }
+        continue;
+      }
 #pragma unroll 1
       for (int j = 0; j < BN / 32; ++j) {
         uint32_t v[32];
@@ -190,46 +297,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
         float acc[32];
 #pragma unroll
         for (int q = 0; q < 32; ++q) acc[q] = __uint_as_float(v[q]);
-        const bool full = col0 + 32 <= g.N;
-        if (g.r != nullptr) {
-          const uint16_t *rp = g.r + row * g.ldr + col0;
-          if (full && (g.ldr % 8 == 0)) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const uint4 w = __ldg(reinterpret_cast<const uint4 *>(rp) + q);
-              const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                acc[q * 8 + 2 * e] = __fadd_rn(acc[q * 8 + 2 * e], lo_bf16(ws[e]));
-                acc[q * 8 + 2 * e + 1] = __fadd_rn(acc[q * 8 + 2 * e + 1], hi_bf16(ws[e]));
-              }
-            }
-          } else {
-            for (int q = 0; q < 32; ++q)
-              if (col0 + q < g.N) acc[q] = __fadd_rn(acc[q], bf16_bits_to_f32(rp[q]));
-          }
-        }
-        if (g.c_f32 != nullptr) {
-          float *cp = g.c_f32 + row * g.ldc + col0;
-          for (int q = 0; q < 32; ++q)
-            if (col0 + q < g.N) cp[q] = acc[q];
-        } else {
-          uint16_t *cp = g.c + row * g.ldc + col0;
-          if (full && (g.ldc % 8 == 0)) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 w;
-              w.x = pack_bf16x2(acc[q * 8 + 0], acc[q * 8 + 1]);
-              w.y = pack_bf16x2(acc[q * 8 + 2], acc[q * 8 + 3]);
-              w.z = pack_bf16x2(acc[q * 8 + 4], acc[q * 8 + 5]);
-              w.w = pack_bf16x2(acc[q * 8 + 6], acc[q * 8 + 7]);
-              reinterpret_cast<uint4 *>(cp)[q] = w;
-            }
-          } else {
-            for (int q = 0; q < 32; ++q)
-              if (col0 + q < g.N) cp[q] = f32_to_bf16_bits(acc[q]);
-          }
-        }
+        gemm_store_row32(g, row, col0, acc);
       }
       sm100::tc_fence_before();
       __syncwarp();
@@ -283,18 +351,53 @@ static int make_tmap_2d(CUtensorMap *m, const void *base, uint64_t cols, uint64_
 template <int BN, bool B_KMAJOR>
 static int run_gemm(GemmArgs &g, int64_t m_rows, const LaunchCtx &c) {
   using Cfg = GemmCfg<BN>;
-  g.tiles_m = int(ceil_div(m_rows, kGemmBM));
-  g.tiles_n = int(ceil_div(g.N, BN));
-  const int tiles = g.tiles_m * g.tiles_n;
-  const int grid = tiles < c.sm_count ? tiles : c.sm_count;
+  const int items = g.tiles_m * g.tiles_n * g.splits;
+  const int grid = items < c.sm_count ? items : c.sm_count;
   auto kern = gemm_tcgen05_kernel<BN, B_KMAJOR>;
   PTSIM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
+  if (g.splits > 1) PTSIM_CUDA(cudaMemsetAsync(g.counters, 0, size_t(g.tiles_m) * g.tiles_n * sizeof(int), c.stream));
   kern<<<grid, kGemmThreads, Cfg::SMEM_BYTES, c.stream>>>(g);
   PTSIM_CUDA(cudaGetLastError());
   return PTSIM_OK;
 }
 
-int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c) {
+// The tile plan of a GEMM launch over `m_rows` rows on `sm_count` SMs: the N tile and the K splits.  A
+// launch with fewer output tiles than SMs cuts K so every SM gets a work item (split-K), when the
+// workspace can hold the partials.
+struct GemmPlan {
+  int bn, splits, kb_per_split;
+  int64_t tiles_m, tiles_n, workspace;
+};
+
+static GemmPlan plan_gemm(int64_t m_rows, int64_t N, int64_t K, int sm_count) {
+  GemmPlan pl;
+  pl.bn = N >= 256 ? 256 : (N > 64 ? 128 : 64);
+  pl.tiles_m = ceil_div(m_rows, kGemmBM);
+  pl.tiles_n = ceil_div(N, pl.bn);
+  const int64_t num_kb = ceil_div(K, kGemmBK);
+  const int64_t tiles = pl.tiles_m * pl.tiles_n;
+  int64_t splits = tiles < sm_count ? sm_count / tiles : 1;
+  if (splits > num_kb / 4) splits = num_kb / 4;     // at least four K blocks per split
+  if (splits > 16) splits = 16;
+  if (splits < 2) splits = 1;
+  pl.kb_per_split = int(ceil_div(num_kb, splits));
+  pl.splits = int(ceil_div(num_kb, pl.kb_per_split));
+  pl.workspace = pl.splits > 1 ? 1024 + tiles * pl.splits * kGemmBM * pl.bn * int64_t(sizeof(float)) : 0;
+  if (pl.splits == 1 && tiles < sm_count / 2 && N > 64) {
+    // No split possible (short K): narrower N tiles give more SMs work instead.
+    pl.bn = N > 128 && pl.tiles_m * ceil_div(N, 128) >= sm_count / 2 ? 128 : 64;
+    pl.tiles_n = ceil_div(N, pl.bn);
+  }
+  return pl;
+}
+
+int64_t gemm_workspace(const ptsim_desc &d, int sm_count) {
+  const ptsim_gemm_params &p = d.p.gemm;
+  return plan_gemm(p.M, p.N, p.K, sm_count).workspace;
+}
+
+int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, void *ws, size_t ws_bytes,
+                const LaunchCtx &c) {
   const ptsim_gemm_params &p = d.p.gemm;
   if (d.arg_dtype[p.a_arg] != PTSIM_DT_BF16 || d.arg_dtype[p.b_arg] != PTSIM_DT_BF16)
     return fail(PTSIM_E_UNSUPPORTED, "GEMM operands must be bf16 (the MXU refuses mixed formats)");
@@ -317,14 +420,26 @@ int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, 
   if (cdt == PTSIM_DT_F32) g.c_f32 = reinterpret_cast<float *>(ptrs[p.c_arg]);
   else g.c = reinterpret_cast<uint16_t *>(ptrs[p.c_arg]);
   g.r = p.r_arg >= 0 ? reinterpret_cast<const uint16_t *>(ptrs[p.r_arg]) : nullptr;
-  // Choose the N tile: the widest one that still gives every SM work.
   const int64_t m_rows = m_end - m_begin;
-  const int64_t tm = ceil_div(m_rows, kGemmBM);
-  int bn = 256;
-  if (tm * ceil_div(p.N, 256) < c.sm_count && p.N > 128) bn = 128;
-  if (tm * ceil_div(p.N, 128) < c.sm_count && p.N > 64) bn = 64;
-  if (p.N <= 128 && bn > 128) bn = 128;
-  if (p.N <= 64) bn = 64;
+  GemmPlan pl = plan_gemm(m_rows, p.N, p.K, c.sm_count);
+  if (pl.splits > 1 && (ws == nullptr || int64_t(ws_bytes) < pl.workspace)) {
+    // No room for the partials: one work item per tile, narrower tiles for parallelism.
+    pl.splits = 1;
+    pl.kb_per_split = int(ceil_div(p.K, kGemmBK));
+    pl.bn = p.N > 128 && pl.tiles_m * ceil_div(p.N, 128) >= c.sm_count / 2 ? 128 : (p.N > 64 ? 64 : 64);
+    if (pl.tiles_m * ceil_div(p.N, 256) >= c.sm_count) pl.bn = 256;
+    pl.tiles_n = ceil_div(p.N, pl.bn);
+  }
+  g.tiles_m = int(pl.tiles_m);
+  g.tiles_n = int(pl.tiles_n);
+  g.splits = pl.splits;
+  g.kb_per_split = pl.kb_per_split;
+  if (pl.splits > 1) {
+    g.counters = reinterpret_cast<int *>(ws);
+    g.partials = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(ws) + 1024);
+    if (pl.tiles_m * pl.tiles_n * sizeof(int) > 1024) return fail(PTSIM_E_RESOURCE, "split-K over too many tiles");
+  }
+  const int bn = pl.bn;
   int rc = make_tmap_2d(&g.tmap_a, ptrs[p.a_arg], uint64_t(p.K), uint64_t(p.M), uint64_t(p.lda), kGemmBK, kGemmBM);
   if (rc) return rc;
   if (p.b_kmajor) {

@@ -248,26 +248,27 @@ __global__ void __launch_bounds__(128) row_stream_kernel(const __grid_constant__
 
 // ---------------------------------------------------------------------------------------------------
 // Warp-per-row streaming path (cols a multiple of 256, up to 16384): one CTA per SM with a producer warp
-// and 31 consumer warps.  The producer keeps a ring of up to 31 whole rows in shared memory filled by
-// bulk async copies (full/empty mbarrier per slot); each consumer warp takes rows k = w, w + 16, ... and
-// works on its slot alone -- warp shuffles only, no block barriers -- in three passes over shared memory
-// (softmax: max on packed bf16 pairs, sum of exp, exp / sum; RMSNorm: sum of squares, scale) with paired
-// fp32 arithmetic (FADD2/FMUL2/FFMA2), then releases the slot.  Per SM ~24 rows are in flight, which
-// covers HBM latency; each element is read from HBM once and written once.
+// and NW consumer warps.  Consumer warp c owns `depth` slots of a shared-memory ring (slots c*depth ..
+// c*depth + depth - 1) and takes rows k = c, c + NW, ...; its i-th row lands in its slot i % depth, so a
+// slot is only ever refilled for the warp that owns it, in that warp's order, and no waiter can run more
+// than one mbarrier phase ahead of the slot (parity waits stay exact).  The producer keeps every slot in
+// flight with bulk async copies; a consumer works on its slot alone -- warp shuffles only, no block
+// barriers -- in three passes over shared memory (softmax: max on packed bf16 pairs, sum of exp,
+// exp / sum; RMSNorm: sum of squares, scale) with paired fp32 arithmetic, then releases the slot.
 // ---------------------------------------------------------------------------------------------------
-constexpr int kRowConsumers = 31;
-constexpr int kRowWarpThreads = 32 * (kRowConsumers + 1);
+constexpr int kRowMaxSlots = 64;
 
 __device__ __forceinline__ float2 unpack_bf16x2(uint32_t w) { return make_float2(lo_bf16(w), hi_bf16(w)); }
 
 template <int KIND>
-__global__ void __launch_bounds__(kRowWarpThreads, 1) row_warp_kernel(const __grid_constant__ RowLaunch L, int slots) {
+__global__ void __launch_bounds__(1024, 1) row_warp_kernel(const __grid_constant__ RowLaunch L, int nw, int depth) {
   extern __shared__ __align__(128) uint8_t dyn[];
-  __shared__ uint64_t full[32], empty[32], wbar;
+  __shared__ uint64_t full[kRowMaxSlots], empty[kRowMaxSlots], wbar;
   __shared__ int abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t row_bytes = uint32_t(L.cols) * 2u;
   const int chunks = int(L.cols / 8);
+  const int slots = nw * depth;
   uint8_t *wrow = dyn;                                        // RMSNorm weight row
   uint8_t *ring = dyn + (KIND == kRmsNorm ? row_bytes : 0);
   const int64_t nrows = L.rows_end - L.rows_begin;
@@ -289,30 +290,36 @@ __global__ void __launch_bounds__(kRowWarpThreads, 1) row_warp_kernel(const __gr
         sm100::mbar_arrive_expect_tx(&wbar, row_bytes);
         bulk_load(wrow, L.weight, row_bytes, &wbar);
       }
-      int64_t k = 0;
-      for (; k < mine && !abort_flag; ++k) {
-        const int s = int(k % slots);
-        if (k >= slots && !sm100::mbar_wait(&empty[s], uint32_t(k / slots - 1) & 1u)) { abort_flag = 1; break; }
+      uint64_t issued = 0, parity = 0;   // bit s: slot s has a copy in flight / the parity it completes
+      for (int64_t k = 0; k < mine && !abort_flag; ++k) {
+        const int c = int(k % nw);
+        const int64_t i = k / nw;
+        const int s = c * depth + int(i % depth);
+        if (i >= depth && !sm100::mbar_wait(&empty[s], uint32_t(i / depth - 1) & 1u)) { abort_flag = 1; break; }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         sm100::mbar_arrive_expect_tx(&full[s], row_bytes);
         bulk_load(ring + size_t(s) * row_bytes, reinterpret_cast<const uint16_t *>(L.in) + row_of(k) * L.in_stride,
                   row_bytes, &full[s]);
+        issued |= 1ull << s;
+        parity = (parity & ~(1ull << s)) | (uint64_t(uint32_t(i / depth) & 1u) << s);
       }
       // Bulk copies still in flight land before the CTA exits (only an aborted run can leave some).
       if (abort_flag)
-        for (int64_t j = (k > slots ? k - slots : 0); j < k; ++j)
-          sm100::mbar_wait(&full[int(j % slots)], uint32_t(j / slots) & 1u);
+        for (int s = 0; s < slots; ++s)
+          if (issued & (1ull << s)) sm100::mbar_wait(&full[s], uint32_t(parity >> s) & 1u);
       if constexpr (KIND == kRmsNorm) sm100::mbar_wait(&wbar, 0);
     }
     return;
   }
   const int c = warp - 1;
+  if (c >= nw) return;
   if constexpr (KIND == kRmsNorm) {
     if (!sm100::mbar_wait(&wbar, 0)) abort_flag = 1;
   }
-  for (int64_t k = c; k < mine && !abort_flag; k += kRowConsumers) {
-    const int s = int(k % slots);
-    if (!sm100::mbar_wait(&full[s], uint32_t(k / slots) & 1u)) { abort_flag = 1; break; }
+  int64_t i = 0;
+  for (int64_t k = c; k < mine && !abort_flag; k += nw, ++i) {
+    const int s = c * depth + int(i % depth);
+    if (!sm100::mbar_wait(&full[s], uint32_t(i / depth) & 1u)) { abort_flag = 1; break; }
     const uint4 *src = reinterpret_cast<const uint4 *>(ring + size_t(s) * row_bytes);
     uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(L.out) + row_of(k) * L.out_stride);
     if constexpr (KIND == kSoftmax) {
@@ -393,15 +400,18 @@ static int launch_row_warp(const RowLaunch &L, const LaunchCtx &c) {
   const int64_t row_bytes = L.cols * 2;
   const int64_t budget = 200 * 1024 - (KIND == kRmsNorm ? row_bytes : 0);
   int slots = int(budget / row_bytes);
-  if (slots > 31) slots = 31;
+  if (slots > kRowMaxSlots) slots = kRowMaxSlots;
   if (slots < 2) return fail(PTSIM_E_RESOURCE, "row of %lld bf16 does not fit the shared-memory ring", (long long)L.cols);
-  const int smem = int(slots * row_bytes + (KIND == kRmsNorm ? row_bytes : 0));
+  // Consumer warps and the slots each owns: as many warps as slots (up to 31), two slots each beyond that.
+  const int depth = slots > 31 ? 2 : 1;
+  const int nw = slots / depth > 31 ? 31 : slots / depth;
+  const int smem = int(int64_t(nw) * depth * row_bytes + (KIND == kRmsNorm ? row_bytes : 0));
   auto kern = row_warp_kernel<KIND>;
   PTSIM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   const int64_t rows = L.rows_end - L.rows_begin;
   int64_t grid = c.sm_count;
   if (grid > rows) grid = rows;
-  kern<<<unsigned(grid), kRowWarpThreads, smem, c.stream>>>(L, slots);
+  kern<<<unsigned(grid), 32 * (nw + 1), smem, c.stream>>>(L, nw, depth);
   PTSIM_CUDA(cudaGetLastError());
   return PTSIM_OK;
 }

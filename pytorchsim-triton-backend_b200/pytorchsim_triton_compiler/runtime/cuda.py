@@ -63,12 +63,20 @@ def split(total, n):
     return [(edges[w], edges[w + 1]) for w in range(n) if edges[w] < edges[w + 1]]
 
 
-def workspace_for(desc, device):
-    """Scratch a launch of `desc` needs, as a device tensor (or None)."""
-    if desc.workspace_bytes <= 0:
+_workspaces = {}
+
+
+def workspace_for(blob, device):
+    """Scratch a launch of `blob` wants on `device` (split-K partials, reduction partials), as a device
+    tensor kept per device and grown on demand (or None)."""
+    n = native.workspace_size(blob, device.index if device.index is not None else 0)
+    if n <= 0:
         return None
     torch = _torch()
-    return torch.empty(int(desc.workspace_bytes), dtype=torch.uint8, device=device)
+    ws = _workspaces.get(device)
+    if ws is None or ws.numel() < n:
+        ws = _workspaces[device] = torch.empty(int(n), dtype=torch.uint8, device=device)
+    return ws
 
 
 def launch_tensors(blob, tensors, lo=0, hi=None, stream=None, sync=True):
@@ -94,9 +102,9 @@ def launch_tensors(blob, tensors, lo=0, hi=None, stream=None, sync=True):
     with torch.cuda.device(dev):
         native.init(dev.index)
         s = stream if stream is not None else torch.cuda.current_stream(dev)
-        ws = workspace_for(desc, dev)
+        ws = workspace_for(blob, dev)
         native.launch(blob, [t.data_ptr() for t in tensors], lo, hi,
-                      ws.data_ptr() if ws is not None else 0, desc.workspace_bytes, s.cuda_stream)
+                      ws.data_ptr() if ws is not None else 0, ws.numel() if ws is not None else 0, s.cuda_stream)
         if sync:
             native.sync(s.cuda_stream)
     return tensors

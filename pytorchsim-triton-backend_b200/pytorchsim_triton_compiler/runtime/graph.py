@@ -44,10 +44,11 @@ class Graph:
             t = self.buffers[b]
             if t.numel() != d.arg_numel[i]:
                 raise ValueError(f"{name}: buffer {b} holds {t.numel()} elements, argument {i} wants {d.arg_numel[i]}")
-        ws = None
-        if d.workspace_bytes:
-            ws = self.torch.empty(int(d.workspace_bytes), dtype=self.torch.uint8, device=self.device)
         native.check(blob)
+        ws = None
+        n = native.workspace_size(blob, self.device.index or 0)
+        if n > 0:
+            ws = self.torch.empty(int(n), dtype=self.torch.uint8, device=self.device)
         self.steps.append((name, bytes(blob), list(bufs), ws, d.units))
 
     def launch_count(self):

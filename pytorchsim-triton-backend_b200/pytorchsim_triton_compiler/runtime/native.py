@@ -20,6 +20,7 @@ SYMBOLS = {
     "ptsim_units": (C.c_int64, [C.c_void_p, C.c_size_t]),
     "ptsim_launch": (C.c_int, [C.c_void_p, C.c_size_t, C.POINTER(C.c_void_p), C.c_int, C.c_int64, C.c_int64,
                                C.c_void_p, C.c_size_t, C.c_void_p]),
+    "ptsim_workspace_size": (C.c_int64, [C.c_void_p, C.c_size_t, C.c_int]),
     "ptsim_sync": (C.c_int, [C.c_void_p, C.POINTER(C.c_int32)]),
     "ptsim_last_error": (C.c_int, [C.c_char_p, C.c_int]),
 }
@@ -100,6 +101,14 @@ def check(blob):
 def units(blob):
     buf = C.create_string_buffer(bytes(blob), len(blob))
     n = load().ptsim_units(buf, len(blob))
+    if n < 0:
+        raise ExecutorError(D.E_DESC, last_error())
+    return n
+
+
+def workspace_size(blob, device=-1):
+    """Device scratch bytes a launch of `blob` wants on `device` (split-K GEMM partials, reduction partials)."""
+    n = load().ptsim_workspace_size(_desc_buffer(blob), len(blob), int(device))
     if n < 0:
         raise ExecutorError(D.E_DESC, last_error())
     return n
