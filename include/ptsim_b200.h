@@ -198,9 +198,8 @@ int ptsim_launch(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int
                  int64_t lo, int64_t hi, void *workspace, size_t workspace_bytes, void *stream);
 
 /* Bytes of device scratch a launch of `desc` wants on `device` (-1 on a bad descriptor): the REDUCE_ALL
- * partials, or the split-K partial tiles of a GEMM whose output has fewer tiles than the device has SMs.
- * A GEMM launched with less (or none) runs without split-K: same result, fewer SMs busy.  No reference
- * counterpart (Spike needed no device scratch). */
+ * pass-1 partials, else desc->workspace_bytes.  No reference counterpart (Spike needed no device
+ * scratch). */
 int64_t ptsim_workspace_size(const void *desc, size_t desc_bytes, int device);
 
 /* Synchronise `stream` and return (and clear) the device status word of the current device:

@@ -13,9 +13,14 @@
 //               tile i drains);
 //   warps 2..5  epilogue: tcgen05.ld of the accumulator (one TMEM lane = one output row per thread),
 //               optional residual add, cast, 16-byte global stores.
+// Split-K (an output with fewer tiles than SMs): the K range of a tile is cut over the CTAs of one
+// thread-block cluster; each CTA parks its fp32 accumulator in its own shared memory, and after a
+// cluster barrier CTA q sums slice q of the tile's columns over every CTA's copy (distributed shared
+// memory reads, in rank order: deterministic) and runs the epilogue on it.  No global scratch.
 // Every wait is bounded (sm100::mbar_wait); on a timeout each role stops issuing, the CTA meets at the
 // final barrier, and TMEM is released before exit.
 #pragma once
+#include <atomic>
 #include <cudaTypedefs.h>
 #include "sm100.cuh"
 
@@ -43,9 +48,7 @@ struct GemmArgs {
   float *c_f32;         // fp32 output instead of bf16 when non-null
   int64_t m_begin, m_end, N, K, ldc, ldr;
   int32_t tiles_m, tiles_n;
-  int32_t splits, kb_per_split;  // split-K: each output tile's K range cut into `splits` work items
-  int *counters;                 // per tile: how many splits have written their partial (zeroed per launch)
-  float *partials;               // [tile][split][BM][BN] fp32 partial accumulators
+  int32_t splits, kb_per_split;  // split-K: each output tile's K range cut over the `splits` CTAs of a cluster
 };
 
 // The epilogue of 32 output columns of one row: + residual (bf16), then the store rounded to the output
@@ -226,7 +229,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
     // Epilogue warps 2..5: TMEM lane quarter = warp % 4.
     const int quarter = warp & 3;
     const int row_in_tile = quarter * 32 + lane;
-    __shared__ int last_split;
     int it = 0;
     for (int u = blockIdx.x; u < num_items; u += gridDim.x, ++it) {
       const int buf = it & 1;
@@ -240,9 +242,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
       const int64_t n0 = int64_t(tn) * BN;
       const bool row_ok = row < g.m_end;
       if (g.splits > 1) {
-        // Split-K: park this split's fp32 accumulator in the workspace; the split that arrives last sums
-        // every split's partial in split order (deterministic) and runs the real epilogue.
-        float *mine = g.partials + (size_t(t) * g.splits + (u % g.splits)) * (kGemmBM * BN) + size_t(row_in_tile) * BN;
+        // Split-K: park this CTA's fp32 accumulator in its own shared memory (the operand ring is idle:
+        // the accumulator is complete only after every MMA has read its stages, and the producer loads
+        // nothing more), rows of BN floats with 16-byte chunk c of row r at chunk position c ^ (r % 8),
+        // so both the row-per-thread writes here and the reads of the exchange are conflict-free.
+        float *park = reinterpret_cast<float *>(smem) + size_t(row_in_tile) * BN;
 #pragma unroll 1
         for (int j = 0; j < BN / 32; ++j) {
           uint32_t v[32];
@@ -250,41 +254,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
           sm100::tmem_wait_ld();
 #pragma unroll
           for (int q = 0; q < 8; ++q)
-            __stcg(reinterpret_cast<float4 *>(mine + j * 32) + q,
-                   make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]), __uint_as_float(v[4 * q + 2]),
-                               __uint_as_float(v[4 * q + 3])));
+            reinterpret_cast<float4 *>(park)[(j * 8 + q) ^ (row_in_tile & 7)] =
+                make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]), __uint_as_float(v[4 * q + 2]),
+                            __uint_as_float(v[4 * q + 3]));
         }
         sm100::tc_fence_before();
         __syncwarp();
-        if (lane == 0) sm100::mbar_arrive(&tempty_bar[buf]);   // the accumulator is free for the next item
-        __threadfence();
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (threadIdx.x == 64) last_split = atomicAdd(&g.counters[t], 1) == g.splits - 1;
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (!last_split) continue;
-        __threadfence();
-        if (!row_ok) continue;
-        const float *base = g.partials + size_t(t) * g.splits * (kGemmBM * BN) + size_t(row_in_tile) * BN;
-#pragma unroll 1
-        for (int j = 0; j < BN / 32; ++j) {
-          const int64_t col0 = n0 + j * 32;
-          if (col0 >= g.N) continue;
-          float acc[32];
-#pragma unroll
-          for (int q = 0; q < 32; ++q) acc[q] = 0.f;
-          for (int sp = 0; sp < g.splits; ++sp) {
-            const float4 *src = reinterpret_cast<const float4 *>(base + size_t(sp) * (kGemmBM * BN) + j * 32);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const float4 w = __ldcg(src + q);
-              acc[4 * q] = __fadd_rn(acc[4 * q], w.x);
-              acc[4 * q + 1] = __fadd_rn(acc[4 * q + 1], w.y);
-              acc[4 * q + 2] = __fadd_rn(acc[4 * q + 2], w.z);
-              acc[4 * q + 3] = __fadd_rn(acc[4 * q + 3], w.w);
-            }
-          }
-          gemm_store_row32(g, row, col0, acc);
-        }
+        if (lane == 0) sm100::mbar_arrive(&tempty_bar[buf]);
         continue;
       }
 #pragma unroll 1
@@ -303,6 +279,48 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(&tempty_bar[buf]);
     }
+  }
+
+  if (g.splits > 1) {
+    // Split-K exchange.  Every thread of every CTA in the cluster takes both cluster barriers, on every
+    // path (an aborted CTA too), so none can wait on a peer that never arrives.
+    __syncwarp();
+    sm100::cluster_sync();   // every CTA's accumulator is parked and visible
+    if (warp >= 2 && !*abort_flag) {
+      const int row_in_tile = (warp & 3) * 32 + lane;
+      const int t = blockIdx.x / g.splits;
+      int tm, tn;
+      tile_coords(t, tm, tn);
+      const int64_t row = g.m_begin + int64_t(tm) * kGemmBM + row_in_tile;
+      const int width = BN / g.splits;                            // columns this CTA finishes
+      const int c_begin = int(sm100::cluster_ctarank()) * width;
+      const uint32_t park = sm100::smem_u32(smem) + uint32_t(row_in_tile) * BN * 4;
+      if (row < g.m_end) {
+#pragma unroll 1
+        for (int c0 = c_begin; c0 < c_begin + width; c0 += 32) {
+          const int64_t col0 = int64_t(tn) * BN + c0;
+          if (col0 >= g.N) break;
+          float acc[32];
+#pragma unroll
+          for (int q = 0; q < 32; ++q) acc[q] = 0.f;
+#pragma unroll 1
+          for (int r = 0; r < g.splits; ++r) {
+            const uint32_t peer = sm100::mapa_shared(park, uint32_t(r));
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float4 w = sm100::ld_dsmem_f4(peer + uint32_t(((c0 / 4 + q) ^ (row_in_tile & 7)) * 16));
+              acc[4 * q] = __fadd_rn(acc[4 * q], w.x);
+              acc[4 * q + 1] = __fadd_rn(acc[4 * q + 1], w.y);
+              acc[4 * q + 2] = __fadd_rn(acc[4 * q + 2], w.z);
+              acc[4 * q + 3] = __fadd_rn(acc[4 * q + 3], w.w);
+            }
+          }
+          gemm_store_row32(g, row, col0, acc);
+        }
+      }
+    }
+    __syncwarp();
+    sm100::cluster_sync();   // no CTA leaves while a peer still reads its shared memory
   }
 
   // Teardown: every role has stopped issuing; make sure no MMA still writes TMEM, then free it.
@@ -348,56 +366,98 @@ static int make_tmap_2d(CUtensorMap *m, const void *base, uint64_t cols, uint64_
   return PTSIM_OK;
 }
 
+// Clusters of `splits` CTAs of this kernel that one device runs at once (0 when it cannot), cached.
 template <int BN, bool B_KMAJOR>
-static int run_gemm(GemmArgs &g, int64_t m_rows, const LaunchCtx &c) {
+static int max_active_clusters(int splits, const LaunchCtx &c) {
   using Cfg = GemmCfg<BN>;
+  static std::atomic<int> cache[64][4];   // [device][log2(splits) - 1]; 0 = unknown, else count + 1
+  const int slot = splits == 2 ? 0 : splits == 4 ? 1 : 2;
+  std::atomic<int> *e = (c.device >= 0 && c.device < 64) ? &cache[c.device][slot] : nullptr;
+  if (e != nullptr && e->load() > 0) return e->load() - 1;
+  auto kern = gemm_tcgen05_kernel<BN, B_KMAJOR>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES) != cudaSuccess) return 0;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3(unsigned(splits * c.sm_count));
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(splits);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  if (e != nullptr) e->store(n + 1);
+  return n;
+}
+
+template <int BN, bool B_KMAJOR>
+static int run_gemm(GemmArgs &g, const LaunchCtx &c) {
+  using Cfg = GemmCfg<BN>;
+  static_assert(size_t(kGemmBM) * BN * sizeof(float) <= size_t(Cfg::STAGES) * Cfg::STAGE_BYTES,
+                "the split-K accumulator is parked in the operand ring");
   const int items = g.tiles_m * g.tiles_n * g.splits;
-  const int grid = items < c.sm_count ? items : c.sm_count;
   auto kern = gemm_tcgen05_kernel<BN, B_KMAJOR>;
   PTSIM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
-  if (g.splits > 1) PTSIM_CUDA(cudaMemsetAsync(g.counters, 0, size_t(g.tiles_m) * g.tiles_n * sizeof(int), c.stream));
-  kern<<<grid, kGemmThreads, Cfg::SMEM_BYTES, c.stream>>>(g);
+  if (g.splits == 1) {
+    const int grid = items < c.sm_count ? items : c.sm_count;
+    kern<<<grid, kGemmThreads, Cfg::SMEM_BYTES, c.stream>>>(g);
+  } else {
+    // One CTA per work item (items <= SMs), the splits of a tile forming one cluster.
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = dim3(unsigned(items));
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    cfg.stream = c.stream;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = unsigned(g.splits);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    PTSIM_CUDA(cudaLaunchKernelEx(&cfg, kern, g));
+  }
   PTSIM_CUDA(cudaGetLastError());
   return PTSIM_OK;
 }
 
-// The tile plan of a GEMM launch over `m_rows` rows on `sm_count` SMs: the N tile and the K splits.  A
-// launch with fewer output tiles than SMs cuts K so every SM gets a work item (split-K), when the
-// workspace can hold the partials.
+// The tile plan of a GEMM: the N tile, and the K splits when the output has fewer tiles than the device
+// has SMs (split-K over a cluster: a power of two up to 8, at most BN / 32 so every CTA finishes at
+// least 32 columns, at least four K blocks each, one CTA per SM).  The split count follows the whole
+// launch's M, never the unit range, so every range of a launch sums K in the same order.
 struct GemmPlan {
   int bn, splits, kb_per_split;
-  int64_t tiles_m, tiles_n, workspace;
+  int64_t tiles_m, tiles_n;
 };
 
-static GemmPlan plan_gemm(int64_t m_rows, int64_t N, int64_t K, int sm_count) {
+static GemmPlan plan_gemm(int64_t m_rows, int64_t m_total, int64_t N, int64_t K, int sm_count) {
   GemmPlan pl;
   pl.bn = N >= 256 ? 256 : (N > 64 ? 128 : 64);
   pl.tiles_m = ceil_div(m_rows, kGemmBM);
   pl.tiles_n = ceil_div(N, pl.bn);
   const int64_t num_kb = ceil_div(K, kGemmBK);
-  const int64_t tiles = pl.tiles_m * pl.tiles_n;
-  int64_t splits = tiles < sm_count ? sm_count / tiles : 1;
-  if (splits > num_kb / 4) splits = num_kb / 4;     // at least four K blocks per split
-  if (splits > 16) splits = 16;
-  if (splits < 2) splits = 1;
+  const int64_t whole_tiles = ceil_div(m_total, kGemmBM) * pl.tiles_n;
+  int splits = 1;
+  while (splits < 8 && splits * 2 <= pl.bn / 32 && whole_tiles * splits * 2 <= sm_count && num_kb / (splits * 2) >= 4)
+    splits *= 2;
+  if (pl.tiles_m * pl.tiles_n * splits > sm_count) splits = 1;   // a range wider than the whole? keep one wave
+  pl.splits = splits;
   pl.kb_per_split = int(ceil_div(num_kb, splits));
-  pl.splits = int(ceil_div(num_kb, pl.kb_per_split));
-  pl.workspace = pl.splits > 1 ? 1024 + tiles * pl.splits * kGemmBM * pl.bn * int64_t(sizeof(float)) : 0;
-  if (pl.splits == 1 && tiles < sm_count / 2 && N > 64) {
+  if (pl.splits == 1 && whole_tiles < sm_count / 2 && N > 64) {
     // No split possible (short K): narrower N tiles give more SMs work instead.
-    pl.bn = N > 128 && pl.tiles_m * ceil_div(N, 128) >= sm_count / 2 ? 128 : 64;
+    pl.bn = N > 128 && ceil_div(m_total, kGemmBM) * ceil_div(N, 128) >= sm_count / 2 ? 128 : 64;
     pl.tiles_n = ceil_div(N, pl.bn);
   }
   return pl;
 }
 
-int64_t gemm_workspace(const ptsim_desc &d, int sm_count) {
-  const ptsim_gemm_params &p = d.p.gemm;
-  return plan_gemm(p.M, p.N, p.K, sm_count).workspace;
-}
-
-int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, void *ws, size_t ws_bytes,
-                const LaunchCtx &c) {
+int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c) {
   const ptsim_gemm_params &p = d.p.gemm;
   if (d.arg_dtype[p.a_arg] != PTSIM_DT_BF16 || d.arg_dtype[p.b_arg] != PTSIM_DT_BF16)
     return fail(PTSIM_E_UNSUPPORTED, "GEMM operands must be bf16 (the MXU refuses mixed formats)");
@@ -420,25 +480,24 @@ int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, 
   if (cdt == PTSIM_DT_F32) g.c_f32 = reinterpret_cast<float *>(ptrs[p.c_arg]);
   else g.c = reinterpret_cast<uint16_t *>(ptrs[p.c_arg]);
   g.r = p.r_arg >= 0 ? reinterpret_cast<const uint16_t *>(ptrs[p.r_arg]) : nullptr;
-  const int64_t m_rows = m_end - m_begin;
-  GemmPlan pl = plan_gemm(m_rows, p.N, p.K, c.sm_count);
-  if (pl.splits > 1 && (ws == nullptr || int64_t(ws_bytes) < pl.workspace)) {
-    // No room for the partials: one work item per tile, narrower tiles for parallelism.
-    pl.splits = 1;
-    pl.kb_per_split = int(ceil_div(p.K, kGemmBK));
-    pl.bn = p.N > 128 && pl.tiles_m * ceil_div(p.N, 128) >= c.sm_count / 2 ? 128 : (p.N > 64 ? 64 : 64);
-    if (pl.tiles_m * ceil_div(p.N, 256) >= c.sm_count) pl.bn = 256;
-    pl.tiles_n = ceil_div(p.N, pl.bn);
+  GemmPlan pl = plan_gemm(m_end - m_begin, p.M, p.N, p.K, c.sm_count);
+  if (pl.splits > 1) {
+    // Fewer K splits when the device cannot run every tile's cluster at once (clusters need their CTAs
+    // on one GPU processing cluster).
+    const bool bk = p.b_kmajor != 0;
+    while (pl.splits > 1) {
+      const int fit = pl.bn == 256 ? (bk ? max_active_clusters<256, true>(pl.splits, c) : max_active_clusters<256, false>(pl.splits, c))
+                    : pl.bn == 128 ? (bk ? max_active_clusters<128, true>(pl.splits, c) : max_active_clusters<128, false>(pl.splits, c))
+                                   : (bk ? max_active_clusters<64, true>(pl.splits, c) : max_active_clusters<64, false>(pl.splits, c));
+      if (fit >= pl.tiles_m * pl.tiles_n) break;
+      pl.splits /= 2;
+    }
+    pl.kb_per_split = int(ceil_div(ceil_div(p.K, kGemmBK), pl.splits));
   }
   g.tiles_m = int(pl.tiles_m);
   g.tiles_n = int(pl.tiles_n);
   g.splits = pl.splits;
   g.kb_per_split = pl.kb_per_split;
-  if (pl.splits > 1) {
-    g.counters = reinterpret_cast<int *>(ws);
-    g.partials = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(ws) + 1024);
-    if (pl.tiles_m * pl.tiles_n * sizeof(int) > 1024) return fail(PTSIM_E_RESOURCE, "split-K over too many tiles");
-  }
   const int bn = pl.bn;
   int rc = make_tmap_2d(&g.tmap_a, ptrs[p.a_arg], uint64_t(p.K), uint64_t(p.M), uint64_t(p.lda), kGemmBK, kGemmBM);
   if (rc) return rc;
@@ -450,13 +509,13 @@ int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, 
   }
   if (rc) return rc;
   if (p.b_kmajor) {
-    if (bn == 256) return run_gemm<256, true>(g, m_rows, c);
-    if (bn == 128) return run_gemm<128, true>(g, m_rows, c);
-    return run_gemm<64, true>(g, m_rows, c);
+    if (bn == 256) return run_gemm<256, true>(g, c);
+    if (bn == 128) return run_gemm<128, true>(g, c);
+    return run_gemm<64, true>(g, c);
   }
-  if (bn == 256) return run_gemm<256, false>(g, m_rows, c);
-  if (bn == 128) return run_gemm<128, false>(g, m_rows, c);
-  return run_gemm<64, false>(g, m_rows, c);
+  if (bn == 256) return run_gemm<256, false>(g, c);
+  if (bn == 128) return run_gemm<128, false>(g, c);
+  return run_gemm<64, false>(g, c);
 }
 
 }  // namespace ptsim

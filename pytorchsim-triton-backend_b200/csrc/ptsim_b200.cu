@@ -227,7 +227,7 @@ int ptsim_launch(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int
     case PTSIM_KIND_ROW_SOFTMAX:
     case PTSIM_KIND_ROW_RMSNORM: return launch_rowops(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_QKNORM_ROPE: return launch_qkrope(d, dev_ptrs, lo, hi, c);
-    case PTSIM_KIND_GEMM: return launch_gemm(d, dev_ptrs, lo, hi, workspace, workspace_bytes, c);
+    case PTSIM_KIND_GEMM: return launch_gemm(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_ATTN_PREFILL: return launch_attention(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_REDUCE_ALL: return launch_reduce(d, dev_ptrs, lo, hi, workspace, workspace_bytes, c);
   }
@@ -241,11 +241,7 @@ int64_t ptsim_workspace_size(const void *desc, size_t desc_bytes, int device) {
   DeviceInfo info;
   if (device >= 0 && device_info(device, &info) == PTSIM_OK) sm_count = info.sm_count;
   int64_t need = d.workspace_bytes;
-  if (d.kind == PTSIM_KIND_GEMM) {
-    const int64_t g = gemm_workspace(d, sm_count);
-    need = g > need ? g : need;
-  }
-  if (d.kind == PTSIM_KIND_REDUCE_ALL) need = need > int64_t(1024 * sizeof(float)) ? need : int64_t(1024 * sizeof(float));
+  if (d.kind == PTSIM_KIND_REDUCE_ALL && need < reduce_workspace(sm_count)) need = reduce_workspace(sm_count);
   return need;
 }
 

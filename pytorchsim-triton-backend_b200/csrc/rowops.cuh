@@ -133,306 +133,142 @@ __global__ void __launch_bounds__(256) row_fast_kernel(const __grid_constant__ R
 }
 
 // ---------------------------------------------------------------------------------------------------
-// Streaming path for long rows (cols = 1024 * CH, CH <= 8): a persistent CTA of 128 threads owns rows
-// blockIdx.x, blockIdx.x + gridDim.x, ...; thread 0 keeps SLOTS whole rows in flight with bulk async
-// copies (cp.async.bulk, completion on an mbarrier per slot) into a shared-memory ring, so HBM sees
-// SLOTS x row bytes outstanding per CTA at all times; the 128 threads take a row out of its slot into
-// registers (CH 16-byte chunks each), release the slot for the row SLOTS ahead, reduce across the 4
-// warps, and write the row back with streaming 16-byte stores.
+// Row-per-CTA path (bf16 rows of cols = 8 * CH * TPR, TPR in 64..512): CTA b owns row rows_begin + b;
+// its TPR threads each load CH 16-byte chunks (chunk c * TPR + tid: every warp access is one contiguous
+// 512-byte run) into registers with one streaming load each, reduce across the CTA (warp shuffles, then
+// one shared-memory slot per warp), and store the row back with 16-byte streaming stores.  Launched with
+// one CTA per row and sized for full occupancy (2048 threads per SM, <= 32 registers each; 1024 threads
+// with 32 values a thread), so every SM keeps 64 KB of loads in flight and the scheduler backfills rows
+// as CTAs finish.  Arithmetic
+// runs on packed pairs (fp32 x2 FMA/ADD/MUL, bf16 x2 max); the softmax evaluates each exp once.
 // ---------------------------------------------------------------------------------------------------
-__device__ __forceinline__ void bulk_load(void *dst_smem, const void *src, uint32_t bytes, uint64_t *bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   sm100::smem_u32(dst_smem)),
-               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(sm100::smem_u32(bar))
-               : "memory");
-}
-
-template <int KIND, int CH>
-__global__ void __launch_bounds__(128) row_stream_kernel(const __grid_constant__ RowLaunch L, int slots) {
-  extern __shared__ __align__(128) uint8_t ring[];
-  __shared__ uint64_t full[16];
-  __shared__ float red_a[4], red_b[4];
-  __shared__ int abort_flag;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const uint32_t row_bytes = uint32_t(L.cols) * 2u;
-  const int64_t nrows = L.rows_end - L.rows_begin;
-  const int64_t mine = nrows > blockIdx.x ? (nrows - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  auto row_of = [&](int64_t k) { return L.rows_begin + int64_t(blockIdx.x) + k * int64_t(gridDim.x); };
-  if (tid == 0) {
-    for (int s = 0; s < slots; ++s) sm100::mbar_init(&full[s], 1);
-    abort_flag = 0;
-    sm100::fence_barrier_init();
-    for (int64_t k = 0; k < mine && k < slots; ++k) {
-      sm100::mbar_arrive_expect_tx(&full[k], row_bytes);
-      bulk_load(ring + size_t(k) * row_bytes, reinterpret_cast<const uint16_t *>(L.in) + row_of(k) * L.in_stride,
-                row_bytes, &full[k]);
-    }
-  }
-  __syncthreads();
-  uint4 wv[KIND == kRmsNorm ? CH : 1];
-  if constexpr (KIND == kRmsNorm) {
-#pragma unroll
-    for (int c = 0; c < CH; ++c) wv[c] = __ldg(reinterpret_cast<const uint4 *>(L.weight) + c * 128 + tid);
-  }
-  int64_t k = 0;
-  for (; k < mine; ++k) {
-    const int s = int(k % slots);
-    const uint32_t phase = uint32_t(k / slots) & 1u;
-    if (!sm100::mbar_wait(&full[s], phase)) abort_flag = 1;
-    float v[CH * 8];
-    const uint4 *src = reinterpret_cast<const uint4 *>(ring + size_t(s) * row_bytes);
-#pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      const uint4 raw = src[c * 128 + tid];
-      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) { v[c * 8 + 2 * j] = lo_bf16(w[j]); v[c * 8 + 2 * j + 1] = hi_bf16(w[j]); }
-    }
-    __syncthreads();  // every thread has its chunks out of slot s (and has seen any abort)
-    if (abort_flag) break;
-    if (tid == 0 && k + slots < mine) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      sm100::mbar_arrive_expect_tx(&full[s], row_bytes);
-      bulk_load(ring + size_t(s) * row_bytes,
-                reinterpret_cast<const uint16_t *>(L.in) + row_of(k + slots) * L.in_stride, row_bytes, &full[s]);
-    }
-    uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(L.out) + row_of(k) * L.out_stride);
-    if constexpr (KIND == kSoftmax) {
-      float m = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < CH * 8; ++i) m = nan_max(m, v[i]);
-      m = row_allreduce<128>(m, true, red_a);
-      const float kLog2e = 1.4426950408889634f;
-      float sum = 0.f;
-#pragma unroll
-      for (int i = 0; i < CH * 8; ++i) {
-        v[i] = ex2_fast(__fmul_rn(__fsub_rn(v[i], m), kLog2e));
-        sum = __fadd_rn(sum, v[i]);
-      }
-      sum = row_allreduce<128>(sum, false, red_b);
-      const float rcp = __frcp_rn(sum);
-#pragma unroll
-      for (int c = 0; c < CH; ++c) {
-        uint32_t w[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          w[j] = pack_bf16x2(div_by(v[c * 8 + 2 * j], sum, rcp), div_by(v[c * 8 + 2 * j + 1], sum, rcp));
-        __stcs(dst + c * 128 + tid, make_uint4(w[0], w[1], w[2], w[3]));
-      }
-    } else {
-      float ss = 0.f;
-#pragma unroll
-      for (int i = 0; i < CH * 8; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
-      ss = row_allreduce<128>(ss, false, red_a);
-      const float rs = rsqrtf(__fadd_rn(__fdiv_rn(ss, float(L.cols)), L.eps));
-#pragma unroll
-      for (int c = 0; c < CH; ++c) {
-        const uint32_t g[4] = {wv[c].x, wv[c].y, wv[c].z, wv[c].w};
-        uint32_t o[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          o[j] = pack_bf16x2(__fmul_rn(__fmul_rn(v[c * 8 + 2 * j], rs), lo_bf16(g[j])),
-                             __fmul_rn(__fmul_rn(v[c * 8 + 2 * j + 1], rs), hi_bf16(g[j])));
-        __stcs(dst + c * 128 + tid, make_uint4(o[0], o[1], o[2], o[3]));
-      }
-    }
-    // red_a / red_b are safe to reuse without another barrier: the next row writes them only after the
-    // slot-read barrier, which every thread reaches after its reads of this row's partials.
-  }
-  if (abort_flag && tid == 0) {
-    // Copies still in flight land before the CTA's shared memory is released.
-    for (int64_t j = k; j < mine && j < k + slots; ++j)
-      sm100::mbar_wait(&full[int(j % slots)], uint32_t(j / slots) & 1u);
-  }
-}
-
-// ---------------------------------------------------------------------------------------------------
-// Warp-per-row streaming path (cols a multiple of 256, up to 16384): one CTA per SM with a producer warp
-// and NW consumer warps.  Consumer warp c owns `depth` slots of a shared-memory ring (slots c*depth ..
-// c*depth + depth - 1) and takes rows k = c, c + NW, ...; its i-th row lands in its slot i % depth, so a
-// slot is only ever refilled for the warp that owns it, in that warp's order, and no waiter can run more
-// than one mbarrier phase ahead of the slot (parity waits stay exact).  The producer keeps every slot in
-// flight with bulk async copies; a consumer works on its slot alone -- warp shuffles only, no block
-// barriers -- in three passes over shared memory (softmax: max on packed bf16 pairs, sum of exp,
-// exp / sum; RMSNorm: sum of squares, scale) with paired fp32 arithmetic, then releases the slot.
-// ---------------------------------------------------------------------------------------------------
-constexpr int kRowMaxSlots = 64;
-
 __device__ __forceinline__ float2 unpack_bf16x2(uint32_t w) { return make_float2(lo_bf16(w), hi_bf16(w)); }
 
-template <int KIND>
-__global__ void __launch_bounds__(1024, 1) row_warp_kernel(const __grid_constant__ RowLaunch L, int nw, int depth) {
-  extern __shared__ __align__(128) uint8_t dyn[];
-  __shared__ uint64_t full[kRowMaxSlots], empty[kRowMaxSlots], wbar;
-  __shared__ int abort_flag;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t row_bytes = uint32_t(L.cols) * 2u;
-  const int chunks = int(L.cols / 8);
-  const int slots = nw * depth;
-  uint8_t *wrow = dyn;                                        // RMSNorm weight row
-  uint8_t *ring = dyn + (KIND == kRmsNorm ? row_bytes : 0);
-  const int64_t nrows = L.rows_end - L.rows_begin;
-  const int64_t mine = nrows > blockIdx.x ? (nrows - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  auto row_of = [&](int64_t k) { return L.rows_begin + int64_t(blockIdx.x) + k * int64_t(gridDim.x); };
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < slots; ++i) {
-      sm100::mbar_init(&full[i], 1);
-      sm100::mbar_init(&empty[i], 1);
-    }
-    sm100::mbar_init(&wbar, 1);
-    abort_flag = 0;
-    sm100::fence_barrier_init();
+template <int KIND, int TPR, int CH>
+__global__ void __launch_bounds__(TPR, (CH >= 4 ? 1024 : 2048) / TPR) row_cta_kernel(const __grid_constant__ RowLaunch L) {
+  constexpr int NW = TPR / 32;
+  __shared__ float red[2][NW];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t row = L.rows_begin + blockIdx.x;
+  const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(L.in) + row * L.in_stride);
+  uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(L.out) + row * L.out_stride);
+  uint32_t w[CH * 4];
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const uint4 v = __ldcs(src + c * TPR + tid);
+    w[c * 4 + 0] = v.x;
+    w[c * 4 + 1] = v.y;
+    w[c * 4 + 2] = v.z;
+    w[c * 4 + 3] = v.w;
   }
-  __syncthreads();
-  if (warp == 0) {
-    if (lane == 0) {
-      if constexpr (KIND == kRmsNorm) {
-        sm100::mbar_arrive_expect_tx(&wbar, row_bytes);
-        bulk_load(wrow, L.weight, row_bytes, &wbar);
-      }
-      uint64_t issued = 0, parity = 0;   // bit s: slot s has a copy in flight / the parity it completes
-      for (int64_t k = 0; k < mine && !abort_flag; ++k) {
-        const int c = int(k % nw);
-        const int64_t i = k / nw;
-        const int s = c * depth + int(i % depth);
-        if (i >= depth && !sm100::mbar_wait(&empty[s], uint32_t(i / depth - 1) & 1u)) { abort_flag = 1; break; }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        sm100::mbar_arrive_expect_tx(&full[s], row_bytes);
-        bulk_load(ring + size_t(s) * row_bytes, reinterpret_cast<const uint16_t *>(L.in) + row_of(k) * L.in_stride,
-                  row_bytes, &full[s]);
-        issued |= 1ull << s;
-        parity = (parity & ~(1ull << s)) | (uint64_t(uint32_t(i / depth) & 1u) << s);
-      }
-      // Bulk copies still in flight land before the CTA exits (only an aborted run can leave some).
-      if (abort_flag)
-        for (int s = 0; s < slots; ++s)
-          if (issued & (1ull << s)) sm100::mbar_wait(&full[s], uint32_t(parity >> s) & 1u);
-      if constexpr (KIND == kRmsNorm) sm100::mbar_wait(&wbar, 0);
+  if constexpr (KIND == kSoftmax) {
+    // Row max on packed bf16 pairs (NaN-propagating; exact, as max only selects).
+    __nv_bfloat162 m2[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) m2[j] = *reinterpret_cast<const __nv_bfloat162 *>(&w[j]);
+#pragma unroll
+    for (int i = 4; i < CH * 4; ++i) m2[i & 3] = __hmax2_nan(m2[i & 3], *reinterpret_cast<const __nv_bfloat162 *>(&w[i]));
+    m2[0] = __hmax2_nan(__hmax2_nan(m2[0], m2[1]), __hmax2_nan(m2[2], m2[3]));
+    float m = nan_max(__low2float(m2[0]), __high2float(m2[0]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = nan_max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[0][warp] = m;
+    __syncthreads();
+    m = red[0][0];
+#pragma unroll
+    for (int i = 1; i < NW; ++i) m = nan_max(m, red[0][i]);
+    // exp(x - m) = 2^((x - m) * log2 e), each evaluated once and kept for the division.
+    const float2 negm = make_float2(-m, -m), l2e = make_float2(1.4426950408889634f, 1.4426950408889634f);
+    float2 e[CH * 4];
+    float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < CH * 4; ++i) {
+      const float2 t = __fmul2_rn(__fadd2_rn(unpack_bf16x2(w[i]), negm), l2e);
+      e[i] = make_float2(ex2_fast(t.x), ex2_fast(t.y));
+      if (i & 1) acc1 = __fadd2_rn(acc1, e[i]);
+      else acc0 = __fadd2_rn(acc0, e[i]);
     }
-    return;
-  }
-  const int c = warp - 1;
-  if (c >= nw) return;
-  if constexpr (KIND == kRmsNorm) {
-    if (!sm100::mbar_wait(&wbar, 0)) abort_flag = 1;
-  }
-  int64_t i = 0;
-  for (int64_t k = c; k < mine && !abort_flag; k += nw, ++i) {
-    const int s = c * depth + int(i % depth);
-    if (!sm100::mbar_wait(&full[s], uint32_t(i / depth) & 1u)) { abort_flag = 1; break; }
-    const uint4 *src = reinterpret_cast<const uint4 *>(ring + size_t(s) * row_bytes);
-    uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(L.out) + row_of(k) * L.out_stride);
-    if constexpr (KIND == kSoftmax) {
-      __nv_bfloat162 mx2 = __floats2bfloat162_rn(-INFINITY, -INFINITY);
-      for (int q = lane; q < chunks; q += 32) {
-        const uint4 w = src[q];
-        mx2 = __hmax2_nan(mx2, *reinterpret_cast<const __nv_bfloat162 *>(&w.x));
-        mx2 = __hmax2_nan(mx2, *reinterpret_cast<const __nv_bfloat162 *>(&w.y));
-        mx2 = __hmax2_nan(mx2, *reinterpret_cast<const __nv_bfloat162 *>(&w.z));
-        mx2 = __hmax2_nan(mx2, *reinterpret_cast<const __nv_bfloat162 *>(&w.w));
-      }
-      float m = nan_max(__low2float(mx2), __high2float(mx2));
-      m = row_allreduce<32>(m, true, nullptr);
-      const float2 negm = make_float2(-m, -m), l2e = make_float2(1.4426950408889634f, 1.4426950408889634f);
-      float2 acc = make_float2(0.f, 0.f);
-      for (int q = lane; q < chunks; q += 32) {
-        const uint4 w = src[q];
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    acc0 = __fadd2_rn(acc0, acc1);
+    float sum = __fadd_rn(acc0.x, acc0.y);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 t = __fmul2_rn(__fadd2_rn(unpack_bf16x2(ws[j]), negm), l2e);
-          acc = __fadd2_rn(acc, make_float2(ex2_fast(t.x), ex2_fast(t.y)));
-        }
-      }
-      float sum = row_allreduce<32>(__fadd_rn(acc.x, acc.y), false, nullptr);
-      const float r = __frcp_rn(sum);
-      const float2 r2 = make_float2(r, r), nsum2 = make_float2(-sum, -sum);
-      for (int q = lane; q < chunks; q += 32) {
-        const uint4 w = src[q];
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-        uint32_t o[4];
+    for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+    if (lane == 0) red[1][warp] = sum;
+    __syncthreads();
+    sum = red[1][0];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 t = __fmul2_rn(__fadd2_rn(unpack_bf16x2(ws[j]), negm), l2e);
-          const float2 e = make_float2(ex2_fast(t.x), ex2_fast(t.y));
-          // e / sum: reciprocal product plus one residual correction (see div_by).
-          const float2 q0 = __fmul2_rn(e, r2);
-          const float2 res = __ffma2_rn(q0, nsum2, e);
-          const float2 q1 = __ffma2_rn(res, r2, q0);
-          o[j] = pack_bf16x2(q1.x, q1.y);
-        }
-        __stcs(dst + q, make_uint4(o[0], o[1], o[2], o[3]));
-      }
-    } else {
-      float2 acc = make_float2(0.f, 0.f);
-      for (int q = lane; q < chunks; q += 32) {
-        const uint4 w = src[q];
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    for (int i = 1; i < NW; ++i) sum = __fadd_rn(sum, red[1][i]);
+    // e / sum: reciprocal product plus one residual correction (div_by), on pairs.
+    const float r = __frcp_rn(sum);
+    const float2 r2 = make_float2(r, r), nsum2 = make_float2(-sum, -sum);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 x = unpack_bf16x2(ws[j]);
-          acc = __fadd2_rn(acc, __fmul2_rn(x, x));
-        }
-      }
-      const float ss = row_allreduce<32>(__fadd_rn(acc.x, acc.y), false, nullptr);
-      const float rs = rsqrtf(__fadd_rn(__fdiv_rn(ss, float(L.cols)), L.eps));
-      const float2 rs2 = make_float2(rs, rs);
-      const uint4 *wsrc = reinterpret_cast<const uint4 *>(wrow);
-      for (int q = lane; q < chunks; q += 32) {
-        const uint4 w = src[q], g = wsrc[q];
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w}, gs[4] = {g.x, g.y, g.z, g.w};
-        uint32_t o[4];
+    for (int c = 0; c < CH; ++c) {
+      uint32_t o[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 y = __fmul2_rn(__fmul2_rn(unpack_bf16x2(ws[j]), rs2), unpack_bf16x2(gs[j]));
-          o[j] = pack_bf16x2(y.x, y.y);
-        }
-        __stcs(dst + q, make_uint4(o[0], o[1], o[2], o[3]));
+      for (int j = 0; j < 4; ++j) {
+        const float2 q0 = __fmul2_rn(e[c * 4 + j], r2);
+        const float2 q1 = __ffma2_rn(__ffma2_rn(q0, nsum2, e[c * 4 + j]), r2, q0);
+        o[j] = pack_bf16x2(q1.x, q1.y);
       }
+      __stcs(dst + c * TPR + tid, make_uint4(o[0], o[1], o[2], o[3]));
     }
-    __syncwarp();
-    if (lane == 0) sm100::mbar_arrive(&empty[s]);
+  } else {
+    float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < CH * 4; ++i) {
+      const float2 x = unpack_bf16x2(w[i]);
+      if (i & 1) acc1 = __fadd2_rn(acc1, __fmul2_rn(x, x));
+      else acc0 = __fadd2_rn(acc0, __fmul2_rn(x, x));
+    }
+    acc0 = __fadd2_rn(acc0, acc1);
+    float ss = __fadd_rn(acc0.x, acc0.y);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    if (lane == 0) red[0][warp] = ss;
+    __syncthreads();
+    ss = red[0][0];
+#pragma unroll
+    for (int i = 1; i < NW; ++i) ss = __fadd_rn(ss, red[0][i]);
+    const float rs = rsqrtf(__fadd_rn(__fdiv_rn(ss, float(L.cols)), L.eps));
+    const float2 rs2 = make_float2(rs, rs);
+    const uint4 *wsrc = reinterpret_cast<const uint4 *>(L.weight);
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const uint4 g = __ldg(wsrc + c * TPR + tid);
+      const uint32_t gs[4] = {g.x, g.y, g.z, g.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 y = __fmul2_rn(__fmul2_rn(unpack_bf16x2(w[c * 4 + j]), rs2), unpack_bf16x2(gs[j]));
+        o[j] = pack_bf16x2(y.x, y.y);
+      }
+      __stcs(dst + c * TPR + tid, make_uint4(o[0], o[1], o[2], o[3]));
+    }
   }
 }
 
-template <int KIND>
-static int launch_row_warp(const RowLaunch &L, const LaunchCtx &c) {
-  const int64_t row_bytes = L.cols * 2;
-  const int64_t budget = 200 * 1024 - (KIND == kRmsNorm ? row_bytes : 0);
-  int slots = int(budget / row_bytes);
-  if (slots > kRowMaxSlots) slots = kRowMaxSlots;
-  if (slots < 2) return fail(PTSIM_E_RESOURCE, "row of %lld bf16 does not fit the shared-memory ring", (long long)L.cols);
-  // Consumer warps and the slots each owns: as many warps as slots (up to 31), two slots each beyond that.
-  const int depth = slots > 31 ? 2 : 1;
-  const int nw = slots / depth > 31 ? 31 : slots / depth;
-  const int smem = int(int64_t(nw) * depth * row_bytes + (KIND == kRmsNorm ? row_bytes : 0));
-  auto kern = row_warp_kernel<KIND>;
-  PTSIM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+template <int KIND, int TPR, int CH>
+static int launch_row_cta(const RowLaunch &L, const LaunchCtx &c) {
   const int64_t rows = L.rows_end - L.rows_begin;
-  int64_t grid = c.sm_count;
-  if (grid > rows) grid = rows;
-  kern<<<unsigned(grid), 32 * (nw + 1), smem, c.stream>>>(L, nw, depth);
+  if (rows > int64_t(0x7fffffff)) return fail(PTSIM_E_UNSUPPORTED, "%lld rows in one launch", (long long)rows);
+  row_cta_kernel<KIND, TPR, CH><<<unsigned(rows), TPR, 0, c.stream>>>(L);
   PTSIM_CUDA(cudaGetLastError());
   return PTSIM_OK;
 }
 
-template <int KIND, int CH>
-static int launch_row_stream(const RowLaunch &L, const LaunchCtx &c) {
-  const int64_t row_bytes = L.cols * 2;
-  int slots = int((48 * 1024) / row_bytes);
-  if (slots > 16) slots = 16;
-  if (slots < 2) slots = 2;
-  const int smem = int(slots * row_bytes);
-  auto kern = row_stream_kernel<KIND, CH>;
-  PTSIM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  const int64_t rows = L.rows_end - L.rows_begin;
-  int per_sm = int((200 * 1024) / (smem + 1024));
-  if (per_sm > 8) per_sm = 8;
-  if (per_sm < 1) per_sm = 1;
-  int64_t grid = int64_t(c.sm_count) * per_sm;
-  if (grid > rows) grid = rows;
-  kern<<<unsigned(grid), 128, smem, c.stream>>>(L, slots);
-  PTSIM_CUDA(cudaGetLastError());
+// The (threads per row, chunks per thread) of the row-per-CTA path for `cols`: 16 values a thread where
+// the thread count allows, else 32, else 8; 0 when no shape fits.
+template <int KIND>
+static int dispatch_row_cta(const RowLaunch &L, const LaunchCtx &c, bool *done) {
+  *done = true;
+  switch (L.cols) {
+    case 1024: return launch_row_cta<KIND, 64, 2>(L, c);
+    case 2048: return launch_row_cta<KIND, 128, 2>(L, c);
+    case 4096: return launch_row_cta<KIND, 256, 2>(L, c);
+    case 8192: return launch_row_cta<KIND, 512, 2>(L, c);
+    case 16384: return launch_row_cta<KIND, 512, 4>(L, c);
+    case 512: return launch_row_cta<KIND, 64, 1>(L, c);
+  }
+  *done = false;
   return PTSIM_OK;
 }
 
@@ -507,19 +343,10 @@ static int launch_row_kind(const RowLaunch &L, const LaunchCtx &c) {
   const bool aligned = (reinterpret_cast<uintptr_t>(L.in) % 16 == 0) && (reinterpret_cast<uintptr_t>(L.out) % 16 == 0) &&
                        (KIND == kSoftmax || reinterpret_cast<uintptr_t>(L.weight) % 16 == 0) &&
                        (L.in_stride % 8 == 0) && (L.out_stride % 8 == 0);
-  if (bf16_io && aligned && L.cols % 256 == 0 && L.cols <= 16384 && L.rows_total >= 4 * c.sm_count &&
-      !(KIND == kRmsNorm && (reinterpret_cast<uintptr_t>(L.weight) % 16 != 0)))
-    return launch_row_warp<KIND>(L, c);
-  if (bf16_io && aligned && L.cols % 1024 == 0 && L.cols <= 8192 && L.in_stride % 8 == 0) {
-    switch (L.cols / 1024) {
-      case 1: return launch_row_stream<KIND, 1>(L, c);
-      case 2: return launch_row_stream<KIND, 2>(L, c);
-      case 3: return launch_row_stream<KIND, 3>(L, c);
-      case 4: return launch_row_stream<KIND, 4>(L, c);
-      case 6: return launch_row_stream<KIND, 6>(L, c);
-      case 8: return launch_row_stream<KIND, 8>(L, c);
-      default: break;
-    }
+  if (bf16_io && aligned) {
+    bool done = false;
+    const int rc = dispatch_row_cta<KIND>(L, c, &done);
+    if (done) return rc;
   }
   if (bf16_io && aligned && L.cols % 8 == 0) {
     // Spread a row over as many threads as keep at most 4 chunks (32 values) each in registers.
@@ -714,6 +541,9 @@ __global__ void __launch_bounds__(kReduceThreads) reduce_pass2(const float *part
 
 // Partials one launch writes: one per CTA of pass 1 (4 CTAs per SM, at most 1024).
 static int reduce_blocks(int sm_count) { return sm_count * 4 < 1024 ? sm_count * 4 : 1024; }
+
+// Scratch bytes a launch needs on a device of `sm_count` SMs: the pass-1 partials.
+int reduce_workspace(int sm_count) { return reduce_blocks(sm_count) * int(sizeof(float)); }
 
 int launch_reduce(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, void *ws, size_t ws_bytes,
                   const LaunchCtx &c) {

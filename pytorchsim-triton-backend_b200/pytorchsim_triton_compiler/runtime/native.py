@@ -107,7 +107,7 @@ def units(blob):
 
 
 def workspace_size(blob, device=-1):
-    """Device scratch bytes a launch of `blob` wants on `device` (split-K GEMM partials, reduction partials)."""
+    """Device scratch bytes a launch of `blob` wants on `device` (the whole-tensor reduction's partials)."""
     n = load().ptsim_workspace_size(_desc_buffer(blob), len(blob), int(device))
     if n < 0:
         raise ExecutorError(D.E_DESC, last_error())
