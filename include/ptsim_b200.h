@@ -202,6 +202,20 @@ int ptsim_launch(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int
  * scratch). */
 int64_t ptsim_workspace_size(const void *desc, size_t desc_bytes, int device);
 
+/* Run a whole-tensor reduction (desc->kind == PTSIM_KIND_REDUCE_ALL) like ptsim_launch(desc, ..., 0,
+ * units, ...), with its scratch -- one fp32 partial per pass-1 CTA -- taken from a 4 KiB array the
+ * library holds on every GPU that loads it: nothing is allocated, by the library or anything it calls.
+ * For callers that cannot allocate device memory -- a foreign-language binding that only holds the raw
+ * pointers it was handed, a host whose memory pool already owns the GPU's memory, or a caller that may
+ * not synchronise the device, as cudaMalloc and cudaFree do.  A launch that needs more scratch than the
+ * array holds (desc->workspace_bytes above 4096) returns PTSIM_E_RESOURCE; other kinds return
+ * PTSIM_E_UNSUPPORTED.  The first call on a device looks the array's device address up
+ * (cudaGetSymbolAddress); make that first call before any stream capture.  Every call on a device
+ * shares the one array: calls that overlap on the GPU (other streams, other threads) race on it, so
+ * order them on one stream.  No counterpart in the reference: Spike ran in host memory and needed no
+ * device scratch. */
+int ptsim_launch_reduce_noalloc(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int nptr, void *stream);
+
 /* Synchronise `stream` and return (and clear) the device status word of the current device:
  * *device_status receives PTSIM_OK or PTSIM_E_OOB / PTSIM_E_TIMEOUT as a kernel recorded it.
  * Replaces the exit-code check of runtime/spike.py:23-33 (run_process). */

@@ -262,3 +262,67 @@ int ptsim_last_error(char *buf, int n) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------------
+// Whole-tensor reduction with library-owned scratch, for callers that cannot allocate device memory: a
+// foreign-language binding (ctypes, cgo, JNI) that only holds the raw pointers it was handed, a host
+// whose memory pool already owns the GPU's memory, or a caller that may not synchronise the device, as
+// cudaMalloc and cudaFree do.  The two-pass reduction parks one fp32 partial per pass-1 CTA in scratch;
+// here that scratch is the file-scope array below, which every GPU that loads this library holds until
+// the process exits.
+// ---------------------------------------------------------------------------------------------------
+namespace ptsim {
+
+// 4 KiB: pass 1 never runs more than 1024 CTAs (4 per SM, capped), one fp32 partial each.
+constexpr size_t kStaticScratchBytes = 1024 * sizeof(float);
+static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
+
+static std::mutex g_static_mu;
+static void *g_static_ptr[64];
+
+// Device address of g_static_scratch on `dev` (the current device), looked up once per device.  In host
+// code the array's name is only a host-side stand-in, so kernels get this address instead.
+static int static_scratch(int dev, void **out) {
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  if (dev < 0 || dev >= 64) return fail(PTSIM_E_ARGS, "device %d out of range", dev);
+  if (g_static_ptr[dev] == nullptr) {
+    void *p = nullptr;
+    PTSIM_CUDA(cudaGetSymbolAddress(&p, g_static_scratch));
+    if (p == nullptr) return fail(PTSIM_E_CUDA, "no device address for the static scratch on device %d", dev);
+    g_static_ptr[dev] = p;
+  }
+  *out = g_static_ptr[dev];
+  return PTSIM_OK;
+}
+
+}  // namespace ptsim
+
+extern "C" int ptsim_launch_reduce_noalloc(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int nptr,
+                                           void *stream) {
+  using namespace ptsim;
+  int rc = check_desc(desc, desc_bytes);
+  if (rc) return rc;
+  const ptsim_desc &d = *reinterpret_cast<const ptsim_desc *>(desc);
+  if (d.kind != PTSIM_KIND_REDUCE_ALL)
+    return fail(PTSIM_E_UNSUPPORTED, "ptsim_launch_reduce_noalloc runs whole-tensor reduction descriptors only");
+  if (nptr != d.nargs) return fail(PTSIM_E_ARGS, "%d pointers for a launch of %d arguments", nptr, d.nargs);
+  for (int a = 0; a < nptr; ++a)
+    if (dev_ptrs[a] == nullptr && d.arg_numel[a] > 0) return fail(PTSIM_E_ARGS, "argument %d is a null pointer", a);
+  if (d.units == 0) return PTSIM_OK;
+  LaunchCtx c;
+  c.stream = reinterpret_cast<cudaStream_t>(stream);
+  PTSIM_CUDA(cudaGetDevice(&c.device));
+  DeviceInfo info;
+  if ((rc = device_info(c.device, &info))) return rc;
+  c.sm_count = info.sm_count;
+  int64_t need = reduce_workspace(c.sm_count);
+  if (d.workspace_bytes > need) need = d.workspace_bytes;
+  if (need > int64_t(kStaticScratchBytes))
+    return fail(PTSIM_E_RESOURCE, "the reduction needs %lld bytes of scratch; the static scratch holds %zu",
+                (long long)need, kStaticScratchBytes);
+  void *scratch = nullptr;
+  if ((rc = static_scratch(c.device, &scratch))) return rc;
+  // Nothing in the scratch has to start at zero: pass 1 writes every partial that pass 2 reads, so the
+  // previous call's contents never reach a result.
+  return launch_reduce(d, dev_ptrs, 0, d.units, scratch, kStaticScratchBytes, c);
+}

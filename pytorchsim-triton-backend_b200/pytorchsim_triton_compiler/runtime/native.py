@@ -21,6 +21,7 @@ SYMBOLS = {
     "ptsim_launch": (C.c_int, [C.c_void_p, C.c_size_t, C.POINTER(C.c_void_p), C.c_int, C.c_int64, C.c_int64,
                                C.c_void_p, C.c_size_t, C.c_void_p]),
     "ptsim_workspace_size": (C.c_int64, [C.c_void_p, C.c_size_t, C.c_int]),
+    "ptsim_launch_reduce_noalloc": (C.c_int, [C.c_void_p, C.c_size_t, C.POINTER(C.c_void_p), C.c_int, C.c_void_p]),
     "ptsim_sync": (C.c_int, [C.c_void_p, C.POINTER(C.c_int32)]),
     "ptsim_last_error": (C.c_int, [C.c_char_p, C.c_int]),
 }
@@ -136,6 +137,15 @@ def launch(blob, ptrs, lo, hi, workspace=0, workspace_bytes=0, stream=0):
     arr = (C.c_void_p * max(1, len(ptrs)))(*[C.c_void_p(int(p)) for p in ptrs])
     _check(lib.ptsim_launch(buf, len(blob), arr, len(ptrs), int(lo), int(hi), C.c_void_p(int(workspace) or None),
                             int(workspace_bytes), C.c_void_p(int(stream) or None)))
+
+
+def launch_reduce_noalloc(blob, ptrs, stream=0):
+    """Enqueue a whole-tensor reduction of `blob` with the library's own 4 KiB static scratch: for callers
+    that cannot allocate device memory.  Calls that overlap on the GPU share that scratch and race."""
+    lib = load()
+    buf = _desc_buffer(blob)
+    arr = (C.c_void_p * max(1, len(ptrs)))(*[C.c_void_p(int(p)) for p in ptrs])
+    _check(lib.ptsim_launch_reduce_noalloc(buf, len(blob), arr, len(ptrs), C.c_void_p(int(stream) or None)))
 
 
 def sync(stream=0):
