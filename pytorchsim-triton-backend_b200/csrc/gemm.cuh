@@ -14,9 +14,11 @@
 //   warps 2..5  epilogue: tcgen05.ld of the accumulator (one TMEM lane = one output row per thread),
 //               optional residual add, cast, 16-byte global stores.
 // Split-K (an output with fewer tiles than SMs): the K range of a tile is cut over the CTAs of one
-// thread-block cluster; each CTA parks its fp32 accumulator in its own shared memory, and after a
-// cluster barrier CTA q sums slice q of the tile's columns over every CTA's copy (distributed shared
-// memory reads, in rank order: deterministic) and runs the epilogue on it.  No global scratch.
+// thread-block cluster.  Once every CTA of the cluster has finished its K range (cluster barrier), each
+// sends column slice q of its fp32 accumulator to CTA q: staged through its own shared memory and moved
+// by bulk asynchronous copies into CTA q's receive slots (distributed shared memory, completion counted
+// on CTA q's mbarrier); CTA q sums its slots in rank order (deterministic) and runs the epilogue on
+// slice q.  No global scratch.
 // Every wait is bounded (sm100::mbar_wait); on a timeout each role stops issuing, the CTA meets at the
 // final barrier, and TMEM is released before exit.
 #pragma once
@@ -109,7 +111,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
   uint64_t *tfull_bar = empty_bar + STAGES;             // 2
   uint64_t *tempty_bar = tfull_bar + 2;                 // 2
   uint64_t *drain_bar = tempty_bar + 2;                 // 1: MMA completion before TMEM is freed
-  uint32_t *tmem_base_slot = reinterpret_cast<uint32_t *>(drain_bar + 1);
+  uint64_t *xbar = drain_bar + 1;                       // 1: split-K slices received from the cluster
+  uint32_t *tmem_base_slot = reinterpret_cast<uint32_t *>(xbar + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_base_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -128,6 +131,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
       sm100::mbar_init(&tempty_bar[b], 4);  // one arrival per epilogue warp
     }
     sm100::mbar_init(drain_bar, 1);
+    sm100::mbar_init(xbar, 1);
     *abort_flag = 0;
     sm100::fence_barrier_init();
     sm100::tma_prefetch_desc(&g.tmap_a);
@@ -241,28 +245,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
       const int64_t row = g.m_begin + int64_t(tm) * kGemmBM + row_in_tile;
       const int64_t n0 = int64_t(tn) * BN;
       const bool row_ok = row < g.m_end;
-      if (g.splits > 1) {
-        // Split-K: park this CTA's fp32 accumulator in its own shared memory (the operand ring is idle:
-        // the accumulator is complete only after every MMA has read its stages, and the producer loads
-        // nothing more), rows of BN floats with 16-byte chunk c of row r at chunk position c ^ (r % 8),
-        // so both the row-per-thread writes here and the reads of the exchange are conflict-free.
-        float *park = reinterpret_cast<float *>(smem) + size_t(row_in_tile) * BN;
-#pragma unroll 1
-        for (int j = 0; j < BN / 32; ++j) {
-          uint32_t v[32];
-          sm100::tmem_ld32(tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(buf * BN + j * 32), v);
-          sm100::tmem_wait_ld();
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            reinterpret_cast<float4 *>(park)[(j * 8 + q) ^ (row_in_tile & 7)] =
-                make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]), __uint_as_float(v[4 * q + 2]),
-                            __uint_as_float(v[4 * q + 3]));
-        }
-        sm100::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) sm100::mbar_arrive(&tempty_bar[buf]);
-        continue;
-      }
+      if (g.splits > 1) continue;   // split-K: the accumulator stays in TMEM for the cluster exchange
 #pragma unroll 1
       for (int j = 0; j < BN / 32; ++j) {
         uint32_t v[32];
@@ -283,44 +266,84 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
 
   if (g.splits > 1) {
     // Split-K exchange.  Every thread of every CTA in the cluster takes both cluster barriers, on every
-    // path (an aborted CTA too), so none can wait on a peer that never arrives.
+    // path (an aborted CTA too), so none can wait on a peer that never arrives.  Shared memory (the
+    // operand ring, free once the CTA's K range is done) holds the receive slots -- sender s, 32-column
+    // chunk c of this CTA's slice: 128 rows x 32 floats (16 KB), row r's 16-byte chunk q at q ^ (r % 8),
+    // conflict-free for the row-per-thread accesses -- followed by the staging blocks of the chunks this
+    // CTA sends (same layout).  The host plan guarantees both fit the ring.
+    const int width = BN / g.splits;                  // columns of the slice each CTA finishes
+    const int cpw = width / 32;                       // 32-column chunks per slice
+    const uint32_t rank = sm100::cluster_ctarank();
+    uint8_t *recv = smem;
+    uint8_t *stage = smem + size_t(kGemmBM) * BN * 4;
+    const int row_in_tile = (warp & 3) * 32 + lane;
+    if (threadIdx.x == 64) sm100::mbar_arrive_expect_tx(xbar, uint32_t((g.splits - 1) * cpw * 16384));
     __syncwarp();
-    sm100::cluster_sync();   // every CTA's accumulator is parked and visible
-    if (warp >= 2 && !*abort_flag) {
-      const int row_in_tile = (warp & 3) * 32 + lane;
-      const int t = blockIdx.x / g.splits;
-      int tm, tn;
-      tile_coords(t, tm, tn);
-      const int64_t row = g.m_begin + int64_t(tm) * kGemmBM + row_in_tile;
-      const int width = BN / g.splits;                            // columns this CTA finishes
-      const int c_begin = int(sm100::cluster_ctarank()) * width;
-      const uint32_t park = sm100::smem_u32(smem) + uint32_t(row_in_tile) * BN * 4;
-      if (row < g.m_end) {
+    sm100::cluster_sync();   // every CTA's K range is done (rings free) and every receive barrier is armed
+    if (warp >= 2) {
+      if (!*abort_flag) {
+        const uint32_t quarter_lane = uint32_t((warp & 3) * 32) << 16;
+        int remote = 0;
 #pragma unroll 1
-        for (int c0 = c_begin; c0 < c_begin + width; c0 += 32) {
-          const int64_t col0 = int64_t(tn) * BN + c0;
-          if (col0 >= g.N) break;
-          float acc[32];
+        for (int j = 0; j < BN / 32; ++j) {
+          uint32_t v[32];
+          sm100::tmem_ld32(tmem_base + quarter_lane + uint32_t(j * 32), v);
+          sm100::tmem_wait_ld();
+          const int owner = j / cpw;
+          uint8_t *blk = owner == int(rank) ? recv + size_t(int(rank) * cpw + j % cpw) * 16384 : stage + size_t(remote++) * 16384;
+          float4 *dst = reinterpret_cast<float4 *>(blk + row_in_tile * 128);
 #pragma unroll
-          for (int q = 0; q < 32; ++q) acc[q] = 0.f;
+          for (int q = 0; q < 8; ++q)
+            dst[q ^ (row_in_tile & 7)] = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                                                     __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // staging visible to the bulk copies
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (threadIdx.x == 64 && !*abort_flag) {
+        int i = 0;
+        for (int j = 0; j < BN / 32; ++j) {
+          const int owner = j / cpw;
+          if (owner == int(rank)) continue;
+          const uint32_t dst = sm100::mapa_shared(sm100::smem_u32(recv + size_t(int(rank) * cpw + j % cpw) * 16384), uint32_t(owner));
+          const uint32_t bar = sm100::mapa_shared(sm100::smem_u32(xbar), uint32_t(owner));
+          sm100::bulk_copy_s2c(dst, sm100::smem_u32(stage + size_t(i++) * 16384), 16384, bar);
+        }
+      }
+      // Receive: the peers' slices land on xbar; then sum the slots in rank order.
+      if (!*abort_flag && !sm100::mbar_wait(xbar, 0)) *abort_flag = 1;
+      if (!*abort_flag) {
+        const int t = blockIdx.x / g.splits;
+        int tm, tn;
+        tile_coords(t, tm, tn);
+        const int64_t row = g.m_begin + int64_t(tm) * kGemmBM + row_in_tile;
+        if (row < g.m_end) {
 #pragma unroll 1
-          for (int r = 0; r < g.splits; ++r) {
-            const uint32_t peer = sm100::mapa_shared(park, uint32_t(r));
+          for (int c = 0; c < cpw; ++c) {
+            const int64_t col0 = int64_t(tn) * BN + int64_t(rank) * width + c * 32;
+            if (col0 >= g.N) break;
+            float acc[32];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const float4 w = sm100::ld_dsmem_f4(peer + uint32_t(((c0 / 4 + q) ^ (row_in_tile & 7)) * 16));
-              acc[4 * q] = __fadd_rn(acc[4 * q], w.x);
-              acc[4 * q + 1] = __fadd_rn(acc[4 * q + 1], w.y);
-              acc[4 * q + 2] = __fadd_rn(acc[4 * q + 2], w.z);
-              acc[4 * q + 3] = __fadd_rn(acc[4 * q + 3], w.w);
+            for (int q = 0; q < 32; ++q) acc[q] = 0.f;
+#pragma unroll 1
+            for (int r = 0; r < g.splits; ++r) {
+              const float4 *src = reinterpret_cast<const float4 *>(recv + size_t(r * cpw + c) * 16384 + row_in_tile * 128);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const float4 w = src[q ^ (row_in_tile & 7)];
+                acc[4 * q] = __fadd_rn(acc[4 * q], w.x);
+                acc[4 * q + 1] = __fadd_rn(acc[4 * q + 1], w.y);
+                acc[4 * q + 2] = __fadd_rn(acc[4 * q + 2], w.z);
+                acc[4 * q + 3] = __fadd_rn(acc[4 * q + 3], w.w);
+              }
             }
+            gemm_store_row32(g, row, col0, acc);
           }
-          gemm_store_row32(g, row, col0, acc);
         }
       }
     }
     __syncwarp();
-    sm100::cluster_sync();   // no CTA leaves while a peer still reads its shared memory
+    sm100::cluster_sync();   // no CTA leaves while a peer's bulk copy may still read its staging
   }
 
   // Teardown: every role has stopped issuing; make sure no MMA still writes TMEM, then free it.
@@ -399,8 +422,6 @@ static int max_active_clusters(int splits, const LaunchCtx &c) {
 template <int BN, bool B_KMAJOR>
 static int run_gemm(GemmArgs &g, const LaunchCtx &c) {
   using Cfg = GemmCfg<BN>;
-  static_assert(size_t(kGemmBM) * BN * sizeof(float) <= size_t(Cfg::STAGES) * Cfg::STAGE_BYTES,
-                "the split-K accumulator is parked in the operand ring");
   const int items = g.tiles_m * g.tiles_n * g.splits;
   auto kern = gemm_tcgen05_kernel<BN, B_KMAJOR>;
   PTSIM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
@@ -427,10 +448,21 @@ static int run_gemm(GemmArgs &g, const LaunchCtx &c) {
   return PTSIM_OK;
 }
 
+// Shared memory of the split-K exchange: the receive slots (128 x BN fp32) plus the staging blocks of
+// the (splits - 1) / splits of the accumulator a CTA sends; and the operand ring that holds it.
+static int64_t splitk_smem(int bn, int splits) { return int64_t(kGemmBM) * bn * 4 * (2 * splits - 1) / splits; }
+static int64_t ring_bytes(int bn) {
+  return bn == 256 ? int64_t(GemmCfg<256>::STAGES) * GemmCfg<256>::STAGE_BYTES
+       : bn == 128 ? int64_t(GemmCfg<128>::STAGES) * GemmCfg<128>::STAGE_BYTES
+                   : int64_t(GemmCfg<64>::STAGES) * GemmCfg<64>::STAGE_BYTES;
+}
+
 // The tile plan of a GEMM: the N tile, and the K splits when the output has fewer tiles than the device
-// has SMs (split-K over a cluster: a power of two up to 8, at most BN / 32 so every CTA finishes at
-// least 32 columns, at least four K blocks each, one CTA per SM).  The split count follows the whole
-// launch's M, never the unit range, so every range of a launch sums K in the same order.
+// has SMs (split-K over a cluster: a power of two up to 8, at most BN / 32 so every CTA finishes whole
+// 32-column chunks, at least four K blocks each, one CTA per SM, the exchange inside the operand ring).
+// 256-wide tiles are preferred (more reuse of each A tile); an output so short that even split 256-wide
+// tiles leave half the SMs idle switches to 128-wide tiles.  The plan follows the whole launch's M,
+// never the unit range, so every range of a launch sums K in the same order.
 struct GemmPlan {
   int bn, splits, kb_per_split;
   int64_t tiles_m, tiles_n;
@@ -438,20 +470,29 @@ struct GemmPlan {
 
 static GemmPlan plan_gemm(int64_t m_rows, int64_t m_total, int64_t N, int64_t K, int sm_count) {
   GemmPlan pl;
+  const int64_t num_kb = ceil_div(K, kGemmBK);
+  const int64_t tm_total = ceil_div(m_total, kGemmBM);
+  auto splits_for = [&](int bn) {
+    const int64_t tiles = tm_total * ceil_div(N, bn);
+    int sp = 1;
+    while (sp < 8 && sp * 2 <= bn / 32 && tiles * sp * 2 <= sm_count && num_kb / (sp * 2) >= 4 &&
+           splitk_smem(bn, sp * 2) <= ring_bytes(bn))
+      sp *= 2;
+    return sp;
+  };
   pl.bn = N >= 256 ? 256 : (N > 64 ? 128 : 64);
+  pl.splits = splits_for(pl.bn);
+  if (pl.bn == 256 && tm_total * ceil_div(N, 256) * pl.splits <= sm_count / 2) {
+    pl.bn = 128;
+    pl.splits = splits_for(128);
+  }
   pl.tiles_m = ceil_div(m_rows, kGemmBM);
   pl.tiles_n = ceil_div(N, pl.bn);
-  const int64_t num_kb = ceil_div(K, kGemmBK);
-  const int64_t whole_tiles = ceil_div(m_total, kGemmBM) * pl.tiles_n;
-  int splits = 1;
-  while (splits < 8 && splits * 2 <= pl.bn / 32 && whole_tiles * splits * 2 <= sm_count && num_kb / (splits * 2) >= 4)
-    splits *= 2;
-  if (pl.tiles_m * pl.tiles_n * splits > sm_count) splits = 1;   // a range wider than the whole? keep one wave
-  pl.splits = splits;
-  pl.kb_per_split = int(ceil_div(num_kb, splits));
-  if (pl.splits == 1 && whole_tiles < sm_count / 2 && N > 64) {
+  if (pl.tiles_m * pl.tiles_n * pl.splits > sm_count) pl.splits = 1;
+  pl.kb_per_split = int(ceil_div(num_kb, pl.splits));
+  if (pl.splits == 1 && tm_total * pl.tiles_n < sm_count / 2 && N > 64) {
     // No split possible (short K): narrower N tiles give more SMs work instead.
-    pl.bn = N > 128 && ceil_div(m_total, kGemmBM) * ceil_div(N, 128) >= sm_count / 2 ? 128 : 64;
+    pl.bn = N > 128 && tm_total * ceil_div(N, 128) >= sm_count / 2 ? 128 : 64;
     pl.tiles_n = ceil_div(N, pl.bn);
   }
   return pl;
@@ -493,6 +534,8 @@ int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, 
       pl.splits /= 2;
     }
     pl.kb_per_split = int(ceil_div(ceil_div(p.K, kGemmBK), pl.splits));
+    if (pl.splits > 1 && (splitk_smem(pl.bn, pl.splits) > ring_bytes(pl.bn) || pl.bn / pl.splits < 32))
+      return fail(PTSIM_E_RESOURCE, "split-K plan BN=%d x %d splits does not fit the exchange", pl.bn, pl.splits);
   }
   g.tiles_m = int(pl.tiles_m);
   g.tiles_n = int(pl.tiles_n);

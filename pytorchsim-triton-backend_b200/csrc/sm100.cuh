@@ -98,8 +98,8 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const void *tmap, uint64_
 // ---------------------------------------------------------------------------------------------------
 // Allocate `ncols` TMEM columns (power of two >= 32); the base address lands in *dst_smem.  Whole warp.
 // Thread-block clusters: the CTA's rank, a barrier over every thread of every CTA in the cluster
-// (release / acquire: shared-memory writes before it are visible to peers after it), and reads of a
-// peer CTA's shared memory (distributed shared memory).
+// (release / acquire: shared-memory writes before it are visible to peers after it), and bulk copies
+// into a peer CTA's shared memory (distributed shared memory).
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -113,13 +113,12 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
 }
-__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
+// Bulk asynchronous copy from this CTA's shared memory into a cluster peer's (dst and bar are
+// shared::cluster addresses from mapa_shared); completion is counted on the peer's mbarrier.
+__device__ __forceinline__ void bulk_copy_s2c(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "r"(src), "r"(bytes), "r"(bar)
                : "memory");
-  return v;
 }
 
 __device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
