@@ -110,6 +110,105 @@ def launch_tensors(blob, tensors, lo=0, hi=None, stream=None, sync=True):
     return tensors
 
 
+def written_args(desc):
+    """Indices of the arguments a launch of `desc` writes (the launch's outputs)."""
+    k = desc.kind
+    if k == D.ELEMENTWISE:
+        e = desc.p.ew
+        return [e.map[e.store_map].arg]
+    if k in (D.ROW_SOFTMAX, D.ROW_RMSNORM):
+        return [desc.p.row.out_arg]
+    if k == D.QKNORM_ROPE:
+        return [desc.p.qk.out_arg]
+    if k == D.GEMM:
+        return [desc.p.gemm.c_arg]
+    if k == D.ATTN_PREFILL:
+        return [desc.p.attn.o_arg]
+    if k == D.REDUCE_ALL:
+        return [desc.p.red.out_arg]
+    raise CudaError(f"descriptor kind {k}")
+
+
+class HostPipeline:
+    """Launches over tensors in host memory, the way a caller holding `.raw` data runs the executor end to
+    end: each launch's arguments are copied to the GPU, the kernels run, and the written arguments are
+    copied back into the host tensors.  Copies run on their own streams (host-to-device, device-to-host)
+    beside the compute stream, and a row-wise launch (softmax, RMSNorm) is cut into `chunks` unit ranges
+    so the transfer of one range overlaps the kernel of the previous one and the return of the one before
+    that; PCIe then carries both directions at once.  Host tensors should be pinned for the copies to be
+    asynchronous.  Launches submitted to one pipeline run in submission order; wait() synchronises and
+    raises ExecutorError if a kernel reported a failure."""
+
+    def __init__(self, device=0, chunks=8):
+        torch = _torch()
+        self.torch = torch
+        self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        self.chunks = max(1, int(chunks))
+        native.init(self.device.index or 0)
+        self.s_in = torch.cuda.Stream(self.device)
+        self.s_run = torch.cuda.Stream(self.device)
+        self.s_out = torch.cuda.Stream(self.device)
+        self._live = []
+
+    def submit(self, blob, host):
+        torch = self.torch
+        desc = D.from_bytes(blob)
+        if len(host) != desc.nargs:
+            raise CudaError(f"{len(host)} host tensors for a launch of {desc.nargs} arguments")
+        for i, t in enumerate(host):
+            if t.is_cuda or not t.is_contiguous() or t.numel() != desc.arg_numel[i]:
+                raise CudaError(f"argument {i}: a contiguous host tensor of {desc.arg_numel[i]} elements is required")
+        outs = written_args(desc)
+        dev = [torch.empty(t.numel(), dtype=t.dtype, device=self.device) for t in host]
+        ptrs = [t.data_ptr() for t in dev]
+        ws = workspace_for(blob, self.device)
+        wsp, wsn = (ws.data_ptr(), ws.numel()) if ws is not None else (0, 0)
+        self._live.append((dev, ws))
+        row = desc.kind in (D.ROW_SOFTMAX, D.ROW_RMSNORM)
+        n_chunks = min(self.chunks, desc.units) if row else 1
+        bounds = split(desc.units, n_chunks)
+        with torch.cuda.device(self.device):
+            # Arguments every range reads whole (or that are not row-partitioned) go first.
+            whole = [i for i in range(desc.nargs) if not row or i not in (desc.p.row.in_arg, desc.p.row.out_arg)]
+            with torch.cuda.stream(self.s_in):
+                for i in whole:
+                    dev[i].copy_(host[i].reshape(-1), non_blocking=True)
+            for lo, hi in bounds:
+                ev_in = torch.cuda.Event()
+                with torch.cuda.stream(self.s_in):
+                    if row:
+                        r = desc.p.row
+                        a, b = self._rows(desc, lo, hi, r.in_row_stride, desc.arg_numel[r.in_arg])
+                        dev[r.in_arg][a:b].copy_(host[r.in_arg].reshape(-1)[a:b], non_blocking=True)
+                    ev_in.record(self.s_in)
+                self.s_run.wait_event(ev_in)
+                native.launch(blob, ptrs, lo, hi, wsp, wsn, self.s_run.cuda_stream)
+                ev_run = torch.cuda.Event()
+                ev_run.record(self.s_run)
+                self.s_out.wait_event(ev_run)
+                with torch.cuda.stream(self.s_out):
+                    for i in outs:
+                        if row:
+                            r = desc.p.row
+                            a, b = self._rows(desc, lo, hi, r.out_row_stride, desc.arg_numel[i])
+                        else:
+                            a, b = 0, desc.arg_numel[i]
+                        host[i].reshape(-1)[a:b].copy_(dev[i][a:b], non_blocking=True)
+        return host
+
+    @staticmethod
+    def _rows(desc, lo, hi, stride, numel):
+        r0 = lo * desc.unit_size
+        r1 = min(hi * desc.unit_size, desc.p.row.rows)
+        return r0 * stride, min(numel, (r1 - 1) * stride + desc.p.row.cols)
+
+    def wait(self):
+        self.s_out.synchronize()
+        self.s_in.synchronize()
+        native.sync(self.s_run.cuda_stream)
+        self._live.clear()
+
+
 def read_raw(path, arg):
     want = ko.numel(arg)
     data = np.fromfile(path, dtype=np.dtype(ko.NP_DTYPE[arg["dtype"]]), count=want)
