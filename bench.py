@@ -152,7 +152,7 @@ def dist_setup(args):
         import datetime
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     return world, rank, local
 
 

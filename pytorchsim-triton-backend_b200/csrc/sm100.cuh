@@ -1,5 +1,5 @@
-// sm_100a building blocks written as inline PTX: mbarriers with bounded waits, TMA tile loads (never
-// with .multicast::cluster), tcgen05 TMEM allocation, MMA issue/commit and TMEM loads, and the shared
+// sm_100a building blocks written as inline PTX: mbarriers with bounded waits, TMA tile loads (each CTA
+// fetches its own tiles; no cluster broadcast), tcgen05 TMEM allocation, MMA issue/commit and TMEM loads, and the shared
 // memory / instruction descriptors the tensor core reads operands through.
 //
 // Descriptor encodings (PTX ISA "Shared memory descriptor" / "Instruction descriptor" for tcgen05):
