@@ -275,20 +275,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
 //               from TMEM in 32-column chunks twice (row max, then exp / sum / bf16 pack), P is written
 //               back as packed bf16 pairs over the consumed S columns, O is rescaled in TMEM when the row
 //               max moved, and at the end O / l is stored.
-// The two softmax warpgroups alternate with the tensor core (while one computes exp, the MMA runs the
-// other tile's products).  In-order MMA execution makes S_X(j)'s commit imply PV_X(j-1) has finished,
-// so a softmax may rescale O_X and overwrite P_X as soon as S_X(j) is ready.
+// The two softmax warpgroups alternate with the tensor core: the MMA warp issues PV_A(j) and S_A(j+1)
+// as soon as P_A(j) is ready, then PV_B(j) and S_B(j+1), so while one tile's softmax computes exp the
+// tensor core runs the other tile's products.  In-order MMA execution makes S_X(j)'s commit imply
+// PV_X(j-1) has finished, so a softmax may rescale O_X and overwrite P_X as soon as S_X(j) is ready.
 // TMEM: S_A [0,128)  S_B [128,256)  O_A [256,384)  O_B [384,512).
 // ---------------------------------------------------------------------------------------------------
 constexpr int kAttn2Threads = 320;
 constexpr int kAttn2Smem = 6 * kAttnTile + 1024 + 256;  // Q_A, Q_B, K x2, V x2
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
-  uint32_t lo[16], hi[16];
-#pragma unroll
-  for (int q = 0; q < 16; ++q) { lo[q] = r[q]; hi[q] = r[16 + q]; }
-  sm100::tmem_st16(taddr, lo);
-  sm100::tmem_st16(taddr + 16, hi);
+  sm100::tmem_st16(taddr, *reinterpret_cast<const uint32_t(*)[16]>(&r[0]));
+  sm100::tmem_st16(taddr + 16, *reinterpret_cast<const uint32_t(*)[16]>(&r[16]));
 }
 
 __global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __grid_constant__ AttnArgs g) {
@@ -366,38 +364,57 @@ __global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __gri
     if (lane == 0) {
       constexpr uint32_t idesc_s = sm100::idesc_bf16_f32(kAttnBM, kAttnBN, false, false);
       constexpr uint32_t idesc_o = sm100::idesc_bf16_f32(kAttnBM, kAttnD, false, true);
-      bool ok = sm100::mbar_wait(q_full, 0);
+      // Issue order (tiles ping-pong): S_A(0) S_B(0) | PV_A(0) S_A(1) | PV_B(0) S_B(1) | PV_A(1) S_A(2) | ...
+      // so the tensor core runs one tile's products while the other tile's softmax computes.  S_X(j+1)
+      // overwrites P_X(j) in TMEM only after PV_X(j), issued before it, has read it (in-order execution).
+      auto issue_s = [&](int t, int j) {
+        const uint32_t k_addr = sm100::smem_u32(sK + (j & 1) * kAttnTile);
+        const uint32_t q_addr = sm100::smem_u32(sQ + t * kAttnTile);
+#pragma unroll
+        for (int k = 0; k < kAttnD / 16; ++k) {
+          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
+          sm100::mma_bf16_ss(tmem + t * 128, sm100::sw128_desc(q_addr + off, 16, 1024),
+                             sm100::sw128_desc(k_addr + off, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
+        }
+        sm100::mma_commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t v_addr = sm100::smem_u32(sV + (j & 1) * kAttnTile);
+#pragma unroll
+        for (int k = 0; k < kAttnBN / 16; ++k)
+          sm100::mma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + k * 8,
+                             sm100::sw128_desc(v_addr + k * 16 * 128, 16384, 1024), idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+        if (j == (t == 0 ? nA : nB) - 1) sm100::mma_commit(&o_done[t]);
+      };
+      bool ok = sm100::mbar_wait(q_full, 0) && sm100::mbar_wait(&k_full[0], 0);
+      if (ok) {
+        sm100::tc_fence_after();
+        if (nA > 0) issue_s(0, 0);
+        issue_s(1, 0);
+      }
       for (int j = 0; ok && j < nB; ++j) {
         const int st = j & 1;
-        if (!sm100::mbar_wait(&k_full[st], (j >> 1) & 1)) { ok = false; break; }
-        sm100::tc_fence_after();
-        const uint32_t k_addr = sm100::smem_u32(sK + st * kAttnTile);
-        for (int t = 0; t < 2; ++t) {
-          if (t == 0 && j >= nA) continue;
-          const uint32_t q_addr = sm100::smem_u32(sQ + t * kAttnTile);
-#pragma unroll
-          for (int k = 0; k < kAttnD / 16; ++k) {
-            const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
-            sm100::mma_bf16_ss(tmem + t * 128, sm100::sw128_desc(q_addr + off, 16, 1024),
-                               sm100::sw128_desc(k_addr + off, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
-          }
-          sm100::mma_commit(&s_full[t]);
-        }
+        const bool next = j + 1 < nB;
         if (!sm100::mbar_wait(&v_full[st], (j >> 1) & 1)) { ok = false; break; }
-        const uint32_t v_addr = sm100::smem_u32(sV + st * kAttnTile);
-        for (int t = 0; t < 2; ++t) {
-          if (t == 0 && j >= nA) continue;
-          if (!sm100::mbar_wait(&p_full[t], j & 1)) { ok = false; break; }
+        if (j < nA) {
+          if (!sm100::mbar_wait(&p_full[0], j & 1)) { ok = false; break; }
           sm100::tc_fence_after();
-#pragma unroll
-          for (int k = 0; k < kAttnBN / 16; ++k)
-            sm100::mma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + k * 8,
-                               sm100::sw128_desc(v_addr + k * 16 * 128, 16384, 1024), idesc_o,
-                               (j > 0 || k > 0) ? 1u : 0u);
-          if (j == (t == 0 ? nA : nB) - 1) sm100::mma_commit(&o_done[t]);
+          issue_pv(0, j);
+          if (j + 1 < nA) {
+            if (!sm100::mbar_wait(&k_full[st ^ 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
+            sm100::tc_fence_after();
+            issue_s(0, j + 1);
+          }
         }
-        if (!ok) break;
-        sm100::mma_commit(&kv_empty[st]);
+        if (!sm100::mbar_wait(&p_full[1], j & 1)) { ok = false; break; }
+        sm100::tc_fence_after();
+        issue_pv(1, j);
+        sm100::mma_commit(&kv_empty[st]);   // K_j and V_j are read once PV_B(j) is done
+        if (next) {
+          if (!sm100::mbar_wait(&k_full[st ^ 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
+          sm100::tc_fence_after();
+          issue_s(1, j + 1);
+        }
       }
       if (!ok) *abort_flag = 1;
       sm100::mma_commit(drain);
@@ -418,62 +435,67 @@ __global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __gri
     for (int j = 0; j < ntiles; ++j) {
       if (*abort_flag || !sm100::mbar_wait(&s_full[t], j & 1)) { ok = false; break; }
       sm100::tc_fence_after();
-      const bool masked = g.causal && j == diag;
-      // Pass 1: row max of the raw products (scale > 0 keeps the arg max; masked keys excluded).
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        sm100::tmem_ld32(tS + c * 32, v);
-        sm100::tmem_wait_ld();
+      // The row's 128 products, read from TMEM once.  On the diagonal tile, keys past the query row become
+      // -inf: they never win the max and their exp is 0, as the reference's -1e30 fill gives.
+      uint32_t v[4][32];
 #pragma unroll
-        for (int q = 0; q < 32; ++q) {
-          const float x = __uint_as_float(v[q]);
-          if (!masked || c * 32 + q <= r) mx = fmaxf(mx, x);
-        }
+      for (int c = 0; c < 4; ++c) sm100::tmem_ld32(tS + c * 32, v[c]);
+      sm100::tmem_wait_ld();
+      if (g.causal && j == diag) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int q = 0; q < 32; ++q)
+            if (c * 32 + q > r) v[c][q] = 0xff800000u;
       }
+      // Row max (scale > 0 keeps the arg max), eight independent chains.
+      float mx8[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) mx8[q] = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int q = 0; q < 32; ++q) mx8[q & 7] = fmaxf(mx8[q & 7], __uint_as_float(v[c][q]));
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float m_new = fmaxf(m, __fmul_rn(mx, sc));
       const float alpha = ex2_fast(__fmul_rn(__fsub_rn(m, m_new), kLog2e));
       const float2 a2 = make_float2(sl, sl), b2 = make_float2(-m_new * kLog2e, -m_new * kLog2e);
-      float2 acc = make_float2(0.f, 0.f);
-      // Pass 2: p = exp(qk - m'), row sum, bf16 P packed over the consumed S columns.
-#pragma unroll 1
+      // p = exp(qk - m'): row sum over four chains, bf16 P packed over the consumed S columns.
+      float2 acc[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[i] = make_float2(0.f, 0.f);
+#pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        sm100::tmem_ld32(tS + c * 32, v);
-        sm100::tmem_wait_ld();
         uint32_t pk[16];
 #pragma unroll
         for (int q = 0; q < 16; ++q) {
-          const float2 x = make_float2(__uint_as_float(v[2 * q]), __uint_as_float(v[2 * q + 1]));
-          const float2 u = __ffma2_rn(x, a2, b2);
-          float p0 = ex2_fast(u.x), p1 = ex2_fast(u.y);
-          if (masked) {
-            if (c * 32 + 2 * q > r) p0 = 0.f;
-            if (c * 32 + 2 * q + 1 > r) p1 = 0.f;
-          }
-          acc = __fadd2_rn(acc, make_float2(p0, p1));
+          const float2 u = __ffma2_rn(make_float2(__uint_as_float(v[c][2 * q]), __uint_as_float(v[c][2 * q + 1])), a2, b2);
+          const float p0 = ex2_fast(u.x), p1 = ex2_fast(u.y);
+          acc[q & 3] = __fadd2_rn(acc[q & 3], make_float2(p0, p1));
           pk[q] = pack_bf16x2(p0, p1);
         }
         sm100::tmem_st16(tS + c * 16, pk);
       }
-      l = __fadd_rn(__fmul_rn(l, alpha), __fadd_rn(acc.x, acc.y));
+      const float2 s2 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
+      l = __fadd_rn(__fmul_rn(l, alpha), __fadd_rn(s2.x, s2.y));
       m = m_new;
       // O rescale (O already holds PV_X(j-1): S_X(j) was issued after it).
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
         const float2 al2 = make_float2(alpha, alpha);
-#pragma unroll 1
+        uint32_t o[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) sm100::tmem_ld32(tO + c * 32, o[c]);
+        sm100::tmem_wait_ld();
+#pragma unroll
         for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          sm100::tmem_ld32(tO + c * 32, v);
-          sm100::tmem_wait_ld();
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
-            const float2 o = __fmul2_rn(make_float2(__uint_as_float(v[2 * q]), __uint_as_float(v[2 * q + 1])), al2);
-            v[2 * q] = __float_as_uint(o.x);
-            v[2 * q + 1] = __float_as_uint(o.y);
+            const float2 x = __fmul2_rn(make_float2(__uint_as_float(o[c][2 * q]), __uint_as_float(o[c][2 * q + 1])), al2);
+            o[c][2 * q] = __float_as_uint(x.x);
+            o[c][2 * q + 1] = __float_as_uint(x.y);
           }
-          tmem_st32(tO + c * 32, v);
+          tmem_st32(tO + c * 32, o[c]);
         }
       }
       sm100::tmem_wait_st();
