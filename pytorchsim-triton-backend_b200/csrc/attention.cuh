@@ -458,9 +458,17 @@ __global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __gri
         for (int q = 0; q < 32; ++q) mx8[q & 7] = fmaxf(mx8[q & 7], __uint_as_float(v[c][q]));
       const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                              fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-      const float m_new = fmaxf(m, __fmul_rn(mx, sc));
-      const float alpha = ex2_fast(__fmul_rn(__fsub_rn(m, m_new), kLog2e));
-      const float2 a2 = make_float2(sl, sl), b2 = make_float2(-m_new * kLog2e, -m_new * kLog2e);
+      // Lazy rescaling: the row keeps its reference max m until the tile's max exceeds it by more than
+      // 2^8 (8 in log2 units), so p <= 256 and O is rescaled only when the reference moves.  O / l is
+      // unchanged (numerator and denominator share the reference); only P's bf16 rounding point moves.
+      const float m_cand = fmaxf(m, __fmul_rn(mx, sc));
+      const bool grow = __fmul_rn(__fsub_rn(m_cand, m), kLog2e) > 8.0f;
+      float alpha = 1.0f;
+      if (grow) {
+        alpha = ex2_fast(__fmul_rn(__fsub_rn(m, m_cand), kLog2e));
+        m = m_cand;
+      }
+      const float2 a2 = make_float2(sl, sl), b2 = make_float2(-m * kLog2e, -m * kLog2e);
       // p = exp(qk - m'): row sum over four chains, bf16 P packed over the consumed S columns.
       float2 acc[4];
 #pragma unroll
@@ -479,9 +487,9 @@ __global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __gri
       }
       const float2 s2 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
       l = __fadd_rn(__fmul_rn(l, alpha), __fadd_rn(s2.x, s2.y));
-      m = m_new;
-      // O rescale (O already holds PV_X(j-1): S_X(j) was issued after it).
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+      // O rescale (O already holds PV_X(j-1): S_X(j) was issued after it); lanes that kept their
+      // reference multiply by 1.
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
         const float2 al2 = make_float2(alpha, alpha);
         uint32_t o[4][32];
 #pragma unroll
