@@ -14,6 +14,20 @@
 
 namespace ptsim {
 
+// An index map in 32-bit form, for launches whose flat index space and tensors stay below 2^31
+// elements: each digit's division by an invariant divisor d is a multiply-high and a shift,
+// q = (umulhi(n, m) + n) >> s with s = ceil(log2 d) and m = floor(2^32 (2^s - d) / d) + 1 (Granlund and
+// Montgomery, "Division by invariant integers using multiplication", PLDI 1994; exact for n < 2^31), and
+// a digit that cannot wrap inside the launch skips its modulo.
+struct FastMap {
+  int32_t ndigit;
+  uint32_t offset;
+  uint32_t wrap;  // bit d: digit d can reach its modulus inside the launch
+  uint32_t div_m[PTSIM_MAX_DIGITS], div_s[PTSIM_MAX_DIGITS];
+  uint32_t mod[PTSIM_MAX_DIGITS], mod_m[PTSIM_MAX_DIGITS], mod_s[PTSIM_MAX_DIGITS];
+  uint32_t stride[PTSIM_MAX_DIGITS];
+};
+
 struct EwLaunch {
   ptsim_ew_params p;
   const void *ptr[PTSIM_MAX_ARGS];
@@ -21,7 +35,23 @@ struct EwLaunch {
   int32_t dtype[PTSIM_MAX_ARGS];
   int32_t vec[PTSIM_MAX_MAPS];  // 1: the map is contiguous over every aligned group of 8 indices
   int64_t begin, end;
+  int32_t idx32;                // 1: every index fits 31 bits; fmap[] holds the maps in 32-bit form
+  FastMap fmap[PTSIM_MAX_MAPS];
 };
+
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, uint32_t m, uint32_t s) { return (__umulhi(n, m) + n) >> s; }
+
+__device__ __forceinline__ uint32_t fast_index(const FastMap &m, uint32_t i) {
+  uint32_t idx = m.offset;
+#pragma unroll
+  for (int d = 0; d < PTSIM_MAX_DIGITS; ++d)
+    if (d < m.ndigit) {
+      uint32_t q = fast_div(i, m.div_m[d], m.div_s[d]);
+      if ((m.wrap >> d) & 1u) q -= fast_div(q, m.mod_m[d], m.mod_s[d]) * m.mod[d];
+      idx += q * m.stride[d];
+    }
+  return idx;
+}
 
 __device__ __forceinline__ int64_t map_index(const ptsim_map &m, int64_t i) {
   int64_t idx = m.offset;
@@ -29,6 +59,11 @@ __device__ __forceinline__ int64_t map_index(const ptsim_map &m, int64_t i) {
   for (int d = 0; d < PTSIM_MAX_DIGITS; ++d)
     if (d < m.ndigit) idx += ((i / m.div[d]) % m.mod[d]) * m.stride[d];
   return idx;
+}
+
+// Element index of flat index i through map mi of the launch.
+__device__ __forceinline__ int64_t ew_index(const EwLaunch &L, int mi, int64_t i) {
+  return L.idx32 ? int64_t(fast_index(L.fmap[mi], uint32_t(i))) : map_index(L.p.map[mi], i);
 }
 
 __device__ __forceinline__ float load_elem(const void *p, int dt, int64_t idx) {
@@ -66,7 +101,7 @@ __device__ __forceinline__ void load8(const EwLaunch &L, int mi, int64_t i0, int
   const void *p = L.ptr[m.arg];
   const int dt = L.dtype[m.arg];
   if (n == 8 && L.vec[mi]) {
-    const int64_t base = map_index(m, i0);
+    const int64_t base = ew_index(L, mi, i0);
     if (base < 0 || base + 8 > L.numel[m.arg]) { record_status(PTSIM_E_OOB); for (int k = 0; k < 8; ++k) v[k] = 0.f; return; }
     if (dt == PTSIM_DT_BF16) {
       uint4 w = __ldg(reinterpret_cast<const uint4 *>(reinterpret_cast<const unsigned short *>(p) + base));
@@ -85,7 +120,7 @@ __device__ __forceinline__ void load8(const EwLaunch &L, int mi, int64_t i0, int
   for (int k = 0; k < 8; ++k) {
     v[k] = 0.f;
     if (k < n) {
-      const int64_t idx = map_index(m, i0 + k);
+      const int64_t idx = ew_index(L, mi, i0 + k);
       if (idx < 0 || idx >= L.numel[m.arg]) { record_status(PTSIM_E_OOB); continue; }
       v[k] = load_elem(p, dt, idx);
     }
@@ -97,7 +132,7 @@ __device__ __forceinline__ void store8(const EwLaunch &L, int64_t i0, int n, con
   void *p = const_cast<void *>(L.ptr[m.arg]);
   const int dt = L.dtype[m.arg];
   if (n == 8 && L.vec[L.p.store_map]) {
-    const int64_t base = map_index(m, i0);
+    const int64_t base = ew_index(L, L.p.store_map, i0);
     if (base < 0 || base + 8 > L.numel[m.arg]) { record_status(PTSIM_E_OOB); return; }
     if (dt == PTSIM_DT_BF16) {
       uint4 w;
@@ -116,7 +151,7 @@ __device__ __forceinline__ void store8(const EwLaunch &L, int64_t i0, int n, con
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     if (k < n) {
-      const int64_t idx = map_index(m, i0 + k);
+      const int64_t idx = ew_index(L, L.p.store_map, i0 + k);
       if (idx < 0 || idx >= L.numel[m.arg]) { record_status(PTSIM_E_OOB); continue; }
       store_elem(p, dt, idx, v[k]);
     }
@@ -196,6 +231,134 @@ __global__ void __launch_bounds__(256) ew_program_kernel(const __grid_constant__
   }
 }
 
+// ---------------------------------------------------------------------------------------------------
+// The program shapes the validation configurations run, unrolled instead of interpreted (no per-op
+// dispatch, no register-file selects).  Each performs the interpreter's operations in the same order,
+// so the results are the same bits:
+//   EW_BINOP     load a; load b; c = a op b; store c               (vector add, smoke add)
+//   EW_SCALAR    load a; const k; c = a op k (or k op a); store c  (vector_add1: x + 1)
+//   EW_SILU_MUL  load g; t = exp(-g); s = t + 1; q = g / s; load u; o = q * u; store o  (Qwen3 10)
+// The host matches a descriptor's code against these shapes exactly (registers, operands, constant);
+// anything else runs on the interpreter.
+// ---------------------------------------------------------------------------------------------------
+enum { EW_VM = 0, EW_BINOP = 1, EW_SCALAR = 2, EW_SILU_MUL = 3 };
+
+struct EwPattern {
+  int32_t kind;
+  int32_t op;           // PTSIM_OP_* of the binary operation (BINOP, SCALAR)
+  int32_t map_a, map_b; // BINOP: a op b; SCALAR: map_a is the tensor operand; SILU_MUL: gate, up
+  int32_t const_first;  // SCALAR: the constant is the left operand
+  float imm;
+};
+
+template <int OP>
+__device__ __forceinline__ float ew_op(float a, float b) {
+  if constexpr (OP == PTSIM_OP_ADD) return __fadd_rn(a, b);
+  else if constexpr (OP == PTSIM_OP_SUB) return __fsub_rn(a, b);
+  else if constexpr (OP == PTSIM_OP_MUL) return __fmul_rn(a, b);
+  else if constexpr (OP == PTSIM_OP_DIV) return __fdiv_rn(a, b);
+  else if constexpr (OP == PTSIM_OP_MAX) return nan_max(a, b);
+  else return nan_min(a, b);
+}
+
+template <int OP>
+__device__ __forceinline__ void ew_binop8(const float a[8], const float b[8], float o[8]) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) o[k] = ew_op<OP>(a[k], b[k]);
+}
+
+__device__ __forceinline__ void ew_dispatch8(int op, const float a[8], const float b[8], float o[8]) {
+  switch (op) {
+    case PTSIM_OP_ADD: ew_binop8<PTSIM_OP_ADD>(a, b, o); break;
+    case PTSIM_OP_SUB: ew_binop8<PTSIM_OP_SUB>(a, b, o); break;
+    case PTSIM_OP_MUL: ew_binop8<PTSIM_OP_MUL>(a, b, o); break;
+    case PTSIM_OP_DIV: ew_binop8<PTSIM_OP_DIV>(a, b, o); break;
+    case PTSIM_OP_MAX: ew_binop8<PTSIM_OP_MAX>(a, b, o); break;
+    default: ew_binop8<PTSIM_OP_MIN>(a, b, o); break;
+  }
+}
+
+template <int KIND>
+__global__ void __launch_bounds__(256) ew_pattern_kernel(const __grid_constant__ EwLaunch L, const EwPattern P) {
+  const int64_t groups = ceil_div(L.end - L.begin, 8);
+  for (int64_t g = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; g < groups; g += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t i0 = L.begin + g * 8;
+    const int n = int((L.end - i0) < 8 ? (L.end - i0) : 8);
+    float a[8], b[8], o[8];
+    load8(L, P.map_a, i0, n, a);
+    if constexpr (KIND == EW_BINOP) {
+      load8(L, P.map_b, i0, n, b);
+      ew_dispatch8(P.op, a, b, o);
+    } else if constexpr (KIND == EW_SCALAR) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) b[k] = P.imm;
+      if (P.const_first) ew_dispatch8(P.op, b, a, o);
+      else ew_dispatch8(P.op, a, b, o);
+    } else {
+      load8(L, P.map_b, i0, n, b);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float t = npu_exp(-a[k]);
+        const float q = __fdiv_rn(a[k], __fadd_rn(t, 1.0f));
+        o[k] = __fmul_rn(q, b[k]);
+      }
+    }
+    store8(L, i0, n, o);
+  }
+}
+
+// Which unrolled shape runs descriptor program p (EW_VM: none).
+static EwPattern match_pattern(const ptsim_ew_params &p) {
+  EwPattern P;
+  memset(&P, 0, sizeof(P));
+  P.kind = EW_VM;
+  const ptsim_insn *c = p.code;
+  auto binop = [](int op) {
+    return op == PTSIM_OP_ADD || op == PTSIM_OP_SUB || op == PTSIM_OP_MUL || op == PTSIM_OP_DIV ||
+           op == PTSIM_OP_MAX || op == PTSIM_OP_MIN;
+  };
+  auto map_ok = [&](int m) { return m >= 0 && m < p.nmap && m != p.store_map; };
+  if (p.ncode == 4 && c[0].op == PTSIM_OP_LOAD && c[3].op == PTSIM_OP_STORE && binop(c[2].op) && c[3].a == c[2].dst &&
+      map_ok(c[0].a)) {
+    const int ra = c[0].dst;
+    if (c[1].op == PTSIM_OP_LOAD && map_ok(c[1].a) && c[1].dst != ra) {
+      const int rb = c[1].dst;
+      if (c[2].a == ra && c[2].b == rb) { P.kind = EW_BINOP; P.map_a = c[0].a; P.map_b = c[1].a; }
+      else if (c[2].a == rb && c[2].b == ra) { P.kind = EW_BINOP; P.map_a = c[1].a; P.map_b = c[0].a; }
+      P.op = c[2].op;
+    } else if (c[1].op == PTSIM_OP_CONST && c[1].dst != ra) {
+      const int rk = c[1].dst;
+      if ((c[2].a == ra && c[2].b == rk) || (c[2].a == rk && c[2].b == ra)) {
+        P.kind = EW_SCALAR;
+        P.map_a = c[0].a;
+        P.const_first = c[2].a == rk;
+        P.imm = c[1].imm;
+        P.op = c[2].op;
+      }
+    }
+  }
+  if (p.ncode == 9) {
+    const int rg = c[0].dst;
+    const bool ok = c[0].op == PTSIM_OP_LOAD && map_ok(c[0].a) &&
+                    c[1].op == PTSIM_OP_NEG && c[1].a == rg && c[1].dst != rg &&
+                    c[2].op == PTSIM_OP_EXP && c[2].a == c[1].dst && c[2].dst != rg &&
+                    c[3].op == PTSIM_OP_CONST && c[3].imm == 1.0f && c[3].dst != rg && c[3].dst != c[2].dst &&
+                    c[4].op == PTSIM_OP_ADD && c[4].dst != rg &&
+                    ((c[4].a == c[2].dst && c[4].b == c[3].dst) || (c[4].a == c[3].dst && c[4].b == c[2].dst)) &&
+                    c[5].op == PTSIM_OP_DIV && c[5].a == rg && c[5].b == c[4].dst &&
+                    c[6].op == PTSIM_OP_LOAD && map_ok(c[6].a) && c[6].dst != c[5].dst &&
+                    c[7].op == PTSIM_OP_MUL &&
+                    ((c[7].a == c[5].dst && c[7].b == c[6].dst) || (c[7].a == c[6].dst && c[7].b == c[5].dst)) &&
+                    c[8].op == PTSIM_OP_STORE && c[8].a == c[7].dst;
+    if (ok) {
+      P.kind = EW_SILU_MUL;
+      P.map_a = c[0].a;
+      P.map_b = c[6].a;
+    }
+  }
+  return P;
+}
+
 // Pure copy: the loaded element's bytes go to the store unchanged (bit exact for every dtype).
 template <int ESIZE>
 __global__ void __launch_bounds__(256) ew_copy_kernel(const __grid_constant__ EwLaunch L) {
@@ -213,7 +376,7 @@ __global__ void __launch_bounds__(256) ew_copy_kernel(const __grid_constant__ Ew
     const int n = int((L.end - i0) < 8 ? (L.end - i0) : 8);
     T v[8];
     if (n == 8 && vs) {
-      const int64_t b = map_index(src, i0);
+      const int64_t b = ew_index(L, 0, i0);
       if (b < 0 || b + 8 > L.numel[src.arg]) { record_status(PTSIM_E_OOB); continue; }
       *reinterpret_cast<uint4 *>(v) = __ldg(reinterpret_cast<const uint4 *>(sp + b));
     } else {
@@ -221,21 +384,21 @@ __global__ void __launch_bounds__(256) ew_copy_kernel(const __grid_constant__ Ew
       for (int k = 0; k < 8; ++k) {
         v[k] = 0;
         if (k < n) {
-          const int64_t idx = map_index(src, i0 + k);
+          const int64_t idx = ew_index(L, 0, i0 + k);
           if (idx < 0 || idx >= L.numel[src.arg]) { record_status(PTSIM_E_OOB); continue; }
           v[k] = sp[idx];
         }
       }
     }
     if (n == 8 && vd) {
-      const int64_t b = map_index(dst, i0);
+      const int64_t b = ew_index(L, L.p.store_map, i0);
       if (b < 0 || b + 8 > L.numel[dst.arg]) { record_status(PTSIM_E_OOB); continue; }
       *reinterpret_cast<uint4 *>(dp + b) = *reinterpret_cast<uint4 *>(v);
     } else {
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         if (k < n) {
-          const int64_t idx = map_index(dst, i0 + k);
+          const int64_t idx = ew_index(L, L.p.store_map, i0 + k);
           if (idx < 0 || idx >= L.numel[dst.arg]) { record_status(PTSIM_E_OOB); continue; }
           dp[idx] = v[k];
         }
@@ -258,6 +421,49 @@ static bool map_vectorizable(const ptsim_map &m, int dt, const void *ptr) {
   return dt == PTSIM_DT_BF16 || dt == PTSIM_DT_F32 || (dt == PTSIM_DT_F16);
 }
 
+// Multiply-high reciprocal of divisor d (see FastMap).
+static void fast_divisor(uint32_t d, uint32_t *m, uint32_t *s) {
+  uint32_t sh = 0;
+  while ((uint64_t(1) << sh) < d) ++sh;
+  *s = sh;
+  *m = uint32_t(((uint64_t(1) << 32) * ((uint64_t(1) << sh) - d)) / d + 1);
+}
+
+// Fill L.fmap and set L.idx32 when every flat index, offset, stride and tensor fits 31 bits.
+static void build_fast_maps(EwLaunch &L) {
+  const int64_t lim = int64_t(1) << 31;
+  L.idx32 = 0;
+  if (L.end + 8 > lim) return;
+  for (int a = 0; a < PTSIM_MAX_ARGS; ++a)
+    if (L.numel[a] >= lim) return;
+  for (int mi = 0; mi < L.p.nmap; ++mi) {
+    const ptsim_map &m = L.p.map[mi];
+    FastMap &f = L.fmap[mi];
+    memset(&f, 0, sizeof(f));
+    if (m.offset < 0 || m.offset >= lim || m.ndigit < 0 || m.ndigit > PTSIM_MAX_DIGITS) return;
+    f.ndigit = m.ndigit;
+    f.offset = uint32_t(m.offset);
+    int64_t reach = m.offset;   // largest index the map produces inside the launch
+    for (int d = 0; d < m.ndigit; ++d) {
+      if (m.div[d] < 1 || m.div[d] >= lim || m.mod[d] < 1 || m.stride[d] < 0 || m.stride[d] >= lim) return;
+      fast_divisor(uint32_t(m.div[d]), &f.div_m[d], &f.div_s[d]);
+      // The digit's quotient over the launch is at most (end - 1) / div; no modulo when that stays
+      // below the modulus.
+      const int64_t top = (L.end - 1) / m.div[d];
+      reach += (top < m.mod[d] - 1 ? top : m.mod[d] - 1) * m.stride[d];
+      if (reach >= lim) return;
+      if (top >= m.mod[d]) {
+        if (m.mod[d] >= lim) return;
+        f.wrap |= 1u << d;
+        f.mod[d] = uint32_t(m.mod[d]);
+        fast_divisor(f.mod[d], &f.mod_m[d], &f.mod_s[d]);
+      }
+      f.stride[d] = uint32_t(m.stride[d]);
+    }
+  }
+  L.idx32 = 1;
+}
+
 int launch_elementwise(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c) {
   EwLaunch L;
   memset(&L, 0, sizeof(L));
@@ -271,6 +477,7 @@ int launch_elementwise(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64
   L.end = hi * d.unit_size < d.p.ew.numel ? hi * d.unit_size : d.p.ew.numel;
   if (L.end <= L.begin) return PTSIM_OK;
   const bool aligned = (L.begin % 8) == 0;
+  build_fast_maps(L);
   for (int m = 0; m < L.p.nmap; ++m) {
     const int dt = d.arg_dtype[L.p.map[m].arg];
     L.vec[m] = aligned && map_vectorizable(L.p.map[m], dt, ptrs[L.p.map[m].arg]) ? 1 : 0;
@@ -290,6 +497,10 @@ int launch_elementwise(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64
       case 8: ew_copy_kernel<8><<<unsigned(blocks), threads, 0, c.stream>>>(L); break;
       default: return fail(PTSIM_E_DESC, "elementwise copy of a %d-byte element", es);
     }
+  } else if (const EwPattern P = match_pattern(L.p); P.kind != EW_VM) {
+    if (P.kind == EW_BINOP) ew_pattern_kernel<EW_BINOP><<<unsigned(blocks), threads, 0, c.stream>>>(L, P);
+    else if (P.kind == EW_SCALAR) ew_pattern_kernel<EW_SCALAR><<<unsigned(blocks), threads, 0, c.stream>>>(L, P);
+    else ew_pattern_kernel<EW_SILU_MUL><<<unsigned(blocks), threads, 0, c.stream>>>(L, P);
   } else {
     int top = 0;
     for (int i = 0; i < L.p.ncode; ++i) {
