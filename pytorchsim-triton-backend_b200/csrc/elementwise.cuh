@@ -278,29 +278,180 @@ __device__ __forceinline__ void ew_dispatch8(int op, const float a[8], const flo
   }
 }
 
-template <int KIND>
+// NG groups of 8 per thread per step, all loads issued before any arithmetic (more bytes in flight per
+// SM); group u of a block's step is u * blockDim + threadIdx, so every load instruction of a warp is one
+// contiguous run.
+template <int KIND, int NG>
 __global__ void __launch_bounds__(256) ew_pattern_kernel(const __grid_constant__ EwLaunch L, const EwPattern P) {
   const int64_t groups = ceil_div(L.end - L.begin, 8);
-  for (int64_t g = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; g < groups; g += int64_t(gridDim.x) * blockDim.x) {
-    const int64_t i0 = L.begin + g * 8;
-    const int n = int((L.end - i0) < 8 ? (L.end - i0) : 8);
-    float a[8], b[8], o[8];
-    load8(L, P.map_a, i0, n, a);
+  const int64_t step = int64_t(gridDim.x) * blockDim.x * NG;
+  for (int64_t g0 = int64_t(blockIdx.x) * blockDim.x * NG + threadIdx.x; g0 < groups; g0 += step) {
+    float a[NG][8], b[NG][8];
+#pragma unroll
+    for (int u = 0; u < NG; ++u) {
+      const int64_t g = g0 + int64_t(u) * blockDim.x;
+      if (g < groups) {
+        const int64_t i0 = L.begin + g * 8;
+        const int n = int((L.end - i0) < 8 ? (L.end - i0) : 8);
+        load8(L, P.map_a, i0, n, a[u]);
+        if constexpr (KIND != EW_SCALAR) load8(L, P.map_b, i0, n, b[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < NG; ++u) {
+      const int64_t g = g0 + int64_t(u) * blockDim.x;
+      if (g >= groups) break;
+      const int64_t i0 = L.begin + g * 8;
+      const int n = int((L.end - i0) < 8 ? (L.end - i0) : 8);
+      float o[8];
+      if constexpr (KIND == EW_BINOP) {
+        ew_dispatch8(P.op, a[u], b[u], o);
+      } else if constexpr (KIND == EW_SCALAR) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) b[u][k] = P.imm;
+        if (P.const_first) ew_dispatch8(P.op, b[u], a[u], o);
+        else ew_dispatch8(P.op, a[u], b[u], o);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float t = npu_exp(-a[u][k]);
+          const float q = __fdiv_rn(a[u][k], __fadd_rn(t, 1.0f));
+          o[k] = __fmul_rn(q, b[u][k]);
+        }
+      }
+      store8(L, i0, n, o);
+    }
+  }
+}
+
+// Vector path of the same shapes: every map of the program contiguous and 16-byte aligned over each group
+// of 8 and all tensors of one dtype (bf16 or fp32).  Groups stay packed in registers until the
+// arithmetic (4 registers per bf16 group, 8 per fp32 group); a block of 256 threads takes 256 x NG
+// consecutive groups, all loads issued before any arithmetic, and the grid has one block per such run so
+// the scheduler keeps every SM full (as the row-per-CTA kernel does).  The ragged last group, if any,
+// takes the general path.
+template <int DT>
+struct RawGroup {
+  uint4 w[DT == PTSIM_DT_F32 ? 2 : 1];
+};
+
+template <int DT>
+__device__ __forceinline__ bool raw_load(const EwLaunch &L, int mi, int64_t i0, RawGroup<DT> &r) {
+  const int arg = L.p.map[mi].arg;
+  const int64_t base = ew_index(L, mi, i0);
+  if (base < 0 || base + 8 > L.numel[arg]) {
+    record_status(PTSIM_E_OOB);
+    return false;
+  }
+  const uint4 *q = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint8_t *>(L.ptr[arg]) + base * (DT == PTSIM_DT_F32 ? 4 : 2));
+  r.w[0] = __ldg(q);
+  if constexpr (DT == PTSIM_DT_F32) r.w[1] = __ldg(q + 1);
+  return true;
+}
+
+template <int DT>
+__device__ __forceinline__ void raw_unpack(const RawGroup<DT> &r, float v[8]) {
+  if constexpr (DT == PTSIM_DT_F32) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      v[4 * h] = __uint_as_float(r.w[h].x);
+      v[4 * h + 1] = __uint_as_float(r.w[h].y);
+      v[4 * h + 2] = __uint_as_float(r.w[h].z);
+      v[4 * h + 3] = __uint_as_float(r.w[h].w);
+    }
+  } else {
+    const uint32_t ws[4] = {r.w[0].x, r.w[0].y, r.w[0].z, r.w[0].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[2 * j] = lo_bf16(ws[j]);
+      v[2 * j + 1] = hi_bf16(ws[j]);
+    }
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ void raw_store(const EwLaunch &L, int64_t i0, const float v[8]) {
+  const int mi = L.p.store_map;
+  const int arg = L.p.map[mi].arg;
+  const int64_t base = ew_index(L, mi, i0);
+  if (base < 0 || base + 8 > L.numel[arg]) {
+    record_status(PTSIM_E_OOB);
+    return;
+  }
+  uint4 *q = reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(const_cast<void *>(L.ptr[arg])) + base * (DT == PTSIM_DT_F32 ? 4 : 2));
+  if constexpr (DT == PTSIM_DT_F32) {
+    __stcs(q, make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]), __float_as_uint(v[3])));
+    __stcs(q + 1, make_uint4(__float_as_uint(v[4]), __float_as_uint(v[5]), __float_as_uint(v[6]), __float_as_uint(v[7])));
+  } else {
+    __stcs(q, make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7])));
+  }
+}
+
+template <int KIND, int NG, int DT>
+__global__ void __launch_bounds__(256, 6) ew_vpattern_kernel(const __grid_constant__ EwLaunch L, const EwPattern P) {
+  const int64_t full = (L.end - L.begin) / 8;   // groups of 8 inside the launch
+  // One block per 256 x NG groups (the scheduler backfills blocks as they finish).
+  {
+    const int64_t g0 = int64_t(blockIdx.x) * blockDim.x * NG + threadIdx.x;
+    RawGroup<DT> a[NG], b[NG];
+    bool ok[NG];
+#pragma unroll
+    for (int u = 0; u < NG; ++u) {
+      const int64_t g = g0 + int64_t(u) * blockDim.x;
+      ok[u] = g < full;
+      if (ok[u]) {
+        const int64_t i0 = L.begin + g * 8;
+        ok[u] = raw_load<DT>(L, P.map_a, i0, a[u]);
+        if constexpr (KIND != EW_SCALAR) ok[u] = raw_load<DT>(L, P.map_b, i0, b[u]) && ok[u];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < NG; ++u) {
+      if (!ok[u]) continue;
+      const int64_t i0 = L.begin + (g0 + int64_t(u) * blockDim.x) * 8;
+      float x[8], y[8], o[8];
+      raw_unpack<DT>(a[u], x);
+      if constexpr (KIND == EW_BINOP) {
+        raw_unpack<DT>(b[u], y);
+        ew_dispatch8(P.op, x, y, o);
+      } else if constexpr (KIND == EW_SCALAR) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) y[k] = P.imm;
+        if (P.const_first) ew_dispatch8(P.op, y, x, o);
+        else ew_dispatch8(P.op, x, y, o);
+      } else {
+        raw_unpack<DT>(b[u], y);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float t = npu_exp(-x[k]);
+          const float q = __fdiv_rn(x[k], __fadd_rn(t, 1.0f));
+          o[k] = __fmul_rn(q, y[k]);
+        }
+      }
+      raw_store<DT>(L, i0, o);
+    }
+  }
+  // The ragged last group.
+  if (blockIdx.x == 0 && threadIdx.x == 0 && L.begin + full * 8 < L.end) {
+    const int64_t i0 = L.begin + full * 8;
+    const int n = int(L.end - i0);
+    float x[8], y[8], o[8];
+    load8(L, P.map_a, i0, n, x);
     if constexpr (KIND == EW_BINOP) {
-      load8(L, P.map_b, i0, n, b);
-      ew_dispatch8(P.op, a, b, o);
+      load8(L, P.map_b, i0, n, y);
+      ew_dispatch8(P.op, x, y, o);
     } else if constexpr (KIND == EW_SCALAR) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) b[k] = P.imm;
-      if (P.const_first) ew_dispatch8(P.op, b, a, o);
-      else ew_dispatch8(P.op, a, b, o);
+      for (int k = 0; k < 8; ++k) y[k] = P.imm;
+      if (P.const_first) ew_dispatch8(P.op, y, x, o);
+      else ew_dispatch8(P.op, x, y, o);
     } else {
-      load8(L, P.map_b, i0, n, b);
+      load8(L, P.map_b, i0, n, y);
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        const float t = npu_exp(-a[k]);
-        const float q = __fdiv_rn(a[k], __fadd_rn(t, 1.0f));
-        o[k] = __fmul_rn(q, b[k]);
+        const float t = npu_exp(-x[k]);
+        const float q = __fdiv_rn(x[k], __fadd_rn(t, 1.0f));
+        o[k] = __fmul_rn(q, y[k]);
       }
     }
     store8(L, i0, n, o);
@@ -498,9 +649,32 @@ int launch_elementwise(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64
       default: return fail(PTSIM_E_DESC, "elementwise copy of a %d-byte element", es);
     }
   } else if (const EwPattern P = match_pattern(L.p); P.kind != EW_VM) {
-    if (P.kind == EW_BINOP) ew_pattern_kernel<EW_BINOP><<<unsigned(blocks), threads, 0, c.stream>>>(L, P);
-    else if (P.kind == EW_SCALAR) ew_pattern_kernel<EW_SCALAR><<<unsigned(blocks), threads, 0, c.stream>>>(L, P);
-    else ew_pattern_kernel<EW_SILU_MUL><<<unsigned(blocks), threads, 0, c.stream>>>(L, P);
+    // Vector path when every map of the shape is contiguous and aligned and all tensors share one dtype.
+    const int dt = d.arg_dtype[L.p.map[P.map_a].arg];
+    bool vec = (dt == PTSIM_DT_BF16 || dt == PTSIM_DT_F32) && L.vec[P.map_a] && L.vec[L.p.store_map] &&
+               d.arg_dtype[L.p.map[L.p.store_map].arg] == dt;
+    if (P.kind != EW_SCALAR) vec = vec && L.vec[P.map_b] && d.arg_dtype[L.p.map[P.map_b].arg] == dt;
+    if (vec) {
+      const int ng = 2;
+      const int64_t pb = ceil_div(groups, int64_t(threads) * ng);
+      if (pb > int64_t(0x7fffffff)) return fail(PTSIM_E_UNSUPPORTED, "elementwise launch of %lld groups", (long long)groups);
+      const unsigned gb = unsigned(pb < 1 ? 1 : pb);
+      if (dt == PTSIM_DT_BF16) {
+        if (P.kind == EW_BINOP) ew_vpattern_kernel<EW_BINOP, 2, PTSIM_DT_BF16><<<gb, threads, 0, c.stream>>>(L, P);
+        else if (P.kind == EW_SCALAR) ew_vpattern_kernel<EW_SCALAR, 2, PTSIM_DT_BF16><<<gb, threads, 0, c.stream>>>(L, P);
+        else ew_vpattern_kernel<EW_SILU_MUL, 2, PTSIM_DT_BF16><<<gb, threads, 0, c.stream>>>(L, P);
+      } else {
+        if (P.kind == EW_BINOP) ew_vpattern_kernel<EW_BINOP, 2, PTSIM_DT_F32><<<gb, threads, 0, c.stream>>>(L, P);
+        else if (P.kind == EW_SCALAR) ew_vpattern_kernel<EW_SCALAR, 2, PTSIM_DT_F32><<<gb, threads, 0, c.stream>>>(L, P);
+        else ew_vpattern_kernel<EW_SILU_MUL, 2, PTSIM_DT_F32><<<gb, threads, 0, c.stream>>>(L, P);
+      }
+    } else {
+      int64_t pb = ceil_div(groups, int64_t(threads) * 2);
+      if (pb > cap) pb = cap;
+      if (P.kind == EW_BINOP) ew_pattern_kernel<EW_BINOP, 2><<<unsigned(pb), threads, 0, c.stream>>>(L, P);
+      else if (P.kind == EW_SCALAR) ew_pattern_kernel<EW_SCALAR, 2><<<unsigned(pb), threads, 0, c.stream>>>(L, P);
+      else ew_pattern_kernel<EW_SILU_MUL, 2><<<unsigned(pb), threads, 0, c.stream>>>(L, P);
+    }
   } else {
     int top = 0;
     for (int i = 0; i < L.p.ncode; ++i) {
