@@ -567,13 +567,13 @@ int launch_attention(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t
   g.scale = a.scale;
   if (int64_t(a.batch * a.hkv * a.seq) >= (int64_t(1) << 31)) return fail(PTSIM_E_UNSUPPORTED, "attention rows exceed int32");
   if (a.seq % (2 * kAttnBM) == 0 && getenv("PTSIM_ATTN_V1") == nullptr) {
-    PTSIM_CUDA(cudaFuncSetAttribute(attn2_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttn2Smem));
+    PTSIM_CUDA(smem_limit_once<attn2_fwd_kernel>(kAttn2Smem, c.device));
     const int64_t grid = (u1 - u0) * (g.q_tiles / 2);
     attn2_fwd_kernel<<<unsigned(grid), kAttn2Threads, kAttn2Smem, c.stream>>>(g);
     PTSIM_CUDA(cudaGetLastError());
     return PTSIM_OK;
   }
-  PTSIM_CUDA(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
+  PTSIM_CUDA(smem_limit_once<attn_fwd_kernel>(kAttnSmem, c.device));
   const int64_t grid = (u1 - u0) * g.q_tiles;
   attn_fwd_kernel<<<unsigned(grid), kAttnThreads, kAttnSmem, c.stream>>>(g);
   PTSIM_CUDA(cudaGetLastError());

@@ -2,6 +2,7 @@
 // the per-device status word kernels report failures through, and bounded waits.
 #pragma once
 
+#include <atomic>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -92,6 +93,18 @@ struct LaunchCtx {
 int fail(int code, const char *fmt, ...);
 
 // Checks a CUDA call's result; on failure records the message and returns PTSIM_E_CUDA.
+// Raise a kernel's dynamic shared memory limit once per device (the attribute is per function and
+// device; setting it on every launch costs a driver round trip in front of each launch).
+template <auto Kern>
+inline cudaError_t smem_limit_once(int bytes, int device) {
+  static std::atomic<uint64_t> done{0};   // one per kernel function (Kern is a template argument)
+  const uint64_t bit = (device >= 0 && device < 64) ? (uint64_t(1) << device) : 0;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
+
 #define PTSIM_CUDA(call)                                                                   \
   do {                                                                                     \
     cudaError_t _e = (call);                                                               \

@@ -325,27 +325,37 @@ __global__ void __launch_bounds__(256) ew_pattern_kernel(const __grid_constant__
 }
 
 // Vector path of the same shapes: every map of the program contiguous and 16-byte aligned over each group
-// of 8 and all tensors of one dtype (bf16 or fp32).  Groups stay packed in registers until the
-// arithmetic (4 registers per bf16 group, 8 per fp32 group); a block of 256 threads takes 256 x NG
-// consecutive groups, all loads issued before any arithmetic, and the grid has one block per such run so
-// the scheduler keeps every SM full (as the row-per-CTA kernel does).  The ragged last group, if any,
-// takes the general path.
+// of 8, all tensors of one dtype (bf16 or fp32), every index below 2^31.  The kernel gets its own small
+// parameter block with the operands' pointers, 32-bit maps and bounds resolved on the host, so it reads
+// only fixed parameter offsets.  Groups stay packed in registers until the arithmetic (4 registers per
+// bf16 group, 8 per fp32 group); a block of 256 threads takes 256 x NG consecutive groups, all loads
+// issued before any arithmetic, and the grid has one block per such run so the scheduler keeps every SM
+// full (as the row-per-CTA kernel does).  The ragged last group, if any, is finished element by element.
+struct EwVec {
+  const void *a, *b;
+  void *o;
+  FastMap ma, mb, mo;
+  uint32_t na, nb, no;     // tensor sizes (elements) for the bounds checks
+  uint32_t begin, end;     // flat index range of the launch
+  int32_t op, const_first;
+  float imm;
+};
+
 template <int DT>
 struct RawGroup {
   uint4 w[DT == PTSIM_DT_F32 ? 2 : 1];
 };
 
 template <int DT>
-__device__ __forceinline__ bool raw_load(const EwLaunch &L, int mi, int64_t i0, RawGroup<DT> &r) {
-  const int arg = L.p.map[mi].arg;
-  const int64_t base = ew_index(L, mi, i0);
-  if (base < 0 || base + 8 > L.numel[arg]) {
+__device__ __forceinline__ bool raw_load(const void *p, const FastMap &m, uint32_t n, uint32_t i0, RawGroup<DT> &r) {
+  const uint32_t base = fast_index(m, i0);
+  if (base + 8 > n) {
     record_status(PTSIM_E_OOB);
     return false;
   }
-  const uint4 *q = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint8_t *>(L.ptr[arg]) + base * (DT == PTSIM_DT_F32 ? 4 : 2));
-  r.w[0] = __ldg(q);
-  if constexpr (DT == PTSIM_DT_F32) r.w[1] = __ldg(q + 1);
+  const uint4 *q = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint8_t *>(p) + size_t(base) * (DT == PTSIM_DT_F32 ? 4 : 2));
+  r.w[0] = __ldcs(q);
+  if constexpr (DT == PTSIM_DT_F32) r.w[1] = __ldcs(q + 1);
   return true;
 }
 
@@ -370,15 +380,13 @@ __device__ __forceinline__ void raw_unpack(const RawGroup<DT> &r, float v[8]) {
 }
 
 template <int DT>
-__device__ __forceinline__ void raw_store(const EwLaunch &L, int64_t i0, const float v[8]) {
-  const int mi = L.p.store_map;
-  const int arg = L.p.map[mi].arg;
-  const int64_t base = ew_index(L, mi, i0);
-  if (base < 0 || base + 8 > L.numel[arg]) {
+__device__ __forceinline__ void raw_store(const EwVec &V, uint32_t i0, const float v[8]) {
+  const uint32_t base = fast_index(V.mo, i0);
+  if (base + 8 > V.no) {
     record_status(PTSIM_E_OOB);
     return;
   }
-  uint4 *q = reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(const_cast<void *>(L.ptr[arg])) + base * (DT == PTSIM_DT_F32 ? 4 : 2));
+  uint4 *q = reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(V.o) + size_t(base) * (DT == PTSIM_DT_F32 ? 4 : 2));
   if constexpr (DT == PTSIM_DT_F32) {
     __stcs(q, make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]), __float_as_uint(v[3])));
     __stcs(q + 1, make_uint4(__float_as_uint(v[4]), __float_as_uint(v[5]), __float_as_uint(v[6]), __float_as_uint(v[7])));
@@ -387,74 +395,69 @@ __device__ __forceinline__ void raw_store(const EwLaunch &L, int64_t i0, const f
   }
 }
 
-template <int KIND, int NG, int DT>
-__global__ void __launch_bounds__(256, 6) ew_vpattern_kernel(const __grid_constant__ EwLaunch L, const EwPattern P) {
-  const int64_t full = (L.end - L.begin) / 8;   // groups of 8 inside the launch
-  // One block per 256 x NG groups (the scheduler backfills blocks as they finish).
-  {
-    const int64_t g0 = int64_t(blockIdx.x) * blockDim.x * NG + threadIdx.x;
-    RawGroup<DT> a[NG], b[NG];
-    bool ok[NG];
+template <int KIND>
+__device__ __forceinline__ void vpattern_math(const EwVec &V, float x[8], float y[8], float o[8]) {
+  if constexpr (KIND == EW_BINOP) {
+    ew_dispatch8(V.op, x, y, o);
+  } else if constexpr (KIND == EW_SCALAR) {
 #pragma unroll
-    for (int u = 0; u < NG; ++u) {
-      const int64_t g = g0 + int64_t(u) * blockDim.x;
-      ok[u] = g < full;
-      if (ok[u]) {
-        const int64_t i0 = L.begin + g * 8;
-        ok[u] = raw_load<DT>(L, P.map_a, i0, a[u]);
-        if constexpr (KIND != EW_SCALAR) ok[u] = raw_load<DT>(L, P.map_b, i0, b[u]) && ok[u];
-      }
-    }
+    for (int k = 0; k < 8; ++k) y[k] = V.imm;
+    if (V.const_first) ew_dispatch8(V.op, y, x, o);
+    else ew_dispatch8(V.op, x, y, o);
+  } else {
 #pragma unroll
-    for (int u = 0; u < NG; ++u) {
-      if (!ok[u]) continue;
-      const int64_t i0 = L.begin + (g0 + int64_t(u) * blockDim.x) * 8;
-      float x[8], y[8], o[8];
-      raw_unpack<DT>(a[u], x);
-      if constexpr (KIND == EW_BINOP) {
-        raw_unpack<DT>(b[u], y);
-        ew_dispatch8(P.op, x, y, o);
-      } else if constexpr (KIND == EW_SCALAR) {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) y[k] = P.imm;
-        if (P.const_first) ew_dispatch8(P.op, y, x, o);
-        else ew_dispatch8(P.op, x, y, o);
-      } else {
-        raw_unpack<DT>(b[u], y);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const float t = npu_exp(-x[k]);
-          const float q = __fdiv_rn(x[k], __fadd_rn(t, 1.0f));
-          o[k] = __fmul_rn(q, y[k]);
-        }
-      }
-      raw_store<DT>(L, i0, o);
+    for (int k = 0; k < 8; ++k) {
+      const float t = npu_exp(-x[k]);
+      const float q = __fdiv_rn(x[k], __fadd_rn(t, 1.0f));
+      o[k] = __fmul_rn(q, y[k]);
     }
   }
-  // The ragged last group.
-  if (blockIdx.x == 0 && threadIdx.x == 0 && L.begin + full * 8 < L.end) {
-    const int64_t i0 = L.begin + full * 8;
-    const int n = int(L.end - i0);
-    float x[8], y[8], o[8];
-    load8(L, P.map_a, i0, n, x);
-    if constexpr (KIND == EW_BINOP) {
-      load8(L, P.map_b, i0, n, y);
-      ew_dispatch8(P.op, x, y, o);
-    } else if constexpr (KIND == EW_SCALAR) {
+}
+
+template <int KIND, int NG, int DT>
+__global__ void __launch_bounds__(256, DT == PTSIM_DT_F32 ? 5 : 8) ew_vpattern_kernel(const __grid_constant__ EwVec V) {
+  const uint32_t full = (V.end - V.begin) / 8;   // groups of 8 inside the launch
+  const uint32_t g0 = blockIdx.x * blockDim.x * NG + threadIdx.x;
+  RawGroup<DT> a[NG], b[NG];
+  bool ok[NG];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) y[k] = P.imm;
-      if (P.const_first) ew_dispatch8(P.op, y, x, o);
-      else ew_dispatch8(P.op, x, y, o);
-    } else {
-      load8(L, P.map_b, i0, n, y);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float t = npu_exp(-x[k]);
-        const float q = __fdiv_rn(x[k], __fadd_rn(t, 1.0f));
-        o[k] = __fmul_rn(q, y[k]);
-      }
+  for (int u = 0; u < NG; ++u) {
+    const uint32_t g = g0 + u * blockDim.x;
+    ok[u] = g < full;
+    if (ok[u]) {
+      const uint32_t i0 = V.begin + g * 8;
+      ok[u] = raw_load<DT>(V.a, V.ma, V.na, i0, a[u]);
+      if constexpr (KIND != EW_SCALAR) ok[u] = raw_load<DT>(V.b, V.mb, V.nb, i0, b[u]) && ok[u];
     }
-    store8(L, i0, n, o);
+  }
+#pragma unroll
+  for (int u = 0; u < NG; ++u) {
+    if (!ok[u]) continue;
+    float x[8], y[8], o[8];
+    raw_unpack<DT>(a[u], x);
+    if constexpr (KIND != EW_SCALAR) raw_unpack<DT>(b[u], y);
+    vpattern_math<KIND>(V, x, y, o);
+    raw_store<DT>(V, V.begin + (g0 + u * blockDim.x) * 8, o);
+  }
+  // The ragged last group, element by element.
+  if (blockIdx.x == 0 && threadIdx.x == 0 && V.begin + full * 8 < V.end) {
+    const uint32_t i0 = V.begin + full * 8, n = V.end - i0;
+    float x[8], y[8], o[8];
+    for (int k = 0; k < 8; ++k) {
+      x[k] = y[k] = 0.f;
+      if (uint32_t(k) >= n) continue;
+      const uint32_t ia = fast_index(V.ma, i0 + k), ib = KIND != EW_SCALAR ? fast_index(V.mb, i0 + k) : 0;
+      if (ia >= V.na || (KIND != EW_SCALAR && ib >= V.nb)) { record_status(PTSIM_E_OOB); continue; }
+      x[k] = load_elem(V.a, DT, ia);
+      if (KIND != EW_SCALAR) y[k] = load_elem(V.b, DT, ib);
+    }
+    vpattern_math<KIND>(V, x, y, o);
+    for (int k = 0; k < 8; ++k) {
+      if (uint32_t(k) >= n) continue;
+      const uint32_t io = fast_index(V.mo, i0 + k);
+      if (io >= V.no) { record_status(PTSIM_E_OOB); continue; }
+      store_elem(V.o, DT, io, o[k]);
+    }
   }
 }
 
@@ -649,24 +652,42 @@ int launch_elementwise(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64
       default: return fail(PTSIM_E_DESC, "elementwise copy of a %d-byte element", es);
     }
   } else if (const EwPattern P = match_pattern(L.p); P.kind != EW_VM) {
-    // Vector path when every map of the shape is contiguous and aligned and all tensors share one dtype.
+    // Vector path when every map of the shape is contiguous and aligned, all tensors share one dtype and
+    // every index fits 31 bits.
     const int dt = d.arg_dtype[L.p.map[P.map_a].arg];
-    bool vec = (dt == PTSIM_DT_BF16 || dt == PTSIM_DT_F32) && L.vec[P.map_a] && L.vec[L.p.store_map] &&
+    bool vec = L.idx32 && (dt == PTSIM_DT_BF16 || dt == PTSIM_DT_F32) && L.vec[P.map_a] && L.vec[L.p.store_map] &&
                d.arg_dtype[L.p.map[L.p.store_map].arg] == dt;
     if (P.kind != EW_SCALAR) vec = vec && L.vec[P.map_b] && d.arg_dtype[L.p.map[P.map_b].arg] == dt;
     if (vec) {
-      const int ng = 2;
+      EwVec V;
+      memset(&V, 0, sizeof(V));
+      const int aa = L.p.map[P.map_a].arg, oa = L.p.map[L.p.store_map].arg;
+      const int ba = P.kind != EW_SCALAR ? L.p.map[P.map_b].arg : aa;
+      V.a = ptrs[aa];
+      V.b = ptrs[ba];
+      V.o = ptrs[oa];
+      V.ma = L.fmap[P.map_a];
+      V.mb = P.kind != EW_SCALAR ? L.fmap[P.map_b] : L.fmap[P.map_a];
+      V.mo = L.fmap[L.p.store_map];
+      V.na = uint32_t(d.arg_numel[aa]);
+      V.nb = uint32_t(d.arg_numel[ba]);
+      V.no = uint32_t(d.arg_numel[oa]);
+      V.begin = uint32_t(L.begin);
+      V.end = uint32_t(L.end);
+      V.op = P.op;
+      V.const_first = P.const_first;
+      V.imm = P.imm;
+      constexpr int ng = 2;
       const int64_t pb = ceil_div(groups, int64_t(threads) * ng);
-      if (pb > int64_t(0x7fffffff)) return fail(PTSIM_E_UNSUPPORTED, "elementwise launch of %lld groups", (long long)groups);
       const unsigned gb = unsigned(pb < 1 ? 1 : pb);
       if (dt == PTSIM_DT_BF16) {
-        if (P.kind == EW_BINOP) ew_vpattern_kernel<EW_BINOP, 2, PTSIM_DT_BF16><<<gb, threads, 0, c.stream>>>(L, P);
-        else if (P.kind == EW_SCALAR) ew_vpattern_kernel<EW_SCALAR, 2, PTSIM_DT_BF16><<<gb, threads, 0, c.stream>>>(L, P);
-        else ew_vpattern_kernel<EW_SILU_MUL, 2, PTSIM_DT_BF16><<<gb, threads, 0, c.stream>>>(L, P);
+        if (P.kind == EW_BINOP) ew_vpattern_kernel<EW_BINOP, ng, PTSIM_DT_BF16><<<gb, threads, 0, c.stream>>>(V);
+        else if (P.kind == EW_SCALAR) ew_vpattern_kernel<EW_SCALAR, ng, PTSIM_DT_BF16><<<gb, threads, 0, c.stream>>>(V);
+        else ew_vpattern_kernel<EW_SILU_MUL, ng, PTSIM_DT_BF16><<<gb, threads, 0, c.stream>>>(V);
       } else {
-        if (P.kind == EW_BINOP) ew_vpattern_kernel<EW_BINOP, 2, PTSIM_DT_F32><<<gb, threads, 0, c.stream>>>(L, P);
-        else if (P.kind == EW_SCALAR) ew_vpattern_kernel<EW_SCALAR, 2, PTSIM_DT_F32><<<gb, threads, 0, c.stream>>>(L, P);
-        else ew_vpattern_kernel<EW_SILU_MUL, 2, PTSIM_DT_F32><<<gb, threads, 0, c.stream>>>(L, P);
+        if (P.kind == EW_BINOP) ew_vpattern_kernel<EW_BINOP, ng, PTSIM_DT_F32><<<gb, threads, 0, c.stream>>>(V);
+        else if (P.kind == EW_SCALAR) ew_vpattern_kernel<EW_SCALAR, ng, PTSIM_DT_F32><<<gb, threads, 0, c.stream>>>(V);
+        else ew_vpattern_kernel<EW_SILU_MUL, ng, PTSIM_DT_F32><<<gb, threads, 0, c.stream>>>(V);
       }
     } else {
       int64_t pb = ceil_div(groups, int64_t(threads) * 2);

@@ -398,7 +398,7 @@ static int max_active_clusters(int splits, const LaunchCtx &c) {
   std::atomic<int> *e = (c.device >= 0 && c.device < 64) ? &cache[c.device][slot] : nullptr;
   if (e != nullptr && e->load() > 0) return e->load() - 1;
   auto kern = gemm_tcgen05_kernel<BN, B_KMAJOR>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES) != cudaSuccess) return 0;
+  if ((smem_limit_once<gemm_tcgen05_kernel<BN, B_KMAJOR>>(Cfg::SMEM_BYTES, c.device)) != cudaSuccess) return 0;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   cfg.gridDim = dim3(unsigned(splits * c.sm_count));
@@ -424,7 +424,7 @@ static int run_gemm(GemmArgs &g, const LaunchCtx &c) {
   using Cfg = GemmCfg<BN>;
   const int items = g.tiles_m * g.tiles_n * g.splits;
   auto kern = gemm_tcgen05_kernel<BN, B_KMAJOR>;
-  PTSIM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
+  PTSIM_CUDA((smem_limit_once<gemm_tcgen05_kernel<BN, B_KMAJOR>>(Cfg::SMEM_BYTES, c.device)));
   if (g.splits == 1) {
     const int grid = items < c.sm_count ? items : c.sm_count;
     kern<<<grid, kGemmThreads, Cfg::SMEM_BYTES, c.stream>>>(g);
