@@ -227,6 +227,47 @@ def run_reference(args, world, rank):
 # B200 arm
 # ---------------------------------------------------------------------------------------------------
 
+def tp_layer_timing(dev, world, rank, steps, warmup):
+    """BASELINE.json config 5 across the ranks: the Qwen3-8B-shaped layer (T = 2048) split column- and
+    row-wise over `world` GPUs, each rank's two segments replayed from CUDA graphs with an NCCL all-reduce
+    after each row-parallel GEMM (o_proj, down).  Whole-layer TFLOP/s from the slowest rank's time."""
+    import torch
+    import torch.distributed as dist
+    from oracle import programs as O
+    from pytorchsim_triton_compiler.runtime import qwen3 as Q
+    T = 2048
+    p = Q.random_params(0)
+    x = torch.randn(T * Q.HIDDEN, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
+    cos, sin = O.rope_tables(T)
+    g1, g2 = Q.build_layer(dev, T, Q.shard(p, rank, world), cos, sin, x, tp=world, rank=rank)
+    g1.capture()
+    g2.capture()
+    x1, y = g1.buffers["x1"], g1.buffers["y"]
+
+    def layer():
+        g1.run()
+        dist.all_reduce(x1)
+        g2.run()
+        dist.all_reduce(y)
+
+    for _ in range(warmup):
+        layer()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in ev:
+        a.record()
+        layer()
+        b.record()
+    torch.cuda.synchronize()
+    ms = reduce_max(statistics.median([a.elapsed_time(b) for a, b in ev]), world, dev)
+    _, tflops, _ = peaks()
+    tf = Q.layer_flops(T) / ms / 1e9
+    del g1, g2
+    return {"n_gpus": world, "ms": round(ms, 4), "TFLOP/s": round(tf, 1), "frac_bf16": round(tf / (world * tflops), 3),
+            "scaling": "strong", "collective": "NCCL all-reduce of 2048 x 4096 bf16 after o_proj and after down"}
+
+
 def run_b200(args, world, rank, local):
     import torch
     from pytorchsim_triton_compiler.codegen import descriptors as D
@@ -351,6 +392,8 @@ def run_b200(args, world, rank, local):
                     "api": "runtime.cuda.HostPipeline (C ABI ptsim_launch) over pinned host buffers, 8 row ranges per launch"},
             "gpu_launches": 2 * args.steps,
             "clocks": clk}
+    if world > 1 and args.suite:
+        line["tp_layer"] = tp_layer_timing(dev, world, rank, steps=10, warmup=3)
     if rank == 0 and world == 1 and args.cpu:
         base, _ = cpu_rate(seconds=10.0)
         line["cpu_baseline"] = base
