@@ -299,12 +299,13 @@ __global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __gri
   uint64_t *q_full = bars + 0;
   uint64_t *k_full = bars + 1;    // 2
   uint64_t *v_full = bars + 3;    // 2
-  uint64_t *kv_empty = bars + 5;  // 2
+  uint64_t *k_empty = bars + 5;   // 2: K_j read by S_A(j) and S_B(j)
   uint64_t *s_full = bars + 7;    // [A, B]
   uint64_t *p_full = bars + 9;    // [A, B], 4 arrivals each
   uint64_t *o_done = bars + 11;   // [A, B]
   uint64_t *drain = bars + 13;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 14);
+  uint64_t *v_empty = bars + 14;  // 2: V_j read by PV_A(j) and PV_B(j)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 16);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -320,7 +321,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __gri
   const int nB = g.causal ? 2 * qp + 2 : nA;                      // and of tile B
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 14; ++i) sm100::mbar_init(&bars[i], (i == 9 || i == 10) ? 4u : 1u);
+    for (int i = 0; i < 16; ++i) sm100::mbar_init(&bars[i], (i == 9 || i == 10) ? 4u : 1u);
     *abort_flag = 0;
     sm100::fence_barrier_init();
   }
@@ -340,24 +341,27 @@ __global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __gri
       sm100::tma_load_2d(sQ + 16384, &g.tq, q_full, 64, q_row0);
       sm100::tma_load_2d(sQ + kAttnTile, &g.tq, q_full, 0, q_row0 + kAttnBM);
       sm100::tma_load_2d(sQ + kAttnTile + 16384, &g.tq, q_full, 64, q_row0 + kAttnBM);
-      int j = 0;
-      for (; j < nB; ++j) {
+      // K and V slots are released separately (K after the S products, V after the PV products), so
+      // K_{j+2} starts loading about half an iteration before V_{j+2} may.
+      int kj = 0, vj = 0;   // K and V tiles issued
+      for (int j = 0; j < nB; ++j) {
         const int st = j & 1;
-        if (!sm100::mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1)) { *abort_flag = 1; break; }
         const int kr = kv_row0 + j * kAttnBN;
+        if (!sm100::mbar_wait(&k_empty[st], ((j >> 1) & 1) ^ 1)) { *abort_flag = 1; break; }
         sm100::mbar_arrive_expect_tx(&k_full[st], kAttnTile);
         sm100::tma_load_2d(sK + st * kAttnTile, &g.tk, &k_full[st], 0, kr);
         sm100::tma_load_2d(sK + st * kAttnTile + 16384, &g.tk, &k_full[st], 64, kr);
+        ++kj;
+        if (!sm100::mbar_wait(&v_empty[st], ((j >> 1) & 1) ^ 1)) { *abort_flag = 1; break; }
         sm100::mbar_arrive_expect_tx(&v_full[st], kAttnTile);
         sm100::tma_load_2d(sV + st * kAttnTile, &g.tv, &v_full[st], 0, kr);
         sm100::tma_load_2d(sV + st * kAttnTile + 16384, &g.tv, &v_full[st], 64, kr);
+        ++vj;
       }
       if (*abort_flag) {
         sm100::mbar_wait(q_full, 0);
-        for (int i = (j - 2 < 0 ? 0 : j - 2); i < j; ++i) {
-          sm100::mbar_wait(&k_full[i & 1], (i >> 1) & 1);
-          sm100::mbar_wait(&v_full[i & 1], (i >> 1) & 1);
-        }
+        for (int i = (kj - 2 < 0 ? 0 : kj - 2); i < kj; ++i) sm100::mbar_wait(&k_full[i & 1], (i >> 1) & 1);
+        for (int i = (vj - 2 < 0 ? 0 : vj - 2); i < vj; ++i) sm100::mbar_wait(&v_full[i & 1], (i >> 1) & 1);
       }
     }
   } else if (warp == 1) {
@@ -391,6 +395,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __gri
         sm100::tc_fence_after();
         if (nA > 0) issue_s(0, 0);
         issue_s(1, 0);
+        sm100::mma_commit(&k_empty[0]);   // K_0 is read once S_A(0) and S_B(0) are done
       }
       for (int j = 0; ok && j < nB; ++j) {
         const int st = j & 1;
@@ -409,11 +414,12 @@ __global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __gri
         if (!sm100::mbar_wait(&p_full[1], j & 1)) { ok = false; break; }
         sm100::tc_fence_after();
         issue_pv(1, j);
-        sm100::mma_commit(&kv_empty[st]);   // K_j and V_j are read once PV_B(j) is done
+        sm100::mma_commit(&v_empty[st]);    // V_j is read once PV_B(j) is done
         if (next) {
           if (!sm100::mbar_wait(&k_full[st ^ 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
           sm100::tc_fence_after();
           issue_s(1, j + 1);
+          sm100::mma_commit(&k_empty[st ^ 1]);   // K_{j+1} is read once S_B(j+1) is done
         }
       }
       if (!ok) *abort_flag = 1;
