@@ -356,6 +356,186 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
 }
 
 // ---------------------------------------------------------------------------------------------------
+// Pair kernel (outputs with at least one 256 x 256 tile per cluster): a 2-CTA cluster computes 256 x 256
+// tiles with the M = 256 tcgen05.mma (cta_group::2).  CTA r holds A rows [128 r, 128 r + 128) and B
+// columns [128 r, 128 r + 128) of each K block in its own shared memory, so each SM reads 8 KB of
+// operands per 128-clock MMA instead of 12 KB for a 128 x 256 tile on one SM, and its TMEM receives
+// its 128 output rows x 256 columns.  Both CTAs' TMA loads count on the leader's (rank 0) full barrier,
+// armed by the leader for both CTAs' bytes; the leader's MMA thread issues the MMAs and commits to both
+// CTAs' barriers (stage release, accumulator ready); each CTA's epilogue drains its own rows and both
+// epilogues release the accumulator on the leader's barrier.  Roles as in the one-CTA kernel; on an
+// abort the leader's producer waits for every stage whose loads it armed, and every thread of both
+// CTAs meets at the final cluster barrier before TMEM is released.
+// ---------------------------------------------------------------------------------------------------
+constexpr int kGemm2Stages = 6;
+constexpr int kGemm2HalfTile = kGemmBM * kGemmBK * 2;        // 16 KB: 128 rows (or columns) x 64 K
+constexpr int kGemm2Smem = kGemm2Stages * 2 * kGemm2HalfTile + 1024 + 512;
+
+template <bool B_KMAJOR>
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm2_tcgen05_kernel(const __grid_constant__ GemmArgs g) {
+  constexpr int S = kGemm2Stages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sA = smem;                          // S x 16 KB: this CTA's 128 rows of A
+  uint8_t *sB = smem + S * kGemm2HalfTile;     // S x 16 KB: this CTA's 128 columns of B
+  uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem + 2 * S * kGemm2HalfTile);  // [S] (leader) both CTAs' loads
+  uint64_t *empty_bar = full_bar + S;          // [S] the pair's MMAs have read the stage
+  uint64_t *tfull_bar = empty_bar + S;         // [2] accumulator ready
+  uint64_t *tempty_bar = tfull_bar + 2;        // [2] (leader) both CTAs' epilogues drained it
+  uint64_t *drain_bar = tempty_bar + 2;        // (leader) every MMA done
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain_bar + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = sm100::cluster_ctarank();
+  const int num_kb = int(ceil_div(g.K, kGemmBK));
+  const int num_tiles = g.tiles_m * g.tiles_n;   // 256 x 256 tiles
+  const int cluster = int(blockIdx.x >> 1), nclusters = int(gridDim.x >> 1);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      sm100::mbar_init(&full_bar[i], 1);
+      sm100::mbar_init(&empty_bar[i], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      sm100::mbar_init(&tfull_bar[b], 1);
+      sm100::mbar_init(&tempty_bar[b], 8);  // four epilogue warps in each CTA
+    }
+    sm100::mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    sm100::fence_barrier_init();
+    sm100::tma_prefetch_desc(&g.tmap_a);
+    sm100::tma_prefetch_desc(&g.tmap_b);
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc2(tmem_slot, 512);
+    sm100::tmem_relinquish2();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::cluster_sync();   // both CTAs' barriers are initialised before any cross-CTA arrival
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  auto tile_coords = [&](int t, int &tm, int &tn) {
+    tm = t % g.tiles_m;
+    tn = t / g.tiles_m;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t full0 = sm100::mapa_shared(sm100::smem_u32(full_bar), 0);   // the leader's full barriers
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed = 0;   // (leader) bit s: stage s armed, parity bit (s + 16)
+      for (int t = cluster; t < num_tiles && !*abort_flag; t += nclusters) {
+        int tm, tn;
+        tile_coords(t, tm, tn);
+        const int m0 = int(g.m_begin) + tm * 256 + int(rank) * kGemmBM;
+        const int n0 = tn * 256 + int(rank) * kGemmBM;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!sm100::mbar_wait(&empty_bar[stage], phase ^ 1)) { *abort_flag = 1; break; }
+          if (rank == 0) {
+            sm100::mbar_arrive_expect_tx(&full_bar[stage], 4 * kGemm2HalfTile);   // both CTAs' A and B halves
+            armed = (armed | (1u << stage)) & ~(1u << (stage + 16));
+            armed |= phase << (stage + 16);
+          }
+          const uint32_t bar = full0 + uint32_t(stage) * 8u;
+          sm100::tma_load_2d_pair(sA + stage * kGemm2HalfTile, &g.tmap_a, bar, kb * kGemmBK, m0);
+          if constexpr (B_KMAJOR) {
+            sm100::tma_load_2d_pair(sB + stage * kGemm2HalfTile, &g.tmap_b, bar, kb * kGemmBK, n0);
+          } else {
+            sm100::tma_load_2d_pair(sB + stage * kGemm2HalfTile, &g.tmap_b, bar, n0, kb * kGemmBK);
+            sm100::tma_load_2d_pair(sB + stage * kGemm2HalfTile + kGemmBK * 128, &g.tmap_b, bar, n0 + 64, kb * kGemmBK);
+          }
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (*abort_flag && rank == 0) {
+        // Every stage the leader armed completes once both CTAs' copies into it have landed.
+        for (int s = 0; s < S; ++s)
+          if (armed & (1u << s)) sm100::mbar_wait(&full_bar[s], (armed >> (s + 16)) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = sm100::idesc_bf16_f32(256, 256, false, !B_KMAJOR);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int t = cluster; t < num_tiles && !*abort_flag; t += nclusters, ++it) {
+        const int buf = it & 1;
+        const uint32_t use = uint32_t(it >> 1) & 1u;
+        if (!sm100::mbar_wait<true>(&tempty_bar[buf], use ^ 1)) { *abort_flag = 1; break; }
+        sm100::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(buf * 256);
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!sm100::mbar_wait(&full_bar[stage], phase)) { ok = false; break; }
+          sm100::tc_fence_after();
+          const uint32_t a_addr = sm100::smem_u32(sA + stage * kGemm2HalfTile);
+          const uint32_t b_addr = sm100::smem_u32(sB + stage * kGemm2HalfTile);
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 16; ++k) {
+            const uint64_t adesc = sm100::sw128_desc(a_addr + k * 32, 16, 1024);
+            uint64_t bdesc;
+            if constexpr (B_KMAJOR) bdesc = sm100::sw128_desc(b_addr + k * 32, 16, 1024);
+            else bdesc = sm100::sw128_desc(b_addr + k * 16 * 128, kGemmBK * 128, 1024);
+            sm100::mma2_bf16_ss(d_tmem, adesc, bdesc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          sm100::mma2_commit_mc(&empty_bar[stage], 0x3);   // frees the stage in both CTAs
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) { *abort_flag = 1; break; }
+        sm100::mma2_commit_mc(&tfull_bar[buf], 0x3);       // both CTAs' accumulator rows are ready
+      }
+      sm100::mma2_commit(drain_bar);
+      sm100::mbar_wait(drain_bar, 0);
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    const uint32_t tempty0 = sm100::mapa_shared(sm100::smem_u32(tempty_bar), 0);   // the leader's
+    int it = 0;
+    for (int t = cluster; t < num_tiles; t += nclusters, ++it) {
+      const int buf = it & 1;
+      const uint32_t use = uint32_t(it >> 1) & 1u;
+      if (*abort_flag || !sm100::mbar_wait(&tfull_bar[buf], use)) { *abort_flag = 1; break; }
+      sm100::tc_fence_after();
+      int tm, tn;
+      tile_coords(t, tm, tn);
+      const int64_t row = g.m_begin + int64_t(tm) * 256 + int64_t(rank) * kGemmBM + row_in_tile;
+      const bool row_ok = row < g.m_end;
+#pragma unroll 1
+      for (int j = 0; j < 256 / 32; ++j) {
+        uint32_t v[32];
+        sm100::tmem_ld32(tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(buf * 256 + j * 32), v);
+        sm100::tmem_wait_ld();
+        const int64_t col0 = int64_t(tn) * 256 + j * 32;
+        if (!row_ok || col0 >= g.N) continue;
+        float acc[32];
+#pragma unroll
+        for (int q = 0; q < 32; ++q) acc[q] = __uint_as_float(v[q]);
+        gemm_store_row32(g, row, col0, acc);
+      }
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive_cluster(tempty0 + uint32_t(buf) * 8u);
+    }
+  }
+
+  // Teardown: both CTAs meet after every role has stopped (the leader's MMAs have drained), so no MMA
+  // still writes either CTA's TMEM, then each releases its share of the pair allocation.
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::cluster_sync();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc2(tmem_base, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------------------------------
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode_tiled() {
@@ -444,6 +624,53 @@ static int run_gemm(GemmArgs &g, const LaunchCtx &c) {
     cfg.numAttrs = 1;
     PTSIM_CUDA(cudaLaunchKernelEx(&cfg, kern, g));
   }
+  PTSIM_CUDA(cudaGetLastError());
+  return PTSIM_OK;
+}
+
+// Clusters of two pair-kernel CTAs one device runs at once (0 when it cannot), cached per device.
+template <bool B_KMAJOR>
+static int pair_clusters(const LaunchCtx &c) {
+  static std::atomic<int> cache[64];   // count + 1; 0 = unknown
+  std::atomic<int> *e = (c.device >= 0 && c.device < 64) ? &cache[c.device] : nullptr;
+  if (e != nullptr && e->load() > 0) return e->load() - 1;
+  if ((smem_limit_once<gemm2_tcgen05_kernel<B_KMAJOR>>(kGemm2Smem, c.device)) != cudaSuccess) return 0;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3(unsigned(2 * c.sm_count));
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = kGemm2Smem;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm2_tcgen05_kernel<B_KMAJOR>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  if (e != nullptr) e->store(n + 1);
+  return n;
+}
+
+template <bool B_KMAJOR>
+static int run_gemm2(GemmArgs &g, int nclusters, const LaunchCtx &c) {
+  PTSIM_CUDA((smem_limit_once<gemm2_tcgen05_kernel<B_KMAJOR>>(kGemm2Smem, c.device)));
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3(unsigned(2 * nclusters));
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = kGemm2Smem;
+  cfg.stream = c.stream;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  PTSIM_CUDA(cudaLaunchKernelEx(&cfg, gemm2_tcgen05_kernel<B_KMAJOR>, g));
   PTSIM_CUDA(cudaGetLastError());
   return PTSIM_OK;
 }
@@ -541,9 +768,30 @@ int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, 
   g.tiles_n = int(pl.tiles_n);
   g.splits = pl.splits;
   g.kb_per_split = pl.kb_per_split;
-  const int bn = pl.bn;
   int rc = make_tmap_2d(&g.tmap_a, ptrs[p.a_arg], uint64_t(p.K), uint64_t(p.M), uint64_t(p.lda), kGemmBK, kGemmBM);
   if (rc) return rc;
+  // The pair kernel (256 x 256 tiles on 2-CTA clusters) when K is not split and the output has at least
+  // one such tile per cluster the device runs at once.
+  if (pl.splits == 1 && p.N >= 256) {
+    const int64_t tm2 = ceil_div(m_end - m_begin, 256), tn2 = ceil_div(p.N, 256);
+    const int pc = p.b_kmajor ? pair_clusters<true>(c) : pair_clusters<false>(c);
+    if (pc > 0 && tm2 * tn2 >= pc) {
+      g.tiles_m = int(tm2);
+      g.tiles_n = int(tn2);
+      g.splits = 1;
+      g.kb_per_split = int(ceil_div(p.K, kGemmBK));
+      if (p.b_kmajor) {
+        rc = make_tmap_2d(&g.tmap_b, ptrs[p.b_arg], uint64_t(p.K), uint64_t(p.N), uint64_t(p.ldb), kGemmBK, kGemmBM);
+      } else {
+        if (p.N % 8 != 0) return fail(PTSIM_E_UNSUPPORTED, "GEMM with N-contiguous B needs N %% 8 == 0");
+        rc = make_tmap_2d(&g.tmap_b, ptrs[p.b_arg], uint64_t(p.N), uint64_t(p.K), uint64_t(p.ldb), 64, kGemmBK);
+      }
+      if (rc) return rc;
+      const int nc = int(tm2 * tn2 < pc ? tm2 * tn2 : pc);
+      return p.b_kmajor ? run_gemm2<true>(g, nc, c) : run_gemm2<false>(g, nc, c);
+    }
+  }
+  const int bn = pl.bn;
   if (p.b_kmajor) {
     rc = make_tmap_2d(&g.tmap_b, ptrs[p.b_arg], uint64_t(p.K), uint64_t(p.N), uint64_t(p.ldb), kGemmBK, uint32_t(bn));
   } else {

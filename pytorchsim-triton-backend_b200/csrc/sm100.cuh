@@ -54,13 +54,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
   return ok != 0;
 }
 
+// The same with cluster-scope acquire, for a barrier that threads of another CTA arrive on (their
+// release then orders their earlier writes before this thread's later reads).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\tselp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for `phase` of `bar` to complete, for at most ~2 seconds of wall time.  Returns false (and
 // records PTSIM_E_TIMEOUT) when it gives up; the caller then unwinds instead of hanging the GPU.
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t phase) {
-  if (mbar_try_wait(bar, phase)) return true;
+  auto try_once = [&]() { return CLUSTER ? mbar_try_wait_cluster(bar, phase) : mbar_try_wait(bar, phase); };
+  if (try_once()) return true;
   uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, phase)) return true;
+    if (try_once()) return true;
     if ((i & 255u) == 0) {
       if (globaltimer_ns() - t0 > 2000000000ull || i > kSpinLimit) {
         record_status(PTSIM_E_TIMEOUT);
@@ -82,6 +96,16 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, uint64_
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
           smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// The pair form: the load lands in this CTA's shared memory and its bytes count on the mbarrier at
+// shared::cluster address `bar` (the leader CTA's, for a cta_group::2 MMA that waits on one barrier).
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const void *tmap, uint32_t bar, int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(x), "r"(y)
       : "memory");
 }
 
@@ -131,6 +155,43 @@ __device__ __forceinline__ void tmem_relinquish() {
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
+// Pair (cta_group::2) forms: TMEM allocation and release issued by the same warp in both CTAs of a
+// 2-CTA cluster (same shared-memory slot offset in each), the M = 256 MMA issued by the leader CTA with
+// operands from both CTAs' shared memory (A rows and B columns split between the pair), and commits
+// that arrive on the barrier at the same offset in every CTA of `mask`.
+__device__ __forceinline__ void tmem_alloc2(uint32_t *dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish2() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void mma2_bf16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma2_commit_mc(uint64_t *bar, uint16_t mask) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                   smem_u32(bar)),
+               "h"(mask)
+               : "memory");
+}
+__device__ __forceinline__ void mma2_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+// Arrive on the mbarrier at shared::cluster address `addr` (another CTA's, from mapa_shared).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 

@@ -135,9 +135,16 @@ def test_gemm_residual(M, N, K):
     _gemm_case(M, N, K, residual=True)
 
 
-@pytest.mark.parametrize("M,N,K", [(512, 1024, 512), (256, 384, 128)])
+@pytest.mark.parametrize("M,N,K", [(512, 1024, 512), (256, 384, 128), (2048, 4096, 512)])
 def test_gemm_b_kmajor(M, N, K):
     _gemm_case(M, N, K, b_kmajor=True)
+
+
+@pytest.mark.parametrize("M,N,K,residual", [(2100, 2560, 520, False), (2304, 4096, 1024, True), (8192, 4096, 256, False)])
+def test_gemm_pair_tiles(M, N, K, residual):
+    """Shapes with at least one 256 x 256 output tile per cluster run on the 2-CTA kernel: ragged M, N
+    and K, the residual epilogue, and many tiles per cluster."""
+    _gemm_case(M, N, K, residual=residual)
 
 
 @pytest.mark.parametrize("batch,hq,hkv,seq,causal", [(1, 4, 1, 256, True), (2, 8, 2, 512, True),
