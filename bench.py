@@ -452,6 +452,8 @@ def suite(dev, stream, iters=5, only=None, warm=1):
             out[name] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1), "frac_bf16": round(tf / tflops, 3)}
 
     timed("vector_add_1m", "hbm", 3 * 4 * 1_048_576)
+    if only is None or only == "vector_add_1m_amortized":
+        out["vector_add_1m_amortized"] = amortized_vector_add(dev, stream, hbm)
     timed("vector_add1_4096x4096", "hbm", 2 * 2 * 4096 * 4096)
     for m in (128, 512, 2048, 4096, 8192):
         timed(f"gemm_{m}x4096x4096", "tensor", 2 * m * 4096 * 4096)
@@ -459,6 +461,49 @@ def suite(dev, stream, iters=5, only=None, warm=1):
     if only is None or only == "qwen3_layer":
         out["qwen3_layer_t2048"] = layer_timing(dev, stream, iters, warm, flush, tflops)
     return out
+
+
+def amortized_vector_add(dev, stream, hbm, sets=16, launches=64):
+    """BASELINE.json configs[0] amortised: the lowered vector-add object (1,048,576 fp32 per launch,
+    12.6 MB) replayed as `launches` back-to-back launches from one CUDA graph over `sets` rotating
+    input/output sets (201 MB, more than L2), so the per-launch figure excludes the host and the timing
+    events but keeps every launch's HBM traffic."""
+    import torch
+    from pytorchsim_triton_compiler.codegen import descriptors as D
+    from pytorchsim_triton_compiler.runtime import native
+    m, blob = load_object("vector_add_1m")
+    d = D.from_bytes(blob)
+    n = 1_048_576
+    g = torch.Generator(device=dev).manual_seed(0)
+    bufs = [(torch.randn(n, generator=g, device=dev), torch.randn(n, generator=g, device=dev),
+             torch.empty(n, device=dev)) for _ in range(sets)]
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        native.launch(blob, [t.data_ptr() for t in bufs[0]], 0, d.units, stream=s.cuda_stream)
+        native.sync(s.cuda_stream)
+        with torch.cuda.graph(graph, stream=s):
+            for i in range(launches):
+                native.launch(blob, [t.data_ptr() for t in bufs[i % sets]], 0, d.units, stream=s.cuda_stream)
+    stream.wait_stream(s)
+    graph.replay()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(5):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        graph.replay()
+        b.record(stream)
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    native.sync(stream.cuda_stream)
+    ms = statistics.median(ts) / launches
+    ok = all(torch.equal(o, x + y) for x, y, o in bufs[:2])
+    gbs = 3 * 4 * n / ms / 1e6
+    del graph
+    return {"ms_per_launch": round(ms, 5), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm, 3),
+            "launches": launches, "sets": sets, "bit_exact": ok}
 
 
 def layer_timing(dev, stream, iters, warm, flush, tflops):

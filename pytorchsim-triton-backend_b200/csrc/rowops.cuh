@@ -398,57 +398,84 @@ int launch_rowops(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi
 // ---------------------------------------------------------------------------------------------------
 // QK-RMSNorm + RoPE (validation/pytorchsim/qwen3_8b_layer_prefill_2048x2048_bf16/02_*/..._triton.py):
 // row (t, h) of `dim` = 128 values: r = rsqrt(mean(x^2) + eps); n = (x * r) * w; the rotated half is
-// cat(-n[64:], n[:64]); out[t, h] stored head-major = n * cos[t] + rot * sin[t].  One warp per row, four
-// values per lane; lane l's rotation partner holds d +- 64, i.e. lane l ^ 16.
+// cat(-n[64:], n[:64]); out[t, h] stored head-major = n * cos[t] + rot * sin[t].  A half-warp per row,
+// eight values per lane (one 16-byte load); lane l's rotation partner holds d +- 64, i.e. lane l ^ 8 of
+// the same half.  A warp takes two rows per step and issues the loads of two steps before computing, so
+// four rows of loads are in flight per warp; row indices are 32-bit (the launch is refused past 2^31).
 // ---------------------------------------------------------------------------------------------------
 struct QkLaunch {
   const uint16_t *in;
   const uint16_t *w;
   const float *cosb, *sinb;
   uint16_t *out;
-  int64_t row_begin, row_end, heads, tok_stride, head_stride;
+  uint32_t row_begin, row_end, heads;
+  int64_t tok_stride, head_stride;
   float eps;
 };
 
 __global__ void __launch_bounds__(256) qk_rope_kernel(const __grid_constant__ QkLaunch L) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
-  const uint2 wv = __ldg(reinterpret_cast<const uint2 *>(L.w) + lane);
-  const float w[4] = {lo_bf16(wv.x), hi_bf16(wv.x), lo_bf16(wv.y), hi_bf16(wv.y)};
-  for (int64_t row = L.row_begin + warp; row < L.row_end; row += nwarps) {
-    const int64_t t = row / L.heads, h = row % L.heads;
-    const uint2 xv = __ldcs(reinterpret_cast<const uint2 *>(L.in + row * 128) + lane);
-    const float x[4] = {lo_bf16(xv.x), hi_bf16(xv.x), lo_bf16(xv.y), hi_bf16(xv.y)};
-    float ss = 0.f;
+  const int lane = threadIdx.x & 31, sub = lane & 15, half = lane >> 4;
+  const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const uint32_t nwarps = (gridDim.x * blockDim.x) >> 5;
+  const uint4 wv = __ldg(reinterpret_cast<const uint4 *>(L.w) + sub);
+  const float w[8] = {lo_bf16(wv.x), hi_bf16(wv.x), lo_bf16(wv.y), hi_bf16(wv.y),
+                      lo_bf16(wv.z), hi_bf16(wv.z), lo_bf16(wv.w), hi_bf16(wv.w)};
+  const unsigned full = 0xffffffffu;
+  for (uint32_t r0 = L.row_begin + 4 * warp; r0 < L.row_end; r0 += 4 * nwarps) {
+    // Rows r0 + half (step 0) and r0 + 2 + half (step 1).
+    uint4 xv[2];
+    bool live[2];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) ss = __fadd_rn(ss, __fmul_rn(x[j], x[j]));
-    ss = row_allreduce<32>(ss, false, nullptr);
-    const float rs = rsqrtf(__fadd_rn(__fdiv_rn(ss, 128.f), L.eps));
-    float n[4], o[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) n[j] = __fmul_rn(__fmul_rn(x[j], rs), w[j]);
-    const float4 cs = __ldg(reinterpret_cast<const float4 *>(L.cosb + t * 128) + lane);
-    const float4 sn = __ldg(reinterpret_cast<const float4 *>(L.sinb + t * 128) + lane);
-    const float cv[4] = {cs.x, cs.y, cs.z, cs.w}, sv[4] = {sn.x, sn.y, sn.z, sn.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float partner = __shfl_xor_sync(0xffffffffu, n[j], 16);
-      const float rot = lane < 16 ? -partner : partner;
-      o[j] = __fadd_rn(__fmul_rn(n[j], cv[j]), __fmul_rn(rot, sv[j]));
+    for (int s = 0; s < 2; ++s) {
+      const uint32_t row = r0 + 2 * s + half;
+      live[s] = row < L.row_end;
+      xv[s] = live[s] ? __ldcs(reinterpret_cast<const uint4 *>(L.in + size_t(row) * 128) + sub) : make_uint4(0, 0, 0, 0);
     }
-    uint2 ov;
-    ov.x = pack_bf16x2(o[0], o[1]);
-    ov.y = pack_bf16x2(o[2], o[3]);
-    *reinterpret_cast<uint2 *>(L.out + t * L.tok_stride + h * L.head_stride + lane * 4) = ov;
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const uint32_t row = r0 + 2 * s + half;
+      const uint32_t t = row / L.heads, h = row - t * L.heads;
+      const uint32_t xs[4] = {xv[s].x, xv[s].y, xv[s].z, xv[s].w};
+      float x[8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        x[2 * j] = lo_bf16(xs[j]);
+        x[2 * j + 1] = hi_bf16(xs[j]);
+      }
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = __fadd_rn(ss, __fmul_rn(x[j], x[j]));
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(full, ss, o));   // within the half
+      const float rs = rsqrtf(__fadd_rn(__fdiv_rn(ss, 128.f), L.eps));
+      float n[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) n[j] = __fmul_rn(__fmul_rn(x[j], rs), w[j]);
+      const float4 *cp = reinterpret_cast<const float4 *>(L.cosb + size_t(t) * 128) + 2 * sub;
+      const float4 *sp = reinterpret_cast<const float4 *>(L.sinb + size_t(t) * 128) + 2 * sub;
+      const float4 c0 = __ldg(cp), c1 = __ldg(cp + 1), s0 = __ldg(sp), s1 = __ldg(sp + 1);
+      const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float partner = __shfl_xor_sync(full, n[j], 8);
+        const float rot = sub < 8 ? -partner : partner;
+        o[j] = __fadd_rn(__fmul_rn(n[j], cv[j]), __fmul_rn(rot, sv[j]));
+      }
+      if (live[s])
+        *reinterpret_cast<uint4 *>(L.out + int64_t(t) * L.tok_stride + int64_t(h) * L.head_stride + sub * 8) =
+            make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+    }
   }
 }
 
 int launch_qkrope(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c) {
   const ptsim_qkrope_params &p = d.p.qk;
   if (p.dim != 128) return fail(PTSIM_E_UNSUPPORTED, "QK-norm+RoPE runs head_dim 128, not %lld", (long long)p.dim);
-  if (p.out_tok_stride % 4 || p.out_head_stride % 4)
-    return fail(PTSIM_E_UNSUPPORTED, "QK-norm+RoPE output strides must keep 8-byte alignment");
+  if (p.out_tok_stride % 8 || p.out_head_stride % 8)
+    return fail(PTSIM_E_UNSUPPORTED, "QK-norm+RoPE output strides must keep 16-byte alignment");
+  if (p.tokens * p.heads >= (int64_t(1) << 31)) return fail(PTSIM_E_UNSUPPORTED, "QK-norm+RoPE over 2^31 rows");
   QkLaunch L;
   L.in = reinterpret_cast<const uint16_t *>(ptrs[p.in_arg]);
   L.w = reinterpret_cast<const uint16_t *>(ptrs[p.weight_arg]);
@@ -456,15 +483,16 @@ int launch_qkrope(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi
   L.sinb = reinterpret_cast<const float *>(ptrs[p.sin_arg]);
   L.out = reinterpret_cast<uint16_t *>(ptrs[p.out_arg]);
   const int64_t rows = p.tokens * p.heads;
-  L.row_begin = lo * d.unit_size;
-  L.row_end = hi * d.unit_size < rows ? hi * d.unit_size : rows;
-  L.heads = p.heads;
+  L.row_begin = uint32_t(lo * d.unit_size);
+  L.row_end = uint32_t(hi * d.unit_size < rows ? hi * d.unit_size : rows);
+  L.heads = uint32_t(p.heads);
   L.tok_stride = p.out_tok_stride;
   L.head_stride = p.out_head_stride;
   L.eps = p.eps;
   if (L.row_end <= L.row_begin) return PTSIM_OK;
-  int64_t blocks = ceil_div(L.row_end - L.row_begin, 8);
-  if (blocks > int64_t(c.sm_count) * 8) blocks = int64_t(c.sm_count) * 8;
+  // Four rows per warp per step, eight warps per block; enough blocks for one step of every row.
+  int64_t blocks = ceil_div(int64_t(L.row_end - L.row_begin), 32);
+  if (blocks > int64_t(c.sm_count) * 16) blocks = int64_t(c.sm_count) * 16;
   qk_rope_kernel<<<unsigned(blocks), 256, 0, c.stream>>>(L);
   PTSIM_CUDA(cudaGetLastError());
   return PTSIM_OK;
