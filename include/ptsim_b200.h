@@ -50,6 +50,7 @@ extern "C" {
 #define PTSIM_KIND_GEMM 5          /* C = A.B (+ residual), bf16 inputs, fp32 accumulate, cast on store */
 #define PTSIM_KIND_ATTN_PREFILL 6  /* causal GQA flash attention forward, fp32 online softmax */
 #define PTSIM_KIND_REDUCE_ALL 7    /* a whole-tensor sum or max to one fp32 value */
+#define PTSIM_KIND_ATTN_DECODE 8   /* one-token GQA attention: per KV head, G query rows over S keys */
 
 /* Element types of tensor arguments (kernel.json dtype names, contract/kernel_object.py:43-56). */
 #define PTSIM_DT_F32 0
@@ -137,6 +138,9 @@ typedef struct ptsim_gemm_params {
   int32_t pad0;
 } ptsim_gemm_params;
 
+/* ATTN_PREFILL: q, o [batch, hq, seq, dim]; k, v [batch, hkv, seq, dim].
+ * ATTN_DECODE (batch 1, one unit per KV head): q, o [hkv, hq / hkv, dim]; k, v [hkv, seq, dim];
+ * ref_bq = the program's padded row count GP, ref_bkv = its key block BKV. */
 typedef struct ptsim_attn_params {
   int64_t batch, hq, hkv, seq, dim;
   int32_t q_arg, k_arg, v_arg, o_arg;
@@ -198,7 +202,7 @@ int ptsim_launch(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int
                  int64_t lo, int64_t hi, void *workspace, size_t workspace_bytes, void *stream);
 
 /* Bytes of device scratch a launch of `desc` wants on `device` (-1 on a bad descriptor): the REDUCE_ALL
- * pass-1 partials, else desc->workspace_bytes.  No reference counterpart (Spike needed no device
+ * pass-1 partials, the ATTN_DECODE per-chunk softmax states, else desc->workspace_bytes.  No reference counterpart (Spike needed no device
  * scratch). */
 int64_t ptsim_workspace_size(const void *desc, size_t desc_bytes, int device);
 

@@ -166,6 +166,34 @@ def attention_prefill(q, k, v, batch, hq, g, seq, dim, bq, bkv, causal, scale):
     return out.reshape(-1)
 
 
+def attention_decode(q, k, v, o_init, hkv, g, gp, seq, dim, bkv, scale):
+    """validation/pytorchsim/attention_decode_32x8x4096_bf16/00__decode_kernel/_decode_kernel_triton.py:4-31, block
+    for block: program p (one KV head) loads its GP query rows (rows >= G masked to 0); m = -1e30, l = 0,
+    acc = 0; per key block of BKV: qk = (q . k^T) * SCALE in fp32, m' = max(m, rowmax qk), alpha = exp(m - m'),
+    p = exp(qk - m'), l = l*alpha + rowsum p, acc = acc*alpha + bf16(p) . v; the G real rows of
+    bf16(acc / l) are stored (o is inout: nothing else of it changes)."""
+    Q = torch.zeros(hkv, gp, dim)
+    Q[:, :g] = f32(q).view(hkv, g, dim)
+    Kt = f32(k).view(hkv, seq, dim)
+    V = f32(v).view(hkv, seq, dim)
+    sc = torch.tensor(scale, dtype=torch.float32)
+    m = torch.full((hkv, gp, 1), -1.0e30)
+    l = torch.zeros((hkv, gp, 1))
+    acc = torch.zeros((hkv, gp, dim))
+    for start in range(0, seq, bkv):
+        kb, vb = Kt[:, start:start + bkv], V[:, start:start + bkv]
+        qk = (Q @ kb.transpose(1, 2)) * sc
+        m_new = torch.maximum(m, torch.amax(qk, dim=2, keepdim=True))
+        alpha = npu_exp(m - m_new)
+        p = npu_exp(qk - m_new)
+        l = l * alpha + p.sum(dim=2, keepdim=True)
+        acc = acc * alpha + f32(p.to(torch.bfloat16)) @ vb
+        m = m_new
+    out = o_init.clone().view(hkv, g, dim)
+    out[:] = (acc / l)[:, :g].to(torch.bfloat16)
+    return out.reshape(-1)
+
+
 def rope_tables(tokens, dim=128, theta=1.0e6):
     """cos/sin tables [tokens, dim] in fp32 for RoPE with base `theta` (the Qwen3 layer feeds them as the
     fp32 inputs in_ptr2/in_ptr3 of 02/04)."""

@@ -25,6 +25,7 @@
 #include <atomic>
 #include <cudaTypedefs.h>
 #include "sm100.cuh"
+#include "gemv.cuh"
 
 namespace ptsim {
 
@@ -732,6 +733,8 @@ int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, 
   const int cdt = d.arg_dtype[p.c_arg];
   if (cdt != PTSIM_DT_BF16 && cdt != PTSIM_DT_F32) return fail(PTSIM_E_UNSUPPORTED, "GEMM output must be bf16 or f32");
   if (p.r_arg >= 0 && d.arg_dtype[p.r_arg] != PTSIM_DT_BF16) return fail(PTSIM_E_UNSUPPORTED, "GEMM residual must be bf16");
+  // One output row: the matrix-vector product, an HBM stream on the CUDA cores.
+  if (p.M == 1) return lo < hi ? launch_gemv(d, ptrs, c) : PTSIM_OK;
   if (p.K % 8 != 0 || p.lda % 8 != 0 || p.ldb % 8 != 0)
     return fail(PTSIM_E_UNSUPPORTED, "GEMM K and leading dimensions must be multiples of 8 (16-byte TMA rows)");
   const int64_t m_begin = lo * d.unit_size;

@@ -1,0 +1,219 @@
+// Matrix-vector product: the gemm_1x* programs of the validation bundle and the o-projection of the
+// Qwen3 decode layer (Inductor's M = 1 matmul, validation/pytorchsim/gemm_1x4096x4096_bf16/00_*_triton.py):
+// out[n] = bf16(sum_k fp32(a[k]) * fp32(B[k, n])), a multiply-reduce program the reference runs on its
+// vector unit (its MXU refuses M = 1, targets/tpu/lower_matmul.py:464-489).  Every element of B is read
+// once and used once (2 FLOP per 2 bytes), so this is an HBM stream on the CUDA cores, not tensor-core
+// work.
+//
+// N-contiguous B ([K, N], the Inductor layout): one cluster of S CTAs per tile of CW columns, each CTA
+// over K / S rows.  Thread t streams 8 adjacent columns of rows k0 + t / (CW / 8) + j * RG with 16-byte
+// loads, eight in flight; the RG row groups of a CTA meet in shared memory, then rank 0 of the cluster adds
+// the S partial columns in rank order through distributed shared memory -- a fixed summation order and
+// no device scratch.
+// K-major B ([N, K]): one warp per output column, 16-byte loads along K, a shuffle tree.
+#pragma once
+#include "sm100.cuh"
+
+namespace ptsim {
+
+constexpr int kGemvThreads = 256;
+constexpr int kGemvUnroll = 8;
+
+struct GemvArgs {
+  const uint16_t *a, *b, *r;   // a [K]; B; residual [N] or null
+  uint16_t *c;                 // bf16 output, or null
+  float *c_f32;                // fp32 output, or null
+  int64_t N, K, ldb;
+  int64_t k_per_cta;           // K rows per CTA of a cluster
+};
+
+__device__ __forceinline__ void gemv_fma8(float (&acc)[8], float a, const uint4 &v) {
+  acc[0] = fmaf(a, lo_bf16(v.x), acc[0]);
+  acc[1] = fmaf(a, hi_bf16(v.x), acc[1]);
+  acc[2] = fmaf(a, lo_bf16(v.y), acc[2]);
+  acc[3] = fmaf(a, hi_bf16(v.y), acc[3]);
+  acc[4] = fmaf(a, lo_bf16(v.z), acc[4]);
+  acc[5] = fmaf(a, hi_bf16(v.z), acc[5]);
+  acc[6] = fmaf(a, lo_bf16(v.w), acc[6]);
+  acc[7] = fmaf(a, hi_bf16(v.w), acc[7]);
+}
+
+__device__ __forceinline__ void gemv_store(const GemvArgs &g, int64_t n, float s) {
+  if (g.r != nullptr) s += bf16_bits_to_f32(g.r[n]);
+  if (g.c_f32 != nullptr) g.c_f32[n] = s;
+  else g.c[n] = f32_to_bf16_bits(s);
+}
+
+// TPRW threads per row of the tile (CW = 8 * TPRW columns); grid (column tiles, S) in clusters (1, S, 1).
+template <int TPRW>
+__global__ void __launch_bounds__(kGemvThreads) gemv_kn_kernel(const __grid_constant__ GemvArgs g) {
+  constexpr int CW = TPRW * 8, RG = kGemvThreads / TPRW, U = kGemvUnroll;
+  __shared__ float red[RG][CW];
+  __shared__ float part[CW];
+  const int tid = threadIdx.x;
+  const int cg = tid % TPRW, rg = tid / TPRW;
+  const int64_t n0 = int64_t(blockIdx.x) * CW + cg * 8;
+  const int64_t k_begin = int64_t(blockIdx.y) * g.k_per_cta;
+  const int64_t k_end = k_begin + g.k_per_cta < g.K ? k_begin + g.k_per_cta : g.K;
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+  if (n0 < g.N) {
+    const uint16_t *bp = g.b + n0;
+    int64_t k = k_begin + rg;
+    for (; k + (U - 1) * RG < k_end; k += U * RG) {
+      uint4 v[U];
+      float av[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        v[u] = __ldcs(reinterpret_cast<const uint4 *>(bp + (k + u * RG) * g.ldb));
+        av[u] = bf16_bits_to_f32(__ldg(g.a + k + u * RG));
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) gemv_fma8(acc, av[u], v[u]);
+    }
+    for (; k < k_end; k += RG) {
+      const uint4 v = __ldcs(reinterpret_cast<const uint4 *>(bp + k * g.ldb));
+      gemv_fma8(acc, bf16_bits_to_f32(__ldg(g.a + k)), v);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) red[rg][cg * 8 + j] = acc[j];
+  __syncthreads();
+  if (tid < CW) {
+    float s = 0.f;
+#pragma unroll 8
+    for (int i = 0; i < RG; ++i) s += red[i][tid];
+    part[tid] = s;
+  }
+  // Every CTA's partial columns are written (and, by the release/acquire of the cluster barrier, visible
+  // to the cluster) before rank 0 reads them; the second barrier keeps the peers resident until it has.
+  sm100::cluster_sync();
+  if (blockIdx.y == 0 && tid < CW) {
+    const int64_t n = int64_t(blockIdx.x) * CW + tid;
+    if (n < g.N) {
+      float s = part[tid];
+      const uint32_t addr = sm100::smem_u32(&part[tid]);
+      for (uint32_t q = 1; q < gridDim.y; ++q) s += sm100::ld_cluster_f32(sm100::mapa_shared(addr, q));
+      gemv_store(g, n, s);
+    }
+  }
+  sm100::cluster_sync();
+}
+
+// K-major B: warp w of CTA b computes column n = 8 b + w; lanes take 8 consecutive k, 256 k per step.
+__global__ void __launch_bounds__(kGemvThreads) gemv_nk_kernel(const __grid_constant__ GemvArgs g) {
+  const int lane = threadIdx.x & 31;
+  const int64_t n = int64_t(blockIdx.x) * (kGemvThreads / 32) + (threadIdx.x >> 5);
+  if (n >= g.N) return;
+  const uint16_t *row = g.b + n * g.ldb;
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+  int64_t k = int64_t(lane) * 8;
+  for (; k + 3 * 256 < g.K; k += 4 * 256) {
+    uint4 v[4], a[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      v[u] = __ldcs(reinterpret_cast<const uint4 *>(row + k + u * 256));
+      a[u] = __ldg(reinterpret_cast<const uint4 *>(g.a + k + u * 256));
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      acc[0] = fmaf(lo_bf16(a[u].x), lo_bf16(v[u].x), acc[0]);
+      acc[1] = fmaf(hi_bf16(a[u].x), hi_bf16(v[u].x), acc[1]);
+      acc[2] = fmaf(lo_bf16(a[u].y), lo_bf16(v[u].y), acc[2]);
+      acc[3] = fmaf(hi_bf16(a[u].y), hi_bf16(v[u].y), acc[3]);
+      acc[4] = fmaf(lo_bf16(a[u].z), lo_bf16(v[u].z), acc[4]);
+      acc[5] = fmaf(hi_bf16(a[u].z), hi_bf16(v[u].z), acc[5]);
+      acc[6] = fmaf(lo_bf16(a[u].w), lo_bf16(v[u].w), acc[6]);
+      acc[7] = fmaf(hi_bf16(a[u].w), hi_bf16(v[u].w), acc[7]);
+    }
+  }
+  for (; k < g.K; k += 256) {
+    const uint4 v = __ldcs(reinterpret_cast<const uint4 *>(row + k));
+    const uint4 a = __ldg(reinterpret_cast<const uint4 *>(g.a + k));
+    acc[0] = fmaf(lo_bf16(a.x), lo_bf16(v.x), acc[0]);
+    acc[1] = fmaf(hi_bf16(a.x), hi_bf16(v.x), acc[1]);
+    acc[2] = fmaf(lo_bf16(a.y), lo_bf16(v.y), acc[2]);
+    acc[3] = fmaf(hi_bf16(a.y), hi_bf16(v.y), acc[3]);
+    acc[4] = fmaf(lo_bf16(a.z), lo_bf16(v.z), acc[4]);
+    acc[5] = fmaf(hi_bf16(a.z), hi_bf16(v.z), acc[5]);
+    acc[6] = fmaf(lo_bf16(a.w), lo_bf16(v.w), acc[6]);
+    acc[7] = fmaf(hi_bf16(a.w), hi_bf16(v.w), acc[7]);
+  }
+  float s = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) gemv_store(g, n, s);
+}
+
+// The tile plan of an N-contiguous GEMV: the widest column tile whose clusters (K split in up to 8,
+// each CTA at least 128 rows) give every SM two CTAs; else 64-column tiles with the deepest split.
+struct GemvPlan {
+  int tprw, splits;
+  int64_t tiles, k_per_cta;
+};
+
+static GemvPlan plan_gemv(int64_t N, int64_t K, int sm_count) {
+  GemvPlan pl{8, 1, 0, K};
+  for (int tprw : {32, 16, 8}) {
+    const int64_t tiles = ceil_div(N, int64_t(tprw) * 8);
+    int s = 1;
+    while (s < 8 && tiles * s < 2 * sm_count && K / (2 * s) >= 128) s *= 2;
+    pl = GemvPlan{tprw, s, tiles, ceil_div(K, s)};
+    if (tiles * s >= 2 * sm_count) break;
+  }
+  return pl;
+}
+
+template <int TPRW>
+static int run_gemv_kn(const GemvArgs &g, const GemvPlan &pl, const LaunchCtx &c) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(pl.tiles), unsigned(pl.splits), 1);
+  cfg.blockDim = dim3(kGemvThreads, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = c.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = unsigned(pl.splits);
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  PTSIM_CUDA(cudaLaunchKernelEx(&cfg, gemv_kn_kernel<TPRW>, g));
+  return PTSIM_OK;
+}
+
+// The GEMM descriptor with M = 1 (checked by the caller), on the CUDA cores.
+static int launch_gemv(const ptsim_desc &d, void *const *ptrs, const LaunchCtx &c) {
+  const ptsim_gemm_params &p = d.p.gemm;
+  GemvArgs g;
+  memset(&g, 0, sizeof(g));
+  g.a = reinterpret_cast<const uint16_t *>(ptrs[p.a_arg]);
+  g.b = reinterpret_cast<const uint16_t *>(ptrs[p.b_arg]);
+  g.r = p.r_arg >= 0 ? reinterpret_cast<const uint16_t *>(ptrs[p.r_arg]) : nullptr;
+  if (d.arg_dtype[p.c_arg] == PTSIM_DT_F32) g.c_f32 = reinterpret_cast<float *>(ptrs[p.c_arg]);
+  else g.c = reinterpret_cast<uint16_t *>(ptrs[p.c_arg]);
+  g.N = p.N;
+  g.K = p.K;
+  g.ldb = p.ldb;
+  if (reinterpret_cast<uintptr_t>(g.b) % 16 != 0) return fail(PTSIM_E_ARGS, "GEMV matrix is not 16-byte aligned");
+  if (p.b_kmajor) {
+    if (p.K % 8 != 0 || p.ldb % 8 != 0 || reinterpret_cast<uintptr_t>(g.a) % 16 != 0)
+      return fail(PTSIM_E_UNSUPPORTED, "GEMV over [N, K] needs K and the row stride multiples of 8 and a 16-byte aligned vector");
+    const int64_t blocks = ceil_div(p.N, kGemvThreads / 32);
+    gemv_nk_kernel<<<unsigned(blocks), kGemvThreads, 0, c.stream>>>(g);
+    PTSIM_CUDA(cudaGetLastError());
+    return PTSIM_OK;
+  }
+  if (p.N % 8 != 0 || p.ldb % 8 != 0)
+    return fail(PTSIM_E_UNSUPPORTED, "GEMV over [K, N] needs N and the row stride multiples of 8");
+  const GemvPlan pl = plan_gemv(p.N, p.K, c.sm_count);
+  g.k_per_cta = pl.k_per_cta;
+  if (pl.tprw == 32) return run_gemv_kn<32>(g, pl, c);
+  if (pl.tprw == 16) return run_gemv_kn<16>(g, pl, c);
+  return run_gemv_kn<8>(g, pl, c);
+}
+
+}  // namespace ptsim

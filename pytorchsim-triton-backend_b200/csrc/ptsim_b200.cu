@@ -11,6 +11,7 @@
 #include "rowops.cuh"
 #include "gemm.cuh"
 #include "attention.cuh"
+#include "decode.cuh"
 
 namespace ptsim {
 
@@ -161,6 +162,20 @@ static int check_desc(const void *p, size_t bytes) {
         return fail(PTSIM_E_OOB, "attention tensors are smaller than batch x heads x seq x dim");
       break;
     }
+    case PTSIM_KIND_ATTN_DECODE: {
+      const ptsim_attn_params &a = d.p.attn;
+      if ((rc = check_arg(d, a.q_arg, "q")) || (rc = check_arg(d, a.k_arg, "k")) || (rc = check_arg(d, a.v_arg, "v")) ||
+          (rc = check_arg(d, a.o_arg, "o")))
+        return rc;
+      if (a.hkv < 1 || a.hq < a.hkv || a.hq % a.hkv != 0 || a.seq < 1 || a.dim < 1)
+        return fail(PTSIM_E_DESC, "decode attention with %lld query rows over %lld KV heads of %lld keys", (long long)a.hq,
+                    (long long)a.hkv, (long long)a.seq);
+      if (d.units != a.hkv || d.unit_size != 1) return fail(PTSIM_E_DESC, "decode attention has one unit per KV head");
+      if (a.hq * a.dim > d.arg_numel[a.q_arg] || a.hq * a.dim > d.arg_numel[a.o_arg] ||
+          a.hkv * a.seq * a.dim > d.arg_numel[a.k_arg] || a.hkv * a.seq * a.dim > d.arg_numel[a.v_arg])
+        return fail(PTSIM_E_OOB, "decode attention tensors are smaller than heads x (rows | keys) x dim");
+      break;
+    }
     case PTSIM_KIND_REDUCE_ALL: {
       const ptsim_reduce_params &r = d.p.red;
       if ((rc = check_arg(d, r.in_arg, "reduce input")) || (rc = check_arg(d, r.out_arg, "reduce output"))) return rc;
@@ -230,6 +245,7 @@ int ptsim_launch(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int
     case PTSIM_KIND_GEMM: return launch_gemm(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_ATTN_PREFILL: return launch_attention(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_REDUCE_ALL: return launch_reduce(d, dev_ptrs, lo, hi, workspace, workspace_bytes, c);
+    case PTSIM_KIND_ATTN_DECODE: return launch_decode(d, dev_ptrs, lo, hi, workspace, workspace_bytes, c);
   }
   return fail(PTSIM_E_DESC, "descriptor kind %u", d.kind);
 }
@@ -242,6 +258,7 @@ int64_t ptsim_workspace_size(const void *desc, size_t desc_bytes, int device) {
   if (device >= 0 && device_info(device, &info) == PTSIM_OK) sm_count = info.sm_count;
   int64_t need = d.workspace_bytes;
   if (d.kind == PTSIM_KIND_REDUCE_ALL && need < reduce_workspace(sm_count)) need = reduce_workspace(sm_count);
+  if (d.kind == PTSIM_KIND_ATTN_DECODE && need < decode_workspace(d, sm_count)) need = decode_workspace(d, sm_count);
   return need;
 }
 

@@ -137,6 +137,12 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
 }
+// Load one fp32 from a cluster peer's shared memory (addr from mapa_shared).
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
 // Bulk asynchronous copy from this CTA's shared memory into a cluster peer's (dst and bar are
 // shared::cluster addresses from mapa_shared); completion is counted on the peer's mbarrier.
 __device__ __forceinline__ void bulk_copy_s2c(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {

@@ -85,6 +85,27 @@ def attention(batch, hq, hkv, seq, dim=128, causal=True, scale=None, bq=1024, bk
     return d
 
 
+def attention_decode(hkv, group, seq, dim=128, scale=None, bkv=None, gp=16):
+    """The attention_decode_* program (validation/pytorchsim/attention_decode_32x8x4096_bf16/00__decode_kernel/
+    _decode_kernel_triton.py): grid hkv, q/o [hkv, group, dim], k/v [hkv, seq, dim]."""
+    nq, nk = hkv * group * dim, hkv * seq * dim
+    d = D.new(D.ATTN_DECODE, _args([("q_ptr", "bfloat16", nq), ("k_ptr", "bfloat16", nk), ("v_ptr", "bfloat16", nk),
+                                    ("o_ptr", "bfloat16", nq)]), (hkv, 1, 1), units=hkv, unit_size=1)
+    a = d.p.attn
+    a.batch, a.hq, a.hkv, a.seq, a.dim = 1, hkv * group, hkv, seq, dim
+    a.q_arg, a.k_arg, a.v_arg, a.o_arg = 0, 1, 2, 3
+    a.causal = 0
+    import math
+    a.scale = float(scale if scale is not None else 1.0 / math.sqrt(dim))
+    a.ref_bq, a.ref_bkv = gp, int(bkv or seq)
+    return d
+
+
+def gemv(N, K, b_kmajor=False, residual=False, out_dtype="bfloat16"):
+    """The gemm_1x* program (Inductor's M = 1 matmul, a multiply-reduce): out[n] = sum_k a[k] * B[k, n]."""
+    return gemm(1, N, K, residual=residual, b_kmajor=b_kmajor, out_dtype=out_dtype)
+
+
 def reduce_all(numel, op="sum", dtype="bfloat16"):
     d = D.new(D.REDUCE_ALL, _args([("in_ptr0", dtype, numel), ("out_ptr0", "float32", 1)]), [1], units=1, unit_size=1,
               workspace_bytes=D.REDUCE_WORKSPACE_BYTES)

@@ -11,9 +11,10 @@ MAGIC = 0x42535450  # "PTSB"
 MAX_ARGS, MAX_MAPS, MAX_DIGITS, MAX_CODE, MAX_REGS = 16, 8, 4, 32, 8
 
 # Kinds (PTSIM_KIND_*).
-ELEMENTWISE, ROW_SOFTMAX, ROW_RMSNORM, QKNORM_ROPE, GEMM, ATTN_PREFILL, REDUCE_ALL = 1, 2, 3, 4, 5, 6, 7
+ELEMENTWISE, ROW_SOFTMAX, ROW_RMSNORM, QKNORM_ROPE, GEMM, ATTN_PREFILL, REDUCE_ALL, ATTN_DECODE = 1, 2, 3, 4, 5, 6, 7, 8
 KIND_NAME = {ELEMENTWISE: "elementwise", ROW_SOFTMAX: "row_softmax", ROW_RMSNORM: "row_rmsnorm",
-             QKNORM_ROPE: "qknorm_rope", GEMM: "gemm", ATTN_PREFILL: "attn_prefill", REDUCE_ALL: "reduce_all"}
+             QKNORM_ROPE: "qknorm_rope", GEMM: "gemm", ATTN_PREFILL: "attn_prefill", REDUCE_ALL: "reduce_all",
+             ATTN_DECODE: "attn_decode"}
 
 # Element types (PTSIM_DT_*), keyed by kernel.json dtype names (contract/kernel_object.py NP_DTYPE keys).
 DTYPE_CODE = {"float32": 0, "bfloat16": 1, "float16": 2, "int32": 3, "int64": 4, "int16": 5, "int8": 6,
@@ -154,6 +155,10 @@ def describe(d):
     elif d.kind == ATTN_PREFILL:
         a = d.p.attn
         out.update(batch=a.batch, hq=a.hq, hkv=a.hkv, seq=a.seq, dim=a.dim, causal=bool(a.causal), scale=a.scale)
+    elif d.kind == ATTN_DECODE:
+        a = d.p.attn
+        out.update(hkv=a.hkv, group=a.hq // max(1, a.hkv), seq=a.seq, dim=a.dim, scale=a.scale,
+                   ref_bkv=a.ref_bkv)
     elif d.kind == REDUCE_ALL:
         out.update(numel=d.p.red.numel, op="max" if d.p.red.op == RED_MAX else "sum")
     return out

@@ -122,7 +122,7 @@ def written_args(desc):
         return [desc.p.qk.out_arg]
     if k == D.GEMM:
         return [desc.p.gemm.c_arg]
-    if k == D.ATTN_PREFILL:
+    if k in (D.ATTN_PREFILL, D.ATTN_DECODE):
         return [desc.p.attn.o_arg]
     if k == D.REDUCE_ALL:
         return [desc.p.red.out_arg]

@@ -121,6 +121,8 @@ def lower(spec, fn=None):
     if dots:
         if len(dots) >= 2 and {"HQ", "G", "S", "D", "SCALE"} <= set(spec.constexprs):
             return _lower_attention(spec, tree)
+        if len(dots) >= 2 and {"HKV", "G", "GP", "S", "D", "BKV", "SCALE"} <= set(spec.constexprs):
+            return _lower_decode(spec, tree)
         return _lower_gemm(spec, tree, src)
     prog = F.Evaluator(spec, F.Program()).run(src, name)
     if len(prog.stores) != 1:
@@ -141,6 +143,8 @@ def lower(spec, fn=None):
         return _lower_rmsnorm(spec, prog, st, loads)
     if "exp" in ops and {r.op for r in reduces} == {"max", "add"} and len(args) == 1:
         return _lower_softmax(spec, prog, st, reduces)
+    if ops == {"mul"} and len(reduces) == 1 and reduces[0].op == "add" and len(args) == 2:
+        return _lower_gemv(spec, prog, st, reduces[0])
     raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a reduction program of ops {sorted(ops)}")
 
 
@@ -378,6 +382,46 @@ def _lower_qknorm_rope(spec, prog, st, loads):
     return Lowered(d, D.describe(d))
 
 
+def _lower_gemv(spec, prog, st, red):
+    """Inductor's M = 1 matmul (validation/pytorchsim/gemm_1x*/00_*_triton.py): out[x] = sum over r of
+    fp32(a[r]) * fp32(B[x + N * r]), one reduction over r, cast on the store.  The reference refuses M = 1
+    on its MXU (targets/tpu/lower_matmul.py:464-489) and runs it on the vector unit; lowered here to a
+    GEMM descriptor with M = 1, which the executor runs on its matrix-vector path."""
+    n, k, _ = _row_sizes(spec, prog, "matrix-vector product")
+    prod = red.value
+    if not (isinstance(prod, F.Op) and prod.name == "mul" and all(isinstance(a, F.Load) for a in prod.args)):
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: the reduced value is not a product of two loads")
+    vec = [a for a in prod.args if a.index.vars() == {"r"}]
+    mat = [a for a in prod.args if a.index.vars() == {"x", "r"}]
+    if len(vec) != 1 or len(mat) != 1:
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: not a vector (over r) times a matrix (over x, r)")
+    vec, mat = vec[0], mat[0]
+    if vec.index.const != 0 or vec.index.terms != {F.Digit("r"): 1}:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: vector index {vec.index} is not r")
+    rk, xn = mat.index.coeff_of("r"), mat.index.coeff_of("x")
+    if mat.index.const != 0 or set(rk) != {F.Digit("r")} or set(xn) != {F.Digit("x")}:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: matrix index {mat.index} is not x * s + r * t")
+    sk, sn = rk[F.Digit("r")], xn[F.Digit("x")]
+    if sn == 1:
+        b_kmajor, ldb = 0, sk
+    elif sk == 1:
+        b_kmajor, ldb = 1, sn
+    else:
+        raise Refused(Reason.SHAPE_NOT_RUN, f"{spec.name}: matrix with strides ({sk}, {sn})")
+    if st.index.const != 0 or st.index.terms != {F.Digit("x"): 1}:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: store index {st.index} is not x")
+    for t, nm in ((vec.arg, "vector"), (mat.arg, "matrix")):
+        if spec.args[t].dtype != "bfloat16":
+            raise Refused(Reason.DTYPE_NOT_RUN, f"{spec.name}: {nm} operand is {spec.args[t].dtype}")
+    d = D.new(D.GEMM, _manifest_args(spec), spec.grid, units=1, unit_size=1)
+    g = d.p.gemm
+    g.M, g.N, g.K = 1, n, k
+    g.lda, g.ldb, g.ldc, g.ldr = k, ldb, n, n
+    g.a_arg, g.b_arg, g.c_arg, g.r_arg = vec.arg, mat.arg, st.arg, -1
+    g.b_kmajor = b_kmajor
+    return Lowered(d, D.describe(d))
+
+
 def _lower_reduce_all(spec, prog, st, reduces):
     xnumel = _lookup(spec, prog, "xnumel", default=1)
     cols = _lookup(spec, prog, "r0_numel", "rnumel")
@@ -504,4 +548,36 @@ def _lower_attention(spec, tree):
     a.causal = 1 if ce.get("CAUSAL", True) else 0
     a.scale = float(ce["SCALE"])
     a.ref_bq, a.ref_bkv = int(ce.get("BQ", 0)), int(ce.get("BKV", 0))
+    return Lowered(d, D.describe(d))
+
+
+def _lower_decode(spec, tree):
+    """The attention_decode_* program (validation/pytorchsim/attention_decode_32x8x4096_bf16/00__decode_kernel/
+    _decode_kernel_triton.py:4-31): program p = one KV head, q/o rows [p*G*D, (p+1)*G*D) (G real rows of GP),
+    k/v [p*S*D, (p+1)*S*D); online softmax over key blocks of BKV (unmasked loads: S is a multiple of BKV)."""
+    ce = spec.constexprs
+    HKV, G, GP, S, Dh, BKV = (int(ce[k]) for k in ("HKV", "G", "GP", "S", "D", "BKV"))
+    ptrs = _pointer_params(spec)
+    idx = {n: i for i, n in enumerate(ptrs)}
+    need = ("q_ptr", "k_ptr", "v_ptr", "o_ptr")
+    if not all(n in idx for n in need):
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: decode attention wants q_ptr, k_ptr, v_ptr, o_ptr")
+    if G < 1 or G > GP or BKV < 1 or S % BKV:
+        raise Refused(Reason.SHAPE_NOT_RUN, f"{spec.name}: G={G} GP={GP} S={S} BKV={BKV}")
+    gx = _grid_programs(spec)[0]
+    if gx != HKV:
+        raise Refused(Reason.SHAPE_NOT_RUN, f"{spec.name}: grid {gx} is not one program per KV head ({HKV})")
+    q, k = spec.args[idx["q_ptr"]], spec.args[idx["k_ptr"]]
+    if q.numel < HKV * G * Dh or k.numel < HKV * S * Dh or spec.args[idx["v_ptr"]].numel < HKV * S * Dh:
+        raise Refused(Reason.SHAPE_NOT_RUN, f"{spec.name}: tensors smaller than {HKV} heads x (G={G} | S={S}) x {Dh}")
+    for n in need:
+        if spec.args[idx[n]].dtype != "bfloat16":
+            raise Refused(Reason.DTYPE_NOT_RUN, f"{spec.name}: {n} is {spec.args[idx[n]].dtype}")
+    d = D.new(D.ATTN_DECODE, _manifest_args(spec), spec.grid, units=HKV, unit_size=1)
+    a = d.p.attn
+    a.batch, a.hq, a.hkv, a.seq, a.dim = 1, HKV * G, HKV, S, Dh
+    a.q_arg, a.k_arg, a.v_arg, a.o_arg = idx["q_ptr"], idx["k_ptr"], idx["v_ptr"], idx["o_ptr"]
+    a.causal = 0
+    a.scale = float(ce["SCALE"])
+    a.ref_bq, a.ref_bkv = GP, BKV
     return Lowered(d, D.describe(d))

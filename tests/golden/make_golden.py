@@ -128,6 +128,16 @@ def cases():
          {"family": "attention_prefill", "batch": 4, "hq": 32, "g": 4, "seq": 4096, "dim": 128, "causal": True,
           "scale": 1 / math.sqrt(128), "modify": "attention_batch4"}, False),
     ]
+    # Decode attention (SCALE 1/sqrt(128), GP 16, BKV = S in every bundle workload) and the M = 1 matmul
+    # (gemm_1xKxN: a multiply-reduce program, out[x] = sum_r in0[r] * in1[x + N r]).
+    for hq, s, gold in ((16, 128, True), (64, 512, True), (32, 4096, True), (32, 8192, False)):
+        g = hq // 8
+        out.append((f"attention_decode_{hq}x8x{s}", spec_file(f"attention_decode_{hq}x8x{s}_bf16", 0),
+                    {"family": "attention_decode", "hkv": 8, "g": g, "gp": 16, "seq": s, "dim": 128, "bkv": s,
+                     "scale": 1 / math.sqrt(128)}, gold))
+    for k, n, gold in ((384, 1152, True), (768, 768, True), (2048, 2048, True), (4096, 4096, False), (4096, 2048, False)):
+        out.append((f"gemm_1x{k}x{n}", spec_file(f"gemm_1x{k}x{n}_bf16", 0),
+                    {"family": "gemm", "M": 1, "N": n, "K": k, "residual": False}, gold))
     for m in (128, 512, 2048, 4096, 8192):
         out.append((f"gemm_{m}x4096x4096", spec_file(f"gemm_{m}x4096x4096_bf16", 0),
                     {"family": "gemm", "M": m, "N": 4096, "K": 4096, "residual": False}, False))

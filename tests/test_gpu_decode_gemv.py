@@ -1,0 +1,155 @@
+"""Parity of the decode-side programs on the B200 against the CPU oracle:
+
+  - the M = 1 matmul (gemm_1x* and the Qwen3 decode layer's o-projection, a multiply-reduce program the
+    reference runs on its vector unit) on the CUDA-core GEMV path: N-contiguous and K-major matrices,
+    ragged N and K, the residual epilogue, fp32 output;
+  - one-token GQA attention (attention_decode_*) on the split-key kernel: every group size 1-16, key
+    counts from one 64-key tile to 8192, head subsets launched as unit ranges.
+
+bf16 results: rtol = atol = 1e-2 (the bf16-store tolerance of the reference's
+tests/cases/mechanism/ops/ops_bf16_store_gemm.py), the absolute floor scaled by the result's RMS for
+the GEMV (its outputs grow with sqrt(K)).  Unit ranges: bit exact against the whole launch."""
+import math
+
+import pytest
+import torch
+
+from pytorchsim_triton_compiler.codegen import build as B
+from pytorchsim_triton_compiler.codegen import descriptors as D
+from pytorchsim_triton_compiler.runtime import cuda as RC
+from pytorchsim_triton_compiler.runtime import native
+from oracle import programs as O
+from tests._helpers import bits_equal, compare
+
+pytestmark = pytest.mark.gpu
+
+RTOL = ATOL = 1e-2
+
+
+def run(desc, tensors, lo=None, hi=None):
+    ts = [t.cuda() for t in tensors]
+    if lo is None:
+        RC.launch_tensors(D.to_bytes(desc), ts)
+    else:
+        RC.launch_tensors(D.to_bytes(desc), ts, lo, hi)
+    return [t.cpu() for t in ts]
+
+
+def _gemv_case(N, K, b_kmajor=False, residual=False, out_dtype="bfloat16", seed=21):
+    g = torch.Generator().manual_seed(seed)
+    a = torch.randn(K, generator=g).to(torch.bfloat16)
+    b = torch.randn(K * N, generator=g).to(torch.bfloat16)
+    r = torch.randn(N, generator=g).to(torch.bfloat16) if residual else None
+    d = B.gemv(N, K, b_kmajor=b_kmajor, residual=residual, out_dtype=out_dtype)
+    dt = getattr(torch, out_dtype)
+    out = run(d, ([r] if residual else []) + [a, b, torch.zeros(N, dtype=dt)])[-1]
+    want = O.gemm(a, b, 1, N, K, residual=r, b_kn=not b_kmajor, out_dtype=dt)
+    atol = ATOL * max(1.0, float(want.float().pow(2).mean().sqrt()))
+    ok, rep = compare(out, want, RTOL, atol)
+    assert ok, f"N={N} K={K} b_kmajor={b_kmajor} residual={residual} {out_dtype}: {rep}"
+
+
+@pytest.mark.parametrize("K,N", [(4096, 4096), (2048, 2048), (384, 1152), (768, 768), (4096, 2048), (2048, 128),
+                                 (3072, 768), (12288, 4096), (8, 8), (200, 72), (1000, 4104)])
+def test_gemv(K, N):
+    _gemv_case(N, K)
+
+
+@pytest.mark.parametrize("K,N", [(4096, 4096), (768, 3072), (264, 40), (4096, 12)])
+def test_gemv_b_kmajor(K, N):
+    _gemv_case(N, K, b_kmajor=True)
+
+
+def test_gemv_residual_and_fp32_output():
+    _gemv_case(4096, 4096, residual=True)
+    _gemv_case(1536, 512, out_dtype="float32")
+
+
+def test_gemv_refuses_ragged_columns():
+    """N-contiguous rows must be 16-byte vectors: N % 8 != 0 is refused, never approximated."""
+    d = B.gemv(12, 64)
+    ts = [torch.zeros(64, dtype=torch.bfloat16, device="cuda"), torch.zeros(64 * 12, dtype=torch.bfloat16, device="cuda"),
+          torch.zeros(12, dtype=torch.bfloat16, device="cuda")]
+    with pytest.raises(native.ExecutorError) as e:
+        RC.launch_tensors(D.to_bytes(d), ts)
+    assert e.value.code == D.E_UNSUPPORTED
+
+
+def _decode_inputs(hkv, g, seq, seed):
+    gen = torch.Generator().manual_seed(seed)
+    q = torch.randn(hkv * g * 128, generator=gen).to(torch.bfloat16)
+    k = torch.randn(hkv * seq * 128, generator=gen).to(torch.bfloat16)
+    v = torch.randn(hkv * seq * 128, generator=gen).to(torch.bfloat16)
+    o = torch.randn(hkv * g * 128, generator=gen).to(torch.bfloat16)   # inout: fully overwritten
+    return q, k, v, o
+
+
+@pytest.mark.parametrize("hkv,g,seq", [(8, 4, 4096), (8, 4, 8192), (8, 2, 128), (8, 8, 1024), (8, 3, 2048),
+                                       (1, 16, 64), (2, 1, 640), (4, 5, 192), (8, 16, 512), (3, 7, 8192)])
+def test_attention_decode(hkv, g, seq):
+    q, k, v, o = _decode_inputs(hkv, g, seq, 31)
+    d = B.attention_decode(hkv, g, seq)
+    out = run(d, [q, k, v, o])[3]
+    want = O.attention_decode(q, k, v, o, hkv, g, 16, seq, 128, seq, 1 / math.sqrt(128))
+    ok, rep = compare(out, want, RTOL, ATOL)
+    assert ok, f"hkv={hkv} G={g} S={seq}: {rep}"
+
+
+def test_attention_decode_reference_blocks():
+    """A program whose key block BKV is shorter than S (the reference restarts its running max per block):
+    the result stays within the bf16 tolerance of the block-for-block oracle."""
+    hkv, g, seq, bkv = 8, 4, 2048, 512
+    q, k, v, o = _decode_inputs(hkv, g, seq, 32)
+    out = run(B.attention_decode(hkv, g, seq, bkv=bkv), [q, k, v, o])[3]
+    want = O.attention_decode(q, k, v, o, hkv, g, 16, seq, 128, bkv, 1 / math.sqrt(128))
+    ok, rep = compare(out, want, RTOL, ATOL)
+    assert ok, rep
+
+
+def test_attention_decode_peaked_scores():
+    """Keys aligned with the query (one dominant score per head): the split-key merge carries the
+    maximum across chunks without losing the other keys' mass."""
+    hkv, g, seq = 4, 4, 4096
+    q, k, v, o = _decode_inputs(hkv, g, seq, 33)
+    kk = k.view(hkv, seq, 128).float()
+    qq = q.view(hkv, g, 128).float()
+    for h in range(hkv):
+        kk[h, 1234 + 500 * h] = qq[h, 0] * 0.5
+    k = kk.to(torch.bfloat16).reshape(-1)
+    out = run(B.attention_decode(hkv, g, seq), [q, k, v, o])[3]
+    want = O.attention_decode(q, k, v, o, hkv, g, 16, seq, 128, seq, 1 / math.sqrt(128))
+    ok, rep = compare(out, want, RTOL, ATOL)
+    assert ok, rep
+
+
+def test_attention_decode_unit_ranges_compose():
+    """Heads [0, 3) then [3, 8) write exactly what one launch of all 8 writes (the split plan follows the
+    whole launch, so each head's chunks and merge order are the same)."""
+    hkv, g, seq = 8, 4, 4096
+    q, k, v, o = _decode_inputs(hkv, g, seq, 34)
+    d = B.attention_decode(hkv, g, seq)
+    whole = run(d, [q, k, v, o])[3]
+    ts = [t.cuda() for t in (q, k, v, o)]
+    RC.launch_tensors(D.to_bytes(d), ts, 0, 3)
+    RC.launch_tensors(D.to_bytes(d), ts, 3, 8)
+    assert bits_equal(ts[3].cpu(), whole)
+
+
+def test_attention_decode_workspace_is_required():
+    native.init(0)
+    d = B.attention_decode(8, 4, 4096)
+    blob = D.to_bytes(d)
+    assert native.workspace_size(blob, 0) > 0
+    ts = [t.cuda() for t in _decode_inputs(8, 4, 4096, 35)]
+    with pytest.raises(native.ExecutorError) as e:
+        native.launch(blob, [t.data_ptr() for t in ts], 0, 8, 0, 0, torch.cuda.current_stream().cuda_stream)
+    assert e.value.code == D.E_RESOURCE
+
+
+def test_attention_decode_refuses_unsupported():
+    """Head dim other than 128 and key counts off the 64-key tile are refused."""
+    for d in (B.attention_decode(2, 4, 100), B.attention_decode(2, 4, 256, dim=64)):
+        ts = [torch.zeros(int(n), dtype=torch.bfloat16, device="cuda") for n in list(d.arg_numel)[:4]]
+        with pytest.raises(native.ExecutorError) as e:
+            RC.launch_tensors(D.to_bytes(d), ts)
+        assert e.value.code == D.E_UNSUPPORTED

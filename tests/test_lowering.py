@@ -69,3 +69,30 @@ def test_reference_kernels_lower_to_the_committed_descriptors(name):
     spec = load_spec(os.path.join(REF, case["source"]))
     lo = L.lower(spec)
     assert lo.blob == ko.read_desc(d), name
+
+
+@pytest.mark.skipif(not os.path.isdir(REF), reason="the reference tree is only in the build container")
+def test_every_decode_and_m1_workload_lowers():
+    """All attention_decode_* (28) and gemm_1x* (13) workloads of the bundle lower: decode to one unit per KV
+    head with the program's G, S and BKV; the M = 1 matmul (a multiply-reduce program) to a GEMM descriptor
+    with M = 1, N = xnumel and K = r0_numel over the N-contiguous matrix."""
+    base = os.path.join(REF, "validation", "pytorchsim")
+    seen = {"decode": 0, "gemv": 0}
+    for wl in sorted(os.listdir(base)):
+        if not (wl.startswith("attention_decode_") or wl.startswith("gemm_1x")):
+            continue
+        kd = os.path.join(base, wl, next(n for n in sorted(os.listdir(os.path.join(base, wl))) if n.startswith("00_")))
+        spec = load_spec(os.path.join(kd, next(f for f in os.listdir(kd) if f.endswith("_spec.py"))))
+        desc = D.from_bytes(L.lower(spec).blob)
+        if wl.startswith("attention_decode_"):
+            hq, hkv, s = (int(v) for v in wl.split("_")[2].split("x"))
+            a = desc.p.attn
+            assert desc.kind == D.ATTN_DECODE and desc.units == hkv == a.hkv, wl
+            assert (a.hq, a.seq, a.dim, a.ref_bq, a.ref_bkv) == (hq, s, 128, 16, s), wl
+            seen["decode"] += 1
+        else:
+            k, n = (int(v) for v in wl.split("_")[1].split("x")[1:3])
+            g = desc.p.gemm
+            assert desc.kind == D.GEMM and (g.M, g.N, g.K, g.b_kmajor, g.ldb) == (1, n, k, 0, n), wl
+            seen["gemv"] += 1
+    assert seen == {"decode": 28, "gemv": 13}

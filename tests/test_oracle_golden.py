@@ -76,6 +76,9 @@ def run_oracle(case, ins):
         if o["residual"]:
             return outs[0], O.gemm(x[1], x[2], o["M"], o["N"], o["K"], residual=x[0])
         return outs[0], O.gemm(x[0], x[1], o["M"], o["N"], o["K"])
+    if fam == "attention_decode":
+        return outs[0], O.attention_decode(x[0], x[1], x[2], x[3], o["hkv"], o["g"], o["gp"], o["seq"], o["dim"],
+                                           o["bkv"], o["scale"])
     if fam == "attention_prefill":
         bq = case.get("ref_bq") or min(1024, o["seq"])
         return outs[0], O.attention_prefill(x[0], x[1], x[2], o["batch"], o["hq"], o["g"], o["seq"], o["dim"],
