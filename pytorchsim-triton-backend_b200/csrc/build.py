@@ -15,8 +15,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.join(os.path.dirname(HERE), "pytorchsim_triton_compiler", "_lib")
 OUT = os.path.join(PKG, "libptsim_b200.so")
 SOURCES = ["ptsim_b200.cu"]
-DEPS = ["common.cuh", "elementwise.cuh", "rowops.cuh", "gemm.cuh", "attention.cuh", "sm100.cuh",
-        os.path.join("..", "..", "include", "ptsim_b200.h")]
+# Every kernel header of this directory (the translation unit includes them) and the ABI header.
+DEPS = sorted(f for f in os.listdir(HERE) if f.endswith(".cuh")) + [os.path.join("..", "..", "include", "ptsim_b200.h")]
 
 
 def nvcc():
