@@ -14,6 +14,9 @@ device holding the tensor arguments (runtime/cuda.py launch_tensors), in place, 
 import json
 import os
 
+from triton.backends.compiler import GPUTarget
+from triton.backends.driver import DriverBase
+
 _LAUNCHER = None
 
 
@@ -61,6 +64,84 @@ class _Launcher:
             kobj = json.dumps({**json.loads(kobj), "constexprs": self.constexprs})
         _launcher()(function, kobj, (grid_x, grid_y, grid_z), args,
                     artifacts=getattr(self.metadata, "artifacts", None))
+
+
+class _Utils:
+    """What Triton's CompiledKernel asks of a driver before a launch: the device's limits and the binary
+    loaded.  The descriptor is its own handle: the registered launcher runs it."""
+
+    def get_device_properties(self, device):
+        _launcher()
+        return {"max_shared_mem": 2 ** 62}
+
+    def load_binary(self, name, kernel, shared, device):
+        _launcher()
+        return kernel, kernel, 0, 0, 1
+
+    def unload_module(self, module):
+        pass
+
+
+class CPUDriver(DriverBase):
+    """Triton's driver for kernels compiled by this backend (the reference's class name; the launches it
+    makes go to the registered launcher, cuda_launcher for the B200).  Never selected automatically: the
+    device owner makes it active with triton.runtime.driver.set_active(CPUDriver())."""
+
+    def __init__(self):
+        self.utils = _Utils()
+        self.launcher_cls = _Launcher
+
+    def get_current_device(self):
+        return 0
+
+    def get_current_stream(self, device):
+        return 0
+
+    def set_current_device(self, device):
+        pass
+
+    @staticmethod
+    def is_active():
+        return False
+
+    def map_python_to_cpp_type(self, ty: str) -> str:
+        raise NotImplementedError("the pytorchsim backend maps no C types: it launches through set_launcher")
+
+    def get_current_target(self):
+        return GPUTarget("b200", 100, 32)
+
+    def get_active_torch_device(self):
+        import torch
+        return torch.device("cuda", 0)
+
+    def get_device_interface(self):
+        import torch
+        return torch.cuda
+
+    def get_benchmarker(self):
+        raise NotImplementedError("the pytorchsim backend benchmarks nothing itself")
+
+    def get_empty_cache_for_benchmark(self):
+        raise NotImplementedError("the pytorchsim backend benchmarks nothing itself")
+
+    def clear_cache(self, cache):
+        pass
+
+
+class activated:
+    """`with activated(): ...` makes a CPUDriver Triton's active driver for the block and then restores the one
+    that was active before (also when none was: Triton then creates its default again on first use)."""
+
+    def __enter__(self):
+        from triton.runtime import driver
+        self._saved = driver._active
+        driver.set_active(CPUDriver())
+        return driver.active
+
+    def __exit__(self, *exc):
+        from triton.runtime import driver
+        driver._active = self._saved
+        return False
 
 
 def cuda_launcher(binary, kernel_object, grid, args, artifacts=None):

@@ -425,11 +425,12 @@ class Evaluator:
 
     def is_extent(self, idx, n):
         """Whether `idx < n` only guards the launch's own extent: idx is the global row (x) or reduction (r)
-        index and n its numel, so the mask holds for every element the program owns."""
+        index and n its numel (a scalar or constexpr named as the pointwise lowering reads the extent), so the
+        mask holds for every element the launch stores (the store is clamped to n)."""
         d = idx.single()
         if d is None or d.div != 1 or d.mod is not None:
             return False
-        names = {"x": ("xnumel",), "r": ("r0_numel", "rnumel")}.get(d.var, ())
+        names = {"x": ("xnumel", "n", "N", "numel", "n_elements"), "r": ("r0_numel", "rnumel")}.get(d.var, ())
         return any(isinstance(self.env.get(nm), int) and self.env.get(nm) == n for nm in names)
 
     def index_of(self, v):
