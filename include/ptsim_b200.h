@@ -51,6 +51,10 @@ extern "C" {
 #define PTSIM_KIND_ATTN_PREFILL 6  /* causal GQA flash attention forward, fp32 online softmax */
 #define PTSIM_KIND_REDUCE_ALL 7    /* a whole-tensor sum or max to one fp32 value */
 #define PTSIM_KIND_ATTN_DECODE 8   /* one-token GQA attention: per KV head, G query rows over S keys */
+#define PTSIM_KIND_ROW_DIVSUM 9    /* each row divided by its sum (the MoE router's top-k weight normalisation) */
+#define PTSIM_KIND_TOPK 10         /* per row, the K largest (or smallest) values and their column indices */
+#define PTSIM_KIND_SORT 11         /* per row, a stable sort of the keys: sorted values and source indices */
+#define PTSIM_KIND_GATHER_ROWS 12  /* out[r, :] = table[t(r), :], t an integer program of an index loaded per row */
 
 /* Element types of tensor arguments (kernel.json dtype names, contract/kernel_object.py:43-56). */
 #define PTSIM_DT_F32 0
@@ -149,6 +153,60 @@ typedef struct ptsim_attn_params {
   int64_t ref_bq, ref_bkv;     /* the reference program's query/key block sizes (its m_i/l_i restarts) */
 } ptsim_attn_params;
 
+/* TOPK and SORT: `rows` rows of `cols` values (row stride `cols`) in `in_arg`.  TOPK writes k values and
+ * their int64 column indices per row (row stride k) to `val_arg` / `idx_arg`, choosing among the program's
+ * `cols_padded` candidate columns (columns past `cols` hold the spent value); `descending` = the largest.
+ * SORT writes every row sorted (ties in source order) with int64 source indices; `descending` sorts high to
+ * low; `float_keys` orders fp32 keys by their bits (NaN after +inf, -0 equal to +0, both canonicalised in
+ * the sorted values). */
+typedef struct ptsim_select_params {
+  int64_t rows, cols, k, cols_padded;
+  int32_t in_arg, val_arg, idx_arg, descending;
+  int32_t float_keys, pad0;
+} ptsim_select_params;
+
+/* One instruction of a gather's int64 index program (registers r0..r31):
+ *   LOAD  dst = the row's index element            CONST dst = imm
+ *   ADD SUB MUL AND OR XOR SHL SHR(arithmetic) dst = a op b
+ *   DIV MOD  dst = a / b, a % b truncated toward zero (0 when b == 0)
+ *   INV dst = ~a    LT LE GT GE EQ NE  dst = (a op b) ? 1 : 0    WHERE dst = c ? a : b */
+#define PTSIM_I_LOAD 1
+#define PTSIM_I_CONST 2
+#define PTSIM_I_ADD 3
+#define PTSIM_I_SUB 4
+#define PTSIM_I_MUL 5
+#define PTSIM_I_DIV 6
+#define PTSIM_I_MOD 7
+#define PTSIM_I_INV 8
+#define PTSIM_I_LT 9
+#define PTSIM_I_LE 10
+#define PTSIM_I_GT 11
+#define PTSIM_I_GE 12
+#define PTSIM_I_EQ 13
+#define PTSIM_I_NE 14
+#define PTSIM_I_WHERE 15
+#define PTSIM_I_AND 16
+#define PTSIM_I_OR 17
+#define PTSIM_I_XOR 18
+#define PTSIM_I_SHR 19
+#define PTSIM_I_SHL 20
+#define PTSIM_MAX_ICODE 32
+
+typedef struct ptsim_iinsn {
+  uint8_t op, dst, a, b, c, pad0, pad1, pad2;
+  int64_t imm;
+} ptsim_iinsn;
+
+/* GATHER_ROWS: out [rows, cols] row-major; row r copies table row t (the result register of the last
+ * instruction) of a [table_rows, cols] table, converting the element type where the two differ; the
+ * program's LOAD reads idx_arg at idx_map applied to r.  A t outside [0, table_rows) records PTSIM_E_OOB. */
+typedef struct ptsim_gather_params {
+  int64_t rows, cols, table_rows;
+  int32_t out_arg, table_arg, idx_arg, ncode;
+  ptsim_map idx_map;
+  ptsim_iinsn code[PTSIM_MAX_ICODE];
+} ptsim_gather_params;
+
 typedef struct ptsim_reduce_params {
   int64_t numel;
   int32_t in_arg, out_arg, op, pad0;
@@ -174,6 +232,8 @@ typedef struct ptsim_desc {
     ptsim_gemm_params gemm;
     ptsim_attn_params attn;
     ptsim_reduce_params red;
+    ptsim_select_params sel;
+    ptsim_gather_params gat;
   } p;
 } ptsim_desc;
 

@@ -76,13 +76,14 @@ def silu_mul(x, tokens, inter):
 # Row programs
 # ---------------------------------------------------------------------------------------------------
 
-def softmax_rows(x, rows, cols):
+def softmax_rows(x, rows, cols, out_dtype=torch.bfloat16):
     """validation/pytorchsim/vector_softmax_*/00_*_triton.py:17-68: per row m = max (NaN-propagating),
-    s = sum exp(x - m), out = bf16(exp(x - m) / s)."""
+    s = sum exp(x - m), out = bf16(exp(x - m) / s).  The MoE router's softmax
+    (layer_op_router_post_*/00_*) stores the same quotient as fp32."""
     v = f32(x).view(rows, cols)
     m = nan_max(v, 1)
     e = npu_exp(v - m)
-    return bf16(e / e.sum(dim=1, keepdim=True)).reshape(-1)
+    return (e / e.sum(dim=1, keepdim=True)).to(out_dtype).reshape(-1)
 
 
 def rmsnorm_rows(x, w, rows, cols, eps):
@@ -192,6 +193,74 @@ def attention_decode(q, k, v, o_init, hkv, g, gp, seq, dim, bkv, scale):
     out = o_init.clone().view(hkv, g, dim)
     out[:] = (acc / l)[:, :g].to(torch.bfloat16)
     return out.reshape(-1)
+
+
+# ---------------------------------------------------------------------------------------------------
+# Mixture-of-experts routing programs (the Qwen3-30B-A3B layer ops of the validation bundle)
+# ---------------------------------------------------------------------------------------------------
+
+def topk_rows(x, rows, cols, cols_padded, k, largest=True):
+    """layer_op_router_post_*/01__topk_kernel/_topk_kernel_triton.py:3-26: per row, columns past `cols` (up to
+    the program's EP = cols_padded) hold the spent value (-inf for largest); k passes each take the best value,
+    then the smallest column holding it, and overwrite that column with the spent value.  Returns (values,
+    int64 column indices), k per row."""
+    spent = float("-inf") if largest else float("inf")
+    X = torch.full((rows, cols_padded), spent, dtype=torch.float32)
+    X[:, :cols] = f32(x).view(rows, cols)
+    c = torch.arange(cols_padded)
+    vals = torch.zeros(rows, k, dtype=torch.float32)
+    idxs = torch.zeros(rows, k, dtype=torch.int64)
+    r = torch.arange(rows)
+    for n in range(k):
+        best = X.max(dim=1).values if largest else X.min(dim=1).values
+        at = torch.where(X == best[:, None], c, cols_padded).min(dim=1).values
+        vals[:, n], idxs[:, n] = best, at
+        X[r, at.clamp(max=cols_padded - 1)] = spent
+    return vals.to(x.dtype).reshape(-1), idxs.reshape(-1)
+
+
+def sort_rows(x, rows, cols, descending=False, float_keys=False):
+    """layer_op_dispatch_*/00__sort_kernel/_sort_kernel_triton.py:3-53: each row sorted by the key k = x (int64)
+    or, for fp32, bits b = (NaN -> 0x7FC00000, +-0 -> 0) mapped to the order-preserving b ^ ((b >> 31) &
+    0x7FFFFFFF); descending sorts ~k; ties by source position (the network compares (k, position)).  The
+    stored values are the sorted keys mapped back, positions as int64."""
+    if float_keys:
+        f = f32(x).view(rows, cols)
+        b = f.view(torch.int32).clone()
+        b = torch.where(torch.isnan(f), torch.full_like(b, 0x7FC00000), b)
+        b = torch.where(f == 0, torch.zeros_like(b), b)
+        k = (b ^ ((b >> 31) & 0x7FFFFFFF)).to(torch.int64)
+    else:
+        k = x.view(rows, cols).to(torch.int64)
+    if descending:
+        k = ~k
+    order = torch.sort(k, dim=1, stable=True).indices
+    ks = torch.gather(k, 1, order)
+    if descending:
+        ks = ~ks
+    if float_keys:
+        b = ks.to(torch.int32)
+        vals = (b ^ ((b >> 31) & 0x7FFFFFFF)).view(torch.float32)
+    else:
+        vals = ks
+    return vals.to(x.dtype).reshape(-1), order.reshape(-1)
+
+
+def row_divsum(x, rows, cols, out_dtype=torch.bfloat16):
+    """layer_op_router_post_*/02_*_triton.py: out = (x / sum(x)) per row in fp32, cast on the store."""
+    v = f32(x).view(rows, cols)
+    return (v / v.sum(dim=1, keepdim=True)).to(out_dtype).reshape(-1)
+
+
+def dispatch_gather(idx, table, tokens, hidden, topk):
+    """layer_op_dispatch_*/01_*_triton.py: output row r (of `hidden` values) is token t of the table, t =
+    Python floor division of the sorted position idx[r] by top-k (the kernel's ~ / // / ~ sequence), negative t
+    wrapped by + tokens; the kernel asserts 0 <= t < tokens.  bf16 -> fp32 -> bf16 is a copy."""
+    q = torch.div(idx.to(torch.int64), topk, rounding_mode="floor")
+    q = torch.where(q < 0, q + tokens, q)
+    if not bool(((q >= 0) & (q < tokens)).all()):
+        raise IndexError("dispatch gather index out of range (the reference asserts)")
+    return table.view(tokens, hidden)[q].reshape(-1)
 
 
 def rope_tables(tokens, dim=128, theta=1.0e6):

@@ -125,5 +125,8 @@ int launch_attention(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t
 int launch_decode(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, void *ws, size_t ws_bytes,
                   const LaunchCtx &c);
 int64_t decode_workspace(const ptsim_desc &d, int sm_count);
+int launch_topk(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c);
+int launch_sort(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c);
+int launch_gather_rows(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c);
 
 }  // namespace ptsim

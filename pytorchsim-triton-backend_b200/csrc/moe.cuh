@@ -1,0 +1,410 @@
+// Mixture-of-experts routing programs of the validation bundle (the Qwen3-30B-A3B layer ops):
+//
+//   topk_kernel  validation/pytorchsim/layer_op_router_post_*/01__topk_kernel: per row of E values, K passes;
+//                pass n takes the best value (largest, or smallest) among the program's EP candidate columns
+//                (columns past E hold the spent value, -inf for largest), then the smallest column holding
+//                it, and overwrites that column with the spent value.  Spent columns stay candidates, so a
+//                row with fewer than K finite values repeats an index, exactly as the reference does.  One
+//                warp per row, the row in registers, warp shuffles for the best value and the first column.
+//   sort_kernel  validation/pytorchsim/layer_op_dispatch_*/00__sort_kernel: each row sorted by the key
+//                k = x (int) or the order-preserving integer of an fp32 x (NaN canonical and last, -0 equal
+//                to +0), complemented when descending, ties broken by source position -- a unique order,
+//                so any correct sort gives the reference's output.  One 1024-thread CTA per row:
+//                  - keys spanning at most 256 values (the expert ids being routed): a stable counting sort,
+//                    each warp owning a contiguous segment; per-warp histograms by __match_any_sync, one
+//                    prefix over (key, warp), and a second pass that scatters every key to its offset plus
+//                    its rank among equal keys before it in the warp's chunk;
+//                  - otherwise a bitonic sort of (key, position) pairs in shared memory, up to 8192 keys;
+//                  - a longer row with a wider key range records PTSIM_E_UNSUPPORTED in the status word.
+#pragma once
+#include <climits>
+#include "common.cuh"
+
+namespace ptsim {
+
+struct TopkArgs {
+  const void *x;
+  void *v;
+  int64_t *idx;
+  int64_t row_begin, row_end, cols, k, cols_padded;
+  int32_t x_dt, v_dt, largest, pad;
+};
+
+template <int NPL>
+__global__ void __launch_bounds__(256) topk_kernel(const __grid_constant__ TopkArgs g) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = g.row_begin + ((int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
+  if (r >= g.row_end) return;
+  const float spent = g.largest ? -INFINITY : INFINITY;
+  float x[NPL];
+#pragma unroll
+  for (int j = 0; j < NPL; ++j) {
+    const int64_t c = int64_t(j) * 32 + lane;
+    x[j] = c < g.cols ? ld_any(g.x, g.x_dt, r * g.cols + c) : spent;
+  }
+  for (int64_t n = 0; n < g.k; ++n) {
+    float b = spent;
+#pragma unroll
+    for (int j = 0; j < NPL; ++j)
+      if (int64_t(j) * 32 + lane < g.cols_padded) b = g.largest ? fmaxf(b, x[j]) : fminf(b, x[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float w = __shfl_xor_sync(0xffffffffu, b, o);
+      b = g.largest ? fmaxf(b, w) : fminf(b, w);
+    }
+    int at = 0x7fffffff;
+#pragma unroll
+    for (int j = NPL - 1; j >= 0; --j) {
+      const int c = j * 32 + lane;
+      if (c < g.cols_padded && x[j] == b) at = c;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) at = min(at, __shfl_xor_sync(0xffffffffu, at, o));
+    if (lane == 0) {
+      st_any(g.v, g.v_dt, r * g.k + n, b);
+      g.idx[r * g.k + n] = at;
+    }
+#pragma unroll
+    for (int j = 0; j < NPL; ++j)
+      if (j * 32 + lane == at) x[j] = spent;
+  }
+}
+
+struct SortArgs {
+  const void *x;
+  void *v;
+  int64_t *idx;
+  int64_t row_begin, cols;
+  int32_t x_dt, v_dt, descending, float_keys;
+};
+
+constexpr int kSortThreads = 1024;
+constexpr int kSortWarps = kSortThreads / 32;
+constexpr int kSortCountRange = 256;
+constexpr int kSortBitonicMax = 8192;
+constexpr int kSortSmem = kSortBitonicMax * 12 + 512;   // keys (8 B) + positions (4 B); the histogram fits inside
+
+__device__ __forceinline__ int64_t sort_key(const SortArgs &g, int64_t at) {
+  int64_t k;
+  if (g.float_keys) {
+    const float f = reinterpret_cast<const float *>(g.x)[at];
+    const int32_t bits = f != f ? 0x7FC00000 : (f == 0.0f ? 0 : __float_as_int(f));
+    k = int64_t(bits ^ ((bits >> 31) & 0x7FFFFFFF));
+  } else {
+    k = g.x_dt == PTSIM_DT_I32 ? int64_t(reinterpret_cast<const int32_t *>(g.x)[at])
+                               : reinterpret_cast<const int64_t *>(g.x)[at];
+  }
+  return g.descending ? ~k : k;
+}
+
+__device__ __forceinline__ void sort_store(const SortArgs &g, int64_t at, int64_t k, int64_t src) {
+  if (g.descending) k = ~k;
+  if (g.float_keys) {
+    const int32_t bits = int32_t(k);
+    st_any(g.v, g.v_dt, at, __int_as_float(bits ^ ((bits >> 31) & 0x7FFFFFFF)));
+  } else if (g.v_dt == PTSIM_DT_I32) {
+    reinterpret_cast<int32_t *>(g.v)[at] = int32_t(k);
+  } else {
+    reinterpret_cast<int64_t *>(g.v)[at] = k;
+  }
+  g.idx[at] = src;
+}
+
+__global__ void __launch_bounds__(kSortThreads, 1) sort_kernel(const __grid_constant__ SortArgs g) {
+  extern __shared__ __align__(16) uint8_t sort_smem[];
+  __shared__ long long s_min[kSortWarps], s_max[kSortWarps];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t r = g.row_begin + blockIdx.x;
+  const int64_t base = r * g.cols;
+  const int64_t n = g.cols;
+  // 1. the row's key range
+  long long lo = LLONG_MAX, hi = LLONG_MIN;
+  for (int64_t c = tid; c < n; c += kSortThreads) {
+    const long long k = sort_key(g, base + c);
+    lo = k < lo ? k : lo;
+    hi = k > hi ? k : hi;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const long long a = __shfl_xor_sync(0xffffffffu, lo, o), b = __shfl_xor_sync(0xffffffffu, hi, o);
+    lo = a < lo ? a : lo;
+    hi = b > hi ? b : hi;
+  }
+  if (lane == 0) {
+    s_min[warp] = lo;
+    s_max[warp] = hi;
+  }
+  __syncthreads();
+  lo = s_min[0];
+  hi = s_max[0];
+  for (int w = 1; w < kSortWarps; ++w) {
+    lo = s_min[w] < lo ? s_min[w] : lo;
+    hi = s_max[w] > hi ? s_max[w] : hi;
+  }
+  if (n == 0) return;
+  const unsigned long long span = static_cast<unsigned long long>(hi) - static_cast<unsigned long long>(lo);
+  if (span < kSortCountRange) {
+    // 2a. stable counting sort; hist[w][key] = warp w's count, then its first output position.
+    int *hist = reinterpret_cast<int *>(sort_smem);   // [kSortWarps][kSortCountRange]
+    for (int i = tid; i < kSortWarps * kSortCountRange; i += kSortThreads) hist[i] = 0;
+    __syncthreads();
+    const int64_t seg = ceil_div(n, kSortWarps);
+    const int64_t s0 = warp * seg, s1 = s0 + seg < n ? s0 + seg : n;
+    for (int64_t c0 = s0; c0 < s1; c0 += 32) {
+      const int64_t c = c0 + lane;
+      const int key = c < s1 ? int(sort_key(g, base + c) - lo) : -1;
+      const unsigned m = __match_any_sync(0xffffffffu, key);
+      if (key >= 0 && lane == __ffs(m) - 1) hist[warp * kSortCountRange + key] += __popc(m);
+      __syncwarp();
+    }
+    __syncthreads();
+    if (warp == 0) {
+      // totals per key (8 keys per lane), an exclusive scan across keys, then per-warp offsets
+      int run = 0;
+      for (int j = 0; j < kSortCountRange / 32; ++j)
+        for (int w = 0; w < kSortWarps; ++w) run += hist[w * kSortCountRange + lane * 8 + j];
+      int incl = run;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      int off = incl - run;
+      for (int j = 0; j < kSortCountRange / 32; ++j) {
+        const int key = lane * 8 + j;
+        for (int w = 0; w < kSortWarps; ++w) {
+          const int cnt = hist[w * kSortCountRange + key];
+          hist[w * kSortCountRange + key] = off;
+          off += cnt;
+        }
+      }
+    }
+    __syncthreads();
+    for (int64_t c0 = s0; c0 < s1; c0 += 32) {
+      const int64_t c = c0 + lane;
+      const int64_t k = c < s1 ? sort_key(g, base + c) : 0;
+      const int key = c < s1 ? int(k - lo) : -1;
+      const unsigned m = __match_any_sync(0xffffffffu, key);
+      if (key >= 0) {
+        const int rank = __popc(m & ((1u << lane) - 1u));
+        sort_store(g, base + hist[warp * kSortCountRange + key] + rank, k, c);
+      }
+      __syncwarp();
+      if (key >= 0 && lane == __ffs(m) - 1) hist[warp * kSortCountRange + key] += __popc(m);
+      __syncwarp();
+    }
+    return;
+  }
+  if (n > kSortBitonicMax) {
+    if (tid == 0) record_status(PTSIM_E_UNSUPPORTED);
+    return;
+  }
+  // 2b. bitonic sort of (key, position) over the next power of two; padding sorts last.
+  int p2 = 1;
+  while (p2 < n) p2 <<= 1;
+  long long *sk = reinterpret_cast<long long *>(sort_smem);
+  int *sp = reinterpret_cast<int *>(sort_smem + kSortBitonicMax * 8);
+  for (int i = tid; i < p2; i += kSortThreads) {
+    sk[i] = i < n ? sort_key(g, base + i) : LLONG_MAX;
+    sp[i] = i;
+  }
+  __syncthreads();
+  for (int size = 2; size <= p2; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = tid; i < (p2 >> 1); i += kSortThreads) {
+        const int a = 2 * stride * (i / stride) + (i % stride), b = a + stride;
+        const bool up = (a & size) == 0;
+        const long long ka = sk[a], kb = sk[b];
+        const int pa = sp[a], pb = sp[b];
+        const bool greater = ka > kb || (ka == kb && pa > pb);
+        if (greater == up) {
+          sk[a] = kb;
+          sk[b] = ka;
+          sp[a] = pb;
+          sp[b] = pa;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int i = tid; i < n; i += kSortThreads) sort_store(g, base + i, sk[i], sp[i]);
+}
+
+// ---------------------------------------------------------------------------------------------------
+// Row gather (index_select): the MoE dispatch's token copy (validation/pytorchsim/layer_op_dispatch_*/01_*:
+// out[x] = table[x % C + C * t(idx[x // C])], t = Python floor division of the sorted position by top-k
+// with negative results wrapped by the token count) and any program of that shape.  The lowering states t
+// as an int64 program (ptsim_iinsn); one warp per output row evaluates it once and copies the row.
+// ---------------------------------------------------------------------------------------------------
+struct GatherArgs {
+  const void *table;
+  void *out;
+  const void *idx;
+  int64_t row_begin, row_end, cols, table_rows;
+  int32_t table_dt, out_dt, idx_dt, ncode;
+  int32_t vec, pad;
+  ptsim_map idx_map;
+  ptsim_iinsn code[PTSIM_MAX_ICODE];
+};
+
+__device__ __forceinline__ int64_t gather_row_of(const GatherArgs &g, int64_t r) {
+  const ptsim_map &m = g.idx_map;
+  int64_t at = m.offset;
+  for (int d = 0; d < m.ndigit; ++d) {
+    int64_t q = r / m.div[d];
+    if (m.mod[d] > 0) q %= m.mod[d];
+    at += q * m.stride[d];
+  }
+  const int64_t loaded = g.idx_dt == PTSIM_DT_I32 ? int64_t(reinterpret_cast<const int32_t *>(g.idx)[at])
+                                                   : reinterpret_cast<const int64_t *>(g.idx)[at];
+  int64_t reg[PTSIM_MAX_ICODE];
+  int64_t res = 0;
+  for (int i = 0; i < g.ncode; ++i) {
+    const ptsim_iinsn &in = g.code[i];
+    const int64_t a = reg[in.a & 31], b = reg[in.b & 31];
+    int64_t v;
+    switch (in.op) {
+      case PTSIM_I_LOAD: v = loaded; break;
+      case PTSIM_I_CONST: v = in.imm; break;
+      case PTSIM_I_ADD: v = int64_t(uint64_t(a) + uint64_t(b)); break;
+      case PTSIM_I_SUB: v = int64_t(uint64_t(a) - uint64_t(b)); break;
+      case PTSIM_I_MUL: v = int64_t(uint64_t(a) * uint64_t(b)); break;
+      case PTSIM_I_DIV: v = b == 0 ? 0 : (a == LLONG_MIN && b == -1 ? a : a / b); break;
+      case PTSIM_I_MOD: v = b == 0 ? 0 : (a == LLONG_MIN && b == -1 ? 0 : a % b); break;
+      case PTSIM_I_INV: v = ~a; break;
+      case PTSIM_I_LT: v = a < b; break;
+      case PTSIM_I_LE: v = a <= b; break;
+      case PTSIM_I_GT: v = a > b; break;
+      case PTSIM_I_GE: v = a >= b; break;
+      case PTSIM_I_EQ: v = a == b; break;
+      case PTSIM_I_NE: v = a != b; break;
+      case PTSIM_I_WHERE: v = reg[in.c & 31] ? a : b; break;
+      case PTSIM_I_AND: v = a & b; break;
+      case PTSIM_I_OR: v = a | b; break;
+      case PTSIM_I_XOR: v = a ^ b; break;
+      case PTSIM_I_SHR: v = a >> (b & 63); break;
+      case PTSIM_I_SHL: v = int64_t(uint64_t(a) << (b & 63)); break;
+      default: v = 0; break;
+    }
+    reg[in.dst & 31] = v;
+    res = v;
+  }
+  return res;
+}
+
+__global__ void __launch_bounds__(256) gather_rows_kernel(const __grid_constant__ GatherArgs g) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t r = g.row_begin + ((int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5); r < g.row_end; r += warps) {
+    const int64_t t = gather_row_of(g, r);
+    if (t < 0 || t >= g.table_rows) {
+      if (lane == 0) record_status(PTSIM_E_OOB);
+      continue;
+    }
+    if (g.vec) {
+      // same element type, 16-byte rows: raw copy
+      const int64_t n16 = g.cols * dtype_size(g.out_dt) / 16;
+      const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint8_t *>(g.table) + t * g.cols * dtype_size(g.table_dt));
+      uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(g.out) + r * g.cols * dtype_size(g.out_dt));
+      for (int64_t i = lane; i < n16; i += 32) __stcs(dst + i, __ldg(src + i));
+    } else {
+      for (int64_t c2 = lane; c2 < g.cols; c2 += 32)
+        st_any(g.out, g.out_dt, r * g.cols + c2, ld_any(g.table, g.table_dt, t * g.cols + c2));
+    }
+  }
+}
+
+int launch_gather_rows(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c) {
+  const ptsim_gather_params &p = d.p.gat;
+  GatherArgs g;
+  memset(&g, 0, sizeof(g));
+  g.table = ptrs[p.table_arg];
+  g.out = ptrs[p.out_arg];
+  g.idx = ptrs[p.idx_arg];
+  g.row_begin = lo * d.unit_size;
+  g.row_end = hi * d.unit_size < p.rows ? hi * d.unit_size : p.rows;
+  g.cols = p.cols;
+  g.table_rows = p.table_rows;
+  g.table_dt = d.arg_dtype[p.table_arg];
+  g.out_dt = d.arg_dtype[p.out_arg];
+  g.idx_dt = d.arg_dtype[p.idx_arg];
+  g.ncode = p.ncode;
+  g.idx_map = p.idx_map;
+  memcpy(g.code, p.code, sizeof(g.code));
+  if (g.idx_dt != PTSIM_DT_I64 && g.idx_dt != PTSIM_DT_I32) return fail(PTSIM_E_UNSUPPORTED, "gather indices must be int32 or int64");
+  const bool floaty = [](int dt) { return dt == PTSIM_DT_F32 || dt == PTSIM_DT_BF16 || dt == PTSIM_DT_F16; }(g.table_dt);
+  if (g.table_dt != g.out_dt && !(floaty && (g.out_dt == PTSIM_DT_F32 || g.out_dt == PTSIM_DT_BF16 || g.out_dt == PTSIM_DT_F16)))
+    return fail(PTSIM_E_UNSUPPORTED, "gather converts between float types only");
+  const int esz = dtype_size(g.out_dt);
+  g.vec = g.table_dt == g.out_dt && (g.cols * esz) % 16 == 0 && reinterpret_cast<uintptr_t>(g.table) % 16 == 0 &&
+          reinterpret_cast<uintptr_t>(g.out) % 16 == 0;
+  if (!g.vec && !floaty) return fail(PTSIM_E_UNSUPPORTED, "gather of integer rows needs 16-byte rows");
+  if (g.row_end <= g.row_begin) return PTSIM_OK;
+  int64_t blocks = ceil_div(g.row_end - g.row_begin, 8);
+  if (blocks > int64_t(c.sm_count) * 16) blocks = int64_t(c.sm_count) * 16;
+  gather_rows_kernel<<<unsigned(blocks), 256, 0, c.stream>>>(g);
+  PTSIM_CUDA(cudaGetLastError());
+  return PTSIM_OK;
+}
+
+int launch_topk(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c) {
+  const ptsim_select_params &p = d.p.sel;
+  const int xdt = d.arg_dtype[p.in_arg], vdt = d.arg_dtype[p.val_arg];
+  if ((xdt != PTSIM_DT_F32 && xdt != PTSIM_DT_BF16) || (vdt != PTSIM_DT_F32 && vdt != PTSIM_DT_BF16) ||
+      d.arg_dtype[p.idx_arg] != PTSIM_DT_I64)
+    return fail(PTSIM_E_UNSUPPORTED, "top-k runs fp32/bf16 values with int64 indices");
+  if (p.cols_padded < p.cols || p.cols_padded > 1024 || p.k < 0 || p.k > p.cols_padded)
+    return fail(PTSIM_E_UNSUPPORTED, "top-k over %lld candidate columns, k = %lld (runs up to 1024 columns)",
+                (long long)p.cols_padded, (long long)p.k);
+  TopkArgs g;
+  g.x = ptrs[p.in_arg];
+  g.v = ptrs[p.val_arg];
+  g.idx = reinterpret_cast<int64_t *>(ptrs[p.idx_arg]);
+  g.row_begin = lo * d.unit_size;
+  g.row_end = hi * d.unit_size < p.rows ? hi * d.unit_size : p.rows;
+  g.cols = p.cols;
+  g.k = p.k;
+  g.cols_padded = p.cols_padded;
+  g.x_dt = xdt;
+  g.v_dt = vdt;
+  g.largest = p.descending;
+  g.pad = 0;
+  if (g.row_end <= g.row_begin) return PTSIM_OK;
+  const unsigned blocks = unsigned(ceil_div(g.row_end - g.row_begin, 8));
+  const int npl = int(ceil_div(p.cols_padded, 32));
+  if (npl <= 1) topk_kernel<1><<<blocks, 256, 0, c.stream>>>(g);
+  else if (npl <= 2) topk_kernel<2><<<blocks, 256, 0, c.stream>>>(g);
+  else if (npl <= 4) topk_kernel<4><<<blocks, 256, 0, c.stream>>>(g);
+  else if (npl <= 8) topk_kernel<8><<<blocks, 256, 0, c.stream>>>(g);
+  else if (npl <= 16) topk_kernel<16><<<blocks, 256, 0, c.stream>>>(g);
+  else topk_kernel<32><<<blocks, 256, 0, c.stream>>>(g);
+  PTSIM_CUDA(cudaGetLastError());
+  return PTSIM_OK;
+}
+
+int launch_sort(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c) {
+  const ptsim_select_params &p = d.p.sel;
+  const int xdt = d.arg_dtype[p.in_arg], vdt = d.arg_dtype[p.val_arg];
+  if (d.arg_dtype[p.idx_arg] != PTSIM_DT_I64) return fail(PTSIM_E_UNSUPPORTED, "sort writes int64 indices");
+  if (p.float_keys ? (xdt != PTSIM_DT_F32 || (vdt != PTSIM_DT_F32 && vdt != PTSIM_DT_BF16))
+                   : ((xdt != PTSIM_DT_I64 && xdt != PTSIM_DT_I32) || (vdt != PTSIM_DT_I64 && vdt != PTSIM_DT_I32)))
+    return fail(PTSIM_E_UNSUPPORTED, "sort runs int32/int64 keys, or fp32 keys ordered by their bits");
+  SortArgs g;
+  g.x = ptrs[p.in_arg];
+  g.v = ptrs[p.val_arg];
+  g.idx = reinterpret_cast<int64_t *>(ptrs[p.idx_arg]);
+  g.row_begin = lo * d.unit_size;
+  const int64_t row_end = hi * d.unit_size < p.rows ? hi * d.unit_size : p.rows;
+  g.cols = p.cols;
+  g.x_dt = xdt;
+  g.v_dt = vdt;
+  g.descending = p.descending;
+  g.float_keys = p.float_keys;
+  if (row_end <= g.row_begin) return PTSIM_OK;
+  PTSIM_CUDA((smem_limit_once<sort_kernel>(kSortSmem, c.device)));
+  sort_kernel<<<unsigned(row_end - g.row_begin), kSortThreads, kSortSmem, c.stream>>>(g);
+  PTSIM_CUDA(cudaGetLastError());
+  return PTSIM_OK;
+}
+
+}  // namespace ptsim

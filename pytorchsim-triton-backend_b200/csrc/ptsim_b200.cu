@@ -12,6 +12,7 @@
 #include "gemm.cuh"
 #include "attention.cuh"
 #include "decode.cuh"
+#include "moe.cuh"
 
 namespace ptsim {
 
@@ -110,6 +111,7 @@ static int check_desc(const void *p, size_t bytes) {
       break;
     }
     case PTSIM_KIND_ROW_SOFTMAX:
+    case PTSIM_KIND_ROW_DIVSUM:
     case PTSIM_KIND_ROW_RMSNORM: {
       const ptsim_row_params &r = d.p.row;
       if ((rc = check_arg(d, r.in_arg, "row input")) || (rc = check_arg(d, r.out_arg, "row output"))) return rc;
@@ -176,6 +178,42 @@ static int check_desc(const void *p, size_t bytes) {
         return fail(PTSIM_E_OOB, "decode attention tensors are smaller than heads x (rows | keys) x dim");
       break;
     }
+    case PTSIM_KIND_TOPK:
+    case PTSIM_KIND_SORT: {
+      const ptsim_select_params &e = d.p.sel;
+      if ((rc = check_arg(d, e.in_arg, "keys")) || (rc = check_arg(d, e.val_arg, "values")) ||
+          (rc = check_arg(d, e.idx_arg, "indices")))
+        return rc;
+      const int64_t kept = d.kind == PTSIM_KIND_TOPK ? e.k : e.cols;
+      if (e.rows < 0 || e.cols < 0 || kept < 0)
+        return fail(PTSIM_E_DESC, "selection over %lld x %lld keeping %lld", (long long)e.rows, (long long)e.cols, (long long)kept);
+      if (e.rows * e.cols > d.arg_numel[e.in_arg] || e.rows * kept > d.arg_numel[e.val_arg] ||
+          e.rows * kept > d.arg_numel[e.idx_arg])
+        return fail(PTSIM_E_OOB, "selection reads or writes past its tensors");
+      if (d.units * d.unit_size < e.rows) return fail(PTSIM_E_DESC, "selection units do not cover its rows");
+      break;
+    }
+    case PTSIM_KIND_GATHER_ROWS: {
+      const ptsim_gather_params &gp = d.p.gat;
+      if ((rc = check_arg(d, gp.out_arg, "gather output")) || (rc = check_arg(d, gp.table_arg, "gather table")) ||
+          (rc = check_arg(d, gp.idx_arg, "gather index")))
+        return rc;
+      if (gp.rows < 0 || gp.cols < 1 || gp.table_rows < 0 || gp.ncode < 1 || gp.ncode > PTSIM_MAX_ICODE)
+        return fail(PTSIM_E_DESC, "gather of %lld x %lld with %d instructions", (long long)gp.rows, (long long)gp.cols, gp.ncode);
+      if (gp.rows * gp.cols > d.arg_numel[gp.out_arg] || gp.table_rows * gp.cols > d.arg_numel[gp.table_arg])
+        return fail(PTSIM_E_OOB, "gather rows extend past their tensors");
+      const ptsim_map &m = gp.idx_map;
+      if (m.ndigit < 0 || m.ndigit > PTSIM_MAX_DIGITS || m.offset < 0) return fail(PTSIM_E_DESC, "gather index map");
+      for (int k = 0; k < m.ndigit; ++k)
+        if (m.div[k] < 1 || m.mod[k] < 1 || m.stride[k] < 0) return fail(PTSIM_E_DESC, "gather index map digit %d", k);
+      if (gp.rows > 0 && map_max_index(m, gp.rows) >= d.arg_numel[gp.idx_arg])
+        return fail(PTSIM_E_OOB, "gather index map reaches past the index tensor");
+      for (int i = 0; i < gp.ncode; ++i)
+        if (gp.code[i].op < PTSIM_I_LOAD || gp.code[i].op > PTSIM_I_SHL || gp.code[i].dst >= PTSIM_MAX_ICODE ||
+            gp.code[i].a >= PTSIM_MAX_ICODE || gp.code[i].b >= PTSIM_MAX_ICODE || gp.code[i].c >= PTSIM_MAX_ICODE)
+          return fail(PTSIM_E_DESC, "gather instruction %d", i);
+      break;
+    }
     case PTSIM_KIND_REDUCE_ALL: {
       const ptsim_reduce_params &r = d.p.red;
       if ((rc = check_arg(d, r.in_arg, "reduce input")) || (rc = check_arg(d, r.out_arg, "reduce output"))) return rc;
@@ -240,7 +278,11 @@ int ptsim_launch(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int
   switch (d.kind) {
     case PTSIM_KIND_ELEMENTWISE: return launch_elementwise(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_ROW_SOFTMAX:
+    case PTSIM_KIND_ROW_DIVSUM:
     case PTSIM_KIND_ROW_RMSNORM: return launch_rowops(d, dev_ptrs, lo, hi, c);
+    case PTSIM_KIND_TOPK: return launch_topk(d, dev_ptrs, lo, hi, c);
+    case PTSIM_KIND_SORT: return launch_sort(d, dev_ptrs, lo, hi, c);
+    case PTSIM_KIND_GATHER_ROWS: return launch_gather_rows(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_QKNORM_ROPE: return launch_qkrope(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_GEMM: return launch_gemm(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_ATTN_PREFILL: return launch_attention(d, dev_ptrs, lo, hi, c);

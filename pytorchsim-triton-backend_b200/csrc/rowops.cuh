@@ -16,7 +16,7 @@
 
 namespace ptsim {
 
-enum RowKind { kSoftmax = 0, kRmsNorm = 1 };
+enum RowKind { kSoftmax = 0, kRmsNorm = 1, kDivSum = 2 };
 
 struct RowLaunch {
   const void *in;
@@ -306,6 +306,12 @@ __global__ void __launch_bounds__(256) row_generic_kernel(const __grid_constant_
       s = row_allreduce<32>(s, false, nullptr);
       for (int64_t c = lane; c < L.cols; c += 32)
         st_any(L.out, L.out_dt, ob + c, __fdiv_rn(npu_exp(__fsub_rn(ld_any(L.in, L.in_dt, ib + c), m)), s));
+    } else if constexpr (KIND == kDivSum) {
+      // x / sum(x) per row (layer_op_router_post_*/02_*: tmp4 = sum(x); x / tmp4 in fp32, cast on the store)
+      float s = 0.f;
+      for (int64_t c = lane; c < L.cols; c += 32) s = __fadd_rn(s, ld_any(L.in, L.in_dt, ib + c));
+      s = row_allreduce<32>(s, false, nullptr);
+      for (int64_t c = lane; c < L.cols; c += 32) st_any(L.out, L.out_dt, ob + c, __fdiv_rn(ld_any(L.in, L.in_dt, ib + c), s));
     } else {
       float ss = 0.f;
       for (int64_t c = lane; c < L.cols; c += 32) { const float x = ld_any(L.in, L.in_dt, ib + c); ss = __fadd_rn(ss, __fmul_rn(x, x)); }
@@ -392,6 +398,14 @@ int launch_rowops(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi
   L.eps = p.eps;
   if (L.rows_end <= L.rows_begin) return PTSIM_OK;
   if (d.kind == PTSIM_KIND_ROW_SOFTMAX) return launch_row_kind<kSoftmax>(L, c);
+  if (d.kind == PTSIM_KIND_ROW_DIVSUM) {
+    // Rows of a few values (the router's top-k weights): one warp per row.
+    int64_t blocks = ceil_div(L.rows_end - L.rows_begin, 8);
+    if (blocks > int64_t(c.sm_count) * 8) blocks = int64_t(c.sm_count) * 8;
+    row_generic_kernel<kDivSum><<<unsigned(blocks), 256, 0, c.stream>>>(L);
+    PTSIM_CUDA(cudaGetLastError());
+    return PTSIM_OK;
+  }
   return launch_row_kind<kRmsNorm>(L, c);
 }
 

@@ -106,6 +106,61 @@ def gemv(N, K, b_kmajor=False, residual=False, out_dtype="bfloat16"):
     return gemm(1, N, K, residual=residual, b_kmajor=b_kmajor, out_dtype=out_dtype)
 
 
+def topk(rows, cols, k, largest=True, cols_padded=None, dtype="float32"):
+    """The MoE router's _topk_kernel (validation/pytorchsim/layer_op_router_post_*/01__topk_kernel): per row of
+    `cols` values, the k largest (or smallest) with their column indices."""
+    d = D.new(D.TOPK, _args([("x_ptr", dtype, rows * cols), ("v_ptr", dtype, rows * k), ("i_ptr", "int64", rows * k)]),
+              (1, 1, 1), units=rows, unit_size=1)
+    e = d.p.sel
+    e.rows, e.cols, e.k = rows, cols, k
+    e.cols_padded = cols_padded or 1 << max(0, (cols - 1).bit_length())
+    e.in_arg, e.val_arg, e.idx_arg, e.descending = 0, 1, 2, 1 if largest else 0
+    return d
+
+
+def sort(rows, cols, descending=False, float_keys=False, dtype="int64"):
+    """The MoE dispatch's _sort_kernel (validation/pytorchsim/layer_op_dispatch_*/00__sort_kernel): each row of
+    `cols` keys sorted, ties in source order, with int64 source indices."""
+    d = D.new(D.SORT, _args([("x_ptr", dtype, rows * cols), ("v_ptr", dtype, rows * cols), ("i_ptr", "int64", rows * cols)]),
+              (rows, 1, 1), units=rows, unit_size=1)
+    e = d.p.sel
+    e.rows, e.cols, e.k, e.cols_padded = rows, cols, 0, 1 << max(0, (cols - 1).bit_length())
+    e.in_arg, e.val_arg, e.idx_arg = 0, 1, 2
+    e.descending, e.float_keys = 1 if descending else 0, 1 if float_keys else 0
+    return d
+
+
+def row_divsum(rows, cols, in_dtype="float32", out_dtype="bfloat16"):
+    """The MoE router's weight normalisation (layer_op_router_post_*/02_*): out = x / sum(x) per row."""
+    d = D.new(D.ROW_DIVSUM, _args([("in_ptr0", in_dtype, rows * cols), ("out_ptr1", out_dtype, rows * cols)]),
+              (1, 1, 1), units=rows, unit_size=1)
+    r = d.p.row
+    r.rows, r.cols, r.in_row_stride, r.out_row_stride = rows, cols, cols, cols
+    r.in_arg, r.out_arg, r.weight_arg = 0, 1, -1
+    return d
+
+
+def gather_rows_floordiv(rows, cols, table_rows, div, dtype="bfloat16", idx_dtype="int64"):
+    """The MoE dispatch's token copy (layer_op_dispatch_*/01_*): out row r = table row t, t = floor(idx[r] / div)
+    (Python floor division), negative t wrapped by + table_rows; the int64 program as the lowering emits it."""
+    d = D.new(D.GATHER_ROWS, _args([("in_ptr0", idx_dtype, rows), ("in_ptr1", dtype, table_rows * cols),
+                                    ("out_ptr0", dtype, rows * cols)]), (1, 1, 1), units=rows, unit_size=1)
+    g = d.p.gat
+    g.rows, g.cols, g.table_rows = rows, cols, table_rows
+    g.out_arg, g.table_arg, g.idx_arg = 2, 1, 0
+    g.idx_map.arg, g.idx_map.ndigit, g.idx_map.offset = 0, 1, 0
+    g.idx_map.div[0], g.idx_map.mod[0], g.idx_map.stride[0] = 1, 1 << 62, 1
+    prog = [("load", 0, 0, 0, 0), ("const", 0, 0, 0, 0), ("lt", 0, 1, 0, 0), ("inv", 0, 0, 0, 0),
+            ("where", 3, 0, 2, 0), ("const", 0, 0, 0, div), ("div", 4, 5, 0, 0), ("inv", 6, 0, 0, 0),
+            ("where", 7, 6, 2, 0), ("lt", 8, 1, 0, 0), ("const", 0, 0, 0, table_rows), ("add", 8, 10, 0, 0),
+            ("where", 11, 8, 9, 0)]
+    for k, (op, a, b, c, imm) in enumerate(prog):
+        ins = g.code[k]
+        ins.op, ins.dst, ins.a, ins.b, ins.c, ins.imm = D.IOP[op], k, a, b, c, imm
+    g.ncode = len(prog)
+    return d
+
+
 def reduce_all(numel, op="sum", dtype="bfloat16"):
     d = D.new(D.REDUCE_ALL, _args([("in_ptr0", dtype, numel), ("out_ptr0", "float32", 1)]), [1], units=1, unit_size=1,
               workspace_bytes=D.REDUCE_WORKSPACE_BYTES)

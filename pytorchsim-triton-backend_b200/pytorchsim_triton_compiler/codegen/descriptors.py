@@ -12,9 +12,11 @@ MAX_ARGS, MAX_MAPS, MAX_DIGITS, MAX_CODE, MAX_REGS = 16, 8, 4, 32, 8
 
 # Kinds (PTSIM_KIND_*).
 ELEMENTWISE, ROW_SOFTMAX, ROW_RMSNORM, QKNORM_ROPE, GEMM, ATTN_PREFILL, REDUCE_ALL, ATTN_DECODE = 1, 2, 3, 4, 5, 6, 7, 8
+ROW_DIVSUM, TOPK, SORT, GATHER_ROWS = 9, 10, 11, 12
 KIND_NAME = {ELEMENTWISE: "elementwise", ROW_SOFTMAX: "row_softmax", ROW_RMSNORM: "row_rmsnorm",
              QKNORM_ROPE: "qknorm_rope", GEMM: "gemm", ATTN_PREFILL: "attn_prefill", REDUCE_ALL: "reduce_all",
-             ATTN_DECODE: "attn_decode"}
+             ATTN_DECODE: "attn_decode", ROW_DIVSUM: "row_divsum", TOPK: "topk", SORT: "sort",
+             GATHER_ROWS: "gather_rows"}
 
 # Element types (PTSIM_DT_*), keyed by kernel.json dtype names (contract/kernel_object.py NP_DTYPE keys).
 DTYPE_CODE = {"float32": 0, "bfloat16": 1, "float16": 2, "int32": 3, "int64": 4, "int16": 5, "int8": 6,
@@ -79,9 +81,32 @@ class ReduceParams(C.Structure):
                 ("pad0", C.c_int32)]
 
 
+class SelectParams(C.Structure):
+    _fields_ = [("rows", C.c_int64), ("cols", C.c_int64), ("k", C.c_int64), ("cols_padded", C.c_int64),
+                ("in_arg", C.c_int32), ("val_arg", C.c_int32), ("idx_arg", C.c_int32), ("descending", C.c_int32),
+                ("float_keys", C.c_int32), ("pad0", C.c_int32)]
+
+
+MAX_ICODE = 32
+IOP = {"load": 1, "const": 2, "add": 3, "sub": 4, "mul": 5, "div": 6, "mod": 7, "inv": 8, "lt": 9, "le": 10,
+       "gt": 11, "ge": 12, "eq": 13, "ne": 14, "where": 15, "and": 16, "or": 17, "xor": 18, "shr": 19, "shl": 20}
+IOP_NAME = {v: k for k, v in IOP.items()}
+
+
+class IInsn(C.Structure):
+    _fields_ = [("op", C.c_uint8), ("dst", C.c_uint8), ("a", C.c_uint8), ("b", C.c_uint8), ("c", C.c_uint8),
+                ("pad0", C.c_uint8), ("pad1", C.c_uint8), ("pad2", C.c_uint8), ("imm", C.c_int64)]
+
+
+class GatherParams(C.Structure):
+    _fields_ = [("rows", C.c_int64), ("cols", C.c_int64), ("table_rows", C.c_int64), ("out_arg", C.c_int32),
+                ("table_arg", C.c_int32), ("idx_arg", C.c_int32), ("ncode", C.c_int32), ("idx_map", Map),
+                ("code", IInsn * MAX_ICODE)]
+
+
 class Params(C.Union):
     _fields_ = [("ew", EwParams), ("row", RowParams), ("qk", QkParams), ("gemm", GemmParams),
-                ("attn", AttnParams), ("red", ReduceParams)]
+                ("attn", AttnParams), ("red", ReduceParams), ("sel", SelectParams), ("gat", GatherParams)]
 
 
 class Desc(C.Structure):
@@ -159,6 +184,19 @@ def describe(d):
         a = d.p.attn
         out.update(hkv=a.hkv, group=a.hq // max(1, a.hkv), seq=a.seq, dim=a.dim, scale=a.scale,
                    ref_bkv=a.ref_bkv)
+    elif d.kind == ROW_DIVSUM:
+        out.update(rows=d.p.row.rows, cols=d.p.row.cols)
+    elif d.kind in (TOPK, SORT):
+        e = d.p.sel
+        out.update(rows=e.rows, cols=e.cols, cols_padded=e.cols_padded, descending=bool(e.descending))
+        if d.kind == TOPK:
+            out["k"] = e.k
+        else:
+            out["float_keys"] = bool(e.float_keys)
+    elif d.kind == GATHER_ROWS:
+        gp = d.p.gat
+        out.update(rows=gp.rows, cols=gp.cols, table_rows=gp.table_rows,
+                   program=[(IOP_NAME.get(i.op, i.op), i.dst, i.a, i.b, i.c, i.imm) for i in list(gp.code)[:gp.ncode]])
     elif d.kind == REDUCE_ALL:
         out.update(numel=d.p.red.numel, op="max" if d.p.red.op == RED_MAX else "sum")
     return out

@@ -163,8 +163,9 @@ class Const(Node):
 class Load(Node):
     kind = "load"
 
-    def __init__(self, arg, index, mask=None, other=None):
-        self.arg, self.index, self.mask, self.other = arg, index, mask, other
+    def __init__(self, arg, index, mask=None, other=None, data=None):
+        # data: a value node added to the affine index (an index loaded from memory, as index_select has)
+        self.arg, self.index, self.mask, self.other, self.data = arg, index, mask, other, data
 
 
 class Op(Node):
@@ -196,10 +197,17 @@ class Cond:
 
 
 class Ptr:
-    """A pointer argument plus an element index."""
+    """A pointer argument plus an element index (affine) and an optional data-dependent offset (a value node)."""
 
-    def __init__(self, arg, index=None):
-        self.arg, self.index = arg, index if index is not None else Index()
+    def __init__(self, arg, index=None, data=None):
+        self.arg, self.index, self.data = arg, index if index is not None else Index(), data
+
+
+class DataIndex:
+    """An affine index plus a value node: the element offset of a gather (x0 + C * loaded_index)."""
+
+    def __init__(self, index, data):
+        self.index, self.data = index, data
 
 
 class Store:
@@ -376,6 +384,11 @@ class Evaluator:
                 return Op("neg", self.value(v))
             if isinstance(e.op, ast.Not):
                 return not v
+            if isinstance(e.op, ast.Invert):
+                if isinstance(v, int) and not isinstance(v, bool):
+                    return ~v
+                if isinstance(v, Node):
+                    return Op("invert", v)
             raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"unary {type(e.op).__name__}")
         if isinstance(e, ast.Compare):
             if len(e.ops) != 1:
@@ -410,6 +423,8 @@ class Evaluator:
         raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"expression {type(e).__name__}")
 
     def compare(self, op, a, b):
+        a = a.v if isinstance(a, Const) else a
+        b = b.v if isinstance(b, Const) else b
         if isinstance(a, (int, float)) and isinstance(b, (int, float)):
             return {ast.Lt: a < b, ast.LtE: a <= b, ast.Gt: a > b, ast.GtE: a >= b, ast.Eq: a == b,
                     ast.NotEq: a != b}[type(op)]
@@ -421,6 +436,9 @@ class Evaluator:
             return Cond(name, idx, b)
         if isinstance(a, (Index, Arange, Pid, LoopVar)) and isinstance(b, (Index, Arange, Pid, LoopVar)):
             return Cond(name, self.index_of(a) - self.index_of(b), 0)
+        if isinstance(a, (Node, int, float)) and isinstance(b, (Node, int, float)):
+            # a comparison of data values: kept as a value node (0/1) for where() and integer programs
+            return Cond("data", None, Op("cmp_" + name, self.value(a), self.value(b)))
         return Cond("data", None, None)
 
     def is_extent(self, idx, n):
@@ -450,6 +468,8 @@ class Evaluator:
         """`v` as a value node."""
         if isinstance(v, Node):
             return v
+        if isinstance(v, Cond) and v.op == "data" and isinstance(v.value, Node):
+            return v.value   # a comparison of data values as 0 / 1
         if isinstance(v, (int, float)) and not isinstance(v, bool):
             return Const(v)
         if isinstance(v, bool):
@@ -494,10 +514,20 @@ class Evaluator:
                 return ia.mod(ib.const)
             raise Refused(Reason.INDEX_NOT_AFFINE, f"index operator {type(op).__name__}")
         if isinstance(a, Ptr) and _is_index(b):
-            return Ptr(a.arg, a.index + self.index_of(b))
+            return Ptr(a.arg, a.index + self.index_of(b), a.data)
         if isinstance(b, Ptr) and _is_index(a):
-            return Ptr(b.arg, b.index + self.index_of(a))
-        name = {ast.Add: "add", ast.Sub: "sub", ast.Mult: "mul", ast.Div: "div"}.get(type(op))
+            return Ptr(b.arg, b.index + self.index_of(a), b.data)
+        if isinstance(op, ast.Add):
+            for p, q in ((a, b), (b, a)):
+                if isinstance(p, Ptr) and isinstance(q, DataIndex) and p.data is None:
+                    return Ptr(p.arg, p.index + q.index, q.data)
+                if isinstance(p, (Index, Arange, Pid, LoopVar)) and isinstance(q, Node) and not isinstance(q, Const):
+                    return DataIndex(self.index_of(p), q)
+                if isinstance(p, DataIndex) and _is_index(q):
+                    return DataIndex(p.index + self.index_of(q), p.data)
+        name = {ast.Add: "add", ast.Sub: "sub", ast.Mult: "mul", ast.Div: "div", ast.FloorDiv: "idiv",
+                ast.Mod: "imod", ast.BitAnd: "iand", ast.BitOr: "ior", ast.BitXor: "ixor", ast.RShift: "ishr",
+                ast.LShift: "ishl"}.get(type(op))
         if name is None:
             raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"value operator {type(op).__name__}")
         return Op(name, self.value(a), self.value(b))
@@ -505,6 +535,9 @@ class Evaluator:
     # ---- calls -----------------------------------------------------------------------------------
     def call(self, e):
         f = self.expr(e.func)
+        if isinstance(f, _Module) and f.name.split(".")[-1] == "device_assert":
+            # a bounds assertion of the reference; the executor's own bounds checks record PTSIM_E_OOB
+            return None
         args = [self.expr(a) for a in e.args]
         kw = {k.arg: self.expr(k.value) for k in e.keywords}
         if isinstance(f, _Bound):
@@ -543,7 +576,7 @@ class Evaluator:
             other = args[2] if len(args) > 2 else kw.get("other")
             if isinstance(mask, Cond) and mask.op == "bounds":
                 mask = None
-            return Load(ptr.arg, ptr.index, mask if isinstance(mask, Cond) else None, other)
+            return Load(ptr.arg, ptr.index, mask if isinstance(mask, Cond) else None, other, ptr.data)
         if name == "store":
             ptr = args[0]
             if not isinstance(ptr, Ptr):
@@ -569,7 +602,8 @@ class Evaluator:
             if isinstance(args[0], Cond) and args[0].op == "bounds":
                 return self.value(args[1])
             if isinstance(args[0], bool):
-                return self.value(args[1] if args[0] else args[2])
+                pick = args[1] if args[0] else args[2]
+                return pick if isinstance(pick, (int, float)) else self.value(pick)
             return Op("where", args[0] if isinstance(args[0], Cond) else Cond("data"), self.value(args[1]), self.value(args[2]))
         if name in ("sum", "max2", "min2") or (name in ("max", "min") and "." in f.name):
             axis = args[1] if len(args) > 1 else kw.get("axis")

@@ -98,10 +98,13 @@ def strip_casts(n):
     return n
 
 
-def _row_index(idx, what):
-    """(row stride) of an index r + stride * x, else Refused."""
+def _row_index(idx, what, rows=None):
+    """(row stride) of an index r + stride * x, else Refused.  A one-row program (xnumel 1: Inductor then
+    indexes by r alone) has row stride 0."""
     r = idx.coeff_of("r")
     x = idx.coeff_of("x")
+    if rows == 1 and idx.const == 0 and r == {F.Digit("r"): 1} and not x and len(idx.terms) == 1:
+        return 0
     if idx.const != 0 or r != {F.Digit("r"): 1} or len(x) != 1 or F.Digit("x") not in x or len(idx.terms) != 2:
         raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{what} index {idx} is not r + stride * x")
     return x[F.Digit("x")]
@@ -117,6 +120,11 @@ def lower(spec, fn=None):
         fn = F.load_kernel(spec)
     src, name = F.kernel_source(fn)
     tree = ast.parse(src)
+    ce = set(spec.constexprs)
+    if {"E", "EP", "K", "KP", "XBLOCK", "LARGEST"} <= ce:
+        return _lower_topk(spec)
+    if {"L", "D", "LOG", "DESCENDING", "FLOAT"} <= ce:
+        return _lower_sort(spec)
     dots = [n for n in ast.walk(tree) if isinstance(n, ast.Call) and isinstance(n.func, ast.Attribute) and n.func.attr == "dot"]
     if dots:
         if len(dots) >= 2 and {"HQ", "G", "S", "D", "SCALE"} <= set(spec.constexprs):
@@ -129,6 +137,8 @@ def lower(spec, fn=None):
         raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: {len(prog.stores)} stores; the executor's "
                                                     f"vector programs have one")
     st = prog.stores[0]
+    if isinstance(strip_casts(st.value), F.Load) and strip_casts(st.value).data is not None:
+        return _lower_gather(spec, prog, st)
     reduces = [n for n in walk(st.value) if isinstance(n, F.Reduce)]
     if not reduces:
         return _lower_elementwise(spec, prog, st)
@@ -145,6 +155,8 @@ def lower(spec, fn=None):
         return _lower_softmax(spec, prog, st, reduces)
     if ops == {"mul"} and len(reduces) == 1 and reduces[0].op == "add" and len(args) == 2:
         return _lower_gemv(spec, prog, st, reduces[0])
+    if ops == {"div"} and len(reduces) == 1 and reduces[0].op == "add" and len(args) == 1:
+        return _lower_divsum(spec, prog, st, reduces[0])
     raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a reduction program of ops {sorted(ops)}")
 
 
@@ -301,8 +313,8 @@ def _lower_softmax(spec, prog, st, reduces):
     d = D.new(D.ROW_SOFTMAX, _manifest_args(spec), spec.grid, units=_grid_programs(spec)[0], unit_size=xblock)
     r = d.p.row
     r.rows, r.cols = rows, cols
-    r.in_row_stride = _row_index(ld.index, "softmax load")
-    r.out_row_stride = _row_index(st.index, "softmax store")
+    r.in_row_stride = _row_index(ld.index, "softmax load", rows)
+    r.out_row_stride = _row_index(st.index, "softmax store", rows)
     r.in_arg, r.out_arg, r.weight_arg = ld.arg, st.arg, -1
     return Lowered(d, D.describe(d))
 
@@ -580,4 +592,199 @@ def _lower_decode(spec, tree):
     a.causal = 0
     a.scale = float(ce["SCALE"])
     a.ref_bq, a.ref_bkv = GP, BKV
+    return Lowered(d, D.describe(d))
+
+
+def _selection_args(spec, what):
+    ptrs = _pointer_params(spec)
+    idx = {n: i for i, n in enumerate(ptrs)}
+    if not all(n in idx for n in ("x_ptr", "v_ptr", "i_ptr")):
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: {what} wants x_ptr, v_ptr, i_ptr")
+    return idx["x_ptr"], idx["v_ptr"], idx["i_ptr"]
+
+
+def _lower_topk(spec):
+    """The MoE router's _topk_kernel (validation/pytorchsim/layer_op_router_post_128x0_bf16/01__topk_kernel/
+    _topk_kernel_triton.py:3-26): rows of E values (row stride E), K passes of (best value, first column
+    holding it) over EP candidate columns, the chosen column overwritten with the spent value; v [rows, K],
+    i [rows, K] int64."""
+    ce = spec.constexprs
+    E, EP, K = int(ce["E"]), int(ce["EP"]), int(ce["K"])
+    x, v, i = _selection_args(spec, "top-k")
+    rows = _lookup(spec, None, "rows")
+    if rows is None:
+        rows = spec.args[x].numel // max(1, E)
+    rows = int(rows)
+    if EP < E or K > EP or spec.args[x].numel < rows * E or spec.args[v].numel < rows * K or spec.args[i].numel < rows * K:
+        raise Refused(Reason.SHAPE_NOT_RUN, f"{spec.name}: rows={rows} E={E} EP={EP} K={K}")
+    d = D.new(D.TOPK, _manifest_args(spec), spec.grid, units=rows, unit_size=1)
+    e = d.p.sel
+    e.rows, e.cols, e.k, e.cols_padded = rows, E, K, EP
+    e.in_arg, e.val_arg, e.idx_arg = x, v, i
+    e.descending = 1 if ce["LARGEST"] else 0
+    return Lowered(d, D.describe(d))
+
+
+def _lower_sort(spec):
+    """The MoE dispatch's _sort_kernel (validation/pytorchsim/layer_op_dispatch_128x0_bf16/00__sort_kernel/
+    _sort_kernel_triton.py:3-53): program `row` sorts its E keys at row * E (a bitonic network over L x D
+    positions, ties broken by position), writes the sorted values (keys mapped back) and int64 positions."""
+    ce = spec.constexprs
+    x, v, i = _selection_args(spec, "sort")
+    rows = _grid_programs(spec)[0]
+    E = _lookup(spec, None, "E")
+    if E is None:
+        E = spec.args[x].numel // max(1, rows)
+    E = int(E)
+    if E > int(ce["L"]) * int(ce["D"]) or spec.args[x].numel < rows * E or spec.args[v].numel < rows * E \
+            or spec.args[i].numel < rows * E:
+        raise Refused(Reason.SHAPE_NOT_RUN, f"{spec.name}: {rows} rows of E={E} over L*D={ce['L'] * ce['D']}")
+    d = D.new(D.SORT, _manifest_args(spec), spec.grid, units=rows, unit_size=1)
+    e = d.p.sel
+    e.rows, e.cols, e.k, e.cols_padded = rows, E, 0, int(ce["L"]) * int(ce["D"])
+    e.in_arg, e.val_arg, e.idx_arg = x, v, i
+    e.descending = 1 if ce["DESCENDING"] else 0
+    e.float_keys = 1 if ce["FLOAT"] else 0
+    return Lowered(d, D.describe(d))
+
+
+def _lower_divsum(spec, prog, st, red):
+    """x / sum(x) per row (the MoE router's weight normalisation, validation/pytorchsim/
+    layer_op_router_post_128x0_bf16/02_*_triton.py: tmp4 = sum over r of x; x / tmp4, cast on the store)."""
+    rows, cols, xblock = _row_sizes(spec, prog, "row normalisation")
+    v = st.value
+    while isinstance(v, F.Op) and v.name in ("to_fp32", "to_bf16", "cast"):
+        v = v.args[0]
+    if not (isinstance(v, F.Op) and v.name == "div" and isinstance(v.args[0], F.Load) and isinstance(v.args[1], F.Reduce)
+            and key(strip_casts(v.args[1].value)) == key(v.args[0])):
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: not x / sum(x)")
+    ld = v.args[0]
+    d = D.new(D.ROW_DIVSUM, _manifest_args(spec), spec.grid, units=_grid_programs(spec)[0], unit_size=xblock)
+    r = d.p.row
+    r.rows, r.cols = rows, cols
+    r.in_row_stride = _row_index(ld.index, "normalisation load", rows)
+    r.out_row_stride = _row_index(st.index, "normalisation store", rows)
+    r.in_arg, r.out_arg, r.weight_arg = ld.arg, st.arg, -1
+    return Lowered(d, D.describe(d))
+
+
+_NO_MOD = 1 << 62
+_CMP = {"cmp_lt": "lt", "cmp_le": "le", "cmp_gt": "gt", "cmp_ge": "ge", "cmp_eq": "eq", "cmp_ne": "ne"}
+_IBIN = {"add": "add", "sub": "sub", "mul": "mul", "idiv": "div", "imod": "mod", "iand": "and", "ior": "or",
+         "ixor": "xor", "ishr": "shr", "ishl": "shl"}
+
+
+def _int_program(spec, tree, idx_load):
+    """The int64 program (descriptor instructions) of an index expression over one loaded index value:
+    Triton's integer semantics (// and % truncate toward zero, comparisons are 0 / 1), shared subtrees
+    computed once.  Result in the last instruction's register."""
+    code, memo = [], {}
+
+    def emit(op, a=0, b=0, c=0, imm=0):
+        if len(code) >= D.MAX_ICODE:
+            raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: an index program over {D.MAX_ICODE} instructions")
+        ins = D.IInsn()
+        ins.op, ins.dst, ins.a, ins.b, ins.c, ins.imm = D.IOP[op], len(code), a, b, c, int(imm)
+        code.append(ins)
+        return ins.dst
+
+    def gen(n):
+        if isinstance(n, F.Cond):
+            if n.op != "data" or not isinstance(n.value, F.Node):
+                raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: an index condition on the program index")
+            n = n.value
+        k = key(n)
+        if k in memo:
+            return memo[k]
+        if isinstance(n, F.Const):
+            if n.v != int(n.v):
+                raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a fractional constant {n.v} in an index")
+            r = emit("const", imm=int(n.v))
+        elif isinstance(n, F.Load):
+            if n.data is not None or n.arg != idx_load.arg or key(n) != key(idx_load):
+                raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: an index program reading two indices")
+            r = emit("load")
+        elif isinstance(n, F.Op):
+            if n.name in _IBIN:
+                a, b = gen(n.args[0]), gen(n.args[1])
+                r = emit(_IBIN[n.name], a, b)
+            elif n.name in _CMP:
+                a, b = gen(n.args[0]), gen(n.args[1])
+                r = emit(_CMP[n.name], a, b)
+            elif n.name == "invert":
+                r = emit("inv", gen(n.args[0]))
+            elif n.name == "neg":
+                z = gen(F.Const(0))
+                r = emit("sub", z, gen(n.args[0]))
+            elif n.name == "where":
+                cnd = gen(n.args[0])
+                a, b = gen(n.args[1]), gen(n.args[2])
+                r = emit("where", a, b, cnd)
+            elif n.name in ("rbf16", "rf16"):
+                r = gen(n.args[0])
+            else:
+                raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: {n.name} in an index program")
+        else:
+            raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: {type(n).__name__} in an index program")
+        memo[k] = r
+        return r
+
+    res = gen(tree)
+    if code[-1].dst != res:
+        emit("add", res, gen(F.Const(0)))
+    return code
+
+
+def _lower_gather(spec, prog, st):
+    """A row gather (index_select), e.g. the MoE dispatch's token copy (validation/pytorchsim/
+    layer_op_dispatch_128x0_bf16/01_*_triton.py: out[x] = table[x % 2048 + 2048 * t], t computed from
+    idx[x // 2048] -- Python floor division by top-k, negative results wrapped by the token count): the
+    store is flat over x, the gathered load's affine part is x % C, its data part C * t(idx[...])."""
+    ld = strip_casts(st.value)
+    if st.mask is not None or ld.mask is not None:
+        raise Refused(Reason.MASKED_STORE_NOT_A_BOX, f"{spec.name}: a masked gather")
+    if st.index.const != 0 or st.index.terms != {F.Digit("x"): 1}:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: gather store index {st.index} is not x")
+    aff = ld.index
+    if aff.const != 0 or len(aff.terms) != 1:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: gathered load index {aff} is not x % C + data")
+    (dg, coef), = aff.terms.items()
+    if dg.var != "x" or dg.div != 1 or dg.mod is None or coef != 1:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: gathered load index {aff} is not x % C + data")
+    C = int(dg.mod)
+    data = ld.data
+    t = None
+    if isinstance(data, F.Op) and data.name == "mul":
+        for a, b in ((data.args[0], data.args[1]), (data.args[1], data.args[0])):
+            if isinstance(a, F.Const) and int(a.v) == C:
+                t = b
+    if t is None:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: the gathered offset is not {C} * row")
+    leaves = [n for n in walk(t) if isinstance(n, F.Load)]
+    if not leaves:
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a gather whose row reads no index")
+    il = leaves[0]
+    m = D.Map()
+    m.arg = il.arg
+    m.offset = il.index.const
+    digits = []
+    for d, c in sorted(il.index.terms.items(), key=lambda kv: (kv[0].var, kv[0].div)):
+        if d.var != "x" or d.div % C != 0:
+            raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: index load {il.index} is not a function of x // {C}")
+        digits.append((d.div // C, _NO_MOD if d.mod is None else int(d.mod), int(c)))
+    if len(digits) > D.MAX_DIGITS:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: index load {il.index} has too many digits")
+    m.ndigit = len(digits)
+    for i, (dv, md, sd) in enumerate(digits):
+        m.div[i], m.mod[i], m.stride[i] = dv, md, sd
+    code = _int_program(spec, t, il)
+    out, table = spec.args[st.arg], spec.args[ld.arg]
+    numel = _lookup(spec, prog, "xnumel") or out.numel
+    d = D.new(D.GATHER_ROWS, _manifest_args(spec), spec.grid, units=int(numel) // C, unit_size=1)
+    g = d.p.gat
+    g.rows, g.cols, g.table_rows = int(numel) // C, C, table.numel // C
+    g.out_arg, g.table_arg, g.idx_arg, g.ncode = st.arg, ld.arg, il.arg, len(code)
+    g.idx_map = m
+    for i, ins in enumerate(code):
+        g.code[i] = ins
     return Lowered(d, D.describe(d))

@@ -138,6 +138,20 @@ def cases():
     for k, n, gold in ((384, 1152, True), (768, 768, True), (2048, 2048, True), (4096, 4096, False), (4096, 2048, False)):
         out.append((f"gemm_1x{k}x{n}", spec_file(f"gemm_1x{k}x{n}_bf16", 0),
                     {"family": "gemm", "M": 1, "N": n, "K": k, "residual": False}, gold))
+    # MoE routing ops (Qwen3-30B-A3B layer ops: 128 experts, top-8, hidden 2048).
+    for T, gold in ((1, True), (128, True), (4096, False)):
+        rp, dp = f"layer_op_router_post_{T}x0_bf16", f"layer_op_dispatch_{T}x0_bf16"
+        out += [
+            (f"moe_router_t{T}_00_softmax", spec_file(rp, 0),
+             {"family": "softmax_rows", "rows": T, "cols": 128, "out_dtype": "float32"}, gold),
+            (f"moe_router_t{T}_01_topk", spec_file(rp, 1),
+             {"family": "topk", "rows": T, "cols": 128, "cols_padded": 128, "k": 8, "largest": True}, gold),
+            (f"moe_router_t{T}_02_normalise", spec_file(rp, 2), {"family": "row_divsum", "rows": T, "cols": 8}, gold),
+            (f"moe_dispatch_t{T}_00_sort", spec_file(dp, 0),
+             {"family": "sort", "rows": 1, "cols": 8 * T, "descending": False, "float_keys": False}, gold),
+            (f"moe_dispatch_t{T}_01_gather", spec_file(dp, 1),
+             {"family": "dispatch_gather", "tokens": T, "hidden": 2048, "topk": 8}, gold),
+        ]
     for m in (128, 512, 2048, 4096, 8192):
         out.append((f"gemm_{m}x4096x4096", spec_file(f"gemm_{m}x4096x4096_bf16", 0),
                     {"family": "gemm", "M": m, "N": 4096, "K": 4096, "residual": False}, False))
@@ -239,6 +253,33 @@ def interpret(spec, inputs):
     return {a.name: t for a, t in zip(spec.args, tens) if a.role in ("out", "inout")}
 
 
+def convention_inputs(spec, skip, given):
+    """The input convention (one generator seeded 0, randn per read argument in order, cast to its dtype),
+    with the arguments in `skip` taken from `given` and drawing nothing."""
+    import torch
+    g = torch.Generator().manual_seed(0)
+    out = {}
+    for a in spec.args:
+        if a.role not in ("in", "inout"):
+            continue
+        out[a.name] = given[a.name] if a.name in skip else torch.randn(a.numel, generator=g).to(getattr(torch, a.dtype))
+    return out
+
+
+def recorded_args(spec, inputs):
+    """The read arguments the spec's make_inputs does not draw (loaded from a recording): grown one at a time
+    until every other argument matches the convention exactly."""
+    import torch
+    skip = []
+    while True:
+        conv = convention_inputs(spec, set(skip), inputs)
+        diff = [n for n in inputs if not torch.equal(conv[n].reshape(-1), inputs[n].reshape(-1))]
+        new = [n for n in diff if n not in skip]
+        if not new:
+            return skip
+        skip.append(new[0])
+
+
 def bits(t):
     import torch
     t = t.contiguous()
@@ -281,6 +322,13 @@ def main():
             inputs = spec.make_inputs(torch, seed=0)
             if list(inputs) != reads:
                 raise SystemExit(f"{name}: make_inputs builds {list(inputs)}, the read arguments are {reads}")
+            recorded = recorded_args(spec, inputs)
+            if recorded:
+                # Arguments the spec loads from a recording beside it (routing indices of a model run): kept as
+                # a fixture; they consume no random draw, so the other arguments still follow the convention.
+                np.savez_compressed(os.path.join(vecdir, f"{name}__inputs.npz"),
+                                    **{a: inputs[a].contiguous().numpy() for a in recorded})
+                case["recorded"] = {"file": f"vectors/{name}__inputs.npz", "args": recorded}
             outs = interpret(spec, inputs)
             payload = {}
             for k, t in outs.items():

@@ -1,0 +1,122 @@
+"""The MoE routing programs on the B200 against the CPU oracle (the Qwen3-30B-A3B layer ops of the bundle):
+top-k selection and row sorts are bit exact (values are copies, indices integers); the row normalisation is
+bf16 within rtol = atol = 1e-2; the dispatch gather is a bit-exact copy.  Edge cases follow the reference's
+own rules: tied values go to the lowest column, -inf inputs make the top-k repeat an index, fp32 sort keys
+order NaN last and -0 with +0, a gather row outside the table records PTSIM_E_OOB (the reference asserts)."""
+import math
+
+import pytest
+import torch
+
+from pytorchsim_triton_compiler.codegen import build as B
+from pytorchsim_triton_compiler.codegen import descriptors as D
+from pytorchsim_triton_compiler.runtime import cuda as RC
+from pytorchsim_triton_compiler.runtime import native
+from oracle import programs as O
+from tests._helpers import bits_equal, compare
+
+pytestmark = pytest.mark.gpu
+
+
+def run(desc, tensors):
+    ts = [t.cuda() for t in tensors]
+    RC.launch_tensors(D.to_bytes(desc), ts)
+    return [t.cpu() for t in ts]
+
+
+@pytest.mark.parametrize("rows,cols,padded,k,largest,dtype", [
+    (4096, 128, 128, 8, True, "float32"), (1, 128, 128, 8, True, "float32"), (37, 100, 128, 5, False, "float32"),
+    (64, 8, 8, 8, True, "float32"), (10, 1000, 1024, 3, True, "float32"), (300, 64, 64, 4, True, "bfloat16")])
+def test_topk(rows, cols, padded, k, largest, dtype):
+    g = torch.Generator().manual_seed(rows + cols)
+    x = torch.randn(rows * cols, generator=g).to(getattr(torch, dtype))
+    v, i = run(B.topk(rows, cols, k, largest, padded, dtype), [x, torch.zeros(rows * k, dtype=x.dtype),
+                                                                torch.zeros(rows * k, dtype=torch.int64)])[1:]
+    wv, wi = O.topk_rows(x, rows, cols, padded, k, largest)
+    assert bits_equal(v, wv) and torch.equal(i, wi)
+
+
+def test_topk_ties_and_spent_columns():
+    """Equal values go to the lowest column; a row with fewer than k finite values takes the lowest spent
+    column again (the reference keeps spent columns as candidates)."""
+    rows, cols, k = 3, 16, 6
+    x = torch.zeros(rows, cols)
+    x[0] = torch.tensor([3.0, 1, 3, 2, 3, 0, 1, 2, 3, 3, 0, 0, 1, 2, 3, 3])
+    x[1] = -math.inf
+    x[1, 5], x[1, 9] = 1.0, 2.0
+    x[2] = torch.arange(cols, dtype=torch.float32).flip(0)
+    x = x.reshape(-1)
+    v, i = run(B.topk(rows, cols, k), [x, torch.zeros(rows * k), torch.zeros(rows * k, dtype=torch.int64)])[1:]
+    wv, wi = O.topk_rows(x, rows, cols, cols, k, True)
+    assert bits_equal(v, wv) and torch.equal(i, wi)
+    assert i.view(rows, k)[1].tolist() == [9, 5, 0, 0, 0, 0]
+
+
+@pytest.mark.parametrize("rows,cols,lo,hi,desc", [
+    (1, 32768, 0, 128, False), (1, 1024, -4, 5, False), (3, 5000, 0, 256, True), (2, 8192, -10**12, 10**12, False),
+    (4, 777, -(1 << 62), 1 << 62, True), (1, 8, 0, 8, False), (5, 1, 0, 3, False)])
+def test_sort_int_keys(rows, cols, lo, hi, desc):
+    g = torch.Generator().manual_seed(cols)
+    x = torch.randint(lo, hi, (rows * cols,), generator=g, dtype=torch.int64)
+    v, i = run(B.sort(rows, cols, desc), [x, torch.zeros_like(x), torch.zeros_like(x)])[1:]
+    wv, wi = O.sort_rows(x, rows, cols, desc)
+    assert torch.equal(v, wv) and torch.equal(i, wi)
+
+
+@pytest.mark.parametrize("desc", [False, True])
+def test_sort_float_keys(desc):
+    rows, cols = 2, 4000
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(rows * cols, generator=g)
+    x[::97] = float("nan")
+    x[5::101] = -0.0
+    x[7::103] = 0.0
+    x[11::107] = math.inf
+    x[13::109] = -math.inf
+    x[17::53] = 1.5      # ties
+    v, i = run(B.sort(rows, cols, desc, float_keys=True, dtype="float32"), [x, torch.zeros_like(x),
+                                                                             torch.zeros(rows * cols, dtype=torch.int64)])[1:]
+    wv, wi = O.sort_rows(x, rows, cols, desc, float_keys=True)
+    assert bits_equal(v, wv) and torch.equal(i, wi)
+
+
+def test_sort_wide_long_row_is_reported():
+    """A row longer than the shared-memory sort whose keys span more than the counting sort's 256 values is
+    not run: the kernel records PTSIM_E_UNSUPPORTED, reported at synchronisation."""
+    x = torch.arange(9000, dtype=torch.int64).flip(0) * 1000
+    ts = [x.cuda(), torch.zeros_like(x).cuda(), torch.zeros_like(x).cuda()]
+    with pytest.raises(native.ExecutorError) as e:
+        RC.launch_tensors(D.to_bytes(B.sort(1, 9000)), ts)
+    assert e.value.code == D.E_UNSUPPORTED
+
+
+@pytest.mark.parametrize("rows,cols", [(4096, 8), (1, 8), (100, 33), (7, 1000)])
+def test_row_divsum(rows, cols):
+    g = torch.Generator().manual_seed(rows)
+    x = torch.rand(rows * cols, generator=g) + 0.1
+    out = run(B.row_divsum(rows, cols), [x, torch.zeros(rows * cols, dtype=torch.bfloat16)])[1]
+    ok, rep = compare(out, O.row_divsum(x, rows, cols), 1e-2, 1e-2)
+    assert ok, rep
+
+
+@pytest.mark.parametrize("tokens,hidden,topk", [(4096, 2048, 8), (128, 2048, 8), (5, 64, 2), (300, 40, 3)])
+def test_dispatch_gather(tokens, hidden, topk):
+    rows = tokens * topk
+    g = torch.Generator().manual_seed(tokens)
+    pos = torch.randperm(rows, generator=g).to(torch.int64)
+    pos[:: 7] -= rows          # negative positions: floor division then the wrap by + tokens
+    table = torch.randn(tokens * hidden, generator=g).to(torch.bfloat16)
+    d = B.gather_rows_floordiv(rows, hidden, tokens, topk)
+    out = run(d, [pos, table, torch.zeros(rows * hidden, dtype=torch.bfloat16)])[2]
+    assert bits_equal(out, O.dispatch_gather(pos, table, tokens, hidden, topk))
+
+
+def test_dispatch_gather_out_of_range_is_recorded():
+    tokens, hidden, topk = 16, 64, 2
+    pos = torch.arange(tokens * topk, dtype=torch.int64)
+    pos[3] = 10 * tokens * topk        # floor(pos / topk) >= tokens: outside the table
+    table = torch.randn(tokens * hidden).to(torch.bfloat16)
+    ts = [pos.cuda(), table.cuda(), torch.zeros(tokens * topk * hidden, dtype=torch.bfloat16).cuda()]
+    with pytest.raises(native.ExecutorError) as e:
+        RC.launch_tensors(D.to_bytes(B.gather_rows_floordiv(tokens * topk, hidden, tokens, topk)), ts)
+    assert e.value.code == D.E_OOB

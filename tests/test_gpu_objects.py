@@ -18,7 +18,7 @@ import torch
 
 from pytorchsim_triton_compiler.contract import kernel_object as ko
 from pytorchsim_triton_compiler.runtime import cuda as RC
-from tests.test_oracle_golden import EXACT, as_bits, as_float, make_inputs, run_oracle
+from tests.test_oracle_golden import EXACT, as_bits, as_float, make_inputs, run_oracle_all
 
 pytestmark = pytest.mark.gpu
 
@@ -76,8 +76,18 @@ def test_reference_program_on_b200(case):
     ins = make_inputs(case)
     got_all = run_object(case, ins)
     fam = case["oracle"]["family"]
-    name = [a["name"] for a in case["args"] if a["role"] in ("out", "inout")][0]
-    got = got_all[name]
+    if fam == "attention_prefill" and case["oracle"]["batch"] * case["oracle"]["hq"] * case["oracle"]["seq"] > 32 * 2048:
+        name = [a["name"] for a in case["args"] if a["role"] in ("out", "inout")][0]
+        _check_golden(case, ins, name, got_all[name])
+        attention_subset(case, ins, got_all[name])
+        return
+    for name, want in run_oracle_all(case, ins).items():
+        _check_golden(case, ins, name, got_all[name])
+        _check_oracle(case, ins, name, got_all[name], want)
+
+
+def _check_golden(case, ins, name, got):
+    fam = case["oracle"]["family"]
     dt = next(a["dtype"] for a in case["args"] if a["name"] == name)
     # 1. The reference kernel's own output (Triton interpreter), where recorded.
     if case["golden"]:
@@ -92,11 +102,10 @@ def test_reference_program_on_b200(case):
         else:
             g, w = as_float(gb[::stride], dt), as_float(gold[name], dt)
             assert torch.allclose(g, w, rtol=1e-2, atol=1e-2), f"max abs err vs reference kernel {float((g - w).abs().max())}"
-    # 2. The oracle.
-    if fam == "attention_prefill" and case["oracle"]["batch"] * case["oracle"]["hq"] * case["oracle"]["seq"] > 32 * 2048:
-        attention_subset(case, ins, got)
-        return
-    _, want = run_oracle(case, ins)
+
+
+def _check_oracle(case, ins, name, got, want):
+    fam = case["oracle"]["family"]
     if fam in EXACT or (fam == "reduce_all" and case["oracle"]["op"] == "max"):
         assert torch.equal(got.reshape(-1).view(torch.uint8) if got.dtype != torch.bool else got,
                            want.reshape(-1).to(got.dtype).view(torch.uint8)), "differs from the oracle"

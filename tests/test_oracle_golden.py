@@ -32,12 +32,18 @@ def golden_cases():
 
 def make_inputs(case):
     """The reference's input convention (validation/pytorchsim/*/..._spec.py make_inputs): one generator
-    seeded 0, randn(numel) per read argument in argument order, cast to the argument's dtype."""
+    seeded 0, randn(numel) per read argument in argument order, cast to the argument's dtype.  Arguments a
+    spec loads from a recording (the MoE dispatch's routing indices) come from the committed fixture and
+    draw nothing."""
     g = torch.Generator().manual_seed(0)
+    rec = case.get("recorded") or {}
+    saved = np.load(os.path.join(HERE, "golden", rec["file"])) if rec else {}
     out = {}
     for a in case["args"]:
         dt = getattr(torch, a["dtype"])
-        if a["role"] in ("in", "inout"):
+        if a["name"] in rec.get("args", ()):
+            out[a["name"]] = torch.from_numpy(saved[a["name"]].copy()).to(dt).reshape(-1)
+        elif a["role"] in ("in", "inout"):
             out[a["name"]] = torch.randn(a["numel"], generator=g).to(dt)
         else:
             out[a["name"]] = torch.zeros(a["numel"], dtype=dt)
@@ -61,7 +67,11 @@ def run_oracle(case, ins):
     if fam == "reduce_all":
         return outs[0], O.reduce_all(x[0], o["op"])
     if fam == "softmax_rows":
-        return outs[0], O.softmax_rows(x[0], o["rows"], o["cols"])
+        return outs[0], O.softmax_rows(x[0], o["rows"], o["cols"], getattr(torch, o.get("out_dtype", "bfloat16")))
+    if fam == "row_divsum":
+        return outs[0], O.row_divsum(x[0], o["rows"], o["cols"])
+    if fam == "dispatch_gather":
+        return outs[0], O.dispatch_gather(x[0], x[1], o["tokens"], o["hidden"], o["topk"])
     if fam == "rmsnorm_rows":
         return outs[0], O.rmsnorm_rows(x[0], x[1], o["rows"], o["cols"], o["eps"])
     if fam == "qknorm_rope":
@@ -86,7 +96,24 @@ def run_oracle(case, ins):
     raise AssertionError(f"no oracle family {fam}")
 
 
-EXACT = {"vector_add", "add_one", "slice_add_one", "token_to_head_major", "heads_to_token_major"}
+EXACT = {"vector_add", "add_one", "slice_add_one", "token_to_head_major", "heads_to_token_major", "topk", "sort",
+         "dispatch_gather"}
+
+
+def run_oracle_all(case, ins):
+    """{output argument name: oracle output} of the case's program family (several for top-k and sort)."""
+    o = dict(case["oracle"])
+    fam = o.pop("family")
+    outs = [a["name"] for a in case["args"] if a["role"] in ("out", "inout")]
+    x = [ins[a["name"]] for a in case["args"] if a["role"] in ("in", "inout")]
+    if fam == "topk":
+        v, i = O.topk_rows(x[0], o["rows"], o["cols"], o["cols_padded"], o["k"], o["largest"])
+        return {outs[0]: v, outs[1]: i}
+    if fam == "sort":
+        v, i = O.sort_rows(x[0], o["rows"], o["cols"], o["descending"], o["float_keys"])
+        return {outs[0]: v, outs[1]: i}
+    name, got = run_oracle(case, ins)
+    return {name: got}
 
 
 def as_bits(t):
@@ -103,7 +130,11 @@ def as_float(bits, dtype):
 @pytest.mark.parametrize("case", golden_cases(), ids=lambda c: c["name"])
 def test_oracle_matches_reference_kernel(case):
     ins = make_inputs(case)
-    name, got = run_oracle(case, ins)
+    for name, got in run_oracle_all(case, ins).items():
+        _check_against_gold(case, ins, name, got)
+
+
+def _check_against_gold(case, ins, name, got):
     gold = np.load(os.path.join(HERE, "golden", case["golden"]))
     stride = int(gold[f"{name}__stride"][0])
     want_bits = gold[name]
