@@ -413,7 +413,7 @@ def suite(dev, stream, iters=5, only=None, warm=1):
     flush = L2Flush(dev)
     out = {}
 
-    def timed(name, bound, work):
+    def timed(name, bound, work, int_fill=None):
         if only is not None and name != only:
             return
         m, blob = load_object(name)
@@ -428,6 +428,8 @@ def suite(dev, stream, iters=5, only=None, warm=1):
                 if d.kind == D.GEMM and a["name"] in ("arg_A", "arg_B"):
                     std = 1.0 / math.sqrt(d.p.gemm.K)   # N(0, 1/sqrt(K))
                 ts.append((torch.randn(n, generator=g, device=dev) * std).to(dt))
+            elif a["role"] in ("in", "inout") and int_fill is not None:
+                ts.append(int_fill(n).to(dt).to(dev))
             else:
                 ts.append(torch.zeros(n, dtype=dt, device=dev))
         wsn = native.workspace_size(blob, dev.index or 0)
@@ -465,6 +467,14 @@ def suite(dev, stream, iters=5, only=None, warm=1):
     timed("gemm_1x4096x4096", "hbm", gemv_bytes)
     timed("attention_decode_32x8x4096", "hbm", dec_bytes[4096])
     timed("attention_decode_32x8x8192", "hbm", dec_bytes[8192])
+    # MoE routing at T = 4096 (128 experts, top-8, hidden 2048): the dispatch copy writes 32768 rows of 4 KB
+    # (each of the 4096 token rows read 8 times, mostly from L2); the top-k reads 4096 x 128 fp32 router
+    # probabilities; the sort reorders 32768 expert ids.
+    perm = lambda n: torch.randperm(n, generator=torch.Generator().manual_seed(1))          # sorted positions
+    experts = lambda n: torch.randint(0, 128, (n,), generator=torch.Generator().manual_seed(2))  # expert ids
+    timed("moe_dispatch_t4096_01_gather", "hbm", 2 * 32768 * 2048 + 2 * 4096 * 2048 + 8 * 32768, perm)
+    timed("moe_router_t4096_01_topk", "hbm", 4 * 4096 * 128 + (4 + 8) * 32768)
+    timed("moe_dispatch_t4096_00_sort", "hbm", 3 * 8 * 32768, experts)
     # The same objects as graph-replayed streams (launch latency amortised; inputs rotate past L2).
     for name, work, sets in (("gemm_1x4096x4096", gemv_bytes, 6), ("attention_decode_32x8x4096", dec_bytes[4096], 12),
                              ("attention_decode_32x8x8192", dec_bytes[8192], 6)):

@@ -55,6 +55,7 @@ extern "C" {
 #define PTSIM_KIND_TOPK 10         /* per row, the K largest (or smallest) values and their column indices */
 #define PTSIM_KIND_SORT 11         /* per row, a stable sort of the keys: sorted values and source indices */
 #define PTSIM_KIND_GATHER_ROWS 12  /* out[r, :] = table[t(r), :], t an integer program of an index loaded per row */
+#define PTSIM_KIND_GROUPED_GEMM 13 /* per listed group g: C[rows of g] = A[rows of g] . B[g] (the MoE expert matmul) */
 
 /* Element types of tensor arguments (kernel.json dtype names, contract/kernel_object.py:43-56). */
 #define PTSIM_DT_F32 0
@@ -207,6 +208,14 @@ typedef struct ptsim_gather_params {
   ptsim_iinsn code[PTSIM_MAX_ICODE];
 } ptsim_gather_params;
 
+/* GROUPED_GEMM: A [M, K], B [groups, K, N] (N contiguous; row stride ldb, group stride ldg = K * ldb), C [M, N];
+ * int32 tables: group[programs] (the group each program takes; an index past the last group with rows
+ * holds 0 rows), start[groups + 1], rows[groups + 1].  C rows no program covers keep their values. */
+typedef struct ptsim_ggemm_params {
+  int64_t M, N, K, groups, programs, ldb, ldg;
+  int32_t a_arg, b_arg, c_arg, group_arg, start_arg, rows_arg;
+} ptsim_ggemm_params;
+
 typedef struct ptsim_reduce_params {
   int64_t numel;
   int32_t in_arg, out_arg, op, pad0;
@@ -234,6 +243,7 @@ typedef struct ptsim_desc {
     ptsim_reduce_params red;
     ptsim_select_params sel;
     ptsim_gather_params gat;
+    ptsim_ggemm_params ggemm;
   } p;
 } ptsim_desc;
 

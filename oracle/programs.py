@@ -263,6 +263,22 @@ def dispatch_gather(idx, table, tokens, hidden, topk):
     return table.view(tokens, hidden)[q].reshape(-1)
 
 
+def grouped_gemm(a, b, group, start, rows, c_init, M, N, K, groups):
+    """layer_op_gmm_*/05__grouped_mm_kernel/_grouped_mm_kernel_triton.py:4-44: program p takes group
+    g = group[p] and its rows [start[g], start[g] + rows[g]); those rows of c become bf16(a_rows . b[g]) with
+    fp32 accumulation; rows no program lists keep c's values."""
+    A = f32(a).view(M, K)
+    B = f32(b).view(groups, K, N)
+    out = c_init.clone().view(M, N)
+    for g in group.tolist():
+        n = int(rows[g])
+        if n <= 0:
+            continue
+        s = int(start[g])
+        out[s:s + n] = (A[s:s + n] @ B[g]).to(out.dtype)
+    return out.reshape(-1)
+
+
 def rope_tables(tokens, dim=128, theta=1.0e6):
     """cos/sin tables [tokens, dim] in fp32 for RoPE with base `theta` (the Qwen3 layer feeds them as the
     fp32 inputs in_ptr2/in_ptr3 of 02/04)."""

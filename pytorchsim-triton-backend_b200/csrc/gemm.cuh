@@ -52,7 +52,18 @@ struct GemmArgs {
   int64_t m_begin, m_end, N, K, ldc, ldr;
   int32_t tiles_m, tiles_n;
   int32_t splits, kb_per_split;  // split-K: each output tile's K range cut over the `splits` CTAs of a cluster
+  // Grouped GEMM (null otherwise): program p multiplies rows [start[g], start[g] + rows[g]) of A by group
+  // g = grp_id[p] of B (rows [g * b_group_rows, +K) of tmap_b); the output tiles are those rows' 128-row
+  // tiles, listed program by program.
+  const int32_t *grp_id, *grp_start, *grp_rows;
+  int32_t programs, groups;
+  int64_t b_group_rows;
 };
+
+// Shared-memory table of a grouped launch: per program its group, first and end row, and the exclusive
+// prefix of 128-row tiles (programs + 1 entries).
+constexpr int kGemmMaxPrograms = 512;
+constexpr int kGemmGroupTableBytes = 4 * (kGemmMaxPrograms + 1) * 4;
 
 // The epilogue of 32 output columns of one row: + residual (bf16), then the store rounded to the output
 // dtype (bf16 RNE, or fp32).
@@ -119,8 +130,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_kb = int(ceil_div(g.K, kGemmBK));
-  const int num_tiles = g.tiles_m * g.tiles_n;
-  const int num_items = num_tiles * g.splits;   // work item u: tile u / splits, K split u % splits
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -142,15 +151,74 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
     sm100::tmem_alloc(tmem_base_slot, Cfg::TMEM_COLS);
     sm100::tmem_relinquish();
   }
+  // Grouped launches: the program table (after the barrier area).
+  int *g_pre = reinterpret_cast<int *>(smem + STAGES * Cfg::STAGE_BYTES + 256);
+  int *g_grp = g_pre + (kGemmMaxPrograms + 1);
+  int *g_start = g_grp + (kGemmMaxPrograms + 1);
+  int *g_end = g_start + (kGemmMaxPrograms + 1);
+  if (g.grp_id != nullptr) {
+    for (int p = threadIdx.x; p < g.programs; p += blockDim.x) {
+      const int gid = g.grp_id[p];
+      int s0 = 0, nr = 0;
+      if (gid >= 0 && gid <= g.groups) {
+        s0 = g.grp_start[gid];
+        nr = g.grp_rows[gid];
+      }
+      if (gid < 0 || gid > g.groups || s0 < 0 || nr < 0 || int64_t(s0) + nr > g.m_end) {
+        if (gid < 0 || gid > g.groups || nr != 0) record_status(PTSIM_E_OOB);
+        nr = 0;
+        s0 = 0;
+      }
+      g_grp[p] = gid < 0 || gid > g.groups ? 0 : gid;
+      g_start[p] = s0;
+      g_end[p] = s0 + nr;
+      g_pre[p] = (nr + kGemmBM - 1) / kGemmBM;
+    }
+  }
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem_base = *tmem_base_slot;
+  int grouped_mt = 0;   // 128-row tiles of all programs
+  if (g.grp_id != nullptr) {
+    if (threadIdx.x == 0) {
+      int run = 0;
+      for (int p = 0; p < g.programs; ++p) {
+        const int c = g_pre[p];
+        g_pre[p] = run;
+        run += c;
+      }
+      g_pre[g.programs] = run;
+    }
+    __syncthreads();
+    grouped_mt = g_pre[g.programs];
+  }
+  const int num_tiles = (g.grp_id != nullptr ? grouped_mt : g.tiles_m) * g.tiles_n;
+  const int num_items = num_tiles * g.splits;   // work item u: tile u / splits, K split u % splits
 
   // Tile order: m inner, n outer (neighbouring CTAs share a B panel in L2).
   auto tile_coords = [&](int t, int &tm, int &tn) {
-    tm = t % g.tiles_m;
-    tn = t / g.tiles_m;
+    const int mt = g.grp_id != nullptr ? grouped_mt : g.tiles_m;
+    tm = t % mt;
+    tn = t / mt;
+  };
+  // The rows of m-tile tm: first row, end row (exclusive; rows past it are not stored) and B's first row.
+  auto tile_rows = [&](int tm, int64_t &m0, int64_t &m_end, int64_t &b_row0) {
+    if (g.grp_id == nullptr) {
+      m0 = g.m_begin + int64_t(tm) * kGemmBM;
+      m_end = g.m_end;
+      b_row0 = 0;
+      return;
+    }
+    int lo = 0, hi = g.programs - 1;   // the program whose tiles hold tm: g_pre[p] <= tm < g_pre[p + 1]
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (g_pre[mid] <= tm) lo = mid;
+      else hi = mid - 1;
+    }
+    m0 = g_start[lo] + int64_t(tm - g_pre[lo]) * kGemmBM;
+    m_end = g_end[lo];
+    b_row0 = int64_t(g_grp[lo]) * g.b_group_rows;
   };
   auto kb_range = [&](int u, int &kb0, int &kb1) {
     const int sp = u % g.splits;
@@ -167,7 +235,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
         int tm, tn, kb0, kb1;
         tile_coords(u / g.splits, tm, tn);
         kb_range(u, kb0, kb1);
-        const int m0 = int(g.m_begin) + tm * kGemmBM;
+        int64_t m0l, m_endl, b_row0;
+        tile_rows(tm, m0l, m_endl, b_row0);
+        const int m0 = int(m0l);
         const int n0 = tn * BN;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!sm100::mbar_wait(&empty_bar[stage], phase ^ 1)) { *abort_flag = 1; break; }
@@ -176,12 +246,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
           pending |= phase << (stage + 16);
           sm100::tma_load_2d(sA + stage * Cfg::A_BYTES, &g.tmap_a, &full_bar[stage], kb * kGemmBK, m0);
           if constexpr (B_KMAJOR) {
-            sm100::tma_load_2d(sB + stage * Cfg::B_BYTES, &g.tmap_b, &full_bar[stage], kb * kGemmBK, n0);
+            sm100::tma_load_2d(sB + stage * Cfg::B_BYTES, &g.tmap_b, &full_bar[stage], kb * kGemmBK, int(b_row0) + n0);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
               sm100::tma_load_2d(sB + stage * Cfg::B_BYTES + j * (kGemmBK * 128), &g.tmap_b, &full_bar[stage],
-                                 n0 + j * 64, kb * kGemmBK);
+                                 n0 + j * 64, int(b_row0) + kb * kGemmBK);
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -243,9 +313,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
       const int t = u / g.splits;
       int tm, tn;
       tile_coords(t, tm, tn);
-      const int64_t row = g.m_begin + int64_t(tm) * kGemmBM + row_in_tile;
+      int64_t m0, m_end, b_row0;
+      tile_rows(tm, m0, m_end, b_row0);
+      const int64_t row = m0 + row_in_tile;
       const int64_t n0 = int64_t(tn) * BN;
-      const bool row_ok = row < g.m_end;
+      const bool row_ok = row < m_end;
       if (g.splits > 1) continue;   // split-K: the accumulator stays in TMEM for the cluster exchange
 #pragma unroll 1
       for (int j = 0; j < BN / 32; ++j) {
@@ -605,8 +677,12 @@ static int run_gemm(GemmArgs &g, const LaunchCtx &c) {
   using Cfg = GemmCfg<BN>;
   const int items = g.tiles_m * g.tiles_n * g.splits;
   auto kern = gemm_tcgen05_kernel<BN, B_KMAJOR>;
-  PTSIM_CUDA((smem_limit_once<gemm_tcgen05_kernel<BN, B_KMAJOR>>(Cfg::SMEM_BYTES, c.device)));
-  if (g.splits == 1) {
+  // The limit covers a grouped launch's program table too (a launch asks for what it uses).
+  PTSIM_CUDA((smem_limit_once<gemm_tcgen05_kernel<BN, B_KMAJOR>>(Cfg::SMEM_BYTES + kGemmGroupTableBytes, c.device)));
+  if (g.grp_id != nullptr) {
+    // Grouped: the tile count is data-dependent (each group's rows), so one persistent CTA per SM.
+    kern<<<c.sm_count, kGemmThreads, Cfg::SMEM_BYTES + kGemmGroupTableBytes, c.stream>>>(g);
+  } else if (g.splits == 1) {
     const int grid = items < c.sm_count ? items : c.sm_count;
     kern<<<grid, kGemmThreads, Cfg::SMEM_BYTES, c.stream>>>(g);
   } else {
@@ -724,6 +800,55 @@ static GemmPlan plan_gemm(int64_t m_rows, int64_t m_total, int64_t N, int64_t K,
     pl.tiles_n = ceil_div(N, pl.bn);
   }
   return pl;
+}
+
+// Grouped GEMM (the MoE expert matmul, validation/pytorchsim/layer_op_gmm_gate_up_*/05__grouped_mm_kernel/
+// _grouped_mm_kernel_triton.py:4-44): program p takes group g = group[p] with rows[g] rows from start[g];
+// C[start[g] + i, :] = bf16(A[start[g] + i, :] . B[g]) in fp32, B[g] = [K, N] N-contiguous at g * ldg.  Rows no
+// program lists are left as they are (C is inout).  Runs on the persistent tcgen05 kernel with the tile
+// list built on the device from the group tables.
+int launch_grouped_gemm(const ptsim_desc &d, void *const *ptrs, const LaunchCtx &c) {
+  const ptsim_ggemm_params &p = d.p.ggemm;
+  for (int a : {p.a_arg, p.b_arg, p.c_arg})
+    if (d.arg_dtype[a] != PTSIM_DT_BF16) return fail(PTSIM_E_UNSUPPORTED, "grouped GEMM runs bf16 A, B and C");
+  for (int a : {p.group_arg, p.start_arg, p.rows_arg})
+    if (d.arg_dtype[a] != PTSIM_DT_I32) return fail(PTSIM_E_UNSUPPORTED, "grouped GEMM group tables must be int32");
+  if (p.programs < 1 || p.programs > kGemmMaxPrograms)
+    return fail(PTSIM_E_UNSUPPORTED, "grouped GEMM with %lld programs (runs 1-%d)", (long long)p.programs, kGemmMaxPrograms);
+  if (p.K % 8 != 0 || p.N % 8 != 0 || p.ldb % 8 != 0 || p.ldg != p.K * p.ldb)
+    return fail(PTSIM_E_UNSUPPORTED, "grouped GEMM needs K, N and the row stride multiples of 8 and contiguous groups");
+  if (p.M >= (int64_t(1) << 31) || p.groups * p.K >= (int64_t(1) << 31))
+    return fail(PTSIM_E_UNSUPPORTED, "grouped GEMM beyond 2^31 rows");
+  GemmArgs g;
+  memset(&g, 0, sizeof(g));
+  g.m_begin = 0;
+  g.m_end = p.M;
+  g.N = p.N;
+  g.K = p.K;
+  g.ldc = p.N;
+  g.c = reinterpret_cast<uint16_t *>(ptrs[p.c_arg]);
+  g.splits = 1;
+  g.kb_per_split = int(ceil_div(p.K, kGemmBK));
+  g.grp_id = reinterpret_cast<const int32_t *>(ptrs[p.group_arg]);
+  g.grp_start = reinterpret_cast<const int32_t *>(ptrs[p.start_arg]);
+  g.grp_rows = reinterpret_cast<const int32_t *>(ptrs[p.rows_arg]);
+  g.programs = int(p.programs);
+  g.groups = int(p.groups);
+  g.b_group_rows = p.K;
+  int rc = make_tmap_2d(&g.tmap_a, ptrs[p.a_arg], uint64_t(p.K), uint64_t(p.M), uint64_t(p.K), kGemmBK, kGemmBM);
+  if (rc) return rc;
+  rc = make_tmap_2d(&g.tmap_b, ptrs[p.b_arg], uint64_t(p.N), uint64_t(p.groups * p.K), uint64_t(p.ldb), 64, kGemmBK);
+  if (rc) return rc;
+  if (p.N >= 256) {
+    g.tiles_n = int(ceil_div(p.N, 256));
+    return run_gemm<256, false>(g, c);
+  }
+  if (p.N > 64) {
+    g.tiles_n = int(ceil_div(p.N, 128));
+    return run_gemm<128, false>(g, c);
+  }
+  g.tiles_n = int(ceil_div(p.N, 64));
+  return run_gemm<64, false>(g, c);
 }
 
 int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c) {

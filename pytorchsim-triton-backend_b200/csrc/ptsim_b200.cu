@@ -214,6 +214,21 @@ static int check_desc(const void *p, size_t bytes) {
           return fail(PTSIM_E_DESC, "gather instruction %d", i);
       break;
     }
+    case PTSIM_KIND_GROUPED_GEMM: {
+      const ptsim_ggemm_params &q = d.p.ggemm;
+      if ((rc = check_arg(d, q.a_arg, "A")) || (rc = check_arg(d, q.b_arg, "B")) || (rc = check_arg(d, q.c_arg, "C")) ||
+          (rc = check_arg(d, q.group_arg, "group ids")) || (rc = check_arg(d, q.start_arg, "group starts")) ||
+          (rc = check_arg(d, q.rows_arg, "group rows")))
+        return rc;
+      if (q.M < 0 || q.N < 1 || q.K < 1 || q.groups < 1 || q.programs < 0 || q.ldb < q.N || q.ldg < q.K * q.ldb)
+        return fail(PTSIM_E_DESC, "grouped GEMM %lld x %lld x %lld over %lld groups", (long long)q.M, (long long)q.N,
+                    (long long)q.K, (long long)q.groups);
+      if (q.M * q.K > d.arg_numel[q.a_arg] || q.M * q.N > d.arg_numel[q.c_arg] ||
+          (q.groups - 1) * q.ldg + (q.K - 1) * q.ldb + q.N > d.arg_numel[q.b_arg] || q.programs > d.arg_numel[q.group_arg] ||
+          q.groups + 1 > d.arg_numel[q.start_arg] || q.groups + 1 > d.arg_numel[q.rows_arg])
+        return fail(PTSIM_E_OOB, "grouped GEMM operands extend past their tensors");
+      break;
+    }
     case PTSIM_KIND_REDUCE_ALL: {
       const ptsim_reduce_params &r = d.p.red;
       if ((rc = check_arg(d, r.in_arg, "reduce input")) || (rc = check_arg(d, r.out_arg, "reduce output"))) return rc;
@@ -283,6 +298,7 @@ int ptsim_launch(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int
     case PTSIM_KIND_TOPK: return launch_topk(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_SORT: return launch_sort(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_GATHER_ROWS: return launch_gather_rows(d, dev_ptrs, lo, hi, c);
+    case PTSIM_KIND_GROUPED_GEMM: return launch_grouped_gemm(d, dev_ptrs, c);
     case PTSIM_KIND_QKNORM_ROPE: return launch_qkrope(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_GEMM: return launch_gemm(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_ATTN_PREFILL: return launch_attention(d, dev_ptrs, lo, hi, c);

@@ -161,6 +161,19 @@ def gather_rows_floordiv(rows, cols, table_rows, div, dtype="bfloat16", idx_dtyp
     return d
 
 
+def grouped_gemm(M, N, K, groups, programs):
+    """The MoE expert matmul (layer_op_gmm_*/05__grouped_mm_kernel): a [M, K], b [groups, K, N], int32 group /
+    start / rows tables, c [M, N] (inout)."""
+    d = D.new(D.GROUPED_GEMM, _args([("a_ptr", "bfloat16", M * K), ("b_ptr", "bfloat16", groups * K * N),
+                                     ("group_ptr", "int32", programs), ("start_ptr", "int32", groups + 1),
+                                     ("rows_ptr", "int32", groups + 1), ("c_ptr", "bfloat16", M * N)]),
+              (programs, 1, 1), units=1, unit_size=1)
+    q = d.p.ggemm
+    q.M, q.N, q.K, q.groups, q.programs, q.ldb, q.ldg = M, N, K, groups, programs, N, K * N
+    q.a_arg, q.b_arg, q.group_arg, q.start_arg, q.rows_arg, q.c_arg = 0, 1, 2, 3, 4, 5
+    return d
+
+
 def reduce_all(numel, op="sum", dtype="bfloat16"):
     d = D.new(D.REDUCE_ALL, _args([("in_ptr0", dtype, numel), ("out_ptr0", "float32", 1)]), [1], units=1, unit_size=1,
               workspace_bytes=D.REDUCE_WORKSPACE_BYTES)

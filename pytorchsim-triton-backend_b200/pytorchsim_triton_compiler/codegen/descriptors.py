@@ -12,11 +12,11 @@ MAX_ARGS, MAX_MAPS, MAX_DIGITS, MAX_CODE, MAX_REGS = 16, 8, 4, 32, 8
 
 # Kinds (PTSIM_KIND_*).
 ELEMENTWISE, ROW_SOFTMAX, ROW_RMSNORM, QKNORM_ROPE, GEMM, ATTN_PREFILL, REDUCE_ALL, ATTN_DECODE = 1, 2, 3, 4, 5, 6, 7, 8
-ROW_DIVSUM, TOPK, SORT, GATHER_ROWS = 9, 10, 11, 12
+ROW_DIVSUM, TOPK, SORT, GATHER_ROWS, GROUPED_GEMM = 9, 10, 11, 12, 13
 KIND_NAME = {ELEMENTWISE: "elementwise", ROW_SOFTMAX: "row_softmax", ROW_RMSNORM: "row_rmsnorm",
              QKNORM_ROPE: "qknorm_rope", GEMM: "gemm", ATTN_PREFILL: "attn_prefill", REDUCE_ALL: "reduce_all",
              ATTN_DECODE: "attn_decode", ROW_DIVSUM: "row_divsum", TOPK: "topk", SORT: "sort",
-             GATHER_ROWS: "gather_rows"}
+             GATHER_ROWS: "gather_rows", GROUPED_GEMM: "grouped_gemm"}
 
 # Element types (PTSIM_DT_*), keyed by kernel.json dtype names (contract/kernel_object.py NP_DTYPE keys).
 DTYPE_CODE = {"float32": 0, "bfloat16": 1, "float16": 2, "int32": 3, "int64": 4, "int16": 5, "int8": 6,
@@ -104,9 +104,16 @@ class GatherParams(C.Structure):
                 ("code", IInsn * MAX_ICODE)]
 
 
+class GGemmParams(C.Structure):
+    _fields_ = [("M", C.c_int64), ("N", C.c_int64), ("K", C.c_int64), ("groups", C.c_int64), ("programs", C.c_int64),
+                ("ldb", C.c_int64), ("ldg", C.c_int64), ("a_arg", C.c_int32), ("b_arg", C.c_int32), ("c_arg", C.c_int32),
+                ("group_arg", C.c_int32), ("start_arg", C.c_int32), ("rows_arg", C.c_int32)]
+
+
 class Params(C.Union):
     _fields_ = [("ew", EwParams), ("row", RowParams), ("qk", QkParams), ("gemm", GemmParams),
-                ("attn", AttnParams), ("red", ReduceParams), ("sel", SelectParams), ("gat", GatherParams)]
+                ("attn", AttnParams), ("red", ReduceParams), ("sel", SelectParams), ("gat", GatherParams),
+                ("ggemm", GGemmParams)]
 
 
 class Desc(C.Structure):
@@ -197,6 +204,9 @@ def describe(d):
         gp = d.p.gat
         out.update(rows=gp.rows, cols=gp.cols, table_rows=gp.table_rows,
                    program=[(IOP_NAME.get(i.op, i.op), i.dst, i.a, i.b, i.c, i.imm) for i in list(gp.code)[:gp.ncode]])
+    elif d.kind == GROUPED_GEMM:
+        q = d.p.ggemm
+        out.update(M=q.M, N=q.N, K=q.K, groups=q.groups, programs=q.programs)
     elif d.kind == REDUCE_ALL:
         out.update(numel=d.p.red.numel, op="max" if d.p.red.op == RED_MAX else "sum")
     return out

@@ -125,6 +125,8 @@ def lower(spec, fn=None):
         return _lower_topk(spec)
     if {"L", "D", "LOG", "DESCENDING", "FLOAT"} <= ce:
         return _lower_sort(spec)
+    if {"sbg", "sbk", "sbn", "K", "KP", "N", "BM", "BN", "BK"} <= ce:
+        return _lower_grouped_gemm(spec)
     dots = [n for n in ast.walk(tree) if isinstance(n, ast.Call) and isinstance(n.func, ast.Attribute) and n.func.attr == "dot"]
     if dots:
         if len(dots) >= 2 and {"HQ", "G", "S", "D", "SCALE"} <= set(spec.constexprs):
@@ -787,4 +789,33 @@ def _lower_gather(spec, prog, st):
     g.idx_map = m
     for i, ins in enumerate(code):
         g.code[i] = ins
+    return Lowered(d, D.describe(d))
+
+
+def _lower_grouped_gemm(spec):
+    """The MoE expert matmul (validation/pytorchsim/layer_op_gmm_gate_up_128x0_bf16/05__grouped_mm_kernel/
+    _grouped_mm_kernel_triton.py:4-44): program p takes group g = group_ptr[p], rows [start_ptr[g],
+    + rows_ptr[g]) of a (row stride K) times b[g] (at g * sbg, strides sbk, sbn), stored to c (row stride N)."""
+    ce = spec.constexprs
+    ptrs = _pointer_params(spec)
+    idx = {n: i for i, n in enumerate(ptrs)}
+    need = ("a_ptr", "b_ptr", "group_ptr", "start_ptr", "rows_ptr", "c_ptr")
+    if not all(n in idx for n in need):
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: grouped matmul wants {', '.join(need)}")
+    K, N, sbg, sbk, sbn = (int(ce[k]) for k in ("K", "N", "sbg", "sbk", "sbn"))
+    if sbn != 1 or sbg != K * sbk:
+        raise Refused(Reason.SHAPE_NOT_RUN, f"{spec.name}: B strides ({sbg}, {sbk}, {sbn}) are not contiguous [K, N] groups")
+    a, b = spec.args[idx["a_ptr"]], spec.args[idx["b_ptr"]]
+    M = a.numel // K
+    groups = b.numel // sbg
+    programs = _grid_programs(spec)[0]
+    for n in need:
+        want = "bfloat16" if n in ("a_ptr", "b_ptr", "c_ptr") else "int32"
+        if spec.args[idx[n]].dtype != want:
+            raise Refused(Reason.DTYPE_NOT_RUN, f"{spec.name}: {n} is {spec.args[idx[n]].dtype}")
+    d = D.new(D.GROUPED_GEMM, _manifest_args(spec), spec.grid, units=1, unit_size=1)
+    q = d.p.ggemm
+    q.M, q.N, q.K, q.groups, q.programs, q.ldb, q.ldg = M, N, K, groups, programs, sbk, sbg
+    q.a_arg, q.b_arg, q.c_arg = idx["a_ptr"], idx["b_ptr"], idx["c_ptr"]
+    q.group_arg, q.start_arg, q.rows_arg = idx["group_ptr"], idx["start_ptr"], idx["rows_ptr"]
     return Lowered(d, D.describe(d))

@@ -152,6 +152,16 @@ def cases():
             (f"moe_dispatch_t{T}_01_gather", spec_file(dp, 1),
              {"family": "dispatch_gather", "tokens": T, "hidden": 2048, "topk": 8}, gold),
         ]
+    # The MoE expert matmul: the reference kernel at an interpreter-sized configuration (golden), and the
+    # bundle's T = 1 and 128 objects (gate_up K 2048 -> N 1536, down K 768 -> N 2048; 128 experts; the group
+    # tables of the recorded routing are kept as input fixtures).
+    out.append(("moe_gmm_small", spec_file("layer_op_gmm_gate_up_1x0_bf16", 5),
+                {"family": "grouped_gemm", "M": 210, "N": 96, "K": 64, "groups": 6, "modify": "gmm_small"}, True))
+    for T in (1, 128):
+        out.append((f"moe_gmm_gate_up_t{T}", spec_file(f"layer_op_gmm_gate_up_{T}x0_bf16", 5),
+                    {"family": "grouped_gemm", "M": 8 * T, "N": 1536, "K": 2048, "groups": 128}, False))
+        out.append((f"moe_gmm_down_t{T}", spec_file(f"layer_op_gmm_down_{T}x0_bf16", 5),
+                    {"family": "grouped_gemm", "M": 8 * T, "N": 2048, "K": 768, "groups": 128}, False))
     for m in (128, 512, 2048, 4096, 8192):
         out.append((f"gemm_{m}x4096x4096", spec_file(f"gemm_{m}x4096x4096_bf16", 0),
                     {"family": "gemm", "M": m, "N": 4096, "K": 4096, "residual": False}, False))
@@ -160,7 +170,35 @@ def cases():
     return out
 
 
-MODIFY = {"add_config": add_config, "attention_batch4": attention_batch4}
+def gmm_small(spec):
+    """The bundle's _grouped_mm_kernel source (layer_op_gmm_gate_up_*/05__grouped_mm_kernel) at a size the
+    interpreter runs: 6 groups of K = 64 x N = 96 weights plus the empty entry, 210 rows of which group 4's 10
+    are listed by no program (their output rows must keep their values), one group of 130 rows (two 128-row
+    tiles), empty groups; the tile constants of the bundle (BM 128, BN 2048 masked to N, BK = KP = K)."""
+    from pytorchsim_triton_compiler.contract.kernel_spec import Arg
+    G, M, K, N = 6, 210, 64, 96
+    rows = [0, 37, 130, 1, 10, 32, 0]
+    start = [sum(rows[:i]) for i in range(G + 1)]
+    group = [1, 2, 3, 5, 6, 6]          # the groups with rows, then the empty entry; group 4 is not listed
+    s = copy.copy(spec)
+    s.constexprs = dict(spec.constexprs, sbg=K * N, sbk=N, sbn=1, K=K, KP=K, N=N, BK=K)
+    s.args = [Arg("a_ptr", "in", "bfloat16", (M * K,)), Arg("b_ptr", "in", "bfloat16", (G * K * N,)),
+              Arg("group_ptr", "in", "int32", (len(group),)), Arg("start_ptr", "in", "int32", (G + 1,)),
+              Arg("rows_ptr", "in", "int32", (G + 1,)), Arg("c_ptr", "inout", "bfloat16", (M * N,))]
+    s.grid = (len(group), 1, 1)
+
+    def make_inputs(torch, seed=0):
+        g = torch.Generator().manual_seed(seed)
+        return {"a_ptr": torch.randn(M * K, generator=g).to(torch.bfloat16),
+                "b_ptr": torch.randn(G * K * N, generator=g).to(torch.bfloat16),
+                "group_ptr": torch.tensor(group, dtype=torch.int32), "start_ptr": torch.tensor(start, dtype=torch.int32),
+                "rows_ptr": torch.tensor(rows, dtype=torch.int32),
+                "c_ptr": torch.randn(M * N, generator=g).to(torch.bfloat16)}
+    s.make_inputs = make_inputs
+    return s
+
+
+MODIFY = {"add_config": add_config, "attention_batch4": attention_batch4, "gmm_small": gmm_small}
 
 # ---------------------------------------------------------------------------------------------------
 # Triton interpreter shims
@@ -305,8 +343,9 @@ def main():
         if opts.only and opts.only != name:
             continue
         spec = load_spec(path)
-        if oracle.get("modify"):
-            spec = MODIFY[oracle.pop("modify")](spec)
+        modified = oracle.pop("modify", None)
+        if modified:
+            spec = MODIFY[modified](spec)
         lowered = L.lower(spec)
         d = os.path.join(objdir, name)
         shutil.rmtree(d, ignore_errors=True)
@@ -315,6 +354,18 @@ def main():
         reads = [a.name for a in spec.args if a.role in ("in", "inout")]
         case = {"name": name, "source": os.path.relpath(path, REF), "kind": lowered.kind, "args": gen,
                 "inputs": reads, "oracle": oracle, "golden": None}
+        if modified:
+            case["modified"] = modified   # the spec was resized from the reference's (MODIFY[modified])
+        if not golden and spec.make_inputs is not None and any(a.dtype.startswith("int") for a in spec.args
+                                                                  if a.role in ("in", "inout")):
+            # integer inputs (routing tables) of a case without output vectors: keep the recorded ones
+            inputs = spec.make_inputs(torch, seed=0)
+            recorded = recorded_args(spec, inputs)
+            if recorded:
+                np.savez_compressed(os.path.join(vecdir, f"{name}__inputs.npz"),
+                                    **{a: inputs[a].contiguous().numpy() for a in recorded})
+                case["recorded"] = {"file": f"vectors/{name}__inputs.npz", "args": recorded}
+            del inputs
         if golden and not opts.no_golden:
             g = torch.Generator().manual_seed(0)
             if spec.make_inputs is None:

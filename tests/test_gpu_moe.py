@@ -120,3 +120,54 @@ def test_dispatch_gather_out_of_range_is_recorded():
     with pytest.raises(native.ExecutorError) as e:
         RC.launch_tensors(D.to_bytes(B.gather_rows_floordiv(tokens * topk, hidden, tokens, topk)), ts)
     assert e.value.code == D.E_OOB
+
+
+def _gmm_tables(sizes, listed, gen):
+    """int32 group / start / rows tables for groups of the given row counts (plus the empty entry at the end);
+    `listed`: the groups the programs take, padded to the table length with the empty entry."""
+    G = len(sizes)
+    rows = torch.tensor(list(sizes) + [0], dtype=torch.int32)
+    start = torch.zeros(G + 1, dtype=torch.int32)
+    start[1:] = torch.cumsum(rows[:-1], 0)
+    start[G] = int(rows[:-1].sum())
+    group = torch.tensor(list(listed) + [G] * (G - len(listed)), dtype=torch.int32)
+    return group, start, rows
+
+
+@pytest.mark.parametrize("T,K,N", [(512, 2048, 1536), (512, 768, 2048), (64, 64, 96), (300, 256, 200)])
+def test_grouped_gemm(T, K, N):
+    """Routing-shaped groups: 128 experts of 8 * T rows with uneven sizes (empty experts, experts longer than
+    one 128-row tile); experts listed in order, one expert with rows left unlisted (its output rows keep
+    their values)."""
+    G, M = 128, 8 * T
+    gen = torch.Generator().manual_seed(T + K)
+    w = torch.rand(G, generator=gen) ** 3
+    w[::9] = 0
+    sizes = (w / w.sum() * M).floor().to(torch.int64)
+    sizes[0] += M - int(sizes.sum())
+    skip = int(torch.nonzero(sizes).flatten()[3])
+    listed = [g for g in range(G) if sizes[g] > 0 and g != skip]
+    group, start, rows = _gmm_tables(sizes.tolist(), listed, gen)
+    std = 1.0 / math.sqrt(K)
+    a = (torch.randn(M * K, generator=gen) * std).to(torch.bfloat16)
+    b = (torch.randn(G * K * N, generator=gen) * std).to(torch.bfloat16)
+    c = torch.randn(M * N, generator=gen).to(torch.bfloat16)
+    out = run(B.grouped_gemm(M, N, K, G, G), [a, b, group, start, rows, c])[5]
+    want = O.grouped_gemm(a, b, group, start, rows, c, M, N, K, G)
+    s0, n0 = int(start[skip]), int(rows[skip])
+    assert bits_equal(out.view(M, N)[s0:s0 + n0], c.view(M, N)[s0:s0 + n0])
+    ok, rep = compare(out, want, 1e-2, 1e-2 * max(1.0, float(want.float().pow(2).mean().sqrt())))
+    assert ok, rep
+
+
+def test_grouped_gemm_bad_table_is_recorded():
+    """A group id past the table records PTSIM_E_OOB; the program's rows are not touched."""
+    G, M, K, N = 4, 64, 64, 64
+    group, start, rows = _gmm_tables([16, 16, 16, 16], [0, 1, 2, 3], None)
+    group[2] = 99
+    ts = [torch.randn(M * K).to(torch.bfloat16), torch.randn(G * K * N).to(torch.bfloat16), group, start, rows,
+          torch.zeros(M * N, dtype=torch.bfloat16)]
+    ts = [t.cuda() for t in ts]
+    with pytest.raises(native.ExecutorError) as e:
+        RC.launch_tensors(D.to_bytes(B.grouped_gemm(M, N, K, G, G)), ts)
+    assert e.value.code == D.E_OOB

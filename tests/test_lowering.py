@@ -66,6 +66,8 @@ def fixture_names():
 def test_reference_kernels_lower_to_the_committed_descriptors(name):
     d = os.path.join(OBJ, name)
     case = json.load(open(os.path.join(d, "case.json")))
+    if case.get("modified"):
+        pytest.skip("lowered from a resized copy of the reference's spec")
     spec = load_spec(os.path.join(REF, case["source"]))
     lo = L.lower(spec)
     assert lo.blob == ko.read_desc(d), name
