@@ -475,6 +475,9 @@ def suite(dev, stream, iters=5, only=None, warm=1):
     timed("moe_dispatch_t4096_01_gather", "hbm", 2 * 32768 * 2048 + 2 * 4096 * 2048 + 8 * 32768, perm)
     timed("moe_router_t4096_01_topk", "hbm", 4 * 4096 * 128 + (4 + 8) * 32768)
     timed("moe_dispatch_t4096_00_sort", "hbm", 3 * 8 * 32768, experts)
+    for nm, K, N in (("moe_gmm_gate_up_t4096", 2048, 1536), ("moe_gmm_down_t4096", 768, 2048)):
+        if only is None or only == nm:
+            out[nm] = grouped_gemm_timing(dev, stream, iters, warm, flush, hbm, tflops, K, N)
     # The same objects as graph-replayed streams (launch latency amortised; inputs rotate past L2).
     for name, work, sets in (("gemm_1x4096x4096", gemv_bytes, 6), ("attention_decode_32x8x4096", dec_bytes[4096], 12),
                              ("attention_decode_32x8x8192", dec_bytes[8192], 6)):
@@ -483,6 +486,43 @@ def suite(dev, stream, iters=5, only=None, warm=1):
     if only is None or only == "qwen3_layer":
         out["qwen3_layer_t2048"] = layer_timing(dev, stream, iters, warm, flush, tflops)
     return out
+
+
+def grouped_gemm_timing(dev, stream, iters, warm, flush, hbm, tflops, K, N, T=4096, G=128):
+    """The MoE expert matmul at T tokens x top-8 over G experts (layer_op_gmm_*_4096x0 shapes), every expert
+    receiving 8 T / G rows as the bundle's recorded routing does: median of `iters` launches, L2 flushed.
+    The roofline is the slower of the weights' HBM read and the tensor work."""
+    import torch
+    from pytorchsim_triton_compiler.codegen import build as Bd
+    from pytorchsim_triton_compiler.codegen import descriptors as D
+    from pytorchsim_triton_compiler.runtime import native
+    M = 8 * T
+    blob = D.to_bytes(Bd.grouped_gemm(M, N, K, G, G))
+    g = torch.Generator(device=dev).manual_seed(0)
+    std = 1.0 / math.sqrt(K)
+    a = (torch.randn(M * K, generator=g, device=dev) * std).to(torch.bfloat16)
+    b = (torch.randn(G * K * N, generator=g, device=dev) * std).to(torch.bfloat16)
+    rows = torch.full((G + 1,), M // G, dtype=torch.int32, device=dev)
+    rows[G] = 0
+    start = torch.arange(G + 1, dtype=torch.int32, device=dev) * (M // G)
+    group = torch.arange(G, dtype=torch.int32, device=dev)
+    c = torch.zeros(M * N, dtype=torch.bfloat16, device=dev)
+    ptrs = [t.data_ptr() for t in (a, b, group, start, rows, c)]
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters + warm)]
+    torch.cuda.synchronize()
+    torch.cuda._sleep(int(1e7))
+    for k in range(iters + warm):
+        flush()
+        ev[k][0].record(stream)
+        native.launch(blob, ptrs, 0, 1, 0, 0, stream.cuda_stream)
+        ev[k][1].record(stream)
+    native.sync(stream.cuda_stream)
+    ms = statistics.median([x.elapsed_time(y) for x, y in ev[warm:]])
+    flops, nbytes = 2 * M * N * K, 2 * (G * K * N + M * K + M * N)
+    ideal = max(flops / (tflops * 1e12), nbytes / (hbm * 1e9))
+    return {"ms": round(ms, 4), "TFLOP/s": round(flops / ms / 1e9, 1), "GB/s": round(nbytes / ms / 1e6, 1),
+            "bound": "hbm" if nbytes / (hbm * 1e9) > flops / (tflops * 1e12) else "tensor",
+            "frac_roofline": round(ideal / (ms * 1e-3), 3)}
 
 
 def amortized_vector_add(dev, stream, hbm, sets=16, launches=64):

@@ -651,7 +651,10 @@ static int max_active_clusters(int splits, const LaunchCtx &c) {
   std::atomic<int> *e = (c.device >= 0 && c.device < 64) ? &cache[c.device][slot] : nullptr;
   if (e != nullptr && e->load() > 0) return e->load() - 1;
   auto kern = gemm_tcgen05_kernel<BN, B_KMAJOR>;
-  if ((smem_limit_once<gemm_tcgen05_kernel<BN, B_KMAJOR>>(Cfg::SMEM_BYTES, c.device)) != cudaSuccess) return 0;
+  // The same limit run_gemm sets (the attribute is set once per kernel and device; a grouped launch's
+  // program table rides on top of the ring).
+  if ((smem_limit_once<gemm_tcgen05_kernel<BN, B_KMAJOR>>(Cfg::SMEM_BYTES + kGemmGroupTableBytes, c.device)) != cudaSuccess)
+    return 0;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   cfg.gridDim = dim3(unsigned(splits * c.sm_count));

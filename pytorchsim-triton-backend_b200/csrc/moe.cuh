@@ -119,10 +119,19 @@ __global__ void __launch_bounds__(kSortThreads, 1) sort_kernel(const __grid_cons
   const int64_t n = g.cols;
   // 1. the row's key range
   long long lo = LLONG_MAX, hi = LLONG_MIN;
-  for (int64_t c = tid; c < n; c += kSortThreads) {
-    const long long k = sort_key(g, base + c);
-    lo = k < lo ? k : lo;
-    hi = k > hi ? k : hi;
+  for (int64_t c0 = tid; c0 < n; c0 += 8 * kSortThreads) {
+    long long k[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {   // eight loads in flight per thread
+      const int64_t c = c0 + int64_t(u) * kSortThreads;
+      k[u] = c < n ? sort_key(g, base + c) : lo;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (c0 + int64_t(u) * kSortThreads >= n) break;
+      lo = k[u] < lo ? k[u] : lo;
+      hi = k[u] > hi ? k[u] : hi;
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -150,12 +159,25 @@ __global__ void __launch_bounds__(kSortThreads, 1) sort_kernel(const __grid_cons
     __syncthreads();
     const int64_t seg = ceil_div(n, kSortWarps);
     const int64_t s0 = warp * seg, s1 = s0 + seg < n ? s0 + seg : n;
-    for (int64_t c0 = s0; c0 < s1; c0 += 32) {
-      const int64_t c = c0 + lane;
-      const int key = c < s1 ? int(sort_key(g, base + c) - lo) : -1;
-      const unsigned m = __match_any_sync(0xffffffffu, key);
-      if (key >= 0 && lane == __ffs(m) - 1) hist[warp * kSortCountRange + key] += __popc(m);
-      __syncwarp();
+    // The keys' offsets from the minimum fit a byte: rows up to kSortBitonicMax * 8 keep them in shared
+    // memory after the histogram pass, so the scatter pass reads no global memory.
+    uint8_t *k8 = sort_smem + kSortWarps * kSortCountRange * 4;
+    const bool cache = n <= int64_t(kSortSmem - kSortWarps * kSortCountRange * 4);
+    for (int64_t c0 = s0; c0 < s1; c0 += 32 * 32) {
+      int key[32];
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {   // a whole 1024-key block in flight per warp
+        const int64_t c = c0 + u * 32 + lane;
+        key[u] = c < s1 ? int(sort_key(g, base + c) - lo) : -1;
+      }
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        if (c0 + u * 32 >= s1) break;
+        const unsigned m = __match_any_sync(0xffffffffu, key[u]);
+        if (key[u] >= 0 && lane == __ffs(m) - 1) hist[warp * kSortCountRange + key[u]] += __popc(m);
+        if (cache && key[u] >= 0) k8[c0 + u * 32 + lane] = uint8_t(key[u]);
+        __syncwarp();
+      }
     }
     __syncthreads();
     if (warp == 0) {
@@ -182,8 +204,8 @@ __global__ void __launch_bounds__(kSortThreads, 1) sort_kernel(const __grid_cons
     __syncthreads();
     for (int64_t c0 = s0; c0 < s1; c0 += 32) {
       const int64_t c = c0 + lane;
-      const int64_t k = c < s1 ? sort_key(g, base + c) : 0;
-      const int key = c < s1 ? int(k - lo) : -1;
+      const int key = c < s1 ? (cache ? int(k8[c]) : int(sort_key(g, base + c) - lo)) : -1;
+      const int64_t k = int64_t(lo) + key;
       const unsigned m = __match_any_sync(0xffffffffu, key);
       if (key >= 0) {
         const int rank = __popc(m & ((1u << lane) - 1u));
@@ -306,7 +328,15 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const __grid_constant_
       const int64_t n16 = g.cols * dtype_size(g.out_dt) / 16;
       const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint8_t *>(g.table) + t * g.cols * dtype_size(g.table_dt));
       uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(g.out) + r * g.cols * dtype_size(g.out_dt));
-      for (int64_t i = lane; i < n16; i += 32) __stcs(dst + i, __ldg(src + i));
+      int64_t i = lane;
+      for (; i + 7 * 32 < n16; i += 8 * 32) {   // eight 16-byte loads in flight per lane
+        uint4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = __ldg(src + i + u * 32);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) __stcs(dst + i + u * 32, v[u]);
+      }
+      for (; i < n16; i += 32) __stcs(dst + i, __ldg(src + i));
     } else {
       for (int64_t c2 = lane; c2 < g.cols; c2 += 32)
         st_any(g.out, g.out_dt, r * g.cols + c2, ld_any(g.table, g.table_dt, t * g.cols + c2));

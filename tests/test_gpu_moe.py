@@ -171,3 +171,13 @@ def test_grouped_gemm_bad_table_is_recorded():
     with pytest.raises(native.ExecutorError) as e:
         RC.launch_tensors(D.to_bytes(B.grouped_gemm(M, N, K, G, G)), ts)
     assert e.value.code == D.E_OOB
+
+
+def test_grouped_gemm_after_split_k_gemm():
+    """A grouped launch after a split-K launch of the same GEMM kernel (whose occupancy query sets the kernel's
+    shared-memory limit first) still gets room for its program table."""
+    gemm = B.gemm(128, 4096, 4096)
+    ts = [t.cuda() for t in (torch.zeros(128 * 4096, dtype=torch.bfloat16), torch.zeros(4096 * 4096, dtype=torch.bfloat16),
+                             torch.zeros(128 * 4096, dtype=torch.bfloat16))]
+    RC.launch_tensors(D.to_bytes(gemm), ts)
+    test_grouped_gemm(64, 2048, 1536)
