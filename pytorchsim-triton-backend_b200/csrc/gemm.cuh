@@ -196,11 +196,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
   const int num_tiles = (g.grp_id != nullptr ? grouped_mt : g.tiles_m) * g.tiles_n;
   const int num_items = num_tiles * g.splits;   // work item u: tile u / splits, K split u % splits
 
-  // Tile order: m inner, n outer (neighbouring CTAs share a B panel in L2).
+  // Tile order: m inner, n outer (neighbouring CTAs share a B panel in L2).  Grouped launches go n inner:
+  // the column tiles of one 128-row block run on neighbouring CTAs and share its A tile in L2, and each
+  // expert's weight panels are read while that expert's rows are resident (A is read once, not once per
+  // column tile).
   auto tile_coords = [&](int t, int &tm, int &tn) {
-    const int mt = g.grp_id != nullptr ? grouped_mt : g.tiles_m;
-    tm = t % mt;
-    tn = t / mt;
+    if (g.grp_id != nullptr) {
+      tn = t % g.tiles_n;
+      tm = t / g.tiles_n;
+      return;
+    }
+    tm = t % g.tiles_m;
+    tn = t / g.tiles_m;
   };
   // The rows of m-tile tm: first row, end row (exclusive; rows past it are not stored) and B's first row.
   auto tile_rows = [&](int tm, int64_t &m0, int64_t &m_end, int64_t &b_row0) {
