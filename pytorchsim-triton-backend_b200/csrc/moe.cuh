@@ -317,8 +317,17 @@ __device__ __forceinline__ int64_t gather_row_of(const GatherArgs &g, int64_t r)
 __global__ void __launch_bounds__(256) gather_rows_kernel(const __grid_constant__ GatherArgs g) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
-  for (int64_t r = g.row_begin + ((int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5); r < g.row_end; r += warps) {
-    const int64_t t = gather_row_of(g, r);
+  // Each warp takes kGatherRows consecutive rows at a time: lane i < kGatherRows evaluates row i's index
+  // program (once per row, not once per lane), then the warp copies the rows, each row's table index
+  // broadcast by shuffle.
+  constexpr int kGatherRows = 8;
+  for (int64_t r0 = g.row_begin + ((int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * kGatherRows;
+       r0 < g.row_end; r0 += warps * kGatherRows) {
+    const int64_t mine = lane < kGatherRows && r0 + lane < g.row_end ? gather_row_of(g, r0 + lane) : 0;
+    const int nrow = g.row_end - r0 < kGatherRows ? int(g.row_end - r0) : kGatherRows;
+    for (int j = 0; j < nrow; ++j) {
+    const int64_t r = r0 + j;
+    const int64_t t = __shfl_sync(0xffffffffu, mine, j);
     if (t < 0 || t >= g.table_rows) {
       if (lane == 0) record_status(PTSIM_E_OOB);
       continue;
@@ -340,6 +349,7 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const __grid_constant_
     } else {
       for (int64_t c2 = lane; c2 < g.cols; c2 += 32)
         st_any(g.out, g.out_dt, r * g.cols + c2, ld_any(g.table, g.table_dt, t * g.cols + c2));
+    }
     }
   }
 }
@@ -370,7 +380,7 @@ int launch_gather_rows(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64
           reinterpret_cast<uintptr_t>(g.out) % 16 == 0;
   if (!g.vec && !floaty) return fail(PTSIM_E_UNSUPPORTED, "gather of integer rows needs 16-byte rows");
   if (g.row_end <= g.row_begin) return PTSIM_OK;
-  int64_t blocks = ceil_div(g.row_end - g.row_begin, 8);
+  int64_t blocks = ceil_div(g.row_end - g.row_begin, 8 * 8);   // 8 warps of 8 rows
   if (blocks > int64_t(c.sm_count) * 16) blocks = int64_t(c.sm_count) * 16;
   gather_rows_kernel<<<unsigned(blocks), 256, 0, c.stream>>>(g);
   PTSIM_CUDA(cudaGetLastError());
