@@ -413,7 +413,7 @@ def suite(dev, stream, iters=5, only=None, warm=1):
     flush = L2Flush(dev)
     out = {}
 
-    def timed(name, bound, work, int_fill=None):
+    def timed(name, bound, work, int_fill=None, given=None):
         if only is not None and name != only:
             return
         m, blob = load_object(name)
@@ -423,7 +423,9 @@ def suite(dev, stream, iters=5, only=None, warm=1):
         for a in m["args"]:
             dt = getattr(torch, a["dtype"])
             n = math.prod(a["shape"])
-            if a["role"] in ("in", "inout") and dt.is_floating_point:
+            if given is not None and a["name"] in given:
+                ts.append(given[a["name"]].to(dt).to(dev))
+            elif a["role"] in ("in", "inout") and dt.is_floating_point:
                 std = 1.0
                 if d.kind == D.GEMM and a["name"] in ("arg_A", "arg_B"):
                     std = 1.0 / math.sqrt(d.p.gemm.K)   # N(0, 1/sqrt(K))
@@ -475,6 +477,11 @@ def suite(dev, stream, iters=5, only=None, warm=1):
     timed("moe_dispatch_t4096_01_gather", "hbm", 2 * 32768 * 2048 + 2 * 4096 * 2048 + 8 * 32768, perm)
     timed("moe_router_t4096_01_topk", "hbm", 4 * 4096 * 128 + (4 + 8) * 32768)
     timed("moe_dispatch_t4096_00_sort", "hbm", 3 * 8 * 32768, experts)
+    # combine: 32768 expert-output rows gathered (4 KB each) and weighted into 4096 token rows
+    if only is None or only == "moe_combine_t4096_03_weighted":
+        ids, cum, cnt, pos = moe_routing(4096, 8, 128, 7)
+        timed("moe_combine_t4096_03_weighted", "hbm", 2 * 32768 * 2048 + 2 * 4096 * 2048 + 8 * 3 * 32768,
+              given={"in_ptr0": ids, "in_ptr1": cum, "in_ptr2": cnt, "in_ptr3": pos})
     for nm, K, N in (("moe_gmm_gate_up_t4096", 2048, 1536), ("moe_gmm_down_t4096", 768, 2048)):
         if only is None or only == nm:
             out[nm] = grouped_gemm_timing(dev, stream, iters, warm, flush, hbm, tflops, K, N)
@@ -486,6 +493,20 @@ def suite(dev, stream, iters=5, only=None, warm=1):
     if only is None or only == "qwen3_layer":
         out["qwen3_layer_t2048"] = layer_timing(dev, stream, iters, warm, flush, tflops)
     return out
+
+
+def moe_routing(tokens, topk, experts, seed):
+    """A consistent synthetic MoE routing: each slot's expert id, the experts' counts and inclusive cumulative
+    counts, and each slot's 1-based rank within its expert."""
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    ids = torch.randint(0, experts, (tokens * topk,), generator=g)
+    cnt = torch.bincount(ids, minlength=experts)
+    cum = torch.cumsum(cnt, 0)
+    order = torch.argsort(ids, stable=True)
+    rank = torch.empty_like(ids)
+    rank[order] = torch.arange(tokens * topk) - (cum - cnt)[ids[order]]
+    return ids, cum, cnt, rank + 1
 
 
 def grouped_gemm_timing(dev, stream, iters, warm, flush, hbm, tflops, K, N, T=4096, G=128):

@@ -56,6 +56,7 @@ extern "C" {
 #define PTSIM_KIND_SORT 11         /* per row, a stable sort of the keys: sorted values and source indices */
 #define PTSIM_KIND_GATHER_ROWS 12  /* out[r, :] = table[t(r), :], t an integer program of an index loaded per row */
 #define PTSIM_KIND_GROUPED_GEMM 13 /* per listed group g: C[rows of g] = A[rows of g] . B[g] (the MoE expert matmul) */
+#define PTSIM_KIND_GATHER_SUM 14   /* out[r, :] = sum over k of w(r, k) * table[t(r, k), :] (the MoE combine) */
 
 /* Element types of tensor arguments (kernel.json dtype names, contract/kernel_object.py:43-56). */
 #define PTSIM_DT_F32 0
@@ -191,6 +192,7 @@ typedef struct ptsim_select_params {
 #define PTSIM_I_XOR 18
 #define PTSIM_I_SHR 19
 #define PTSIM_I_SHL 20
+#define PTSIM_I_LOADI 21   /* dst = argument c's element at position reg[a] (an index read through an index) */
 #define PTSIM_MAX_ICODE 32
 
 typedef struct ptsim_iinsn {
@@ -215,6 +217,19 @@ typedef struct ptsim_ggemm_params {
   int64_t M, N, K, groups, programs, ldb, ldg;
   int32_t a_arg, b_arg, c_arg, group_arg, start_arg, rows_arg;
 } ptsim_ggemm_params;
+
+/* GATHER_SUM: out [rows, cols]; term (r, k < terms) adds w(r, k) * table row t(r, k) (fp32, terms in order; a
+ * [table_rows, cols] table), the store cast to out's type.  The program runs per term over f = r * terms + k:
+ * LOAD dst = maps[a] applied to f (maps[a].arg names the tensor), LOADI dst = argument c at reg[a]; w is
+ * w_map applied to f.  A row or index outside its tensor records PTSIM_E_OOB and the term adds nothing. */
+#define PTSIM_GSUM_MAPS 4
+typedef struct ptsim_gsum_params {
+  int64_t rows, cols, terms, table_rows;
+  int32_t out_arg, table_arg, w_arg, ncode;
+  ptsim_map w_map;
+  ptsim_map maps[PTSIM_GSUM_MAPS];
+  ptsim_iinsn code[PTSIM_MAX_ICODE];
+} ptsim_gsum_params;
 
 typedef struct ptsim_reduce_params {
   int64_t numel;
@@ -244,6 +259,7 @@ typedef struct ptsim_desc {
     ptsim_select_params sel;
     ptsim_gather_params gat;
     ptsim_ggemm_params ggemm;
+    ptsim_gsum_params gsum;
   } p;
 } ptsim_desc;
 

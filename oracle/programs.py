@@ -263,6 +263,22 @@ def dispatch_gather(idx, table, tokens, hidden, topk):
     return table.view(tokens, hidden)[q].reshape(-1)
 
 
+def combine_weighted(idx, cum, cnt, pos, expert_out, w, tokens, hidden, topk, experts):
+    """layer_op_combine_*/03_*_triton.py: token t's k-th choice e = idx[t, k] (negative e wrapped by + experts)
+    sits in expert order at row p = cum[e] - cnt[e] + (pos[t, k] - 1) (negative p wrapped by + tokens * topk; the
+    kernel asserts both ranges); out[t, :] = bf16(sum over k of float(expert_out[p, :]) * float(w[t, k]))."""
+    e = idx.to(torch.int64).view(tokens, topk)
+    e = torch.where(e < 0, e + experts, e)
+    rows = tokens * topk
+    p = cum.to(torch.int64)[e] - cnt.to(torch.int64)[e] + (pos.to(torch.int64).view(tokens, topk) - 1)
+    p = torch.where(p < 0, p + rows, p)
+    if not bool(((e >= 0) & (e < experts)).all() and ((p >= 0) & (p < rows)).all()):
+        raise IndexError("combine index out of range (the reference asserts)")
+    g = f32(expert_out).view(rows, hidden)[p]                  # [tokens, topk, hidden]
+    acc = (g * f32(w).view(tokens, topk, 1)).sum(dim=1)
+    return acc.to(torch.bfloat16).reshape(-1)
+
+
 def grouped_gemm(a, b, group, start, rows, c_init, M, N, K, groups):
     """layer_op_gmm_*/05__grouped_mm_kernel/_grouped_mm_kernel_triton.py:4-44: program p takes group
     g = group[p] and its rows [start[g], start[g] + rows[g]); those rows of c become bf16(a_rows . b[g]) with

@@ -129,5 +129,6 @@ int launch_topk(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, 
 int launch_sort(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c);
 int launch_gather_rows(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c);
 int launch_grouped_gemm(const ptsim_desc &d, void *const *ptrs, const LaunchCtx &c);
+int launch_gather_sum(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c);
 
 }  // namespace ptsim

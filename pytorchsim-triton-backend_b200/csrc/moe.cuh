@@ -387,6 +387,207 @@ int launch_gather_rows(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64
   return PTSIM_OK;
 }
 
+// ---------------------------------------------------------------------------------------------------
+// Gather-sum: the MoE combine (validation/pytorchsim/layer_op_combine_*/03_*: out[t, d] = sum over the top-k
+// terms k of w[t, k] * expert_out[p(t, k), d], p the row where token t's k-th expert wrote it, read through
+// the expert id, that expert's running offsets and the slot).  The index programs of 32 (row, term) pairs
+// run at once (lane l: row r0 + l / terms, term l % terms); each row is then accumulated over its terms in
+// order, 8 columns per thread per step with 16-byte loads.
+// ---------------------------------------------------------------------------------------------------
+struct GsumArgs {
+  const void *arg[PTSIM_MAX_ARGS];
+  int64_t numel[PTSIM_MAX_ARGS];
+  int32_t dt[PTSIM_MAX_ARGS];
+  void *out;
+  const void *table;
+  int64_t row_begin, row_end, cols, terms, table_rows;
+  int32_t out_dt, table_dt, w_arg, ncode;
+  ptsim_map w_map;
+  ptsim_map maps[PTSIM_GSUM_MAPS];
+  ptsim_iinsn code[PTSIM_MAX_ICODE];
+};
+
+__device__ __forceinline__ int64_t map_at(const ptsim_map &m, int64_t f) {
+  int64_t at = m.offset;
+  for (int d = 0; d < m.ndigit; ++d) {
+    int64_t q = f / m.div[d];
+    if (m.mod[d] > 0) q %= m.mod[d];
+    at += q * m.stride[d];
+  }
+  return at;
+}
+
+// Element `at` of argument `a` as int64 (integer arguments) -- false when `at` is outside it.
+__device__ __forceinline__ bool load_int(const GsumArgs &g, int a, int64_t at, int64_t &v) {
+  if (a < 0 || a >= PTSIM_MAX_ARGS || at < 0 || at >= g.numel[a]) return false;
+  switch (g.dt[a]) {
+    case PTSIM_DT_I64: v = reinterpret_cast<const int64_t *>(g.arg[a])[at]; return true;
+    case PTSIM_DT_I32: v = reinterpret_cast<const int32_t *>(g.arg[a])[at]; return true;
+    case PTSIM_DT_I16: v = reinterpret_cast<const int16_t *>(g.arg[a])[at]; return true;
+    case PTSIM_DT_I8: v = reinterpret_cast<const int8_t *>(g.arg[a])[at]; return true;
+    case PTSIM_DT_U8: v = reinterpret_cast<const uint8_t *>(g.arg[a])[at]; return true;
+  }
+  return false;
+}
+
+// The table row of term f = r * terms + k, or -1 when an index read fell outside its tensor.
+__device__ int64_t gsum_row_of(const GsumArgs &g, int64_t f) {
+  int64_t reg[PTSIM_MAX_ICODE];
+  int64_t res = 0;
+  for (int i = 0; i < g.ncode; ++i) {
+    const ptsim_iinsn &in = g.code[i];
+    const int64_t a = reg[in.a & 31], b = reg[in.b & 31];
+    int64_t v = 0;
+    switch (in.op) {
+      case PTSIM_I_LOAD:
+        if (in.a >= PTSIM_GSUM_MAPS || !load_int(g, g.maps[in.a].arg, map_at(g.maps[in.a], f), v)) return -1;
+        break;
+      case PTSIM_I_LOADI:
+        if (!load_int(g, in.c, a, v)) return -1;
+        break;
+      case PTSIM_I_CONST: v = in.imm; break;
+      case PTSIM_I_ADD: v = int64_t(uint64_t(a) + uint64_t(b)); break;
+      case PTSIM_I_SUB: v = int64_t(uint64_t(a) - uint64_t(b)); break;
+      case PTSIM_I_MUL: v = int64_t(uint64_t(a) * uint64_t(b)); break;
+      case PTSIM_I_DIV: v = b == 0 ? 0 : (a == LLONG_MIN && b == -1 ? a : a / b); break;
+      case PTSIM_I_MOD: v = b == 0 ? 0 : (a == LLONG_MIN && b == -1 ? 0 : a % b); break;
+      case PTSIM_I_INV: v = ~a; break;
+      case PTSIM_I_LT: v = a < b; break;
+      case PTSIM_I_LE: v = a <= b; break;
+      case PTSIM_I_GT: v = a > b; break;
+      case PTSIM_I_GE: v = a >= b; break;
+      case PTSIM_I_EQ: v = a == b; break;
+      case PTSIM_I_NE: v = a != b; break;
+      case PTSIM_I_WHERE: v = reg[in.c & 31] ? a : b; break;
+      case PTSIM_I_AND: v = a & b; break;
+      case PTSIM_I_OR: v = a | b; break;
+      case PTSIM_I_XOR: v = a ^ b; break;
+      case PTSIM_I_SHR: v = a >> (b & 63); break;
+      case PTSIM_I_SHL: v = int64_t(uint64_t(a) << (b & 63)); break;
+    }
+    reg[in.dst & 31] = v;
+    res = v;
+  }
+  return res;
+}
+
+// A CTA takes 32 / terms output rows: warp 0 evaluates their (row, term) index programs into shared memory,
+// then all 256 threads split the columns, each loading its 8-column slice of every term's row (all TERMS
+// loads in flight when the term count is a template constant) before accumulating in term order.
+template <int TERMS>
+__device__ __forceinline__ void gsum_slice(const GsumArgs &g, const int64_t *rows, const float *ws, int nterms,
+                                           int64_t orow, int64_t c8) {
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  const bool vec = g.table_dt == PTSIM_DT_BF16 && c8 + 8 <= g.cols && (g.cols % 8) == 0;
+  if (TERMS > 0 && vec) {
+    uint4 v[TERMS > 0 ? TERMS : 1];
+#pragma unroll
+    for (int k = 0; k < TERMS; ++k)
+      v[k] = rows[k] >= 0 ? __ldg(reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(g.table) + rows[k] * g.cols + c8))
+                          : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int k = 0; k < TERMS; ++k) {
+      if (rows[k] < 0) continue;
+      const uint32_t wsv[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        acc[2 * e] = fmaf(lo_bf16(wsv[e]), ws[k], acc[2 * e]);
+        acc[2 * e + 1] = fmaf(hi_bf16(wsv[e]), ws[k], acc[2 * e + 1]);
+      }
+    }
+  } else {
+    for (int k = 0; k < nterms; ++k) {
+      const int64_t t = rows[k];
+      if (t < 0) continue;
+      for (int e = 0; e < 8 && c8 + e < g.cols; ++e) acc[e] = fmaf(ld_any(g.table, g.table_dt, t * g.cols + c8 + e), ws[k], acc[e]);
+    }
+  }
+  if (g.out_dt == PTSIM_DT_BF16 && c8 + 8 <= g.cols && (g.cols % 8) == 0) {
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    __stcs(reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(g.out) + orow * g.cols + c8), o);
+  } else {
+    for (int e = 0; e < 8 && c8 + e < g.cols; ++e) st_any(g.out, g.out_dt, orow * g.cols + c8 + e, acc[e]);
+  }
+}
+
+template <int TERMS>
+__global__ void __launch_bounds__(256) gather_sum_kernel(const __grid_constant__ GsumArgs g) {
+  __shared__ int64_t s_row[32];
+  __shared__ float s_w[32];
+  const int nterms = TERMS > 0 ? TERMS : int(g.terms);
+  const int per = 32 / nterms;
+  for (int64_t r0 = g.row_begin + int64_t(blockIdx.x) * per; r0 < g.row_end; r0 += int64_t(gridDim.x) * per) {
+    __syncthreads();   // the previous group's pairs are read
+    if (threadIdx.x < 32) {
+      const int lane = threadIdx.x;
+      int64_t trow = -1;
+      float w = 0.f;
+      const int64_t r = r0 + lane / nterms;
+      if (lane < per * nterms && r < g.row_end) {
+        const int64_t f = r * g.terms + lane % nterms;
+        trow = gsum_row_of(g, f);
+        const int64_t wat = map_at(g.w_map, f);
+        if (trow < 0 || trow >= g.table_rows || wat < 0 || wat >= g.numel[g.w_arg]) {
+          record_status(PTSIM_E_OOB);
+          trow = -1;
+        } else {
+          w = ld_any(g.arg[g.w_arg], g.dt[g.w_arg], wat);
+        }
+      }
+      s_row[lane] = trow;
+      s_w[lane] = w;
+    }
+    __syncthreads();
+    for (int j = 0; j < per && r0 + j < g.row_end; ++j)
+      for (int64_t c8 = int64_t(threadIdx.x) * 8; c8 < g.cols; c8 += int64_t(blockDim.x) * 8)
+        gsum_slice<TERMS>(g, s_row + j * nterms, s_w + j * nterms, nterms, r0 + j, c8);
+  }
+}
+
+int launch_gather_sum(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c) {
+  const ptsim_gsum_params &p = d.p.gsum;
+  GsumArgs g;
+  memset(&g, 0, sizeof(g));
+  for (int a = 0; a < d.nargs; ++a) {
+    g.arg[a] = ptrs[a];
+    g.numel[a] = d.arg_numel[a];
+    g.dt[a] = d.arg_dtype[a];
+  }
+  if (p.terms < 1 || p.terms > 32) return fail(PTSIM_E_UNSUPPORTED, "gather-sum over %lld terms (runs 1-32)", (long long)p.terms);
+  const bool floaty = [](int dt) { return dt == PTSIM_DT_F32 || dt == PTSIM_DT_BF16 || dt == PTSIM_DT_F16; }(d.arg_dtype[p.table_arg]);
+  if (!floaty || (d.arg_dtype[p.out_arg] != PTSIM_DT_F32 && d.arg_dtype[p.out_arg] != PTSIM_DT_BF16 &&
+                  d.arg_dtype[p.out_arg] != PTSIM_DT_F16))
+    return fail(PTSIM_E_UNSUPPORTED, "gather-sum runs float tables and outputs");
+  g.out = ptrs[p.out_arg];
+  g.table = ptrs[p.table_arg];
+  g.row_begin = lo * d.unit_size;
+  g.row_end = hi * d.unit_size < p.rows ? hi * d.unit_size : p.rows;
+  g.cols = p.cols;
+  g.terms = p.terms;
+  g.table_rows = p.table_rows;
+  g.out_dt = d.arg_dtype[p.out_arg];
+  g.table_dt = d.arg_dtype[p.table_arg];
+  g.w_arg = p.w_arg;
+  g.ncode = p.ncode;
+  g.w_map = p.w_map;
+  memcpy(g.maps, p.maps, sizeof(g.maps));
+  memcpy(g.code, p.code, sizeof(g.code));
+  if ((reinterpret_cast<uintptr_t>(g.table) | reinterpret_cast<uintptr_t>(g.out)) % 16 != 0)
+    return fail(PTSIM_E_ARGS, "gather-sum table and output must be 16-byte aligned");
+  if (g.row_end <= g.row_begin) return PTSIM_OK;
+  const int per = 32 / int(p.terms);
+  int64_t blocks = ceil_div(g.row_end - g.row_begin, per);
+  if (blocks > int64_t(c.sm_count) * 16) blocks = int64_t(c.sm_count) * 16;
+  if (p.terms == 8) gather_sum_kernel<8><<<unsigned(blocks), 256, 0, c.stream>>>(g);
+  else gather_sum_kernel<0><<<unsigned(blocks), 256, 0, c.stream>>>(g);
+  PTSIM_CUDA(cudaGetLastError());
+  return PTSIM_OK;
+}
+
 int launch_topk(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c) {
   const ptsim_select_params &p = d.p.sel;
   const int xdt = d.arg_dtype[p.in_arg], vdt = d.arg_dtype[p.val_arg];

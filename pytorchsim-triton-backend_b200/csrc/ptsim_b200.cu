@@ -229,6 +229,27 @@ static int check_desc(const void *p, size_t bytes) {
         return fail(PTSIM_E_OOB, "grouped GEMM operands extend past their tensors");
       break;
     }
+    case PTSIM_KIND_GATHER_SUM: {
+      const ptsim_gsum_params &q = d.p.gsum;
+      if ((rc = check_arg(d, q.out_arg, "gather-sum output")) || (rc = check_arg(d, q.table_arg, "gather-sum table")) ||
+          (rc = check_arg(d, q.w_arg, "gather-sum weights")) || (rc = check_arg(d, q.w_map.arg, "gather-sum weight map")))
+        return rc;
+      if (q.rows < 0 || q.cols < 1 || q.terms < 1 || q.table_rows < 0 || q.ncode < 1 || q.ncode > PTSIM_MAX_ICODE)
+        return fail(PTSIM_E_DESC, "gather-sum of %lld x %lld over %lld terms", (long long)q.rows, (long long)q.cols, (long long)q.terms);
+      if (q.rows * q.cols > d.arg_numel[q.out_arg] || q.table_rows * q.cols > d.arg_numel[q.table_arg])
+        return fail(PTSIM_E_OOB, "gather-sum rows extend past their tensors");
+      const ptsim_map *ms[PTSIM_GSUM_MAPS + 1] = {&q.w_map, &q.maps[0], &q.maps[1], &q.maps[2], &q.maps[3]};
+      for (const ptsim_map *m : ms) {
+        if (m->ndigit < 0 || m->ndigit > PTSIM_MAX_DIGITS || m->offset < 0) return fail(PTSIM_E_DESC, "gather-sum map");
+        for (int k = 0; k < m->ndigit; ++k)
+          if (m->div[k] < 1 || m->mod[k] < 1 || m->stride[k] < 0) return fail(PTSIM_E_DESC, "gather-sum map digit %d", k);
+      }
+      for (int i = 0; i < q.ncode; ++i)
+        if (q.code[i].op < PTSIM_I_LOAD || q.code[i].op > PTSIM_I_LOADI || q.code[i].dst >= PTSIM_MAX_ICODE ||
+            q.code[i].a >= PTSIM_MAX_ICODE || q.code[i].b >= PTSIM_MAX_ICODE || q.code[i].c >= PTSIM_MAX_ICODE)
+          return fail(PTSIM_E_DESC, "gather-sum instruction %d", i);
+      break;
+    }
     case PTSIM_KIND_REDUCE_ALL: {
       const ptsim_reduce_params &r = d.p.red;
       if ((rc = check_arg(d, r.in_arg, "reduce input")) || (rc = check_arg(d, r.out_arg, "reduce output"))) return rc;
@@ -299,6 +320,7 @@ int ptsim_launch(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int
     case PTSIM_KIND_SORT: return launch_sort(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_GATHER_ROWS: return launch_gather_rows(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_GROUPED_GEMM: return launch_grouped_gemm(d, dev_ptrs, c);
+    case PTSIM_KIND_GATHER_SUM: return launch_gather_sum(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_QKNORM_ROPE: return launch_qkrope(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_GEMM: return launch_gemm(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_ATTN_PREFILL: return launch_attention(d, dev_ptrs, lo, hi, c);

@@ -174,6 +174,37 @@ def grouped_gemm(M, N, K, groups, programs):
     return d
 
 
+def combine_gather_sum(tokens, hidden, topk, experts):
+    """The MoE combine's weighted gather (layer_op_combine_*/03_*): out[t, :] = sum over k of w[t, k] *
+    expert_out[p(t, k), :], p = cum[e] - cnt[e] + pos[t, k] - 1 with e = idx[t, k] (both wrapped when
+    negative); arguments idx, cum, cnt, pos (int64), expert_out, w (bf16), out (bf16)."""
+    rows = tokens * topk
+    d = D.new(D.GATHER_SUM, _args([("in_ptr0", "int64", rows), ("in_ptr1", "int64", experts), ("in_ptr2", "int64", experts),
+                                   ("in_ptr3", "int64", rows), ("in_ptr4", "bfloat16", rows * hidden),
+                                   ("in_ptr5", "bfloat16", rows), ("out_ptr1", "bfloat16", tokens * hidden)]),
+              (1, 1, 1), units=tokens, unit_size=1)
+    g = d.p.gsum
+    g.rows, g.cols, g.terms, g.table_rows = tokens, hidden, topk, rows
+    g.out_arg, g.table_arg, g.w_arg = 6, 4, 5
+
+    def flat(m, arg):
+        m.arg, m.ndigit, m.offset = arg, 1, 0
+        m.div[0], m.mod[0], m.stride[0] = 1, 1 << 62, 1
+    flat(g.w_map, 5)
+    flat(g.maps[0], 0)
+    flat(g.maps[1], 3)
+    prog = [("load", 0, 0, 0, 0), ("const", 0, 0, 0, 0), ("lt", 0, 1, 0, 0), ("const", 0, 0, 0, experts),
+            ("add", 0, 3, 0, 0), ("where", 4, 0, 2, 0), ("loadi", 5, 0, 1, 0), ("loadi", 5, 0, 2, 0),
+            ("sub", 6, 7, 0, 0), ("load", 1, 0, 0, 0), ("const", 0, 0, 0, 1), ("sub", 9, 10, 0, 0),
+            ("add", 8, 11, 0, 0), ("lt", 12, 1, 0, 0), ("const", 0, 0, 0, rows), ("add", 12, 14, 0, 0),
+            ("where", 15, 12, 13, 0)]
+    for k, (op, a, b, c, imm) in enumerate(prog):
+        ins = g.code[k]
+        ins.op, ins.dst, ins.a, ins.b, ins.c, ins.imm = D.IOP[op], k, a, b, c, imm
+    g.ncode = len(prog)
+    return d
+
+
 def reduce_all(numel, op="sum", dtype="bfloat16"):
     d = D.new(D.REDUCE_ALL, _args([("in_ptr0", dtype, numel), ("out_ptr0", "float32", 1)]), [1], units=1, unit_size=1,
               workspace_bytes=D.REDUCE_WORKSPACE_BYTES)

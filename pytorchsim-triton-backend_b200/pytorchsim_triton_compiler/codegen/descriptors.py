@@ -12,11 +12,11 @@ MAX_ARGS, MAX_MAPS, MAX_DIGITS, MAX_CODE, MAX_REGS = 16, 8, 4, 32, 8
 
 # Kinds (PTSIM_KIND_*).
 ELEMENTWISE, ROW_SOFTMAX, ROW_RMSNORM, QKNORM_ROPE, GEMM, ATTN_PREFILL, REDUCE_ALL, ATTN_DECODE = 1, 2, 3, 4, 5, 6, 7, 8
-ROW_DIVSUM, TOPK, SORT, GATHER_ROWS, GROUPED_GEMM = 9, 10, 11, 12, 13
+ROW_DIVSUM, TOPK, SORT, GATHER_ROWS, GROUPED_GEMM, GATHER_SUM = 9, 10, 11, 12, 13, 14
 KIND_NAME = {ELEMENTWISE: "elementwise", ROW_SOFTMAX: "row_softmax", ROW_RMSNORM: "row_rmsnorm",
              QKNORM_ROPE: "qknorm_rope", GEMM: "gemm", ATTN_PREFILL: "attn_prefill", REDUCE_ALL: "reduce_all",
              ATTN_DECODE: "attn_decode", ROW_DIVSUM: "row_divsum", TOPK: "topk", SORT: "sort",
-             GATHER_ROWS: "gather_rows", GROUPED_GEMM: "grouped_gemm"}
+             GATHER_ROWS: "gather_rows", GROUPED_GEMM: "grouped_gemm", GATHER_SUM: "gather_sum"}
 
 # Element types (PTSIM_DT_*), keyed by kernel.json dtype names (contract/kernel_object.py NP_DTYPE keys).
 DTYPE_CODE = {"float32": 0, "bfloat16": 1, "float16": 2, "int32": 3, "int64": 4, "int16": 5, "int8": 6,
@@ -89,7 +89,8 @@ class SelectParams(C.Structure):
 
 MAX_ICODE = 32
 IOP = {"load": 1, "const": 2, "add": 3, "sub": 4, "mul": 5, "div": 6, "mod": 7, "inv": 8, "lt": 9, "le": 10,
-       "gt": 11, "ge": 12, "eq": 13, "ne": 14, "where": 15, "and": 16, "or": 17, "xor": 18, "shr": 19, "shl": 20}
+       "gt": 11, "ge": 12, "eq": 13, "ne": 14, "where": 15, "and": 16, "or": 17, "xor": 18, "shr": 19, "shl": 20,
+       "loadi": 21}
 IOP_NAME = {v: k for k, v in IOP.items()}
 
 
@@ -110,10 +111,19 @@ class GGemmParams(C.Structure):
                 ("group_arg", C.c_int32), ("start_arg", C.c_int32), ("rows_arg", C.c_int32)]
 
 
+GSUM_MAPS = 4
+
+
+class GsumParams(C.Structure):
+    _fields_ = [("rows", C.c_int64), ("cols", C.c_int64), ("terms", C.c_int64), ("table_rows", C.c_int64),
+                ("out_arg", C.c_int32), ("table_arg", C.c_int32), ("w_arg", C.c_int32), ("ncode", C.c_int32),
+                ("w_map", Map), ("maps", Map * GSUM_MAPS), ("code", IInsn * MAX_ICODE)]
+
+
 class Params(C.Union):
     _fields_ = [("ew", EwParams), ("row", RowParams), ("qk", QkParams), ("gemm", GemmParams),
                 ("attn", AttnParams), ("red", ReduceParams), ("sel", SelectParams), ("gat", GatherParams),
-                ("ggemm", GGemmParams)]
+                ("ggemm", GGemmParams), ("gsum", GsumParams)]
 
 
 class Desc(C.Structure):
@@ -207,6 +217,10 @@ def describe(d):
     elif d.kind == GROUPED_GEMM:
         q = d.p.ggemm
         out.update(M=q.M, N=q.N, K=q.K, groups=q.groups, programs=q.programs)
+    elif d.kind == GATHER_SUM:
+        q = d.p.gsum
+        out.update(rows=q.rows, cols=q.cols, terms=q.terms, table_rows=q.table_rows,
+                   program=[(IOP_NAME.get(i.op, i.op), i.dst, i.a, i.b, i.c, i.imm) for i in list(q.code)[:q.ncode]])
     elif d.kind == REDUCE_ALL:
         out.update(numel=d.p.red.numel, op="max" if d.p.red.op == RED_MAX else "sum")
     return out

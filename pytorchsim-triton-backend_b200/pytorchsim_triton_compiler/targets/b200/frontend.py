@@ -521,6 +521,8 @@ class Evaluator:
             for p, q in ((a, b), (b, a)):
                 if isinstance(p, Ptr) and isinstance(q, DataIndex) and p.data is None:
                     return Ptr(p.arg, p.index + q.index, q.data)
+                if isinstance(p, Ptr) and isinstance(q, Node) and not isinstance(q, Const) and p.data is None:
+                    return Ptr(p.arg, p.index, q)   # a pointer offset by a loaded value (an index load)
                 if isinstance(p, (Index, Arange, Pid, LoopVar)) and isinstance(q, Node) and not isinstance(q, Const):
                     return DataIndex(self.index_of(p), q)
                 if isinstance(p, DataIndex) and _is_index(q):

@@ -141,6 +141,11 @@ def lower(spec, fn=None):
     st = prog.stores[0]
     if isinstance(strip_casts(st.value), F.Load) and strip_casts(st.value).data is not None:
         return _lower_gather(spec, prog, st)
+    sv = strip_casts(st.value)
+    if isinstance(sv, F.Reduce) and sv.op == "add" and isinstance(strip_casts(sv.value), F.Op) \
+            and strip_casts(sv.value).name == "mul" and any(isinstance(strip_casts(a), F.Load) and strip_casts(a).data is not None
+                                                            for a in strip_casts(sv.value).args):
+        return _lower_gather_sum(spec, prog, st, sv)
     reduces = [n for n in walk(st.value) if isinstance(n, F.Reduce)]
     if not reduces:
         return _lower_elementwise(spec, prog, st)
@@ -818,4 +823,146 @@ def _lower_grouped_gemm(spec):
     q.M, q.N, q.K, q.groups, q.programs, q.ldb, q.ldg = M, N, K, groups, programs, sbk, sbg
     q.a_arg, q.b_arg, q.c_arg = idx["a_ptr"], idx["b_ptr"], idx["c_ptr"]
     q.group_arg, q.start_arg, q.rows_arg = idx["group_ptr"], idx["start_ptr"], idx["rows_ptr"]
+    return Lowered(d, D.describe(d))
+
+
+def _term_map(spec, idx, C, terms, arg):
+    """The descriptor map over the term index f = row * terms + k of an index affine in x // C (rows of C
+    output columns) and r (the term k)."""
+    m = D.Map()
+    m.arg, m.offset = arg, idx.const
+    digits = []
+    for d, c in sorted(idx.terms.items(), key=lambda kv: (kv[0].var, kv[0].div)):
+        if d.var == "x" and d.div % C == 0:
+            digits.append(((d.div // C) * terms, _NO_MOD if d.mod is None else int(d.mod), int(c)))
+        elif d.var == "r" and terms % d.div == 0:
+            span = terms // d.div
+            digits.append((d.div, span if d.mod is None else min(span, int(d.mod)), int(c)))
+        else:
+            raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: index {idx} is not a function of (x // {C}, r)")
+    if len(digits) > D.MAX_DIGITS:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: index {idx} has too many digits")
+    m.ndigit = len(digits)
+    for i, (dv, md, sd) in enumerate(digits):
+        m.div[i], m.mod[i], m.stride[i] = dv, md, sd
+    return m
+
+
+def _term_program(spec, tree, C, terms):
+    """(instructions, maps) of an int64 index program over the term (row, k): direct loads through up to
+    PTSIM_GSUM_MAPS maps over f = row * terms + k, loads through a loaded position as LOADI."""
+    code, memo, maps = [], {}, []
+
+    def emit(op, a=0, b=0, c=0, imm=0):
+        if len(code) >= D.MAX_ICODE:
+            raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: an index program over {D.MAX_ICODE} instructions")
+        ins = D.IInsn()
+        ins.op, ins.dst, ins.a, ins.b, ins.c, ins.imm = D.IOP[op], len(code), a, b, c, int(imm)
+        code.append(ins)
+        return ins.dst
+
+    def gen(n):
+        if isinstance(n, F.Cond):
+            if n.op != "data" or not isinstance(n.value, F.Node):
+                raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: an index condition on the program index")
+            n = n.value
+        k = key(n)
+        if k in memo:
+            return memo[k]
+        if isinstance(n, F.Const):
+            if n.v != int(n.v):
+                raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a fractional constant {n.v} in an index")
+            r = emit("const", imm=int(n.v))
+        elif isinstance(n, F.Load) and n.data is None:
+            mk = (n.arg, key(n))
+            slot = next((i for i, (kk, _) in enumerate(maps) if kk == mk), None)
+            if slot is None:
+                if len(maps) >= D.GSUM_MAPS:
+                    raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: more than {D.GSUM_MAPS} index reads")
+                maps.append((mk, _term_map(spec, n.index, C, terms, n.arg)))
+                slot = len(maps) - 1
+            r = emit("load", slot)
+        elif isinstance(n, F.Load):
+            if n.index.terms:
+                raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: an index read at {n.index} + data")
+            pos = gen(n.data)
+            if n.index.const:
+                pos = emit("add", pos, gen(F.Const(n.index.const)))
+            r = emit("loadi", pos, 0, n.arg)
+        elif isinstance(n, F.Op):
+            if n.name in _IBIN:
+                a, b = gen(n.args[0]), gen(n.args[1])
+                r = emit(_IBIN[n.name], a, b)
+            elif n.name in _CMP:
+                a, b = gen(n.args[0]), gen(n.args[1])
+                r = emit(_CMP[n.name], a, b)
+            elif n.name == "invert":
+                r = emit("inv", gen(n.args[0]))
+            elif n.name == "neg":
+                r = emit("sub", gen(F.Const(0)), gen(n.args[0]))
+            elif n.name == "where":
+                cnd = gen(n.args[0])
+                a, b = gen(n.args[1]), gen(n.args[2])
+                r = emit("where", a, b, cnd)
+            elif n.name in ("rbf16", "rf16"):
+                r = gen(n.args[0])
+            else:
+                raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: {n.name} in an index program")
+        else:
+            raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: {type(n).__name__} in an index program")
+        memo[k] = r
+        return r
+
+    res = gen(tree)
+    if code[-1].dst != res:
+        emit("add", res, gen(F.Const(0)))
+    return code, [m for _, m in maps]
+
+
+def _lower_gather_sum(spec, prog, st, red):
+    """A weighted sum of gathered rows, e.g. the MoE combine (validation/pytorchsim/layer_op_combine_128x0_bf16/
+    03_*_triton.py: out[x] = sum over r of float(in4[x % 2048 + 2048 * p]) * float(in5[r + 8 * (x // 2048)]), p
+    the expert-ordered row of token x // 2048's r-th choice, read through in0 (expert id), in1 / in2 (that
+    expert's running offsets) and in3 (the slot))."""
+    if st.mask is not None:
+        raise Refused(Reason.MASKED_STORE_NOT_A_BOX, f"{spec.name}: a masked weighted gather")
+    if st.index.const != 0 or st.index.terms != {F.Digit("x"): 1}:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: weighted gather store index {st.index} is not x")
+    prod = strip_casts(red.value)
+    a0, a1 = (strip_casts(a) for a in prod.args)
+    tab, w = (a0, a1) if isinstance(a0, F.Load) and a0.data is not None else (a1, a0)
+    if not (isinstance(w, F.Load) and w.data is None) or tab.mask is not None or w.mask is not None:
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: not a gathered row times a weight")
+    aff = tab.index
+    if aff.const != 0 or len(aff.terms) != 1:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: gathered load index {aff} is not x % C + data")
+    (dg, coef), = aff.terms.items()
+    if dg.var != "x" or dg.div != 1 or coef != 1:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: gathered load index {aff} is not x % C + data")
+    # x % C over rows of C columns; a one-row program indexes by x alone (C = xnumel)
+    C = int(dg.mod) if dg.mod is not None else int(_lookup(spec, prog, "xnumel") or spec.args[st.arg].numel)
+    t = None
+    if isinstance(tab.data, F.Op) and tab.data.name == "mul":
+        for p, q in ((tab.data.args[0], tab.data.args[1]), (tab.data.args[1], tab.data.args[0])):
+            if isinstance(p, F.Const) and int(p.v) == C:
+                t = q
+    if t is None:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: the gathered offset is not {C} * row")
+    terms = _lookup(spec, prog, "r0_numel", "rnumel")
+    rblock = prog.block.get("r") or _lookup(spec, prog, "R0_BLOCK")
+    if terms is None or (rblock is not None and int(rblock) != int(terms)):
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: a weighted gather over a looped reduction")
+    terms = int(terms)
+    code, maps = _term_program(spec, t, C, terms)
+    out, table = spec.args[st.arg], spec.args[tab.arg]
+    numel = _lookup(spec, prog, "xnumel") or out.numel
+    d = D.new(D.GATHER_SUM, _manifest_args(spec), spec.grid, units=int(numel) // C, unit_size=1)
+    g = d.p.gsum
+    g.rows, g.cols, g.terms, g.table_rows = int(numel) // C, C, terms, table.numel // C
+    g.out_arg, g.table_arg, g.w_arg, g.ncode = st.arg, tab.arg, w.arg, len(code)
+    g.w_map = _term_map(spec, w.index, C, terms, w.arg)
+    for i, m in enumerate(maps):
+        g.maps[i] = m
+    for i, ins in enumerate(code):
+        g.code[i] = ins
     return Lowered(d, D.describe(d))

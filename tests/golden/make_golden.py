@@ -151,6 +151,8 @@ def cases():
              {"family": "sort", "rows": 1, "cols": 8 * T, "descending": False, "float_keys": False}, gold),
             (f"moe_dispatch_t{T}_01_gather", spec_file(dp, 1),
              {"family": "dispatch_gather", "tokens": T, "hidden": 2048, "topk": 8}, gold),
+            (f"moe_combine_t{T}_03_weighted", spec_file(f"layer_op_combine_{T}x0_bf16", 3),
+             {"family": "combine_weighted", "tokens": T, "hidden": 2048, "topk": 8, "experts": 128}, gold),
         ]
     # The MoE expert matmul: the reference kernel at an interpreter-sized configuration (golden), and the
     # bundle's T = 1 and 128 objects (gate_up K 2048 -> N 1536, down K 768 -> N 2048; 128 experts; the group

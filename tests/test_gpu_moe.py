@@ -181,3 +181,44 @@ def test_grouped_gemm_after_split_k_gemm():
                              torch.zeros(128 * 4096, dtype=torch.bfloat16))]
     RC.launch_tensors(D.to_bytes(gemm), ts)
     test_grouped_gemm(64, 2048, 1536)
+
+
+def moe_routing(tokens, topk, experts, seed):
+    """A consistent routing: each (token, k) slot's expert id, the experts' counts and inclusive cumulative
+    counts, and each slot's 1-based rank among the slots of its expert (so cum - cnt + pos - 1 is the slot's row
+    in expert order)."""
+    g = torch.Generator().manual_seed(seed)
+    ids = torch.randint(0, experts, (tokens * topk,), generator=g)
+    cnt = torch.bincount(ids, minlength=experts)
+    cum = torch.cumsum(cnt, 0)
+    order = torch.argsort(ids, stable=True)
+    rank = torch.empty_like(ids)
+    rank[order] = torch.arange(tokens * topk) - (cum - cnt)[ids[order]]
+    return ids, cum, cnt, rank + 1
+
+
+@pytest.mark.parametrize("tokens,hidden,topk,experts", [(4096, 2048, 8, 128), (128, 2048, 8, 128), (3, 64, 2, 4),
+                                                        (100, 200, 4, 16)])
+def test_combine_weighted(tokens, hidden, topk, experts):
+    ids, cum, cnt, pos = moe_routing(tokens, topk, experts, tokens)
+    ids[::5] -= experts                      # negative ids: wrapped by + experts
+    g = torch.Generator().manual_seed(1)
+    expert_out = torch.randn(tokens * topk * hidden, generator=g).to(torch.bfloat16)
+    w = torch.rand(tokens * topk, generator=g).to(torch.bfloat16)
+    ins = [ids, cum, cnt, pos, expert_out, w, torch.zeros(tokens * hidden, dtype=torch.bfloat16)]
+    out = run(B.combine_gather_sum(tokens, hidden, topk, experts), ins)[6]
+    want = O.combine_weighted(ids, cum, cnt, pos, expert_out, w, tokens, hidden, topk, experts)
+    ok, rep = compare(out, want, 1e-2, 1e-2)
+    assert ok, rep
+
+
+def test_combine_out_of_range_is_recorded():
+    tokens, hidden, topk, experts = 8, 64, 2, 4
+    ids, cum, cnt, pos = moe_routing(tokens, topk, experts, 3)
+    pos[5] += 1000                           # a slot past the expert-ordered rows
+    ts = [ids, cum, cnt, pos, torch.randn(tokens * topk * hidden).to(torch.bfloat16),
+          torch.rand(tokens * topk).to(torch.bfloat16), torch.zeros(tokens * hidden, dtype=torch.bfloat16)]
+    ts = [t.cuda() for t in ts]
+    with pytest.raises(native.ExecutorError) as e:
+        RC.launch_tensors(D.to_bytes(B.combine_gather_sum(tokens, hidden, topk, experts)), ts)
+    assert e.value.code == D.E_OOB

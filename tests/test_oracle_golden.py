@@ -68,6 +68,9 @@ def run_oracle(case, ins):
         return outs[0], O.reduce_all(x[0], o["op"])
     if fam == "softmax_rows":
         return outs[0], O.softmax_rows(x[0], o["rows"], o["cols"], getattr(torch, o.get("out_dtype", "bfloat16")))
+    if fam == "combine_weighted":
+        return outs[0], O.combine_weighted(x[0], x[1], x[2], x[3], x[4], x[5], o["tokens"], o["hidden"], o["topk"],
+                                           o["experts"])
     if fam == "grouped_gemm":
         return outs[0], O.grouped_gemm(x[0], x[1], x[2], x[3], x[4], x[5], o["M"], o["N"], o["K"], o["groups"])
     if fam == "row_divsum":
