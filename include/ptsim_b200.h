@@ -57,6 +57,7 @@ extern "C" {
 #define PTSIM_KIND_GATHER_ROWS 12  /* out[r, :] = table[t(r), :], t an integer program of an index loaded per row */
 #define PTSIM_KIND_GROUPED_GEMM 13 /* per listed group g: C[rows of g] = A[rows of g] . B[g] (the MoE expert matmul) */
 #define PTSIM_KIND_GATHER_SUM 14   /* out[r, :] = sum over k of w(r, k) * table[t(r, k), :] (the MoE combine) */
+#define PTSIM_KIND_INT_TABLE 15    /* an int64 program over [rows, cols] stored per element, summed or scanned along a row */
 
 /* Element types of tensor arguments (kernel.json dtype names, contract/kernel_object.py:43-56). */
 #define PTSIM_DT_F32 0
@@ -193,6 +194,8 @@ typedef struct ptsim_select_params {
 #define PTSIM_I_SHR 19
 #define PTSIM_I_SHL 20
 #define PTSIM_I_LOADI 21   /* dst = argument c's element at position reg[a] (an index read through an index) */
+#define PTSIM_I_LOADM 22   /* INT_TABLE: dst = reg[b] ? argument c at maps[a] applied to f : imm (a masked load) */
+#define PTSIM_I_IDX 23     /* INT_TABLE: dst = maps[a] applied to f (an index as a value) */
 #define PTSIM_MAX_ICODE 32
 
 typedef struct ptsim_iinsn {
@@ -231,6 +234,31 @@ typedef struct ptsim_gsum_params {
   ptsim_iinsn code[PTSIM_MAX_ICODE];
 } ptsim_gsum_params;
 
+/* INT_TABLE: an int64 program run for every element f = x * cols + r of a [rows, cols] space (registers
+ * r0..r31).  LOAD dst = argument c at maps[a] applied to f, LOADM the same when reg[b] is non-zero and imm
+ * otherwise, IDX dst = maps[a] applied to f, LOADI dst = argument c at reg[a]; a position outside its tensor
+ * records PTSIM_E_OOB and reads 0.  Output k stores register out[k].reg to argument out[k].arg, cast to its
+ * integer type, at maps[out[k].map] applied to
+ *   ELEM: f, for every element;
+ *   SUM:  x * cols, the row's total over r;
+ *   SCAN: f, the inclusive running total over r up to this element.
+ * Integer arithmetic wraps at 64 bits.  Partition units are rows. */
+#define PTSIM_ITAB_MAPS 5
+#define PTSIM_ITAB_OUTS 4
+#define PTSIM_ITAB_ELEM 0
+#define PTSIM_ITAB_SUM 1
+#define PTSIM_ITAB_SCAN 2
+typedef struct ptsim_itab_out {
+  int32_t arg, map, reg, mode;
+} ptsim_itab_out;
+typedef struct ptsim_itab_params {
+  int64_t rows, cols;
+  int32_t ncode, nout;
+  ptsim_map maps[PTSIM_ITAB_MAPS];
+  ptsim_itab_out out[PTSIM_ITAB_OUTS];
+  ptsim_iinsn code[PTSIM_MAX_ICODE];
+} ptsim_itab_params;
+
 typedef struct ptsim_reduce_params {
   int64_t numel;
   int32_t in_arg, out_arg, op, pad0;
@@ -260,6 +288,7 @@ typedef struct ptsim_desc {
     ptsim_gather_params gat;
     ptsim_ggemm_params ggemm;
     ptsim_gsum_params gsum;
+    ptsim_itab_params itab;
   } p;
 } ptsim_desc;
 
@@ -288,7 +317,8 @@ int ptsim_launch(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int
                  int64_t lo, int64_t hi, void *workspace, size_t workspace_bytes, void *stream);
 
 /* Bytes of device scratch a launch of `desc` wants on `device` (-1 on a bad descriptor): the REDUCE_ALL
- * pass-1 partials, the ATTN_DECODE per-chunk softmax states, else desc->workspace_bytes.  No reference counterpart (Spike needed no device
+ * pass-1 partials, the ATTN_DECODE per-chunk softmax states, the INT_TABLE segment totals of a split row
+ * scan, else desc->workspace_bytes.  No reference counterpart (Spike needed no device
  * scratch). */
 int64_t ptsim_workspace_size(const void *desc, size_t desc_bytes, int device);
 

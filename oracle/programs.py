@@ -279,6 +279,47 @@ def combine_weighted(idx, cum, cnt, pos, expert_out, w, tokens, hidden, topk, ex
     return acc.to(torch.bfloat16).reshape(-1)
 
 
+def expert_counts(ids, experts, n):
+    """layer_op_combine_*/00_*_triton.py: over the n routed expert ids (int64), for each expert x < experts
+    count[x] = the number of ids equal to x (out_ptr0), and running[x + experts * r] = the number of
+    ids[0..r] equal to x, inclusive (out_ptr1: the kernel's block scan plus the carried total of the blocks
+    before, rows of `experts`)."""
+    onehot = (ids.reshape(-1)[:n].to(torch.int64)[:, None] == torch.arange(experts)[None, :]).to(torch.int64)
+    return onehot.sum(dim=0), onehot.cumsum(dim=0).reshape(-1)
+
+
+def cumsum_int(x, n, out_dtype):
+    """layer_op_gmm_*/01_*_triton.py (int32) and layer_op_combine_*/01_*_triton.py (int64): the inclusive
+    running sum of n integers, stored as out_dtype (integer sums wrap; an int32 scan's low 32 bits equal the
+    int64 sum's)."""
+    return torch.cumsum(x.reshape(-1)[:n].to(torch.int64), dim=0).to(out_dtype)
+
+
+def slot_of(running, ids, n, experts):
+    """layer_op_combine_*/02_*_triton.py: out[x] = sum over r < experts of running[r + experts * x] *
+    (ids[x] == r), i.e. running[x, ids[x]] for ids in [0, experts), else 0 (int64)."""
+    run = running.reshape(-1)[:n * experts].to(torch.int64).view(n, experts)
+    hit = (ids.reshape(-1)[:n].to(torch.int64)[:, None] == torch.arange(experts)[None, :]).to(torch.int64)
+    return (run * hit).sum(dim=1)
+
+
+def group_tables(offsets, n):
+    """layer_op_gmm_*/02_*_triton.py over the n running offsets o (int32 in, int64 out): prev[r] = o[r - 1]
+    (0 at r = 0; out_ptr1), count[r] = o[r] - prev[r] (out_ptr2), and the inclusive running number of
+    non-empty groups, cumsum(count > 0) (out_ptr0)."""
+    o = offsets.reshape(-1)[:n].to(torch.int64)
+    prev = torch.cat([torch.zeros(1, dtype=torch.int64), o[:-1]])
+    count = o - prev
+    return torch.cumsum((count > 0).to(torch.int64), dim=0), prev, count
+
+
+def count_le(x, n, rows, out_dtype):
+    """layer_op_gmm_*/03_*_triton.py: out[e] = the number of r < n with x[r] <= e, for e < rows (cast on the
+    store)."""
+    v = x.reshape(-1)[:n].to(torch.int64)
+    return (v[None, :] <= torch.arange(rows)[:, None]).to(torch.int64).sum(dim=1).to(out_dtype)
+
+
 def grouped_gemm(a, b, group, start, rows, c_init, M, N, K, groups):
     """layer_op_gmm_*/05__grouped_mm_kernel/_grouped_mm_kernel_triton.py:4-44: program p takes group
     g = group[p] and its rows [start[g], start[g] + rows[g]); those rows of c become bf16(a_rows . b[g]) with

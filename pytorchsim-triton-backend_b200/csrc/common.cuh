@@ -130,5 +130,8 @@ int launch_sort(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, 
 int launch_gather_rows(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c);
 int launch_grouped_gemm(const ptsim_desc &d, void *const *ptrs, const LaunchCtx &c);
 int launch_gather_sum(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c);
+int launch_itab(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, void *ws, size_t ws_bytes,
+                const LaunchCtx &c);
+int64_t itab_workspace(const ptsim_desc &d, int sm_count);
 
 }  // namespace ptsim

@@ -13,6 +13,7 @@
 #include "attention.cuh"
 #include "decode.cuh"
 #include "moe.cuh"
+#include "itable.cuh"
 
 namespace ptsim {
 
@@ -250,6 +251,40 @@ static int check_desc(const void *p, size_t bytes) {
           return fail(PTSIM_E_DESC, "gather-sum instruction %d", i);
       break;
     }
+    case PTSIM_KIND_INT_TABLE: {
+      const ptsim_itab_params &q = d.p.itab;
+      if (q.rows < 0 || q.cols < 1 || q.ncode < 1 || q.ncode > PTSIM_MAX_ICODE || q.nout < 1 || q.nout > PTSIM_ITAB_OUTS)
+        return fail(PTSIM_E_DESC, "integer table of %lld x %lld with %d instructions and %d outputs", (long long)q.rows,
+                    (long long)q.cols, q.ncode, q.nout);
+      if (q.rows > 0 && q.cols > (int64_t(1) << 62) / q.rows) return fail(PTSIM_E_DESC, "integer table too large");
+      for (int m = 0; m < PTSIM_ITAB_MAPS; ++m) {
+        const ptsim_map &mp = q.maps[m];
+        if (mp.ndigit < 0 || mp.ndigit > PTSIM_MAX_DIGITS) return fail(PTSIM_E_DESC, "integer table map %d", m);
+        for (int k = 0; k < mp.ndigit; ++k)
+          if (mp.div[k] < 1 || mp.mod[k] < 1) return fail(PTSIM_E_DESC, "integer table map %d digit %d", m, k);
+      }
+      for (int k = 0; k < q.nout; ++k) {
+        const ptsim_itab_out &o = q.out[k];
+        if ((rc = check_arg(d, o.arg, "integer table output"))) return rc;
+        if (o.map < 0 || o.map >= PTSIM_ITAB_MAPS || o.reg < 0 || o.reg >= PTSIM_MAX_ICODE || o.mode < PTSIM_ITAB_ELEM ||
+            o.mode > PTSIM_ITAB_SCAN)
+          return fail(PTSIM_E_DESC, "integer table output %d", k);
+        const int dt = d.arg_dtype[o.arg];
+        if (dt != PTSIM_DT_I64 && dt != PTSIM_DT_I32 && dt != PTSIM_DT_I16 && dt != PTSIM_DT_I8 && dt != PTSIM_DT_U8)
+          return fail(PTSIM_E_UNSUPPORTED, "integer table output %d is not an integer tensor", k);
+      }
+      for (int i = 0; i < q.ncode; ++i) {
+        const ptsim_iinsn &in = q.code[i];
+        const bool known = (in.op >= PTSIM_I_LOAD && in.op <= PTSIM_I_LOADI) || in.op == PTSIM_I_LOADM || in.op == PTSIM_I_IDX;
+        if (!known || in.dst >= PTSIM_MAX_ICODE || in.a >= PTSIM_MAX_ICODE || in.b >= PTSIM_MAX_ICODE || in.c >= PTSIM_MAX_ICODE)
+          return fail(PTSIM_E_DESC, "integer table instruction %d", i);
+        if ((in.op == PTSIM_I_LOAD || in.op == PTSIM_I_LOADM || in.op == PTSIM_I_IDX) && in.a >= PTSIM_ITAB_MAPS)
+          return fail(PTSIM_E_DESC, "integer table instruction %d reads map %d", i, in.a);
+        if ((in.op == PTSIM_I_LOAD || in.op == PTSIM_I_LOADM || in.op == PTSIM_I_LOADI) && (rc = check_arg(d, in.c, "integer table load")))
+          return rc;
+      }
+      break;
+    }
     case PTSIM_KIND_REDUCE_ALL: {
       const ptsim_reduce_params &r = d.p.red;
       if ((rc = check_arg(d, r.in_arg, "reduce input")) || (rc = check_arg(d, r.out_arg, "reduce output"))) return rc;
@@ -321,6 +356,7 @@ int ptsim_launch(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int
     case PTSIM_KIND_GATHER_ROWS: return launch_gather_rows(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_GROUPED_GEMM: return launch_grouped_gemm(d, dev_ptrs, c);
     case PTSIM_KIND_GATHER_SUM: return launch_gather_sum(d, dev_ptrs, lo, hi, c);
+    case PTSIM_KIND_INT_TABLE: return launch_itab(d, dev_ptrs, lo, hi, workspace, workspace_bytes, c);
     case PTSIM_KIND_QKNORM_ROPE: return launch_qkrope(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_GEMM: return launch_gemm(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_ATTN_PREFILL: return launch_attention(d, dev_ptrs, lo, hi, c);
@@ -339,6 +375,7 @@ int64_t ptsim_workspace_size(const void *desc, size_t desc_bytes, int device) {
   int64_t need = d.workspace_bytes;
   if (d.kind == PTSIM_KIND_REDUCE_ALL && need < reduce_workspace(sm_count)) need = reduce_workspace(sm_count);
   if (d.kind == PTSIM_KIND_ATTN_DECODE && need < decode_workspace(d, sm_count)) need = decode_workspace(d, sm_count);
+  if (d.kind == PTSIM_KIND_INT_TABLE && need < itab_workspace(d, sm_count)) need = itab_workspace(d, sm_count);
   return need;
 }
 

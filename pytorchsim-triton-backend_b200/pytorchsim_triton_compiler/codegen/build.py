@@ -205,6 +205,74 @@ def combine_gather_sum(tokens, hidden, topk, experts):
     return d
 
 
+_NOMOD = 1 << 62
+
+
+def _int_table(args, rows, cols, maps, code, outs):
+    """An INT_TABLE descriptor: maps [(offset, [(div, mod, stride), ...])], code [(op, a, b, c, imm)] (the
+    destination of instruction k is register k), outs [(mode, arg, map, reg)]."""
+    d = D.new(D.INT_TABLE, _args(args), (1, 1, 1), units=rows, unit_size=1)
+    q = d.p.itab
+    q.rows, q.cols, q.ncode, q.nout = rows, cols, len(code), len(outs)
+    for i, (offset, digits) in enumerate(maps):
+        m = q.maps[i]
+        m.arg, m.offset, m.ndigit = -1, offset, len(digits)
+        for k, (dv, md, sd) in enumerate(digits):
+            m.div[k], m.mod[k], m.stride[k] = dv, md, sd
+    for k, (op, a, b, c, imm) in enumerate(code):
+        ins = q.code[k]
+        ins.op, ins.dst, ins.a, ins.b, ins.c, ins.imm = D.IOP[op], k, a, b, c, imm
+    for i, (mode, arg, mp, reg) in enumerate(outs):
+        o = q.out[i]
+        o.mode, o.arg, o.map, o.reg = D.ITAB_MODE[mode], arg, mp, reg
+    return d
+
+
+def expert_counts(n, experts):
+    """The MoE combine's expert counts (layer_op_combine_*/00_*): ids [n] (int64) -> count [experts] and the
+    inclusive running counts [n * experts] (expert x after routed row r at x + experts * r)."""
+    return _int_table([("in_ptr0", "int64", n), ("out_ptr0", "int64", experts), ("out_ptr1", "int64", n * experts)],
+                      experts, n, [(0, [(1, n, 1)]), (0, [(n, _NOMOD, 1)]), (0, [(1, n, experts), (n, _NOMOD, 1)])],
+                      [("load", 0, 0, 0, 0), ("idx", 1, 0, 0, 0), ("eq", 0, 1, 0, 0)],
+                      [("scan", 2, 2, 2), ("sum", 1, 1, 2)])
+
+
+def cumsum_int(n, in_dtype="int64", out_dtype="int64"):
+    """An integer running sum (layer_op_gmm_*/01_* in int32, layer_op_combine_*/01_* in int64)."""
+    return _int_table([("in_ptr0", in_dtype, n), ("out_ptr0", out_dtype, n)], 1, n, [(0, [(1, n, 1)])],
+                      [("load", 0, 0, 0, 0)], [("scan", 1, 0, 0)])
+
+
+def slot_of(n, experts):
+    """Each routed row's slot in its expert (layer_op_combine_*/02_*): out[x] = sum over r of
+    running[r + experts * x] * (ids[x] == r); arguments running, ids, out (int64)."""
+    e = experts
+    return _int_table([("in_ptr0", "int64", n * e), ("in_ptr1", "int64", n), ("out_ptr0", "int64", n)], n, e,
+                      [(0, [(1, e, 1), (e, _NOMOD, e)]), (0, [(e, _NOMOD, 1)]), (0, [(1, e, 1)])],
+                      [("load", 0, 0, 0, 0), ("load", 1, 0, 1, 0), ("idx", 2, 0, 0, 0), ("eq", 1, 2, 0, 0),
+                       ("mul", 0, 3, 0, 0)],
+                      [("sum", 2, 1, 4)])
+
+
+def group_tables(n):
+    """The grouped matmul's group tables (layer_op_gmm_*/02_*) from the running offsets o [n] (int32):
+    nonempty = cumsum(o[r] - o[r - 1] > 0), prev = o[r - 1] (0 at r = 0), count = o[r] - prev (int64)."""
+    return _int_table([("in_ptr0", "int32", n), ("out_ptr0", "int64", n), ("out_ptr1", "int64", n),
+                       ("out_ptr2", "int64", n)], 1, n, [(0, [(1, n, 1)]), (-1, [(1, n, 1)])],
+                      [("load", 0, 0, 0, 0), ("idx", 0, 0, 0, 0), ("const", 0, 0, 0, 1), ("lt", 1, 2, 0, 0),
+                       ("const", 0, 0, 0, 0), ("where", 4, 4, 3, 0), ("ge", 1, 2, 0, 0), ("loadm", 1, 6, 0, 0),
+                       ("where", 7, 4, 6, 0), ("where", 5, 8, 3, 0), ("sub", 0, 9, 0, 0), ("gt", 10, 4, 0, 0)],
+                      [("scan", 1, 0, 11), ("elem", 2, 0, 9), ("elem", 3, 0, 10)])
+
+
+def count_le(n, rows, in_dtype="int64", out_dtype="int32"):
+    """Groups at or below each expert (layer_op_gmm_*/03_*): out[x] = the number of r < n with v[r] <= x."""
+    return _int_table([("in_ptr0", in_dtype, n), ("out_ptr1", out_dtype, rows)], rows, n,
+                      [(0, [(1, n, 1)]), (0, [(n, _NOMOD, 1)])],
+                      [("load", 0, 0, 0, 0), ("idx", 1, 0, 0, 0), ("le", 0, 1, 0, 0)],
+                      [("sum", 1, 1, 2)])
+
+
 def reduce_all(numel, op="sum", dtype="bfloat16"):
     d = D.new(D.REDUCE_ALL, _args([("in_ptr0", dtype, numel), ("out_ptr0", "float32", 1)]), [1], units=1, unit_size=1,
               workspace_bytes=D.REDUCE_WORKSPACE_BYTES)

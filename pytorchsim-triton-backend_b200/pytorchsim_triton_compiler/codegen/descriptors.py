@@ -12,11 +12,12 @@ MAX_ARGS, MAX_MAPS, MAX_DIGITS, MAX_CODE, MAX_REGS = 16, 8, 4, 32, 8
 
 # Kinds (PTSIM_KIND_*).
 ELEMENTWISE, ROW_SOFTMAX, ROW_RMSNORM, QKNORM_ROPE, GEMM, ATTN_PREFILL, REDUCE_ALL, ATTN_DECODE = 1, 2, 3, 4, 5, 6, 7, 8
-ROW_DIVSUM, TOPK, SORT, GATHER_ROWS, GROUPED_GEMM, GATHER_SUM = 9, 10, 11, 12, 13, 14
+ROW_DIVSUM, TOPK, SORT, GATHER_ROWS, GROUPED_GEMM, GATHER_SUM, INT_TABLE = 9, 10, 11, 12, 13, 14, 15
 KIND_NAME = {ELEMENTWISE: "elementwise", ROW_SOFTMAX: "row_softmax", ROW_RMSNORM: "row_rmsnorm",
              QKNORM_ROPE: "qknorm_rope", GEMM: "gemm", ATTN_PREFILL: "attn_prefill", REDUCE_ALL: "reduce_all",
              ATTN_DECODE: "attn_decode", ROW_DIVSUM: "row_divsum", TOPK: "topk", SORT: "sort",
-             GATHER_ROWS: "gather_rows", GROUPED_GEMM: "grouped_gemm", GATHER_SUM: "gather_sum"}
+             GATHER_ROWS: "gather_rows", GROUPED_GEMM: "grouped_gemm", GATHER_SUM: "gather_sum",
+             INT_TABLE: "int_table"}
 
 # Element types (PTSIM_DT_*), keyed by kernel.json dtype names (contract/kernel_object.py NP_DTYPE keys).
 DTYPE_CODE = {"float32": 0, "bfloat16": 1, "float16": 2, "int32": 3, "int64": 4, "int16": 5, "int8": 6,
@@ -90,7 +91,7 @@ class SelectParams(C.Structure):
 MAX_ICODE = 32
 IOP = {"load": 1, "const": 2, "add": 3, "sub": 4, "mul": 5, "div": 6, "mod": 7, "inv": 8, "lt": 9, "le": 10,
        "gt": 11, "ge": 12, "eq": 13, "ne": 14, "where": 15, "and": 16, "or": 17, "xor": 18, "shr": 19, "shl": 20,
-       "loadi": 21}
+       "loadi": 21, "loadm": 22, "idx": 23}
 IOP_NAME = {v: k for k, v in IOP.items()}
 
 
@@ -120,10 +121,24 @@ class GsumParams(C.Structure):
                 ("w_map", Map), ("maps", Map * GSUM_MAPS), ("code", IInsn * MAX_ICODE)]
 
 
+ITAB_MAPS, ITAB_OUTS = 5, 4
+ITAB_MODE = {"elem": 0, "sum": 1, "scan": 2}
+ITAB_MODE_NAME = {v: k for k, v in ITAB_MODE.items()}
+
+
+class ItabOut(C.Structure):
+    _fields_ = [("arg", C.c_int32), ("map", C.c_int32), ("reg", C.c_int32), ("mode", C.c_int32)]
+
+
+class ItabParams(C.Structure):
+    _fields_ = [("rows", C.c_int64), ("cols", C.c_int64), ("ncode", C.c_int32), ("nout", C.c_int32),
+                ("maps", Map * ITAB_MAPS), ("out", ItabOut * ITAB_OUTS), ("code", IInsn * MAX_ICODE)]
+
+
 class Params(C.Union):
     _fields_ = [("ew", EwParams), ("row", RowParams), ("qk", QkParams), ("gemm", GemmParams),
                 ("attn", AttnParams), ("red", ReduceParams), ("sel", SelectParams), ("gat", GatherParams),
-                ("ggemm", GGemmParams), ("gsum", GsumParams)]
+                ("ggemm", GGemmParams), ("gsum", GsumParams), ("itab", ItabParams)]
 
 
 class Desc(C.Structure):
@@ -220,6 +235,11 @@ def describe(d):
     elif d.kind == GATHER_SUM:
         q = d.p.gsum
         out.update(rows=q.rows, cols=q.cols, terms=q.terms, table_rows=q.table_rows,
+                   program=[(IOP_NAME.get(i.op, i.op), i.dst, i.a, i.b, i.c, i.imm) for i in list(q.code)[:q.ncode]])
+    elif d.kind == INT_TABLE:
+        q = d.p.itab
+        out.update(rows=q.rows, cols=q.cols,
+                   outputs=[(ITAB_MODE_NAME.get(o.mode, o.mode), o.arg, o.map, o.reg) for o in list(q.out)[:q.nout]],
                    program=[(IOP_NAME.get(i.op, i.op), i.dst, i.a, i.b, i.c, i.imm) for i in list(q.code)[:q.ncode]])
     elif d.kind == REDUCE_ALL:
         out.update(numel=d.p.red.numel, op="max" if d.p.red.op == RED_MAX else "sum")

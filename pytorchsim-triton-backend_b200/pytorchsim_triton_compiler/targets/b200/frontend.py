@@ -11,6 +11,9 @@ The IR:
   index expressions (Index): const + sum coeff * digit(var, div, mod), digit = (var // div) % mod, over
     the launch's global row index 'x' (pid * XBLOCK + arange), the reduction index 'r', and program ids;
   values (Node): Load(arg, index, mask, other), Const, Op(name, *args), Reduce(op, value), Dot(a, b);
+    integer programs add IndexValue(index) (an index used as data), Scan(op, value, axis) (an inclusive
+    scan along the block), ChunkLast(value) (a scan's last element in the block) and Carry (an integer
+    loop-carried value as the loop body sees it);
   Store(arg, index, value, mask) records.
 Anything outside that (an index the algebra cannot state, a call it does not know) raises Refused, the
 reference's refusal discipline (contract/stop.py); nothing is guessed."""
@@ -189,6 +192,46 @@ class Dot(Node):
         self.a, self.b = a, b
 
 
+class IndexValue(Node):
+    """An index expression used as an integer value (tmp = (x0).to(tl.int64); tmp == loaded)."""
+    kind = "index"
+
+    def __init__(self, index):
+        self.index = index
+
+
+class Scan(Node):
+    """tl.associative_scan(value, axis, combine) with an additive combine: the inclusive running sum along the
+    block's `axis` (within one block of a looped reduction)."""
+    kind = "scan"
+
+    def __init__(self, op, value, axis):
+        self.op, self.value, self.axis = op, value, axis
+
+
+class ChunkLast(Node):
+    """The last element of `value` along the reduction block (triton_helpers.select_one(v, rbase == RBLOCK - 1)):
+    for a Scan, the block's total."""
+    kind = "chunk_last"
+
+    def __init__(self, value):
+        self.value = value
+
+
+class Carry(Node):
+    """An integer value carried across the iterations of `loop` (a name holding an integer tl.full before the
+    loop and reassigned in its body), as one iteration sees it on entry.  `init` is its value before the
+    loop; the body's update is recorded in Program.carries."""
+    kind = "carry"
+
+    def __init__(self, name, init, loop):
+        self.name, self.init, self.loop = name, init, loop
+
+
+class IntFull(int):
+    """The value of an integer tl.full / tl.zeros: a loop-carried integer accumulator starts from one."""
+
+
 class Cond:
     """A mask: a comparison of an index with a constant, or a conjunction of masks."""
 
@@ -236,6 +279,7 @@ class Program:
         self.assigned = {}   # name -> last constant value assigned in the body (M = 4096, eps, ...)
         self.calls = set()   # every tl./libdevice. call name met
         self.block = {}      # axis -> block size of a pid * BLOCK + arange(BLOCK) index
+        self.carries = {}    # Carry -> its value at the end of the loop body (integer loop-carried values)
 
 
 def kernel_source(fn):
@@ -251,11 +295,53 @@ def kernel_source(fn):
     return textwrap.dedent(inspect.getsource(inner)), inner.__name__
 
 
+def kernel_globals(fn):
+    """The module globals of a @triton.jit kernel (where its @triton.jit helpers live), or {}."""
+    inner = fn
+    for _ in range(4):
+        g = getattr(inner, "__globals__", None)
+        if isinstance(g, dict):
+            return g
+        inner = getattr(inner, "fn", None)
+        if inner is None:
+            break
+    return {}
+
+
+def combine_op(helper):
+    """'add' when the @triton.jit function `helper` returns the sum of its two arguments (Inductor's
+    _triton_helper_fn_add0), else None."""
+    try:
+        src, name = kernel_source(helper)
+    except (TypeError, OSError):
+        return None
+    fn = next((n for n in ast.walk(ast.parse(src)) if isinstance(n, ast.FunctionDef)), None)
+    if fn is None or len(fn.args.args) != 2:
+        return None
+    a, b = (x.arg for x in fn.args.args)
+    env = {}
+    for st in fn.body:
+        if isinstance(st, ast.Assign) and len(st.targets) == 1 and isinstance(st.targets[0], ast.Name):
+            env[st.targets[0].id] = st.value
+        elif isinstance(st, ast.Return) and st.value is not None:
+            e = st.value
+            while isinstance(e, ast.Name) and e.id in env:
+                e = env[e.id]
+            if isinstance(e, ast.BinOp) and isinstance(e.op, ast.Add) and isinstance(e.left, ast.Name) \
+                    and isinstance(e.right, ast.Name) and {e.left.id, e.right.id} == {a, b}:
+                return "add"
+            return None
+        elif not isinstance(st, (ast.Expr, ast.Pass)):
+            return None
+    return None
+
+
 class Evaluator:
-    def __init__(self, spec, prog):
+    def __init__(self, spec, prog, globals_=None):
         self.spec, self.prog = spec, prog
         self.env = {}
         self.acc_init = {}
+        self.globals = globals_ or {}
 
     # ---- entry ---------------------------------------------------------------------------------
     def run(self, src, name):
@@ -318,6 +404,10 @@ class Evaluator:
             raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"statement {type(s).__name__} at line {s.lineno}")
 
     def assign(self, target, v):
+        if isinstance(target, ast.Tuple) and isinstance(v, (list, tuple)) and len(v) == len(target.elts):
+            for t, x in zip(target.elts, v):
+                self.assign(t, x)
+            return
         if isinstance(target, ast.Name):
             if isinstance(v, Arange) and v.dim is None:
                 # A 1-D block index: the program names which axis it walks (x*: rows, r*: reduction).
@@ -345,7 +435,22 @@ class Evaluator:
         self.prog.loops.append(lv)
         before = dict(self.env)
         self.env[s.target.id] = lv
+        # Integer loop-carried names: an integer tl.full before the loop, reassigned in the body.
+        assigned = {t.id for st in s.body for n in ast.walk(st) if isinstance(n, ast.Assign)
+                    for t in n.targets if isinstance(t, ast.Name)}
+        carries = {}
+        for name in sorted(assigned):
+            if isinstance(self.env.get(name), IntFull):
+                carries[name] = self.env[name] = Carry(name, int(self.env[name]), lv)
         self.block(s.body)
+        for name, c in carries.items():
+            v = self.env.get(name)
+            if v is c:
+                self.env[name] = before[name]
+                continue
+            self.prog.carries[c] = v
+            if isinstance(v, Op) and v.name in ("add", "max", "min") and len(v.args) == 2 and v.args[0] is c:
+                self.env[name] = Op("acc_" + v.name, v.args[1])
         # Accumulators: a name holding a constant before the loop and op(previous, x) after one pass.
         for name, v in list(self.env.items()):
             old = before.get(name)
@@ -436,6 +541,10 @@ class Evaluator:
             return Cond(name, idx, b)
         if isinstance(a, (Index, Arange, Pid, LoopVar)) and isinstance(b, (Index, Arange, Pid, LoopVar)):
             return Cond(name, self.index_of(a) - self.index_of(b), 0)
+        idx_like = (Index, Arange, Pid, LoopVar)
+        if (isinstance(a, idx_like) and isinstance(b, Node)) or (isinstance(a, Node) and isinstance(b, idx_like)):
+            # loaded data against an index (an expert id against the row's expert number)
+            return Cond("data", None, Op("cmp_" + name, self.value(a), self.value(b)))
         if isinstance(a, (Node, int, float)) and isinstance(b, (Node, int, float)):
             # a comparison of data values: kept as a value node (0/1) for where() and integer programs
             return Cond("data", None, Op("cmp_" + name, self.value(a), self.value(b)))
@@ -470,6 +579,12 @@ class Evaluator:
             return v
         if isinstance(v, Cond) and v.op == "data" and isinstance(v.value, Node):
             return v.value   # a comparison of data values as 0 / 1
+        if isinstance(v, (Index, Arange, Pid, LoopVar)):
+            return IndexValue(self.index_of(v))
+        if isinstance(v, DataIndex):
+            return Op("add", IndexValue(v.index), v.data)
+        if isinstance(v, Cond) and v.op in ("lt", "le", "gt", "ge", "eq", "ne") and isinstance(v.index, Index):
+            return Op("cmp_" + v.op, IndexValue(v.index), Const(v.value))   # an index comparison as 0 / 1
         if isinstance(v, (int, float)) and not isinstance(v, bool):
             return Const(v)
         if isinstance(v, bool):
@@ -559,7 +674,7 @@ class Evaluator:
             if isinstance(fill, bool) or isinstance(fill, (Index, Pid, Arange, LoopVar)):
                 return fill
             if is_int:
-                return int(fill)
+                return IntFull(int(fill))
             return Const(float(fill))
         if name in ("cdiv",):
             return -(-int(args[0]) // int(args[1]))
@@ -601,6 +716,12 @@ class Evaluator:
         if name in ("maximum", "minimum"):
             return Op("max" if name == "maximum" else "min", self.value(args[0]), self.value(args[1]))
         if name == "where":
+            if self._first_iteration_guard(args[0]):
+                # where(roffset > 0, carry + v, v) with the carry 0 before the loop: carry + v on every pass
+                a1, a2 = self.value(args[1]), self.value(args[2])
+                if isinstance(a1, Op) and a1.name == "add" and isinstance(a1.args[0], Carry) and a1.args[0].init == 0 \
+                        and a1.args[1] is a2 and a1.args[0].loop.name == args[0].index.single()[0][len("loop:"):]:
+                    return a1
             if isinstance(args[0], Cond) and args[0].op == "bounds":
                 return self.value(args[1])
             if isinstance(args[0], bool):
@@ -614,11 +735,38 @@ class Evaluator:
             if isinstance(v, Op) and v.name == "acc_" + op:
                 v = v.args[0]
             return Reduce(op, v)
+        if name == "associative_scan":
+            vals = args[0] if args else kw.get("input")
+            axis = args[1] if len(args) > 1 else kw.get("axis")
+            fn = args[2] if len(args) > 2 else kw.get("combine_fn")
+            if not isinstance(vals, list) or len(vals) != 1 or not isinstance(axis, int):
+                raise Refused(Reason.MATH_UNLOWERED, f"{f.name} over {len(vals) if isinstance(vals, list) else '?'} values")
+            helper = self.globals.get(fn.name) if isinstance(fn, _Module) else None
+            if helper is None or combine_op(helper) != "add":
+                raise Refused(Reason.MATH_UNLOWERED, f"{f.name} with a combine function other than a + b")
+            return [Scan("add", self.value(vals[0]), axis)]
+        if name == "select_one":
+            cond = args[1] if len(args) > 1 else None
+            rb = self.prog.block.get("r") or self.env.get("R0_BLOCK") or self.env.get("RBLOCK")
+            if isinstance(cond, Cond) and cond.op == "eq" and isinstance(cond.index, Index) and cond.index.const == 0 \
+                    and cond.index.terms == {Digit("r"): 1} and isinstance(rb, int) and cond.value == rb - 1:
+                return ChunkLast(self.value(args[0]))
+            raise Refused(Reason.MATH_UNLOWERED, f"{f.name} of other than the block's last element")
         if name in ("fma",):
             return Op("add", Op("mul", self.value(args[0]), self.value(args[1])), self.value(args[2]))
         if name.startswith("atomic"):
             raise Refused(Reason.ATOMICS, f"{f.name}: atomics have no tile program on this executor")
         raise Refused(Reason.MATH_UNLOWERED, f"call of {f.name}")
+
+    def _first_iteration_guard(self, c):
+        """Whether `c` is `loopvar > 0` for a loop starting at 0 (false exactly on the first pass)."""
+        if not (isinstance(c, Cond) and c.op == "gt" and c.value == 0 and isinstance(c.index, Index)):
+            return False
+        d = c.index.single()
+        if d is None or c.index.const != 0 or not str(d[0]).startswith("loop:") or d[1] != 1 or d[2] is not None:
+            return False
+        lv = next((l for l in self.prog.loops if l.name == d[0][len("loop:"):]), None)
+        return lv is not None and lv.start == 0 and isinstance(lv.step, int) and lv.step > 0
 
     def method(self, obj, attr, args, kw):
         if attr == "to":
@@ -684,7 +832,7 @@ def trace(spec, fn=None):
     if fn is None:
         fn = load_kernel(spec)
     src, name = kernel_source(fn)
-    return Evaluator(spec, Program()).run(src, name)
+    return Evaluator(spec, Program(), kernel_globals(fn)).run(src, name)
 
 
 def load_kernel(spec):

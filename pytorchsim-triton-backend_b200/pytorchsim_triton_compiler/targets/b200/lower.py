@@ -67,12 +67,23 @@ def key(n):
     if isinstance(n, F.Load):
         return ("l", n.arg, tuple(sorted(n.index.terms.items())), n.index.const, n.mask is not None)
     if isinstance(n, F.Op):
-        return ("o", n.name) + tuple(key(a) if isinstance(a, F.Node) else ("m",) for a in n.args)
+        return ("o", n.name) + tuple(key(a) if isinstance(a, F.Node) else _cond_key(a) for a in n.args)
     if isinstance(n, F.Reduce):
         return ("r", n.op, key(n.value))
+    if isinstance(n, F.IndexValue):
+        return ("i", tuple(sorted(n.index.terms.items())), n.index.const)
     if isinstance(n, F.Dot):
         return ("d", key(n.a), key(n.b))
     return ("?", id(n))
+
+
+def _cond_key(c):
+    """A hashable form of a mask / condition operand (index comparisons by their index and bound)."""
+    if not isinstance(c, F.Cond):
+        return ("m",)
+    idx = (tuple(sorted(c.index.terms.items())), c.index.const) if isinstance(c.index, F.Index) else None
+    val = key(c.value) if isinstance(c.value, F.Node) else c.value
+    return ("m", c.op, idx, val, tuple(_cond_key(p) for p in c.parts))
 
 
 def walk(n, seen=None):
@@ -86,7 +97,7 @@ def walk(n, seen=None):
         for a in n.args:
             if isinstance(a, F.Node):
                 yield from walk(a, seen)
-    elif isinstance(n, F.Reduce):
+    elif isinstance(n, (F.Reduce, F.Scan, F.ChunkLast)):
         yield from walk(n.value, seen)
     elif isinstance(n, F.Dot):
         yield from walk(n.a, seen)
@@ -134,7 +145,10 @@ def lower(spec, fn=None):
         if len(dots) >= 2 and {"HKV", "G", "GP", "S", "D", "BKV", "SCALE"} <= set(spec.constexprs):
             return _lower_decode(spec, tree)
         return _lower_gemm(spec, tree, src)
-    prog = F.Evaluator(spec, F.Program()).run(src, name)
+    prog = F.Evaluator(spec, F.Program(), F.kernel_globals(fn)).run(src, name)
+    if prog.stores and all(spec.args[st.arg].dtype in _INT_TYPES for st in prog.stores) and any(
+            isinstance(n, (F.Scan, F.Reduce, F.Carry, F.ChunkLast)) for st in prog.stores for n in walk(st.value)):
+        return _lower_int_table(spec, prog)
     if len(prog.stores) != 1:
         raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: {len(prog.stores)} stores; the executor's "
                                                     f"vector programs have one")
@@ -965,4 +979,177 @@ def _lower_gather_sum(spec, prog, st, red):
         g.maps[i] = m
     for i, ins in enumerate(code):
         g.code[i] = ins
+    return Lowered(d, D.describe(d))
+
+
+# ---------------------------------------------------------------------------------------------------
+# Integer table programs
+# ---------------------------------------------------------------------------------------------------
+
+_INT_TYPES = ("int64", "int32", "int16", "int8", "uint8", "bool")
+
+
+def _itab_program(spec, cols, exprs):
+    """(instructions, maps, result register per expression) of int64 programs over the element f = x * cols + r:
+    loads and index values through up to PTSIM_ITAB_MAPS maps (deduplicated by index, the argument in the
+    instruction), masked loads as LOADM, loads through a loaded position as LOADI, index comparisons as
+    IDX + compare, shared subtrees computed once."""
+    code, memo, maps = [], {}, []
+
+    def emit(op, a=0, b=0, c=0, imm=0):
+        if len(code) >= D.MAX_ICODE:
+            raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: an integer program over {D.MAX_ICODE} instructions")
+        ins = D.IInsn()
+        ins.op, ins.dst, ins.a, ins.b, ins.c, ins.imm = D.IOP[op], len(code), a, b, c, int(imm)
+        code.append(ins)
+        return ins.dst
+
+    def slot(idx):
+        k = (tuple(sorted(idx.terms.items())), idx.const)
+        for i, (kk, _) in enumerate(maps):
+            if kk == k:
+                return i
+        if len(maps) >= D.ITAB_MAPS:
+            raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: more than {D.ITAB_MAPS} distinct indices")
+        maps.append((k, _term_map(spec, idx, 1, cols, -1)))
+        return len(maps) - 1
+
+    def int_arg(a):
+        if spec.args[a].dtype not in _INT_TYPES:
+            raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a {spec.args[a].dtype} load in an integer program")
+        return a
+
+    def gen_cond(c):
+        if c.op == "data" and isinstance(c.value, F.Node):
+            return gen(c.value)
+        if c.op == "bounds":
+            return gen(F.Const(1))
+        if c.op in ("lt", "le", "gt", "ge", "eq", "ne") and isinstance(c.index, F.Index) and isinstance(c.value, int):
+            return gen(F.Op("cmp_" + c.op, F.IndexValue(c.index), F.Const(c.value)))
+        if c.op == "and" and c.parts:
+            r = gen_cond(c.parts[0])
+            for p in c.parts[1:]:
+                r = emit("and", r, gen_cond(p))
+            return r
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a condition {c.op} in an integer program")
+
+    def gen(n):
+        if isinstance(n, F.Cond):
+            return gen_cond(n)
+        k = (key(n), _cond_key(n.mask)) if isinstance(n, F.Load) else key(n)
+        if k in memo:
+            return memo[k]
+        if isinstance(n, F.Const):
+            if n.v != int(n.v):
+                raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a fractional constant {n.v} in an integer program")
+            r = emit("const", imm=int(n.v))
+        elif isinstance(n, F.IndexValue):
+            r = emit("idx", slot(n.index))
+        elif isinstance(n, F.Load) and n.data is None:
+            if n.mask is None:
+                r = emit("load", slot(n.index), 0, int_arg(n.arg))
+            else:
+                other = n.other.v if isinstance(n.other, F.Const) else (n.other or 0)
+                if not isinstance(other, (int, float)) or other != int(other):
+                    raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a masked load whose fill is not an integer")
+                cnd = gen_cond(n.mask)
+                r = emit("loadm", slot(n.index), cnd, int_arg(n.arg), imm=int(other))
+        elif isinstance(n, F.Load):
+            if n.mask is not None:
+                raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a masked load through a loaded position")
+            pos = gen(n.data)
+            if n.index.terms:
+                pos = emit("add", pos, emit("idx", slot(n.index)))
+            elif n.index.const:
+                pos = emit("add", pos, gen(F.Const(n.index.const)))
+            r = emit("loadi", pos, 0, int_arg(n.arg))
+        elif isinstance(n, F.Op):
+            if n.name in _IBIN or n.name in _CMP:
+                a, b = gen(n.args[0]), gen(n.args[1])
+                r = emit(_IBIN.get(n.name) or _CMP[n.name], a, b)
+            elif n.name == "invert":
+                r = emit("inv", gen(n.args[0]))
+            elif n.name == "neg":
+                r = emit("sub", gen(F.Const(0)), gen(n.args[0]))
+            elif n.name == "where":
+                cnd = gen(n.args[0])
+                a, b = gen(n.args[1]), gen(n.args[2])
+                r = emit("where", a, b, cnd)
+            else:
+                raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: {n.name} in an integer program")
+        else:
+            raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: {type(n).__name__} in an integer program")
+        memo[k] = r
+        return r
+
+    regs = [gen(e) for e in exprs]
+    return code, regs, slot, maps
+
+
+def _lower_int_table(spec, prog):
+    """The MoE routing tables (validation/pytorchsim/layer_op_gmm_*/01_* to 03_*, layer_op_combine_*/00_* to
+    02_*): integer programs over a [rows = xnumel, cols = r0_numel] space whose stores are per element,
+    a row total (tl.sum over r), or an inclusive running total over r (tl.associative_scan with a + b; in
+    a looped reduction, the block scan plus a carry that adds each block's last element, Inductor's
+    split-scan form).  Each store becomes an output of one PTSIM_KIND_INT_TABLE descriptor."""
+    cols = _lookup(spec, prog, "r0_numel", "rnumel")
+    if cols is None:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: an integer table without a reduction extent")
+    rows, cols = int(_lookup(spec, prog, "xnumel") or 1), int(cols)
+    rblock = prog.block.get("r") or _lookup(spec, prog, "R0_BLOCK", "RBLOCK")
+    rblock = int(rblock) if rblock is not None else cols
+
+    def along_r(sc):
+        if not (sc.axis == 1 or (sc.axis in (0, -1) and rows == 1)):
+            raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a scan along axis {sc.axis}")
+
+    outs = []
+    for st in prog.stores:
+        if st.mask is not None:
+            raise Refused(Reason.MASKED_STORE_NOT_A_BOX, f"{spec.name}: a masked store in an integer program")
+        v = st.value
+        if isinstance(v, F.Reduce):
+            if v.op != "add":
+                raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: an integer {v.op} reduction")
+            if "r" in st.index.vars():
+                raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: a row total stored at every r")
+            mode, e = "sum", v.value
+        elif isinstance(v, F.Scan):
+            along_r(v)
+            if prog.loops or rblock != cols:
+                raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a scan restarted in every block")
+            mode, e = "scan", v.value
+        elif isinstance(v, F.Op) and v.name == "add" and len(v.args) == 2 and isinstance(v.args[0], F.Carry) \
+                and isinstance(v.args[1], F.Scan):
+            c, sc = v.args
+            along_r(sc)
+            upd = prog.carries.get(c)
+            lp = c.loop
+            if not (c.init == 0 and isinstance(upd, F.Op) and upd.name == "add" and upd.args[0] is c
+                    and isinstance(upd.args[1], F.ChunkLast) and upd.args[1].value is sc
+                    and lp.start == 0 and lp.step == rblock and lp.stop == cols and cols % rblock == 0):
+                raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a block scan whose carry is not the "
+                                                            f"running total of the blocks before")
+            mode, e = "scan", sc.value
+        else:
+            mode, e = "elem", v
+            if "r" not in st.index.vars() and cols != 1:
+                raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: an element store without the r index")
+        if any(isinstance(n, (F.Scan, F.Reduce, F.Carry, F.ChunkLast)) for n in walk(e)):
+            raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a nested scan or reduction")
+        outs.append((st, mode, e))
+    if len(outs) > D.ITAB_OUTS:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: {len(outs)} stores (at most {D.ITAB_OUTS})")
+    code, regs, slot, maps = _itab_program(spec, cols, [e for _, _, e in outs])
+    out_maps = [slot(st.index) for st, _, _ in outs]   # store indices share the table with the loads
+    d = D.new(D.INT_TABLE, _manifest_args(spec), spec.grid, units=rows, unit_size=1)
+    q = d.p.itab
+    q.rows, q.cols, q.ncode, q.nout = rows, cols, len(code), len(outs)
+    for i, (_, m) in enumerate(maps):
+        q.maps[i] = m
+    for i, ((st, mode, _), reg, m) in enumerate(zip(outs, regs, out_maps)):
+        o = q.out[i]
+        o.arg, o.map, o.reg, o.mode = st.arg, m, reg, D.ITAB_MODE[mode]
+    for i, ins in enumerate(code):
+        q.code[i] = ins
     return Lowered(d, D.describe(d))

@@ -153,7 +153,23 @@ def cases():
              {"family": "dispatch_gather", "tokens": T, "hidden": 2048, "topk": 8}, gold),
             (f"moe_combine_t{T}_03_weighted", spec_file(f"layer_op_combine_{T}x0_bf16", 3),
              {"family": "combine_weighted", "tokens": T, "hidden": 2048, "topk": 8, "experts": 128}, gold),
+            # the combine's routing tables: per-expert counts and running counts over the 8T routed ids
+            # (00), their running sum (01), each routed row's slot within its expert (02)
+            (f"moe_combine_t{T}_00_counts", spec_file(f"layer_op_combine_{T}x0_bf16", 0),
+             {"family": "expert_counts", "experts": 128, "n": 8 * T}, gold),
+            (f"moe_combine_t{T}_02_slot", spec_file(f"layer_op_combine_{T}x0_bf16", 2),
+             {"family": "slot_of", "experts": 128, "n": 8 * T}, gold),
         ]
+    # the grouped matmul's group tables over the 128 experts (the same three programs at every T):
+    # running offsets (01), previous offset / count / running non-empty groups (02), groups at or below each
+    # expert (03); and the combine's int64 running sum of the expert counts (01)
+    gu = "layer_op_gmm_gate_up_128x0_bf16"
+    out += [
+        ("moe_gmm_01_offsets", spec_file(gu, 1), {"family": "cumsum_int", "n": 128}, True),
+        ("moe_gmm_02_group_tables", spec_file(gu, 2), {"family": "group_tables", "n": 128}, True),
+        ("moe_gmm_03_count_le", spec_file(gu, 3), {"family": "count_le", "n": 128, "rows": 128}, True),
+        ("moe_combine_01_offsets", spec_file("layer_op_combine_128x0_bf16", 1), {"family": "cumsum_int", "n": 128}, True),
+    ]
     # The MoE expert matmul: the reference kernel at an interpreter-sized configuration (golden), and the
     # bundle's T = 1 and 128 objects (gate_up K 2048 -> N 1536, down K 768 -> N 2048; 128 experts; the group
     # tables of the recorded routing are kept as input fixtures).

@@ -222,3 +222,101 @@ def test_combine_out_of_range_is_recorded():
     with pytest.raises(native.ExecutorError) as e:
         RC.launch_tensors(D.to_bytes(B.combine_gather_sum(tokens, hidden, topk, experts)), ts)
     assert e.value.code == D.E_OOB
+
+
+# ---- the routing tables (INT_TABLE): exact integer results ------------------------------------------------
+
+def routed_ids(n, experts, seed, wild=False):
+    g = torch.Generator().manual_seed(seed)
+    ids = torch.randint(0, experts, (n,), generator=g)
+    if wild:                                  # ids no expert matches: negative and past the last expert
+        ids[::7] = -1 - ids[::7]
+        ids[3::11] += experts
+    return ids
+
+
+@pytest.mark.parametrize("n,experts,wild", [(32768, 128, False), (1024, 128, True), (8, 128, False),
+                                            (5000, 16, True), (100000, 3, False), (1, 1, False)])
+def test_expert_counts(n, experts, wild):
+    """Counts and running counts: the unsplit path (short routed range) and the split one (a long range
+    over few experts: chunk totals through the workspace)."""
+    ids = routed_ids(n, experts, n, wild)
+    cnt, run_ = run(B.expert_counts(n, experts), [ids, torch.zeros(experts, dtype=torch.int64),
+                                                  torch.zeros(n * experts, dtype=torch.int64)])[1:]
+    wc, wr = O.expert_counts(ids, experts, n)
+    assert torch.equal(cnt, wc) and torch.equal(run_, wr)
+
+
+@pytest.mark.parametrize("n,in_dtype,out_dtype", [(128, "int32", "int32"), (128, "int64", "int64"),
+                                                  (100000, "int64", "int64"), (3, "int32", "int64"),
+                                                  (70000, "int32", "int32")])
+def test_cumsum_int(n, in_dtype, out_dtype):
+    g = torch.Generator().manual_seed(n)
+    x = torch.randint(-1000, 100000, (n,), generator=g).to(getattr(torch, in_dtype))
+    if in_dtype == "int32" and n > 1000:
+        x[::3] = 2**31 - 5                    # the int32 running sum wraps, as the reference's int32 scan does
+    got = run(B.cumsum_int(n, in_dtype, out_dtype), [x, torch.zeros(n, dtype=getattr(torch, out_dtype))])[1]
+    assert torch.equal(got, O.cumsum_int(x, n, getattr(torch, out_dtype)))
+
+
+@pytest.mark.parametrize("n,experts", [(32768, 128), (8, 128), (3000, 7)])
+def test_slot_of(n, experts):
+    ids = routed_ids(n, experts, 7, wild=True)
+    g = torch.Generator().manual_seed(8)
+    running = torch.randint(-50, 50, (n * experts,), generator=g)
+    got = run(B.slot_of(n, experts), [running, ids, torch.zeros(n, dtype=torch.int64)])[2]
+    assert torch.equal(got, O.slot_of(running, ids, n, experts))
+
+
+@pytest.mark.parametrize("n", [128, 5, 1, 4096])
+def test_group_tables(n):
+    g = torch.Generator().manual_seed(n)
+    counts = torch.randint(0, 4, (n,), generator=g) * (torch.rand(n, generator=g) < 0.6)   # empty groups
+    offs = torch.cumsum(counts, 0).to(torch.int32)
+    got = run(B.group_tables(n), [offs] + [torch.zeros(n, dtype=torch.int64) for _ in range(3)])[1:]
+    for a, b in zip(got, O.group_tables(offs, n)):
+        assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("n,rows", [(128, 128), (129, 7), (4096, 300)])
+def test_count_le(n, rows):
+    g = torch.Generator().manual_seed(rows)
+    v = torch.sort(torch.randint(-2, rows + 3, (n,), generator=g)).values
+    got = run(B.count_le(n, rows), [v, torch.zeros(rows, dtype=torch.int32)])[1]
+    assert torch.equal(got, O.count_le(v, n, rows, torch.int32))
+
+
+def test_routing_chain_reproduces_the_routing():
+    """counts (00) -> their running sum (01) -> each routed row's slot (02) rebuild the (cum, cnt, pos) tables a
+    consistent routing has, which the weighted combine (03) reads."""
+    tokens, topk, experts = 4096, 8, 128
+    n = tokens * topk
+    ids, cum, cnt, pos = moe_routing(tokens, topk, experts, 11)
+    c0, r0 = run(B.expert_counts(n, experts), [ids, torch.zeros(experts, dtype=torch.int64),
+                                               torch.zeros(n * experts, dtype=torch.int64)])[1:]
+    c1 = run(B.cumsum_int(experts), [c0, torch.zeros(experts, dtype=torch.int64)])[1]
+    s2 = run(B.slot_of(n, experts), [r0, ids, torch.zeros(n, dtype=torch.int64)])[2]
+    assert torch.equal(c0, cnt) and torch.equal(c1, cum) and torch.equal(s2, pos)
+
+
+def test_int_table_unit_ranges():
+    """Rows launched in parts (the runtime's split of a launch over GPUs) give the whole launch's tables."""
+    n, experts = 20000, 64
+    ids = routed_ids(n, experts, 5)
+    d = D.to_bytes(B.expert_counts(n, experts))
+    ts = [t.cuda() for t in (ids, torch.zeros(experts, dtype=torch.int64), torch.zeros(n * experts, dtype=torch.int64))]
+    for lo, hi in ((0, 5), (5, 40), (40, 64)):
+        RC.launch_tensors(d, ts, lo, hi)
+    wc, wr = O.expert_counts(ids, experts, n)
+    assert torch.equal(ts[1].cpu(), wc) and torch.equal(ts[2].cpu(), wr)
+
+
+def test_int_table_out_of_range_is_recorded():
+    """A load past its tensor records PTSIM_E_OOB (the reference's bounds assertion) and reads 0."""
+    n = 64
+    desc = B.cumsum_int(n)
+    desc.arg_numel[0] = n - 1                 # the tensor holds one element fewer than the program reads
+    ts = [torch.arange(n - 1, dtype=torch.int64).cuda(), torch.zeros(n, dtype=torch.int64).cuda()]
+    with pytest.raises(native.ExecutorError) as e:
+        RC.launch_tensors(D.to_bytes(desc), ts)
+    assert e.value.code == D.E_OOB

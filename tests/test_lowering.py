@@ -98,3 +98,23 @@ def test_every_decode_and_m1_workload_lowers():
             assert desc.kind == D.GEMM and (g.M, g.N, g.K, g.b_kmajor, g.ldb) == (1, n, k, 0, n), wl
             seen["gemv"] += 1
     assert seen == {"decode": 28, "gemv": 13}
+
+
+def test_routing_table_builders_match_the_lowered_objects():
+    """The INT_TABLE builders (codegen/build.py) state the same descriptors the lowering made from the
+    reference's kernels (layer_op_combine_*/00-02, layer_op_gmm_*/01-03)."""
+    import os
+    from pytorchsim_triton_compiler.codegen import build as B
+    from pytorchsim_triton_compiler.codegen import descriptors as D
+    from pytorchsim_triton_compiler.contract import kernel_object as ko
+    obj = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "objects")
+    pairs = [("moe_combine_t128_00_counts", B.expert_counts(1024, 128)), ("moe_combine_01_offsets", B.cumsum_int(128)),
+             ("moe_gmm_01_offsets", B.cumsum_int(128, "int32", "int32")),
+             ("moe_combine_t128_02_slot", B.slot_of(1024, 128)), ("moe_gmm_02_group_tables", B.group_tables(128)),
+             ("moe_gmm_03_count_le", B.count_le(128, 128)), ("moe_combine_t4096_00_counts", B.expert_counts(32768, 128))]
+    for name, d in pairs:
+        m = ko.read(os.path.join(obj, name))
+        ref = D.from_bytes(ko.read_desc(os.path.join(obj, name), m))
+        assert bytes(ref.p.itab) == bytes(d.p.itab), name
+        assert list(ref.arg_numel)[:ref.nargs] == list(d.arg_numel)[:d.nargs], name
+        assert list(ref.arg_dtype)[:ref.nargs] == list(d.arg_dtype)[:d.nargs], name

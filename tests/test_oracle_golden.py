@@ -73,6 +73,14 @@ def run_oracle(case, ins):
                                            o["experts"])
     if fam == "grouped_gemm":
         return outs[0], O.grouped_gemm(x[0], x[1], x[2], x[3], x[4], x[5], o["M"], o["N"], o["K"], o["groups"])
+    if fam == "cumsum_int":
+        dt = next(getattr(torch, a["dtype"]) for a in args if a["name"] == outs[0])
+        return outs[0], O.cumsum_int(x[0], o["n"], dt)
+    if fam == "slot_of":
+        return outs[0], O.slot_of(x[0], x[1], o["n"], o["experts"])
+    if fam == "count_le":
+        dt = next(getattr(torch, a["dtype"]) for a in args if a["name"] == outs[0])
+        return outs[0], O.count_le(x[0], o["n"], o["rows"], dt)
     if fam == "row_divsum":
         return outs[0], O.row_divsum(x[0], o["rows"], o["cols"])
     if fam == "dispatch_gather":
@@ -102,7 +110,7 @@ def run_oracle(case, ins):
 
 
 EXACT = {"vector_add", "add_one", "slice_add_one", "token_to_head_major", "heads_to_token_major", "topk", "sort",
-         "dispatch_gather"}
+         "dispatch_gather", "expert_counts", "cumsum_int", "slot_of", "group_tables", "count_le"}
 
 
 def run_oracle_all(case, ins):
@@ -117,6 +125,12 @@ def run_oracle_all(case, ins):
     if fam == "sort":
         v, i = O.sort_rows(x[0], o["rows"], o["cols"], o["descending"], o["float_keys"])
         return {outs[0]: v, outs[1]: i}
+    if fam == "expert_counts":
+        cnt, run = O.expert_counts(x[0], o["experts"], o["n"])
+        return {outs[0]: cnt, outs[1]: run}
+    if fam == "group_tables":
+        nonempty, prev, count = O.group_tables(x[0], o["n"])
+        return {outs[0]: nonempty, outs[1]: prev, outs[2]: count}
     name, got = run_oracle(case, ins)
     return {name: got}
 
