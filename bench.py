@@ -483,12 +483,13 @@ def suite(dev, stream, iters=5, only=None, warm=1):
         timed("moe_combine_t4096_03_weighted", "hbm", 2 * 32768 * 2048 + 2 * 4096 * 2048 + 8 * 3 * 32768,
               given={"in_ptr0": ids, "in_ptr1": cum, "in_ptr2": cnt, "in_ptr3": pos})
     # combine's routing tables: counts and running counts of 128 experts over 32768 routed ids (writes the
-    # [32768, 128] int64 running table), and each routed row's slot (reads that table once)
+    # [32768, 128] int64 running table), and each routed row's slot (the program sums the table row times a
+    # one-hot of the row's expert: the one selected element, its id and the output per row are what it needs)
     if only is None or only in ("moe_combine_t4096_00_counts", "moe_combine_t4096_02_slot"):
         ids = moe_routing(4096, 8, 128, 7)[0]
         timed("moe_combine_t4096_00_counts", "hbm", 8 * 32768 * 128 + 8 * 32768 + 8 * 128, given={"in_ptr0": ids})
         run_ = torch.randint(0, 300, (32768 * 128,), generator=torch.Generator().manual_seed(3))
-        timed("moe_combine_t4096_02_slot", "hbm", 8 * 32768 * 128 + 2 * 8 * 32768, given={"in_ptr0": run_, "in_ptr1": ids})
+        timed("moe_combine_t4096_02_slot", "hbm", 3 * 8 * 32768, given={"in_ptr0": run_, "in_ptr1": ids})
     for nm, K, N in (("moe_gmm_gate_up_t4096", 2048, 1536), ("moe_gmm_down_t4096", 768, 2048)):
         if only is None or only == nm:
             out[nm] = grouped_gemm_timing(dev, stream, iters, warm, flush, hbm, tflops, K, N)

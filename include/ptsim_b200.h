@@ -244,6 +244,10 @@ typedef struct ptsim_gsum_params {
  *   SCAN: f, the inclusive running total over r up to this element.
  * Integer arithmetic wraps at 64 bits.  Partition units are rows. */
 #define PTSIM_ITAB_MAPS 5
+/* desc->flags bit: run an INT_TABLE program on the element interpreter even where the library has a direct
+ * kernel for it (the one-hot count / running count of the combine's 00 program, the indexed select of its
+ * 02 program); the results are the same. */
+#define PTSIM_FLAG_INTERPRET 1u
 #define PTSIM_ITAB_OUTS 4
 #define PTSIM_ITAB_ELEM 0
 #define PTSIM_ITAB_SUM 1
@@ -268,7 +272,7 @@ typedef struct ptsim_desc {
   uint32_t magic;        /* PTSIM_DESC_MAGIC */
   uint32_t version;      /* PTSIM_ABI_VERSION */
   uint32_t kind;         /* PTSIM_KIND_* */
-  uint32_t flags;
+  uint32_t flags;        /* PTSIM_FLAG_* */
   int32_t nargs, pad0;
   int32_t arg_dtype[PTSIM_MAX_ARGS];
   int64_t arg_numel[PTSIM_MAX_ARGS];

@@ -122,6 +122,7 @@ class GsumParams(C.Structure):
 
 
 ITAB_MAPS, ITAB_OUTS = 5, 4
+FLAG_INTERPRET = 1   # desc.flags: INT_TABLE on the element interpreter only
 ITAB_MODE = {"elem": 0, "sum": 1, "scan": 2}
 ITAB_MODE_NAME = {v: k for k, v in ITAB_MODE.items()}
 

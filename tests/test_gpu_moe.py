@@ -235,14 +235,23 @@ def routed_ids(n, experts, seed, wild=False):
     return ids
 
 
+def interpreted(desc, on):
+    """`desc` with PTSIM_FLAG_INTERPRET set when `on` (the element interpreter instead of a direct kernel)."""
+    if on:
+        desc.flags |= D.FLAG_INTERPRET
+    return desc
+
+
+@pytest.mark.parametrize("interp", [False, True], ids=["direct", "interpreter"])
 @pytest.mark.parametrize("n,experts,wild", [(32768, 128, False), (1024, 128, True), (8, 128, False),
-                                            (5000, 16, True), (100000, 3, False), (1, 1, False)])
-def test_expert_counts(n, experts, wild):
-    """Counts and running counts: the unsplit path (short routed range) and the split one (a long range
-    over few experts: chunk totals through the workspace)."""
+                                            (5000, 16, True), (100000, 3, False), (1, 1, False), (3000, 1000, True),
+                                            (700, 45, True)])
+def test_expert_counts(n, experts, wild, interp):
+    """Counts and running counts: the direct one-hot kernels, and the interpreter's unsplit path (short
+    routed range) and split one (a long range over few experts: chunk totals through the workspace)."""
     ids = routed_ids(n, experts, n, wild)
-    cnt, run_ = run(B.expert_counts(n, experts), [ids, torch.zeros(experts, dtype=torch.int64),
-                                                  torch.zeros(n * experts, dtype=torch.int64)])[1:]
+    cnt, run_ = run(interpreted(B.expert_counts(n, experts), interp),
+                    [ids, torch.zeros(experts, dtype=torch.int64), torch.zeros(n * experts, dtype=torch.int64)])[1:]
     wc, wr = O.expert_counts(ids, experts, n)
     assert torch.equal(cnt, wc) and torch.equal(run_, wr)
 
@@ -259,12 +268,13 @@ def test_cumsum_int(n, in_dtype, out_dtype):
     assert torch.equal(got, O.cumsum_int(x, n, getattr(torch, out_dtype)))
 
 
+@pytest.mark.parametrize("interp", [False, True], ids=["direct", "interpreter"])
 @pytest.mark.parametrize("n,experts", [(32768, 128), (8, 128), (3000, 7)])
-def test_slot_of(n, experts):
+def test_slot_of(n, experts, interp):
     ids = routed_ids(n, experts, 7, wild=True)
     g = torch.Generator().manual_seed(8)
     running = torch.randint(-50, 50, (n * experts,), generator=g)
-    got = run(B.slot_of(n, experts), [running, ids, torch.zeros(n, dtype=torch.int64)])[2]
+    got = run(interpreted(B.slot_of(n, experts), interp), [running, ids, torch.zeros(n, dtype=torch.int64)])[2]
     assert torch.equal(got, O.slot_of(running, ids, n, experts))
 
 
@@ -299,11 +309,12 @@ def test_routing_chain_reproduces_the_routing():
     assert torch.equal(c0, cnt) and torch.equal(c1, cum) and torch.equal(s2, pos)
 
 
-def test_int_table_unit_ranges():
+@pytest.mark.parametrize("interp", [False, True], ids=["direct", "interpreter"])
+def test_int_table_unit_ranges(interp):
     """Rows launched in parts (the runtime's split of a launch over GPUs) give the whole launch's tables."""
     n, experts = 20000, 64
     ids = routed_ids(n, experts, 5)
-    d = D.to_bytes(B.expert_counts(n, experts))
+    d = D.to_bytes(interpreted(B.expert_counts(n, experts), interp))
     ts = [t.cuda() for t in (ids, torch.zeros(experts, dtype=torch.int64), torch.zeros(n * experts, dtype=torch.int64))]
     for lo, hi in ((0, 5), (5, 40), (40, 64)):
         RC.launch_tensors(d, ts, lo, hi)
@@ -320,3 +331,16 @@ def test_int_table_out_of_range_is_recorded():
     with pytest.raises(native.ExecutorError) as e:
         RC.launch_tensors(D.to_bytes(desc), ts)
     assert e.value.code == D.E_OOB
+
+
+def test_select_out_of_range_ids_report_like_the_interpreter():
+    """An id read past its tensor records PTSIM_E_OOB on both paths."""
+    n, experts = 16, 8
+    for interp in (False, True):
+        desc = interpreted(B.slot_of(n, experts), interp)
+        desc.arg_numel[1] = n - 1
+        ts = [torch.zeros(n * experts, dtype=torch.int64).cuda(), torch.zeros(n - 1, dtype=torch.int64).cuda(),
+              torch.zeros(n, dtype=torch.int64).cuda()]
+        with pytest.raises(native.ExecutorError) as e:
+            RC.launch_tensors(D.to_bytes(desc), ts)
+        assert e.value.code == D.E_OOB
