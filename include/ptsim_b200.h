@@ -137,12 +137,31 @@ typedef struct ptsim_qkrope_params {
   float eps, pad1;
 } ptsim_qkrope_params;
 
+/* A fused vector program: the M = 1 matmul's vector prologue and output epilogue, a whole-tensor reduction's
+ * operand.  Ops as the elementwise program's (PTSIM_OP_*, fp32 registers r0..r7), run for one index i: LOAD dst =
+ * widen(argument load[a].arg at load[a].offset + i * load[a].stride) (an element outside the argument
+ * records PTSIM_E_OOB and reads 0); the result is the last instruction's register.  An epilogue finds the
+ * dot product in r7 when it starts.  ncode 0: no program. */
+#define PTSIM_VPROG_LOADS 4
+#define PTSIM_VPROG_CODE 16
+typedef struct ptsim_vload {
+  int32_t arg, pad0;
+  int64_t offset, stride;
+} ptsim_vload;
+typedef struct ptsim_vprog {
+  int32_t ncode, nload;
+  ptsim_vload load[PTSIM_VPROG_LOADS];
+  ptsim_insn code[PTSIM_VPROG_CODE];
+} ptsim_vprog;
+
 typedef struct ptsim_gemm_params {
   int64_t M, N, K;
   int64_t lda, ldb, ldc, ldr;  /* row strides in elements: A [M,K] row-major; B [K,N] or [N,K]; C, R [M,N] */
   int32_t a_arg, b_arg, c_arg, r_arg;  /* r_arg: residual added before the store, -1 when absent */
   int32_t b_kmajor;            /* 0: B is [K,N] with N contiguous (the Inductor mm layout); 1: B is [N,K] */
   int32_t pad0;
+  ptsim_vprog pro;             /* M = 1, [K,N] B: the vector is this program over k (a_arg unread) */
+  ptsim_vprog epi;             /* M = 1: out[n] = this program over n, the dot product in r7 (r_arg -1) */
 } ptsim_gemm_params;
 
 /* ATTN_PREFILL: q, o [batch, hq, seq, dim]; k, v [batch, hkv, seq, dim].
@@ -266,6 +285,7 @@ typedef struct ptsim_itab_params {
 typedef struct ptsim_reduce_params {
   int64_t numel;
   int32_t in_arg, out_arg, op, pad0;
+  ptsim_vprog pro;             /* the reduced operand as this program over the element index (in_arg unread) */
 } ptsim_reduce_params;
 
 typedef struct ptsim_desc {

@@ -336,6 +336,36 @@ def grouped_gemm(a, b, group, start, rows, c_init, M, N, K, groups):
     return out.reshape(-1)
 
 
+def sumsq(x, n, res=None):
+    """qwen3_8b_layer_decode_*/00_*_triton.py (and 05_*, with a residual row added first, unrounded): one fp32
+    value, the sum over the n elements of (x (+ res))^2."""
+    v = f32(x).reshape(-1)[:n]
+    if res is not None:
+        v = v + f32(res).reshape(-1)[:n]
+    return (v * v).sum().reshape(1)
+
+
+def rmsnorm_gemv(x, ss, w, mat, K, N, eps, res=None, out_dtype=torch.bfloat16):
+    """qwen3_8b_layer_decode_*/01_*_triton.py (and 06_*, with a residual row added first): the RMSNorm'd vector
+    v = (x (+ res)) * rsqrt(ss / K + eps) * w in fp32, never rounded to bf16, times the [K, N] matrix (fp32
+    accumulation), cast on the store; ss is the fp32 sum of squares the previous program stored."""
+    v = f32(x).reshape(-1)[:K]
+    if res is not None:
+        v = v + f32(res).reshape(-1)[:K]
+    v = (v * torch.rsqrt(f32(ss).reshape(-1)[0] / K + eps)) * f32(w).reshape(-1)[:K]
+    return (v @ f32(mat).view(K, N)).to(out_dtype)
+
+
+def silu_gemv(gate_up, mat, res1, res2, K, N, out_dtype=torch.bfloat16):
+    """qwen3_8b_layer_decode_*/07_*_triton.py: v = silu(gate) * up over the [gate | up] row (gate / (1 + exp(-gate))
+    in fp32, unrounded), out = v . [K, N] matrix + (res1 + res2), cast on the store."""
+    gu = f32(gate_up).reshape(-1)
+    g, u = gu[:K], gu[K:2 * K]
+    v = (g / (npu_exp(-g) + 1.0)) * u
+    acc = v @ f32(mat).view(K, N)
+    return (acc + (f32(res1).reshape(-1)[:N] + f32(res2).reshape(-1)[:N])).to(out_dtype)
+
+
 def rope_tables(tokens, dim=128, theta=1.0e6):
     """cos/sin tables [tokens, dim] in fp32 for RoPE with base `theta` (the Qwen3 layer feeds them as the
     fp32 inputs in_ptr2/in_ptr3 of 02/04)."""

@@ -11,13 +11,21 @@
 // the S partial columns in rank order through distributed shared memory -- a fixed summation order and
 // no device scratch.
 // K-major B ([N, K]): one warp per output column, 16-byte loads along K, a shuffle tree.
+//
+// Fused forms (the Qwen3 decode layer's programs, validation/pytorchsim/qwen3_8b_layer_decode_*/01_*, 06_*,
+// 07_*): a vector prologue (ptsim_vprog over k: an RMSNorm x * rsqrt(ss / n + eps) * w, a SiLU gate times
+// its up half) is evaluated once per CTA for its K slice into shared memory in fp32, unrounded, as the
+// programs keep it; an epilogue (over n, the dot product in r7) adds residual rows before the store.
 #pragma once
 #include "sm100.cuh"
+#include "vprog.cuh"
 
 namespace ptsim {
 
 constexpr int kGemvThreads = 256;
 constexpr int kGemvUnroll = 8;
+
+constexpr int kGemvMaxVecBytes = 160 * 1024;   // shared-memory vector slice of a prologue launch
 
 struct GemvArgs {
   const uint16_t *a, *b, *r;   // a [K]; B; residual [N] or null
@@ -25,6 +33,8 @@ struct GemvArgs {
   float *c_f32;                // fp32 output, or null
   int64_t N, K, ldb;
   int64_t k_per_cta;           // K rows per CTA of a cluster
+  ptsim_vprog pro, epi;        // fused vector prologue / output epilogue (ncode 0: none)
+  VArgs t;
 };
 
 __device__ __forceinline__ void gemv_fma8(float (&acc)[8], float a, const uint4 &v) {
@@ -38,23 +48,33 @@ __device__ __forceinline__ void gemv_fma8(float (&acc)[8], float a, const uint4 
   acc[7] = fmaf(a, hi_bf16(v.w), acc[7]);
 }
 
+// The epilogue out of line: the plain kernels keep their registers for the stream.
+__device__ __noinline__ float gemv_epilogue(const GemvArgs &g, int64_t n, float s) { return vprog_eval(g.epi, g.t, n, s); }
+
 __device__ __forceinline__ void gemv_store(const GemvArgs &g, int64_t n, float s) {
-  if (g.r != nullptr) s += bf16_bits_to_f32(g.r[n]);
+  if (g.epi.ncode > 0) s = gemv_epilogue(g, n, s);
+  else if (g.r != nullptr) s += bf16_bits_to_f32(g.r[n]);
   if (g.c_f32 != nullptr) g.c_f32[n] = s;
   else g.c[n] = f32_to_bf16_bits(s);
 }
 
 // TPRW threads per row of the tile (CW = 8 * TPRW columns); grid (column tiles, S) in clusters (1, S, 1).
-template <int TPRW>
+// PRO: the vector comes from the prologue, staged for the CTA's K slice in dynamic shared memory.
+template <int TPRW, bool PRO>
 __global__ void __launch_bounds__(kGemvThreads) gemv_kn_kernel(const __grid_constant__ GemvArgs g) {
   constexpr int CW = TPRW * 8, RG = kGemvThreads / TPRW, U = kGemvUnroll;
   __shared__ float red[RG][CW];
   __shared__ float part[CW];
+  extern __shared__ float vec[];
   const int tid = threadIdx.x;
   const int cg = tid % TPRW, rg = tid / TPRW;
   const int64_t n0 = int64_t(blockIdx.x) * CW + cg * 8;
   const int64_t k_begin = int64_t(blockIdx.y) * g.k_per_cta;
   const int64_t k_end = k_begin + g.k_per_cta < g.K ? k_begin + g.k_per_cta : g.K;
+  if (PRO) {
+    for (int64_t k = k_begin + tid; k < k_end; k += kGemvThreads) vec[k - k_begin] = vprog_eval(g.pro, g.t, k, 0.f);
+    __syncthreads();
+  }
   float acc[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) acc[j] = 0.f;
@@ -67,14 +87,14 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kn_kernel(const __grid_cons
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         v[u] = __ldcs(reinterpret_cast<const uint4 *>(bp + (k + u * RG) * g.ldb));
-        av[u] = bf16_bits_to_f32(__ldg(g.a + k + u * RG));
+        av[u] = PRO ? vec[k + u * RG - k_begin] : bf16_bits_to_f32(__ldg(g.a + k + u * RG));
       }
 #pragma unroll
       for (int u = 0; u < U; ++u) gemv_fma8(acc, av[u], v[u]);
     }
     for (; k < k_end; k += RG) {
       const uint4 v = __ldcs(reinterpret_cast<const uint4 *>(bp + k * g.ldb));
-      gemv_fma8(acc, bf16_bits_to_f32(__ldg(g.a + k)), v);
+      gemv_fma8(acc, PRO ? vec[k - k_begin] : bf16_bits_to_f32(__ldg(g.a + k)), v);
     }
   }
 #pragma unroll
@@ -167,12 +187,14 @@ static GemvPlan plan_gemv(int64_t N, int64_t K, int sm_count) {
   return pl;
 }
 
-template <int TPRW>
+template <int TPRW, bool PRO>
 static int run_gemv_kn(const GemvArgs &g, const GemvPlan &pl, const LaunchCtx &c) {
+  const int vec_bytes = PRO ? int(pl.k_per_cta * int64_t(sizeof(float))) : 0;
+  if (PRO) PTSIM_CUDA((smem_limit_once<gemv_kn_kernel<TPRW, true>>(kGemvMaxVecBytes, c.device)));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(pl.tiles), unsigned(pl.splits), 1);
   cfg.blockDim = dim3(kGemvThreads, 1, 1);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = size_t(vec_bytes);
   cfg.stream = c.stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -181,7 +203,7 @@ static int run_gemv_kn(const GemvArgs &g, const GemvPlan &pl, const LaunchCtx &c
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  PTSIM_CUDA(cudaLaunchKernelEx(&cfg, gemv_kn_kernel<TPRW>, g));
+  PTSIM_CUDA(cudaLaunchKernelEx(&cfg, gemv_kn_kernel<TPRW, PRO>, g));
   return PTSIM_OK;
 }
 
@@ -198,8 +220,13 @@ static int launch_gemv(const ptsim_desc &d, void *const *ptrs, const LaunchCtx &
   g.N = p.N;
   g.K = p.K;
   g.ldb = p.ldb;
+  g.pro = p.pro;
+  g.epi = p.epi;
+  vargs_fill(g.t, d, ptrs);
+  const bool pro = p.pro.ncode > 0;
   if (reinterpret_cast<uintptr_t>(g.b) % 16 != 0) return fail(PTSIM_E_ARGS, "GEMV matrix is not 16-byte aligned");
   if (p.b_kmajor) {
+    if (pro) return fail(PTSIM_E_UNSUPPORTED, "a GEMV vector prologue over an [N, K] matrix");
     if (p.K % 8 != 0 || p.ldb % 8 != 0 || reinterpret_cast<uintptr_t>(g.a) % 16 != 0)
       return fail(PTSIM_E_UNSUPPORTED, "GEMV over [N, K] needs K and the row stride multiples of 8 and a 16-byte aligned vector");
     const int64_t blocks = ceil_div(p.N, kGemvThreads / 32);
@@ -211,9 +238,16 @@ static int launch_gemv(const ptsim_desc &d, void *const *ptrs, const LaunchCtx &
     return fail(PTSIM_E_UNSUPPORTED, "GEMV over [K, N] needs N and the row stride multiples of 8");
   const GemvPlan pl = plan_gemv(p.N, p.K, c.sm_count);
   g.k_per_cta = pl.k_per_cta;
-  if (pl.tprw == 32) return run_gemv_kn<32>(g, pl, c);
-  if (pl.tprw == 16) return run_gemv_kn<16>(g, pl, c);
-  return run_gemv_kn<8>(g, pl, c);
+  if (pro) {
+    if (pl.k_per_cta * int64_t(sizeof(float)) > kGemvMaxVecBytes)
+      return fail(PTSIM_E_UNSUPPORTED, "a GEMV vector prologue over %lld rows per CTA", (long long)pl.k_per_cta);
+    if (pl.tprw == 32) return run_gemv_kn<32, true>(g, pl, c);
+    if (pl.tprw == 16) return run_gemv_kn<16, true>(g, pl, c);
+    return run_gemv_kn<8, true>(g, pl, c);
+  }
+  if (pl.tprw == 32) return run_gemv_kn<32, false>(g, pl, c);
+  if (pl.tprw == 16) return run_gemv_kn<16, false>(g, pl, c);
+  return run_gemv_kn<8, false>(g, pl, c);
 }
 
 }  // namespace ptsim

@@ -70,6 +70,27 @@ static int64_t map_max_index(const ptsim_map &m, int64_t numel) {
   return hi;
 }
 
+// A fused vector program: opcodes, registers, load slots and their arguments.
+static int check_vprog(const ptsim_desc &d, const ptsim_vprog &v, const char *what) {
+  if (v.ncode == 0) return PTSIM_OK;
+  if (v.ncode < 0 || v.ncode > PTSIM_VPROG_CODE || v.nload < 0 || v.nload > PTSIM_VPROG_LOADS)
+    return fail(PTSIM_E_DESC, "%s of %d instructions and %d loads", what, v.ncode, v.nload);
+  for (int l = 0; l < v.nload; ++l) {
+    int rc = check_arg(d, v.load[l].arg, what);
+    if (rc) return rc;
+    const int dt = d.arg_dtype[v.load[l].arg];
+    if (dt != PTSIM_DT_F32 && dt != PTSIM_DT_BF16 && dt != PTSIM_DT_F16)
+      return fail(PTSIM_E_UNSUPPORTED, "%s loads a non-floating argument %d", what, v.load[l].arg);
+  }
+  for (int i = 0; i < v.ncode; ++i) {
+    const ptsim_insn &c = v.code[i];
+    if (c.op < PTSIM_OP_LOAD || c.op >= PTSIM_OP_STORE || c.dst >= 8 || c.b >= 8 ||
+        (c.op == PTSIM_OP_LOAD ? c.a >= v.nload : c.a >= 8))
+      return fail(PTSIM_E_DESC, "%s instruction %d", what, i);
+  }
+  return PTSIM_OK;
+}
+
 static int check_desc(const void *p, size_t bytes) {
   if (p == nullptr || bytes < sizeof(ptsim_desc))
     return fail(PTSIM_E_DESC, "descriptor of %zu bytes; this library reads %zu", bytes, sizeof(ptsim_desc));
@@ -146,9 +167,13 @@ static int check_desc(const void *p, size_t bytes) {
       if ((rc = check_arg(d, g.a_arg, "A")) || (rc = check_arg(d, g.b_arg, "B")) || (rc = check_arg(d, g.c_arg, "C"))) return rc;
       if (g.r_arg >= 0 && (rc = check_arg(d, g.r_arg, "residual"))) return rc;
       if (g.M < 0 || g.N < 1 || g.K < 1) return fail(PTSIM_E_DESC, "GEMM %lldx%lldx%lld", (long long)g.M, (long long)g.N, (long long)g.K);
+      if ((g.pro.ncode != 0 || g.epi.ncode != 0) && g.M != 1)
+        return fail(PTSIM_E_DESC, "a fused vector prologue or epilogue on a GEMM of M = %lld", (long long)g.M);
+      if ((rc = check_vprog(d, g.pro, "GEMV prologue")) || (rc = check_vprog(d, g.epi, "GEMV epilogue"))) return rc;
       if (g.M > 0) {
         const int64_t b_need = g.b_kmajor ? (g.N - 1) * g.ldb + g.K : (g.K - 1) * g.ldb + g.N;
-        if ((g.M - 1) * g.lda + g.K > d.arg_numel[g.a_arg] || b_need > d.arg_numel[g.b_arg] ||
+        const int64_t a_need = g.pro.ncode > 0 ? 0 : (g.M - 1) * g.lda + g.K;
+        if (a_need > d.arg_numel[g.a_arg] || b_need > d.arg_numel[g.b_arg] ||
             (g.M - 1) * g.ldc + g.N > d.arg_numel[g.c_arg] || (g.r_arg >= 0 && (g.M - 1) * g.ldr + g.N > d.arg_numel[g.r_arg]))
           return fail(PTSIM_E_OOB, "GEMM operands extend past their tensors");
       }
@@ -288,7 +313,9 @@ static int check_desc(const void *p, size_t bytes) {
     case PTSIM_KIND_REDUCE_ALL: {
       const ptsim_reduce_params &r = d.p.red;
       if ((rc = check_arg(d, r.in_arg, "reduce input")) || (rc = check_arg(d, r.out_arg, "reduce output"))) return rc;
-      if (r.numel > d.arg_numel[r.in_arg] || d.arg_numel[r.out_arg] < 1) return fail(PTSIM_E_OOB, "reduction past its tensors");
+      if ((rc = check_vprog(d, r.pro, "reduction operand"))) return rc;
+      if ((r.pro.ncode == 0 && r.numel > d.arg_numel[r.in_arg]) || d.arg_numel[r.out_arg] < 1)
+        return fail(PTSIM_E_OOB, "reduction past its tensors");
       break;
     }
     default:

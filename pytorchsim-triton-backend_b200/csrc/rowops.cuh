@@ -13,6 +13,7 @@
 #pragma once
 #include "common.cuh"
 #include "sm100.cuh"
+#include "vprog.cuh"
 
 namespace ptsim {
 
@@ -572,6 +573,28 @@ __global__ void __launch_bounds__(kReduceThreads) reduce_pass1(const void *in, i
   if (threadIdx.x == 0) partials[blockIdx.x] = acc;
 }
 
+// Pass 1 over a fused operand (the decode layer's sums of squares, qwen3_8b_layer_decode_*/00_*, 05_*:
+// x^2 or (x + residual)^2 per element, fp32 unrounded).
+struct ReduceProgArgs {
+  ptsim_vprog pro;
+  VArgs t;
+  int64_t numel;
+  float *partials;
+};
+
+template <bool IS_MAX>
+__global__ void __launch_bounds__(kReduceThreads) reduce_pass1_prog(const __grid_constant__ ReduceProgArgs a) {
+  __shared__ float sh[32];
+  float acc = IS_MAX ? -INFINITY : 0.f;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < a.numel; i += stride) {
+    const float x = vprog_eval(a.pro, a.t, i, 0.f);
+    acc = IS_MAX ? nan_max(acc, x) : __fadd_rn(acc, x);
+  }
+  acc = block_reduce<IS_MAX>(acc, sh);
+  if (threadIdx.x == 0) a.partials[blockIdx.x] = acc;
+}
+
 template <bool IS_MAX>
 __global__ void __launch_bounds__(kReduceThreads) reduce_pass2(const float *partials, int n, float *out) {
   __shared__ float sh[32];
@@ -599,6 +622,23 @@ int launch_reduce(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi
   float *out = reinterpret_cast<float *>(ptrs[p.out_arg]);
   if (d.arg_dtype[p.out_arg] != PTSIM_DT_F32) return fail(PTSIM_E_UNSUPPORTED, "reduction output must be float32");
   const int dt = d.arg_dtype[p.in_arg];
+  if (p.pro.ncode > 0) {
+    ReduceProgArgs a;
+    memset(&a, 0, sizeof(a));
+    a.pro = p.pro;
+    vargs_fill(a.t, d, ptrs);
+    a.numel = p.numel;
+    a.partials = partials;
+    if (p.op == PTSIM_RED_MAX) {
+      reduce_pass1_prog<true><<<blocks, kReduceThreads, 0, c.stream>>>(a);
+      reduce_pass2<true><<<1, kReduceThreads, 0, c.stream>>>(partials, blocks, out);
+    } else {
+      reduce_pass1_prog<false><<<blocks, kReduceThreads, 0, c.stream>>>(a);
+      reduce_pass2<false><<<1, kReduceThreads, 0, c.stream>>>(partials, blocks, out);
+    }
+    PTSIM_CUDA(cudaGetLastError());
+    return PTSIM_OK;
+  }
   if (p.op == PTSIM_RED_MAX) {
     reduce_pass1<true><<<blocks, kReduceThreads, 0, c.stream>>>(ptrs[p.in_arg], dt, 0, p.numel, partials);
     reduce_pass2<true><<<1, kReduceThreads, 0, c.stream>>>(partials, blocks, out);

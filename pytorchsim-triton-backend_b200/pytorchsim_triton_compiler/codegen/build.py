@@ -106,6 +106,85 @@ def gemv(N, K, b_kmajor=False, residual=False, out_dtype="bfloat16"):
     return gemm(1, N, K, residual=residual, b_kmajor=b_kmajor, out_dtype=out_dtype)
 
 
+class _Shapes:
+    """The name and argument dtypes a fused-program generator reads of a kernel spec."""
+
+    class _Arg:
+        def __init__(self, dtype):
+            self.dtype = dtype
+
+    def __init__(self, name, dtypes):
+        self.name, self.args = name, [self._Arg(dt) for dt in dtypes]
+
+
+def _fused_gemv(name, specs, N, K, vec, epi=None, red=None):
+    """An M = 1 matmul descriptor over argument `specs` whose vector is expression `vec` (front-end nodes over
+    r) and, when given, whose stored value is `epi` with `red` standing for the sum: the programs are the
+    ones the lowering emits for the same expressions (targets/b200/lower.py _vprog)."""
+    from ..targets.b200 import lower as L
+    shapes = _Shapes(name, [dt for _, dt, _ in specs])
+    mat = next(i for i, (n, _, _) in enumerate(specs) if n == "mat")
+    out = len(specs) - 1
+    d = D.new(D.GEMM, _args(specs), (1, 1, 1), units=1, unit_size=1)
+    g = d.p.gemm
+    g.M, g.N, g.K = 1, N, K
+    g.lda, g.ldb, g.ldc, g.ldr = K, N, N, N
+    g.b_arg, g.c_arg, g.r_arg, g.b_kmajor = mat, out, -1, 0
+    g.pro = L._vprog(shapes, vec, "r")
+    g.a_arg = g.pro.load[0].arg
+    if epi is not None:
+        g.epi = L._vprog(shapes, epi, "x", acc=red)
+    return d
+
+
+def rmsnorm_gemv(N, K, eps=1e-6, residual=False):
+    """The Qwen3 decode layer's RMSNorm'd matrix-vector product (qwen3_8b_layer_decode_*/01_*, 06_* with the
+    residual row): out[n] = sum_k ((x[k] (+ res[k])) * rsqrt(ss / K + eps) * w[k]) * B[k, n], the vector in
+    fp32; arguments x, (res,) ss (fp32 [1]), w, mat [K, N], out (bf16)."""
+    from ..targets.b200 import frontend as F
+    r = F.Index.var("r")
+    specs = [("x", "bfloat16", K)] + ([("res", "bfloat16", K)] if residual else []) + \
+        [("ss", "float32", 1), ("w", "bfloat16", K), ("mat", "bfloat16", K * N), ("out", "bfloat16", N)]
+    i = {n: k for k, (n, _, _) in enumerate(specs)}
+    x = F.Load(i["x"], r)
+    if residual:
+        x = F.Op("add", x, F.Load(i["res"], r))
+    scale = F.Op("rsqrt", F.Op("add", F.Op("div", F.Load(i["ss"], F.Index()), F.Const(K)), F.Const(eps)))
+    return _fused_gemv("rmsnorm_gemv", specs, N, K, F.Op("mul", F.Op("mul", x, scale), F.Load(i["w"], r)))
+
+
+def silu_gemv(N, K):
+    """The Qwen3 decode layer's down projection (qwen3_8b_layer_decode_*/07_*): out[n] = sum_k (silu(gu[k]) *
+    gu[K + k]) * B[k, n] + (res1[n] + res2[n]); arguments gu [2K], mat [K, N], res1, res2, out (bf16)."""
+    from ..targets.b200 import frontend as F
+    r, x = F.Index.var("r"), F.Index.var("x")
+    specs = [("gu", "bfloat16", 2 * K), ("mat", "bfloat16", K * N), ("res1", "bfloat16", N), ("res2", "bfloat16", N),
+             ("out", "bfloat16", N)]
+    gate = F.Load(0, r)
+    silu = F.Op("div", gate, F.Op("add", F.Op("exp", F.Op("neg", gate)), F.Const(1.0)))
+    vec = F.Op("mul", silu, F.Load(0, r + K))
+    red = F.Reduce("add", F.Const(0.0))
+    epi = F.Op("add", red, F.Op("add", F.Load(2, x), F.Load(3, x)))
+    return _fused_gemv("silu_gemv", specs, N, K, vec, epi, red)
+
+
+def sumsq(n, residual=False):
+    """A sum of squares (qwen3_8b_layer_decode_*/00_*, 05_* with the residual row): out = sum (x (+ res))^2 in
+    fp32; arguments x, (res,) out (fp32 [1])."""
+    from ..targets.b200 import frontend as F
+    from ..targets.b200 import lower as L
+    r = F.Index.var("r")
+    specs = [("x", "bfloat16", n)] + ([("res", "bfloat16", n)] if residual else []) + [("out", "float32", 1)]
+    v = F.Load(0, r)
+    if residual:
+        v = F.Op("add", v, F.Load(1, r))
+    d = D.new(D.REDUCE_ALL, _args(specs), [1], units=1, unit_size=1, workspace_bytes=D.REDUCE_WORKSPACE_BYTES)
+    q = d.p.red
+    q.pro = L._vprog(_Shapes("sumsq", [dt for _, dt, _ in specs]), F.Op("mul", v, v), "r")
+    q.numel, q.in_arg, q.out_arg, q.op = n, 0, len(specs) - 1, D.RED_SUM
+    return d
+
+
 def topk(rows, cols, k, largest=True, cols_padded=None, dtype="float32"):
     """The MoE router's _topk_kernel (validation/pytorchsim/layer_op_router_post_*/01__topk_kernel): per row of
     `cols` values, the k largest (or smallest) with their column indices."""

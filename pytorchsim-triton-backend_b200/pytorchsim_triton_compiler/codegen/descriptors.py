@@ -46,6 +46,19 @@ class Insn(C.Structure):
     _fields_ = [("op", C.c_uint8), ("dst", C.c_uint8), ("a", C.c_uint8), ("b", C.c_uint8), ("imm", C.c_float)]
 
 
+VPROG_LOADS, VPROG_CODE = 4, 16
+
+
+class VLoad(C.Structure):
+    _fields_ = [("arg", C.c_int32), ("pad0", C.c_int32), ("offset", C.c_int64), ("stride", C.c_int64)]
+
+
+class VProg(C.Structure):
+    """ptsim_vprog: a fused fp32 program over one index (the M = 1 matmul's prologue / epilogue, a reduction's
+    operand)."""
+    _fields_ = [("ncode", C.c_int32), ("nload", C.c_int32), ("load", VLoad * VPROG_LOADS), ("code", Insn * VPROG_CODE)]
+
+
 class EwParams(C.Structure):
     _fields_ = [("numel", C.c_int64), ("nmap", C.c_int32), ("ncode", C.c_int32), ("store_map", C.c_int32),
                 ("pure_copy", C.c_int32), ("map", Map * MAX_MAPS), ("code", Insn * MAX_CODE)]
@@ -67,7 +80,8 @@ class QkParams(C.Structure):
 class GemmParams(C.Structure):
     _fields_ = [("M", C.c_int64), ("N", C.c_int64), ("K", C.c_int64), ("lda", C.c_int64), ("ldb", C.c_int64),
                 ("ldc", C.c_int64), ("ldr", C.c_int64), ("a_arg", C.c_int32), ("b_arg", C.c_int32),
-                ("c_arg", C.c_int32), ("r_arg", C.c_int32), ("b_kmajor", C.c_int32), ("pad0", C.c_int32)]
+                ("c_arg", C.c_int32), ("r_arg", C.c_int32), ("b_kmajor", C.c_int32), ("pad0", C.c_int32),
+                ("pro", VProg), ("epi", VProg)]
 
 
 class AttnParams(C.Structure):
@@ -79,7 +93,7 @@ class AttnParams(C.Structure):
 
 class ReduceParams(C.Structure):
     _fields_ = [("numel", C.c_int64), ("in_arg", C.c_int32), ("out_arg", C.c_int32), ("op", C.c_int32),
-                ("pad0", C.c_int32)]
+                ("pad0", C.c_int32), ("pro", VProg)]
 
 
 class SelectParams(C.Structure):
@@ -188,6 +202,11 @@ def from_bytes(blob):
     return d
 
 
+def describe_vprog(v):
+    return {"loads": [(l.arg, l.offset, l.stride) for l in list(v.load)[:v.nload]],
+            "code": [(OP_NAME.get(i.op, i.op), i.dst, i.a, i.b, i.imm) for i in list(v.code)[:v.ncode]]}
+
+
 def describe(d):
     """A JSON-able summary of descriptor `d` (what kernel.json records next to the blob)."""
     out = {"kind": KIND_NAME.get(d.kind, d.kind), "units": d.units, "unit_size": d.unit_size,
@@ -210,6 +229,9 @@ def describe(d):
     elif d.kind == GEMM:
         g = d.p.gemm
         out.update(M=g.M, N=g.N, K=g.K, residual=g.r_arg >= 0, b_kmajor=bool(g.b_kmajor))
+        for nm in ("pro", "epi"):
+            if getattr(g, nm).ncode:
+                out[nm] = describe_vprog(getattr(g, nm))
     elif d.kind == ATTN_PREFILL:
         a = d.p.attn
         out.update(batch=a.batch, hq=a.hq, hkv=a.hkv, seq=a.seq, dim=a.dim, causal=bool(a.causal), scale=a.scale)
@@ -244,4 +266,6 @@ def describe(d):
                    program=[(IOP_NAME.get(i.op, i.op), i.dst, i.a, i.b, i.c, i.imm) for i in list(q.code)[:q.ncode]])
     elif d.kind == REDUCE_ALL:
         out.update(numel=d.p.red.numel, op="max" if d.p.red.op == RED_MAX else "sum")
+        if d.p.red.pro.ncode:
+            out["pro"] = describe_vprog(d.p.red.pro)
     return out

@@ -168,14 +168,14 @@ def lower(spec, fn=None):
     args = {l.arg for l in loads}
     if not st.index.terms:
         return _lower_reduce_all(spec, prog, st, reduces)
+    if _gemv_parts(st, reduces) is not None:
+        return _lower_gemv(spec, prog, st, reduces[0])
     if "where" in ops and "rsqrt" in ops:
         return _lower_qknorm_rope(spec, prog, st, loads)
     if "rsqrt" in ops and len(args) == 2:
         return _lower_rmsnorm(spec, prog, st, loads)
     if "exp" in ops and {r.op for r in reduces} == {"max", "add"} and len(args) == 1:
         return _lower_softmax(spec, prog, st, reduces)
-    if ops == {"mul"} and len(reduces) == 1 and reduces[0].op == "add" and len(args) == 2:
-        return _lower_gemv(spec, prog, st, reduces[0])
     if ops == {"div"} and len(reduces) == 1 and reduces[0].op == "add" and len(args) == 1:
         return _lower_divsum(spec, prog, st, reduces[0])
     raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a reduction program of ops {sorted(ops)}")
@@ -415,22 +415,36 @@ def _lower_qknorm_rope(spec, prog, st, loads):
     return Lowered(d, D.describe(d))
 
 
+def _gemv_parts(st, reduces):
+    """(vector, matrix) of a matrix-vector program: one sum over r of vector * matrix, the matrix a load over x
+    and r, every load of the vector over r alone (or a fixed element), stored at x; else None."""
+    if len(reduces) != 1 or reduces[0].op != "add" or st.index.const != 0 or st.index.terms != {F.Digit("x"): 1}:
+        return None
+    prod = reduces[0].value
+    if not (isinstance(prod, F.Op) and prod.name == "mul" and len(prod.args) == 2):
+        return None
+    for mat, vec in ((prod.args[1], prod.args[0]), (prod.args[0], prod.args[1])):
+        if not (isinstance(mat, F.Load) and mat.index.vars() == {"x", "r"} and mat.mask is None and mat.data is None):
+            continue
+        vloads = [n for n in walk(vec) if isinstance(n, F.Load)]
+        if vloads and all(l.index.vars() <= {"r"} for l in vloads) and not any(
+                isinstance(n, (F.Reduce, F.Dot)) for n in walk(vec)):
+            return vec, mat
+    return None
+
+
 def _lower_gemv(spec, prog, st, red):
     """Inductor's M = 1 matmul (validation/pytorchsim/gemm_1x*/00_*_triton.py): out[x] = sum over r of
     fp32(a[r]) * fp32(B[x + N * r]), one reduction over r, cast on the store.  The reference refuses M = 1
     on its MXU (targets/tpu/lower_matmul.py:464-489) and runs it on the vector unit; lowered here to a
-    GEMM descriptor with M = 1, which the executor runs on its matrix-vector path."""
+    GEMM descriptor with M = 1, which the executor runs on its matrix-vector path.
+
+    Fused forms (validation/pytorchsim/qwen3_8b_layer_decode_*/01_*, 06_*, 07_*): the vector may be any fp32
+    expression of loads over r (an RMSNorm x * rsqrt(ss / n + eps) * w, silu(gate) * up), kept unrounded as
+    the program keeps it -- a prologue program; the store may add loads over x to the sum (residual rows) --
+    an epilogue program with the sum in r7."""
     n, k, _ = _row_sizes(spec, prog, "matrix-vector product")
-    prod = red.value
-    if not (isinstance(prod, F.Op) and prod.name == "mul" and all(isinstance(a, F.Load) for a in prod.args)):
-        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: the reduced value is not a product of two loads")
-    vec = [a for a in prod.args if a.index.vars() == {"r"}]
-    mat = [a for a in prod.args if a.index.vars() == {"x", "r"}]
-    if len(vec) != 1 or len(mat) != 1:
-        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: not a vector (over r) times a matrix (over x, r)")
-    vec, mat = vec[0], mat[0]
-    if vec.index.const != 0 or vec.index.terms != {F.Digit("r"): 1}:
-        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: vector index {vec.index} is not r")
+    vec, mat = _gemv_parts(st, [red])
     rk, xn = mat.index.coeff_of("r"), mat.index.coeff_of("x")
     if mat.index.const != 0 or set(rk) != {F.Digit("r")} or set(xn) != {F.Digit("x")}:
         raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: matrix index {mat.index} is not x * s + r * t")
@@ -441,18 +455,121 @@ def _lower_gemv(spec, prog, st, red):
         b_kmajor, ldb = 1, sn
     else:
         raise Refused(Reason.SHAPE_NOT_RUN, f"{spec.name}: matrix with strides ({sk}, {sn})")
-    if st.index.const != 0 or st.index.terms != {F.Digit("x"): 1}:
-        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: store index {st.index} is not x")
-    for t, nm in ((vec.arg, "vector"), (mat.arg, "matrix")):
-        if spec.args[t].dtype != "bfloat16":
-            raise Refused(Reason.DTYPE_NOT_RUN, f"{spec.name}: {nm} operand is {spec.args[t].dtype}")
+    if spec.args[mat.arg].dtype != "bfloat16":
+        raise Refused(Reason.DTYPE_NOT_RUN, f"{spec.name}: matrix operand is {spec.args[mat.arg].dtype}")
+    plain = isinstance(vec, F.Load) and vec.index.const == 0 and vec.index.terms == {F.Digit("r"): 1} \
+        and vec.mask is None and spec.args[vec.arg].dtype == "bfloat16"
     d = D.new(D.GEMM, _manifest_args(spec), spec.grid, units=1, unit_size=1)
     g = d.p.gemm
     g.M, g.N, g.K = 1, n, k
     g.lda, g.ldb, g.ldc, g.ldr = k, ldb, n, n
-    g.a_arg, g.b_arg, g.c_arg, g.r_arg = vec.arg, mat.arg, st.arg, -1
+    g.c_arg, g.r_arg = st.arg, -1
+    g.b_arg = mat.arg
     g.b_kmajor = b_kmajor
+    if plain:
+        g.a_arg = vec.arg
+    else:
+        if b_kmajor:
+            raise Refused(Reason.SHAPE_NOT_RUN, f"{spec.name}: a fused vector over an [N, K] matrix")
+        g.pro = _vprog(spec, vec, "r")
+        g.a_arg = g.pro.load[0].arg if g.pro.nload else mat.arg
+    if st.value is not red:
+        if sum(1 for x in walk(st.value) if x is red) != 1:
+            raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: the stored value uses the sum twice")
+        g.epi = _vprog(spec, st.value, "x", acc=red)
     return Lowered(d, D.describe(d))
+
+
+def _vprog(spec, root, var, acc=None):
+    """The fused vector program (ptsim_vprog) of fp32 expression `root` over the one index `var` ('r': a
+    matrix-vector prologue or a reduction's operand; 'x': an epilogue, with `acc` -- the reduction -- in r7):
+    loads at offset + var * stride (or a fixed element), the elementwise op set, registers r0..r6 allocated
+    over the DAG (a value's register is freed after its last use)."""
+    v = D.VProg()
+    loads, code = [], []
+    uses = {}
+    for n in walk(root):
+        for a in (n.args if isinstance(n, F.Op) else ()):
+            if isinstance(a, F.Node):
+                uses[id(a)] = uses.get(id(a), 0) + 1
+    reg_of, free = {}, [6, 5, 4, 3, 2, 1, 0]
+
+    def emit(op, dst, a=0, b=0, imm=0.0):
+        if len(code) >= D.VPROG_CODE:
+            raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: a fused vector program over {D.VPROG_CODE} ops")
+        ins = D.Insn()
+        ins.op, ins.dst, ins.a, ins.b, ins.imm = D.OP[op], dst, a, b, imm
+        code.append(ins)
+
+    def take():
+        if not free:
+            raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: a fused vector program over 7 live values")
+        return free.pop()
+
+    def release(n):
+        if n is acc or not isinstance(n, F.Node):
+            return
+        uses[id(n)] -= 1
+        if uses[id(n)] == 0 and id(n) in reg_of:
+            free.append(reg_of.pop(id(n)))
+
+    def slot(l):
+        idx = l.index
+        if l.mask is not None or l.data is not None or idx.vars() - {var}:
+            raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a fused load at {idx} (over {var} only)")
+        stride = 0
+        if idx.terms:
+            if len(idx.terms) != 1 or F.Digit(var) not in idx.terms:
+                raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: fused load index {idx} is not {var} * s + c")
+            stride = idx.terms[F.Digit(var)]
+        if spec.args[l.arg].dtype not in ("float32", "bfloat16", "float16"):
+            raise Refused(Reason.DTYPE_NOT_RUN, f"{spec.name}: a fused load of {spec.args[l.arg].dtype}")
+        key_ = (l.arg, idx.const, stride)
+        if key_ not in loads:
+            if len(loads) >= D.VPROG_LOADS:
+                raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: more than {D.VPROG_LOADS} fused loads")
+            loads.append(key_)
+        return loads.index(key_)
+
+    def gen(n):
+        if n is acc:
+            return 7
+        if id(n) in reg_of:
+            return reg_of[id(n)]
+        if isinstance(n, F.Load):
+            s_ = slot(n)
+            r = take()
+            emit("load", r, s_)
+        elif isinstance(n, F.Const):
+            r = take()
+            emit("const", r, imm=n.v)
+        elif isinstance(n, F.Op):
+            if n.name == "sigmoid":
+                one = F.Const(1.0)
+                return gen(_retarget(n, F.Op("div", one, F.Op("add", one, F.Op("exp", F.Op("neg", n.args[0])))), uses))
+            if n.name not in D.OP or n.name in ("load", "const", "store"):
+                raise Refused(Reason.MATH_UNLOWERED, f"{spec.name}: fused vector op {n.name}")
+            srcs = [gen(a) for a in n.args]
+            for a in n.args:
+                release(a)
+            r = take()
+            emit(n.name, r, srcs[0], srcs[1] if len(srcs) > 1 else srcs[0])
+        else:
+            raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a {type(n).__name__} in a fused vector program")
+        reg_of[id(n)] = r
+        uses.setdefault(id(n), 0)
+        return r
+
+    uses[id(root)] = uses.get(id(root), 0) + 1
+    out = gen(root)
+    if not code or code[-1].dst != out:
+        emit("add", take() if out == 7 else out, out, gen(F.Const(0.0)) if out != 7 else out)
+    v.ncode, v.nload = len(code), len(loads)
+    for i, (arg, off, stride) in enumerate(loads):
+        v.load[i].arg, v.load[i].offset, v.load[i].stride = arg, off, stride
+    for i, c in enumerate(code):
+        v.code[i] = c
+    return v
 
 
 def _lower_reduce_all(spec, prog, st, reduces):
@@ -462,14 +579,24 @@ def _lower_reduce_all(spec, prog, st, reduces):
         raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a whole-tensor reduction wants xnumel 1")
     red = reduces[0]
     v = red.value
-    if not isinstance(v, F.Load) or v.index.vars() != {"r"} or v.index.const != 0:
-        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: reduces something other than one contiguous load")
     if red.op not in ("add", "max"):
         raise Refused(Reason.MATH_UNLOWERED, f"{spec.name}: reduction {red.op}")
+    if st.value is not red:
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a whole-tensor reduction with work after it")
     d = D.new(D.REDUCE_ALL, _manifest_args(spec), spec.grid, units=1, unit_size=1,
               workspace_bytes=D.REDUCE_WORKSPACE_BYTES)
     r = d.p.red
-    r.numel, r.in_arg, r.out_arg = int(cols), v.arg, st.arg
+    if isinstance(v, F.Load) and v.index.vars() == {"r"} and v.index.const == 0 and v.index.terms == {F.Digit("r"): 1} \
+            and v.mask is None:
+        in_arg = v.arg
+    else:
+        # a fused operand (the decode layer's sums of squares: x * x, (x + residual)^2), validation/pytorchsim/
+        # qwen3_8b_layer_decode_*/00_*, 05_*
+        r.pro = _vprog(spec, v, "r")
+        if not r.pro.nload:
+            raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a reduction of constants")
+        in_arg = r.pro.load[0].arg
+    r.numel, r.in_arg, r.out_arg = int(cols), in_arg, st.arg
     r.op = D.RED_MAX if red.op == "max" else D.RED_SUM
     return Lowered(d, D.describe(d))
 

@@ -180,6 +180,20 @@ def cases():
                     {"family": "grouped_gemm", "M": 8 * T, "N": 1536, "K": 2048, "groups": 128}, False))
         out.append((f"moe_gmm_down_t{T}", spec_file(f"layer_op_gmm_down_{T}x0_bf16", 5),
                     {"family": "grouped_gemm", "M": 8 * T, "N": 2048, "K": 768, "groups": 128}, False))
+    # The Qwen3-8B decode layer's fused programs (T = 1, context 128; hidden 4096): the sums of squares of the
+    # two RMSNorms (00; 05 over the residual sum) and the matrix-vector products with the RMSNorm'd vector
+    # (01: q 4096 -> 4096; 06: residual sum, gate_up 4096 -> 24576) or the SiLU'd vector and two residual rows
+    # (07: down 12288 -> 4096).
+    dw = "qwen3_8b_layer_decode_1x128_bf16"
+    out += [
+        ("qwen3_decode_00_sumsq", spec_file(dw, 0), {"family": "sumsq", "n": 4096}, True),
+        ("qwen3_decode_01_rmsnorm_q_mm", spec_file(dw, 1),
+         {"family": "rmsnorm_gemv", "K": 4096, "N": 4096, "eps": EPS}, True),
+        ("qwen3_decode_05_sumsq_residual", spec_file(dw, 5), {"family": "sumsq", "n": 4096}, True),
+        ("qwen3_decode_06_rmsnorm_gate_up_mm", spec_file(dw, 6),
+         {"family": "rmsnorm_gemv", "K": 4096, "N": 24576, "eps": EPS, "residual": True}, True),
+        ("qwen3_decode_07_silu_down_mm", spec_file(dw, 7), {"family": "silu_gemv", "K": 12288, "N": 4096}, True),
+    ]
     for m in (128, 512, 2048, 4096, 8192):
         out.append((f"gemm_{m}x4096x4096", spec_file(f"gemm_{m}x4096x4096_bf16", 0),
                     {"family": "gemm", "M": m, "N": 4096, "K": 4096, "residual": False}, False))

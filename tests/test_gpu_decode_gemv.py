@@ -153,3 +153,59 @@ def test_attention_decode_refuses_unsupported():
         with pytest.raises(native.ExecutorError) as e:
             RC.launch_tensors(D.to_bytes(d), ts)
         assert e.value.code == D.E_UNSUPPORTED
+
+
+# ---- fused matrix-vector products of the decode layer (vector prologue / output epilogue) -------------------
+
+def _wide_compare(got, want):
+    """bf16 outputs of K-term sums: rtol 1e-2, the absolute floor scaled by the result's RMS."""
+    g, w = got.float(), want.float()
+    atol = 1e-2 * max(1.0, float(w.pow(2).mean().sqrt()))
+    assert torch.allclose(g, w, rtol=RTOL, atol=atol), f"max abs err {float((g - w).abs().max())}"
+
+
+@pytest.mark.parametrize("N,K,residual", [(4096, 4096, False), (24576, 4096, True), (520, 3000, False),
+                                          (64, 100000, True), (8, 16, False)])
+def test_rmsnorm_gemv(N, K, residual):
+    g = torch.Generator().manual_seed(N + K)
+    x = torch.randn(K, generator=g).to(torch.bfloat16)
+    res = torch.randn(K, generator=g).to(torch.bfloat16)
+    w = torch.randn(K, generator=g).to(torch.bfloat16)
+    mat = (torch.randn(K * N, generator=g) / math.sqrt(K)).to(torch.bfloat16)
+    ss = O.sumsq(x, K, res if residual else None)
+    ins = [x] + ([res] if residual else []) + [ss, w, mat, torch.zeros(N, dtype=torch.bfloat16)]
+    got = run(B.rmsnorm_gemv(N, K, residual=residual), ins)[-1]
+    _wide_compare(got, O.rmsnorm_gemv(x, ss, w, mat, K, N, 1e-6, res=res if residual else None))
+
+
+@pytest.mark.parametrize("N,K", [(4096, 12288), (1000, 2000), (8, 8)])
+def test_silu_gemv(N, K):
+    g = torch.Generator().manual_seed(N * 3 + K)
+    gu = torch.randn(2 * K, generator=g).to(torch.bfloat16)
+    mat = (torch.randn(K * N, generator=g) / math.sqrt(K)).to(torch.bfloat16)
+    r1, r2 = (torch.randn(N, generator=g).to(torch.bfloat16) for _ in range(2))
+    got = run(B.silu_gemv(N, K), [gu, mat, r1, r2, torch.zeros(N, dtype=torch.bfloat16)])[-1]
+    _wide_compare(got, O.silu_gemv(gu, mat, r1, r2, K, N))
+
+
+@pytest.mark.parametrize("n,residual", [(4096, False), (4096, True), (1, False), (1000003, True)])
+def test_sumsq(n, residual):
+    g = torch.Generator().manual_seed(n)
+    x = torch.randn(n, generator=g).to(torch.bfloat16)
+    res = torch.randn(n, generator=g).to(torch.bfloat16)
+    ins = [x] + ([res] if residual else []) + [torch.zeros(1)]
+    got = run(B.sumsq(n, residual), ins)[-1]
+    want = O.sumsq(x, n, res if residual else None)
+    assert abs(float(got[0]) - float(want[0])) <= 1e-5 * float(want[0])
+
+
+def test_fused_vector_load_out_of_range_is_recorded():
+    """A prologue load past its tensor records PTSIM_E_OOB."""
+    N, K = 64, 256
+    desc = B.rmsnorm_gemv(N, K)
+    desc.arg_numel[2] = K - 1                 # the weight row holds one element fewer than the program reads
+    ts = [torch.randn(K).to(torch.bfloat16), torch.ones(1), torch.randn(K - 1).to(torch.bfloat16),
+          torch.randn(K * N).to(torch.bfloat16), torch.zeros(N, dtype=torch.bfloat16)]
+    with pytest.raises(native.ExecutorError) as e:
+        RC.launch_tensors(D.to_bytes(desc), [t.cuda() for t in ts])
+    assert e.value.code == D.E_OOB

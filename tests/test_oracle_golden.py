@@ -81,6 +81,14 @@ def run_oracle(case, ins):
     if fam == "count_le":
         dt = next(getattr(torch, a["dtype"]) for a in args if a["name"] == outs[0])
         return outs[0], O.count_le(x[0], o["n"], o["rows"], dt)
+    if fam == "sumsq":
+        return outs[0], O.sumsq(x[0], o["n"], x[1] if len(x) > 1 else None)
+    if fam == "rmsnorm_gemv":
+        if o.get("residual"):
+            return outs[0], O.rmsnorm_gemv(x[0], x[2], x[3], x[4], o["K"], o["N"], o["eps"], res=x[1])
+        return outs[0], O.rmsnorm_gemv(x[0], x[1], x[2], x[3], o["K"], o["N"], o["eps"])
+    if fam == "silu_gemv":
+        return outs[0], O.silu_gemv(x[1], x[2], x[3], x[4], o["K"], o["N"])
     if fam == "row_divsum":
         return outs[0], O.row_divsum(x[0], o["rows"], o["cols"])
     if fam == "dispatch_gather":
@@ -170,6 +178,9 @@ def _check_against_gold(case, ins, name, got):
     if fam == "reduce_all":
         scale = float(ins[case["inputs"][0]].float().abs().sum())
         assert abs(float(g[0]) - float(w[0])) <= 1e-5 * scale
+        return
+    if fam == "sumsq":   # a sum of non-negative terms: within 1e-5 of itself
+        assert abs(float(g[0]) - float(w[0])) <= 1e-5 * abs(float(w[0]))
         return
     ok = torch.allclose(g, w, rtol=1e-2, atol=1e-2, equal_nan=True)
     assert ok, f"{case['name']}: max abs err {float((g - w).abs().max()):.4g}"
