@@ -58,6 +58,7 @@ extern "C" {
 #define PTSIM_KIND_GROUPED_GEMM 13 /* per listed group g: C[rows of g] = A[rows of g] . B[g] (the MoE expert matmul) */
 #define PTSIM_KIND_GATHER_SUM 14   /* out[r, :] = sum over k of w(r, k) * table[t(r, k), :] (the MoE combine) */
 #define PTSIM_KIND_INT_TABLE 15    /* an int64 program over [rows, cols] stored per element, summed or scanned along a row */
+#define PTSIM_KIND_ROW_SUM 16      /* out[r] = fp32 sum of row r (the MoE layer's per-token weight sums) */
 
 /* Element types of tensor arguments (kernel.json dtype names, contract/kernel_object.py:43-56). */
 #define PTSIM_DT_F32 0
@@ -125,7 +126,9 @@ typedef struct ptsim_ew_params {
 typedef struct ptsim_row_params {
   int64_t rows, cols;
   int64_t in_row_stride, out_row_stride;
-  int32_t in_arg, out_arg, weight_arg, pad0; /* weight_arg -1 when absent */
+  int32_t in_arg, out_arg, weight_arg;      /* weight_arg -1 when absent */
+  int32_t res_arg_p1;     /* ROW_RMSNORM: 1 + the argument of a residual row (same row stride) added to the input in
+                             fp32 before the norm, the sum normalised unrounded; 0 when absent */
   float eps;              /* RMSNorm epsilon */
   float inv_cols;         /* unused by the kernels (they divide by cols in fp32, as the program does) */
 } ptsim_row_params;
@@ -133,7 +136,8 @@ typedef struct ptsim_row_params {
 typedef struct ptsim_qkrope_params {
   int64_t tokens, heads, dim;           /* input rows are (token, head) pairs of `dim` values */
   int64_t out_tok_stride, out_head_stride; /* output element offset = t*tok_stride + h*head_stride + d */
-  int32_t in_arg, weight_arg, cos_arg, sin_arg, out_arg, pad0;
+  int32_t in_arg, weight_arg, cos_arg, sin_arg, out_arg;
+  int32_t no_norm;      /* 1: rotary embedding of the rows as they are (layer_op_rope_*: no RMSNorm, weight_arg unread) */
   float eps, pad1;
 } ptsim_qkrope_params;
 
@@ -251,6 +255,14 @@ typedef struct ptsim_gsum_params {
   ptsim_map w_map;
   ptsim_map maps[PTSIM_GSUM_MAPS];
   ptsim_iinsn code[PTSIM_MAX_ICODE];
+  /* The MoE layer's fused combine (layer_layer_*: weights renormalised, the residual stream added):
+   * wdiv != 0 divides each weight (fp32) by wdiv_arg[wdiv_offset + r * wdiv_stride] of its output row r;
+   * nres (0-2) residual tensors res_arg[] are read at the output's own index and added as
+   * (res_arg[0] + res_arg[1]) + sum before the store (res_arg[1] may be the output itself). */
+  int32_t wdiv, nres;
+  int32_t res_arg[2];
+  int32_t wdiv_arg, pad0;
+  int64_t wdiv_offset, wdiv_stride;
 } ptsim_gsum_params;
 
 /* INT_TABLE: an int64 program run for every element f = x * cols + r of a [rows, cols] space (registers

@@ -86,9 +86,12 @@ def softmax_rows(x, rows, cols, out_dtype=torch.bfloat16):
     return (e / e.sum(dim=1, keepdim=True)).to(out_dtype).reshape(-1)
 
 
-def rmsnorm_rows(x, w, rows, cols, eps):
-    """qwen3_8b_layer_prefill_*/00_*_triton.py: r = rsqrt(sum(x^2) / cols + eps); out = bf16((x * r) * w)."""
+def rmsnorm_rows(x, w, rows, cols, eps, res=None):
+    """qwen3_8b_layer_prefill_*/00_*_triton.py: r = rsqrt(sum(x^2) / cols + eps); out = bf16((x * r) * w); with
+    `res` (layer_layer_prefill_*/18_*) the row is x + res in fp32, unrounded."""
     v = f32(x).view(rows, cols)
+    if res is not None:
+        v = v + f32(res).view(rows, cols)
     ss = (v * v).sum(dim=1, keepdim=True)
     r = torch.rsqrt(ss / float(cols) + torch.tensor(eps, dtype=torch.float32))
     return bf16((v * r) * f32(w).view(1, cols)).reshape(-1)
@@ -107,6 +110,23 @@ def qknorm_rope(x, w, cos, sin, tokens, heads, eps, dim=128):
     s = f32(sin).view(tokens, 1, dim)
     out = n * c + rot * s
     return bf16(out).transpose(0, 1).contiguous().reshape(-1)
+
+
+def row_sum(x, rows, cols):
+    """layer_layer_prefill_*/22_*_triton.py: out[r] = the fp32 sum of row r (the top-k weights of a token)."""
+    return f32(x).view(rows, cols).sum(dim=1)
+
+
+def rope_rows(x, cos, sin, tokens, heads, dim=128):
+    """layer_op_rope_{q,k}_*/00_*_triton.py: each (token, head) row of `dim`: rot = cat(-x[half:], x[:half]),
+    out = bf16(x * cos[t] + rot * sin[t]) in fp32, token-major like the input (one token: the tables are that
+    position's)."""
+    v = f32(x).view(tokens, heads, dim)
+    half = dim // 2
+    rot = torch.cat([-v[..., half:], v[..., :half]], dim=2)
+    c = f32(cos).view(tokens, 1, dim)
+    s = f32(sin).view(tokens, 1, dim)
+    return bf16(v * c + rot * s).reshape(-1)
 
 
 def reduce_all(x, op):
@@ -318,6 +338,24 @@ def count_le(x, n, rows, out_dtype):
     store)."""
     v = x.reshape(-1)[:n].to(torch.int64)
     return (v[None, :] <= torch.arange(rows)[:, None]).to(torch.int64).sum(dim=1).to(out_dtype)
+
+
+def combine_weighted_fused(idx, cum, cnt, pos, expert_out, w, wsum, res_a, res_b, tokens, hidden, topk, experts):
+    """layer_layer_{decode,prefill}_*/23_*, 27_*: the combine with each token's weights divided by their sum
+    (fp32 w[t, k] / wsum[t]) and the residual stream added: out = bf16((res_a + res_b) + sum over k of
+    float(expert_out[p, :]) * (w / wsum)), p as combine_weighted's."""
+    e = idx.to(torch.int64).view(tokens, topk)
+    e = torch.where(e < 0, e + experts, e)
+    rows = tokens * topk
+    p = cum.to(torch.int64)[e] - cnt.to(torch.int64)[e] + (pos.to(torch.int64).view(tokens, topk) - 1)
+    p = torch.where(p < 0, p + rows, p)
+    if not bool(((e >= 0) & (e < experts)).all() and ((p >= 0) & (p < rows)).all()):
+        raise IndexError("combine index out of range (the reference asserts)")
+    g = f32(expert_out).view(rows, hidden)[p]
+    wk = f32(w).view(tokens, topk) / f32(wsum).view(-1)[:tokens].view(tokens, 1)
+    acc = (g * wk.view(tokens, topk, 1)).sum(dim=1)
+    resid = f32(res_a).view(tokens, hidden) + f32(res_b).view(tokens, hidden)
+    return (resid + acc).to(torch.bfloat16).reshape(-1)
 
 
 def grouped_gemm(a, b, group, start, rows, c_init, M, N, K, groups):

@@ -405,6 +405,9 @@ struct GsumArgs {
   ptsim_map w_map;
   ptsim_map maps[PTSIM_GSUM_MAPS];
   ptsim_iinsn code[PTSIM_MAX_ICODE];
+  int32_t wdiv, nres, wdiv_arg, res_dt;   // weight divisor; residual rows (same element type each)
+  const void *res[2];
+  int64_t wdiv_offset, wdiv_stride;
 };
 
 __device__ __forceinline__ int64_t map_at(const ptsim_map &m, int64_t f) {
@@ -502,6 +505,14 @@ __device__ __forceinline__ void gsum_slice(const GsumArgs &g, const int64_t *row
       for (int e = 0; e < 8 && c8 + e < g.cols; ++e) acc[e] = fmaf(ld_any(g.table, g.table_dt, t * g.cols + c8 + e), ws[k], acc[e]);
     }
   }
+  if (g.nres > 0) {   // (res0 + res1) + sum, read at the output's own index before it is written
+    for (int e = 0; e < 8 && c8 + e < g.cols; ++e) {
+      const int64_t at = orow * g.cols + c8 + e;
+      float rs = ld_any(g.res[0], g.res_dt, at);
+      if (g.nres > 1) rs = __fadd_rn(rs, ld_any(g.res[1], g.res_dt, at));
+      acc[e] = __fadd_rn(rs, acc[e]);
+    }
+  }
   if (g.out_dt == PTSIM_DT_BF16 && c8 + 8 <= g.cols && (g.cols % 8) == 0) {
     uint4 o;
     o.x = pack_bf16x2(acc[0], acc[1]);
@@ -531,11 +542,14 @@ __global__ void __launch_bounds__(256) gather_sum_kernel(const __grid_constant__
         const int64_t f = r * g.terms + lane % nterms;
         trow = gsum_row_of(g, f);
         const int64_t wat = map_at(g.w_map, f);
-        if (trow < 0 || trow >= g.table_rows || wat < 0 || wat >= g.numel[g.w_arg]) {
+        const int64_t dat = g.wdiv_offset + r * g.wdiv_stride;
+        if (trow < 0 || trow >= g.table_rows || wat < 0 || wat >= g.numel[g.w_arg] ||
+            (g.wdiv && (dat < 0 || dat >= g.numel[g.wdiv_arg]))) {
           record_status(PTSIM_E_OOB);
           trow = -1;
         } else {
           w = ld_any(g.arg[g.w_arg], g.dt[g.w_arg], wat);
+          if (g.wdiv) w = __fdiv_rn(w, ld_any(g.arg[g.wdiv_arg], g.dt[g.wdiv_arg], dat));
         }
       }
       s_row[lane] = trow;
@@ -576,6 +590,17 @@ int launch_gather_sum(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_
   g.w_map = p.w_map;
   memcpy(g.maps, p.maps, sizeof(g.maps));
   memcpy(g.code, p.code, sizeof(g.code));
+  g.wdiv = p.wdiv;
+  g.wdiv_arg = p.wdiv_arg;
+  g.wdiv_offset = p.wdiv_offset;
+  g.wdiv_stride = p.wdiv_stride;
+  g.nres = p.nres;
+  for (int k = 0; k < p.nres; ++k) {
+    g.res[k] = ptrs[p.res_arg[k]];
+    if (d.arg_numel[p.res_arg[k]] < p.rows * p.cols || d.arg_dtype[p.res_arg[k]] != d.arg_dtype[p.res_arg[0]])
+      return fail(PTSIM_E_UNSUPPORTED, "gather-sum residual %d: as many elements as the output, one element type", k);
+  }
+  g.res_dt = p.nres > 0 ? d.arg_dtype[p.res_arg[0]] : 0;
   if ((reinterpret_cast<uintptr_t>(g.table) | reinterpret_cast<uintptr_t>(g.out)) % 16 != 0)
     return fail(PTSIM_E_ARGS, "gather-sum table and output must be 16-byte aligned");
   if (g.row_end <= g.row_begin) return PTSIM_OK;

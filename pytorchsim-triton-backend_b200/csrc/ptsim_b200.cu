@@ -134,14 +134,21 @@ static int check_desc(const void *p, size_t bytes) {
     }
     case PTSIM_KIND_ROW_SOFTMAX:
     case PTSIM_KIND_ROW_DIVSUM:
+    case PTSIM_KIND_ROW_SUM:
     case PTSIM_KIND_ROW_RMSNORM: {
       const ptsim_row_params &r = d.p.row;
       if ((rc = check_arg(d, r.in_arg, "row input")) || (rc = check_arg(d, r.out_arg, "row output"))) return rc;
+      if (d.kind == PTSIM_KIND_ROW_RMSNORM && r.res_arg_p1 > 0) {
+        if ((rc = check_arg(d, r.res_arg_p1 - 1, "RMSNorm residual"))) return rc;
+        if (r.rows > 0 && (r.rows - 1) * r.in_row_stride + r.cols > d.arg_numel[r.res_arg_p1 - 1])
+          return fail(PTSIM_E_OOB, "RMSNorm residual rows extend past their tensor");
+      }
       if (d.kind == PTSIM_KIND_ROW_RMSNORM && (rc = check_arg(d, r.weight_arg, "RMSNorm weight"))) return rc;
       if (r.rows < 0 || r.cols < 1) return fail(PTSIM_E_DESC, "row program over %lld x %lld", (long long)r.rows, (long long)r.cols);
+      const int64_t out_row = d.kind == PTSIM_KIND_ROW_SUM ? 1 : r.cols;   // a row sum stores one value per row
       if (r.rows > 0) {
         if ((r.rows - 1) * r.in_row_stride + r.cols > d.arg_numel[r.in_arg] ||
-            (r.rows - 1) * r.out_row_stride + r.cols > d.arg_numel[r.out_arg])
+            (r.rows - 1) * r.out_row_stride + out_row > d.arg_numel[r.out_arg])
           return fail(PTSIM_E_OOB, "row program reads or writes past its tensors");
         if (d.kind == PTSIM_KIND_ROW_RMSNORM && r.cols > d.arg_numel[r.weight_arg])
           return fail(PTSIM_E_OOB, "RMSNorm weight holds fewer than %lld values", (long long)r.cols);
@@ -150,7 +157,7 @@ static int check_desc(const void *p, size_t bytes) {
     }
     case PTSIM_KIND_QKNORM_ROPE: {
       const ptsim_qkrope_params &q = d.p.qk;
-      if ((rc = check_arg(d, q.in_arg, "qk input")) || (rc = check_arg(d, q.weight_arg, "qk weight")) ||
+      if ((rc = check_arg(d, q.in_arg, "qk input")) || (!q.no_norm && (rc = check_arg(d, q.weight_arg, "qk weight"))) ||
           (rc = check_arg(d, q.cos_arg, "cos")) || (rc = check_arg(d, q.sin_arg, "sin")) || (rc = check_arg(d, q.out_arg, "qk output")))
         return rc;
       if (q.tokens * q.heads * q.dim > d.arg_numel[q.in_arg] || q.tokens * q.dim > d.arg_numel[q.cos_arg] ||
@@ -158,7 +165,8 @@ static int check_desc(const void *p, size_t bytes) {
           (q.tokens > 0 && (q.tokens - 1) * q.out_tok_stride + (q.heads - 1) * q.out_head_stride + q.dim > d.arg_numel[q.out_arg]))
         return fail(PTSIM_E_OOB, "QK-norm+RoPE reads or writes past its tensors");
       if (d.arg_dtype[q.cos_arg] != PTSIM_DT_F32 || d.arg_dtype[q.sin_arg] != PTSIM_DT_F32 ||
-          d.arg_dtype[q.in_arg] != PTSIM_DT_BF16 || d.arg_dtype[q.out_arg] != PTSIM_DT_BF16 || d.arg_dtype[q.weight_arg] != PTSIM_DT_BF16)
+          d.arg_dtype[q.in_arg] != PTSIM_DT_BF16 || d.arg_dtype[q.out_arg] != PTSIM_DT_BF16 ||
+          (!q.no_norm && d.arg_dtype[q.weight_arg] != PTSIM_DT_BF16))
         return fail(PTSIM_E_UNSUPPORTED, "QK-norm+RoPE runs bf16 rows with fp32 cos/sin tables");
       break;
     }
@@ -270,6 +278,10 @@ static int check_desc(const void *p, size_t bytes) {
         for (int k = 0; k < m->ndigit; ++k)
           if (m->div[k] < 1 || m->mod[k] < 1 || m->stride[k] < 0) return fail(PTSIM_E_DESC, "gather-sum map digit %d", k);
       }
+      if (q.nres < 0 || q.nres > 2) return fail(PTSIM_E_DESC, "gather-sum with %d residuals", q.nres);
+      for (int k = 0; k < q.nres; ++k)
+        if ((rc = check_arg(d, q.res_arg[k], "gather-sum residual"))) return rc;
+      if (q.wdiv && (rc = check_arg(d, q.wdiv_arg, "gather-sum weight divisor"))) return rc;
       for (int i = 0; i < q.ncode; ++i)
         if (q.code[i].op < PTSIM_I_LOAD || q.code[i].op > PTSIM_I_LOADI || q.code[i].dst >= PTSIM_MAX_ICODE ||
             q.code[i].a >= PTSIM_MAX_ICODE || q.code[i].b >= PTSIM_MAX_ICODE || q.code[i].c >= PTSIM_MAX_ICODE)
@@ -377,6 +389,7 @@ int ptsim_launch(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int
     case PTSIM_KIND_ELEMENTWISE: return launch_elementwise(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_ROW_SOFTMAX:
     case PTSIM_KIND_ROW_DIVSUM:
+    case PTSIM_KIND_ROW_SUM:
     case PTSIM_KIND_ROW_RMSNORM: return launch_rowops(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_TOPK: return launch_topk(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_SORT: return launch_sort(d, dev_ptrs, lo, hi, c);

@@ -17,10 +17,11 @@
 
 namespace ptsim {
 
-enum RowKind { kSoftmax = 0, kRmsNorm = 1, kDivSum = 2 };
+enum RowKind { kSoftmax = 0, kRmsNorm = 1, kDivSum = 2, kRowSum = 3 };
 
 struct RowLaunch {
   const void *in;
+  const void *res;     // RMSNorm: a residual row added to the input (same stride and type), or null
   void *out;
   const void *weight;
   int64_t rows_begin, rows_end, cols, in_stride, out_stride;
@@ -83,6 +84,20 @@ __global__ void __launch_bounds__(256) row_fast_kernel(const __grid_constant__ R
       const uint32_t w[4] = {raw[c].x, raw[c].y, raw[c].z, raw[c].w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) { v[c * 8 + 2 * j] = lo_bf16(w[j]); v[c * 8 + 2 * j + 1] = hi_bf16(w[j]); }
+    }
+    if (KIND == kRmsNorm && L.res != nullptr) {   // the row normalised is in + res, in fp32
+      const uint4 *rsrc = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(L.res) + (live ? r : L.rows_begin) * L.in_stride);
+#pragma unroll
+      for (int c = 0; c < CH; ++c) raw[c] = live ? __ldcs(rsrc + c * TPR + lane_in_row) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        const uint32_t w[4] = {raw[c].x, raw[c].y, raw[c].z, raw[c].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          v[c * 8 + 2 * j] = __fadd_rn(v[c * 8 + 2 * j], lo_bf16(w[j]));
+          v[c * 8 + 2 * j + 1] = __fadd_rn(v[c * 8 + 2 * j + 1], hi_bf16(w[j]));
+        }
+      }
     }
   }
   uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(L.out) + (live ? r : L.rows_begin) * L.out_stride);
@@ -307,6 +322,12 @@ __global__ void __launch_bounds__(256) row_generic_kernel(const __grid_constant_
       s = row_allreduce<32>(s, false, nullptr);
       for (int64_t c = lane; c < L.cols; c += 32)
         st_any(L.out, L.out_dt, ob + c, __fdiv_rn(npu_exp(__fsub_rn(ld_any(L.in, L.in_dt, ib + c), m)), s));
+    } else if constexpr (KIND == kRowSum) {
+      // sum(x) per row in fp32 (layer_layer_prefill_*/22_*: the top-k weight sums), stored at the row
+      float s = 0.f;
+      for (int64_t c = lane; c < L.cols; c += 32) s = __fadd_rn(s, ld_any(L.in, L.in_dt, ib + c));
+      s = row_allreduce<32>(s, false, nullptr);
+      if (lane == 0) st_any(L.out, L.out_dt, r * L.out_stride, s);
     } else if constexpr (KIND == kDivSum) {
       // x / sum(x) per row (layer_op_router_post_*/02_*: tmp4 = sum(x); x / tmp4 in fp32, cast on the store)
       float s = 0.f;
@@ -314,13 +335,16 @@ __global__ void __launch_bounds__(256) row_generic_kernel(const __grid_constant_
       s = row_allreduce<32>(s, false, nullptr);
       for (int64_t c = lane; c < L.cols; c += 32) st_any(L.out, L.out_dt, ob + c, __fdiv_rn(ld_any(L.in, L.in_dt, ib + c), s));
     } else {
+      auto xval = [&](int64_t c) {
+        const float x = ld_any(L.in, L.in_dt, ib + c);
+        return L.res != nullptr ? __fadd_rn(x, ld_any(L.res, L.in_dt, ib + c)) : x;
+      };
       float ss = 0.f;
-      for (int64_t c = lane; c < L.cols; c += 32) { const float x = ld_any(L.in, L.in_dt, ib + c); ss = __fadd_rn(ss, __fmul_rn(x, x)); }
+      for (int64_t c = lane; c < L.cols; c += 32) { const float x = xval(c); ss = __fadd_rn(ss, __fmul_rn(x, x)); }
       ss = row_allreduce<32>(ss, false, nullptr);
       const float rs = rsqrtf(__fadd_rn(__fdiv_rn(ss, float(L.cols)), L.eps));
       for (int64_t c = lane; c < L.cols; c += 32)
-        st_any(L.out, L.out_dt, ob + c,
-               __fmul_rn(__fmul_rn(ld_any(L.in, L.in_dt, ib + c), rs), ld_any(L.weight, L.w_dt, c)));
+        st_any(L.out, L.out_dt, ob + c, __fmul_rn(__fmul_rn(xval(c), rs), ld_any(L.weight, L.w_dt, c)));
     }
   }
 }
@@ -350,7 +374,7 @@ static int launch_row_kind(const RowLaunch &L, const LaunchCtx &c) {
   const bool aligned = (reinterpret_cast<uintptr_t>(L.in) % 16 == 0) && (reinterpret_cast<uintptr_t>(L.out) % 16 == 0) &&
                        (KIND == kSoftmax || reinterpret_cast<uintptr_t>(L.weight) % 16 == 0) &&
                        (L.in_stride % 8 == 0) && (L.out_stride % 8 == 0);
-  if (bf16_io && aligned) {
+  if (bf16_io && aligned && L.res == nullptr) {
     bool done = false;
     const int rc = dispatch_row_cta<KIND>(L, c, &done);
     if (done) return rc;
@@ -387,6 +411,9 @@ int launch_rowops(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi
   L.in = ptrs[p.in_arg];
   L.out = ptrs[p.out_arg];
   L.weight = p.weight_arg >= 0 ? ptrs[p.weight_arg] : nullptr;
+  L.res = (d.kind == PTSIM_KIND_ROW_RMSNORM && p.res_arg_p1 > 0) ? ptrs[p.res_arg_p1 - 1] : nullptr;
+  if (L.res != nullptr && (d.arg_dtype[p.res_arg_p1 - 1] != d.arg_dtype[p.in_arg] || reinterpret_cast<uintptr_t>(L.res) % 16 != 0))
+    return fail(PTSIM_E_UNSUPPORTED, "RMSNorm residual row: the input's element type, 16-byte aligned");
   L.rows_begin = lo * d.unit_size;
   L.rows_end = hi * d.unit_size < p.rows ? hi * d.unit_size : p.rows;
   L.rows_total = p.rows;
@@ -399,11 +426,12 @@ int launch_rowops(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi
   L.eps = p.eps;
   if (L.rows_end <= L.rows_begin) return PTSIM_OK;
   if (d.kind == PTSIM_KIND_ROW_SOFTMAX) return launch_row_kind<kSoftmax>(L, c);
-  if (d.kind == PTSIM_KIND_ROW_DIVSUM) {
+  if (d.kind == PTSIM_KIND_ROW_DIVSUM || d.kind == PTSIM_KIND_ROW_SUM) {
     // Rows of a few values (the router's top-k weights): one warp per row.
     int64_t blocks = ceil_div(L.rows_end - L.rows_begin, 8);
     if (blocks > int64_t(c.sm_count) * 8) blocks = int64_t(c.sm_count) * 8;
-    row_generic_kernel<kDivSum><<<unsigned(blocks), 256, 0, c.stream>>>(L);
+    if (d.kind == PTSIM_KIND_ROW_SUM) row_generic_kernel<kRowSum><<<unsigned(blocks), 256, 0, c.stream>>>(L);
+    else row_generic_kernel<kDivSum><<<unsigned(blocks), 256, 0, c.stream>>>(L);
     PTSIM_CUDA(cudaGetLastError());
     return PTSIM_OK;
   }
@@ -426,13 +454,14 @@ struct QkLaunch {
   uint32_t row_begin, row_end, heads;
   int64_t tok_stride, head_stride;
   float eps;
+  int32_t no_norm;   // the rotation alone (layer_op_rope_*): n = x
 };
 
 __global__ void __launch_bounds__(256) qk_rope_kernel(const __grid_constant__ QkLaunch L) {
   const int lane = threadIdx.x & 31, sub = lane & 15, half = lane >> 4;
   const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const uint32_t nwarps = (gridDim.x * blockDim.x) >> 5;
-  const uint4 wv = __ldg(reinterpret_cast<const uint4 *>(L.w) + sub);
+  const uint4 wv = L.no_norm ? make_uint4(0, 0, 0, 0) : __ldg(reinterpret_cast<const uint4 *>(L.w) + sub);
   const float w[8] = {lo_bf16(wv.x), hi_bf16(wv.x), lo_bf16(wv.y), hi_bf16(wv.y),
                       lo_bf16(wv.z), hi_bf16(wv.z), lo_bf16(wv.w), hi_bf16(wv.w)};
   const unsigned full = 0xffffffffu;
@@ -465,7 +494,7 @@ __global__ void __launch_bounds__(256) qk_rope_kernel(const __grid_constant__ Qk
       const float rs = rsqrtf(__fadd_rn(__fdiv_rn(ss, 128.f), L.eps));
       float n[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) n[j] = __fmul_rn(__fmul_rn(x[j], rs), w[j]);
+      for (int j = 0; j < 8; ++j) n[j] = L.no_norm ? x[j] : __fmul_rn(__fmul_rn(x[j], rs), w[j]);
       const float4 *cp = reinterpret_cast<const float4 *>(L.cosb + size_t(t) * 128) + 2 * sub;
       const float4 *sp = reinterpret_cast<const float4 *>(L.sinb + size_t(t) * 128) + 2 * sub;
       const float4 c0 = __ldg(cp), c1 = __ldg(cp + 1), s0 = __ldg(sp), s1 = __ldg(sp + 1);
@@ -493,7 +522,8 @@ int launch_qkrope(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi
   if (p.tokens * p.heads >= (int64_t(1) << 31)) return fail(PTSIM_E_UNSUPPORTED, "QK-norm+RoPE over 2^31 rows");
   QkLaunch L;
   L.in = reinterpret_cast<const uint16_t *>(ptrs[p.in_arg]);
-  L.w = reinterpret_cast<const uint16_t *>(ptrs[p.weight_arg]);
+  L.w = p.no_norm ? nullptr : reinterpret_cast<const uint16_t *>(ptrs[p.weight_arg]);
+  L.no_norm = p.no_norm;
   L.cosb = reinterpret_cast<const float *>(ptrs[p.cos_arg]);
   L.sinb = reinterpret_cast<const float *>(ptrs[p.sin_arg]);
   L.out = reinterpret_cast<uint16_t *>(ptrs[p.out_arg]);

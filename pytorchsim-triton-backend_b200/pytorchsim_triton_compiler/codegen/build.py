@@ -253,18 +253,27 @@ def grouped_gemm(M, N, K, groups, programs):
     return d
 
 
-def combine_gather_sum(tokens, hidden, topk, experts):
+def combine_gather_sum(tokens, hidden, topk, experts, fused=False):
     """The MoE combine's weighted gather (layer_op_combine_*/03_*): out[t, :] = sum over k of w[t, k] *
     expert_out[p(t, k), :], p = cum[e] - cnt[e] + pos[t, k] - 1 with e = idx[t, k] (both wrapped when
-    negative); arguments idx, cum, cnt, pos (int64), expert_out, w (bf16), out (bf16)."""
+    negative); arguments idx, cum, cnt, pos (int64), expert_out, w (bf16), out (bf16).  fused: the MoE layer's
+    form (layer_layer_*/23_*, 27_*): fp32 weights divided by the token's sum wsum[t], and out = (res + out) +
+    the sum, out read first; arguments idx, cum, cnt, pos, expert_out, w (fp32), wsum (fp32), res, out."""
     rows = tokens * topk
-    d = D.new(D.GATHER_SUM, _args([("in_ptr0", "int64", rows), ("in_ptr1", "int64", experts), ("in_ptr2", "int64", experts),
-                                   ("in_ptr3", "int64", rows), ("in_ptr4", "bfloat16", rows * hidden),
-                                   ("in_ptr5", "bfloat16", rows), ("out_ptr1", "bfloat16", tokens * hidden)]),
-              (1, 1, 1), units=tokens, unit_size=1)
+    specs = [("in_ptr0", "int64", rows), ("in_ptr1", "int64", experts), ("in_ptr2", "int64", experts),
+             ("in_ptr3", "int64", rows), ("in_ptr4", "bfloat16", rows * hidden)]
+    if fused:
+        specs += [("in_ptr5", "float32", rows), ("in_ptr6", "float32", tokens), ("in_ptr7", "bfloat16", tokens * hidden)]
+    else:
+        specs += [("in_ptr5", "bfloat16", rows)]
+    specs += [("out_ptr1", "bfloat16", tokens * hidden)]
+    d = D.new(D.GATHER_SUM, _args(specs), (1, 1, 1), units=tokens, unit_size=1)
     g = d.p.gsum
     g.rows, g.cols, g.terms, g.table_rows = tokens, hidden, topk, rows
-    g.out_arg, g.table_arg, g.w_arg = 6, 4, 5
+    g.out_arg, g.table_arg, g.w_arg = len(specs) - 1, 4, 5
+    if fused:
+        g.wdiv, g.wdiv_arg, g.wdiv_offset, g.wdiv_stride = 1, 6, 0, 1
+        g.nres, g.res_arg[0], g.res_arg[1] = 2, 7, len(specs) - 1
 
     def flat(m, arg):
         m.arg, m.ndigit, m.offset = arg, 1, 0

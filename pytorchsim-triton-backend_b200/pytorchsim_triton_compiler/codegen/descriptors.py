@@ -12,12 +12,12 @@ MAX_ARGS, MAX_MAPS, MAX_DIGITS, MAX_CODE, MAX_REGS = 16, 8, 4, 32, 8
 
 # Kinds (PTSIM_KIND_*).
 ELEMENTWISE, ROW_SOFTMAX, ROW_RMSNORM, QKNORM_ROPE, GEMM, ATTN_PREFILL, REDUCE_ALL, ATTN_DECODE = 1, 2, 3, 4, 5, 6, 7, 8
-ROW_DIVSUM, TOPK, SORT, GATHER_ROWS, GROUPED_GEMM, GATHER_SUM, INT_TABLE = 9, 10, 11, 12, 13, 14, 15
+ROW_DIVSUM, TOPK, SORT, GATHER_ROWS, GROUPED_GEMM, GATHER_SUM, INT_TABLE, ROW_SUM = 9, 10, 11, 12, 13, 14, 15, 16
 KIND_NAME = {ELEMENTWISE: "elementwise", ROW_SOFTMAX: "row_softmax", ROW_RMSNORM: "row_rmsnorm",
              QKNORM_ROPE: "qknorm_rope", GEMM: "gemm", ATTN_PREFILL: "attn_prefill", REDUCE_ALL: "reduce_all",
              ATTN_DECODE: "attn_decode", ROW_DIVSUM: "row_divsum", TOPK: "topk", SORT: "sort",
              GATHER_ROWS: "gather_rows", GROUPED_GEMM: "grouped_gemm", GATHER_SUM: "gather_sum",
-             INT_TABLE: "int_table"}
+             INT_TABLE: "int_table", ROW_SUM: "row_sum"}
 
 # Element types (PTSIM_DT_*), keyed by kernel.json dtype names (contract/kernel_object.py NP_DTYPE keys).
 DTYPE_CODE = {"float32": 0, "bfloat16": 1, "float16": 2, "int32": 3, "int64": 4, "int16": 5, "int8": 6,
@@ -66,14 +66,14 @@ class EwParams(C.Structure):
 
 class RowParams(C.Structure):
     _fields_ = [("rows", C.c_int64), ("cols", C.c_int64), ("in_row_stride", C.c_int64), ("out_row_stride", C.c_int64),
-                ("in_arg", C.c_int32), ("out_arg", C.c_int32), ("weight_arg", C.c_int32), ("pad0", C.c_int32),
+                ("in_arg", C.c_int32), ("out_arg", C.c_int32), ("weight_arg", C.c_int32), ("res_arg_p1", C.c_int32),
                 ("eps", C.c_float), ("inv_cols", C.c_float)]
 
 
 class QkParams(C.Structure):
     _fields_ = [("tokens", C.c_int64), ("heads", C.c_int64), ("dim", C.c_int64), ("out_tok_stride", C.c_int64),
                 ("out_head_stride", C.c_int64), ("in_arg", C.c_int32), ("weight_arg", C.c_int32),
-                ("cos_arg", C.c_int32), ("sin_arg", C.c_int32), ("out_arg", C.c_int32), ("pad0", C.c_int32),
+                ("cos_arg", C.c_int32), ("sin_arg", C.c_int32), ("out_arg", C.c_int32), ("no_norm", C.c_int32),
                 ("eps", C.c_float), ("pad1", C.c_float)]
 
 
@@ -132,7 +132,9 @@ GSUM_MAPS = 4
 class GsumParams(C.Structure):
     _fields_ = [("rows", C.c_int64), ("cols", C.c_int64), ("terms", C.c_int64), ("table_rows", C.c_int64),
                 ("out_arg", C.c_int32), ("table_arg", C.c_int32), ("w_arg", C.c_int32), ("ncode", C.c_int32),
-                ("w_map", Map), ("maps", Map * GSUM_MAPS), ("code", IInsn * MAX_ICODE)]
+                ("w_map", Map), ("maps", Map * GSUM_MAPS), ("code", IInsn * MAX_ICODE),
+                ("wdiv", C.c_int32), ("nres", C.c_int32), ("res_arg", C.c_int32 * 2), ("wdiv_arg", C.c_int32),
+                ("pad0", C.c_int32), ("wdiv_offset", C.c_int64), ("wdiv_stride", C.c_int64)]
 
 
 ITAB_MAPS, ITAB_OUTS = 5, 4
@@ -222,10 +224,14 @@ def describe(d):
     elif d.kind in (ROW_SOFTMAX, ROW_RMSNORM):
         r = d.p.row
         out.update(rows=r.rows, cols=r.cols, eps=r.eps)
+        if r.res_arg_p1:
+            out["residual"] = r.res_arg_p1 - 1
     elif d.kind == QKNORM_ROPE:
         q = d.p.qk
         out.update(tokens=q.tokens, heads=q.heads, dim=q.dim, eps=q.eps,
                    out_strides=[q.out_tok_stride, q.out_head_stride])
+        if q.no_norm:
+            out["no_norm"] = True
     elif d.kind == GEMM:
         g = d.p.gemm
         out.update(M=g.M, N=g.N, K=g.K, residual=g.r_arg >= 0, b_kmajor=bool(g.b_kmajor))
@@ -239,7 +245,7 @@ def describe(d):
         a = d.p.attn
         out.update(hkv=a.hkv, group=a.hq // max(1, a.hkv), seq=a.seq, dim=a.dim, scale=a.scale,
                    ref_bkv=a.ref_bkv)
-    elif d.kind == ROW_DIVSUM:
+    elif d.kind in (ROW_DIVSUM, ROW_SUM):
         out.update(rows=d.p.row.rows, cols=d.p.row.cols)
     elif d.kind in (TOPK, SORT):
         e = d.p.sel
@@ -259,6 +265,10 @@ def describe(d):
         q = d.p.gsum
         out.update(rows=q.rows, cols=q.cols, terms=q.terms, table_rows=q.table_rows,
                    program=[(IOP_NAME.get(i.op, i.op), i.dst, i.a, i.b, i.c, i.imm) for i in list(q.code)[:q.ncode]])
+        if q.wdiv:
+            out["weight_divisor"] = (q.wdiv_arg, q.wdiv_offset, q.wdiv_stride)
+        if q.nres:
+            out["residuals"] = list(q.res_arg)[:q.nres]
     elif d.kind == INT_TABLE:
         q = d.p.itab
         out.update(rows=q.rows, cols=q.cols,

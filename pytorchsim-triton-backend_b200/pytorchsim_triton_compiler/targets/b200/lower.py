@@ -155,13 +155,17 @@ def lower(spec, fn=None):
     st = prog.stores[0]
     if isinstance(strip_casts(st.value), F.Load) and strip_casts(st.value).data is not None:
         return _lower_gather(spec, prog, st)
-    sv = strip_casts(st.value)
-    if isinstance(sv, F.Reduce) and sv.op == "add" and isinstance(strip_casts(sv.value), F.Op) \
+    sums = [n for n in walk(st.value) if isinstance(n, F.Reduce)]
+    sv = sums[0] if len(sums) == 1 else None
+    if sv is not None and sv.op == "add" and isinstance(strip_casts(sv.value), F.Op) \
             and strip_casts(sv.value).name == "mul" and any(isinstance(strip_casts(a), F.Load) and strip_casts(a).data is not None
                                                             for a in strip_casts(sv.value).args):
         return _lower_gather_sum(spec, prog, st, sv)
     reduces = [n for n in walk(st.value) if isinstance(n, F.Reduce)]
     if not reduces:
+        if any(isinstance(n, F.Op) and n.name == "where" for n in walk(st.value)) and \
+                len({n.arg for n in walk(st.value) if isinstance(n, F.Load)}) == 3:
+            return _lower_rope(spec, prog, st)
         return _lower_elementwise(spec, prog, st)
     ops = {n.name for n in walk(st.value) if isinstance(n, F.Op)}
     loads = [n for n in walk(st.value) if isinstance(n, F.Load)]
@@ -172,12 +176,14 @@ def lower(spec, fn=None):
         return _lower_gemv(spec, prog, st, reduces[0])
     if "where" in ops and "rsqrt" in ops:
         return _lower_qknorm_rope(spec, prog, st, loads)
-    if "rsqrt" in ops and len(args) == 2:
+    if "rsqrt" in ops and len(args) in (2, 3):
         return _lower_rmsnorm(spec, prog, st, loads)
     if "exp" in ops and {r.op for r in reduces} == {"max", "add"} and len(args) == 1:
         return _lower_softmax(spec, prog, st, reduces)
     if ops == {"div"} and len(reduces) == 1 and reduces[0].op == "add" and len(args) == 1:
         return _lower_divsum(spec, prog, st, reduces[0])
+    if not ops and st.value is reduces[0] and reduces[0].op == "add" and len(args) == 1:
+        return _lower_rowsum(spec, prog, st, reduces[0])
     raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a reduction program of ops {sorted(ops)}")
 
 
@@ -341,11 +347,10 @@ def _lower_softmax(spec, prog, st, reduces):
 
 
 def _lower_rmsnorm(spec, prog, st, loads):
+    """(x * rsqrt(sum(x^2) / cols + eps)) * w per row (qwen3_8b_layer_prefill_*/00_*); x may be the fp32 sum of
+    two rows, unrounded (the MoE layer's residual add, layer_layer_prefill_*/18_*), and a one-row program
+    indexes its row by r alone (layer_op_rmsnorm_1x0_bf16)."""
     rows, cols, xblock = _row_sizes(spec, prog, "RMSNorm")
-    row_loads = [l for l in loads if "x" in l.index.vars()]
-    w_loads = [l for l in loads if l.index.vars() == {"r"}]
-    if not row_loads or not w_loads or len({l.arg for l in row_loads}) != 1 or len({l.arg for l in w_loads}) != 1:
-        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: RMSNorm wants one row input and one weight")
     rs = [n for n in walk(st.value) if isinstance(n, F.Op) and n.name == "rsqrt"]
     inner = rs[0].args[0]
     if not (isinstance(inner, F.Op) and inner.name == "add" and isinstance(inner.args[1], F.Const)):
@@ -358,12 +363,31 @@ def _lower_rmsnorm(spec, prog, st, loads):
     sq = mean.args[0].value
     if not (isinstance(sq, F.Op) and sq.name == "mul" and key(sq.args[0]) == key(sq.args[1])):
         raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: the reduced value is not x * x")
+    xv = sq.args[0]
+    if isinstance(xv, F.Load):
+        row, res = xv, None
+    elif isinstance(xv, F.Op) and xv.name == "add" and all(isinstance(a, F.Load) for a in xv.args) \
+            and xv.args[0].arg != xv.args[1].arg and key(F.Load(0, xv.args[0].index)) == key(F.Load(0, xv.args[1].index)):
+        row, res = xv.args
+    else:
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: RMSNorm of something other than a row or a row sum")
+    if row.mask is not None or (res is not None and res.mask is not None):
+        raise Refused(Reason.MASKED_BOX_BEFORE_TENSOR, f"{spec.name}: a masked RMSNorm row")
+    row_args = {row.arg} | ({res.arg} if res is not None else set())
+    w_args = {l.arg for l in loads} - row_args
+    if len(w_args) != 1:
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: RMSNorm wants one row input and one weight")
+    w_arg = w_args.pop()
+    if any(l.arg == w_arg and l.index.vars() != {"r"} for l in loads):
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: the RMSNorm weight is not a row over r")
     d = D.new(D.ROW_RMSNORM, _manifest_args(spec), spec.grid, units=_grid_programs(spec)[0], unit_size=xblock)
     r = d.p.row
     r.rows, r.cols, r.eps = rows, cols, eps
-    r.in_row_stride = _row_index(row_loads[0].index, "RMSNorm load")
-    r.out_row_stride = _row_index(st.index, "RMSNorm store")
-    r.in_arg, r.out_arg, r.weight_arg = row_loads[0].arg, st.arg, w_loads[0].arg
+    r.in_row_stride = _row_index(row.index, "RMSNorm load", rows)
+    r.out_row_stride = _row_index(st.index, "RMSNorm store", rows)
+    r.in_arg, r.out_arg, r.weight_arg = row.arg, st.arg, w_arg
+    if res is not None:
+        r.res_arg_p1 = res.arg + 1
     return Lowered(d, D.describe(d))
 
 
@@ -395,13 +419,21 @@ def _lower_qknorm_rope(spec, prog, st, loads):
     if cos_arg is None or sin_arg is None:
         raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: cannot tell the cos table from the sin table")
     tdig = [dg for dg in sin_load.index.terms if dg.var == "x"]
-    if len(tdig) != 1 or tdig[0].mod is not None:
-        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: the table index is not x // heads")
-    heads = tdig[0].div
-    tok = st.index.terms.get(F.Digit("x", heads, None))
-    head = st.index.terms.get(F.Digit("x", 1, heads))
-    if tok is None or head is None or st.index.terms.get(F.Digit("r")) != 1:
-        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: the store index {st.index} is not r + t*T + h*H")
+    if not tdig:
+        # One token (the decode layer, qwen3_8b_layer_decode_*/02_*): every row is a head and the tables are
+        # the one position's, indexed by r alone; the store index is r + h * H.
+        heads, tok = rows, 0
+        head = st.index.terms.get(F.Digit("x"))
+        if head is None or st.index.terms.get(F.Digit("r")) != 1 or len(st.index.terms) != 2 or st.index.const:
+            raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: the store index {st.index} is not r + h*H")
+    else:
+        if len(tdig) != 1 or tdig[0].mod is not None:
+            raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: the table index is not x // heads")
+        heads = tdig[0].div
+        tok = st.index.terms.get(F.Digit("x", heads, None))
+        head = st.index.terms.get(F.Digit("x", 1, heads))
+        if tok is None or head is None or st.index.terms.get(F.Digit("r")) != 1:
+            raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: the store index {st.index} is not r + t*T + h*H")
     rs = [n for n in walk(v) if isinstance(n, F.Op) and n.name == "rsqrt"]
     inner = rs[0].args[0]
     if not (isinstance(inner, F.Op) and inner.name == "add" and isinstance(inner.args[1], F.Const)):
@@ -412,6 +444,60 @@ def _lower_qknorm_rope(spec, prog, st, loads):
     q.out_tok_stride, q.out_head_stride = tok, head
     q.in_arg, q.weight_arg, q.cos_arg, q.sin_arg, q.out_arg = x_arg, w_arg, cos_arg, sin_arg, st.arg
     q.eps = inner.args[1].v
+    return Lowered(d, D.describe(d))
+
+
+def _lower_rope(spec, prog, st):
+    """The rotary embedding alone (validation/pytorchsim/layer_op_rope_{q,k}_*/00_*_triton.py): over [T, H, 128]
+    rows, out = x * cos[t] + rot * sin[t], rot = cat(-x[64:], x[:64]) per row, the fp32 tables per token
+    (index d + 128 * t).  The QK-norm + RoPE kernel with its norm off."""
+    v = st.value
+    if not (isinstance(v, F.Op) and v.name == "add" and all(isinstance(a, F.Op) and a.name == "mul" for a in v.args)):
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: not x * cos + rot * sin")
+    flat = {F.Digit("x"): 1}
+    d_of = F.Digit("x", 1, 128)
+    row_of = F.Digit("x", 128, None)
+    x = cos = sin = rot = None
+    for m in v.args:
+        tab = [a for a in m.args if isinstance(a, F.Load) and spec.args[a.arg].dtype == "float32"]
+        if len(tab) != 1:
+            raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a rotary product without its table")
+        other = next(a for a in m.args if a is not tab[0])
+        if any(isinstance(n, F.Op) and n.name == "where" for n in walk(other)):
+            sin, rot = tab[0], other
+        else:
+            cos, x = tab[0], other
+    if x is None or rot is None or not isinstance(x, F.Load) or x.index.const != 0 or x.index.terms != flat \
+            or x.mask is not None or spec.args[x.arg].dtype != "bfloat16":
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: the rotated rows are not one bf16 load at x")
+    numel = int(_lookup(spec, prog, "xnumel") or spec.args[st.arg].numel)
+    tdig = [dg for dg in cos.index.terms if dg != d_of]
+    one_token = not tdig and cos.index.terms == {d_of: 1}   # T = 1: the one position's tables, indexed by d
+    if cos.index.const != 0 or cos.index.terms.get(d_of) != 1 or key(F.Load(0, cos.index)) != key(F.Load(0, sin.index)) \
+            or not (one_token or (len(tdig) == 1 and tdig[0].mod is None and cos.index.terms[tdig[0]] == 128)):
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: table index {cos.index} is not d + 128 * t")
+    hd = numel if one_token else tdig[0].div
+    if hd % 128:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: tokens of {hd} values are not whole heads")
+    # rot: where(d < 64, -x[row, d + 64], x[row, d - 64]) over the same rows
+    rloads = [n for n in walk(rot) if isinstance(n, F.Load)]
+    negs = [n for n in walk(rot) if isinstance(n, F.Op) and n.name == "neg"]
+    ops = {n.name for n in walk(rot) if isinstance(n, F.Op)}
+    conds = [a for n in walk(rot) if isinstance(n, F.Op) and n.name == "where" for a in n.args[:1]]
+    half = {F.Digit("x", 128, None): 128, d_of: 1}
+    if ops - {"where", "neg"} or len(negs) != 1 or not all(l.arg == x.arg and l.index.terms == half for l in rloads) \
+            or {l.index.const for l in rloads} != {64, -64} or not (isinstance(negs[0].args[0], F.Load) and negs[0].args[0].index.const == 64) \
+            or not all(isinstance(c, F.Cond) and c.op == "lt" and c.value == 64 and c.index.terms == {d_of: 1} for c in conds):
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: the rotated half is not cat(-x[64:], x[:64])")
+    if st.index.const != 0 or st.index.terms != flat or st.mask is not None:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: rotary store index {st.index} is not x")
+    heads, tokens = hd // 128, numel // hd
+    d = D.new(D.QKNORM_ROPE, _manifest_args(spec), spec.grid, units=tokens * heads, unit_size=1)
+    q = d.p.qk
+    q.tokens, q.heads, q.dim = tokens, heads, 128
+    q.out_tok_stride, q.out_head_stride = hd, 128
+    q.in_arg, q.weight_arg, q.cos_arg, q.sin_arg, q.out_arg = x.arg, -1, cos.arg, sin.arg, st.arg
+    q.no_norm = 1
     return Lowered(d, D.describe(d))
 
 
@@ -816,6 +902,24 @@ def _lower_divsum(spec, prog, st, red):
     return Lowered(d, D.describe(d))
 
 
+def _lower_rowsum(spec, prog, st, red):
+    """sum over r of x per row (the MoE layer's top-k weight sums, validation/pytorchsim/layer_layer_prefill_*/
+    22_*_triton.py: an fp32 sum of the 8 weights of each token)."""
+    rows, cols, xblock = _row_sizes(spec, prog, "row sum")
+    ld = red.value
+    if not isinstance(ld, F.Load) or ld.data is not None or ld.mask is not None:
+        raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a row sum of something other than a load")
+    d = D.new(D.ROW_SUM, _manifest_args(spec), spec.grid, units=_grid_programs(spec)[0], unit_size=xblock)
+    r = d.p.row
+    r.rows, r.cols = rows, cols
+    r.in_row_stride = _row_index(ld.index, "row-sum load", rows)
+    r.out_row_stride = 1
+    if st.index.const != 0 or st.index.terms != {F.Digit("x"): 1}:
+        raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: row-sum store index {st.index} is not x")
+    r.in_arg, r.out_arg, r.weight_arg = ld.arg, st.arg, -1
+    return Lowered(d, D.describe(d))
+
+
 _NO_MOD = 1 << 62
 _CMP = {"cmp_lt": "lt", "cmp_le": "le", "cmp_gt": "gt", "cmp_ge": "ge", "cmp_eq": "eq", "cmp_ne": "ne"}
 _IBIN = {"add": "add", "sub": "sub", "mul": "mul", "idiv": "div", "imod": "mod", "iand": "and", "ior": "or",
@@ -1069,9 +1173,30 @@ def _lower_gather_sum(spec, prog, st, red):
         raise Refused(Reason.MASKED_STORE_NOT_A_BOX, f"{spec.name}: a masked weighted gather")
     if st.index.const != 0 or st.index.terms != {F.Digit("x"): 1}:
         raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: weighted gather store index {st.index} is not x")
+
+    def at_out(n):
+        return isinstance(n, F.Load) and n.data is None and n.mask is None and n.index.const == 0 \
+            and n.index.terms == {F.Digit("x"): 1}
+
+    # The MoE layer's fused combine (layer_layer_*/23_*, 27_*) adds the residual stream: (a + b) + sum.
+    residuals = []
+    if st.value is not red:
+        v = st.value
+        if not (isinstance(v, F.Op) and v.name == "add" and v.args[1] is red):
+            raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: a weighted gather with work after the sum")
+        rs = v.args[0]
+        if at_out(rs):
+            residuals = [rs.arg]
+        elif isinstance(rs, F.Op) and rs.name == "add" and all(at_out(a) for a in rs.args):
+            residuals = [rs.args[0].arg, rs.args[1].arg]
+        else:
+            raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: the added rows are not loads at the output index")
     prod = strip_casts(red.value)
     a0, a1 = (strip_casts(a) for a in prod.args)
     tab, w = (a0, a1) if isinstance(a0, F.Load) and a0.data is not None else (a1, a0)
+    divisor = None
+    if isinstance(w, F.Op) and w.name == "div" and all(isinstance(a, F.Load) for a in w.args):
+        w, divisor = w.args   # weights renormalised by their sum (layer_layer_*/23_*, 27_*)
     if not (isinstance(w, F.Load) and w.data is None) or tab.mask is not None or w.mask is not None:
         raise Refused(Reason.PROGRAM_CLASS_UNKNOWN, f"{spec.name}: not a gathered row times a weight")
     aff = tab.index
@@ -1104,6 +1229,17 @@ def _lower_gather_sum(spec, prog, st, red):
     g.w_map = _term_map(spec, w.index, C, terms, w.arg)
     for i, m in enumerate(maps):
         g.maps[i] = m
+    if divisor is not None:
+        # divided per output row: a fixed element, or one per row (x // C)
+        di = divisor.index
+        if divisor.data is not None or divisor.mask is not None or \
+                (di.terms and (len(di.terms) != 1 or next(iter(di.terms)) != F.Digit("x", C, None))):
+            raise Refused(Reason.DESCRIPTOR_CANNOT_STATE, f"{spec.name}: weight divisor index {di} is not a per-row element")
+        g.wdiv, g.wdiv_arg, g.wdiv_offset = 1, divisor.arg, di.const
+        g.wdiv_stride = next(iter(di.terms.values())) if di.terms else 0
+    g.nres = len(residuals)
+    for i, a in enumerate(residuals):
+        g.res_arg[i] = a
     for i, ins in enumerate(code):
         g.code[i] = ins
     return Lowered(d, D.describe(d))

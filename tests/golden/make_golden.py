@@ -193,6 +193,27 @@ def cases():
         ("qwen3_decode_06_rmsnorm_gate_up_mm", spec_file(dw, 6),
          {"family": "rmsnorm_gemv", "K": 4096, "N": 24576, "eps": EPS, "residual": True}, True),
         ("qwen3_decode_07_silu_down_mm", spec_file(dw, 7), {"family": "silu_gemv", "K": 12288, "N": 4096}, True),
+        ("qwen3_decode_02_qnorm_rope", spec_file(dw, 2),
+         {"family": "qknorm_rope", "tokens": 1, "heads": 32, "eps": EPS, "inout_first": True}, True),
+    ]
+    # The Qwen3-30B-A3B MoE layer's own fused programs (hidden 2048, 128 experts, top-8): the combine with
+    # renormalised weights and the residual stream (decode 23 at T = 1, prefill 27 at T = 128), the RMSNorm
+    # of the residual sum (prefill 18), the per-token weight sums (prefill 22), the rotary embedding layer ops
+    # (32 q / 4 k heads of 128) and the one-token RMSNorm layer op.
+    ld, lp = "layer_layer_decode_1x128_bf16", "layer_layer_prefill_128x128_bf16"
+    out += [
+        ("moe_layer_decode_23_combine", spec_file(ld, 23),
+         {"family": "combine_weighted_fused", "tokens": 1, "hidden": 2048, "topk": 8, "experts": 128}, True),
+        ("moe_layer_prefill_27_combine", spec_file(lp, 27),
+         {"family": "combine_weighted_fused", "tokens": 128, "hidden": 2048, "topk": 8, "experts": 128}, True),
+        ("moe_layer_prefill_18_rmsnorm_residual", spec_file(lp, 18),
+         {"family": "rmsnorm_rows", "rows": 128, "cols": 2048, "eps": EPS, "residual": True}, True),
+        ("moe_layer_prefill_22_weight_sum", spec_file(lp, 22), {"family": "row_sum", "rows": 128, "cols": 8}, True),
+        ("moe_rope_q_t128", spec_file("layer_op_rope_q_128x0_bf16", 0), {"family": "rope_rows", "tokens": 128, "heads": 32}, True),
+        ("moe_rope_k_t128", spec_file("layer_op_rope_k_128x0_bf16", 0), {"family": "rope_rows", "tokens": 128, "heads": 4}, True),
+        ("moe_rope_q_t1", spec_file("layer_op_rope_q_1x0_bf16", 0), {"family": "rope_rows", "tokens": 1, "heads": 32}, True),
+        ("moe_rmsnorm_t1", spec_file("layer_op_rmsnorm_1x0_bf16", 0),
+         {"family": "rmsnorm_rows", "rows": 1, "cols": 2048, "eps": EPS}, True),
     ]
     for m in (128, 512, 2048, 4096, 8192):
         out.append((f"gemm_{m}x4096x4096", spec_file(f"gemm_{m}x4096x4096_bf16", 0),

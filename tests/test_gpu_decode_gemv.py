@@ -209,3 +209,20 @@ def test_fused_vector_load_out_of_range_is_recorded():
     with pytest.raises(native.ExecutorError) as e:
         RC.launch_tensors(D.to_bytes(desc), [t.cuda() for t in ts])
     assert e.value.code == D.E_OOB
+
+
+@pytest.mark.parametrize("tokens,heads", [(4096, 32), (1, 4), (333, 8)])
+def test_rope_rows(tokens, heads):
+    """The rotary embedding layer op: the QK kernel with its norm off."""
+    from tests.test_oracle_golden import make_inputs
+    g = torch.Generator().manual_seed(tokens)
+    n = tokens * heads * 128
+    x = torch.randn(n, generator=g).to(torch.bfloat16)
+    cos, sin = torch.randn(tokens * 128, generator=g), torch.randn(tokens * 128, generator=g)
+    desc = B.qknorm_rope(tokens, heads)
+    q = desc.p.qk
+    q.no_norm, q.out_tok_stride, q.out_head_stride = 1, heads * 128, 128
+    ts = [x, torch.zeros(128, dtype=torch.bfloat16), cos, sin, torch.zeros(n, dtype=torch.bfloat16)]
+    got = run(desc, ts)[4]
+    ok, rep = compare(got, O.rope_rows(x, cos, sin, tokens, heads), RTOL, ATOL)
+    assert ok, rep

@@ -212,6 +212,24 @@ def test_combine_weighted(tokens, hidden, topk, experts):
     assert ok, rep
 
 
+@pytest.mark.parametrize("tokens,hidden", [(4096, 2048), (1, 2048), (37, 200)])
+def test_combine_weighted_fused(tokens, hidden):
+    """The MoE layer's combine: weights renormalised by each token's sum, the residual stream added."""
+    topk, experts = 8, 128
+    ids, cum, cnt, pos = moe_routing(tokens, topk, experts, tokens + 5)
+    g = torch.Generator().manual_seed(2)
+    expert_out = torch.randn(tokens * topk * hidden, generator=g).to(torch.bfloat16)
+    w = torch.rand(tokens * topk, generator=g)
+    wsum = w.view(tokens, topk).sum(dim=1)
+    res = torch.randn(tokens * hidden, generator=g).to(torch.bfloat16)
+    out0 = torch.randn(tokens * hidden, generator=g).to(torch.bfloat16)
+    ins = [ids, cum, cnt, pos, expert_out, w, wsum, res, out0.clone()]
+    got = run(B.combine_gather_sum(tokens, hidden, topk, experts, fused=True), ins)[8]
+    want = O.combine_weighted_fused(ids, cum, cnt, pos, expert_out, w, wsum, res, out0, tokens, hidden, topk, experts)
+    ok, rep = compare(got, want, 1e-2, 1e-2)
+    assert ok, rep
+
+
 def test_combine_out_of_range_is_recorded():
     tokens, hidden, topk, experts = 8, 64, 2, 4
     ids, cum, cnt, pos = moe_routing(tokens, topk, experts, 3)

@@ -94,9 +94,19 @@ def run_oracle(case, ins):
     if fam == "dispatch_gather":
         return outs[0], O.dispatch_gather(x[0], x[1], o["tokens"], o["hidden"], o["topk"])
     if fam == "rmsnorm_rows":
+        if o.get("residual"):
+            return outs[0], O.rmsnorm_rows(x[0], x[2], o["rows"], o["cols"], o["eps"], res=x[1])
         return outs[0], O.rmsnorm_rows(x[0], x[1], o["rows"], o["cols"], o["eps"])
+    if fam == "row_sum":
+        return outs[0], O.row_sum(x[0], o["rows"], o["cols"])
+    if fam == "rope_rows":
+        return outs[0], O.rope_rows(x[0], x[1], x[2], o["tokens"], o["heads"])
+    if fam == "combine_weighted_fused":
+        return outs[0], O.combine_weighted_fused(x[1], x[2], x[3], x[4], x[5], x[6], x[7], x[8], x[0], o["tokens"],
+                                                 o["hidden"], o["topk"], o["experts"])
     if fam == "qknorm_rope":
-        return outs[0], O.qknorm_rope(x[0], x[1], x[2], x[3], o["tokens"], o["heads"], o["eps"])
+        q = x[1:] if o.get("inout_first") else x    # the decode program's output row comes first, unread
+        return outs[0], O.qknorm_rope(q[0], q[1], q[2], q[3], o["tokens"], o["heads"], o["eps"])
     if fam == "token_to_head_major":
         return outs[0], O.token_to_head_major(x[0], o["tokens"], o["heads"], o["dim"])
     if fam == "heads_to_token_major":
