@@ -490,6 +490,11 @@ def suite(dev, stream, iters=5, only=None, warm=1):
         timed("moe_combine_t4096_00_counts", "hbm", 8 * 32768 * 128 + 8 * 32768 + 8 * 128, given={"in_ptr0": ids})
         run_ = torch.randint(0, 300, (32768 * 128,), generator=torch.Generator().manual_seed(3))
         timed("moe_combine_t4096_02_slot", "hbm", 3 * 8 * 32768, given={"in_ptr0": run_, "in_ptr1": ids})
+    # The Qwen3-8B decode layer's fused matrix-vector products: the RMSNorm'd vector times the gate_up weights
+    # (4096 x 24576, residual row added first), the SiLU'd vector times the down weights (12288 x 4096, two
+    # residual rows added after); each streams its weights once.
+    timed("qwen3_decode_06_rmsnorm_gate_up_mm", "hbm", 2 * 4096 * 24576 + 2 * 3 * 4096 + 4 + 2 * 24576)
+    timed("qwen3_decode_07_silu_down_mm", "hbm", 2 * 12288 * 4096 + 2 * 24576 + 2 * 3 * 4096)
     for nm, K, N in (("moe_gmm_gate_up_t4096", 2048, 1536), ("moe_gmm_down_t4096", 768, 2048)):
         if only is None or only == nm:
             out[nm] = grouped_gemm_timing(dev, stream, iters, warm, flush, hbm, tflops, K, N)
