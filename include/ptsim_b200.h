@@ -354,7 +354,7 @@ int ptsim_launch(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int
 
 /* Bytes of device scratch a launch of `desc` wants on `device` (-1 on a bad descriptor): the REDUCE_ALL
  * pass-1 partials, the ATTN_DECODE per-chunk softmax states, the INT_TABLE segment totals of a split row
- * scan, else desc->workspace_bytes.  No reference counterpart (Spike needed no device
+ * scan, the M = 1 GEMM's partial columns, else desc->workspace_bytes.  No reference counterpart (Spike needed no device
  * scratch). */
 int64_t ptsim_workspace_size(const void *desc, size_t desc_bytes, int device);
 

@@ -119,7 +119,9 @@ int launch_rowops(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi
 int launch_qkrope(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c);
 int launch_reduce(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, void *ws, size_t ws_bytes,
                   const LaunchCtx &c);
-int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c);
+int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, void *ws, size_t ws_bytes,
+                const LaunchCtx &c);
+int64_t gemv_workspace(const ptsim_desc &d, int sm_count);
 int reduce_workspace(int sm_count);
 int launch_attention(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c);
 int launch_decode(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, void *ws, size_t ws_bytes,

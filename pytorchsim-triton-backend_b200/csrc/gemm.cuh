@@ -618,37 +618,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2_tcgen05_kernel(const __
 // ---------------------------------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------------------------------
-static PFN_cuTensorMapEncodeTiled_v12000 get_encode_tiled() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (fn == nullptr) {
-    void *p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
-// 2-D bf16 tensor map over a row-major [rows, cols] matrix with row stride `ld` elements, box
-// {box_cols (inner), box_rows}, 128-byte swizzle, zero fill outside the matrix.
-static int make_tmap_2d(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_cols,
-                        uint32_t box_rows) {
-  auto enc = get_encode_tiled();
-  if (enc == nullptr) return fail(PTSIM_E_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return fail(PTSIM_E_ARGS, "TMA base address not 16-byte aligned");
-  if ((ld * 2) % 16 != 0) return fail(PTSIM_E_ARGS, "TMA row stride %llu elements is not a multiple of 16 bytes", (unsigned long long)ld);
-  cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {ld * 2};
-  cuuint32_t box[2] = {box_cols, box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(PTSIM_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
-  return PTSIM_OK;
-}
-
 // Clusters of `splits` CTAs of this kernel that one device runs at once (0 when it cannot), cached.
 template <int BN, bool B_KMAJOR>
 static int max_active_clusters(int splits, const LaunchCtx &c) {
@@ -861,7 +830,8 @@ int launch_grouped_gemm(const ptsim_desc &d, void *const *ptrs, const LaunchCtx 
   return run_gemm<64, false>(g, c);
 }
 
-int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c) {
+int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, void *ws, size_t ws_bytes,
+                const LaunchCtx &c) {
   const ptsim_gemm_params &p = d.p.gemm;
   if (d.arg_dtype[p.a_arg] != PTSIM_DT_BF16 || d.arg_dtype[p.b_arg] != PTSIM_DT_BF16)
     return fail(PTSIM_E_UNSUPPORTED, "GEMM operands must be bf16 (the MXU refuses mixed formats)");
@@ -869,7 +839,7 @@ int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, 
   if (cdt != PTSIM_DT_BF16 && cdt != PTSIM_DT_F32) return fail(PTSIM_E_UNSUPPORTED, "GEMM output must be bf16 or f32");
   if (p.r_arg >= 0 && d.arg_dtype[p.r_arg] != PTSIM_DT_BF16) return fail(PTSIM_E_UNSUPPORTED, "GEMM residual must be bf16");
   // One output row: the matrix-vector product, an HBM stream on the CUDA cores.
-  if (p.M == 1) return lo < hi ? launch_gemv(d, ptrs, c) : PTSIM_OK;
+  if (p.M == 1) return lo < hi ? launch_gemv(d, ptrs, ws, ws_bytes, c) : PTSIM_OK;
   if (p.K % 8 != 0 || p.lda % 8 != 0 || p.ldb % 8 != 0)
     return fail(PTSIM_E_UNSUPPORTED, "GEMM K and leading dimensions must be multiples of 8 (16-byte TMA rows)");
   const int64_t m_begin = lo * d.unit_size;

@@ -16,8 +16,10 @@
 // 07_*): a vector prologue (ptsim_vprog over k: an RMSNorm x * rsqrt(ss / n + eps) * w, a SiLU gate times
 // its up half) is evaluated once per CTA for its K slice into shared memory in fp32, unrounded, as the
 // programs keep it; an epilogue (over n, the dot product in r7) adds residual rows before the store.
+
 #pragma once
 #include "sm100.cuh"
+#include "tmap.cuh"
 #include "vprog.cuh"
 
 namespace ptsim {
@@ -72,7 +74,21 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kn_kernel(const __grid_cons
   const int64_t k_begin = int64_t(blockIdx.y) * g.k_per_cta;
   const int64_t k_end = k_begin + g.k_per_cta < g.K ? k_begin + g.k_per_cta : g.K;
   if (PRO) {
-    for (int64_t k = k_begin + tid; k < k_end; k += kGemvThreads) vec[k - k_begin] = vprog_eval(g.pro, g.t, k, 0.f);
+    // four elements per thread per step, their loads in flight together
+    for (int64_t k0 = k_begin + tid; k0 < k_end; k0 += 4 * kGemvThreads) {
+      int64_t idx[4];
+      bool live[4];
+      float o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        idx[j] = k0 + j * kGemvThreads;
+        live[j] = idx[j] < k_end;
+      }
+      vprog_eval_batch<4>(g.pro, g.t, idx, live, o);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (live[j]) vec[idx[j] - k_begin] = o[j];
+    }
     __syncthreads();
   }
   float acc[8];
@@ -119,6 +135,112 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kn_kernel(const __grid_cons
     }
   }
   sm100::cluster_sync();
+}
+
+// Row-streaming path (N-contiguous B, N % 8 == 0, with scratch): a CTA of 1024 threads covers 2048 adjacent
+// columns (4 KB of each row) with 4 row groups of 256 column threads, each thread with kGrU 16-byte loads in
+// flight -- 32 warps and 128 KB of reads in flight per SM, the occupancy a streaming read needs here.  K is
+// cut over grid.y (about one CTA per SM in all); the row groups meet in shared memory and every CTA writes
+// its partial columns to scratch, which gemv_reduce_kernel sums in split order (fixed) before the
+// epilogue and the store.
+constexpr int kGrU = 8, kGrRG = 4, kGrThreads = 256 * kGrRG, kGrCols = 2048;
+
+template <bool PRO>
+__global__ void __launch_bounds__(kGrThreads, 1) gemv_rows_kernel(const __grid_constant__ GemvArgs g, float *part) {
+  extern __shared__ float vec[];             // the K slice, then [kGrRG][kGrCols] row-group partials
+  const int tid = threadIdx.x, ct = tid % 256, rg = tid / 256;
+  const int64_t n0 = int64_t(blockIdx.x) * kGrCols;
+  const int64_t k_begin = int64_t(blockIdx.y) * g.k_per_cta;
+  const int64_t k_end = k_begin + g.k_per_cta < g.K ? k_begin + g.k_per_cta : g.K;
+  if (PRO) {
+    for (int64_t k0 = k_begin + tid; k0 < k_end; k0 += 4 * kGrThreads) {
+      int64_t idx[4];
+      bool live[4];
+      float o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        idx[j] = k0 + j * kGrThreads;
+        live[j] = idx[j] < k_end;
+      }
+      vprog_eval_batch<4>(g.pro, g.t, idx, live, o);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (live[j]) vec[idx[j] - k_begin] = o[j];
+    }
+  } else {
+    for (int64_t k = k_begin + tid; k < k_end; k += kGrThreads) vec[k - k_begin] = bf16_bits_to_f32(__ldg(g.a + k));
+  }
+  __syncthreads();
+  const int64_t col = n0 + ct * 8;
+  const bool ok = col < g.N;
+  float acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+  if (ok) {
+    const uint16_t *bp = g.b + col;
+    int64_t k = k_begin + rg;
+    for (; k + (kGrU - 1) * kGrRG < k_end; k += kGrU * kGrRG) {
+      uint4 v[kGrU];
+#pragma unroll
+      for (int u = 0; u < kGrU; ++u) v[u] = __ldcs(reinterpret_cast<const uint4 *>(bp + (k + u * kGrRG) * g.ldb));
+#pragma unroll
+      for (int u = 0; u < kGrU; ++u) gemv_fma8(acc, vec[k + u * kGrRG - k_begin], v[u]);
+    }
+    for (; k < k_end; k += kGrRG) gemv_fma8(acc, vec[k - k_begin], __ldcs(reinterpret_cast<const uint4 *>(bp + k * g.ldb)));
+  }
+  __syncthreads();   // the vector slice is read; its space holds the row groups' partials now
+  float *red = vec;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) red[rg * kGrCols + ct * 8 + e] = acc[e];
+  __syncthreads();
+  float *dst = part + int64_t(blockIdx.y) * g.N;
+  for (int c = tid; c < kGrCols; c += kGrThreads) {
+    if (n0 + c >= g.N) break;
+    float s = 0.f;
+#pragma unroll
+    for (int q = 0; q < kGrRG; ++q) s += red[q * kGrCols + c];
+    dst[n0 + c] = s;
+  }
+}
+
+// out[n] = the splits' partial columns summed in split order, then the epilogue / residual and the store.
+__global__ void __launch_bounds__(kGemvThreads) gemv_reduce_kernel(const __grid_constant__ GemvArgs g, const float *part,
+                                                                     int splits) {
+  const int64_t n = int64_t(blockIdx.x) * kGemvThreads + threadIdx.x;
+  if (n >= g.N) return;
+  float s = 0.f;
+  for (int q = 0; q < splits; ++q) s += __ldcs(part + int64_t(q) * g.N + n);
+  gemv_store(g, n, s);
+}
+
+// The row-streaming plan: 2048-column tiles, about one CTA per SM, at least 32 rows and at most kGrMaxRows (the
+// staged vector) per CTA.
+constexpr int64_t kGrMaxRows = 12288;
+// Matrices from 32M elements (64 MB) up stream on this path; smaller ones run the single-launch cluster path,
+// where the second launch and the short K slices of a split over every SM cost more than they save.
+constexpr int64_t kGrMinElems = int64_t(32) << 20;
+struct GemvRowsPlan {
+  int splits;
+  int64_t tiles, k_per_cta;
+};
+static GemvRowsPlan plan_gemv_rows(int64_t N, int64_t K, int sm_count) {
+  GemvRowsPlan pl;
+  pl.tiles = ceil_div(N, int64_t(kGrCols));
+  int64_t s = int64_t(sm_count) / pl.tiles;
+  if (s > K / 32) s = K / 32;
+  if (s < 1) s = 1;
+  while (ceil_div(K, s) > kGrMaxRows) ++s;
+  pl.k_per_cta = ceil_div(K, s);
+  pl.splits = int(ceil_div(K, pl.k_per_cta));
+  return pl;
+}
+
+// Scratch of a matrix-vector launch (the row-streaming path's partial columns), 0 for other GEMMs.
+int64_t gemv_workspace(const ptsim_desc &d, int sm_count) {
+  const ptsim_gemm_params &p = d.p.gemm;
+  if (p.M != 1 || p.b_kmajor || p.N % 8 != 0 || p.ldb % 8 != 0 || p.K * p.N < kGrMinElems) return 0;
+  const GemvRowsPlan pl = plan_gemv_rows(p.N, p.K, sm_count);
+  return int64_t(pl.splits) * p.N * int64_t(sizeof(float));
 }
 
 // K-major B: warp w of CTA b computes column n = 8 b + w; lanes take 8 consecutive k, 256 k per step.
@@ -208,7 +330,7 @@ static int run_gemv_kn(const GemvArgs &g, const GemvPlan &pl, const LaunchCtx &c
 }
 
 // The GEMM descriptor with M = 1 (checked by the caller), on the CUDA cores.
-static int launch_gemv(const ptsim_desc &d, void *const *ptrs, const LaunchCtx &c) {
+static int launch_gemv(const ptsim_desc &d, void *const *ptrs, void *ws, size_t ws_bytes, const LaunchCtx &c) {
   const ptsim_gemm_params &p = d.p.gemm;
   GemvArgs g;
   memset(&g, 0, sizeof(g));
@@ -236,6 +358,25 @@ static int launch_gemv(const ptsim_desc &d, void *const *ptrs, const LaunchCtx &
   }
   if (p.N % 8 != 0 || p.ldb % 8 != 0)
     return fail(PTSIM_E_UNSUPPORTED, "GEMV over [K, N] needs N and the row stride multiples of 8");
+  {
+    const GemvRowsPlan pr = plan_gemv_rows(p.N, p.K, c.sm_count);
+    const int64_t need = int64_t(pr.splits) * p.N * int64_t(sizeof(float));
+    if (p.K * p.N >= kGrMinElems && ws != nullptr && int64_t(ws_bytes) >= need && reinterpret_cast<uintptr_t>(ws) % 16 == 0) {
+      GemvArgs gr = g;
+      gr.k_per_cta = pr.k_per_cta;
+      float *part = reinterpret_cast<float *>(ws);
+      const dim3 grid(unsigned(pr.tiles), unsigned(pr.splits));
+      const int64_t vec_bytes = pr.k_per_cta * int64_t(sizeof(float)), red_bytes = int64_t(kGrRG) * kGrCols * int64_t(sizeof(float));
+      const size_t smem = size_t(vec_bytes > red_bytes ? vec_bytes : red_bytes);
+      if (pro) PTSIM_CUDA((smem_limit_once<gemv_rows_kernel<true>>(int(kGrMaxRows * 4), c.device)));
+      else PTSIM_CUDA((smem_limit_once<gemv_rows_kernel<false>>(int(kGrMaxRows * 4), c.device)));
+      if (pro) gemv_rows_kernel<true><<<grid, kGrThreads, smem, c.stream>>>(gr, part);
+      else gemv_rows_kernel<false><<<grid, kGrThreads, smem, c.stream>>>(gr, part);
+      gemv_reduce_kernel<<<unsigned(ceil_div(p.N, int64_t(kGemvThreads))), kGemvThreads, 0, c.stream>>>(gr, part, pr.splits);
+      PTSIM_CUDA(cudaGetLastError());
+      return PTSIM_OK;
+    }
+  }
   const GemvPlan pl = plan_gemv(p.N, p.K, c.sm_count);
   g.k_per_cta = pl.k_per_cta;
   if (pro) {

@@ -398,7 +398,7 @@ int ptsim_launch(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int
     case PTSIM_KIND_GATHER_SUM: return launch_gather_sum(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_INT_TABLE: return launch_itab(d, dev_ptrs, lo, hi, workspace, workspace_bytes, c);
     case PTSIM_KIND_QKNORM_ROPE: return launch_qkrope(d, dev_ptrs, lo, hi, c);
-    case PTSIM_KIND_GEMM: return launch_gemm(d, dev_ptrs, lo, hi, c);
+    case PTSIM_KIND_GEMM: return launch_gemm(d, dev_ptrs, lo, hi, workspace, workspace_bytes, c);
     case PTSIM_KIND_ATTN_PREFILL: return launch_attention(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_REDUCE_ALL: return launch_reduce(d, dev_ptrs, lo, hi, workspace, workspace_bytes, c);
     case PTSIM_KIND_ATTN_DECODE: return launch_decode(d, dev_ptrs, lo, hi, workspace, workspace_bytes, c);
@@ -416,6 +416,7 @@ int64_t ptsim_workspace_size(const void *desc, size_t desc_bytes, int device) {
   if (d.kind == PTSIM_KIND_REDUCE_ALL && need < reduce_workspace(sm_count)) need = reduce_workspace(sm_count);
   if (d.kind == PTSIM_KIND_ATTN_DECODE && need < decode_workspace(d, sm_count)) need = decode_workspace(d, sm_count);
   if (d.kind == PTSIM_KIND_INT_TABLE && need < itab_workspace(d, sm_count)) need = itab_workspace(d, sm_count);
+  if (d.kind == PTSIM_KIND_GEMM && need < gemv_workspace(d, sm_count)) need = gemv_workspace(d, sm_count);
   return need;
 }
 

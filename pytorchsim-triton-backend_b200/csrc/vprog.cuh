@@ -39,15 +39,15 @@ __device__ __forceinline__ float vprog_load(const VArgs &t, const ptsim_vload &l
   return 0.f;
 }
 
-// The program's value at index i (r7 = `in` when it starts).
-__device__ __forceinline__ float vprog_eval(const ptsim_vprog &p, const VArgs &t, int64_t i, float in) {
+// The program over its loaded values pre[] (load slot l's element for this index; r7 = `in` when it starts).
+__device__ __forceinline__ float vprog_run(const ptsim_vprog &p, const float (&pre)[PTSIM_VPROG_LOADS], float in) {
   float r[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, in};
   float o = in;
   for (int k = 0; k < p.ncode; ++k) {
     const ptsim_insn &c = p.code[k];
     const float a = r[c.a & 7], b = r[c.b & 7];
     switch (c.op) {
-      case PTSIM_OP_LOAD: o = vprog_load(t, p.load[c.a % PTSIM_VPROG_LOADS], i); break;
+      case PTSIM_OP_LOAD: o = pre[c.a % PTSIM_VPROG_LOADS]; break;
       case PTSIM_OP_CONST: o = c.imm; break;
       case PTSIM_OP_ADD: o = __fadd_rn(a, b); break;
       case PTSIM_OP_SUB: o = __fsub_rn(a, b); break;
@@ -65,6 +65,28 @@ __device__ __forceinline__ float vprog_eval(const ptsim_vprog &p, const VArgs &t
     r[c.dst & 7] = o;
   }
   return o;
+}
+
+// The program's value at index i.  Every LOAD runs unconditionally, so all of them are issued before the
+// program runs: one memory round trip per evaluation, not one per load.
+__device__ __forceinline__ float vprog_eval(const ptsim_vprog &p, const VArgs &t, int64_t i, float in) {
+  float pre[PTSIM_VPROG_LOADS];
+#pragma unroll
+  for (int l = 0; l < PTSIM_VPROG_LOADS; ++l) pre[l] = l < p.nload ? vprog_load(t, p.load[l], i) : 0.f;
+  return vprog_run(p, pre, in);
+}
+
+// B indices at once: the loads of all of them in flight together, then the B programs.
+template <int B>
+__device__ __forceinline__ void vprog_eval_batch(const ptsim_vprog &p, const VArgs &t, const int64_t (&idx)[B],
+                                                 const bool (&live)[B], float (&out)[B]) {
+  float pre[B][PTSIM_VPROG_LOADS];
+#pragma unroll
+  for (int j = 0; j < B; ++j)
+#pragma unroll
+    for (int l = 0; l < PTSIM_VPROG_LOADS; ++l) pre[j][l] = (live[j] && l < p.nload) ? vprog_load(t, p.load[l], idx[j]) : 0.f;
+#pragma unroll
+  for (int j = 0; j < B; ++j) out[j] = live[j] ? vprog_run(p, pre[j], 0.f) : 0.f;
 }
 
 }  // namespace ptsim

@@ -65,6 +65,14 @@ def test_gemv_residual_and_fp32_output():
     _gemv_case(1536, 512, out_dtype="float32")
 
 
+@pytest.mark.parametrize("K,N,residual,out_dtype", [(8192, 8192, False, "bfloat16"), (30000, 2056, True, "bfloat16"),
+                                                    (4096, 12296, False, "float32"), (131072, 256, True, "float32")])
+def test_gemv_row_streaming(K, N, residual, out_dtype):
+    """Matrices from 32M elements stream whole 4 KB row runs with partial columns in scratch: ragged column
+    tiles (N not a multiple of 2048), K slices of many rows, the residual and fp32 stores after the sum."""
+    _gemv_case(N, K, residual=residual, out_dtype=out_dtype)
+
+
 def test_gemv_refuses_ragged_columns():
     """N-contiguous rows must be 16-byte vectors: N % 8 != 0 is refused, never approximated."""
     d = B.gemv(12, 64)
