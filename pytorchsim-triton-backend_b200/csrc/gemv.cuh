@@ -203,14 +203,31 @@ __global__ void __launch_bounds__(kGrThreads, 1) gemv_rows_kernel(const __grid_c
   }
 }
 
-// out[n] = the splits' partial columns summed in split order, then the epilogue / residual and the store.
+// out[n] = the splits' partial columns summed, then the epilogue / residual and the store.  A CTA takes 32
+// columns with 8 threads each: thread j sums splits j, j + 8, ... in order (eight loads in flight), and the
+// 8 sums are added in j order -- a fixed order, so every launch gives the same bits.
 __global__ void __launch_bounds__(kGemvThreads) gemv_reduce_kernel(const __grid_constant__ GemvArgs g, const float *part,
                                                                      int splits) {
-  const int64_t n = int64_t(blockIdx.x) * kGemvThreads + threadIdx.x;
-  if (n >= g.N) return;
+  __shared__ float sh[8][32];
+  const int c = threadIdx.x & 31, j = threadIdx.x >> 5;
+  const int64_t n = int64_t(blockIdx.x) * 32 + c;
   float s = 0.f;
-  for (int q = 0; q < splits; ++q) s += __ldcs(part + int64_t(q) * g.N + n);
-  gemv_store(g, n, s);
+  if (n < g.N)
+    for (int q0 = j; q0 < splits; q0 += 64) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = q0 + 8 * u < splits ? __ldcs(part + int64_t(q0 + 8 * u) * g.N + n) : 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) s += v[u];
+    }
+  sh[j][c] = s;
+  __syncthreads();
+  if (j == 0 && n < g.N) {
+    float t = sh[0][c];
+#pragma unroll
+    for (int q = 1; q < 8; ++q) t += sh[q][c];
+    gemv_store(g, n, t);
+  }
 }
 
 // The row-streaming plan: 2048-column tiles, about one CTA per SM, at least 32 rows and at most kGrMaxRows (the
@@ -372,7 +389,7 @@ static int launch_gemv(const ptsim_desc &d, void *const *ptrs, void *ws, size_t 
       else PTSIM_CUDA((smem_limit_once<gemv_rows_kernel<false>>(int(kGrMaxRows * 4), c.device)));
       if (pro) gemv_rows_kernel<true><<<grid, kGrThreads, smem, c.stream>>>(gr, part);
       else gemv_rows_kernel<false><<<grid, kGrThreads, smem, c.stream>>>(gr, part);
-      gemv_reduce_kernel<<<unsigned(ceil_div(p.N, int64_t(kGemvThreads))), kGemvThreads, 0, c.stream>>>(gr, part, pr.splits);
+      gemv_reduce_kernel<<<unsigned(ceil_div(p.N, int64_t(32))), kGemvThreads, 0, c.stream>>>(gr, part, pr.splits);
       PTSIM_CUDA(cudaGetLastError());
       return PTSIM_OK;
     }

@@ -368,11 +368,20 @@ __global__ void __launch_bounds__(1024) onehot_scan_kernel(const __grid_constant
   const bool live = xi < a.nx;
   const int64_t x = a.lo + xi;
   int64_t pb = 0, pt = 0;
-  if (live)
-    for (int64_t q = grp; q < chunks; q += a.groups) {
-      const int64_t v = a.counts[q * a.nx + xi];
-      if (q < c) pb += v;
-      pt += v;
+  if (live)   // this group's share of the chunk counts, eight loads in flight (integer sums: any order)
+    for (int64_t q0 = grp; q0 < chunks; q0 += 8 * int64_t(a.groups)) {
+      int64_t v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t q = q0 + int64_t(u) * a.groups;
+        v[u] = q < chunks ? __ldcg(a.counts + q * a.nx + xi) : 0;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t q = q0 + int64_t(u) * a.groups;
+        if (q < c) pb += v[u];
+        pt += v[u];
+      }
     }
   __syncthreads();
   const int64_t g0 = r0 + int64_t(grp) * kOnehotSub, g1 = min(r1, g0 + kOnehotSub);
