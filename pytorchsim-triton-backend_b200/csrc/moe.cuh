@@ -391,8 +391,8 @@ int launch_gather_rows(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64
 // Gather-sum: the MoE combine (validation/pytorchsim/layer_op_combine_*/03_*: out[t, d] = sum over the top-k
 // terms k of w[t, k] * expert_out[p(t, k), d], p the row where token t's k-th expert wrote it, read through
 // the expert id, that expert's running offsets and the slot).  The index programs of 32 (row, term) pairs
-// run at once (lane l: row r0 + l / terms, term l % terms); each row is then accumulated over its terms in
-// order, 8 columns per thread per step with 16-byte loads.
+// run at once on one warp; each row is then accumulated over its terms in order by 256 threads, 8 columns
+// per thread per step with 16-byte loads.
 // ---------------------------------------------------------------------------------------------------
 struct GsumArgs {
   const void *arg[PTSIM_MAX_ARGS];
@@ -474,9 +474,8 @@ __device__ int64_t gsum_row_of(const GsumArgs &g, int64_t f) {
   return res;
 }
 
-// A CTA takes 32 / terms output rows: warp 0 evaluates their (row, term) index programs into shared memory,
-// then all 256 threads split the columns, each loading its 8-column slice of every term's row (all TERMS
-// loads in flight when the term count is a template constant) before accumulating in term order.
+// One output row's 8-column slice: the slice of every term's table row loaded (all TERMS loads in flight when
+// the term count is a template constant), then accumulated in term order, the residual rows added, stored.
 template <int TERMS>
 __device__ __forceinline__ void gsum_slice(const GsumArgs &g, const int64_t *rows, const float *ws, int nterms,
                                            int64_t orow, int64_t c8) {
@@ -525,16 +524,30 @@ __device__ __forceinline__ void gsum_slice(const GsumArgs &g, const int64_t *row
   }
 }
 
+// Warp-specialised: warp 8 runs a group's (row, term) index programs (32 at once, lane l: row r0 + l / terms,
+// term l % terms) into one half of a double-buffered table while warps 0-7 stream the group before it from
+// the other half; named barriers hand each half over (1 + b: filled, 3 + b: drained, 288 threads each).
+__device__ __forceinline__ void named_bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+__device__ __forceinline__ void named_bar_arrive(int id, int n) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
+constexpr int kGsumThreads = 288;
+
 template <int TERMS>
-__global__ void __launch_bounds__(256) gather_sum_kernel(const __grid_constant__ GsumArgs g) {
-  __shared__ int64_t s_row[32];
-  __shared__ float s_w[32];
+__global__ void __launch_bounds__(kGsumThreads) gather_sum_kernel(const __grid_constant__ GsumArgs g) {
+  __shared__ int64_t s_row[2][32];
+  __shared__ float s_w[2][32];
   const int nterms = TERMS > 0 ? TERMS : int(g.terms);
   const int per = 32 / nterms;
-  for (int64_t r0 = g.row_begin + int64_t(blockIdx.x) * per; r0 < g.row_end; r0 += int64_t(gridDim.x) * per) {
-    __syncthreads();   // the previous group's pairs are read
-    if (threadIdx.x < 32) {
-      const int lane = threadIdx.x;
+  const int64_t stride = int64_t(gridDim.x) * per;
+  const int64_t first = g.row_begin + int64_t(blockIdx.x) * per;
+  const int64_t ngroups = first < g.row_end ? (g.row_end - first + stride - 1) / stride : 0;
+  const int warp = threadIdx.x >> 5;
+  if (warp == 8) {
+    const int lane = threadIdx.x & 31;
+    for (int64_t i = 0; i < ngroups; ++i) {
+      const int b = int(i & 1);
+      const int64_t r0 = first + i * stride;
+      if (i >= 2) named_bar_sync(3 + b, kGsumThreads);   // the consumers are done with this half
       int64_t trow = -1;
       float w = 0.f;
       const int64_t r = r0 + lane / nterms;
@@ -552,13 +565,22 @@ __global__ void __launch_bounds__(256) gather_sum_kernel(const __grid_constant__
           if (g.wdiv) w = __fdiv_rn(w, ld_any(g.arg[g.wdiv_arg], g.dt[g.wdiv_arg], dat));
         }
       }
-      s_row[lane] = trow;
-      s_w[lane] = w;
+      s_row[b][lane] = trow;
+      s_w[b][lane] = w;
+      named_bar_arrive(1 + b, kGsumThreads);
     }
-    __syncthreads();
-    for (int j = 0; j < per && r0 + j < g.row_end; ++j)
-      for (int64_t c8 = int64_t(threadIdx.x) * 8; c8 < g.cols; c8 += int64_t(blockDim.x) * 8)
-        gsum_slice<TERMS>(g, s_row + j * nterms, s_w + j * nterms, nterms, r0 + j, c8);
+    // Match the consumers' drained-arrivals of the last group of each half.
+    for (int64_t i = ngroups >= 2 ? ngroups - 2 : 0; i < ngroups; ++i) named_bar_sync(3 + int(i & 1), kGsumThreads);
+  } else {
+    for (int64_t i = 0; i < ngroups; ++i) {
+      const int b = int(i & 1);
+      const int64_t r0 = first + i * stride;
+      named_bar_sync(1 + b, kGsumThreads);
+      for (int j = 0; j < per && r0 + j < g.row_end; ++j)
+        for (int64_t c8 = int64_t(threadIdx.x) * 8; c8 < g.cols; c8 += 256 * 8)
+          gsum_slice<TERMS>(g, s_row[b] + j * nterms, s_w[b] + j * nterms, nterms, r0 + j, c8);
+      named_bar_arrive(3 + b, kGsumThreads);
+    }
   }
 }
 
@@ -605,10 +627,12 @@ int launch_gather_sum(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_
     return fail(PTSIM_E_ARGS, "gather-sum table and output must be 16-byte aligned");
   if (g.row_end <= g.row_begin) return PTSIM_OK;
   const int per = 32 / int(p.terms);
+  // Three CTAs per SM (288 threads, 64 registers), each taking several groups so the index programs of the
+  // next one run under the current one's stream.
   int64_t blocks = ceil_div(g.row_end - g.row_begin, per);
-  if (blocks > int64_t(c.sm_count) * 16) blocks = int64_t(c.sm_count) * 16;
-  if (p.terms == 8) gather_sum_kernel<8><<<unsigned(blocks), 256, 0, c.stream>>>(g);
-  else gather_sum_kernel<0><<<unsigned(blocks), 256, 0, c.stream>>>(g);
+  if (blocks > int64_t(c.sm_count) * 3) blocks = int64_t(c.sm_count) * 3;
+  if (p.terms == 8) gather_sum_kernel<8><<<unsigned(blocks), kGsumThreads, 0, c.stream>>>(g);
+  else gather_sum_kernel<0><<<unsigned(blocks), kGsumThreads, 0, c.stream>>>(g);
   PTSIM_CUDA(cudaGetLastError());
   return PTSIM_OK;
 }
