@@ -95,3 +95,41 @@ def test_descriptor_round_trip():
     e = D.from_bytes(blob)
     assert (e.kind, e.p.gemm.M, e.p.gemm.N, e.p.gemm.K, e.p.gemm.r_arg) == (D.GEMM, 256, 512, 128, 0)
     assert D.describe(e)["residual"] is True
+
+
+def test_fused_and_routing_descriptors_are_checked_on_the_host():
+    """The newer descriptor fields: fused vector programs, integer tables, the fused combine, the residual
+    RMSNorm row -- valid ones pass ptsim_check, malformed ones are refused with their code."""
+    for good in (B.rmsnorm_gemv(4096, 4096), B.silu_gemv(4096, 12288), B.sumsq(4096, True), B.expert_counts(1024, 128),
+                 B.slot_of(1024, 128), B.group_tables(128), B.count_le(128, 128), B.cumsum_int(128, "int32", "int32"),
+                 B.combine_gather_sum(128, 2048, 8, 128, fused=True)):
+        native.check(D.to_bytes(good))
+    # a vector program with an opcode past the elementwise set, a register past r7, a load slot it lacks
+    for field, value in (("op", 99), ("dst", 8), ("a", 3)):
+        d = B.rmsnorm_gemv(256, 256)
+        setattr(d.p.gemm.pro.code[0], field, value)
+        assert _code(lambda: native.check(D.to_bytes(d))) == D.E_DESC, field
+    # a fused program on a GEMM of M > 1
+    d = B.rmsnorm_gemv(256, 256)
+    d.p.gemm.M = 2
+    assert _code(lambda: native.check(D.to_bytes(d))) in (D.E_DESC, D.E_OOB)
+    # an integer table storing into a float tensor, an output past the table, an unknown instruction
+    d = B.expert_counts(64, 8)
+    d.arg_dtype[1] = D.DTYPE_CODE["float32"]
+    assert _code(lambda: native.check(D.to_bytes(d))) == D.E_UNSUPPORTED
+    d = B.expert_counts(64, 8)
+    d.p.itab.nout = 5
+    assert _code(lambda: native.check(D.to_bytes(d))) == D.E_DESC
+    d = B.expert_counts(64, 8)
+    d.p.itab.code[0].op = 40
+    assert _code(lambda: native.check(D.to_bytes(d))) == D.E_DESC
+    # a combine with three residual rows; a residual RMSNorm whose residual tensor is too short
+    d = B.combine_gather_sum(16, 64, 2, 4, fused=True)
+    d.p.gsum.nres = 3
+    assert _code(lambda: native.check(D.to_bytes(d))) == D.E_DESC
+    d = B.row_rmsnorm(64, 256)
+    d.p.row.res_arg_p1 = 1        # the residual is argument 0: the input itself, as long as the rows -- valid
+    native.check(D.to_bytes(d))
+    d.p.row.rows = 64
+    d.arg_numel[0] = 64 * 256 - 1
+    assert _code(lambda: native.check(D.to_bytes(d))) == D.E_OOB
