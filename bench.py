@@ -505,6 +505,8 @@ def suite(dev, stream, iters=5, only=None, warm=1):
             out[name + "_amortized"] = amortized_object(dev, stream, hbm, name, work, sets)
     if only is None or only == "qwen3_layer":
         out["qwen3_layer_t2048"] = layer_timing(dev, stream, iters, warm, flush, tflops)
+    if only is None or only == "qwen3_decode_layer_s4096":
+        out["qwen3_decode_layer_s4096"] = decode_layer_timing(dev, stream, iters, warm, flush, hbm)
     return out
 
 
@@ -650,6 +652,62 @@ def amortized_object(dev, stream, hbm, name, work, sets, launches=48):
     del graph
     return {"ms_per_launch": round(ms, 5), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm, 3),
             "launches": launches, "sets": sets}
+
+
+def decode_layer_timing(dev, stream, iters, warm, flush, hbm):
+    """The Qwen3-8B decode layer at a 4096-token context (validation/pytorchsim/qwen3_8b_layer_decode_1x4096_bf16:
+    sums of squares, the RMSNorm'd q projection, q-norm + RoPE, decode attention over the KV cache, the o
+    projection, the residual sum's sum of squares, the RMSNorm'd gate_up projection, the SiLU'd down projection)
+    as its 8 lowered kernel objects, one step replayed from a CUDA graph with L2 flushed before it.  Every
+    argument is read or written once: their bytes are the step's algorithmic HBM traffic."""
+    import torch
+    from pytorchsim_triton_compiler.codegen import descriptors as D
+    from pytorchsim_triton_compiler.runtime import native
+    names = sorted(n for n in os.listdir(OBJECTS) if n.startswith("qwen3_decode_s4096_"))
+    g = torch.Generator(device=dev).manual_seed(0)
+    steps, keep, work = [], [], 0
+    for name in names:
+        m, blob = load_object(name)
+        d = D.from_bytes(blob)
+        ts = []
+        for a in m["args"]:
+            dt = getattr(torch, a["dtype"])
+            n = math.prod(a["shape"])
+            t = torch.randn(n, generator=g, device=dev)
+            if n > 1 << 20:
+                t = t / 64.0                       # weights and caches at a realistic scale
+            ts.append((t.abs() if n == 1 else t).to(dt) if a["role"] in ("in", "inout") else torch.zeros(n, dtype=dt, device=dev))
+            work += n * ts[-1].element_size()
+        wsn = native.workspace_size(blob, dev.index or 0)
+        ws = torch.empty(max(1, wsn), dtype=torch.uint8, device=dev)
+        keep += ts + [ws]
+        steps.append((blob, [t.data_ptr() for t in ts], d.units, ws.data_ptr(), wsn))
+    s_ = torch.cuda.Stream(dev)
+    s_.wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s_):
+        for blob, ptrs, units, wp, wn in steps:
+            native.launch(blob, ptrs, 0, units, wp, wn, s_.cuda_stream)
+        native.sync(s_.cuda_stream)
+        with torch.cuda.graph(graph, stream=s_):
+            for blob, ptrs, units, wp, wn in steps:
+                native.launch(blob, ptrs, 0, units, wp, wn, s_.cuda_stream)
+    stream.wait_stream(s_)
+    graph.replay()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters + warm)]
+    for k in range(iters + warm):
+        flush()
+        ev[k][0].record(stream)
+        graph.replay()
+        ev[k][1].record(stream)
+    torch.cuda.synchronize()
+    native.sync(stream.cuda_stream)
+    ms = statistics.median(a.elapsed_time(b) for a, b in ev[warm:])
+    del graph
+    gbs = work / ms / 1e6
+    return {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm, 3), "programs": len(steps),
+            "bytes": work}
 
 
 def layer_timing(dev, stream, iters, warm, flush, tflops):

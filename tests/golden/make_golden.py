@@ -196,6 +196,25 @@ def cases():
         ("qwen3_decode_02_qnorm_rope", spec_file(dw, 2),
          {"family": "qknorm_rope", "tokens": 1, "heads": 32, "eps": EPS, "inout_first": True}, True),
     ]
+    # The whole Qwen3-8B decode layer at a 4096-token context (objects for the GPU parity run and the bench's
+    # decode-layer step; the oracle checks them, the weights are too large for committed vectors).
+    d4 = "qwen3_8b_layer_decode_1x4096_bf16"
+    out += [
+        ("qwen3_decode_s4096_00_sumsq", spec_file(d4, 0), {"family": "sumsq", "n": 4096}, False),
+        ("qwen3_decode_s4096_01_rmsnorm_q_mm", spec_file(d4, 1),
+         {"family": "rmsnorm_gemv", "K": 4096, "N": 4096, "eps": EPS}, False),
+        ("qwen3_decode_s4096_02_qnorm_rope", spec_file(d4, 2),
+         {"family": "qknorm_rope", "tokens": 1, "heads": 32, "eps": EPS, "inout_first": True}, False),
+        ("qwen3_decode_s4096_03_attention", spec_file(d4, 3),
+         {"family": "attention_decode", "hkv": 8, "g": 4, "gp": 16, "seq": 4096, "dim": 128, "bkv": 4096,
+          "scale": 1 / math.sqrt(128)}, False),
+        ("qwen3_decode_s4096_04_o_mm", spec_file(d4, 4), {"family": "gemm", "M": 1, "N": 4096, "K": 4096, "residual": False},
+         False),
+        ("qwen3_decode_s4096_05_sumsq_residual", spec_file(d4, 5), {"family": "sumsq", "n": 4096}, False),
+        ("qwen3_decode_s4096_06_rmsnorm_gate_up_mm", spec_file(d4, 6),
+         {"family": "rmsnorm_gemv", "K": 4096, "N": 24576, "eps": EPS, "residual": True}, False),
+        ("qwen3_decode_s4096_07_silu_down_mm", spec_file(d4, 7), {"family": "silu_gemv", "K": 12288, "N": 4096}, False),
+    ]
     # The Qwen3-30B-A3B MoE layer's own fused programs (hidden 2048, 128 experts, top-8): the combine with
     # renormalised weights and the residual stream (decode 23 at T = 1, prefill 27 at T = 128), the RMSNorm
     # of the residual sum (prefill 18), the per-token weight sums (prefill 22), the rotary embedding layer ops

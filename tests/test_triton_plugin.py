@@ -150,8 +150,10 @@ def test_backend_hash_follows_the_pipeline_source():
     assert before != after
 
 
-def test_keep_option_leaves_the_workdir():
+def test_keep_option_leaves_the_workdir(tmp_path, monkeypatch):
     import shutil
+    # A private Triton cache: a cached compile from an earlier run would name a workdir that run removed.
+    monkeypatch.setenv("TRITON_CACHE_DIR", str(tmp_path / "triton-cache"))
     gone, kept = _compile(ADD), _compile(ADD, pytorchsim_keep_workdir=True)
     work = kept.metadata.workdir
     try:
