@@ -137,69 +137,114 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kn_kernel(const __grid_cons
   sm100::cluster_sync();
 }
 
-// Row-streaming path (N-contiguous B, N % 8 == 0, with scratch): a CTA of 1024 threads covers 2048 adjacent
-// columns (4 KB of each row) with 4 row groups of 256 column threads, each thread with kGrU 16-byte loads in
-// flight -- 32 warps and 128 KB of reads in flight per SM, the occupancy a streaming read needs here.  K is
-// cut over grid.y (about one CTA per SM in all); the row groups meet in shared memory and every CTA writes
-// its partial columns to scratch, which gemv_reduce_kernel sums in split order (fixed) before the
-// epilogue and the store.
-constexpr int kGrU = 8, kGrRG = 4, kGrThreads = 256 * kGrRG, kGrCols = 2048;
+// Row-streaming path (N-contiguous B, N % 8 == 0, with scratch): a CTA covers 2048 adjacent columns (4 KB of each
+// row), K is cut over grid.y (about one CTA per SM in all); every CTA writes its partial columns to scratch and
+// gemv_reduce_kernel sums them in split order (fixed) before the epilogue and the store.
+constexpr int kGrCols = 2048;
+
+// B comes in through the bulk-copy engine, not through loads.  One
+// producer thread copies each row's 4 KB run of the tile (cp.async.bulk, one request per row) into a ring of
+// kGbStages stages of kGbRows rows, 192 KB in flight per CTA with no register cost; 256 consumer threads each own
+// 8 columns of the tile and read their 16 bytes of every row from shared memory, so a column's partial sum is
+// one thread's and the CTA writes its partial columns straight to scratch.
+constexpr int kGbRows = 8, kGbStages = 6;
+constexpr int kGbStageBytes = kGbRows * kGrCols * 2;   // 32 KB
+constexpr int kGbConsumers = 256, kGbThreads = kGbConsumers + 32;
+constexpr int64_t kGbMaxRows = 4096;                   // vector rows a CTA stages (16 KB)
 
 template <bool PRO>
-__global__ void __launch_bounds__(kGrThreads, 1) gemv_rows_kernel(const __grid_constant__ GemvArgs g, float *part) {
-  extern __shared__ float vec[];             // the K slice, then [kGrRG][kGrCols] row-group partials
-  const int tid = threadIdx.x, ct = tid % 256, rg = tid / 256;
+__global__ void __launch_bounds__(kGbThreads, 1) gemv_bulk_kernel(const __grid_constant__ GemvArgs g, float *part) {
+  extern __shared__ __align__(128) uint8_t gb_smem[];
+  uint8_t *ring = gb_smem;
+  float *vec = reinterpret_cast<float *>(gb_smem + kGbStages * kGbStageBytes);
+  __shared__ __align__(8) uint64_t full[kGbStages], empty[kGbStages];
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t n0 = int64_t(blockIdx.x) * kGrCols;
+  const int64_t ncols = g.N - n0 < kGrCols ? g.N - n0 : kGrCols;
+  const uint32_t row_bytes = uint32_t(ncols * 2);
   const int64_t k_begin = int64_t(blockIdx.y) * g.k_per_cta;
   const int64_t k_end = k_begin + g.k_per_cta < g.K ? k_begin + g.k_per_cta : g.K;
-  if (PRO) {
-    for (int64_t k0 = k_begin + tid; k0 < k_end; k0 += 4 * kGrThreads) {
-      int64_t idx[4];
-      bool live[4];
-      float o[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        idx[j] = k0 + j * kGrThreads;
-        live[j] = idx[j] < k_end;
+  const int64_t nrows = k_end - k_begin;
+  const int nst = int((nrows + kGbRows - 1) / kGbRows);
+  if (tid == 0) {
+    for (int st = 0; st < kGbStages; ++st) {
+      sm100::mbar_init(&full[st], 1);
+      sm100::mbar_init(&empty[st], kGbConsumers / 32);
+    }
+    sm100::fence_barrier_init();
+    abort_flag = 0;
+  }
+  __syncthreads();
+  if (warp == kGbConsumers / 32) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < nst; ++i) {
+        const int st = i % kGbStages;
+        if (i >= kGbStages && !sm100::mbar_wait(&empty[st], uint32_t((i / kGbStages - 1) & 1))) {
+          atomicExch(&abort_flag, 1);
+          break;
+        }
+        if (*reinterpret_cast<volatile int *>(&abort_flag)) break;
+        const int64_t r0 = int64_t(i) * kGbRows;
+        const int rows = nrows - r0 < kGbRows ? int(nrows - r0) : kGbRows;
+        sm100::mbar_arrive_expect_tx(&full[st], uint32_t(rows) * row_bytes);
+        for (int r = 0; r < rows; ++r)
+          sm100::bulk_load_g2s(ring + st * kGbStageBytes + r * (kGrCols * 2), g.b + (k_begin + r0 + r) * g.ldb + n0,
+                               row_bytes, &full[st]);
+        issued = i + 1;
       }
-      vprog_eval_batch<4>(g.pro, g.t, idx, live, o);
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (live[j]) vec[idx[j] - k_begin] = o[j];
+      // Every copy issued lands before the CTA moves on (bounded waits).
+      for (int i = issued - kGbStages > 0 ? issued - kGbStages : 0; i < issued; ++i)
+        sm100::mbar_wait(&full[i % kGbStages], uint32_t((i / kGbStages) & 1));
     }
   } else {
-    for (int64_t k = k_begin + tid; k < k_end; k += kGrThreads) vec[k - k_begin] = bf16_bits_to_f32(__ldg(g.a + k));
-  }
-  __syncthreads();
-  const int64_t col = n0 + ct * 8;
-  const bool ok = col < g.N;
-  float acc[8];
+    if (PRO) {
+      for (int64_t k0 = tid; k0 < nrows; k0 += 4 * kGbConsumers) {
+        int64_t idx[4];
+        bool live[4];
+        float o[4];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-  if (ok) {
-    const uint16_t *bp = g.b + col;
-    int64_t k = k_begin + rg;
-    for (; k + (kGrU - 1) * kGrRG < k_end; k += kGrU * kGrRG) {
-      uint4 v[kGrU];
+        for (int j = 0; j < 4; ++j) {
+          idx[j] = k_begin + k0 + j * kGbConsumers;
+          live[j] = idx[j] < k_end;
+        }
+        vprog_eval_batch<4>(g.pro, g.t, idx, live, o);
 #pragma unroll
-      for (int u = 0; u < kGrU; ++u) v[u] = __ldcs(reinterpret_cast<const uint4 *>(bp + (k + u * kGrRG) * g.ldb));
-#pragma unroll
-      for (int u = 0; u < kGrU; ++u) gemv_fma8(acc, vec[k + u * kGrRG - k_begin], v[u]);
+        for (int j = 0; j < 4; ++j)
+          if (live[j]) vec[k0 + j * kGbConsumers] = o[j];
+      }
+    } else {
+      for (int64_t k = tid; k < nrows; k += kGbConsumers) vec[k] = bf16_bits_to_f32(__ldg(g.a + k_begin + k));
     }
-    for (; k < k_end; k += kGrRG) gemv_fma8(acc, vec[k - k_begin], __ldcs(reinterpret_cast<const uint4 *>(bp + k * g.ldb)));
-  }
-  __syncthreads();   // the vector slice is read; its space holds the row groups' partials now
-  float *red = vec;
+    asm volatile("bar.sync 1, %0;" ::"n"(kGbConsumers));   // the vector slice, seen by every consumer
+    float acc[8];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) red[rg * kGrCols + ct * 8 + e] = acc[e];
-  __syncthreads();
-  float *dst = part + int64_t(blockIdx.y) * g.N;
-  for (int c = tid; c < kGrCols; c += kGrThreads) {
-    if (n0 + c >= g.N) break;
-    float s = 0.f;
-#pragma unroll
-    for (int q = 0; q < kGrRG; ++q) s += red[q * kGrCols + c];
-    dst[n0 + c] = s;
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    const int64_t col = int64_t(tid) * 8;
+    const bool active = col < ncols;
+    for (int i = 0; i < nst; ++i) {
+      const int st = i % kGbStages;
+      if (*reinterpret_cast<volatile int *>(&abort_flag)) break;
+      if (!sm100::mbar_wait(&full[st], uint32_t((i / kGbStages) & 1))) {
+        atomicExch(&abort_flag, 1);
+        break;
+      }
+      const int64_t r0 = int64_t(i) * kGbRows;
+      const int rows = nrows - r0 < kGbRows ? int(nrows - r0) : kGbRows;
+      if (active) {
+        const uint8_t *box = ring + st * kGbStageBytes + tid * 16;
+        for (int r = 0; r < rows; ++r)
+          gemv_fma8(acc, vec[r0 + r], *reinterpret_cast<const uint4 *>(box + r * (kGrCols * 2)));
+      }
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&empty[st]);
+    }
+    if (active) {
+      float *dst = part + int64_t(blockIdx.y) * g.N + n0 + col;
+      reinterpret_cast<float4 *>(dst)[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      reinterpret_cast<float4 *>(dst)[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
   }
 }
 
@@ -230,9 +275,8 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_reduce_kernel(const __grid_
   }
 }
 
-// The row-streaming plan: 2048-column tiles, about one CTA per SM, at least 32 rows and at most kGrMaxRows (the
+// The row-streaming plan: 2048-column tiles, about one CTA per SM, at least 32 rows and at most kGbMaxRows (the
 // staged vector) per CTA.
-constexpr int64_t kGrMaxRows = 12288;
 // Matrices from 32M elements (64 MB) up stream on this path; smaller ones run the single-launch cluster path,
 // where the second launch and the short K slices of a split over every SM cost more than they save.
 constexpr int64_t kGrMinElems = int64_t(32) << 20;
@@ -246,7 +290,7 @@ static GemvRowsPlan plan_gemv_rows(int64_t N, int64_t K, int sm_count) {
   int64_t s = int64_t(sm_count) / pl.tiles;
   if (s > K / 32) s = K / 32;
   if (s < 1) s = 1;
-  while (ceil_div(K, s) > kGrMaxRows) ++s;
+  while (ceil_div(K, s) > kGbMaxRows) ++s;
   pl.k_per_cta = ceil_div(K, s);
   pl.splits = int(ceil_div(K, pl.k_per_cta));
   return pl;
@@ -383,12 +427,12 @@ static int launch_gemv(const ptsim_desc &d, void *const *ptrs, void *ws, size_t 
       gr.k_per_cta = pr.k_per_cta;
       float *part = reinterpret_cast<float *>(ws);
       const dim3 grid(unsigned(pr.tiles), unsigned(pr.splits));
-      const int64_t vec_bytes = pr.k_per_cta * int64_t(sizeof(float)), red_bytes = int64_t(kGrRG) * kGrCols * int64_t(sizeof(float));
-      const size_t smem = size_t(vec_bytes > red_bytes ? vec_bytes : red_bytes);
-      if (pro) PTSIM_CUDA((smem_limit_once<gemv_rows_kernel<true>>(int(kGrMaxRows * 4), c.device)));
-      else PTSIM_CUDA((smem_limit_once<gemv_rows_kernel<false>>(int(kGrMaxRows * 4), c.device)));
-      if (pro) gemv_rows_kernel<true><<<grid, kGrThreads, smem, c.stream>>>(gr, part);
-      else gemv_rows_kernel<false><<<grid, kGrThreads, smem, c.stream>>>(gr, part);
+      const size_t smem = size_t(kGbStages) * kGbStageBytes + size_t(pr.k_per_cta) * sizeof(float);
+      const int cap = int(kGbStages * kGbStageBytes + kGbMaxRows * 4);
+      if (pro) PTSIM_CUDA((smem_limit_once<gemv_bulk_kernel<true>>(cap, c.device)));
+      else PTSIM_CUDA((smem_limit_once<gemv_bulk_kernel<false>>(cap, c.device)));
+      if (pro) gemv_bulk_kernel<true><<<grid, kGbThreads, smem, c.stream>>>(gr, part);
+      else gemv_bulk_kernel<false><<<grid, kGbThreads, smem, c.stream>>>(gr, part);
       gemv_reduce_kernel<<<unsigned(ceil_div(p.N, int64_t(32))), kGemvThreads, 0, c.stream>>>(gr, part, pr.splits);
       PTSIM_CUDA(cudaGetLastError());
       return PTSIM_OK;

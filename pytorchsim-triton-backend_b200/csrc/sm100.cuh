@@ -151,6 +151,15 @@ __device__ __forceinline__ void bulk_copy_s2c(uint32_t dst, uint32_t src, uint32
                : "memory");
 }
 
+// A 1-D bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from global memory into this
+// CTA's shared memory, its completion counted on the mbarrier `bar`.  No multicast.
+__device__ __forceinline__ void bulk_load_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(ncols)
                : "memory");
