@@ -128,7 +128,9 @@ int launch_decode(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi
                   const LaunchCtx &c);
 int64_t decode_workspace(const ptsim_desc &d, int sm_count);
 int launch_topk(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c);
-int launch_sort(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c);
+int launch_sort(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, void *ws, size_t ws_bytes,
+                const LaunchCtx &c);
+int64_t sort_workspace(const ptsim_desc &d);
 int launch_gather_rows(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c);
 int launch_grouped_gemm(const ptsim_desc &d, void *const *ptrs, const LaunchCtx &c);
 int launch_gather_sum(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c);

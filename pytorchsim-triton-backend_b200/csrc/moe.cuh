@@ -672,7 +672,171 @@ int launch_topk(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, 
   return PTSIM_OK;
 }
 
-int launch_sort(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c) {
+// ---------------------------------------------------------------------------------------------------
+// Long rows (more than kSortBitonicMax keys, e.g. the dispatch's 8T expert ids): the stable counting sort over
+// CTAs of 1024 keys (one key per thread) in three launches -- each chunk's key range; the row's range (keys
+// spanning 256 values or more record PTSIM_E_UNSUPPORTED, as the one-CTA path does) and each chunk's
+// histogram; then every chunk's base offset per key (the keys below it in the whole row plus the same key in
+// earlier chunks), the ranks of its keys among earlier warps (per-warp counts in shared memory) and earlier
+// lanes (__match_any_sync), and the scatter.  Grid (chunks, rows); scratch: per row and chunk the range (2 int64)
+// and the histogram (256 int32).
+// ---------------------------------------------------------------------------------------------------
+constexpr int kSortChunk = 1024;
+
+struct SortMultiArgs {
+  SortArgs g;
+  int64_t chunks;
+  long long *range;   // [rows][chunks][2]
+  int *hist;          // [rows][chunks][kSortCountRange]
+};
+
+__device__ __forceinline__ void block_minmax(long long &lo, long long &hi, long long *s_min, long long *s_max) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const long long a = __shfl_xor_sync(0xffffffffu, lo, o), b = __shfl_xor_sync(0xffffffffu, hi, o);
+    lo = a < lo ? a : lo;
+    hi = b > hi ? b : hi;
+  }
+  if (lane == 0) {
+    s_min[warp] = lo;
+    s_max[warp] = hi;
+  }
+  __syncthreads();
+  lo = s_min[0];
+  hi = s_max[0];
+  for (int w = 1; w < int(blockDim.x >> 5); ++w) {
+    lo = s_min[w] < lo ? s_min[w] : lo;
+    hi = s_max[w] > hi ? s_max[w] : hi;
+  }
+}
+
+// The histogram and scatter launches are programmatic dependents: each kernel releases the next as it starts
+// (griddepcontrol.launch_dependents), and the next waits (griddepcontrol.wait) for the previous grid to finish
+// and flush before it reads that grid's scratch, so the launches overlap instead of queueing.
+__global__ void __launch_bounds__(kSortChunk) sort_range_kernel(const __grid_constant__ SortMultiArgs a) {
+  __shared__ long long s_min[32], s_max[32];
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int64_t row = a.g.row_begin + blockIdx.y, ri = blockIdx.y;
+  const int64_t c = int64_t(blockIdx.x) * kSortChunk + threadIdx.x;
+  long long lo = LLONG_MAX, hi = LLONG_MIN;
+  if (c < a.g.cols) lo = hi = sort_key(a.g, row * a.g.cols + c);
+  block_minmax(lo, hi, s_min, s_max);
+  if (threadIdx.x == 0) {
+    a.range[(ri * a.chunks + blockIdx.x) * 2] = lo;
+    a.range[(ri * a.chunks + blockIdx.x) * 2 + 1] = hi;
+  }
+}
+
+// The row's key range from its chunks' ranges (every thread holds it after the call).
+__device__ __forceinline__ void row_range(const SortMultiArgs &a, int64_t ri, long long &lo, long long &hi,
+                                          long long *s_min, long long *s_max) {
+  lo = LLONG_MAX;
+  hi = LLONG_MIN;
+  for (int64_t q = threadIdx.x; q < a.chunks; q += blockDim.x) {
+    const long long l = a.range[(ri * a.chunks + q) * 2], h = a.range[(ri * a.chunks + q) * 2 + 1];
+    lo = l < lo ? l : lo;
+    hi = h > hi ? h : hi;
+  }
+  block_minmax(lo, hi, s_min, s_max);
+}
+
+__global__ void __launch_bounds__(kSortChunk) sort_hist_kernel(const __grid_constant__ SortMultiArgs a) {
+  __shared__ long long s_min[32], s_max[32];
+  __shared__ int h[kSortCountRange];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int64_t row = a.g.row_begin + blockIdx.y, ri = blockIdx.y;
+  long long lo, hi;
+  row_range(a, ri, lo, hi, s_min, s_max);
+  if (static_cast<unsigned long long>(hi) - static_cast<unsigned long long>(lo) >= kSortCountRange) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) record_status(PTSIM_E_UNSUPPORTED);
+    return;
+  }
+  for (int i = threadIdx.x; i < kSortCountRange; i += blockDim.x) h[i] = 0;
+  __syncthreads();
+  const int64_t c = int64_t(blockIdx.x) * kSortChunk + threadIdx.x;
+  if (c < a.g.cols) atomicAdd(&h[int(sort_key(a.g, row * a.g.cols + c) - lo)], 1);
+  __syncthreads();
+  for (int i = threadIdx.x; i < kSortCountRange; i += blockDim.x)
+    a.hist[(ri * a.chunks + blockIdx.x) * kSortCountRange + i] = h[i];
+}
+
+__global__ void __launch_bounds__(kSortChunk) sort_scatter_kernel(const __grid_constant__ SortMultiArgs a) {
+  __shared__ long long s_min[32], s_max[32];
+  __shared__ int tot[4][kSortCountRange], bef[4][kSortCountRange];
+  __shared__ int off[kSortCountRange];
+  __shared__ int wh[kSortWarps][kSortCountRange];   // per-warp counts, then per-warp first positions
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t row = a.g.row_begin + blockIdx.y, ri = blockIdx.y;
+  long long lo, hi;
+  row_range(a, ri, lo, hi, s_min, s_max);
+  if (static_cast<unsigned long long>(hi) - static_cast<unsigned long long>(lo) >= kSortCountRange) return;
+  // totals of every key over the row, and over the chunks before this one (4 threads per key)
+  {
+    const int key = tid % kSortCountRange, q = tid / kSortCountRange;
+    int t = 0, b = 0;
+    for (int64_t ch = q; ch < a.chunks; ch += 4) {
+      const int v = a.hist[(ri * a.chunks + ch) * kSortCountRange + key];
+      t += v;
+      if (ch < int64_t(blockIdx.x)) b += v;
+    }
+    tot[q][key] = t;
+    bef[q][key] = b;
+  }
+  const int64_t c = int64_t(blockIdx.x) * kSortChunk + tid;
+  const int key = c < a.g.cols ? int(sort_key(a.g, row * a.g.cols + c) - lo) : -1;
+  for (int i = tid; i < kSortWarps * kSortCountRange; i += kSortChunk) (&wh[0][0])[i] = 0;
+  __syncthreads();
+  if (warp == 0) {
+    // exclusive scan of the totals over keys (8 keys per lane), plus the earlier chunks' count of each key
+    int run = 0;
+    for (int j = 0; j < kSortCountRange / 32; ++j) {
+      const int k = lane * 8 + j;
+      run += tot[0][k] + tot[1][k] + tot[2][k] + tot[3][k];
+    }
+    int incl = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    int o = incl - run;
+    for (int j = 0; j < kSortCountRange / 32; ++j) {
+      const int k = lane * 8 + j;
+      off[k] = o + bef[0][k] + bef[1][k] + bef[2][k] + bef[3][k];
+      o += tot[0][k] + tot[1][k] + tot[2][k] + tot[3][k];
+    }
+  }
+  const unsigned m = __match_any_sync(0xffffffffu, key);
+  if (key >= 0 && lane == __ffs(m) - 1) wh[warp][key] = __popc(m);
+  __syncthreads();
+  if (tid < kSortCountRange) {   // per-warp first positions of each key, warps in order
+    int base = off[tid];
+    for (int w = 0; w < kSortWarps; ++w) {
+      const int n = wh[w][tid];
+      wh[w][tid] = base;
+      base += n;
+    }
+  }
+  __syncthreads();
+  if (key >= 0) {
+    const int rank = __popc(m & ((1u << lane) - 1u));
+    sort_store(a.g, row * a.g.cols + wh[warp][key] + rank, int64_t(lo) + key, c);
+  }
+}
+
+// Scratch of a SORT launch: the multi-CTA path's ranges and histograms for every row (0 for rows it never takes).
+int64_t sort_workspace(const ptsim_desc &d) {
+  const ptsim_select_params &p = d.p.sel;
+  if (p.cols <= kSortBitonicMax) return 0;
+  const int64_t chunks = ceil_div(p.cols, int64_t(kSortChunk));
+  return p.rows * chunks * int64_t(2 * sizeof(long long) + kSortCountRange * sizeof(int));
+}
+
+int launch_sort(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, void *ws, size_t ws_bytes,
+                const LaunchCtx &c) {
   const ptsim_select_params &p = d.p.sel;
   const int xdt = d.arg_dtype[p.in_arg], vdt = d.arg_dtype[p.val_arg];
   if (d.arg_dtype[p.idx_arg] != PTSIM_DT_I64) return fail(PTSIM_E_UNSUPPORTED, "sort writes int64 indices");
@@ -691,6 +855,30 @@ int launch_sort(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, 
   g.descending = p.descending;
   g.float_keys = p.float_keys;
   if (row_end <= g.row_begin) return PTSIM_OK;
+  const int64_t rows = row_end - g.row_begin;
+  if (p.cols > kSortBitonicMax && rows <= 65535 && ws != nullptr && int64_t(ws_bytes) >= sort_workspace(d) &&
+      reinterpret_cast<uintptr_t>(ws) % 16 == 0) {
+    SortMultiArgs a;
+    a.g = g;
+    a.chunks = ceil_div(p.cols, int64_t(kSortChunk));
+    a.range = reinterpret_cast<long long *>(ws);
+    a.hist = reinterpret_cast<int *>(a.range + rows * a.chunks * 2);
+    const dim3 grid(unsigned(a.chunks), unsigned(rows));
+    sort_range_kernel<<<grid, kSortChunk, 0, c.stream>>>(a);
+    PTSIM_CUDA(cudaGetLastError());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kSortChunk, 1, 1);
+    cfg.stream = c.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    PTSIM_CUDA(cudaLaunchKernelEx(&cfg, sort_hist_kernel, a));
+    PTSIM_CUDA(cudaLaunchKernelEx(&cfg, sort_scatter_kernel, a));
+    return PTSIM_OK;
+  }
   PTSIM_CUDA((smem_limit_once<sort_kernel>(kSortSmem, c.device)));
   sort_kernel<<<unsigned(row_end - g.row_begin), kSortThreads, kSortSmem, c.stream>>>(g);
   PTSIM_CUDA(cudaGetLastError());

@@ -392,7 +392,7 @@ int ptsim_launch(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int
     case PTSIM_KIND_ROW_SUM:
     case PTSIM_KIND_ROW_RMSNORM: return launch_rowops(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_TOPK: return launch_topk(d, dev_ptrs, lo, hi, c);
-    case PTSIM_KIND_SORT: return launch_sort(d, dev_ptrs, lo, hi, c);
+    case PTSIM_KIND_SORT: return launch_sort(d, dev_ptrs, lo, hi, workspace, workspace_bytes, c);
     case PTSIM_KIND_GATHER_ROWS: return launch_gather_rows(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_GROUPED_GEMM: return launch_grouped_gemm(d, dev_ptrs, c);
     case PTSIM_KIND_GATHER_SUM: return launch_gather_sum(d, dev_ptrs, lo, hi, c);
@@ -417,6 +417,7 @@ int64_t ptsim_workspace_size(const void *desc, size_t desc_bytes, int device) {
   if (d.kind == PTSIM_KIND_ATTN_DECODE && need < decode_workspace(d, sm_count)) need = decode_workspace(d, sm_count);
   if (d.kind == PTSIM_KIND_INT_TABLE && need < itab_workspace(d, sm_count)) need = itab_workspace(d, sm_count);
   if (d.kind == PTSIM_KIND_GEMM && need < gemv_workspace(d, sm_count)) need = gemv_workspace(d, sm_count);
+  if (d.kind == PTSIM_KIND_SORT && need < sort_workspace(d)) need = sort_workspace(d);
   return need;
 }
 

@@ -80,6 +80,32 @@ def test_sort_float_keys(desc):
     assert bits_equal(v, wv) and torch.equal(i, wi)
 
 
+@pytest.mark.parametrize("rows,cols,lo,hi,desc", [(1, 32768, 0, 128, False), (3, 20000, -5, 200, True),
+                                                  (2, 100000, 0, 256, False), (1, 8193, 7, 9, False),
+                                                  (4, 65536, 0, 1, True)])
+def test_sort_long_rows_over_ctas(rows, cols, lo, hi, desc):
+    """Rows past the shared-memory sort: the stable counting sort over 1024-key chunks (ragged last chunks,
+    several rows per launch, descending order, a span of exactly 256 values, one repeated key)."""
+    g = torch.Generator().manual_seed(cols + rows)
+    x = torch.randint(lo, hi, (rows * cols,), generator=g, dtype=torch.int64)
+    v, i = run(B.sort(rows, cols, desc), [x, torch.zeros_like(x), torch.zeros_like(x)])[1:]
+    wv, wi = O.sort_rows(x, rows, cols, desc)
+    assert torch.equal(v, wv) and torch.equal(i, wi)
+
+
+def test_sort_long_row_paths_agree():
+    """Given no scratch, a long row runs the one-CTA counting sort; both paths give the same bits."""
+    cols = 32768
+    x = torch.randint(0, 128, (cols,), generator=torch.Generator().manual_seed(9), dtype=torch.int64).cuda()
+    multi = [x, torch.zeros_like(x), torch.zeros_like(x)]
+    RC.launch_tensors(D.to_bytes(B.sort(1, cols)), multi)
+    single = [x, torch.zeros_like(x), torch.zeros_like(x)]
+    stream = torch.cuda.current_stream()
+    native.launch(D.to_bytes(B.sort(1, cols)), [t.data_ptr() for t in single], 0, 1, 0, 0, stream.cuda_stream)
+    native.sync(stream.cuda_stream)
+    assert torch.equal(multi[1], single[1]) and torch.equal(multi[2], single[2])
+
+
 def test_sort_wide_long_row_is_reported():
     """A row longer than the shared-memory sort whose keys span more than the counting sort's 256 values is
     not run: the kernel records PTSIM_E_UNSUPPORTED, reported at synchronisation."""
