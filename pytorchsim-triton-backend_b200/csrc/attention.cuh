@@ -271,17 +271,27 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
 //   warp 0      TMA: Q_A, Q_B once; K_j, V_j into a two-deep ring;
 //   warp 1      MMA: S_A(j) = Q_A.K_j^T, S_B(j) = Q_B.K_j^T into TMEM; then O_A += P_A(j).V_j and
 //               O_B += P_B(j).V_j with P read from TMEM (the A operand of a TMEM-sourced MMA);
-//   warps 2..5  softmax of tile A, warps 6..9 softmax of tile B (one query row per thread): S is read
-//               from TMEM in 32-column chunks twice (row max, then exp / sum / bf16 pack), P is written
-//               back as packed bf16 pairs over the consumed S columns, O is rescaled in TMEM when the row
-//               max moved, and at the end O / l is stored.
+//   warps 2, 3  idle (they complete the first warpgroup, whose registers go to the softmax);
+//   warps 4..7  softmax of tile A, warps 8..11 softmax of tile B (one query row per thread): the row's
+//               128 scores are read from TMEM once, P is written back as packed bf16 pairs over the
+//               consumed S columns, O is rescaled in TMEM when the row max moved, and at the end O / l is
+//               stored.
 // The two softmax warpgroups alternate with the tensor core: the MMA warp issues PV_A(j) and S_A(j+1)
 // as soon as P_A(j) is ready, then PV_B(j) and S_B(j+1), so while one tile's softmax computes exp the
 // tensor core runs the other tile's products.  In-order MMA execution makes S_X(j)'s commit imply
 // PV_X(j-1) has finished, so a softmax may rescale O_X and overwrite P_X as soon as S_X(j) is ready.
 // TMEM: S_A [0,128)  S_B [128,256)  O_A [256,384)  O_B [384,512).
 // ---------------------------------------------------------------------------------------------------
-constexpr int kAttn2Threads = 320;
+// Three warpgroups: TMA + MMA (+ two idle warps), the softmax of tile A, the softmax of tile B.  Launched
+// at 168 registers a thread (12 warps, three on each SMSP), setmaxnreg then moves registers from the first
+// warpgroup to the other two: 128 x 56 + 256 x 224 = 64,512, exactly the 384 x 168 the launch holds (a split
+// above it would wait forever; the launcher checks the build's count), and 56 + 224 + 224 = 504 <= 512 per
+// SMSP.  The softmax holds a row's 128 scores in registers with room to keep many exponentials in flight.
+constexpr int kAttn2Threads = 384;
+constexpr int kAttn2SoftmaxWarp0 = 4;
+constexpr int kAttn2ProducerRegs = 56, kAttn2SoftmaxRegs = 224;
+static_assert(128 * kAttn2ProducerRegs + 256 * kAttn2SoftmaxRegs <= kAttn2Threads * 168,
+              "register split above the launch's registers");
 constexpr int kAttn2Smem = 6 * kAttnTile + 1024 + 256;  // Q_A, Q_B, K x2, V x2
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
@@ -334,6 +344,9 @@ __global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __gri
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  if (warp < kAttn2SoftmaxWarp0) {
+  // Producer warpgroup: every warp of it gives its registers back at this one instruction.
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kAttn2ProducerRegs));
   if (warp == 0) {
     if (lane == 0) {
       sm100::mbar_arrive_expect_tx(q_full, 2 * kAttnTile);
@@ -426,8 +439,10 @@ __global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __gri
       sm100::mma_commit(drain);
       sm100::mbar_wait(drain, 0);
     }
+  }
   } else {
-    const int t = (warp - 2) >> 2;          // 0: tile A, 1: tile B
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kAttn2SoftmaxRegs));
+    const int t = (warp - kAttn2SoftmaxWarp0) >> 2;   // 0: tile A, 1: tile B
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;       // query row within the tile = TMEM lane
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
@@ -574,6 +589,17 @@ int launch_attention(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t
   if (int64_t(a.batch * a.hkv * a.seq) >= (int64_t(1) << 31)) return fail(PTSIM_E_UNSUPPORTED, "attention rows exceed int32");
   if (a.seq % (2 * kAttnBM) == 0 && getenv("PTSIM_ATTN_V1") == nullptr) {
     PTSIM_CUDA(smem_limit_once<attn2_fwd_kernel>(kAttn2Smem, c.device));
+    {
+      // setmaxnreg.inc waits until the registers it asks for are free, so the warpgroups' shares must fit
+      // the registers the block is launched with; refuse (rather than wait forever) if the build disagrees.
+      static std::atomic<int> regs_ok{0};   // 0 unknown, 1 fits, 2 does not
+      if (regs_ok.load() == 0) {
+        cudaFuncAttributes fa;
+        PTSIM_CUDA(cudaFuncGetAttributes(&fa, attn2_fwd_kernel));
+        regs_ok.store(int64_t(fa.numRegs) * kAttn2Threads >= 128 * kAttn2ProducerRegs + 256 * kAttn2SoftmaxRegs ? 1 : 2);
+      }
+      if (regs_ok.load() != 1) return fail(PTSIM_E_RESOURCE, "attention register split does not fit this build's registers");
+    }
     const int64_t grid = (u1 - u0) * (g.q_tiles / 2);
     attn2_fwd_kernel<<<unsigned(grid), kAttn2Threads, kAttn2Smem, c.stream>>>(g);
     PTSIM_CUDA(cudaGetLastError());
