@@ -344,7 +344,11 @@ __device__ __forceinline__ int64_t onehot_id(const OnehotArgs &a, int64_t r) {
   return __ldg(a.ids + at);
 }
 
+// The scan kernel is launched as this one's programmatic dependent: released at the start here, it loads its
+// chunk of ids while the histograms are still being counted, and waits (griddepcontrol.wait: this grid has
+// finished and its stores are visible) only before it reads the chunk counts.
 __global__ void __launch_bounds__(256) onehot_hist_kernel(const __grid_constant__ OnehotArgs a) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __shared__ int h[kOnehotMaxRows];
   for (int i = threadIdx.x; i < a.nx; i += blockDim.x) h[i] = 0;
   __syncthreads();
@@ -365,6 +369,7 @@ __global__ void __launch_bounds__(1024) onehot_scan_kernel(const __grid_constant
   const int64_t c = blockIdx.x, chunks = gridDim.x;
   const int64_t r0 = c * a.chunk_len, r1 = min(a.cols, r0 + a.chunk_len);
   for (int64_t r = r0 + threadIdx.x; r < r1; r += blockDim.x) s_ids[r - r0] = onehot_id(a, r);
+  asm volatile("griddepcontrol.wait;" ::: "memory");   // the histogram grid's counts (a no-op when launched plainly)
   const bool live = xi < a.nx;
   const int64_t x = a.lo + xi;
   int64_t pb = 0, pt = 0;
@@ -660,8 +665,17 @@ int launch_itab(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, 
         return fail(PTSIM_E_RESOURCE, "integer table launch needs %lld bytes of workspace, given %zu", (long long)need, ws_bytes);
       oa.counts = reinterpret_cast<int64_t *>(ws);
       onehot_hist_kernel<<<unsigned(chunks), 256, 0, c.stream>>>(oa);
-      onehot_scan_kernel<<<unsigned(chunks), oa.groups * oa.xpad, 0, c.stream>>>(oa);
       PTSIM_CUDA(cudaGetLastError());
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(unsigned(chunks), 1, 1);
+      cfg.blockDim = dim3(unsigned(oa.groups * oa.xpad), 1, 1);
+      cfg.stream = c.stream;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      PTSIM_CUDA(cudaLaunchKernelEx(&cfg, onehot_scan_kernel, oa));
       return PTSIM_OK;
     }
   }
