@@ -154,6 +154,7 @@ constexpr int64_t kGbMaxRows = 4096;                   // vector rows a CTA stag
 
 template <bool PRO>
 __global__ void __launch_bounds__(kGbThreads, 1) gemv_bulk_kernel(const __grid_constant__ GemvArgs g, float *part) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // the reduce may launch (and wait) early
   extern __shared__ __align__(128) uint8_t gb_smem[];
   uint8_t *ring = gb_smem;
   float *vec = reinterpret_cast<float *>(gb_smem + kGbStages * kGbStageBytes);
@@ -250,9 +251,11 @@ __global__ void __launch_bounds__(kGbThreads, 1) gemv_bulk_kernel(const __grid_c
 
 // out[n] = the splits' partial columns summed, then the epilogue / residual and the store.  A CTA takes 32
 // columns with 8 threads each: thread j sums splits j, j + 8, ... in order (eight loads in flight), and the
-// 8 sums are added in j order -- a fixed order, so every launch gives the same bits.
+// 8 sums are added in j order -- a fixed order, so every launch gives the same bits.  Launched as the bulk
+// kernel's programmatic dependent: it waits for that grid (and its partial stores) before reading.
 __global__ void __launch_bounds__(kGemvThreads) gemv_reduce_kernel(const __grid_constant__ GemvArgs g, const float *part,
                                                                      int splits) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ float sh[8][32];
   const int c = threadIdx.x & 31, j = threadIdx.x >> 5;
   const int64_t n = int64_t(blockIdx.x) * 32 + c;
@@ -433,8 +436,18 @@ static int launch_gemv(const ptsim_desc &d, void *const *ptrs, void *ws, size_t 
       else PTSIM_CUDA((smem_limit_once<gemv_bulk_kernel<false>>(cap, c.device)));
       if (pro) gemv_bulk_kernel<true><<<grid, kGbThreads, smem, c.stream>>>(gr, part);
       else gemv_bulk_kernel<false><<<grid, kGbThreads, smem, c.stream>>>(gr, part);
-      gemv_reduce_kernel<<<unsigned(ceil_div(p.N, int64_t(32))), kGemvThreads, 0, c.stream>>>(gr, part, pr.splits);
       PTSIM_CUDA(cudaGetLastError());
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(unsigned(ceil_div(p.N, int64_t(32))), 1, 1);
+      cfg.blockDim = dim3(kGemvThreads, 1, 1);
+      cfg.stream = c.stream;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      PTSIM_CUDA(cudaLaunchKernelEx(&cfg, gemv_reduce_kernel, static_cast<const GemvArgs &>(gr),
+                                    static_cast<const float *>(part), int(pr.splits)));
       return PTSIM_OK;
     }
   }
