@@ -306,10 +306,12 @@ def run_b200(args, world, rank, local):
     chk = slice(0, 64 * 4096)
     want_s = O.softmax_rows(xs_h[chk], 64, 4096)
     want_r = O.rmsnorm_rows(xr_h[chk], w_h, 64, 4096, 1e-6)
-    ok = torch.allclose(ys[chk].float().cpu(), want_s.float(), rtol=1e-2, atol=1e-4) and \
-        torch.allclose(yr[chk].float().cpu(), want_r.float(), rtol=1e-2, atol=1e-2)
-    if not ok:
-        raise SystemExit("bench: the timed kernels disagree with the oracle")
+    from oracle import tolerance as T
+    try:
+        T.check(ys[chk], want_s, T.POINTWISE, name="softmax rows 0-63")
+        T.check(yr[chk], want_r, T.POINTWISE, name="RMSNorm rows 0-63")
+    except AssertionError as why:
+        raise SystemExit(f"bench: the timed kernels disagree with the oracle: {why}")
 
     clocks = Clocks(local)
     events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
@@ -354,9 +356,11 @@ def run_b200(args, world, rank, local):
         pipe.wait()
         if k > 0:
             e2e_ms += e0.elapsed_time(e1)
-    if not (torch.allclose(ys_p[chk].float(), want_s.float(), rtol=1e-2, atol=1e-4) and
-            torch.allclose(yr_p[chk].float(), want_r.float(), rtol=1e-2, atol=1e-2)):
-        raise SystemExit("bench: the end-to-end outputs disagree with the oracle")
+    try:
+        T.check(ys_p[chk], want_s, T.POINTWISE, name="end-to-end softmax rows 0-63")
+        T.check(yr_p[chk], want_r, T.POINTWISE, name="end-to-end RMSNorm rows 0-63")
+    except AssertionError as why:
+        raise SystemExit(f"bench: the end-to-end outputs disagree with the oracle: {why}")
     e2e_ms = reduce_max(e2e_ms, world, dev)
     e2e_val = world * STEP_BYTES * e2e_steps / (e2e_ms / 1e3) / 1e9
 

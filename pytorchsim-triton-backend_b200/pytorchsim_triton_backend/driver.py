@@ -145,8 +145,14 @@ class activated:
 
 
 def cuda_launcher(binary, kernel_object, grid, args, artifacts=None):
-    """A launcher for set_launcher: run descriptor `binary` over the tensor arguments `args` (scalars, which
-    the lowering already folded into the descriptor, are skipped) on their CUDA device."""
+    """A launcher for set_launcher: run descriptor `binary` over the tensor arguments `args` on their CUDA
+    device, in place, on torch's current stream.
+
+    Scalars: the lowering folded the kernel's scalar parameters into the descriptor, so each scalar the
+    launch passes (positionally, or specialised by Triton into the kernel object's "constexprs") must equal
+    the value the descriptor holds; another value is refused, never run with the old one.
+    Tensors: a non-contiguous argument runs on a contiguous copy, and a written one (out / inout) is copied
+    back into the caller's tensor after the launch."""
     from pytorchsim_triton_compiler.contract import kernel_object as ko
     from pytorchsim_triton_compiler.runtime import cuda as RC
     manifest = json.loads(kernel_object) if isinstance(kernel_object, (str, bytes)) else kernel_object
@@ -157,4 +163,19 @@ def cuda_launcher(binary, kernel_object, grid, args, artifacts=None):
     tensors = [a for a in args if hasattr(a, "data_ptr")]
     if len(tensors) != len(manifest["args"]):
         raise RuntimeError(f"{manifest.get('name')}: {len(tensors)} tensors for {len(manifest['args'])} arguments")
-    return RC.launch_tensors(bytes(binary), [t.contiguous() if not t.is_contiguous() else t for t in tensors])
+    specialised = manifest.get("constexprs", {}) or {}
+    table = [s["name"] for s in manifest.get("scalars", [])]
+    positional = [n for n in table if n not in specialised]
+    values = [a for a in args if not hasattr(a, "data_ptr")]
+    if len(values) != len(positional):
+        raise RuntimeError(f"{manifest.get('name')}: {len(values)} scalar arguments for the scalar parameters "
+                           f"{positional}")
+    given = dict(zip(positional, values))
+    given.update({n: v for n, v in specialised.items() if n in table})
+    ko.check_launch_scalars(manifest, given)
+    run = [t if t.is_contiguous() else t.contiguous() for t in tensors]
+    RC.launch_tensors(bytes(binary), run)
+    for arg, mine, ran in zip(manifest["args"], tensors, run):
+        if ran is not mine and arg["role"] != "in":
+            mine.copy_(ran)
+    return tensors

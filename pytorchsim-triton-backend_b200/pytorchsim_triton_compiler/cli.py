@@ -47,9 +47,11 @@ def doctor():
 
 
 def target():
+    """The target this build lowers for and every descriptor kind its executor runs (codegen/descriptors.py
+    KIND_NAME, the PTSIM_KIND_* values of include/ptsim_b200.h)."""
+    from .codegen import descriptors as D
     print(json.dumps({"name": "b200", "arch": "sm_100a", "executor": "libptsim_b200.so",
-                      "kinds": ["elementwise", "row_softmax", "row_rmsnorm", "qknorm_rope", "gemm", "attn_prefill",
-                                "reduce_all"]}, indent=1))
+                      "kinds": [D.KIND_NAME[k] for k in sorted(D.KIND_NAME)]}, indent=1))
     return 0
 
 

@@ -219,6 +219,16 @@ def row_divsum(rows, cols, in_dtype="float32", out_dtype="bfloat16"):
     return d
 
 
+def row_sum(rows, cols, dtype="float32"):
+    """The MoE layer's per-token weight sums (layer_layer_prefill_*/22_*): out[r] = fp32 sum of row r."""
+    d = D.new(D.ROW_SUM, _args([("in_ptr0", dtype, rows * cols), ("out_ptr0", "float32", rows)]),
+              (1, 1, 1), units=rows, unit_size=1)
+    r = d.p.row
+    r.rows, r.cols, r.in_row_stride, r.out_row_stride = rows, cols, cols, 1
+    r.in_arg, r.out_arg, r.weight_arg = 0, 1, -1
+    return d
+
+
 def gather_rows_floordiv(rows, cols, table_rows, div, dtype="bfloat16", idx_dtype="int64"):
     """The MoE dispatch's token copy (layer_op_dispatch_*/01_*): out row r = table row t, t = floor(idx[r] / div)
     (Python floor division), negative t wrapped by + table_rows; the int64 program as the lowering emits it."""

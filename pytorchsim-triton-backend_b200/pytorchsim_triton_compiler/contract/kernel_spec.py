@@ -1,17 +1,30 @@
-"""What a kernel file declares (the reference's contract/kernel_spec.py:24-214): the Triton kernel, its
-signature and constexprs, each tensor argument's role/dtype/shape, the launch grid, a torch reference and
-an input generator with tolerances.  Kernel files written for the reference load unchanged."""
+"""The kernel-file contract: a kernel file defines a module-level `SPEC = KernelSpec(...)` naming its Triton
+kernel, the kernel's signature and constexprs, each tensor argument's role / dtype / shape, the launch grid,
+a torch reference with its tolerances and an input generator.
+
+The field names and their meaning are the reference's (pytorchsim_triton_compiler/contract/kernel_spec.py),
+so kernel files written for it load here unchanged; the fields that steer the reference's scratchpad and
+timing graph (graph_prefetch, on_chip, prefetch, expect_ir*, expect_stage) are accepted and checked for
+consistency but do not change how the B200 executor runs the program.
+
+A JSON spec (`spec_to_json` / `spec_from_json`) carries the fields a compile reads beyond the kernel's
+source: it is what the Triton plugin passes as its `pytorchsim_spec` option."""
 import dataclasses
-import importlib.util
+import hashlib
+import importlib.machinery
 import json
 import math
 import os
-import re
+import types
 from typing import Callable
 
 from .kernel_object import ITEMSIZE
 
 IN, OUT, INOUT = "in", "out", "inout"
+ROLES = (IN, OUT, INOUT)
+EXPECTATIONS = ("pass", "refuse", "blocked", "open")
+PINNED_STAGES = ("", "togcheck", "timing")
+AXES = ("x", "y", "z")
 
 
 def is_read(arg):
@@ -24,7 +37,7 @@ def is_written(arg):
 
 @dataclasses.dataclass
 class Arg:
-    """One tensor argument."""
+    """One tensor argument of the kernel, in signature order."""
     name: str
     role: str
     dtype: str
@@ -37,6 +50,19 @@ class Arg:
     @property
     def nbytes(self):
         return self.numel * ITEMSIZE[self.dtype]
+
+
+def _arg_indices(spec, value, what, inputs_only=False):
+    """`value` as a tuple of distinct indices into spec.args (inputs only, if asked); ValueError otherwise."""
+    got = tuple(value)
+    n = len(spec.args)
+    problems = [a for a in got if not isinstance(a, int) or not 0 <= a < n]
+    if inputs_only:
+        problems += [a for a in got if isinstance(a, int) and 0 <= a < n and spec.args[a].role != IN]
+    if problems or len(set(got)) != len(got):
+        kind = "inputs" if inputs_only else "arguments"
+        raise ValueError(f"{spec.name}: KernelSpec.{what} lists distinct indices of {kind}, got {value!r}")
+    return got
 
 
 @dataclasses.dataclass
@@ -66,45 +92,38 @@ class KernelSpec:
     prefetch: tuple = ()
 
     def __post_init__(self):
-        if not self.parallel_axes:
-            self.parallel_axes = ("x", "y", "z")[:max(1, len(self.grid))]
-        axes = tuple(self.parallel_axes)
-        if any(a not in ("x", "y", "z") for a in axes) or len(set(axes)) != len(axes):
-            raise ValueError(f"KernelSpec.parallel_axes is distinct 'x'/'y'/'z', outermost first; got {axes!r}")
-        self.parallel_axes = axes
-
-        def indices(value, what, inputs_only=False):
-            got = tuple(value)
-            ok = all(isinstance(a, int) and 0 <= a < len(self.args) for a in got) and len(set(got)) == len(got)
-            if ok and inputs_only:
-                ok = all(self.args[a].role == IN for a in got)
-            if not ok:
-                raise ValueError(f"KernelSpec.{what} holds distinct argument indices, not {value!r}: {self.name}")
-            return got
-
-        if self.graph_prefetch is not None:
-            self.graph_prefetch = indices(self.graph_prefetch, "graph_prefetch")
-        self.on_chip = indices(self.on_chip, "on_chip")
-        self.prefetch = indices(self.prefetch, "prefetch", inputs_only=True)
-        if set(self.prefetch) & (set(self.on_chip) | set(self.graph_prefetch or ())):
-            raise ValueError(f"KernelSpec.prefetch overlaps on_chip or graph_prefetch: {self.name}")
-        if self.expect not in ("pass", "refuse", "blocked", "open"):
-            raise ValueError(f"KernelSpec.expect is pass/refuse/blocked/open, not {self.expect!r}")
-        if self.expect_stage not in ("", "togcheck", "timing"):
-            raise ValueError(f"KernelSpec.expect_stage is '', 'togcheck' or 'timing', not {self.expect_stage!r}")
-        if self.expect != "pass" and not self.expect_why:
-            raise ValueError(f"a kernel that is not expected to pass says why (expect_why): {self.name}")
         from .stop import Stop
-        if (self.expect == "pass") != (self.expect_stop is None):
-            raise ValueError(f"only a refuse/blocked/open kernel states expect_stop: {self.name}")
-        if self.expect_stop is not None and not isinstance(self.expect_stop, Stop):
-            raise ValueError(f"KernelSpec.expect_stop is a contract.stop.Stop: {self.name}")
+        axes = tuple(self.parallel_axes) or AXES[:max(1, len(self.grid))]
+        if not set(axes) <= set(AXES) or len(set(axes)) < len(axes):
+            raise ValueError(f"{self.name}: parallel_axes are distinct x/y/z, outermost first, got {axes!r}")
+        self.parallel_axes = axes
+        if self.graph_prefetch is not None:
+            self.graph_prefetch = _arg_indices(self, self.graph_prefetch, "graph_prefetch")
+        self.on_chip = _arg_indices(self, self.on_chip, "on_chip")
+        self.prefetch = _arg_indices(self, self.prefetch, "prefetch", inputs_only=True)
+        if set(self.prefetch) & (set(self.on_chip) | set(self.graph_prefetch or ())):
+            raise ValueError(f"{self.name}: an argument in prefetch is also on_chip or in graph_prefetch")
+        for a in self.args:
+            if a.role not in ROLES:
+                raise ValueError(f"{self.name}: argument {a.name} has role {a.role!r}, not one of {ROLES}")
+        if self.expect not in EXPECTATIONS:
+            raise ValueError(f"{self.name}: expect is one of {EXPECTATIONS}, got {self.expect!r}")
+        if self.expect_stage not in PINNED_STAGES:
+            raise ValueError(f"{self.name}: expect_stage is one of {PINNED_STAGES}, got {self.expect_stage!r}")
+        passing = self.expect == "pass"
+        if not passing and not self.expect_why:
+            raise ValueError(f"{self.name}: a kernel expected to stop states why (expect_why)")
+        if passing and self.expect_stop is not None:
+            raise ValueError(f"{self.name}: a passing kernel declares no expect_stop")
+        if not passing and not isinstance(self.expect_stop, Stop):
+            raise ValueError(f"{self.name}: a kernel expected to stop declares where, as a contract.stop.Stop")
 
     def expect_ir_for(self, machine_name):
-        out = {f: dict(c) for f, c in (self.expect_ir or {}).items()}
-        for f, counts in self.expect_ir_on.get(machine_name, {}).items():
-            out.setdefault(f, {}).update(counts)
-        return out
+        """expect_ir with the counts stated for one machine laid over it."""
+        merged = {fn: dict(counts) for fn, counts in (self.expect_ir or {}).items()}
+        for fn, counts in (self.expect_ir_on or {}).get(machine_name, {}).items():
+            merged.setdefault(fn, {}).update(counts)
+        return merged
 
     def inputs(self):
         return [a for a in self.args if is_read(a)]
@@ -116,73 +135,110 @@ class KernelSpec:
 JSON_FIELDS = ("name", "signature", "args", "grid", "grid_rule", "graph_prefetch", "on_chip", "prefetch",
                "parallel_axes", "extra")
 
-_TTIR_TOKEN = {"f64": "fp64", "f32": "fp32", "f16": "fp16", "bf16": "bf16", "i64": "i64", "i32": "i32",
-               "i16": "i16", "i8": "i8", "i1": "i1"}
-_TOKEN_DTYPE = {"fp64": "float64", "fp32": "float32", "fp16": "float16", "bf16": "bfloat16", "i64": "int64",
-                "i32": "int32", "i16": "int16", "i8": "int8", "i1": "bool"}
+# Triton's type names in TTIR (the element type of a !tt.ptr, or a scalar) and in a kernel signature, and
+# the kernel.json dtype each signature token stands for.
+_IR_TYPE_TO_TOKEN = {"f64": "fp64", "f32": "fp32", "f16": "fp16", "bf16": "bf16", "i64": "i64", "i32": "i32",
+                     "i16": "i16", "i8": "i8", "i1": "i1"}
+_TOKEN_TO_DTYPE = {"fp64": "float64", "fp32": "float32", "fp16": "float16", "bf16": "bfloat16", "i64": "int64",
+                   "i32": "int32", "i16": "int16", "i8": "int8", "i1": "bool"}
+
+
+def _split_params(text):
+    """The comma-separated parameters of a parameter list, ignoring commas inside <> () {} brackets."""
+    out, depth, cur = [], 0, []
+    for ch in text:
+        if ch in "<({":
+            depth += 1
+        elif ch in ">)}":
+            depth -= 1
+        if ch == "," and depth == 0:
+            out.append("".join(cur).strip())
+            cur = []
+        else:
+            cur.append(ch)
+    if "".join(cur).strip():
+        out.append("".join(cur).strip())
+    return out
 
 
 def signature_from_ttir(ttir):
-    """(name, signature) of the tt.func in the Triton IR file `ttir`."""
-    with open(ttir) as f:
-        head = next((line for line in f if "tt.func" in line), None)
-    if head is None:
-        raise ValueError(f"{ttir} holds no tt.func")
-    name = re.search(r"@(\w+)\(", head).group(1)
-    sig = {}
-    for m in re.finditer(r"%(\w+): (?:!tt\.ptr<(\w+)>|(\w+))", head):
-        elem, scalar = m.group(2), m.group(3)
-        tok = _TTIR_TOKEN.get(elem or scalar)
-        if tok is None:
-            raise ValueError(f"{ttir}: parameter {m.group(1)} has type {elem or scalar}, which has no Triton token")
-        sig[m.group(1)] = ("*" + tok) if elem else tok
-    return name, sig
-
-
-def spec_from_json(text, ttir=""):
-    """A KernelSpec from JSON_FIELDS' JSON (the Triton backend's pytorchsim_spec option)."""
-    got = json.loads(text)
-    unknown = sorted(set(got) - set(JSON_FIELDS))
-    if unknown:
-        raise ValueError(f"a JSON spec holds {', '.join(JSON_FIELDS)}, not {', '.join(unknown)}")
-    if not got.get("name") or not got.get("signature"):
-        name, sig = signature_from_ttir(ttir)
-        got["name"] = got.get("name") or name
-        got["signature"] = got.get("signature") or sig
-    pointers = [(n, _TOKEN_DTYPE[t[1:]]) for n, t in got["signature"].items() if t.startswith("*")]
-    wanted = got.pop("args")
-    if len(wanted) != len(pointers):
-        raise ValueError(f"{got['name']}: the spec states {len(wanted)} tensors, its kernel takes {len(pointers)}")
-    args = [Arg(a.get("name") or n, a["role"], a.get("dtype") or d, tuple(a["shape"])) for a, (n, d) in zip(wanted, pointers)]
-    got["grid"] = tuple(got["grid"])
-    if got.get("parallel_axes") is not None:
-        got["parallel_axes"] = tuple(got["parallel_axes"])
-    return KernelSpec(kernel=None, constexprs={}, args=args, reference=None, make_inputs=None, ttir=ttir, **got)
+    """(kernel name, signature) read from the `tt.func` header of a Triton IR file: pointer parameters
+    become "*<token>", scalars "<token>"."""
+    with open(ttir) as fh:
+        header = next((line for line in fh if "tt.func" in line), None)
+    if header is None:
+        raise ValueError(f"{ttir}: no tt.func in the file")
+    at = header.index("@") + 1
+    open_paren = header.index("(", at)
+    name = header[at:open_paren].strip()
+    depth, close = 0, None
+    for i in range(open_paren, len(header)):
+        depth += {"(": 1, ")": -1}.get(header[i], 0)
+        if depth == 0:
+            close = i
+            break
+    signature = {}
+    for param in _split_params(header[open_paren + 1:close]):
+        pname, _, ptype = param.partition(":")
+        pname, ptype = pname.strip().lstrip("%"), ptype.strip().split(" ")[0].split("{")[0].strip()
+        pointer = ptype.startswith("!tt.ptr<")
+        elem = ptype[len("!tt.ptr<"):].split(">")[0].split(",")[0].strip() if pointer else ptype
+        token = _IR_TYPE_TO_TOKEN.get(elem)
+        if token is None:
+            raise ValueError(f"{ttir}: parameter {pname} of type {ptype} has no Triton signature token")
+        signature[pname] = ("*" if pointer else "") + token
+    return name, signature
 
 
 def spec_to_json(spec):
-    """The JSON_FIELDS of `spec` as text (what the Triton backend passes as pytorchsim_spec)."""
-    out = {}
-    for f in JSON_FIELDS:
-        v = getattr(spec, f)
-        if f == "args":
-            v = [{"name": a.name, "role": a.role, "dtype": a.dtype, "shape": list(a.shape)} for a in v]
-        elif isinstance(v, tuple):
-            v = list(v)
-        out[f] = v
-    return json.dumps(out)
+    """The JSON_FIELDS of `spec` as JSON text."""
+    def plain(field, value):
+        if field == "args":
+            return [{"name": a.name, "role": a.role, "dtype": a.dtype, "shape": list(a.shape)} for a in value]
+        return list(value) if isinstance(value, tuple) else value
+    return json.dumps({f: plain(f, getattr(spec, f)) for f in JSON_FIELDS})
+
+
+def spec_from_json(text, ttir=""):
+    """A KernelSpec from JSON_FIELDS text; a missing name or signature is read from the TTIR at `ttir`.
+    Each tensor argument's dtype defaults to its pointer's element type."""
+    fields = json.loads(text)
+    extra_keys = set(fields) - set(JSON_FIELDS)
+    if extra_keys:
+        raise ValueError(f"a JSON spec holds only {', '.join(JSON_FIELDS)}; it also has {', '.join(sorted(extra_keys))}")
+    if not fields.get("name") or not fields.get("signature"):
+        ir_name, ir_sig = signature_from_ttir(ttir)
+        fields.setdefault("name", ir_name)
+        fields["name"] = fields["name"] or ir_name
+        fields["signature"] = fields.get("signature") or ir_sig
+    pointer_params = [(p, _TOKEN_TO_DTYPE[tok[1:]]) for p, tok in fields["signature"].items() if tok.startswith("*")]
+    stated = fields.pop("args")
+    if len(stated) != len(pointer_params):
+        raise ValueError(f"{fields['name']}: {len(stated)} tensor arguments stated, the kernel takes "
+                         f"{len(pointer_params)} pointers")
+    args = [Arg(s.get("name") or p, s["role"], s.get("dtype") or dt, tuple(s["shape"]))
+            for s, (p, dt) in zip(stated, pointer_params)]
+    fields["grid"] = tuple(fields["grid"])
+    if fields.get("parallel_axes") is not None:
+        fields["parallel_axes"] = tuple(fields["parallel_axes"])
+    return KernelSpec(kernel=None, constexprs={}, args=args, reference=None, make_inputs=None, ttir=ttir, **fields)
 
 
 def load_spec(path):
-    """Import a kernel file and return its SPEC; a .json file is a JSON spec with its .ttir beside it."""
+    """The SPEC of a kernel file, or of a JSON spec (`*.json`, its TTIR beside it as `*.ttir`).  A kernel
+    file is executed as a module of its own, named by a hash of its path so two files never share one."""
+    path = os.path.abspath(path)
     if path.endswith(".json"):
-        with open(path) as f:
-            return spec_from_json(f.read(), os.path.splitext(os.path.abspath(path))[0] + ".ttir")
-    modspec = importlib.util.spec_from_file_location("pytorchsim_kernel_" + os.path.basename(path).replace(".", "_"), path)
-    mod = importlib.util.module_from_spec(modspec)
-    modspec.loader.exec_module(mod)
-    if not hasattr(mod, "SPEC"):
-        raise SystemExit(f"{path}: a kernel file defines a module-level SPEC (KernelSpec)")
-    spec = mod.SPEC
-    spec.extra.setdefault("source_path", os.path.abspath(path))
+        with open(path) as fh:
+            return spec_from_json(fh.read(), os.path.splitext(path)[0] + ".ttir")
+    modname = "ptsim_kernel_file_" + hashlib.sha1(path.encode()).hexdigest()[:16]
+    loader = importlib.machinery.SourceFileLoader(modname, path)
+    module = types.ModuleType(modname)
+    module.__file__ = path
+    module.__loader__ = loader
+    loader.exec_module(module)
+    spec = getattr(module, "SPEC", None)
+    if spec is None or not hasattr(spec, "args"):
+        raise SystemExit(f"{path}: a kernel file defines SPEC = KernelSpec(...) at module level")
+    spec.extra.setdefault("source_path", path)
     return spec

@@ -1,18 +1,16 @@
-"""Why a lowering stops on purpose (the reference's contract/stop.py:13-31): a Reason per decision, raised as
-Refused, recorded by the process that compiled, and declared by a kernel file that expects it.
+"""Deliberate stops of the lowering.
 
-The B200 lowering adds its own reasons for tile programs it recognises but does not execute; it never falls
-back to an approximate or CPU path."""
-import dataclasses
+A program the B200 executor does not run is refused, never approximated: the lowering raises `Refused`
+with a `Reason`, the compile stage leaves failure.json of kind "refuse" naming the Reason's value, and a
+kernel file that expects the stop declares where and why with `Stop(step, reason)` in its KernelSpec.
+
+The Reason values are the reference's (pytorchsim_triton_compiler/contract/stop.py:13-31), so a kernel file
+written for the reference still names its stop; the last three are this executor's own."""
 import enum
-import json
-import os
-
-RECORD = "00-stop.json"
 
 
 class Reason(enum.Enum):
-    # Reasons the reference's compiler states (kept so a kernel file's expect_stop still names one).
+    # Decisions of the reference's MLIR lowering, kept as names a kernel file may declare.
     TRITON_PASS_FAILED = "triton-pass-failed"
     ATOMICS = "atomics"
     DTYPE_NOT_RUN = "dtype-not-run"
@@ -30,52 +28,53 @@ class Reason(enum.Enum):
     MASKED_STORE_NOT_A_BOX = "masked-store-not-a-box"
     MASKED_BOX_BEFORE_TENSOR = "masked-box-before-tensor"
     DIGIT_REFUSED = "digit-refused"
-    # B200 lowering: the program's class is not one the executor runs, or a shape it does not run.
+    # The B200 lowering: no executor class matches the program, the class does not run this shape, or an
+    # index is not an affine digit expression of the program's variables.
     PROGRAM_CLASS_UNKNOWN = "program-class-unknown"
     SHAPE_NOT_RUN = "shape-not-run"
     INDEX_NOT_AFFINE = "index-not-affine"
 
 
-class Refusal(Exception):
-    """A stop made on purpose; `reason` names the decision."""
-    reason = None
+class Refused(Exception):
+    """The lowering declines a program on purpose.  `reason` is the Reason; str(e) says what was seen."""
 
-
-class Refused(Refusal):
     def __init__(self, reason, message):
+        if not isinstance(reason, Reason):
+            raise TypeError(f"a refusal names a Reason, got {reason!r}")
         super().__init__(message)
         self.reason = reason
 
 
-def record(workdir, e):
-    with open(os.path.join(workdir, RECORD), "w") as f:
-        json.dump({"reason": e.reason.value, "message": str(e)}, f)
+def _valid_reason(reason):
+    """A Reason, or the dotted name of the Python exception an open kernel dies on ("pkg.Error")."""
+    if isinstance(reason, Reason):
+        return reason
+    if not isinstance(reason, str):
+        raise TypeError(f"a Stop's reason is a Reason or a dotted exception name, not {reason!r}")
+    owner, _, leaf = reason.rpartition(".")
+    if not owner or not leaf.isidentifier():
+        raise ValueError(f"{reason!r} is not a dotted exception name (module.Exception)")
+    return reason
 
 
-def recorded(workdir):
-    path = os.path.join(workdir, RECORD)
-    if not os.path.exists(path):
-        return None
-    with open(path) as f:
-        got = json.load(f)
-    return Reason(got["reason"]), got["message"]
-
-
-def clear(workdir):
-    try:
-        os.unlink(os.path.join(workdir, RECORD))
-    except FileNotFoundError:
-        pass
-
-
-@dataclasses.dataclass(frozen=True)
 class Stop:
-    """Where a refuse/blocked/open kernel stops: the step, and a Reason or a dotted exception name."""
-    step: str
-    reason: object
+    """Where a kernel that is not expected to pass stops: the stage (`step`) and the Reason (or, for an open
+    kernel, the dotted exception name).  Immutable and comparable, so a test can compare it with what the
+    compile recorded."""
+    __slots__ = ("step", "reason")
 
-    def __post_init__(self):
-        if not isinstance(self.reason, (Reason, str)):
-            raise TypeError(f"Stop.reason is a Reason or a dotted exception name, not {self.reason!r}")
-        if isinstance(self.reason, str) and "." not in self.reason:
-            raise ValueError(f"Stop.reason {self.reason!r} is not a dotted exception name")
+    def __init__(self, step, reason):
+        object.__setattr__(self, "step", str(step))
+        object.__setattr__(self, "reason", _valid_reason(reason))
+
+    def __setattr__(self, name, value):
+        raise AttributeError("a Stop does not change once declared")
+
+    def __eq__(self, other):
+        return isinstance(other, Stop) and (self.step, self.reason) == (other.step, other.reason)
+
+    def __hash__(self):
+        return hash((self.step, self.reason))
+
+    def __repr__(self):
+        return f"Stop({self.step!r}, {self.reason!r})"

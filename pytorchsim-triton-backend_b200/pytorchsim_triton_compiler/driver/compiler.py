@@ -155,7 +155,7 @@ def run(spec, workdir, frm=None, to=None, log=None):
     lo = names.index(frm) if frm else 0
     hi = names.index(to) if to else len(names) - 1
     ctx = Ctx(spec, workdir, _log)
-    failure.clear(workdir)
+    failure.forget(workdir)
     result = None
     try:
         for st in STAGES[lo:hi + 1]:
@@ -163,14 +163,14 @@ def run(spec, workdir, frm=None, to=None, log=None):
             try:
                 result = st.fn(ctx)
             except Refused as e:
-                failure.write(workdir, st.name, failure.REFUSED, str(e), reason=e.reason.value)
+                failure.leave(workdir, st.name, failure.REFUSED, str(e), reason=e.reason.value)
                 raise
             except StageError as e:
-                failure.write(workdir, st.name, failure.DEVICE if st.name == "cuda" else failure.ERROR, str(e),
+                failure.leave(workdir, st.name, failure.DEVICE if st.name == "cuda" else failure.ERROR, str(e),
                               **{k: v for k, v in e.facts.items() if isinstance(v, (int, str, float))})
                 raise
             except Exception as e:  # noqa: BLE001 -- recorded, then re-raised
-                failure.write(workdir, st.name, failure.ERROR, f"{type(e).__name__}: {e}")
+                failure.leave(workdir, st.name, failure.ERROR, f"{type(e).__name__}: {e}")
                 raise
             ctx.timings[st.name] = time.perf_counter() - t0
             _log(f"[{st.name}] done in {ctx.timings[st.name]:.3f} s")

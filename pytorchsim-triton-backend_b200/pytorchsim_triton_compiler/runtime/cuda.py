@@ -111,22 +111,32 @@ def launch_tensors(blob, tensors, lo=0, hi=None, stream=None, sync=True):
 
 
 def written_args(desc):
-    """Indices of the arguments a launch of `desc` writes (the launch's outputs)."""
-    k = desc.kind
+    """Indices of the arguments a launch of `desc` writes (the launch's outputs), for every descriptor
+    kind; CudaError for a kind this build does not know."""
+    k, p = desc.kind, desc.p
     if k == D.ELEMENTWISE:
-        e = desc.p.ew
-        return [e.map[e.store_map].arg]
-    if k in (D.ROW_SOFTMAX, D.ROW_RMSNORM):
-        return [desc.p.row.out_arg]
+        return [p.ew.map[p.ew.store_map].arg]
+    if k in (D.ROW_SOFTMAX, D.ROW_RMSNORM, D.ROW_DIVSUM, D.ROW_SUM):
+        return [p.row.out_arg]
     if k == D.QKNORM_ROPE:
-        return [desc.p.qk.out_arg]
+        return [p.qk.out_arg]
     if k == D.GEMM:
-        return [desc.p.gemm.c_arg]
+        return [p.gemm.c_arg]
     if k in (D.ATTN_PREFILL, D.ATTN_DECODE):
-        return [desc.p.attn.o_arg]
+        return [p.attn.o_arg]
     if k == D.REDUCE_ALL:
-        return [desc.p.red.out_arg]
-    raise CudaError(f"descriptor kind {k}")
+        return [p.red.out_arg]
+    if k in (D.TOPK, D.SORT):
+        return [p.sel.val_arg, p.sel.idx_arg]
+    if k == D.GATHER_ROWS:
+        return [p.gat.out_arg]
+    if k == D.GROUPED_GEMM:
+        return [p.ggemm.c_arg]
+    if k == D.GATHER_SUM:
+        return [p.gsum.out_arg]
+    if k == D.INT_TABLE:
+        return sorted({o.arg for o in list(p.itab.out)[:p.itab.nout]})
+    raise CudaError(f"descriptor kind {k} ({D.KIND_NAME.get(k, 'unknown')}) has no known outputs")
 
 
 class HostPipeline:
@@ -266,9 +276,12 @@ def launch(desc_blob, manifest, runtime, raw_paths, options=None, *, log=print, 
            scalar_values=None, grid=None, devices=None):
     """Run the whole launch over the .raw files in `raw_paths` (name -> path), leaving each written argument
     in its file.  `desc_blob` is the kernel object's descriptor (kernel_object.read_desc).  `devices` lists
-    the GPUs to use (all visible ones by default); `want_jobs` caps how many."""
+    the GPUs to use (all visible ones by default); `want_jobs` caps how many.  `scalar_values` ({name:
+    value}) are the launch's scalar arguments, as spike.launch takes them: the descriptor holds the values
+    it was lowered with, so a value that differs is refused (relower the kernel for it) instead of ignored."""
     try:
         ko.refuse_grid_past_bound(manifest, manifest["grid"] if grid is None else grid)
+        ko.check_launch_scalars(manifest, scalar_values)
         if grid is not None and tuple(ko.grid3(grid)) != tuple(ko.grid3(manifest["grid"])):
             raise error(f"{manifest.get('name')}: the descriptor was lowered for grid {tuple(ko.grid3(manifest['grid']))}"
                         f"; relower for grid {tuple(ko.grid3(grid))}")

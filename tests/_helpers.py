@@ -1,6 +1,9 @@
-"""Shared helpers of the parity tests: seeded inputs with the reference's conventions and the comparison
-report of its verify stage (tests/runtime/verify.py:28-69 in the reference: allclose, max abs/rel error)."""
+"""Shared helpers of the parity tests: seeded inputs with the reference's conventions, and the parity
+assertion (oracle/tolerance.py), whose failure report follows the reference's verify stage
+(tests/runtime/verify.py:28-69 in the reference: max abs / rel error and the worst index)."""
 import torch
+
+from oracle import tolerance as T
 
 
 def randn(numel, seed, dtype=torch.bfloat16, std=1.0, mean=0.0, gen=None):
@@ -23,17 +26,10 @@ def make_inputs(args, seed=0):
     return out
 
 
-def compare(got, want, rtol, atol):
-    """(ok, report) of a CUDA result against the oracle: torch.allclose plus the reference's error report."""
-    g, w = got.detach().float().cpu(), want.detach().float().cpu()
-    ok = torch.allclose(g, w, rtol=rtol, atol=atol, equal_nan=True)
-    diff = (g - w).abs()
-    diff = torch.where(torch.isnan(g) & torch.isnan(w), torch.zeros_like(diff), diff)
-    rel = diff / w.abs().clamp_min(1e-12)
-    i = int(diff.argmax()) if diff.numel() else 0
-    rep = (f"max_abs_err={float(diff.max()) if diff.numel() else 0:.6g} max_rel_err={float(rel.max()) if rel.numel() else 0:.6g}"
-           f" worst@{i}: got={float(g.reshape(-1)[i]) if g.numel() else 0!r} want={float(w.reshape(-1)[i]) if w.numel() else 0!r}")
-    return ok, rep
+def parity(got, want, bar, row=None, name="", magnitude=None):
+    """Assert that a CUDA result meets its parity bar against the oracle (oracle/tolerance.py: EXACT,
+    POINTWISE, CONTRACTION, FP32, FP32_SUM); returns the comparison's statistics."""
+    return T.check(got, want, bar, row=row, name=name, magnitude=magnitude)
 
 
 def bits_equal(got, want):

@@ -11,7 +11,9 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("PTSIM_REFERENCE", "/root/reference")
+REF = os.environ.get("PTSIM_REFERENCE", "")
+if not REF or not os.path.isdir(REF):
+    raise SystemExit("set PTSIM_REFERENCE to the reference checkout (the PyTorchSim-Triton-Backend source tree)")
 sys.path.insert(0, os.path.join(ROOT, "pytorchsim-triton-backend_b200"))
 
 

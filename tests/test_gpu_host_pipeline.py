@@ -57,3 +57,25 @@ def test_pipeline_refuses_device_tensors():
     pipe = RC.HostPipeline(0)
     with pytest.raises(RC.CudaError):
         pipe.submit(D.to_bytes(d), [torch.zeros(16, device="cuda"), torch.zeros(16), torch.zeros(16)])
+
+
+def test_pipelined_moe_kinds():
+    """Kinds with two outputs (top-k values and indices), integer tables (expert counts and running counts)
+    and the combine's gather-sum: the pipeline copies back every written argument, bit for bit what a
+    device-resident launch writes."""
+    g = torch.Generator().manual_seed(17)
+    rows, cols, k = 512, 128, 8
+    x = torch.randn(rows * cols, generator=g)
+    d_t = B.topk(rows, cols, k)
+    d_c = B.expert_counts(4096, 128)
+    ids = torch.randint(0, 128, (4096,), generator=g)
+    outs_t = [torch.zeros(rows * k), torch.zeros(rows * k, dtype=torch.int64)]
+    outs_c = [torch.zeros(128, dtype=torch.int64), torch.zeros(4096 * 128, dtype=torch.int64)]
+    pipe = RC.HostPipeline(0)
+    pipe.submit(D.to_bytes(d_t), [x] + outs_t)
+    pipe.submit(D.to_bytes(d_c), [ids] + outs_c)
+    pipe.wait()
+    want_t = _device_run(d_t, [x, torch.zeros(rows * k), torch.zeros(rows * k, dtype=torch.int64)])
+    want_c = _device_run(d_c, [ids, torch.zeros(128, dtype=torch.int64), torch.zeros(4096 * 128, dtype=torch.int64)])
+    assert bits_equal(outs_t[0], want_t[1]) and bits_equal(outs_t[1], want_t[2])
+    assert bits_equal(outs_c[0], want_c[1]) and bits_equal(outs_c[1], want_c[2])

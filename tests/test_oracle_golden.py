@@ -1,9 +1,9 @@
 """The oracle is pinned: each restatement in oracle/programs.py reproduces the outputs of the reference's own
 kernel (its Triton source run by the Triton interpreter, tests/golden/make_golden.py) on the reference's
 seeded inputs (make_inputs(torch, seed=0)).  Bit exact where the program is exact (copies, fp32 adds, bf16
-+ 1, max); within the bf16 tolerance of the reference's bf16-store case (rtol = atol = 1e-2,
-tests/cases/mechanism/ops/ops_bf16_store_gemm.py) otherwise; fp32 sums within 1e-5 of the sum of
-magnitudes.  CPU only."""
++ 1, max, integer tables); otherwise under the parity bars of oracle/tolerance.py (bf16: 1e-2 relative with
+no absolute floor and at most 2 ulps for element- and row-wise programs, plus 2^-10 of the row's RMS for
+sums of products, the ATTENTION envelope for attention; fp32: 1e-5).  CPU only."""
 import json
 import math
 import os
@@ -13,6 +13,7 @@ import pytest
 import torch
 
 from oracle import programs as O
+from oracle import tolerance as T
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OBJ = os.path.join(HERE, "golden", "objects")
@@ -171,26 +172,53 @@ def test_oracle_matches_reference_kernel(case):
         _check_against_gold(case, ins, name, got)
 
 
+def row_of(case):
+    """Elements per row of a contraction family's output (the CONTRACTION bar's scale), or None (one row)."""
+    o = case["oracle"]
+    fam = o["family"]
+    if fam in ("gemm", "grouped_gemm"):
+        return o["N"]
+    if fam in ("attention_prefill", "attention_decode"):
+        return o["dim"]
+    if fam in ("combine_weighted", "combine_weighted_fused"):
+        return o["hidden"]
+    if fam in ("qknorm_rope", "rope_rows"):      # x cos + rot sin: the POINTWISE bar's fp32-level floor
+        return o.get("dim", 128)
+    return None
+
+
+def bar_of(case, name):
+    """The parity bar (oracle/tolerance.py) of output `name` of a case."""
+    o = case["oracle"]
+    if o["family"] in EXACT or (o["family"] == "reduce_all" and o["op"] == "max"):
+        return T.EXACT
+    dt = next(a["dtype"] for a in case["args"] if a["name"] == name)
+    return T.bar_for(o["family"], dt)
+
+
+def magnitude_of(case, ins, want):
+    """Sum of the summands' magnitudes of an FP32_SUM output: sum |x| of a whole-tensor sum; a sum of
+    squares is its own magnitude."""
+    if case["oracle"]["family"] == "reduce_all":
+        return float(ins[case["inputs"][0]].float().abs().sum())
+    return float(want.float().abs().sum())
+
+
 def _check_against_gold(case, ins, name, got):
     gold = np.load(os.path.join(HERE, "golden", case["golden"]))
     stride = int(gold[f"{name}__stride"][0])
     want_bits = gold[name]
     dt = next(a["dtype"] for a in case["args"] if a["name"] == name)
     got_bits = as_bits(got.reshape(-1))
-    fam = case["oracle"]["family"]
-    if fam in EXACT or (fam == "reduce_all" and case["oracle"]["op"] == "max"):
+    bar = bar_of(case, name)
+    if bar == T.EXACT:
         # Exact programs: the whole output's hash matches, not only the sample.
         import hashlib
         assert hashlib.sha256(got_bits.tobytes()).digest() == bytes(gold[f"{name}__sha256"]), case["name"]
         return
     g = as_float(got_bits[::stride], dt)
     w = as_float(want_bits, dt)
-    if fam == "reduce_all":
-        scale = float(ins[case["inputs"][0]].float().abs().sum())
-        assert abs(float(g[0]) - float(w[0])) <= 1e-5 * scale
-        return
-    if fam == "sumsq":   # a sum of non-negative terms: within 1e-5 of itself
-        assert abs(float(g[0]) - float(w[0])) <= 1e-5 * abs(float(w[0]))
-        return
-    ok = torch.allclose(g, w, rtol=1e-2, atol=1e-2, equal_nan=True)
-    assert ok, f"{case['name']}: max abs err {float((g - w).abs().max()):.4g}"
+    if dt == "bfloat16":
+        g, w = g.to(torch.bfloat16), w.to(torch.bfloat16)
+    T.check(g, w, bar, row=row_of(case) if stride == 1 else None,
+            magnitude=magnitude_of(case, ins, w) if bar == T.FP32_SUM else None, name=case["name"])

@@ -185,3 +185,26 @@ def test_plugin_launch_runs_on_the_b200():
         finally:
             set_launcher(None)
     assert torch.equal(o.cpu(), O.vector_add(x, y))
+
+
+@pytest.mark.gpu
+def test_plugin_launch_writes_a_strided_output_view():
+    """A written argument that is a non-contiguous view runs on a contiguous copy, and the result is copied
+    back into the caller's view; the elements between the view's elements keep their values."""
+    import torch
+    from pytorchsim_triton_backend.driver import activated, cuda_launcher, set_launcher
+    from oracle import programs as O
+    n = 1 << 16
+    g = torch.Generator().manual_seed(6)
+    x, y = torch.randn(n, generator=g), torch.randn(n, generator=g)
+    backing = torch.full((2 * n,), -7.0, device="cuda")
+    o = backing[::2]
+    assert not o.is_contiguous()
+    with activated():
+        set_launcher(cuda_launcher)
+        try:
+            _compile(ADD)[(64, 1, 1)](x.cuda(), y.cuda(), o, n)
+        finally:
+            set_launcher(None)
+    assert torch.equal(o.cpu(), O.vector_add(x, y))
+    assert bool((backing[1::2] == -7.0).all())
