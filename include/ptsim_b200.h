@@ -279,6 +279,15 @@ typedef struct ptsim_gsum_params {
  * kernel for it (the one-hot count / running count of the combine's 00 program, the indexed select of its
  * 02 program); the results are the same. */
 #define PTSIM_FLAG_INTERPRET 1u
+/* desc->flags bit, for tests of the timeout path only: the launch's pipelined kernels (tcgen05 GEMM, its
+ * split-K cluster and 2-CTA forms, the grouped GEMM, both attention kernels, decode attention and the
+ * bulk-copy GEMV) withhold the copies of one pipeline stage in their first CTA (or cluster) and give every
+ * bounded wait a 1 ms limit instead of 2 s.  The waits on that stage give up, PTSIM_E_TIMEOUT is recorded
+ * and every CTA unwinds (copies in flight land, issued MMAs drain, TMEM is freed, cluster barriers are
+ * all met); ptsim_sync() then reports the status and the device stays usable.  The outputs of such a
+ * launch are undefined.  Other kinds ignore the bit.  No reference counterpart: it plays the role of a
+ * program that ends in one of Spike's named traps (runtime/spike.py:12,36-41). */
+#define PTSIM_FLAG_TEST_STALL 2u
 #define PTSIM_ITAB_OUTS 4
 #define PTSIM_ITAB_ELEM 0
 #define PTSIM_ITAB_SUM 1

@@ -34,6 +34,9 @@ struct AttnArgs {
   int32_t q_tiles, causal;
   int64_t unit_begin, unit_end;  // (batch, head) units of this launch
   float scale;
+  // PTSIM_FLAG_TEST_STALL: CTA 0 arms its first K tile but issues none of its copies, and every wait
+  // gives up after kTestWaitUs -- the timeout path under test.
+  int32_t stall;
 };
 
 // Store 128 bf16 values of row r of a [128 x 128] K-major operand tile (two 64-column halves, each
@@ -82,6 +85,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
   const int q_row0 = int(unit * g.seq + int64_t(qt) * kAttnBM);
   const int kv_row0 = int(kvh * g.seq);
   const int nkv = g.causal ? qt + 1 : int(g.seq / kAttnBN);
+  const uint32_t wl = g.stall ? kTestWaitUs : kWaitUs;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 12; ++i) sm100::mbar_init(&bars[i], i == 9 ? 4u : 1u);  // p_full: one per softmax warp
@@ -98,6 +102,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS0 = tmem, tO = tmem + 256;  // S buffers at columns [0,128) and [128,256); O at [256,384)
 
+  int issued = 0;   // (producer) K/V tiles whose stages were armed
   if (warp == 0) {
     if (lane == 0) {
       sm100::mbar_arrive_expect_tx(q_full, kAttnTile);
@@ -105,19 +110,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       sm100::tma_load_2d(sQ + 16384, &g.tq, q_full, 64, q_row0);
       for (int j = 0; j < nkv; ++j) {
         const int st = j & 1;
-        if (!sm100::mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1)) { *abort_flag = 1; break; }
+        if (!sm100::mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, wl)) { *abort_flag = 1; break; }
         const int kr = kv_row0 + j * kAttnBN;
         sm100::mbar_arrive_expect_tx(&k_full[st], kAttnTile);
+        sm100::mbar_arrive_expect_tx(&v_full[st], kAttnTile);
+        ++issued;
+        if (g.stall && blockIdx.x == 0 && j == 0) continue;   // test hook: stage armed, no copy in flight
         sm100::tma_load_2d(sK + st * kAttnTile, &g.tk, &k_full[st], 0, kr);
         sm100::tma_load_2d(sK + st * kAttnTile + 16384, &g.tk, &k_full[st], 64, kr);
-        sm100::mbar_arrive_expect_tx(&v_full[st], kAttnTile);
         sm100::tma_load_2d(sV + st * kAttnTile, &g.tv, &v_full[st], 0, kr);
         sm100::tma_load_2d(sV + st * kAttnTile + 16384, &g.tv, &v_full[st], 64, kr);
-      }
-      // Copies in flight land before exit: wait on the last fill of each stage.
-      for (int j = nkv - 2 < 0 ? 0 : nkv - 2; j < nkv && *abort_flag; ++j) {
-        sm100::mbar_wait(&k_full[j & 1], (j >> 1) & 1);
-        sm100::mbar_wait(&v_full[j & 1], (j >> 1) & 1);
       }
     }
   } else if (warp == 1) {
@@ -125,10 +127,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       constexpr uint32_t idesc_s = sm100::idesc_bf16_f32(kAttnBM, kAttnBN, false, false);
       constexpr uint32_t idesc_o = sm100::idesc_bf16_f32(kAttnBM, kAttnD, false, true);
       const uint32_t q_addr = sm100::smem_u32(sQ), p_addr = sm100::smem_u32(sP);
-      bool ok = sm100::mbar_wait(q_full, 0);
+      bool ok = sm100::mbar_wait(q_full, 0, wl);
       auto issue_s = [&](int j) -> bool {
         const int st = j & 1;
-        if (!sm100::mbar_wait(&k_full[st], (j >> 1) & 1)) return false;
+        if (!sm100::mbar_wait(&k_full[st], (j >> 1) & 1, wl)) return false;
         sm100::tc_fence_after();
         const uint32_t k_addr = sm100::smem_u32(sK + st * kAttnTile);
 #pragma unroll
@@ -142,8 +144,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       };
       auto issue_pv = [&](int j) -> bool {
         const int st = j & 1;
-        if (!sm100::mbar_wait(p_full, j & 1)) return false;
-        if (!sm100::mbar_wait(&v_full[st], (j >> 1) & 1)) return false;
+        if (!sm100::mbar_wait(p_full, j & 1, wl)) return false;
+        if (!sm100::mbar_wait(&v_full[st], (j >> 1) & 1, wl)) return false;
         sm100::tc_fence_after();
         const uint32_t v_addr = sm100::smem_u32(sV + st * kAttnTile);
 #pragma unroll
@@ -165,7 +167,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       if (ok) ok = issue_pv(nkv - 1);
       if (!ok) *abort_flag = 1;
       sm100::mma_commit(drain);
-      sm100::mbar_wait(drain, 0);
+      sm100::mbar_wait(drain, 0, wl);
     }
   } else {
     const int quarter = warp & 3;
@@ -177,7 +179,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
       const int st = j & 1;
-      if (*abort_flag || !sm100::mbar_wait(&s_full[st], (j >> 1) & 1)) { ok = false; break; }
+      if (*abort_flag || !sm100::mbar_wait(&s_full[st], (j >> 1) & 1, wl)) { ok = false; break; }
       sm100::tc_fence_after();
       float s[128];
 #pragma unroll
@@ -210,7 +212,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       m = m_new;
       if (j > 0) {
         // PV_{j-1} has finished: the P buffer is free and O holds every earlier tile.
-        if (!sm100::mbar_wait(pv_done, (j - 1) & 1)) { ok = false; break; }
+        if (!sm100::mbar_wait(pv_done, (j - 1) & 1, wl)) { ok = false; break; }
         sm100::tc_fence_after();
       }
       store_sw128_row(sP, r, pk);
@@ -235,7 +237,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(p_full);
     }
-    if (ok && !*abort_flag && sm100::mbar_wait(pv_done, (nkv - 1) & 1)) {
+    if (ok && !*abort_flag && sm100::mbar_wait(pv_done, (nkv - 1) & 1, wl)) {
       sm100::tc_fence_after();
       const float inv_l = l;  // divide, as the program does (acc / l)
       uint16_t *orow = g.o + (int64_t(q_row0) + r) * kAttnD;
@@ -260,6 +262,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
   }
   sm100::tc_fence_before();
   __syncthreads();
+  // After an abort (final at the barrier above) the producer waits, bounded, for Q and the last fill of
+  // each K/V stage, so no copy still lands in shared memory once the CTA has exited.
+  if (warp == 0 && lane == 0 && *abort_flag) {
+    sm100::mbar_wait(q_full, 0, wl);
+    for (int j = issued - 2 < 0 ? 0 : issued - 2; j < issued; ++j) {
+      sm100::mbar_wait(&k_full[j & 1], (j >> 1) & 1, wl);
+      sm100::mbar_wait(&v_full[j & 1], (j >> 1) & 1, wl);
+    }
+  }
   if (warp == 1) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem, 512);
@@ -329,6 +340,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __gri
   const int kv_row0 = int(kvh * g.seq);
   const int nA = g.causal ? 2 * qp + 1 : int(g.seq / kAttnBN);   // key tiles of query tile A
   const int nB = g.causal ? 2 * qp + 2 : nA;                      // and of tile B
+  const uint32_t wl = g.stall ? kTestWaitUs : kWaitUs;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 16; ++i) sm100::mbar_init(&bars[i], (i == 9 || i == 10) ? 4u : 1u);
@@ -344,6 +356,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __gri
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  int kj = 0, vj = 0;   // (producer) K and V tiles whose stages were armed
   if (warp < kAttn2SoftmaxWarp0) {
   // Producer warpgroup: every warp of it gives its registers back at this one instruction.
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kAttn2ProducerRegs));
@@ -356,25 +369,21 @@ __global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __gri
       sm100::tma_load_2d(sQ + kAttnTile + 16384, &g.tq, q_full, 64, q_row0 + kAttnBM);
       // K and V slots are released separately (K after the S products, V after the PV products), so
       // K_{j+2} starts loading about half an iteration before V_{j+2} may.
-      int kj = 0, vj = 0;   // K and V tiles issued
       for (int j = 0; j < nB; ++j) {
         const int st = j & 1;
         const int kr = kv_row0 + j * kAttnBN;
-        if (!sm100::mbar_wait(&k_empty[st], ((j >> 1) & 1) ^ 1)) { *abort_flag = 1; break; }
+        if (!sm100::mbar_wait(&k_empty[st], ((j >> 1) & 1) ^ 1, wl)) { *abort_flag = 1; break; }
         sm100::mbar_arrive_expect_tx(&k_full[st], kAttnTile);
-        sm100::tma_load_2d(sK + st * kAttnTile, &g.tk, &k_full[st], 0, kr);
-        sm100::tma_load_2d(sK + st * kAttnTile + 16384, &g.tk, &k_full[st], 64, kr);
+        if (!(g.stall && blockIdx.x == 0 && j == 0)) {   // test hook: K_0 armed, no copy in flight
+          sm100::tma_load_2d(sK + st * kAttnTile, &g.tk, &k_full[st], 0, kr);
+          sm100::tma_load_2d(sK + st * kAttnTile + 16384, &g.tk, &k_full[st], 64, kr);
+        }
         ++kj;
-        if (!sm100::mbar_wait(&v_empty[st], ((j >> 1) & 1) ^ 1)) { *abort_flag = 1; break; }
+        if (!sm100::mbar_wait(&v_empty[st], ((j >> 1) & 1) ^ 1, wl)) { *abort_flag = 1; break; }
         sm100::mbar_arrive_expect_tx(&v_full[st], kAttnTile);
         sm100::tma_load_2d(sV + st * kAttnTile, &g.tv, &v_full[st], 0, kr);
         sm100::tma_load_2d(sV + st * kAttnTile + 16384, &g.tv, &v_full[st], 64, kr);
         ++vj;
-      }
-      if (*abort_flag) {
-        sm100::mbar_wait(q_full, 0);
-        for (int i = (kj - 2 < 0 ? 0 : kj - 2); i < kj; ++i) sm100::mbar_wait(&k_full[i & 1], (i >> 1) & 1);
-        for (int i = (vj - 2 < 0 ? 0 : vj - 2); i < vj; ++i) sm100::mbar_wait(&v_full[i & 1], (i >> 1) & 1);
       }
     }
   } else if (warp == 1) {
@@ -403,7 +412,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __gri
                              sm100::sw128_desc(v_addr + k * 16 * 128, 16384, 1024), idesc_o, (j > 0 || k > 0) ? 1u : 0u);
         if (j == (t == 0 ? nA : nB) - 1) sm100::mma_commit(&o_done[t]);
       };
-      bool ok = sm100::mbar_wait(q_full, 0) && sm100::mbar_wait(&k_full[0], 0);
+      bool ok = sm100::mbar_wait(q_full, 0, wl) && sm100::mbar_wait(&k_full[0], 0, wl);
       if (ok) {
         sm100::tc_fence_after();
         if (nA > 0) issue_s(0, 0);
@@ -413,23 +422,23 @@ __global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __gri
       for (int j = 0; ok && j < nB; ++j) {
         const int st = j & 1;
         const bool next = j + 1 < nB;
-        if (!sm100::mbar_wait(&v_full[st], (j >> 1) & 1)) { ok = false; break; }
+        if (!sm100::mbar_wait(&v_full[st], (j >> 1) & 1, wl)) { ok = false; break; }
         if (j < nA) {
-          if (!sm100::mbar_wait(&p_full[0], j & 1)) { ok = false; break; }
+          if (!sm100::mbar_wait(&p_full[0], j & 1, wl)) { ok = false; break; }
           sm100::tc_fence_after();
           issue_pv(0, j);
           if (j + 1 < nA) {
-            if (!sm100::mbar_wait(&k_full[st ^ 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
+            if (!sm100::mbar_wait(&k_full[st ^ 1], ((j + 1) >> 1) & 1, wl)) { ok = false; break; }
             sm100::tc_fence_after();
             issue_s(0, j + 1);
           }
         }
-        if (!sm100::mbar_wait(&p_full[1], j & 1)) { ok = false; break; }
+        if (!sm100::mbar_wait(&p_full[1], j & 1, wl)) { ok = false; break; }
         sm100::tc_fence_after();
         issue_pv(1, j);
         sm100::mma_commit(&v_empty[st]);    // V_j is read once PV_B(j) is done
         if (next) {
-          if (!sm100::mbar_wait(&k_full[st ^ 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
+          if (!sm100::mbar_wait(&k_full[st ^ 1], ((j + 1) >> 1) & 1, wl)) { ok = false; break; }
           sm100::tc_fence_after();
           issue_s(1, j + 1);
           sm100::mma_commit(&k_empty[st ^ 1]);   // K_{j+1} is read once S_B(j+1) is done
@@ -437,7 +446,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __gri
       }
       if (!ok) *abort_flag = 1;
       sm100::mma_commit(drain);
-      sm100::mbar_wait(drain, 0);
+      sm100::mbar_wait(drain, 0, wl);
     }
   }
   } else {
@@ -454,7 +463,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __gri
     float m = -1.0e30f, l = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
-      if (*abort_flag || !sm100::mbar_wait(&s_full[t], j & 1)) { ok = false; break; }
+      if (*abort_flag || !sm100::mbar_wait(&s_full[t], j & 1, wl)) { ok = false; break; }
       sm100::tc_fence_after();
       // The row's 128 products, read from TMEM once.  On the diagonal tile, keys past the query row become
       // -inf: they never win the max and their exp is 0, as the reference's -1e30 fill gives.
@@ -532,7 +541,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __gri
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(&p_full[t]);
     }
-    if (ok && !*abort_flag && sm100::mbar_wait(&o_done[t], 0)) {
+    if (ok && !*abort_flag && sm100::mbar_wait(&o_done[t], 0, wl)) {
       sm100::tc_fence_after();
       uint16_t *orow = g.o + (int64_t(q_row0) + t * kAttnBM + r) * kAttnD;
 #pragma unroll 1
@@ -556,6 +565,13 @@ __global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __gri
   }
   sm100::tc_fence_before();
   __syncthreads();
+  // After an abort (final at the barrier above) the producer waits, bounded, for Q and the last fill of
+  // each K and V stage, so no copy still lands in shared memory once the CTA has exited.
+  if (warp == 0 && lane == 0 && *abort_flag) {
+    sm100::mbar_wait(q_full, 0, wl);
+    for (int i = (kj - 2 < 0 ? 0 : kj - 2); i < kj; ++i) sm100::mbar_wait(&k_full[i & 1], (i >> 1) & 1, wl);
+    for (int i = (vj - 2 < 0 ? 0 : vj - 2); i < vj; ++i) sm100::mbar_wait(&v_full[i & 1], (i >> 1) & 1, wl);
+  }
   if (warp == 1) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem, 512);
@@ -586,6 +602,7 @@ int launch_attention(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t
   g.unit_begin = u0;
   g.unit_end = u1;
   g.scale = a.scale;
+  g.stall = (d.flags & PTSIM_FLAG_TEST_STALL) ? 1 : 0;
   if (int64_t(a.batch * a.hkv * a.seq) >= (int64_t(1) << 31)) return fail(PTSIM_E_UNSUPPORTED, "attention rows exceed int32");
   if (a.seq % (2 * kAttnBM) == 0 && getenv("PTSIM_ATTN_V1") == nullptr) {
     PTSIM_CUDA(smem_limit_once<attn2_fwd_kernel>(kAttn2Smem, c.device));

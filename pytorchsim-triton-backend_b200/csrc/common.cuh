@@ -23,6 +23,10 @@ __device__ __forceinline__ void record_status(int code) { atomicCAS(&g_status, 0
 // Iteration cap of every spin-wait on an mbarrier or flag: far above any legitimate wait of these
 // kernels (a few microseconds), far below a watchdog.  A wait that reaches it records PTSIM_E_TIMEOUT.
 constexpr uint32_t kSpinLimit = 1u << 26;
+// Wall-time limit of every such wait (microseconds), and the limit a launch with PTSIM_FLAG_TEST_STALL
+// uses instead, so a test that withholds a hand-off sees the timeout and the unwind within milliseconds.
+constexpr uint32_t kWaitUs = 2000000u;
+constexpr uint32_t kTestWaitUs = 1000u;
 
 // ---------------------------------------------------------------------------------------------------
 // bf16 <-> fp32.  Widening is exact (bits << 16).  Narrowing rounds to nearest, ties to even, and keeps

@@ -49,6 +49,9 @@ struct DecodeArgs {
   int64_t unit_begin;      // first KV head of the launch
   int32_t G, S, chunks, chunk_keys;
   float scale;
+  // PTSIM_FLAG_TEST_STALL: the first chunk of the first KV head arms its first stage but issues none of
+  // its copies, and every wait gives up after kTestWaitUs -- the timeout path under test.
+  int32_t stall;
 };
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
@@ -88,6 +91,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_part_kernel(const __gri
   const int nkeys = g.S - key0 < g.chunk_keys ? g.S - key0 : g.chunk_keys;
   const int ntiles = nkeys / kDecTile;
   const int row0 = int(unit * g.S) + key0;         // TMA row of the chunk's first key
+  const uint32_t wl = g.stall ? kTestWaitUs : kWaitUs;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kDecStages; ++i) {
@@ -115,13 +119,14 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_part_kernel(const __gri
       int j = 0;
       for (; j < ntiles; ++j) {
         const int st = j % kDecStages;
-        if (j >= kDecStages && !sm100::mbar_wait(&empty[st], ((j / kDecStages) - 1) & 1)) {
+        if (j >= kDecStages && !sm100::mbar_wait(&empty[st], ((j / kDecStages) - 1) & 1, wl)) {
           *abort_flag = 1;
           break;
         }
         uint8_t *b = smem + st * kDecStage;
         const int y = row0 + j * kDecTile;
         sm100::mbar_arrive_expect_tx(&full[st], kDecStage);
+        if (g.stall && chunk == 0 && ul == 0 && j == 0) continue;   // test hook: armed, no copy in flight
         sm100::tma_load_2d(b, &g.tk, &full[st], 0, y);
         sm100::tma_load_2d(b + kDecBox, &g.tk, &full[st], 64, y);
         sm100::tma_load_2d(b + 2 * kDecBox, &g.tv, &full[st], 0, y);
@@ -129,7 +134,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_part_kernel(const __gri
       }
       // The last fills of each stage have landed before the ring is reused by the epilogue.
       for (int i = j - kDecStages < 0 ? 0 : j - kDecStages; i < j; ++i)
-        sm100::mbar_wait(&full[i % kDecStages], (i / kDecStages) & 1);
+        sm100::mbar_wait(&full[i % kDecStages], (i / kDecStages) & 1, wl);
     }
   } else {
     // Q fragments (A operand, rows gq and gq + 8, zero past G): d = 16 kk + 2 qd (+1) and + 8.
@@ -155,7 +160,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_part_kernel(const __gri
     const float scale = g.scale;
     for (int j = 0; j < ntiles; ++j) {
       const int st = j % kDecStages;
-      if (!sm100::mbar_wait(&full[st], (j / kDecStages) & 1)) {
+      if (!sm100::mbar_wait(&full[st], (j / kDecStages) & 1, wl)) {
         *abort_flag = 1;
         break;
       }
@@ -367,6 +372,7 @@ int launch_decode(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi
   g.chunks = pl.chunks;
   g.chunk_keys = pl.chunk_keys;
   g.scale = a.scale;
+  g.stall = (d.flags & PTSIM_FLAG_TEST_STALL) ? 1 : 0;
   PTSIM_CUDA((smem_limit_once<decode_part_kernel>(kDecSmem, c.device)));
   decode_part_kernel<<<dim3(unsigned(pl.chunks), unsigned(units), 1), kDecThreads, kDecSmem, c.stream>>>(g);
   PTSIM_CUDA(cudaGetLastError());

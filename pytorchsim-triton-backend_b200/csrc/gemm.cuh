@@ -58,6 +58,9 @@ struct GemmArgs {
   const int32_t *grp_id, *grp_start, *grp_rows;
   int32_t programs, groups;
   int64_t b_group_rows;
+  // PTSIM_FLAG_TEST_STALL: the first CTA (the first cluster of the pair kernel) arms its first stage but
+  // issues none of its copies, and every wait gives up after kTestWaitUs -- the timeout path under test.
+  int32_t stall;
 };
 
 // Shared-memory table of a grouped launch: per program its group, first and end row, and the exclusive
@@ -130,6 +133,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_kb = int(ceil_div(g.K, kGemmBK));
+  const uint32_t wl = g.stall ? kTestWaitUs : kWaitUs;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -233,11 +237,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
     kb1 = kb0 + g.kb_per_split < num_kb ? kb0 + g.kb_per_split : num_kb;
   };
 
+  uint32_t pending = 0;  // (producer) bit s: stage s armed, with parity bit (s + 16)
   if (warp == 0) {
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t pending = 0;  // bit s: stage s holds a load issued with parity bit (s + 16)
       for (int u = blockIdx.x; u < num_items && !*abort_flag; u += gridDim.x) {
         int tm, tn, kb0, kb1;
         tile_coords(u / g.splits, tm, tn);
@@ -247,10 +251,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
         const int m0 = int(m0l);
         const int n0 = tn * BN;
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!sm100::mbar_wait(&empty_bar[stage], phase ^ 1)) { *abort_flag = 1; break; }
+          if (!sm100::mbar_wait(&empty_bar[stage], phase ^ 1, wl)) { *abort_flag = 1; break; }
           sm100::mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
           pending = (pending | (1u << stage)) & ~(1u << (stage + 16));
           pending |= phase << (stage + 16);
+          if (g.stall && blockIdx.x == 0 && u == int(blockIdx.x) && kb == kb0) {
+            if (++stage == STAGES) { stage = 0; phase ^= 1; }
+            continue;   // test hook: the stage stays armed with no copy in flight
+          }
           sm100::tma_load_2d(sA + stage * Cfg::A_BYTES, &g.tmap_a, &full_bar[stage], kb * kGemmBK, m0);
           if constexpr (B_KMAJOR) {
             sm100::tma_load_2d(sB + stage * Cfg::B_BYTES, &g.tmap_b, &full_bar[stage], kb * kGemmBK, int(b_row0) + n0);
@@ -263,11 +271,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
-      if (*abort_flag) {
-        // Let every bulk copy this CTA started land before the CTA's shared memory is released.
-        for (int s = 0; s < STAGES; ++s)
-          if (pending & (1u << s)) sm100::mbar_wait(&full_bar[s], (pending >> (s + 16)) & 1u);
-      }
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -278,14 +281,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
       for (int u = blockIdx.x; u < num_items && !*abort_flag; u += gridDim.x, ++it) {
         const int buf = it & 1;
         const uint32_t use = uint32_t(it >> 1) & 1u;
-        if (!sm100::mbar_wait(&tempty_bar[buf], use ^ 1)) { *abort_flag = 1; break; }
+        if (!sm100::mbar_wait(&tempty_bar[buf], use ^ 1, wl)) { *abort_flag = 1; break; }
         sm100::tc_fence_after();
         const uint32_t d_tmem = tmem_base + uint32_t(buf * BN);
         bool ok = true;
         int kb0, kb1;
         kb_range(u, kb0, kb1);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!sm100::mbar_wait(&full_bar[stage], phase)) { ok = false; break; }
+          if (!sm100::mbar_wait(&full_bar[stage], phase, wl)) { ok = false; break; }
           sm100::tc_fence_after();
           const uint32_t a_addr = sm100::smem_u32(sA + stage * Cfg::A_BYTES);
           const uint32_t b_addr = sm100::smem_u32(sB + stage * Cfg::B_BYTES);
@@ -305,7 +308,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
       }
       // Every MMA this thread issued has finished once the drain barrier flips.
       sm100::mma_commit(drain_bar);
-      sm100::mbar_wait(drain_bar, 0);
+      sm100::mbar_wait(drain_bar, 0, wl);
     }
   } else {
     // Epilogue warps 2..5: TMEM lane quarter = warp % 4.
@@ -315,7 +318,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
     for (int u = blockIdx.x; u < num_items; u += gridDim.x, ++it) {
       const int buf = it & 1;
       const uint32_t use = uint32_t(it >> 1) & 1u;
-      if (*abort_flag || !sm100::mbar_wait(&tfull_bar[buf], use)) { *abort_flag = 1; break; }
+      if (*abort_flag || !sm100::mbar_wait(&tfull_bar[buf], use, wl)) { *abort_flag = 1; break; }
       sm100::tc_fence_after();
       const int t = u / g.splits;
       int tm, tn;
@@ -360,8 +363,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
     if (threadIdx.x == 64) sm100::mbar_arrive_expect_tx(xbar, uint32_t((g.splits - 1) * cpw * 16384));
     __syncwarp();
     sm100::cluster_sync();   // every CTA's K range is done (rings free) and every receive barrier is armed
+    // The exchange runs only if no CTA of the cluster gave up: every abort flag is final at the barrier
+    // above and every thread reads the same ones, so either all CTAs send and wait for their slices or
+    // none does (a CTA that skipped its wait could otherwise leave while a peer's copy still lands in it).
+    int cluster_abort = 0;
+    for (int q = 0; q < g.splits; ++q) {
+      uint32_t f;
+      asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(f)
+                   : "r"(sm100::mapa_shared(sm100::smem_u32(const_cast<int *>(abort_flag)), uint32_t(q))) : "memory");
+      cluster_abort |= int(f);
+    }
     if (warp >= 2) {
-      if (!*abort_flag) {
+      if (!cluster_abort) {
         const uint32_t quarter_lane = uint32_t((warp & 3) * 32) << 16;
         int remote = 0;
 #pragma unroll 1
@@ -380,7 +393,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // staging visible to the bulk copies
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (threadIdx.x == 64 && !*abort_flag) {
+      if (threadIdx.x == 64 && !cluster_abort) {
         int i = 0;
         for (int j = 0; j < BN / 32; ++j) {
           const int owner = j / cpw;
@@ -391,8 +404,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
         }
       }
       // Receive: the peers' slices land on xbar; then sum the slots in rank order.
-      if (!*abort_flag && !sm100::mbar_wait(xbar, 0)) *abort_flag = 1;
-      if (!*abort_flag) {
+      bool received = !cluster_abort && sm100::mbar_wait(xbar, 0, wl);
+      if (!cluster_abort && !received) *abort_flag = 1;
+      if (received) {
         const int t = blockIdx.x / g.splits;
         int tm, tn;
         tile_coords(t, tm, tn);
@@ -426,9 +440,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
     sm100::cluster_sync();   // no CTA leaves while a peer's bulk copy may still read its staging
   }
 
-  // Teardown: every role has stopped issuing; make sure no MMA still writes TMEM, then free it.
+  // Teardown: every role has stopped issuing; make sure no MMA still writes TMEM, then free it.  After an
+  // abort (final once every role has reached this barrier) the producer waits, bounded, for every stage it
+  // armed, so no copy still lands in shared memory once the CTA has exited.
   sm100::tc_fence_before();
   __syncthreads();
+  if (warp == 0 && lane == 0 && *abort_flag)
+    for (int s = 0; s < STAGES; ++s)
+      if (pending & (1u << s)) sm100::mbar_wait(&full_bar[s], (pending >> (s + 16)) & 1u, wl);
   if (warp == 1) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
@@ -469,6 +488,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2_tcgen05_kernel(const __
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = sm100::cluster_ctarank();
   const int num_kb = int(ceil_div(g.K, kGemmBK));
+  const uint32_t wl = g.stall ? kTestWaitUs : kWaitUs;
   const int num_tiles = g.tiles_m * g.tiles_n;   // 256 x 256 tiles
   const int cluster = int(blockIdx.x >> 1), nclusters = int(gridDim.x >> 1);
 
@@ -502,25 +522,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2_tcgen05_kernel(const __
     tn = t / g.tiles_m;
   };
 
+  uint32_t armed = 0;   // (leader's producer) bit s: stage s armed, parity bit (s + 16)
   if (warp == 0) {
     if (lane == 0) {
       const uint32_t full0 = sm100::mapa_shared(sm100::smem_u32(full_bar), 0);   // the leader's full barriers
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t armed = 0;   // (leader) bit s: stage s armed, parity bit (s + 16)
       for (int t = cluster; t < num_tiles && !*abort_flag; t += nclusters) {
         int tm, tn;
         tile_coords(t, tm, tn);
         const int m0 = int(g.m_begin) + tm * 256 + int(rank) * kGemmBM;
         const int n0 = tn * 256 + int(rank) * kGemmBM;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!sm100::mbar_wait(&empty_bar[stage], phase ^ 1)) { *abort_flag = 1; break; }
+          if (!sm100::mbar_wait(&empty_bar[stage], phase ^ 1, wl)) { *abort_flag = 1; break; }
           if (rank == 0) {
             sm100::mbar_arrive_expect_tx(&full_bar[stage], 4 * kGemm2HalfTile);   // both CTAs' A and B halves
             armed = (armed | (1u << stage)) & ~(1u << (stage + 16));
             armed |= phase << (stage + 16);
           }
           const uint32_t bar = full0 + uint32_t(stage) * 8u;
+          if (g.stall && cluster == 0 && t == cluster && kb == 0) {
+            if (++stage == S) { stage = 0; phase ^= 1; }
+            continue;   // test hook: the leader's stage stays armed and neither CTA issues a copy into it
+          }
           sm100::tma_load_2d_pair(sA + stage * kGemm2HalfTile, &g.tmap_a, bar, kb * kGemmBK, m0);
           if constexpr (B_KMAJOR) {
             sm100::tma_load_2d_pair(sB + stage * kGemm2HalfTile, &g.tmap_b, bar, kb * kGemmBK, n0);
@@ -530,11 +554,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2_tcgen05_kernel(const __
           }
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
-      }
-      if (*abort_flag && rank == 0) {
-        // Every stage the leader armed completes once both CTAs' copies into it have landed.
-        for (int s = 0; s < S; ++s)
-          if (armed & (1u << s)) sm100::mbar_wait(&full_bar[s], (armed >> (s + 16)) & 1u);
       }
     }
   } else if (warp == 1) {
@@ -546,12 +565,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2_tcgen05_kernel(const __
       for (int t = cluster; t < num_tiles && !*abort_flag; t += nclusters, ++it) {
         const int buf = it & 1;
         const uint32_t use = uint32_t(it >> 1) & 1u;
-        if (!sm100::mbar_wait<true>(&tempty_bar[buf], use ^ 1)) { *abort_flag = 1; break; }
+        if (!sm100::mbar_wait<true>(&tempty_bar[buf], use ^ 1, wl)) { *abort_flag = 1; break; }
         sm100::tc_fence_after();
         const uint32_t d_tmem = tmem_base + uint32_t(buf * 256);
         bool ok = true;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!sm100::mbar_wait(&full_bar[stage], phase)) { ok = false; break; }
+          if (!sm100::mbar_wait(&full_bar[stage], phase, wl)) { ok = false; break; }
           sm100::tc_fence_after();
           const uint32_t a_addr = sm100::smem_u32(sA + stage * kGemm2HalfTile);
           const uint32_t b_addr = sm100::smem_u32(sB + stage * kGemm2HalfTile);
@@ -570,7 +589,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2_tcgen05_kernel(const __
         sm100::mma2_commit_mc(&tfull_bar[buf], 0x3);       // both CTAs' accumulator rows are ready
       }
       sm100::mma2_commit(drain_bar);
-      sm100::mbar_wait(drain_bar, 0);
+      sm100::mbar_wait(drain_bar, 0, wl);
     }
   } else {
     const int quarter = warp & 3;
@@ -580,7 +599,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2_tcgen05_kernel(const __
     for (int t = cluster; t < num_tiles; t += nclusters, ++it) {
       const int buf = it & 1;
       const uint32_t use = uint32_t(it >> 1) & 1u;
-      if (*abort_flag || !sm100::mbar_wait(&tfull_bar[buf], use)) { *abort_flag = 1; break; }
+      if (*abort_flag || !sm100::mbar_wait(&tfull_bar[buf], use, wl)) { *abort_flag = 1; break; }
       sm100::tc_fence_after();
       int tm, tn;
       tile_coords(t, tm, tn);
@@ -605,9 +624,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2_tcgen05_kernel(const __
   }
 
   // Teardown: both CTAs meet after every role has stopped (the leader's MMAs have drained), so no MMA
-  // still writes either CTA's TMEM, then each releases its share of the pair allocation.
+  // still writes either CTA's TMEM, then each releases its share of the pair allocation.  After an abort
+  // (final once every role has reached the CTA barrier) the leader's producer first waits, bounded, for
+  // every stage it armed: both CTAs' copies into it have then landed, before either CTA passes the
+  // cluster barrier and may exit.  A peer that gave up alone is caught the same way: the leader's MMA
+  // waits run out on the stages the peer stopped filling, which sets the leader's flag too.
   sm100::tc_fence_before();
   __syncthreads();
+  if (warp == 0 && lane == 0 && rank == 0 && *abort_flag)
+    for (int s = 0; s < S; ++s)
+      if (armed & (1u << s)) sm100::mbar_wait(&full_bar[s], (armed >> (s + 16)) & 1u, wl);
   sm100::cluster_sync();
   if (warp == 1) {
     sm100::tc_fence_after();
@@ -814,6 +840,7 @@ int launch_grouped_gemm(const ptsim_desc &d, void *const *ptrs, const LaunchCtx 
   g.programs = int(p.programs);
   g.groups = int(p.groups);
   g.b_group_rows = p.K;
+  g.stall = (d.flags & PTSIM_FLAG_TEST_STALL) ? 1 : 0;
   int rc = make_tmap_2d(&g.tmap_a, ptrs[p.a_arg], uint64_t(p.K), uint64_t(p.M), uint64_t(p.K), kGemmBK, kGemmBM);
   if (rc) return rc;
   rc = make_tmap_2d(&g.tmap_b, ptrs[p.b_arg], uint64_t(p.N), uint64_t(p.groups * p.K), uint64_t(p.ldb), 64, kGemmBK);
@@ -856,6 +883,7 @@ int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, 
   if (cdt == PTSIM_DT_F32) g.c_f32 = reinterpret_cast<float *>(ptrs[p.c_arg]);
   else g.c = reinterpret_cast<uint16_t *>(ptrs[p.c_arg]);
   g.r = p.r_arg >= 0 ? reinterpret_cast<const uint16_t *>(ptrs[p.r_arg]) : nullptr;
+  g.stall = (d.flags & PTSIM_FLAG_TEST_STALL) ? 1 : 0;
   GemmPlan pl = plan_gemm(m_end - m_begin, p.M, p.N, p.K, c.sm_count);
   if (pl.splits > 1) {
     // Fewer K splits when the device cannot run every tile's cluster at once (clusters need their CTAs

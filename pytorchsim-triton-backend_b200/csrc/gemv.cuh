@@ -37,6 +37,9 @@ struct GemvArgs {
   int64_t k_per_cta;           // K rows per CTA of a cluster
   ptsim_vprog pro, epi;        // fused vector prologue / output epilogue (ncode 0: none)
   VArgs t;
+  // PTSIM_FLAG_TEST_STALL (bulk path): CTA (0, 0) arms its first stage but issues none of its copies, and
+  // every wait gives up after kTestWaitUs -- the timeout path under test.
+  int32_t stall;
 };
 
 __device__ __forceinline__ void gemv_fma8(float (&acc)[8], float a, const uint4 &v) {
@@ -168,6 +171,7 @@ __global__ void __launch_bounds__(kGbThreads, 1) gemv_bulk_kernel(const __grid_c
   const int64_t k_end = k_begin + g.k_per_cta < g.K ? k_begin + g.k_per_cta : g.K;
   const int64_t nrows = k_end - k_begin;
   const int nst = int((nrows + kGbRows - 1) / kGbRows);
+  const uint32_t wl = g.stall ? kTestWaitUs : kWaitUs;
   if (tid == 0) {
     for (int st = 0; st < kGbStages; ++st) {
       sm100::mbar_init(&full[st], 1);
@@ -182,7 +186,7 @@ __global__ void __launch_bounds__(kGbThreads, 1) gemv_bulk_kernel(const __grid_c
       int issued = 0;
       for (int i = 0; i < nst; ++i) {
         const int st = i % kGbStages;
-        if (i >= kGbStages && !sm100::mbar_wait(&empty[st], uint32_t((i / kGbStages - 1) & 1))) {
+        if (i >= kGbStages && !sm100::mbar_wait(&empty[st], uint32_t((i / kGbStages - 1) & 1), wl)) {
           atomicExch(&abort_flag, 1);
           break;
         }
@@ -190,6 +194,8 @@ __global__ void __launch_bounds__(kGbThreads, 1) gemv_bulk_kernel(const __grid_c
         const int64_t r0 = int64_t(i) * kGbRows;
         const int rows = nrows - r0 < kGbRows ? int(nrows - r0) : kGbRows;
         sm100::mbar_arrive_expect_tx(&full[st], uint32_t(rows) * row_bytes);
+        issued = i + 1;
+        if (g.stall && blockIdx.x == 0 && blockIdx.y == 0 && i == 0) continue;   // test hook: armed, no copy
         for (int r = 0; r < rows; ++r)
           sm100::bulk_load_g2s(ring + st * kGbStageBytes + r * (kGrCols * 2), g.b + (k_begin + r0 + r) * g.ldb + n0,
                                row_bytes, &full[st]);
@@ -197,7 +203,7 @@ __global__ void __launch_bounds__(kGbThreads, 1) gemv_bulk_kernel(const __grid_c
       }
       // Every copy issued lands before the CTA moves on (bounded waits).
       for (int i = issued - kGbStages > 0 ? issued - kGbStages : 0; i < issued; ++i)
-        sm100::mbar_wait(&full[i % kGbStages], uint32_t((i / kGbStages) & 1));
+        sm100::mbar_wait(&full[i % kGbStages], uint32_t((i / kGbStages) & 1), wl);
     }
   } else {
     if (PRO) {
@@ -227,7 +233,7 @@ __global__ void __launch_bounds__(kGbThreads, 1) gemv_bulk_kernel(const __grid_c
     for (int i = 0; i < nst; ++i) {
       const int st = i % kGbStages;
       if (*reinterpret_cast<volatile int *>(&abort_flag)) break;
-      if (!sm100::mbar_wait(&full[st], uint32_t((i / kGbStages) & 1))) {
+      if (!sm100::mbar_wait(&full[st], uint32_t((i / kGbStages) & 1), wl)) {
         atomicExch(&abort_flag, 1);
         break;
       }
@@ -409,6 +415,7 @@ static int launch_gemv(const ptsim_desc &d, void *const *ptrs, void *ws, size_t 
   g.pro = p.pro;
   g.epi = p.epi;
   vargs_fill(g.t, d, ptrs);
+  g.stall = (d.flags & PTSIM_FLAG_TEST_STALL) ? 1 : 0;
   const bool pro = p.pro.ncode > 0;
   if (reinterpret_cast<uintptr_t>(g.b) % 16 != 0) return fail(PTSIM_E_ARGS, "GEMV matrix is not 16-byte aligned");
   if (p.b_kmajor) {

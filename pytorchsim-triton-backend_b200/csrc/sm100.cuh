@@ -66,17 +66,18 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t ph
   return ok != 0;
 }
 
-// Wait for `phase` of `bar` to complete, for at most ~2 seconds of wall time.  Returns false (and
-// records PTSIM_E_TIMEOUT) when it gives up; the caller then unwinds instead of hanging the GPU.
+// Wait for `phase` of `bar` to complete, for at most `limit_us` microseconds of wall time (2 s unless a
+// test launch asks for less).  Returns false (and records PTSIM_E_TIMEOUT) when it gives up; the caller
+// then unwinds instead of hanging the GPU.
 template <bool CLUSTER = false>
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t phase) {
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t phase, uint32_t limit_us = kWaitUs) {
   auto try_once = [&]() { return CLUSTER ? mbar_try_wait_cluster(bar, phase) : mbar_try_wait(bar, phase); };
   if (try_once()) return true;
   uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (try_once()) return true;
     if ((i & 255u) == 0) {
-      if (globaltimer_ns() - t0 > 2000000000ull || i > kSpinLimit) {
+      if (globaltimer_ns() - t0 > uint64_t(limit_us) * 1000ull || i > kSpinLimit) {
         record_status(PTSIM_E_TIMEOUT);
         return false;
       }

@@ -139,6 +139,7 @@ class GsumParams(C.Structure):
 
 ITAB_MAPS, ITAB_OUTS = 5, 4
 FLAG_INTERPRET = 1   # desc.flags: INT_TABLE on the element interpreter only
+FLAG_TEST_STALL = 2  # desc.flags: pipelined kernels withhold one stage and time out in 1 ms (timeout tests)
 ITAB_MODE = {"elem": 0, "sum": 1, "scan": 2}
 ITAB_MODE_NAME = {v: k for k, v in ITAB_MODE.items()}
 
