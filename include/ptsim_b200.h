@@ -343,7 +343,9 @@ int ptsim_version(void);
 /* sizeof(ptsim_desc) as compiled, so a binding can check its own mirror of the struct. */
 size_t ptsim_desc_size(void);
 
-/* Select `device`, create its status word and check it is an sm_100 part.  Idempotent per device.
+/* Select `device`, create its status word, check it is an sm_100 part and look up the device address of
+ * the scratch ptsim_launch_reduce_noalloc uses.  Idempotent per device; call it again after a
+ * cudaDeviceReset of the device.
  * Replaces the reference's discovery of Spike/pk/model (toolchain.py:19-75, kernel_object.py:289-320). */
 int ptsim_init(int device);
 
@@ -374,8 +376,10 @@ int64_t ptsim_workspace_size(const void *desc, size_t desc_bytes, int device);
  * pointers it was handed, a host whose memory pool already owns the GPU's memory, or a caller that may
  * not synchronise the device, as cudaMalloc and cudaFree do.  A launch that needs more scratch than the
  * array holds (desc->workspace_bytes above 4096) returns PTSIM_E_RESOURCE; other kinds return
- * PTSIM_E_UNSUPPORTED.  The first call on a device looks the array's device address up
- * (cudaGetSymbolAddress); make that first call before any stream capture.  Every call on a device
+ * PTSIM_E_UNSUPPORTED.  ptsim_init(device) looks the array's device address up (cudaGetSymbolAddress) and
+ * caches it; call ptsim_init first, outside any stream capture (without it the first call on a device does
+ * the lookup itself, and must then come before any capture).  The cached address dies with the device's
+ * context: after a cudaDeviceReset, call ptsim_init again before the next call.  Every call on a device
  * shares the one array: calls that overlap on the GPU (other streams, other threads) race on it, so
  * order them on one stream.  No counterpart in the reference: Spike ran in host memory and needed no
  * device scratch. */

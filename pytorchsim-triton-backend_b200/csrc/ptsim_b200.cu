@@ -338,6 +338,42 @@ static int check_desc(const void *p, size_t bytes) {
 
 }  // namespace ptsim
 
+// ---------------------------------------------------------------------------------------------------
+// Whole-tensor reduction with library-owned scratch, for callers that cannot allocate device memory: a
+// foreign-language binding (ctypes, cgo, JNI) that only holds the raw pointers it was handed, a host
+// whose memory pool already owns the GPU's memory, or a caller that may not synchronise the device, as
+// cudaMalloc and cudaFree do.  The two-pass reduction parks one fp32 partial per pass-1 CTA in scratch;
+// here that scratch is the file-scope array below, which every GPU that loads this library holds until
+// the process exits.
+// ---------------------------------------------------------------------------------------------------
+namespace ptsim {
+
+// 4 KiB: pass 1 never runs more than 1024 CTAs (4 per SM, capped), one fp32 partial each.
+constexpr size_t kStaticScratchBytes = 1024 * sizeof(float);
+static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
+
+static std::mutex g_static_mu;
+static void *g_static_ptr[64];
+
+// Device address of g_static_scratch on `dev` (the current device), looked up once per device and again
+// whenever `refresh` is set (ptsim_init does, so a call after a cudaDeviceReset finds the new address).  In
+// host code the array's name is only a host-side stand-in, so kernels get this address instead.
+static int static_scratch(int dev, void **out, bool refresh = false) {
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  if (dev < 0 || dev >= 64) return fail(PTSIM_E_ARGS, "device %d out of range", dev);
+  if (refresh) g_static_ptr[dev] = nullptr;
+  if (g_static_ptr[dev] == nullptr) {
+    void *p = nullptr;
+    PTSIM_CUDA(cudaGetSymbolAddress(&p, g_static_scratch));
+    if (p == nullptr) return fail(PTSIM_E_CUDA, "no device address for the static scratch on device %d", dev);
+    g_static_ptr[dev] = p;
+  }
+  *out = g_static_ptr[dev];
+  return PTSIM_OK;
+}
+
+}  // namespace ptsim
+
 using namespace ptsim;
 
 extern "C" {
@@ -358,7 +394,10 @@ int ptsim_init(int device) {
     return fail(PTSIM_E_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a (B200)", device, info.major, info.minor);
   int zero = 0;
   PTSIM_CUDA(cudaMemcpyToSymbol(g_status, &zero, sizeof(int)));
-  return PTSIM_OK;
+  // The no-allocation reduction's scratch address, looked up here (outside any stream capture) and again on
+  // every call, so re-initialising a device after a reset refreshes it.
+  void *scratch = nullptr;
+  return static_scratch(device, &scratch, true);
 }
 
 int ptsim_check(const void *desc, size_t desc_bytes) { return check_desc(desc, desc_bytes); }
@@ -438,40 +477,6 @@ int ptsim_last_error(char *buf, int n) {
 }
 
 }  // extern "C"
-
-// ---------------------------------------------------------------------------------------------------
-// Whole-tensor reduction with library-owned scratch, for callers that cannot allocate device memory: a
-// foreign-language binding (ctypes, cgo, JNI) that only holds the raw pointers it was handed, a host
-// whose memory pool already owns the GPU's memory, or a caller that may not synchronise the device, as
-// cudaMalloc and cudaFree do.  The two-pass reduction parks one fp32 partial per pass-1 CTA in scratch;
-// here that scratch is the file-scope array below, which every GPU that loads this library holds until
-// the process exits.
-// ---------------------------------------------------------------------------------------------------
-namespace ptsim {
-
-// 4 KiB: pass 1 never runs more than 1024 CTAs (4 per SM, capped), one fp32 partial each.
-constexpr size_t kStaticScratchBytes = 1024 * sizeof(float);
-static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
-
-static std::mutex g_static_mu;
-static void *g_static_ptr[64];
-
-// Device address of g_static_scratch on `dev` (the current device), looked up once per device.  In host
-// code the array's name is only a host-side stand-in, so kernels get this address instead.
-static int static_scratch(int dev, void **out) {
-  std::lock_guard<std::mutex> lk(g_static_mu);
-  if (dev < 0 || dev >= 64) return fail(PTSIM_E_ARGS, "device %d out of range", dev);
-  if (g_static_ptr[dev] == nullptr) {
-    void *p = nullptr;
-    PTSIM_CUDA(cudaGetSymbolAddress(&p, g_static_scratch));
-    if (p == nullptr) return fail(PTSIM_E_CUDA, "no device address for the static scratch on device %d", dev);
-    g_static_ptr[dev] = p;
-  }
-  *out = g_static_ptr[dev];
-  return PTSIM_OK;
-}
-
-}  // namespace ptsim
 
 extern "C" int ptsim_launch_reduce_noalloc(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int nptr,
                                            void *stream) {

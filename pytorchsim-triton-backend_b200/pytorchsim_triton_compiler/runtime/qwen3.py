@@ -119,6 +119,97 @@ def build_layer(device, T, params, cos, sin, x, tp=1, rank=0, objects=None):
     return g1, g2
 
 
+class TpLayer:
+    """Rank `rank`'s share of the tensor-parallel layer with its two all-reduces overlapped with compute.
+
+    The o projection and everything after it (RMSNorm, gate_up, SiLU * mul, down) treat token rows
+    independently, so they run in `chunks` row blocks: the all-reduce of the o projection's block c goes
+    out on a communication stream while block c + 1 is computed, the MLP of block c starts as soon as its
+    reduced rows are in, and the all-reduce of the MLP's block c overlaps block c + 1.  Only the last
+    block's all-reduce is exposed.  Each piece is a CUDA graph over the same resident buffers; the
+    collective is the caller's (`all_reduce(tensor)`, e.g. torch.distributed.all_reduce over NCCL), issued
+    on the communication stream.  Rows are cut into equal blocks (T % chunks == 0)."""
+
+    def __init__(self, device, T, params, cos, sin, x, tp, rank, chunks=2):
+        import torch
+        if tp < 2 or T % chunks != 0:
+            raise ValueError(f"TpLayer needs tp >= 2 and T divisible by chunks, got tp={tp}, T={T}, chunks={chunks}")
+        self.torch = torch
+        self.device = torch.device(device)
+        self.chunks = chunks
+        hq, it = HQ // tp, INTER // tp
+        self.main, _ = build_layer(device, T, params, cos, sin, x, tp=tp, rank=rank)
+        self.main.steps = [st for st in self.main.steps if not st[0].startswith("08_")]   # o proj goes by blocks
+        bufs = self.main.buffers
+        Tc = T // chunks
+        self.o_parts, self.mlp_parts = [], []
+        resid = rank == 0
+        for c in range(chunks):
+            def view(name, width):
+                key = f"{name}@{c}"
+                bufs[key] = bufs[name][c * Tc * width:(c + 1) * Tc * width]
+                return key
+            xc, otc, x1c = view("x", HIDDEN), view("ot", hq * DIM), view("x1", HIDDEN)
+            h2c, guc, ac, yc = view("h2", HIDDEN), view("gu", 2 * it), view("a", it), view("y", HIDDEN)
+            go = Graph(device)
+            go.buffers = bufs
+            if resid:
+                go.add("08_o_mm_residual", D.to_bytes(B.gemm(Tc, HIDDEN, hq * DIM, residual=True)), [xc, otc, "wo", x1c])
+            else:
+                go.add("08_o_mm", D.to_bytes(B.gemm(Tc, HIDDEN, hq * DIM)), [otc, "wo", x1c])
+            gm = Graph(device)
+            gm.buffers = bufs
+            gm.add("00_rmsnorm_2", D.to_bytes(B.row_rmsnorm(Tc, HIDDEN, 1e-6)), [x1c, "ln2", h2c])
+            gm.add("09_gate_up_mm", D.to_bytes(B.gemm(Tc, 2 * it, HIDDEN)), [h2c, "wgu", guc])
+            gm.add("10_silu_mul", D.to_bytes(B.silu_mul(Tc, it)), [guc, ac])
+            if resid:
+                gm.add("11_down_mm_residual", D.to_bytes(B.gemm(Tc, HIDDEN, it, residual=True)), [x1c, ac, "wd", yc])
+            else:
+                gm.add("11_down_mm", D.to_bytes(B.gemm(Tc, HIDDEN, it)), [ac, "wd", yc])
+            self.o_parts.append((go, bufs[x1c]))
+            self.mlp_parts.append((gm, bufs[yc]))
+        self.buffers = bufs
+        self.comm = torch.cuda.Stream(self.device)
+
+    def graphs(self):
+        return [self.main] + [g for g, _ in self.o_parts] + [g for g, _ in self.mlp_parts]
+
+    def capture(self):
+        for g in self.graphs():
+            g.capture()
+
+    def launch_count(self):
+        return sum(g.launch_count() for g in self.graphs())
+
+    def run(self, all_reduce):
+        """Enqueue one layer on the current stream (compute) and the communication stream; returns with the
+        current stream ordered after the last all-reduce."""
+        torch = self.torch
+        compute = torch.cuda.current_stream(self.device)
+        comm = self.comm
+        self.main.run()
+        done_x1 = []
+        for g, part in self.o_parts:
+            g.run()
+            ev = torch.cuda.Event()
+            ev.record(compute)
+            comm.wait_event(ev)
+            with torch.cuda.stream(comm):
+                all_reduce(part)
+                e2 = torch.cuda.Event()
+                e2.record(comm)
+            done_x1.append(e2)
+        for (g, part), ev_x1 in zip(self.mlp_parts, done_x1):
+            compute.wait_event(ev_x1)
+            g.run()
+            ev = torch.cuda.Event()
+            ev.record(compute)
+            comm.wait_event(ev)
+            with torch.cuda.stream(comm):
+                all_reduce(part)
+        compute.wait_stream(comm)
+
+
 def layer_flops(T):
     """GEMM + causal attention flops of one layer (824,633,720,832 at T = 2048)."""
     gemm = 2 * T * HIDDEN * (HQ * DIM + 2 * HKV * DIM) + 2 * T * HQ * DIM * HIDDEN + 2 * T * HIDDEN * 2 * INTER \

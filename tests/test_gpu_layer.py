@@ -51,7 +51,7 @@ def test_layer_t2048_reference_objects_cuda_graph():
     assert run_layer(2048, objs, graph=True) < 1e-2
 
 
-def _tp_rank(rank, world, port, q, T):
+def _tp_rank(rank, world, port, q, T, chunks=0):
     import datetime
     import sys
     root = os.path.dirname(HERE)
@@ -66,15 +66,22 @@ def _tp_rank(rank, world, port, q, T):
         p = Q2.random_params(0)
         x = torch.randn(T * Q2.HIDDEN, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
         cos, sin = O2.rope_tables(T)
-        g1, g2 = Q2.build_layer(f"cuda:{rank}", T, Q2.shard(p, rank, world), cos, sin, x, tp=world, rank=rank)
-        g1.run()
-        dist.all_reduce(g1.buffers["x1"])
-        g2.run()
-        dist.all_reduce(g1.buffers["y"])
+        if chunks:
+            layer = Q2.TpLayer(f"cuda:{rank}", T, Q2.shard(p, rank, world), cos, sin, x, world, rank, chunks=chunks)
+            layer.capture()
+            layer.run(dist.all_reduce)
+            buffers = layer.buffers
+        else:
+            g1, g2 = Q2.build_layer(f"cuda:{rank}", T, Q2.shard(p, rank, world), cos, sin, x, tp=world, rank=rank)
+            g1.run()
+            dist.all_reduce(g1.buffers["x1"])
+            g2.run()
+            dist.all_reduce(g1.buffers["y"])
+            buffers = g1.buffers
         torch.cuda.synchronize()
         if rank == 0:
             want = O2.decoder_layer(x, p, T, cos=cos, sin=sin).float()
-            got = g1.buffers["y"].float().cpu()
+            got = buffers["y"].float().cpu()
             q.put((rank, float((got - want).norm() / want.norm())))
         else:
             q.put((rank, None))
@@ -85,7 +92,10 @@ def _tp_rank(rank, world, port, q, T):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="tensor parallel needs two GPUs")
-def test_layer_tp2_nccl():
+@pytest.mark.parametrize("chunks", [0, 2, 4])
+def test_layer_tp2_nccl(chunks):
+    """The layer over two GPUs: serial all-reduces (chunks 0), or the o projection and the MLP in row blocks
+    whose all-reduces overlap the next block's compute (runtime/qwen3.py TpLayer)."""
     import socket
     import torch.multiprocessing as mp
     s = socket.socket()
@@ -94,7 +104,7 @@ def test_layer_tp2_nccl():
     s.close()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    ps = [ctx.Process(target=_tp_rank, args=(r, 2, port, q, 256)) for r in range(2)]
+    ps = [ctx.Process(target=_tp_rank, args=(r, 2, port, q, 256, chunks)) for r in range(2)]
     for p in ps:
         p.start()
     got = dict(q.get(timeout=600) for _ in range(2))
