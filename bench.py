@@ -225,6 +225,17 @@ def cpu_rate(seconds=10.0, rows=4096):
                                       f"restatement of the reference programs (oracle/programs.py)"}, dt / n
 
 
+def interpreter_baseline():
+    """The reference's own Triton kernels timed under the Triton interpreter (one core), as
+    tests/golden/interpreter_baseline.py recorded them in the build container (the reference tree is not on
+    the GPU box), or None."""
+    try:
+        with open(os.path.join(ROOT, "tests", "golden", "interpreter_baseline.json")) as fh:
+            return json.load(fh)
+    except (OSError, ValueError):
+        return None
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return
@@ -579,6 +590,9 @@ def run_b200(args, world, rank, local):
         line["tp_layer"] = tp_layer_timing(dev, world, rank, steps=10, warmup=3)
     if rank == 0 and world == 1 and args.cpu:
         base, _ = cpu_rate(seconds=10.0)
+        interp = interpreter_baseline()
+        if interp is not None:
+            base["interpreter"] = interp
         line["cpu_baseline"] = base
         if args.suite:
             line["suite"] = suite(dev, stream)
