@@ -16,7 +16,7 @@ import numpy as np
 
 from ..codegen import descriptors as D
 from ..contract import kernel_object as ko
-from . import native
+from . import dma_access, native
 
 
 class CudaError(RuntimeError):
@@ -297,6 +297,7 @@ def launch(desc_blob, manifest, runtime, raw_paths, options=None, *, log=print, 
     ranges = split(total, n)
     log(f"[cuda] {total} units over {len(ranges)} device(s)")
     base = {a["name"]: host[a["name"]].view(np.uint8).copy() for a in ko.writable(manifest)}
+    ran = [(devs[w], lo, hi) for w, (lo, hi) in enumerate(ranges)]
     try:
         if len(ranges) == 1:
             parts = [_run_range(desc_blob, manifest, host, devs[0], *ranges[0])]
@@ -310,8 +311,12 @@ def launch(desc_blob, manifest, runtime, raw_paths, options=None, *, log=print, 
         except NotSplittable as why:
             log(f"[cuda] {why} -- running the grid on one device instead")
             merged = merge(manifest, base, [_run_range(desc_blob, manifest, host, devs[0], 0, total)])
+            ran = [(devs[0], 0, total)]
     except native.ExecutorError as e:
         raise error(str(e)) from None
     for a in ko.writable(manifest):
         merged[a["name"]].tofile(raw_paths[a["name"]])
+    # The DMA-access trace of the ranges that ran (runtime/dma_access/trace.json), from the descriptor's index
+    # maps; the grouped GEMM's data-dependent rows resolved from the launch's own tables.
+    dma_access.write(runtime, manifest, desc, ran, host)
     return runtime
