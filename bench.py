@@ -489,13 +489,14 @@ def run_b200(args, world, rank, local):
     ms_per_step = total_ms / args.steps
     value = world * STEP_BYTES * args.steps / (total_ms / 1e3) / 1e9
 
-    # e2e: the same step through the runtime's host-memory launcher (runtime.cuda.HostPipeline, over the C
-    # ABI) with pinned host buffers: every step copies the inputs in and the outputs back inside the timed
-    # region, row ranges pipelined so PCIe carries both directions while the kernels run.
+    # e2e: the same step through the runtime's host-memory launcher (runtime.cuda.HostPipeline, one C-ABI call
+    # ptsim_launch_host per launch) with pinned host buffers: every step copies the inputs in and the outputs
+    # back inside the timed region, 4 row ranges pipelined so PCIe carries both directions while the kernels
+    # run (8, 16 and 32 ranges measured slower: 77.4, 66.8 and 59.3 GB/s against 80.7).
     xs_p, xr_p, w_p = xs_h.pin_memory(), xr_h.pin_memory(), w_h.pin_memory()
     ys_p, yr_p = torch.empty_like(xs_p).pin_memory(), torch.empty_like(xr_p).pin_memory()
     e2e_steps = max(3, args.steps)
-    pipe = RC.HostPipeline(local, chunks=8)
+    pipe = RC.HostPipeline(local, chunks=4)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     h2d = xs_p.numel() * 2 + xr_p.numel() * 2 + w_p.numel() * 2
     d2h = ys_p.numel() * 2 + yr_p.numel() * 2
@@ -575,7 +576,7 @@ def run_b200(args, world, rank, local):
                          "per_kernel": {"row_softmax": {"ms": round(soft_ms, 4), "GB/s": round(SOFTMAX_BYTES / soft_ms / 1e6, 1)},
                                         "row_rmsnorm": {"ms": round(rms_ms, 4), "GB/s": round(RMSNORM_BYTES / rms_ms / 1e6, 1)}}},
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "api": "runtime.cuda.HostPipeline (C ABI ptsim_launch) over pinned host buffers, 8 row ranges per launch",
+                    "api": "runtime.cuda.HostPipeline -> C ABI ptsim_launch_host over pinned host buffers, 4 pipelined row ranges per launch",
                     "copy_ceiling": round(e2e_ceiling, 2), "frac_of_copy_ceiling": round(e2e_val / e2e_ceiling, 3),
                     "copy_ceiling_note": "the same bytes as plain pinned copies (inputs in and outputs out on two "
                                          "streams at once, no kernel), in this metric's units"},

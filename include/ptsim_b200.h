@@ -385,6 +385,20 @@ int64_t ptsim_workspace_size(const void *desc, size_t desc_bytes, int device);
  * device scratch. */
 int ptsim_launch_reduce_noalloc(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int nptr, void *stream);
 
+/* Run the whole launch `desc` over tensors in HOST memory, the way a caller holding .raw data runs it end to
+ * end: the arguments in `copy_in_mask` (bit a = argument a) are copied from host_ptrs[a] to dev_ptrs[a], the
+ * kernels run, and the arguments in `copy_out_mask` are copied back.  Device buffers are the caller's (the
+ * library allocates nothing).  A row launch (softmax, RMSNorm) is cut into `chunks` unit ranges (edges
+ * units * k / chunks) so that, over three streams (copies in, kernels, copies out), the copy of one range's
+ * input rows overlaps the kernel of the range before and the return of that range's output rows; PCIe then
+ * carries both directions at once.  Other kinds copy in, run once and copy out.  Host memory should be pinned
+ * (page-locked) for the copies to overlap.  Asynchronous like ptsim_launch: synchronise `stream_out` (and
+ * check ptsim_sync on `stream_run`) before reading the outputs.  Replaces the reference's .raw round trip
+ * around a Spike run (runtime/spike.py:100-120). */
+int ptsim_launch_host(const void *desc, size_t desc_bytes, void *const *host_ptrs, void *const *dev_ptrs, int nptr,
+                      uint32_t copy_in_mask, uint32_t copy_out_mask, int chunks, void *workspace,
+                      size_t workspace_bytes, void *stream_in, void *stream_run, void *stream_out);
+
 /* Synchronise `stream` and return (and clear) the device status word of the current device:
  * *device_status receives PTSIM_OK or PTSIM_E_OOB / PTSIM_E_TIMEOUT as a kernel recorded it.
  * Replaces the exit-code check of runtime/spike.py:23-33 (run_process). */

@@ -460,6 +460,76 @@ int64_t ptsim_workspace_size(const void *desc, size_t desc_bytes, int device) {
   return need;
 }
 
+int ptsim_launch_host(const void *desc, size_t desc_bytes, void *const *host_ptrs, void *const *dev_ptrs, int nptr,
+                      uint32_t copy_in_mask, uint32_t copy_out_mask, int chunks, void *workspace,
+                      size_t workspace_bytes, void *stream_in, void *stream_run, void *stream_out) {
+  int rc = check_desc(desc, desc_bytes);
+  if (rc) return rc;
+  const ptsim_desc &d = *reinterpret_cast<const ptsim_desc *>(desc);
+  if (nptr != d.nargs) return fail(PTSIM_E_ARGS, "%d pointers for a launch of %d arguments", nptr, d.nargs);
+  for (int a = 0; a < nptr; ++a)
+    if ((host_ptrs[a] == nullptr || dev_ptrs[a] == nullptr) && d.arg_numel[a] > 0)
+      return fail(PTSIM_E_ARGS, "argument %d has a null host or device pointer", a);
+  cudaStream_t s_in = reinterpret_cast<cudaStream_t>(stream_in), s_run = reinterpret_cast<cudaStream_t>(stream_run),
+               s_out = reinterpret_cast<cudaStream_t>(stream_out);
+  const bool row = d.kind == PTSIM_KIND_ROW_SOFTMAX || d.kind == PTSIM_KIND_ROW_RMSNORM;
+  const ptsim_row_params &rp = d.p.row;
+  int64_t n = row ? (chunks < 1 ? 1 : chunks) : 1;
+  if (n > d.units) n = d.units < 1 ? 1 : d.units;
+  auto bytes_of = [&](int a) { return d.arg_numel[a] * int64_t(dtype_size(d.arg_dtype[a])); };
+  // The elements [first, end) of a row argument that units [lo, hi) touch (rows at `stride`).
+  auto row_span = [&](int a, int64_t lo, int64_t hi, int64_t stride, int64_t &first, int64_t &end) {
+    const int64_t r0 = lo * d.unit_size, r1 = hi * d.unit_size < rp.rows ? hi * d.unit_size : rp.rows;
+    first = r0 * stride;
+    end = r1 > r0 ? (r1 - 1) * stride + rp.cols : first;
+    if (end > d.arg_numel[a]) end = d.arg_numel[a];
+  };
+  // Arguments copied whole, before the first range (a row launch's row-partitioned input and output go by range).
+  for (int a = 0; a < nptr; ++a) {
+    if (!(copy_in_mask & (1u << a)) || (row && (a == rp.in_arg || a == rp.out_arg))) continue;
+    PTSIM_CUDA(cudaMemcpyAsync(dev_ptrs[a], host_ptrs[a], size_t(bytes_of(a)), cudaMemcpyHostToDevice, s_in));
+  }
+  for (int64_t k = 0; k < n; ++k) {
+    const int64_t lo = d.units * k / n, hi = d.units * (k + 1) / n;   // the reference's split edges
+    if (lo == hi) continue;
+    if (row && (copy_in_mask & (1u << rp.in_arg))) {
+      int64_t f, e;
+      row_span(rp.in_arg, lo, hi, rp.in_row_stride, f, e);
+      const int64_t es = dtype_size(d.arg_dtype[rp.in_arg]);
+      if (e > f)
+        PTSIM_CUDA(cudaMemcpyAsync(static_cast<char *>(dev_ptrs[rp.in_arg]) + f * es,
+                                   static_cast<const char *>(host_ptrs[rp.in_arg]) + f * es, size_t((e - f) * es),
+                                   cudaMemcpyHostToDevice, s_in));
+    }
+    cudaEvent_t ev_in, ev_run;
+    PTSIM_CUDA(cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming));
+    PTSIM_CUDA(cudaEventCreateWithFlags(&ev_run, cudaEventDisableTiming));
+    PTSIM_CUDA(cudaEventRecord(ev_in, s_in));
+    PTSIM_CUDA(cudaStreamWaitEvent(s_run, ev_in, 0));
+    rc = ptsim_launch(desc, desc_bytes, dev_ptrs, nptr, lo, hi, workspace, workspace_bytes, stream_run);
+    if (rc) {
+      cudaEventDestroy(ev_in);
+      cudaEventDestroy(ev_run);
+      return rc;
+    }
+    PTSIM_CUDA(cudaEventRecord(ev_run, s_run));
+    PTSIM_CUDA(cudaStreamWaitEvent(s_out, ev_run, 0));
+    cudaEventDestroy(ev_in);    // released once their work completes
+    cudaEventDestroy(ev_run);
+    for (int a = 0; a < nptr; ++a) {
+      if (!(copy_out_mask & (1u << a))) continue;
+      int64_t f = 0, e = d.arg_numel[a];
+      if (row && a == rp.out_arg) row_span(a, lo, hi, rp.out_row_stride, f, e);
+      else if (k + 1 < n) continue;   // copied whole after the last range
+      const int64_t es = dtype_size(d.arg_dtype[a]);
+      if (e > f)
+        PTSIM_CUDA(cudaMemcpyAsync(static_cast<char *>(host_ptrs[a]) + f * es, static_cast<const char *>(dev_ptrs[a]) + f * es,
+                                   size_t((e - f) * es), cudaMemcpyDeviceToHost, s_out));
+    }
+  }
+  return PTSIM_OK;
+}
+
 int ptsim_sync(void *stream, int32_t *device_status) {
   PTSIM_CUDA(cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)));
   int st = 0, zero = 0;

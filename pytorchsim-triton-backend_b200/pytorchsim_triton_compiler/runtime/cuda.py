@@ -145,11 +145,12 @@ class HostPipeline:
     copied back into the host tensors.  Copies run on their own streams (host-to-device, device-to-host)
     beside the compute stream, and a row-wise launch (softmax, RMSNorm) is cut into `chunks` unit ranges
     so the transfer of one range overlaps the kernel of the previous one and the return of the one before
-    that; PCIe then carries both directions at once.  Host tensors should be pinned for the copies to be
-    asynchronous.  Launches submitted to one pipeline run in submission order; wait() synchronises and
-    raises ExecutorError if a kernel reported a failure."""
+    that; PCIe then carries both directions at once.  The copies, kernels and stream ordering of a launch are
+    enqueued by one native call (ptsim_launch_host), so the host cost per range is microseconds.  Host
+    tensors should be pinned for the copies to be asynchronous.  Launches submitted to one pipeline run in
+    submission order; wait() synchronises and raises ExecutorError if a kernel reported a failure."""
 
-    def __init__(self, device=0, chunks=8):
+    def __init__(self, device=0, chunks=4):
         torch = _torch()
         self.torch = torch
         self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
@@ -174,43 +175,13 @@ class HostPipeline:
         ws = workspace_for(blob, self.device)
         wsp, wsn = (ws.data_ptr(), ws.numel()) if ws is not None else (0, 0)
         self._live.append((dev, ws))
-        row = desc.kind in (D.ROW_SOFTMAX, D.ROW_RMSNORM)
-        n_chunks = min(self.chunks, desc.units) if row else 1
-        bounds = split(desc.units, n_chunks)
+        # One native call enqueues the copies in, the kernels and the copies back (a row launch in pipelined unit
+        # ranges): every argument goes in (an output's initial bytes matter for arguments read as well as
+        # written), the written ones come back.
         with torch.cuda.device(self.device):
-            # Arguments every range reads whole (or that are not row-partitioned) go first.
-            whole = [i for i in range(desc.nargs) if not row or i not in (desc.p.row.in_arg, desc.p.row.out_arg)]
-            with torch.cuda.stream(self.s_in):
-                for i in whole:
-                    dev[i].copy_(host[i].reshape(-1), non_blocking=True)
-            for lo, hi in bounds:
-                ev_in = torch.cuda.Event()
-                with torch.cuda.stream(self.s_in):
-                    if row:
-                        r = desc.p.row
-                        a, b = self._rows(desc, lo, hi, r.in_row_stride, desc.arg_numel[r.in_arg])
-                        dev[r.in_arg][a:b].copy_(host[r.in_arg].reshape(-1)[a:b], non_blocking=True)
-                    ev_in.record(self.s_in)
-                self.s_run.wait_event(ev_in)
-                native.launch(blob, ptrs, lo, hi, wsp, wsn, self.s_run.cuda_stream)
-                ev_run = torch.cuda.Event()
-                ev_run.record(self.s_run)
-                self.s_out.wait_event(ev_run)
-                with torch.cuda.stream(self.s_out):
-                    for i in outs:
-                        if row:
-                            r = desc.p.row
-                            a, b = self._rows(desc, lo, hi, r.out_row_stride, desc.arg_numel[i])
-                        else:
-                            a, b = 0, desc.arg_numel[i]
-                        host[i].reshape(-1)[a:b].copy_(dev[i][a:b], non_blocking=True)
+            native.launch_host(blob, [t.data_ptr() for t in host], ptrs, range(desc.nargs), outs, self.chunks, wsp, wsn,
+                               self.s_in.cuda_stream, self.s_run.cuda_stream, self.s_out.cuda_stream)
         return host
-
-    @staticmethod
-    def _rows(desc, lo, hi, stride, numel):
-        r0 = lo * desc.unit_size
-        r1 = min(hi * desc.unit_size, desc.p.row.rows)
-        return r0 * stride, min(numel, (r1 - 1) * stride + desc.p.row.cols)
 
     def wait(self):
         self.s_out.synchronize()

@@ -22,6 +22,9 @@ SYMBOLS = {
                                C.c_void_p, C.c_size_t, C.c_void_p]),
     "ptsim_workspace_size": (C.c_int64, [C.c_void_p, C.c_size_t, C.c_int]),
     "ptsim_launch_reduce_noalloc": (C.c_int, [C.c_void_p, C.c_size_t, C.POINTER(C.c_void_p), C.c_int, C.c_void_p]),
+    "ptsim_launch_host": (C.c_int, [C.c_void_p, C.c_size_t, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.c_int,
+                                    C.c_uint32, C.c_uint32, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p,
+                                    C.c_void_p]),
     "ptsim_sync": (C.c_int, [C.c_void_p, C.POINTER(C.c_int32)]),
     "ptsim_last_error": (C.c_int, [C.c_char_p, C.c_int]),
 }
@@ -146,6 +149,23 @@ def launch_reduce_noalloc(blob, ptrs, stream=0):
     buf = _desc_buffer(blob)
     arr = (C.c_void_p * max(1, len(ptrs)))(*[C.c_void_p(int(p)) for p in ptrs])
     _check(lib.ptsim_launch_reduce_noalloc(buf, len(blob), arr, len(ptrs), C.c_void_p(int(stream) or None)))
+
+
+def launch_host(blob, host_ptrs, dev_ptrs, copy_in, copy_out, chunks, workspace=0, workspace_bytes=0,
+                stream_in=0, stream_run=0, stream_out=0):
+    """Enqueue the whole launch of `blob` over host tensors (ptsim_launch_host): the arguments whose indices are in
+    `copy_in` copied to their device buffers, the kernels run (a row launch in `chunks` pipelined unit ranges),
+    the arguments in `copy_out` copied back.  Asynchronous."""
+    lib = load()
+    buf = _desc_buffer(blob)
+    n = max(1, len(host_ptrs))
+    hp = (C.c_void_p * n)(*[C.c_void_p(int(p)) for p in host_ptrs])
+    dp = (C.c_void_p * n)(*[C.c_void_p(int(p)) for p in dev_ptrs])
+    cin = sum(1 << int(i) for i in copy_in)
+    cout = sum(1 << int(i) for i in copy_out)
+    _check(lib.ptsim_launch_host(buf, len(blob), hp, dp, len(host_ptrs), cin, cout, int(chunks),
+                                 C.c_void_p(int(workspace) or None), int(workspace_bytes), C.c_void_p(int(stream_in) or None),
+                                 C.c_void_p(int(stream_run) or None), C.c_void_p(int(stream_out) or None)))
 
 
 def sync(stream=0):
