@@ -3,6 +3,7 @@
 #pragma once
 
 #include <atomic>
+#include <utility>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -73,6 +74,17 @@ __device__ __forceinline__ float nan_min(float a, float b) {
 
 __host__ __device__ __forceinline__ int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Programmatic dependent launch.  Kernels launched with launch_pdl may be scheduled while the kernel before
+// them in the stream is still running: each first waits for that kernel to finish and its memory to be
+// visible (griddepcontrol.wait, before any global access, so reads after writes and writes after reads of
+// the previous kernel stay ordered), then lets the kernel after it be scheduled (launch_dependents).  What
+// overlaps is the next launch's scheduling and start-up with this kernel's tail.  Both instructions are
+// no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Element size in bytes of a PTSIM_DT_* type.
 __host__ __device__ __forceinline__ int dtype_size(int dt) {
   switch (dt) {
@@ -107,6 +119,24 @@ inline cudaError_t smem_limit_once(int bytes, int device) {
   const cudaError_t e = cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
   return e;
+}
+
+// Launch `kern` on `stream` with programmatic stream serialization (see pdl_enter); the kernel must call
+// pdl_enter() before it touches global memory.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 #define PTSIM_CUDA(call)                                                                   \

@@ -182,6 +182,7 @@ __device__ __forceinline__ void reg_write(float (&r)[NREG][8], int i, const floa
 
 template <int NREG>
 __global__ void __launch_bounds__(256) ew_program_kernel(const __grid_constant__ EwLaunch L) {
+  pdl_enter();
   const int64_t groups = ceil_div(L.end - L.begin, 8);
   float r[NREG][8];
 #pragma unroll
@@ -283,6 +284,7 @@ __device__ __forceinline__ void ew_dispatch8(int op, const float a[8], const flo
 // contiguous run.
 template <int KIND, int NG>
 __global__ void __launch_bounds__(256) ew_pattern_kernel(const __grid_constant__ EwLaunch L, const EwPattern P) {
+  pdl_enter();
   const int64_t groups = ceil_div(L.end - L.begin, 8);
   const int64_t step = int64_t(gridDim.x) * blockDim.x * NG;
   for (int64_t g0 = int64_t(blockIdx.x) * blockDim.x * NG + threadIdx.x; g0 < groups; g0 += step) {
@@ -416,6 +418,7 @@ __device__ __forceinline__ void vpattern_math(const EwVec &V, float x[8], float 
 
 template <int KIND, int NG, int DT>
 __global__ void __launch_bounds__(256, DT == PTSIM_DT_F32 ? 5 : 8) ew_vpattern_kernel(const __grid_constant__ EwVec V) {
+  pdl_enter();
   const uint32_t full = (V.end - V.begin) / 8;   // groups of 8 inside the launch
   const uint32_t g0 = blockIdx.x * blockDim.x * NG + threadIdx.x;
   RawGroup<DT> a[NG], b[NG];
@@ -516,6 +519,7 @@ static EwPattern match_pattern(const ptsim_ew_params &p) {
 // Pure copy: the loaded element's bytes go to the store unchanged (bit exact for every dtype).
 template <int ESIZE>
 __global__ void __launch_bounds__(256) ew_copy_kernel(const __grid_constant__ EwLaunch L) {
+  pdl_enter();
   using T = typename std::conditional<ESIZE == 1, uint8_t,
             typename std::conditional<ESIZE == 2, uint16_t,
             typename std::conditional<ESIZE == 4, uint32_t, uint64_t>::type>::type>::type;
@@ -645,10 +649,10 @@ int launch_elementwise(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64
   if (L.p.pure_copy) {
     const int es = dtype_size(d.arg_dtype[L.p.map[0].arg]);
     switch (es) {
-      case 1: ew_copy_kernel<1><<<unsigned(blocks), threads, 0, c.stream>>>(L); break;
-      case 2: ew_copy_kernel<2><<<unsigned(blocks), threads, 0, c.stream>>>(L); break;
-      case 4: ew_copy_kernel<4><<<unsigned(blocks), threads, 0, c.stream>>>(L); break;
-      case 8: ew_copy_kernel<8><<<unsigned(blocks), threads, 0, c.stream>>>(L); break;
+      case 1: PTSIM_CUDA(launch_pdl(ew_copy_kernel<1>, dim3(unsigned(blocks)), dim3(threads), 0, c.stream, L)); break;
+      case 2: PTSIM_CUDA(launch_pdl(ew_copy_kernel<2>, dim3(unsigned(blocks)), dim3(threads), 0, c.stream, L)); break;
+      case 4: PTSIM_CUDA(launch_pdl(ew_copy_kernel<4>, dim3(unsigned(blocks)), dim3(threads), 0, c.stream, L)); break;
+      case 8: PTSIM_CUDA(launch_pdl(ew_copy_kernel<8>, dim3(unsigned(blocks)), dim3(threads), 0, c.stream, L)); break;
       default: return fail(PTSIM_E_DESC, "elementwise copy of a %d-byte element", es);
     }
   } else if (const EwPattern P = match_pattern(L.p); P.kind != EW_VM) {
@@ -681,20 +685,20 @@ int launch_elementwise(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64
       const int64_t pb = ceil_div(groups, int64_t(threads) * ng);
       const unsigned gb = unsigned(pb < 1 ? 1 : pb);
       if (dt == PTSIM_DT_BF16) {
-        if (P.kind == EW_BINOP) ew_vpattern_kernel<EW_BINOP, ng, PTSIM_DT_BF16><<<gb, threads, 0, c.stream>>>(V);
-        else if (P.kind == EW_SCALAR) ew_vpattern_kernel<EW_SCALAR, ng, PTSIM_DT_BF16><<<gb, threads, 0, c.stream>>>(V);
-        else ew_vpattern_kernel<EW_SILU_MUL, ng, PTSIM_DT_BF16><<<gb, threads, 0, c.stream>>>(V);
+        if (P.kind == EW_BINOP) PTSIM_CUDA(launch_pdl(ew_vpattern_kernel<EW_BINOP, ng, PTSIM_DT_BF16>, dim3(gb), dim3(threads), 0, c.stream, V));
+        else if (P.kind == EW_SCALAR) PTSIM_CUDA(launch_pdl(ew_vpattern_kernel<EW_SCALAR, ng, PTSIM_DT_BF16>, dim3(gb), dim3(threads), 0, c.stream, V));
+        else PTSIM_CUDA(launch_pdl(ew_vpattern_kernel<EW_SILU_MUL, ng, PTSIM_DT_BF16>, dim3(gb), dim3(threads), 0, c.stream, V));
       } else {
-        if (P.kind == EW_BINOP) ew_vpattern_kernel<EW_BINOP, ng, PTSIM_DT_F32><<<gb, threads, 0, c.stream>>>(V);
-        else if (P.kind == EW_SCALAR) ew_vpattern_kernel<EW_SCALAR, ng, PTSIM_DT_F32><<<gb, threads, 0, c.stream>>>(V);
-        else ew_vpattern_kernel<EW_SILU_MUL, ng, PTSIM_DT_F32><<<gb, threads, 0, c.stream>>>(V);
+        if (P.kind == EW_BINOP) PTSIM_CUDA(launch_pdl(ew_vpattern_kernel<EW_BINOP, ng, PTSIM_DT_F32>, dim3(gb), dim3(threads), 0, c.stream, V));
+        else if (P.kind == EW_SCALAR) PTSIM_CUDA(launch_pdl(ew_vpattern_kernel<EW_SCALAR, ng, PTSIM_DT_F32>, dim3(gb), dim3(threads), 0, c.stream, V));
+        else PTSIM_CUDA(launch_pdl(ew_vpattern_kernel<EW_SILU_MUL, ng, PTSIM_DT_F32>, dim3(gb), dim3(threads), 0, c.stream, V));
       }
     } else {
       int64_t pb = ceil_div(groups, int64_t(threads) * 2);
       if (pb > cap) pb = cap;
-      if (P.kind == EW_BINOP) ew_pattern_kernel<EW_BINOP, 2><<<unsigned(pb), threads, 0, c.stream>>>(L, P);
-      else if (P.kind == EW_SCALAR) ew_pattern_kernel<EW_SCALAR, 2><<<unsigned(pb), threads, 0, c.stream>>>(L, P);
-      else ew_pattern_kernel<EW_SILU_MUL, 2><<<unsigned(pb), threads, 0, c.stream>>>(L, P);
+      if (P.kind == EW_BINOP) PTSIM_CUDA(launch_pdl(ew_pattern_kernel<EW_BINOP, 2>, dim3(unsigned(pb)), dim3(threads), 0, c.stream, L, P));
+      else if (P.kind == EW_SCALAR) PTSIM_CUDA(launch_pdl(ew_pattern_kernel<EW_SCALAR, 2>, dim3(unsigned(pb)), dim3(threads), 0, c.stream, L, P));
+      else PTSIM_CUDA(launch_pdl(ew_pattern_kernel<EW_SILU_MUL, 2>, dim3(unsigned(pb)), dim3(threads), 0, c.stream, L, P));
     }
   } else {
     int top = 0;
@@ -706,9 +710,9 @@ int launch_elementwise(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64
         top = in.b > top ? in.b : top;
       }
     }
-    if (top < 2) ew_program_kernel<2><<<unsigned(blocks), threads, 0, c.stream>>>(L);
-    else if (top < 4) ew_program_kernel<4><<<unsigned(blocks), threads, 0, c.stream>>>(L);
-    else ew_program_kernel<8><<<unsigned(blocks), threads, 0, c.stream>>>(L);
+    if (top < 2) PTSIM_CUDA(launch_pdl(ew_program_kernel<2>, dim3(unsigned(blocks)), dim3(threads), 0, c.stream, L));
+    else if (top < 4) PTSIM_CUDA(launch_pdl(ew_program_kernel<4>, dim3(unsigned(blocks)), dim3(threads), 0, c.stream, L));
+    else PTSIM_CUDA(launch_pdl(ew_program_kernel<8>, dim3(unsigned(blocks)), dim3(threads), 0, c.stream, L));
   }
   PTSIM_CUDA(cudaGetLastError());
   return PTSIM_OK;
