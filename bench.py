@@ -324,17 +324,39 @@ def tp_layer_timing(dev, world, rank, steps, warmup):
         overlapped[chunks] = alone(lambda: lay.run(dist.all_reduce), n=steps + 2)
         del lay
     best = min(overlapped, key=overlapped.get)
-    ms = min(ms, overlapped[best])
+    # The layer with both all-reduces done by the executor's own kernels over NVLink peer memory (rank-order sum of
+    # the rows each rank owns, stored into every rank's buffer; runtime/qwen3.py TpLayerPeer): "pull" loads every
+    # rank's partial in one all-reduce kernel; "fused" pushes each GEMM's output rows to their owners from the
+    # GEMM's epilogue and sums the staging in a second kernel.  Beside each: its collective (the 16 MiB all-reduce,
+    # or the reduce-gather half) and its two segments timed alone.
+    s_ = torch.cuda.current_stream(dev).cuda_stream
+    peer = {}
+    for fused in (False, True):
+        lay = Q.TpLayerPeer(dev, T, Q.shard(p, rank, world), cos, sin, x, world, rank, fused=fused)
+        lay.capture()
+        for _ in range(warmup):
+            lay.run()
+        key = "fused" if fused else "pull"
+        peer[key] = {"ms": alone(lay.run, n=steps + 2),
+                     "collective_alone_ms": alone(lambda: lay.allreduce("x1p", "x1", "sig1", s_), n=10),
+                     "segment_1_ms": alone(lay.g1.run), "segment_2_ms": alone(lay.g2.run)}
+        lay.close()
+        del lay
+    peer_ms = min(v["ms"] for v in peer.values())
+    ms = min(ms, overlapped[best], peer_ms)
     tf = Q.layer_flops(T) / ms / 1e9
     return {"n_gpus": world, "ms": round(ms, 4), "TFLOP/s": round(tf, 1), "frac_bf16": round(tf / (world * tflops), 3),
             "scaling": "strong", "one_gpu_ms": round(t1, 4), "speedup": round(t1 / ms, 3),
             "efficiency": round(t1 / (world * ms), 3),
-            "serial_all_reduce_ms": round(serial_ms, 4),
-            "overlapped_ms": {f"{c}_row_blocks": round(v, 4) for c, v in overlapped.items()},
-            "parts_ms": {"segment_1": round(seg1, 4), "segment_2": round(seg2, 4), "all_reduce_16MiB": round(ar, 4),
-                         "all_reduces_per_layer": 2},
-            "collective": "NCCL all-reduce of 2048 x 4096 bf16 after o_proj and after down, in row blocks "
-                          "overlapped with the next block's compute (serial figure beside it)"}
+            "nccl_serial_ms": round(serial_ms, 4),
+            "nccl_overlapped_ms": {f"{c}_row_blocks": round(v, 4) for c, v in overlapped.items()},
+            "peer": {k: {kk: round(vv, 4) for kk, vv in v.items()} for k, v in peer.items()},
+            "parts_ms": {"segment_1": round(seg1, 4), "segment_2": round(seg2, 4),
+                         "nccl_all_reduce_16MiB": round(ar, 4), "all_reduces_per_layer": 2},
+            "collective": "after o_proj and after down, an all-reduce of the 2048 x 4096 bf16 partial sums: NCCL "
+                          "(serial, or in row blocks overlapped with compute) or the executor's own kernels over "
+                          "NVLink peer memory (pull: ptsim_tp_allreduce; fused: the GEMM pushes its rows to their "
+                          "owners, ptsim_launch_rows_to_owners, then ptsim_tp_reduce_gather); ms is the fastest"}
 
 
 def strong_headline(dev, world, rank, steps, warmup, d_s, d_r, ps, pr, flush, stream):

@@ -399,6 +399,48 @@ int ptsim_launch_host(const void *desc, size_t desc_bytes, void *const *host_ptr
                       uint32_t copy_in_mask, uint32_t copy_out_mask, int chunks, void *workspace,
                       size_t workspace_bytes, void *stream_in, void *stream_run, void *stream_out);
 
+/* Peer-visible buffers for the tensor-parallel all-reduce, set up once per process before the launches that use
+ * them (these calls allocate and synchronise; the launches do not).  ptsim_peer_alloc makes a zero-filled device
+ * buffer on the current device; ptsim_peer_handle writes its 64-byte CUDA IPC handle, which the other ranks'
+ * processes pass to ptsim_peer_open to map it (their pointer to this rank's buffer); ptsim_peer_close unmaps a
+ * peer's buffer and ptsim_peer_free releases one's own.  No reference counterpart (the reference runs one
+ * device). */
+int ptsim_peer_alloc(size_t bytes, void **dev_ptr);
+int ptsim_peer_free(void *dev_ptr);
+int ptsim_peer_handle(void *dev_ptr, void *handle);
+int ptsim_peer_open(const void *handle, void **dev_ptr);
+int ptsim_peer_close(void *dev_ptr);
+
+/* All-reduce of the tensor-parallel layer's row-parallel partial sums (bf16 [rows, cols]) over NVLink peer
+ * memory, on `stream` of the calling rank.  part[r], out[r] and signal[r] are rank r's partial, output and
+ * 256-byte signal block (zero-filled before the first call) as this rank addresses them (its own, or the peer
+ * mapping).  Rank q sums rows [q R, (q + 1) R), R = rows / nranks, of every partial in rank order (fp32, one
+ * bf16 rounding: the same bits on every run) and stores them into every rank's output; the kernel ends once
+ * every rank's rows have landed in this rank's output.  Every rank calls it, in the same order, with the same
+ * rows and cols.  Waits are bounded (PTSIM_E_TIMEOUT).  Replaces the NCCL all-reduce the tensor-parallel split
+ * adds after o_proj and down (no reference counterpart). */
+int ptsim_tp_allreduce(void *const *part, void *const *out, void *const *signal, int nranks, int rank, int64_t rows,
+                       int64_t cols, int dtype, void *stream);
+
+/* The same all-reduce with its reduce-scatter fused into the row-parallel GEMM, in two calls on `stream`:
+ *
+ * ptsim_launch_rows_to_owners: ptsim_launch of a GEMM descriptor (bf16 output, M = nowners * owner_rows) whose
+ * output rows [q owner_rows, (q + 1) owner_rows) are stored, as they leave the tensor cores, at owner_ptrs[q]
+ * (rank q's staging slot for this rank: rank q's staging + this rank * owner_rows * N, as this rank maps it; a
+ * peer store over NVLink) instead of into the descriptor's output argument, which is not written.
+ *
+ * ptsim_tp_reduce_gather: `stage` is this rank's staging (nranks slots of rows / nranks rows, slot r filled by
+ * rank r's GEMM); it sums the slots in rank order (fp32, one bf16 rounding: the bits ptsim_tp_allreduce gives)
+ * and stores the rows into every rank's output out[r]; signal[] as for ptsim_tp_allreduce (one block per
+ * collective: this call and ptsim_tp_allreduce must not share one).  Every rank launches both, in the same
+ * order.  Replaces the NCCL all-reduce after o_proj and down of the tensor-parallel split (no reference
+ * counterpart). */
+int ptsim_launch_rows_to_owners(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int nptr, int64_t lo,
+                                int64_t hi, void *workspace, size_t workspace_bytes, void *const *owner_ptrs,
+                                int nowners, int64_t owner_rows, void *stream);
+int ptsim_tp_reduce_gather(const void *stage, void *const *out, void *const *signal, int nranks, int rank, int64_t rows,
+                           int64_t cols, int dtype, void *stream);
+
 /* Synchronise `stream` and return (and clear) the device status word of the current device:
  * *device_status receives PTSIM_OK or PTSIM_E_OOB / PTSIM_E_TIMEOUT as a kernel recorded it.
  * Replaces the exit-code check of runtime/spike.py:23-33 (run_process). */

@@ -153,8 +153,15 @@ int launch_rowops(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi
 int launch_qkrope(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c);
 int launch_reduce(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, void *ws, size_t ws_bytes,
                   const LaunchCtx &c);
+// Where a row-parallel GEMM's output rows go when they are pushed to their owner ranks: `n` blocks of `rows`
+// rows, block q's to ptr[q] (GemmArgs.owners in gemm.cuh).
+struct GemmOwners {
+  int n;
+  int64_t rows;
+  void *const *ptr;
+};
 int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, void *ws, size_t ws_bytes,
-                const LaunchCtx &c);
+                const LaunchCtx &c, const GemmOwners *own = nullptr);
 int64_t gemv_workspace(const ptsim_desc &d, int sm_count);
 int reduce_workspace(int sm_count);
 int launch_attention(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, const LaunchCtx &c);

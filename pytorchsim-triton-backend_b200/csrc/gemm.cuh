@@ -61,6 +61,14 @@ struct GemmArgs {
   // PTSIM_FLAG_TEST_STALL: the first CTA (the first cluster of the pair kernel) arms its first stage but
   // issues none of its copies, and every wait gives up after kTestWaitUs -- the timeout path under test.
   int32_t stall;
+  // Row-parallel GEMM of a tensor-parallel group with the reduce-scatter in its epilogue (owners > 0, bf16
+  // output): the output rows are cut into `owners` blocks of `owner_rows`; row r is stored as row
+  // r - q owner_rows of owner[q], q = r / owner_rows -- rank q's staging slot for this rank's partial, in
+  // rank q's memory (a peer store over NVLink) -- instead of into c.  Every thread fences at system scope
+  // before the kernel ends, so the stores have landed when the stream's next kernel announces them.
+  int32_t owners;
+  int64_t owner_rows;
+  uint16_t *owner[8];
 };
 
 // Shared-memory table of a grouped launch: per program its group, first and end row, and the exclusive
@@ -96,6 +104,10 @@ __device__ __forceinline__ void gemm_store_row32(const GemmArgs &g, int64_t row,
       if (col0 + q < g.N) cp[q] = acc[q];
   } else {
     uint16_t *cp = g.c + row * g.ldc + col0;
+    if (g.owners > 0) {
+      const int64_t q = row / g.owner_rows;
+      cp = g.owner[q] + (row - q * g.owner_rows) * g.ldc + col0;
+    }
     if (full && (g.ldc % 8 == 0)) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -444,6 +456,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
   // abort (final once every role has reached this barrier) the producer waits, bounded, for every stage it
   // armed, so no copy still lands in shared memory once the CTA has exited.
   sm100::tc_fence_before();
+  if (g.owners > 0) __threadfence_system();
   __syncthreads();
   if (warp == 0 && lane == 0 && *abort_flag)
     for (int s = 0; s < STAGES; ++s)
@@ -630,6 +643,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2_tcgen05_kernel(const __
   // cluster barrier and may exit.  A peer that gave up alone is caught the same way: the leader's MMA
   // waits run out on the stages the peer stopped filling, which sets the leader's flag too.
   sm100::tc_fence_before();
+  if (g.owners > 0) __threadfence_system();
   __syncthreads();
   if (warp == 0 && lane == 0 && rank == 0 && *abort_flag)
     for (int s = 0; s < S; ++s)
@@ -858,7 +872,7 @@ int launch_grouped_gemm(const ptsim_desc &d, void *const *ptrs, const LaunchCtx 
 }
 
 int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, void *ws, size_t ws_bytes,
-                const LaunchCtx &c) {
+                const LaunchCtx &c, const GemmOwners *own) {
   const ptsim_gemm_params &p = d.p.gemm;
   if (d.arg_dtype[p.a_arg] != PTSIM_DT_BF16 || d.arg_dtype[p.b_arg] != PTSIM_DT_BF16)
     return fail(PTSIM_E_UNSUPPORTED, "GEMM operands must be bf16 (the MXU refuses mixed formats)");
@@ -866,6 +880,10 @@ int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, 
   if (cdt != PTSIM_DT_BF16 && cdt != PTSIM_DT_F32) return fail(PTSIM_E_UNSUPPORTED, "GEMM output must be bf16 or f32");
   if (p.r_arg >= 0 && d.arg_dtype[p.r_arg] != PTSIM_DT_BF16) return fail(PTSIM_E_UNSUPPORTED, "GEMM residual must be bf16");
   // One output row: the matrix-vector product, an HBM stream on the CUDA cores.
+  if (own != nullptr && (p.M == 1 || cdt != PTSIM_DT_BF16 || own->rows < 1 || own->n < 1 || own->n > 8 ||
+                         own->rows * own->n != p.M || p.ldc % 8 != 0))
+    return fail(PTSIM_E_UNSUPPORTED, "rows to owners: a bf16 GEMM of M > 1 rows cut into 1-8 equal blocks (M %lld, "
+                "%d blocks of %lld)", (long long)p.M, own ? own->n : 0, own ? (long long)own->rows : 0ll);
   if (p.M == 1) return lo < hi ? launch_gemv(d, ptrs, ws, ws_bytes, c) : PTSIM_OK;
   if (p.K % 8 != 0 || p.lda % 8 != 0 || p.ldb % 8 != 0)
     return fail(PTSIM_E_UNSUPPORTED, "GEMM K and leading dimensions must be multiples of 8 (16-byte TMA rows)");
@@ -884,6 +902,15 @@ int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, 
   else g.c = reinterpret_cast<uint16_t *>(ptrs[p.c_arg]);
   g.r = p.r_arg >= 0 ? reinterpret_cast<const uint16_t *>(ptrs[p.r_arg]) : nullptr;
   g.stall = (d.flags & PTSIM_FLAG_TEST_STALL) ? 1 : 0;
+  if (own != nullptr) {
+    g.owners = own->n;
+    g.owner_rows = own->rows;
+    for (int q = 0; q < own->n; ++q) {
+      if (own->ptr[q] == nullptr || reinterpret_cast<uintptr_t>(own->ptr[q]) % 16)
+        return fail(PTSIM_E_ARGS, "rows to owners: block %d's destination is null or not 16-byte aligned", q);
+      g.owner[q] = static_cast<uint16_t *>(own->ptr[q]);
+    }
+  }
   GemmPlan pl = plan_gemm(m_end - m_begin, p.M, p.N, p.K, c.sm_count);
   if (pl.splits > 1) {
     // Fewer K splits when the device cannot run every tile's cluster at once (clusters need their CTAs

@@ -14,6 +14,7 @@
 #include "decode.cuh"
 #include "moe.cuh"
 #include "itable.cuh"
+#include "collective.cuh"
 
 namespace ptsim {
 
@@ -372,6 +373,11 @@ static int static_scratch(int dev, void **out, bool refresh = false) {
   return PTSIM_OK;
 }
 
+// One launch of a checked descriptor over device pointers (ptsim_launch); `own` redirects a GEMM's output
+// rows to their owner ranks (ptsim_launch_rows_to_owners), null otherwise.
+static int launch_desc(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int nptr, int64_t lo, int64_t hi,
+                       void *workspace, size_t workspace_bytes, void *stream, const GemmOwners *own);
+
 }  // namespace ptsim
 
 using namespace ptsim;
@@ -409,6 +415,33 @@ int64_t ptsim_units(const void *desc, size_t desc_bytes) {
 
 int ptsim_launch(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int nptr, int64_t lo, int64_t hi,
                  void *workspace, size_t workspace_bytes, void *stream) {
+  return launch_desc(desc, desc_bytes, dev_ptrs, nptr, lo, hi, workspace, workspace_bytes, stream, nullptr);
+}
+
+int ptsim_launch_rows_to_owners(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int nptr, int64_t lo,
+                                int64_t hi, void *workspace, size_t workspace_bytes, void *const *owner_ptrs,
+                                int nowners, int64_t owner_rows, void *stream) {
+  int rc = check_desc(desc, desc_bytes);
+  if (rc) return rc;
+  if (reinterpret_cast<const ptsim_desc *>(desc)->kind != PTSIM_KIND_GEMM)
+    return fail(PTSIM_E_UNSUPPORTED, "rows to owners: GEMM descriptors only");
+  if (owner_ptrs == nullptr) return fail(PTSIM_E_ARGS, "rows to owners: no destination pointers");
+  GemmOwners own{nowners, owner_rows, owner_ptrs};
+  return launch_desc(desc, desc_bytes, dev_ptrs, nptr, lo, hi, workspace, workspace_bytes, stream, &own);
+}
+
+int ptsim_tp_reduce_gather(const void *stage, void *const *out, void *const *signal, int nranks, int rank, int64_t rows,
+                           int64_t cols, int dtype, void *stream) {
+  if (stage == nullptr || out == nullptr || signal == nullptr) return fail(PTSIM_E_ARGS, "reduce-gather pointers");
+  return launch_tp_allreduce(nullptr, stage, out, signal, nranks, rank, rows, cols, dtype,
+                             reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
+
+namespace ptsim {
+static int launch_desc(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int nptr, int64_t lo, int64_t hi,
+                       void *workspace, size_t workspace_bytes, void *stream, const GemmOwners *own) {
   int rc = check_desc(desc, desc_bytes);
   if (rc) return rc;
   const ptsim_desc &d = *reinterpret_cast<const ptsim_desc *>(desc);
@@ -437,13 +470,16 @@ int ptsim_launch(const void *desc, size_t desc_bytes, void *const *dev_ptrs, int
     case PTSIM_KIND_GATHER_SUM: return launch_gather_sum(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_INT_TABLE: return launch_itab(d, dev_ptrs, lo, hi, workspace, workspace_bytes, c);
     case PTSIM_KIND_QKNORM_ROPE: return launch_qkrope(d, dev_ptrs, lo, hi, c);
-    case PTSIM_KIND_GEMM: return launch_gemm(d, dev_ptrs, lo, hi, workspace, workspace_bytes, c);
+    case PTSIM_KIND_GEMM: return launch_gemm(d, dev_ptrs, lo, hi, workspace, workspace_bytes, c, own);
     case PTSIM_KIND_ATTN_PREFILL: return launch_attention(d, dev_ptrs, lo, hi, c);
     case PTSIM_KIND_REDUCE_ALL: return launch_reduce(d, dev_ptrs, lo, hi, workspace, workspace_bytes, c);
     case PTSIM_KIND_ATTN_DECODE: return launch_decode(d, dev_ptrs, lo, hi, workspace, workspace_bytes, c);
   }
   return fail(PTSIM_E_DESC, "descriptor kind %u", d.kind);
 }
+}  // namespace ptsim
+
+extern "C" {
 
 int64_t ptsim_workspace_size(const void *desc, size_t desc_bytes, int device) {
   if (check_desc(desc, desc_bytes)) return -1;
@@ -528,6 +564,48 @@ int ptsim_launch_host(const void *desc, size_t desc_bytes, void *const *host_ptr
     }
   }
   return PTSIM_OK;
+}
+
+int ptsim_peer_alloc(size_t bytes, void **dev_ptr) {
+  if (dev_ptr == nullptr || bytes == 0) return fail(PTSIM_E_ARGS, "peer buffer of %zu bytes", bytes);
+  *dev_ptr = nullptr;
+  PTSIM_CUDA(cudaMalloc(dev_ptr, bytes));
+  PTSIM_CUDA(cudaMemset(*dev_ptr, 0, bytes));
+  PTSIM_CUDA(cudaDeviceSynchronize());
+  return PTSIM_OK;
+}
+
+int ptsim_peer_free(void *dev_ptr) {
+  PTSIM_CUDA(cudaFree(dev_ptr));
+  return PTSIM_OK;
+}
+
+int ptsim_peer_handle(void *dev_ptr, void *handle) {
+  if (handle == nullptr) return fail(PTSIM_E_ARGS, "no room for the handle");
+  cudaIpcMemHandle_t h;
+  PTSIM_CUDA(cudaIpcGetMemHandle(&h, dev_ptr));
+  memcpy(handle, &h, sizeof(h));
+  return PTSIM_OK;
+}
+
+int ptsim_peer_open(const void *handle, void **dev_ptr) {
+  if (handle == nullptr || dev_ptr == nullptr) return fail(PTSIM_E_ARGS, "peer open without a handle");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  PTSIM_CUDA(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return PTSIM_OK;
+}
+
+int ptsim_peer_close(void *dev_ptr) {
+  PTSIM_CUDA(cudaIpcCloseMemHandle(dev_ptr));
+  return PTSIM_OK;
+}
+
+int ptsim_tp_allreduce(void *const *part, void *const *out, void *const *signal, int nranks, int rank, int64_t rows,
+                       int64_t cols, int dtype, void *stream) {
+  if (part == nullptr || out == nullptr || signal == nullptr) return fail(PTSIM_E_ARGS, "all-reduce pointer arrays");
+  return launch_tp_allreduce(part, nullptr, out, signal, nranks, rank, rows, cols, dtype,
+                             reinterpret_cast<cudaStream_t>(stream));
 }
 
 int ptsim_sync(void *stream, int32_t *device_status) {

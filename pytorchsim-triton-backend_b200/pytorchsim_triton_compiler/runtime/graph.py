@@ -15,7 +15,7 @@ class Graph:
         self.torch = torch
         self.device = torch.device(device)
         self.buffers = {}
-        self.steps = []          # (name, blob, [buffer names], workspace)
+        self.steps = []          # (name, blob, [buffer names], workspace, units, owners)
         self.cuda_graph = None
 
     def buffer(self, name, numel, dtype, init=None):
@@ -34,9 +34,11 @@ class Graph:
             t.copy_(init.reshape(-1).to(dt))
         return t
 
-    def add(self, name, blob, bufs):
+    def add(self, name, blob, bufs, owners=None):
         """Append a launch of descriptor `blob` whose tensor arguments are the buffers `bufs`, in the
-        descriptor's argument order; every buffer must exist with the descriptor's element count."""
+        descriptor's argument order; every buffer must exist with the descriptor's element count.  `owners`
+        = (device pointers, rows): a GEMM whose output rows go to their owner ranks in blocks of `rows`
+        (native.launch_rows_to_owners) instead of into its output buffer."""
         d = D.from_bytes(blob)
         if len(bufs) != d.nargs:
             raise ValueError(f"{name}: {len(bufs)} buffers for {d.nargs} arguments")
@@ -49,7 +51,7 @@ class Graph:
         n = native.workspace_size(blob, self.device.index or 0)
         if n > 0:
             ws = self.torch.empty(int(n), dtype=self.torch.uint8, device=self.device)
-        self.steps.append((name, bytes(blob), list(bufs), ws, d.units))
+        self.steps.append((name, bytes(blob), list(bufs), ws, d.units, owners))
 
     def launch_count(self):
         return len(self.steps)
@@ -61,12 +63,19 @@ class Graph:
         if self.cuda_graph is not None and stream is None:
             self.cuda_graph.replay()
         else:
-            for name, blob, bufs, ws, units in self.steps:
-                native.launch(blob, [self.buffers[b].data_ptr() for b in bufs], 0, units,
-                              ws.data_ptr() if ws is not None else 0, ws.numel() if ws is not None else 0,
-                              s.cuda_stream)
+            for step in self.steps:
+                self._launch(step, s.cuda_stream)
         if sync:
             native.sync(s.cuda_stream)
+
+    def _launch(self, step, stream):
+        name, blob, bufs, ws, units, owners = step
+        ptrs = [self.buffers[b].data_ptr() for b in bufs]
+        wp, wn = (ws.data_ptr(), ws.numel()) if ws is not None else (0, 0)
+        if owners is None:
+            native.launch(blob, ptrs, 0, units, wp, wn, stream)
+        else:
+            native.launch_rows_to_owners(blob, ptrs, 0, units, owners[0], owners[1], wp, wn, stream)
 
     def capture(self):
         """Capture the launch sequence into a CUDA graph (replayed by run())."""
@@ -78,10 +87,8 @@ class Graph:
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
             with torch.cuda.graph(g, stream=s):
-                for name, blob, bufs, ws, units in self.steps:
-                    native.launch(blob, [self.buffers[b].data_ptr() for b in bufs], 0, units,
-                                  ws.data_ptr() if ws is not None else 0, ws.numel() if ws is not None else 0,
-                                  s.cuda_stream)
+                for step in self.steps:
+                    self._launch(step, s.cuda_stream)
         torch.cuda.current_stream(self.device).wait_stream(s)
         self.cuda_graph = g
         return g

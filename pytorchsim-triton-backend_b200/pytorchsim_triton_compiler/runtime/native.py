@@ -25,6 +25,18 @@ SYMBOLS = {
     "ptsim_launch_host": (C.c_int, [C.c_void_p, C.c_size_t, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.c_int,
                                     C.c_uint32, C.c_uint32, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p,
                                     C.c_void_p]),
+    "ptsim_peer_alloc": (C.c_int, [C.c_size_t, C.POINTER(C.c_void_p)]),
+    "ptsim_peer_free": (C.c_int, [C.c_void_p]),
+    "ptsim_peer_handle": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "ptsim_peer_open": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    "ptsim_peer_close": (C.c_int, [C.c_void_p]),
+    "ptsim_tp_allreduce": (C.c_int, [C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.c_int,
+                                     C.c_int, C.c_int64, C.c_int64, C.c_int, C.c_void_p]),
+    "ptsim_launch_rows_to_owners": (C.c_int, [C.c_void_p, C.c_size_t, C.POINTER(C.c_void_p), C.c_int, C.c_int64,
+                                              C.c_int64, C.c_void_p, C.c_size_t, C.POINTER(C.c_void_p), C.c_int,
+                                              C.c_int64, C.c_void_p]),
+    "ptsim_tp_reduce_gather": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.c_int, C.c_int,
+                                         C.c_int64, C.c_int64, C.c_int, C.c_void_p]),
     "ptsim_sync": (C.c_int, [C.c_void_p, C.POINTER(C.c_int32)]),
     "ptsim_last_error": (C.c_int, [C.c_char_p, C.c_int]),
 }
@@ -168,9 +180,69 @@ def launch_host(blob, host_ptrs, dev_ptrs, copy_in, copy_out, chunks, workspace=
                                  C.c_void_p(int(stream_run) or None), C.c_void_p(int(stream_out) or None)))
 
 
+def peer_alloc(nbytes):
+    """A zero-filled device buffer on the current device that other processes may map; its pointer."""
+    p = C.c_void_p()
+    _check(load().ptsim_peer_alloc(int(nbytes), C.byref(p)))
+    return int(p.value)
+
+
+def peer_free(ptr):
+    _check(load().ptsim_peer_free(C.c_void_p(int(ptr))))
+
+
+def peer_handle(ptr):
+    """The 64-byte CUDA IPC handle of a buffer from peer_alloc."""
+    buf = C.create_string_buffer(64)
+    _check(load().ptsim_peer_handle(C.c_void_p(int(ptr)), buf))
+    return bytes(buf.raw)
+
+
+def peer_open(handle):
+    """This process's pointer to another process's buffer, from its handle."""
+    buf = C.create_string_buffer(bytes(handle), 64)
+    p = C.c_void_p()
+    _check(load().ptsim_peer_open(buf, C.byref(p)))
+    return int(p.value)
+
+
+def peer_close(ptr):
+    _check(load().ptsim_peer_close(C.c_void_p(int(ptr))))
+
+
+def tp_allreduce(part, out, signal, rank, rows, cols, stream=0):
+    """Enqueue the tensor-parallel all-reduce (ptsim_tp_allreduce) of bf16 [rows, cols] partials; `part`, `out` and
+    `signal` list every rank's pointers as this rank addresses them."""
+    n = len(part)
+    arr = lambda xs: (C.c_void_p * n)(*[C.c_void_p(int(x)) for x in xs])  # noqa: E731
+    _check(load().ptsim_tp_allreduce(arr(part), arr(out), arr(signal), n, int(rank), int(rows), int(cols),
+                                     D.DTYPE_CODE["bfloat16"], C.c_void_p(int(stream) or None)))
+
+
 def sync(stream=0):
     """Wait for `stream`; raise ExecutorError when a kernel recorded a device-side failure."""
     st = C.c_int32(0)
     _check(load().ptsim_sync(C.c_void_p(int(stream) or None), C.byref(st)))
     if st.value:
         raise ExecutorError(st.value, "reported by a kernel on the device (status word)")
+
+
+def launch_rows_to_owners(blob, ptrs, lo, hi, owners, owner_rows, workspace=0, workspace_bytes=0, stream=0):
+    """ptsim_launch of GEMM descriptor `blob` with its output rows pushed to their owner ranks
+    (ptsim_launch_rows_to_owners): rows [q owner_rows, (q + 1) owner_rows) go to device pointer owners[q]."""
+    lib = load()
+    buf = _desc_buffer(blob)
+    arr = (C.c_void_p * max(1, len(ptrs)))(*[C.c_void_p(int(p)) for p in ptrs])
+    own = (C.c_void_p * max(1, len(owners)))(*[C.c_void_p(int(p)) for p in owners])
+    _check(lib.ptsim_launch_rows_to_owners(buf, len(blob), arr, len(ptrs), int(lo), int(hi),
+                                           C.c_void_p(int(workspace) or None), int(workspace_bytes), own, len(owners),
+                                           int(owner_rows), C.c_void_p(int(stream) or None)))
+
+
+def tp_reduce_gather(stage, out, signal, rank, rows, cols, stream=0):
+    """Enqueue the second half of the fused all-reduce (ptsim_tp_reduce_gather): this rank's staging `stage` (a
+    device pointer) summed slot by slot into every rank's `out` (pointers as this rank addresses them)."""
+    n = len(out)
+    arr = lambda xs: (C.c_void_p * n)(*[C.c_void_p(int(x)) for x in xs])  # noqa: E731
+    _check(load().ptsim_tp_reduce_gather(C.c_void_p(int(stage)), arr(out), arr(signal), n, int(rank), int(rows),
+                                         int(cols), D.DTYPE_CODE["bfloat16"], C.c_void_p(int(stream) or None)))

@@ -210,6 +210,80 @@ class TpLayer:
         compute.wait_stream(comm)
 
 
+class TpLayerPeer:
+    """Rank `rank`'s share of the tensor-parallel layer with its two all-reduces done by the executor's own kernels
+    over NVLink peer memory instead of NCCL.  Every sum is over the ranks' bf16 partials in rank order in fp32 with
+    one bf16 rounding, so both forms give the same bits on every rank and every run.
+
+    fused=True: the o projection and the down projection push their output rows to the rank that owns them as
+    they leave the tensor cores (ptsim_launch_rows_to_owners: rank q owns token rows [q T / tp, (q + 1) T / tp)
+    and holds one staging slot per rank for them), so the reduce-scatter half of the all-reduce travels inside the
+    GEMM; a second kernel (ptsim_tp_reduce_gather) sums each rank's staging from local memory and stores the rows
+    into every rank's x1 (y).  fused=False: the GEMMs write a local partial and one kernel (ptsim_tp_allreduce)
+    loads the owned rows of every rank's partial over NVLink, sums them and stores them everywhere.
+
+    The collectives run on the compute stream, on grids sized to keep every owned row's loads in flight at once,
+    and need no communication stream.  Buffers are set up once (runtime/peer.py PeerSet); the two graph segments
+    are replayed from CUDA graphs.  Every rank of the process group builds it and calls run() the same number of
+    times."""
+
+    def __init__(self, device, T, params, cos, sin, x, tp, rank, group=None, fused=True):
+        from . import native
+        from .peer import PeerSet
+        if tp < 2 or T % tp != 0:
+            raise ValueError(f"TpLayerPeer needs tp >= 2 dividing T, got tp={tp}, T={T}")
+        self.native = native
+        self.T, self.tp, self.rank, self.fused = T, tp, rank, fused
+        self.g1, self.g2 = build_layer(device, T, params, cos, sin, x, tp=tp, rank=rank)
+        self.peers = PeerSet(device, tp, rank, group)
+        bufs = self.g1.buffers
+        # x1p / yp: the o and down projections' partials (fused: each rank's staging, tp slots of T / tp rows).
+        for name in ("x1p", "x1", "yp", "y"):
+            t, _ = self.peers.alloc(name, T * HIDDEN)
+            bufs[name] = t
+        self.peers.alloc("sig1", 64, "int32")
+        self.peers.alloc("sig2", 64, "int32")
+        R = T // tp
+        slot = rank * R * HIDDEN * 2            # bytes: this rank's slot in every staging
+
+        def redirect(g, step_prefix, old, new):
+            for k, st in enumerate(g.steps):
+                if not st[0].startswith(step_prefix):
+                    continue
+                if fused:   # the output argument stays `old` (not written); the rows go to the owners' staging
+                    g.steps[k] = tuple(st[:5]) + (([p + slot for p in self.peers.ptrs[new]], R),)
+                else:
+                    g.steps[k] = (st[0], st[1], [new if b == old else b for b in st[2]]) + tuple(st[3:])
+        redirect(self.g1, "08_", "x1", "x1p")     # the o projection (rank 0's with the residual)
+        redirect(self.g2, "11_", "y", "yp")       # the down projection (rank 0's with the residual x1)
+        self.buffers = bufs
+
+    def capture(self):
+        self.g1.capture()
+        self.g2.capture()
+
+    def launch_count(self):
+        return self.g1.launch_count() + self.g2.launch_count() + 2
+
+    def allreduce(self, part, out, sig, stream):
+        p = self.peers.ptrs
+        if self.fused:
+            self.native.tp_reduce_gather(p[part][self.rank], p[out], p[sig], self.rank, self.T, HIDDEN, stream)
+        else:
+            self.native.tp_allreduce(p[part], p[out], p[sig], self.rank, self.T, HIDDEN, stream)
+
+    def run(self):
+        torch = self.peers.torch
+        s = torch.cuda.current_stream(self.peers.device).cuda_stream
+        self.g1.run()
+        self.allreduce("x1p", "x1", "sig1", s)
+        self.g2.run()
+        self.allreduce("yp", "y", "sig2", s)
+
+    def close(self):
+        self.peers.close()
+
+
 def layer_flops(T):
     """GEMM + causal attention flops of one layer (824,633,720,832 at T = 2048)."""
     gemm = 2 * T * HIDDEN * (HQ * DIM + 2 * HKV * DIM) + 2 * T * HQ * DIM * HIDDEN + 2 * T * HIDDEN * 2 * INTER \
