@@ -424,10 +424,11 @@ int ptsim_tp_allreduce(void *const *part, void *const *out, void *const *signal,
 
 /* The same all-reduce with its reduce-scatter fused into the row-parallel GEMM, in two calls on `stream`:
  *
- * ptsim_launch_rows_to_owners: ptsim_launch of a GEMM descriptor (bf16 output, M = nowners * owner_rows) whose
- * output rows [q owner_rows, (q + 1) owner_rows) are stored, as they leave the tensor cores, at owner_ptrs[q]
- * (rank q's staging slot for this rank: rank q's staging + this rank * owner_rows * N, as this rank maps it; a
- * peer store over NVLink) instead of into the descriptor's output argument, which is not written.
+ * ptsim_launch_rows_to_owners: ptsim_launch of a GEMM descriptor (bf16 output, M = nowners * owner_rows, N a
+ * multiple of 16) whose output rows [q owner_rows, (q + 1) owner_rows) are stored, as they leave the tensor
+ * cores, at owner_ptrs[q] (32-byte aligned: rank q's staging slot for this rank, rank q's staging + this rank *
+ * owner_rows * N, as this rank maps it; a peer store over NVLink) instead of into the descriptor's output
+ * argument, which is not written.
  *
  * ptsim_tp_reduce_gather: `stage` is this rank's staging (nranks slots of rows / nranks rows, slot r filled by
  * rank r's GEMM); it sums the slots in rank order (fp32, one bf16 rounding: the bits ptsim_tp_allreduce gives)

@@ -107,6 +107,19 @@ __device__ __forceinline__ void gemm_store_row32(const GemmArgs &g, int64_t row,
     if (g.owners > 0) {
       const int64_t q = row / g.owner_rows;
       cp = g.owner[q] + (row - q * g.owner_rows) * g.ldc + col0;
+      if (full) {
+        // Two 32-byte stores: a peer store over NVLink moves about twice the bytes per second in 32-byte
+        // pieces as in 16-byte ones (the launch checks 32-byte alignment of every destination row).
+        uint32_t w[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) w[e] = pack_bf16x2(acc[2 * e], acc[2 * e + 1]);
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(cp + h * 16), "r"(w[8 * h]),
+                       "r"(w[8 * h + 1]), "r"(w[8 * h + 2]), "r"(w[8 * h + 3]), "r"(w[8 * h + 4]), "r"(w[8 * h + 5]),
+                       "r"(w[8 * h + 6]), "r"(w[8 * h + 7]) : "memory");
+        return;
+      }
     }
     if (full && (g.ldc % 8 == 0)) {
 #pragma unroll
@@ -881,9 +894,9 @@ int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, 
   if (p.r_arg >= 0 && d.arg_dtype[p.r_arg] != PTSIM_DT_BF16) return fail(PTSIM_E_UNSUPPORTED, "GEMM residual must be bf16");
   // One output row: the matrix-vector product, an HBM stream on the CUDA cores.
   if (own != nullptr && (p.M == 1 || cdt != PTSIM_DT_BF16 || own->rows < 1 || own->n < 1 || own->n > 8 ||
-                         own->rows * own->n != p.M || p.ldc % 8 != 0))
-    return fail(PTSIM_E_UNSUPPORTED, "rows to owners: a bf16 GEMM of M > 1 rows cut into 1-8 equal blocks (M %lld, "
-                "%d blocks of %lld)", (long long)p.M, own ? own->n : 0, own ? (long long)own->rows : 0ll);
+                         own->rows * own->n != p.M || p.ldc % 16 != 0))
+    return fail(PTSIM_E_UNSUPPORTED, "rows to owners: a bf16 GEMM of M > 1 rows cut into 1-8 equal blocks, N a "
+                "multiple of 16 (M %lld, %d blocks of %lld)", (long long)p.M, own ? own->n : 0, own ? (long long)own->rows : 0ll);
   if (p.M == 1) return lo < hi ? launch_gemv(d, ptrs, ws, ws_bytes, c) : PTSIM_OK;
   if (p.K % 8 != 0 || p.lda % 8 != 0 || p.ldb % 8 != 0)
     return fail(PTSIM_E_UNSUPPORTED, "GEMM K and leading dimensions must be multiples of 8 (16-byte TMA rows)");
@@ -906,8 +919,8 @@ int launch_gemm(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi, 
     g.owners = own->n;
     g.owner_rows = own->rows;
     for (int q = 0; q < own->n; ++q) {
-      if (own->ptr[q] == nullptr || reinterpret_cast<uintptr_t>(own->ptr[q]) % 16)
-        return fail(PTSIM_E_ARGS, "rows to owners: block %d's destination is null or not 16-byte aligned", q);
+      if (own->ptr[q] == nullptr || reinterpret_cast<uintptr_t>(own->ptr[q]) % 32)
+        return fail(PTSIM_E_ARGS, "rows to owners: block %d's destination is null or not 32-byte aligned", q);
       g.owner[q] = static_cast<uint16_t *>(own->ptr[q]);
     }
   }
