@@ -1,10 +1,10 @@
-"""The tensor-parallel all-reduce over NVLink peer memory (ptsim_tp_allreduce, csrc/collective.cuh), on two GPUs,
-one process each (skipped with fewer GPUs):
+"""The tensor-parallel all-reduce over NVLink peer memory (ptsim_tp_allreduce, csrc/collective.cuh), on 2, 4 and 8
+GPUs, one process each (each size skipped with fewer GPUs):
 
   - the kernel alone: every rank's output equals bf16 of the fp32 sum of all ranks' bf16 partials in rank order,
     bit for bit, on four calls in a row of different shapes with new partials each time (the generation counter
     runs on, the done count starts from zero each call);
-  - the Qwen3-shaped layer split over the two GPUs with both all-reduces done by the executor's kernels
+  - the Qwen3-shaped layer split over the GPUs with both all-reduces done by the executor's kernels
     (runtime/qwen3.py TpLayerPeer, replayed from CUDA graphs), in both forms -- one all-reduce kernel over the
     partials, and the GEMM pushing its rows to their owners (ptsim_launch_rows_to_owners) followed by
     ptsim_tp_reduce_gather -- gives the same bits either way and matches the whole layer within the bf16 bar."""
@@ -40,8 +40,8 @@ def _setup(rank, world, port):
     return dist
 
 
-# Calls in a row on one signal block, with shapes whose grids differ (64, 2, 64 and 1 CTAs over two ranks).
-SHAPES = [(512, 4096), (64, 1024), (512, 4096), (6, 24)]
+# Calls in a row on one signal block, with shapes whose grids differ (over two ranks: 64, 2, 64 and 1 CTAs).
+SHAPES = [(512, 4096), (64, 1024), (512, 4096), (8, 24)]
 
 
 def _allreduce_rank(rank, world, port, q):
@@ -110,32 +110,35 @@ def _layer_rank(rank, world, port, q, T):
         dist.destroy_process_group()
 
 
-def _spawn(target, *args):
+def _spawn(world, target, *args):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    ps = [ctx.Process(target=target, args=(r, 2, port, q) + args) for r in range(2)]
+    ps = [ctx.Process(target=target, args=(r, world, port, q) + args) for r in range(world)]
     for p in ps:
         p.start()
-    got = dict(q.get(timeout=600) for _ in range(2))
+    got = dict(q.get(timeout=600) for _ in range(world))
     for p in ps:
         p.join(timeout=60)
     return got
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="the peer all-reduce needs two GPUs")
-def test_peer_allreduce_bit_exact():
-    got = _spawn(_allreduce_rank)
-    assert got[0] == [] and got[1] == [], got
+WORLDS = [pytest.param(w, marks=pytest.mark.skipif(torch.cuda.device_count() < w, reason=f"needs {w} GPUs"))
+          for w in (2, 4, 8)]
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="tensor parallel needs two GPUs")
-def test_layer_tp2_peer_allreduce():
+@pytest.mark.parametrize("world", WORLDS)
+def test_peer_allreduce_bit_exact(world):
+    got = _spawn(world, _allreduce_rank)
+    assert all(got[r] == [] for r in range(world)), got
+
+
+@pytest.mark.parametrize("world", WORLDS)
+def test_layer_tp_peer_allreduce(world):
     """Both forms (pull, and the GEMM pushing its rows to their owners) give the same bits on every rank, and the
     layer matches the one-GPU oracle within the bf16 bar."""
-    got = _spawn(_layer_rank, 256)
+    got = _spawn(world, _layer_rank, 256)
     assert all(isinstance(v, tuple) for v in got.values()), got
-    (err, same0), (_, same1) = got[0], got[1]
-    assert same0 and same1, got
-    assert err < 1e-2, got
+    assert all(got[r][1] for r in range(world)), got
+    assert got[0][0] < 1e-2, got
