@@ -351,6 +351,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1) attn2_fwd_kernel(const __gri
     sm100::tmem_alloc(tmem_slot, 512);
     sm100::tmem_relinquish();
   }
+  pdl_enter();   // set-up above overlaps the previous kernel's tail; global memory after
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
@@ -618,8 +619,7 @@ int launch_attention(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t
       if (regs_ok.load() != 1) return fail(PTSIM_E_RESOURCE, "attention register split does not fit this build's registers");
     }
     const int64_t grid = (u1 - u0) * (g.q_tiles / 2);
-    attn2_fwd_kernel<<<unsigned(grid), kAttn2Threads, kAttn2Smem, c.stream>>>(g);
-    PTSIM_CUDA(cudaGetLastError());
+    PTSIM_CUDA(launch_pdl(attn2_fwd_kernel, dim3(unsigned(grid)), dim3(kAttn2Threads), kAttn2Smem, c.stream, g));
     return PTSIM_OK;
   }
   PTSIM_CUDA(smem_limit_once<attn_fwd_kernel>(kAttnSmem, c.device));

@@ -180,6 +180,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tcgen05_kernel(const __g
     sm100::tmem_alloc(tmem_base_slot, Cfg::TMEM_COLS);
     sm100::tmem_relinquish();
   }
+  // Set-up above overlaps the previous kernel's tail (programmatic dependent launch); global memory after.
+  pdl_enter();
   // Grouped launches: the program table (after the barrier area).
   int *g_pre = reinterpret_cast<int *>(smem + STAGES * Cfg::STAGE_BYTES + 256);
   int *g_grp = g_pre + (kGemmMaxPrograms + 1);
@@ -537,6 +539,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2_tcgen05_kernel(const __
     sm100::tmem_alloc2(tmem_slot, 512);
     sm100::tmem_relinquish2();
   }
+  pdl_enter();   // set-up above overlaps the previous kernel's tail; global memory after
   sm100::tc_fence_before();
   __syncthreads();
   sm100::cluster_sync();   // both CTAs' barriers are initialised before any cross-CTA arrival
@@ -713,14 +716,15 @@ static int run_gemm(GemmArgs &g, const LaunchCtx &c) {
   PTSIM_CUDA((smem_limit_once<gemm_tcgen05_kernel<BN, B_KMAJOR>>(Cfg::SMEM_BYTES + kGemmGroupTableBytes, c.device)));
   if (g.grp_id != nullptr) {
     // Grouped: the tile count is data-dependent (each group's rows), so one persistent CTA per SM.
-    kern<<<c.sm_count, kGemmThreads, Cfg::SMEM_BYTES + kGemmGroupTableBytes, c.stream>>>(g);
+    PTSIM_CUDA(launch_pdl(kern, dim3(unsigned(c.sm_count)), dim3(kGemmThreads), Cfg::SMEM_BYTES + kGemmGroupTableBytes,
+                          c.stream, g));
   } else if (g.splits == 1) {
     const int grid = items < c.sm_count ? items : c.sm_count;
-    kern<<<grid, kGemmThreads, Cfg::SMEM_BYTES, c.stream>>>(g);
+    PTSIM_CUDA(launch_pdl(kern, dim3(unsigned(grid)), dim3(kGemmThreads), Cfg::SMEM_BYTES, c.stream, g));
   } else {
     // One CTA per work item (items <= SMs), the splits of a tile forming one cluster.
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     cfg.gridDim = dim3(unsigned(items));
     cfg.blockDim = dim3(kGemmThreads);
     cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
@@ -729,8 +733,10 @@ static int run_gemm(GemmArgs &g, const LaunchCtx &c) {
     attr[0].val.clusterDim.x = unsigned(g.splits);
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     PTSIM_CUDA(cudaLaunchKernelEx(&cfg, kern, g));
   }
   PTSIM_CUDA(cudaGetLastError());
@@ -768,7 +774,7 @@ template <bool B_KMAJOR>
 static int run_gemm2(GemmArgs &g, int nclusters, const LaunchCtx &c) {
   PTSIM_CUDA((smem_limit_once<gemm2_tcgen05_kernel<B_KMAJOR>>(kGemm2Smem, c.device)));
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   cfg.gridDim = dim3(unsigned(2 * nclusters));
   cfg.blockDim = dim3(kGemmThreads);
   cfg.dynamicSmemBytes = kGemm2Smem;
@@ -777,8 +783,10 @@ static int run_gemm2(GemmArgs &g, int nclusters, const LaunchCtx &c) {
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   PTSIM_CUDA(cudaLaunchKernelEx(&cfg, gemm2_tcgen05_kernel<B_KMAJOR>, g));
   PTSIM_CUDA(cudaGetLastError());
   return PTSIM_OK;

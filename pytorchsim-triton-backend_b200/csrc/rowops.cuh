@@ -69,6 +69,7 @@ __global__ void __launch_bounds__(256) row_fast_kernel(const __grid_constant__ R
   constexpr int RPC = 256 / TPR;                 // rows per CTA
   constexpr int W = TPR >= 32 ? TPR / 32 : 1;    // warps per row
   __shared__ float red_a[RPC * W], red_b[RPC * W];
+  pdl_enter();
   const int lane_in_row = threadIdx.x % TPR;
   const int row_in_cta = threadIdx.x / TPR;
   const int64_t r = L.rows_begin + int64_t(blockIdx.x) * RPC + row_in_cta;
@@ -164,6 +165,7 @@ template <int KIND, int TPR, int CH>
 __global__ void __launch_bounds__(TPR, (CH >= 4 ? 1024 : 2048) / TPR) row_cta_kernel(const __grid_constant__ RowLaunch L) {
   constexpr int NW = TPR / 32;
   __shared__ float red[2][NW];
+  pdl_enter();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t row = L.rows_begin + blockIdx.x;
   const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(L.in) + row * L.in_stride);
@@ -266,8 +268,7 @@ template <int KIND, int TPR, int CH>
 static int launch_row_cta(const RowLaunch &L, const LaunchCtx &c) {
   const int64_t rows = L.rows_end - L.rows_begin;
   if (rows > int64_t(0x7fffffff)) return fail(PTSIM_E_UNSUPPORTED, "%lld rows in one launch", (long long)rows);
-  row_cta_kernel<KIND, TPR, CH><<<unsigned(rows), TPR, 0, c.stream>>>(L);
-  PTSIM_CUDA(cudaGetLastError());
+  PTSIM_CUDA(launch_pdl(row_cta_kernel<KIND, TPR, CH>, dim3(unsigned(rows)), dim3(TPR), 0, c.stream, L));
   return PTSIM_OK;
 }
 
@@ -308,6 +309,7 @@ __device__ __forceinline__ void st_any(void *p, int dt, int64_t i, float v) {
 // passes hit L1/L2).
 template <int KIND>
 __global__ void __launch_bounds__(256) row_generic_kernel(const __grid_constant__ RowLaunch L) {
+  pdl_enter();
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
@@ -353,7 +355,7 @@ template <int KIND, int TPR, int CH>
 static void launch_row_fast(const RowLaunch &L, const LaunchCtx &c) {
   constexpr int RPC = 256 / TPR;
   const int64_t rows = L.rows_end - L.rows_begin;
-  row_fast_kernel<KIND, TPR, CH><<<unsigned(ceil_div(rows, RPC)), 256, 0, c.stream>>>(L);
+  (void)launch_pdl(row_fast_kernel<KIND, TPR, CH>, dim3(unsigned(ceil_div(rows, RPC))), dim3(256), 0, c.stream, L);
 }
 
 template <int KIND, int TPR>
@@ -399,8 +401,7 @@ static int launch_row_kind(const RowLaunch &L, const LaunchCtx &c) {
   }
   int64_t blocks = ceil_div(L.rows_end - L.rows_begin, 8);
   if (blocks > int64_t(c.sm_count) * 8) blocks = int64_t(c.sm_count) * 8;
-  row_generic_kernel<KIND><<<unsigned(blocks), 256, 0, c.stream>>>(L);
-  PTSIM_CUDA(cudaGetLastError());
+  PTSIM_CUDA(launch_pdl(row_generic_kernel<KIND>, dim3(unsigned(blocks)), dim3(256), 0, c.stream, L));
   return PTSIM_OK;
 }
 
@@ -430,9 +431,8 @@ int launch_rowops(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi
     // Rows of a few values (the router's top-k weights): one warp per row.
     int64_t blocks = ceil_div(L.rows_end - L.rows_begin, 8);
     if (blocks > int64_t(c.sm_count) * 8) blocks = int64_t(c.sm_count) * 8;
-    if (d.kind == PTSIM_KIND_ROW_SUM) row_generic_kernel<kRowSum><<<unsigned(blocks), 256, 0, c.stream>>>(L);
-    else row_generic_kernel<kDivSum><<<unsigned(blocks), 256, 0, c.stream>>>(L);
-    PTSIM_CUDA(cudaGetLastError());
+    if (d.kind == PTSIM_KIND_ROW_SUM) PTSIM_CUDA(launch_pdl(row_generic_kernel<kRowSum>, dim3(unsigned(blocks)), dim3(256), 0, c.stream, L));
+    else PTSIM_CUDA(launch_pdl(row_generic_kernel<kDivSum>, dim3(unsigned(blocks)), dim3(256), 0, c.stream, L));
     return PTSIM_OK;
   }
   return launch_row_kind<kRmsNorm>(L, c);
@@ -458,6 +458,7 @@ struct QkLaunch {
 };
 
 __global__ void __launch_bounds__(256) qk_rope_kernel(const __grid_constant__ QkLaunch L) {
+  pdl_enter();
   const int lane = threadIdx.x & 31, sub = lane & 15, half = lane >> 4;
   const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const uint32_t nwarps = (gridDim.x * blockDim.x) >> 5;
@@ -538,8 +539,7 @@ int launch_qkrope(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t hi
   // Four rows per warp per step, eight warps per block; enough blocks for one step of every row.
   int64_t blocks = ceil_div(int64_t(L.row_end - L.row_begin), 32);
   if (blocks > int64_t(c.sm_count) * 16) blocks = int64_t(c.sm_count) * 16;
-  qk_rope_kernel<<<unsigned(blocks), 256, 0, c.stream>>>(L);
-  PTSIM_CUDA(cudaGetLastError());
+  PTSIM_CUDA(launch_pdl(qk_rope_kernel, dim3(unsigned(blocks)), dim3(256), 0, c.stream, L));
   return PTSIM_OK;
 }
 
