@@ -444,6 +444,72 @@ def split_suite(dev, world, rank, iters=5, warm=2):
     return out
 
 
+def sweep_timing(dev, world, rank, iters=5, warm=2):
+    """BASELINE.json configs[2]'s M sweep (M in {128, 512, 2048, 4096, 8192}, N = K = 4096) spread over the ranks
+    by longest processing time (runtime/sweep.py, the reference's validation/gemm/simulate_shapes.py shard): each
+    rank runs only its own points on its own GPU, no collective.  Per iteration a rank's time is the sum of its
+    points' device times (L2 flushed before each launch); the job's time is the maximum over ranks.  Beside it:
+    the whole sweep on one GPU (every rank runs all points at once; the slowest counts), and the bound no split
+    of these points can beat (the costliest point alone, 8192 x 4096 x 4096)."""
+    import torch
+    from pytorchsim_triton_compiler.codegen import descriptors as D
+    from pytorchsim_triton_compiler.runtime import native
+    from pytorchsim_triton_compiler.runtime import sweep as SW
+    _, tflops, _ = peaks()
+    flush = L2Flush(dev)
+    stream = torch.cuda.current_stream(dev)
+    names = [f"gemm_{m}x4096x4096" for m in (128, 512, 2048, 4096, 8192)]
+    objs = {n: load_object(n) for n in names}
+    pts = [SW.Point(n, objs[n][1]) for n in names]
+    bufs = {}
+    for n in names:
+        m, blob = objs[n]
+        d = D.from_bytes(blob)
+        g = torch.Generator(device=dev).manual_seed(0)
+        ts = [(torch.randn(math.prod(a["shape"]), generator=g, device=dev) / math.sqrt(d.p.gemm.K)).to(torch.bfloat16)
+              if a["role"] in ("in", "inout") else torch.zeros(math.prod(a["shape"]), dtype=torch.bfloat16, device=dev)
+              for a in m["args"]]
+        wsn = native.workspace_size(blob, dev.index or 0)
+        bufs[n] = (blob, d.units, ts, torch.empty(max(1, wsn), dtype=torch.uint8, device=dev), wsn)
+
+    def run(points):
+        """Per iteration, this rank's summed device time (ms) over `points`, and each point's median."""
+        each = {p.name: [] for p in points}
+        total = []
+        barrier(world)
+        torch.cuda.synchronize()
+        for k in range(iters + warm):
+            ev = []
+            for p in points:
+                blob, units, ts, ws, wsn = bufs[p.name]
+                flush()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                native.launch(blob, [t.data_ptr() for t in ts], 0, units, ws.data_ptr(), wsn, stream.cuda_stream)
+                b.record(stream)
+                ev.append((p.name, a, b))
+            native.sync(stream.cuda_stream)
+            if k >= warm:
+                ms = [(n, a.elapsed_time(b)) for n, a, b in ev]
+                total.append(sum(t for _, t in ms))
+                for n, t in ms:
+                    each[n].append(t)
+        return total, {n: statistics.median(v) for n, v in each.items() if v}
+
+    mine = SW.shard(pts, rank, world)
+    t_n, _ = run(mine)   # every rank runs it (a rank without points too: run() meets the barrier)
+    tn = statistics.median(max_per_step(t_n, world, dev))
+    t_1, per_point = run(pts)
+    t1 = statistics.median(max_per_step(t_1, world, dev))
+    flops = 2 * sum(p.cost for p in pts)
+    return {"points": [p.name for p in SW.longest_first(pts)], "shards": [[p.name for p in SW.shard(pts, r, world)] for r in range(world)],
+            "ms": round(tn, 4), "TFLOP/s": round(flops / tn / 1e9, 1), "frac_bf16": round(flops / tn / 1e9 / (world * tflops), 3),
+            "one_gpu_ms": round(t1, 4), "speedup": round(t1 / tn, 3),
+            "costliest_point_ms": round(per_point.get(names[-1], 0.0), 4),
+            "note": "no split of these five points finishes before the costliest one (8192 x 4096 x 4096); "
+                    "speedup is bounded by one_gpu_ms / costliest_point_ms"}
+
+
 def run_b200(args, world, rank, local):
     import torch
     from pytorchsim_triton_compiler.codegen import descriptors as D
@@ -610,6 +676,7 @@ def run_b200(args, world, rank, local):
                                          flush, stream)
     if world > 1 and args.suite:
         line["split_suite"] = split_suite(dev, world, rank)
+        line["sweep"] = sweep_timing(dev, world, rank)
         line["tp_layer"] = tp_layer_timing(dev, world, rank, steps=10, warmup=3)
     if rank == 0 and world == 1 and args.cpu:
         base, _ = cpu_rate(seconds=10.0)
