@@ -556,26 +556,41 @@ def run_b200(args, world, rank, local):
         raise SystemExit(f"bench: the timed kernels disagree with the oracle: {why}")
 
     clocks = Clocks(local)
-    events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
     barrier(world)
     torch.cuda.synchronize()
     clocks.start()
     # The GPU spins while the host enqueues every timed step, so the events measure kernels, not the
-    # host's launch latency.
+    # host's launch latency.  A step is timed from an event before the softmax launch to one after the
+    # RMSNorm launch: the RMSNorm kernel, a programmatic dependent, is scheduled while the softmax grid
+    # drains (an event between the two would serialise them).
     torch.cuda._sleep(int(1e7))
     for k in range(args.steps):
         flush()                     # L2 flush, outside the timed events
-        step(events[k])
+        events[k][0].record(stream)
+        step()
+        events[k][1].record(stream)
     torch.cuda.synchronize()
     barrier(world)
     clk = clocks.stop()
     native.sync(sp)
-    t_soft = [e[0].elapsed_time(e[1]) for e in events]
-    t_rms = [e[1].elapsed_time(e[2]) for e in events]
-    total_ms = sum(t_soft) + sum(t_rms)
+    total_ms = sum(e[0].elapsed_time(e[1]) for e in events)
     total_ms = reduce_max(total_ms, world, dev)
     ms_per_step = total_ms / args.steps
     value = world * STEP_BYTES * args.steps / (total_ms / 1e3) / 1e9
+
+    # Per-kernel device times for the roofline, from the same number of extra steps with an event between
+    # the two launches (each launch then runs alone).
+    kev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    torch.cuda._sleep(int(1e7))
+    for k in range(args.steps):
+        flush()
+        step(kev[k])
+    torch.cuda.synchronize()
+    native.sync(sp)
+    t_soft = [e[0].elapsed_time(e[1]) for e in kev]
+    t_rms = [e[1].elapsed_time(e[2]) for e in kev]
 
     # e2e: the same step through the runtime's host-memory launcher (runtime.cuda.HostPipeline, one C-ABI call
     # ptsim_launch_host per launch) with pinned host buffers: every step copies the inputs in and the outputs
@@ -669,6 +684,9 @@ def run_b200(args, world, rank, local):
                     "copy_ceiling_note": "the same bytes as plain pinned copies (inputs in and outputs out on two "
                                          "streams at once, no kernel), in this metric's units"},
             "gpu_launches": 2 * args.steps,
+            "timing": "value and ms_per_step: one event pair around each step's two launches (the RMSNorm launch "
+                      "is the softmax's programmatic dependent); roofline.per_kernel: the same steps again with an "
+                      "event between the launches",
             "clocks": clk}
     if world > 1:
         line["strong"] = strong_headline(dev, world, rank, args.steps, args.warmup, d_s, d_r,
