@@ -605,7 +605,7 @@ int launch_attention(const ptsim_desc &d, void *const *ptrs, int64_t lo, int64_t
   g.scale = a.scale;
   g.stall = (d.flags & PTSIM_FLAG_TEST_STALL) ? 1 : 0;
   if (int64_t(a.batch * a.hkv * a.seq) >= (int64_t(1) << 31)) return fail(PTSIM_E_UNSUPPORTED, "attention rows exceed int32");
-  if (a.seq % (2 * kAttnBM) == 0 && getenv("PTSIM_ATTN_V1") == nullptr) {
+  if (a.seq % (2 * kAttnBM) == 0) {
     PTSIM_CUDA(smem_limit_once<attn2_fwd_kernel>(kAttn2Smem, c.device));
     {
       // setmaxnreg.inc waits until the registers it asks for are free, so the warpgroups' shares must fit
